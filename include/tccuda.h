@@ -1,0 +1,255 @@
+/*
+ * tccuda.h — the C ABI of the tensorcrate CUDA backend (sm_100a, B200).
+ *
+ * Each entry point is what the crate's `Cuda` implementation of the sealed
+ * `Backend` and `Kernels<T>` traits binds over FFI (`extern "C"`, plain
+ * pointers and sizes).  The comment above each one names the reference
+ * interface it replaces, as `file:line` inside the tensorcrate crate.
+ *
+ * Conventions
+ *  - Every call returns `int` status: TC_OK (0) or a TC_E* code.  The message
+ *    of the last failure on the calling thread is read with tc_last_error().
+ *    The Rust side maps a non-zero status to a panic naming the operation,
+ *    as `require_metal` does for Metal (src/tensors/backend.rs:418-426).
+ *  - Pointers named `*_dev` / device buffers come from tc_malloc (or any
+ *    cudaMalloc'd memory); `stream` is a cudaStream_t passed as void*
+ *    (NULL = the per-thread default stream).  Every compute call is
+ *    asynchronous on `stream`; nothing synchronises except tc_stream_sync and
+ *    the tc_memcpy_* calls given a NULL stream.
+ *  - Sizes, offsets and strides count ELEMENTS (as `Strided` does,
+ *    src/tensors/backend.rs:196-203), never bytes, except where named `bytes`.
+ *  - Shapes have at most TC_MAX_RANK axes (src/tensors/layout.rs:16).
+ *  - Scalars of the element type travel as `double`: every f32, f16 and bf16
+ *    value is exact in f64, and the callee rounds nothing on the way in.
+ */
+#ifndef TCCUDA_H
+#define TCCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TC_MAX_RANK 6
+
+/* ---- status codes ------------------------------------------------------ */
+enum tc_status {
+  TC_OK = 0,
+  TC_EINVAL = 1,   /* bad argument: shape, stride, dtype, op or size      */
+  TC_ERANGE = 2,   /* a layout reads or writes past its storage           */
+  TC_ENOMEM = 3,   /* device or pinned allocation failed                  */
+  TC_ECUDA = 4,    /* a CUDA runtime/driver call or kernel launch failed  */
+  TC_ENCCL = 5,    /* an NCCL call failed or NCCL could not be loaded     */
+  TC_ETIMEOUT = 6, /* a bounded device-side wait gave up                  */
+  TC_ENOTSUP = 7   /* the combination is not provided by this build       */
+};
+
+/* ---- element types ----------------------------------------------------- */
+/* The `Real` element types the Cuda backend implements Kernels<T> for
+ * (src/tensors/kernels.rs:808-829): f32, f16, bf16.  U32 is the index type
+ * arg_reduce returns (src/tensors/kernels.rs:1187). */
+enum tc_dtype { TC_F32 = 0, TC_F16 = 1, TC_BF16 = 2, TC_U32 = 3 };
+
+/* ---- operation enums: the discriminants of the reference's enums -------- */
+/* BinaryOp, src/tensors/kernels.rs:32-38 */
+enum tc_binary_op { TC_ADD = 0, TC_SUB = 1, TC_MUL = 2, TC_DIV = 3, TC_REM = 4 };
+/* Compare, src/tensors/kernels.rs:106-121 */
+enum tc_compare {
+  TC_MIN = 0, TC_MAX = 1, TC_MAX_SHARE = 2, TC_LESS = 3,
+  TC_LESS_EQUAL = 4, TC_GREATER = 5, TC_GREATER_EQUAL = 6
+};
+/* Reduce, src/tensors/kernels.rs:183-188 */
+enum tc_reduce { TC_SUM = 0, TC_RMIN = 1, TC_RMAX = 2 };
+/* Pairwise, src/tensors/kernels.rs:411-416: which enum `op` belongs to */
+enum tc_pairwise { TC_PAIR_ARITHMETIC = 0, TC_PAIR_COMPARE = 1, TC_PAIR_POWER = 2 };
+/* AxisReduction, src/tensors/kernels.rs:449-457 */
+enum tc_axis_reduction { TC_AXIS_FOLD = 0, TC_AXIS_MEAN = 1, TC_AXIS_VARIANCE = 2 };
+/* Transposed, src/tensors/kernels.rs:462-467, plus "neither" */
+enum tc_transposed { TC_TRANS_NONE = 0, TC_TRANS_LEFT = 1, TC_TRANS_RIGHT = 2 };
+
+/* One block of an assemble or strided write: `shape` copied from `source`
+ * (holding `source_len` elements) at (from_offset, from_strides) to the
+ * target at (to_offset, to_strides).  Mirrors `Region`
+ * (src/tensors/backend.rs:205-221) with `Strided` flattened in. */
+typedef struct tc_region {
+  const void *source;
+  size_t source_len;
+  uint32_t rank;
+  size_t shape[TC_MAX_RANK];
+  size_t from_offset;
+  size_t from_strides[TC_MAX_RANK];
+  size_t to_offset;
+  size_t to_strides[TC_MAX_RANK];
+} tc_region;
+
+/* ---- errors, devices, memory, streams ----------------------------------- */
+/* The message of this thread's last failure (NUL-terminated, truncated to
+ * `len`).  Returns the status of that failure. */
+int tc_last_error(char *buf, size_t len);
+/* Library build string: version, arch, and which kernels are compiled in. */
+const char *tc_build_info(void);
+/* Make `device` current for this thread (Metal's per-thread device,
+ * src/metal/device.rs; env TC_CUDA_DEVICE picks the default). */
+int tc_set_device(int device);
+int tc_device_count(int *count);
+
+/* Device storage: `Backend::Storage<T>` (src/tensors/backend.rs:84).
+ * Served from a per-device caching pool, as Metal's src/metal/pool.rs. */
+int tc_malloc(void **out_dev, size_t bytes);
+int tc_free(void *dev);
+/* Release every cached block back to CUDA. */
+int tc_pool_trim(void);
+/* Pinned host staging, for the lazily filled host mirror behind
+ * `Backend::as_slice` (src/tensors/backend.rs:96-99). */
+int tc_host_alloc(void **out_host, size_t bytes);
+int tc_host_free(void *host);
+
+/* `Backend::store`/`from_vec` (src/tensors/backend.rs:88-93): upload. */
+int tc_memcpy_h2d(void *dst_dev, const void *src_host, size_t bytes, void *stream);
+/* `Backend::as_slice`/`as_mut_slice` (src/tensors/backend.rs:96-104):
+ * download; with a NULL stream it returns after the copy is complete. */
+int tc_memcpy_d2h(void *dst_host, const void *src_dev, size_t bytes, void *stream);
+/* `Backend::duplicate` (src/tensors/backend.rs:111): device copy, no wait. */
+int tc_memcpy_d2d(void *dst_dev, const void *src_dev, size_t bytes, void *stream);
+int tc_memset(void *dst_dev, int value, size_t bytes, void *stream);
+int tc_stream_sync(void *stream);
+
+/* ---- layout copies (bits; any element width 1, 2, 4, 8 or 16 bytes) ---- */
+/* `Backend::strided_copy` (src/tensors/backend.rs:141-145; Host
+ * strided_copy_slice :255-274): the elements a layout of `shape` reads from
+ * `src` (`src_len` elements) at (src_offset, src_strides), written row-major
+ * into `dst` (prod(shape) elements).  TC_ERANGE if the layout reaches past
+ * src_len (check_strided, :225-252). */
+int tc_strided_copy(size_t elem_bytes, uint32_t rank, const size_t *shape,
+                    const void *src, size_t src_len, size_t src_offset,
+                    const size_t *src_strides, void *dst, void *stream);
+
+/* `Backend::strided_write` (src/tensors/backend.rs:170-173; Host
+ * strided_write_slice :277-300): copy one region into `target`
+ * (`target_len` elements) in place. */
+int tc_strided_write(size_t elem_bytes, void *target, size_t target_len,
+                     const tc_region *region, void *stream);
+
+/* `Backend::assemble` (src/tensors/backend.rs:157-160; Host assemble_slices
+ * :303-323): a new storage of `len` elements built from `n` regions.  Every
+ * region is copied in one launch; elements no region writes are left as they
+ * were in `dst` (the reference leaves them unspecified). */
+int tc_assemble(size_t elem_bytes, void *dst, size_t len, const tc_region *regions,
+                size_t n, void *stream);
+
+/* ---- same-shape elementwise (Kernels<T>, src/tensors/kernels.rs:832-863) */
+/* `vector_elementwise`/`matrix_elementwise`: out = a op b. */
+int tc_elementwise(int dtype, int op, const void *a, const void *b, void *out,
+                   size_t n, void *stream);
+/* `vector_broadcast`/`matrix_broadcast`: out = a op s, or s op a when
+ * scalar_left. */
+int tc_broadcast_scalar(int dtype, int op, const void *a, double scalar,
+                        int scalar_left, void *out, size_t n, void *stream);
+/* `vector_compare`/`matrix_compare` (Compare::value, kernels.rs:138-153). */
+int tc_compare(int dtype, int cmp, const void *a, const void *b, void *out,
+               size_t n, void *stream);
+/* `vector_compare_scalar`/`matrix_compare_scalar`. */
+int tc_compare_scalar(int dtype, int cmp, const void *a, double scalar,
+                      int scalar_left, void *out, size_t n, void *stream);
+/* `vector_clamp`/`matrix_clamp` (kernels.rs:863): TC_EINVAL unless
+ * low <= high. */
+int tc_clamp(int dtype, const void *a, double low, double high, void *out,
+             size_t n, void *stream);
+/* `vector_reduce` (kernels.rs:867): the whole vector folded into
+ * out_dev[0] (one element of `dtype`); an empty vector gives the identity. */
+int tc_vector_reduce(int dtype, int op, const void *a, size_t n, void *out_dev,
+                     void *stream);
+/* `dot` (kernels.rs:897): sum of a[i]*b[i], f32 accumulate, into out_dev[0]. */
+int tc_dot(int dtype, const void *a, const void *b, size_t n, void *out_dev,
+           void *stream);
+
+/* ---- strided kernels (src/tensors/kernels.rs:1162-1187) ------------------ */
+/* `strided_binary` (kernels.rs:1162; Host strided::binary, strided.rs:29):
+ * op(a, b) over the common `shape`, each operand read through its own
+ * offset and strides (a zero stride repeats an element), into a new
+ * row-major `out`.  `kind` is tc_pairwise; `op` a tc_binary_op or
+ * tc_compare (ignored for TC_PAIR_POWER).  a_len/b_len bound the reads. */
+int tc_strided_binary(int dtype, int kind, int op, uint32_t rank, const size_t *shape,
+                      const void *a, size_t a_len, size_t a_offset, const size_t *a_strides,
+                      const void *b, size_t b_len, size_t b_offset, const size_t *b_strides,
+                      void *out, void *stream);
+
+/* `reduce_axes` (kernels.rs:1175; Host strided::reduce, strided.rs:105-184):
+ * `input` folded over `axes` (distinct, ascending, n_axes of them), one
+ * result per index of the kept axes in row-major order.  `kind` is
+ * tc_axis_reduction; `op` the tc_reduce of a fold; `divisor` the
+ * Variance divisor.  f32/f16/bf16 accumulate in f32 and round once.  Every
+ * slice holds at least one element (the front-end, reduction.rs:126-143,
+ * fills empty results itself). */
+int tc_reduce_axes(int dtype, uint32_t rank, const size_t *shape, const void *input,
+                   size_t input_len, size_t offset, const size_t *strides,
+                   uint32_t n_axes, const uint32_t *axes, int kind, int op,
+                   size_t divisor, void *out, void *stream);
+
+/* `arg_reduce` (kernels.rs:1187; Host strided::arg_reduce, strided.rs:201):
+ * the u32 position along `axis` of each slice's max (op = TC_RMAX) or min
+ * (TC_RMIN): first position on ties, NaNs passed over, all-NaN -> 0. */
+int tc_arg_reduce(int dtype, uint32_t rank, const size_t *shape, const void *input,
+                  size_t input_len, size_t offset, const size_t *strides, uint32_t axis,
+                  int op, uint32_t *out, void *stream);
+
+/* ---- products ------------------------------------------------------------ */
+/* `matmul` (kernels.rs:956), `matmul_add` (:963) and `matmul_transposed_add`
+ * (:975-985), row-major:  C[rows x cols] (+)= op(A)·op(B) with inner
+ * dimension `inner`.  transposed = TC_TRANS_NONE: A is rows x inner, B is
+ * inner x cols; TC_TRANS_LEFT: A is stored inner x rows (Aᵀ·B);
+ * TC_TRANS_RIGHT: B is stored cols x inner (A·Bᵀ).  accumulate != 0 adds
+ * into C (the moved-in addend); otherwise C is overwritten.  f32 runs FP32
+ * CUDA-core tiles; f16/bf16 run the tcgen05 tensor-core kernel with f32
+ * accumulation, rounding each output once (compact::matmul,
+ * src/compact.rs:232-253). */
+int tc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
+              const void *a, const void *b, void *c, int accumulate, void *stream);
+
+/* `matvec`/`matvec_add` (kernels.rs:901-908; matrix.rs:675-730):
+ * y[rows] (+)= M[rows x cols]·x[cols]. */
+int tc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x,
+              void *y, int accumulate, void *stream);
+/* `vecmat` (kernels.rs:899; vector.rs:491-505): y[cols] = xᵀ[rows]·M. */
+int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m,
+              void *y, void *stream);
+
+/* ---- optimizer updates (the fused programs of src/optim.rs) ------------- */
+/* Adam's fused program (optim.rs:1048-1099), run in place over n elements:
+ * resumed = 0 is the first step (m, v are written fresh), resumed = 1 every
+ * later one.  rate, beta1, beta2, eps and the two corrections
+ * 1/(1-beta^t) are values of the element type, computed on the host as
+ * Adam::update does (optim.rs:1106-1124).  Every operation rounds to the
+ * element type, in the program's order. */
+int tc_adam(int dtype, size_t n, void *p, const void *g, void *m, void *v, int resumed,
+            double rate, double beta1, double beta2, double eps, double first_correction,
+            double second_correction, void *stream);
+/* Sgd's fused program (optim.rs:773-787): p <- p - g·rate. */
+int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *stream);
+
+/* ---- layout helpers (host only; src/tensors/layout.rs) ------------------ */
+/* `coalesce` (layout.rs:419-446) for n_ops operands whose strides are
+ * strides[op*rank + axis]; writes the merged shape and strides (same
+ * packing, out_rank axes).  Exposed so the descriptor builder can be tested
+ * without a GPU. */
+int tc_coalesce(uint32_t rank, const size_t *shape, uint32_t n_ops, const size_t *strides,
+                uint32_t *out_rank, size_t *out_shape, size_t *out_strides);
+
+/* ---- multi-GPU (NCCL over NVLink; no counterpart in the reference) ------ */
+typedef struct tc_comm tc_comm;
+/* 128 opaque bytes (ncclUniqueId) for rank 0 to share with the others. */
+int tc_comm_unique_id(uint8_t id[128]);
+int tc_comm_init(int rank, int nranks, const uint8_t id[128], tc_comm **out);
+int tc_comm_destroy(tc_comm *comm);
+/* Concatenate every rank's `count` elements into recv (nranks*count). */
+int tc_allgather(tc_comm *comm, int dtype, const void *send, void *recv, size_t count,
+                 void *stream);
+/* In-place all-reduce of `count` elements; op is tc_reduce. */
+int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TCCUDA_H */

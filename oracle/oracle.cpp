@@ -1,0 +1,1003 @@
+// oracle.cpp — CPU restatement of tensorcrate's Host backend (test
+// infrastructure only: the checker and the timed CPU baseline, never part of
+// the product).  Built with -ffp-contract=off so that a*b+c is two roundings
+// unless a function below calls std::fma or an FMA intrinsic where the
+// reference does.
+#include "oracle.h"
+
+#include <immintrin.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// f16 / bf16 <-> f32.  Crate `half` 2.7.1 (Cargo.lock:51-54) converts with
+// round-to-nearest-even and keeps a NaN quiet with the top of its payload;
+// the compact types compute every operation in f32 and round once
+// (src/compact.rs:5-22).
+// ---------------------------------------------------------------------------
+inline uint32_t bits_of(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+inline float float_of(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+
+inline uint16_t f32_to_bf16(float f) {
+  uint32_t x = bits_of(f);
+  if ((x & 0x7fffffffu) > 0x7f800000u) return uint16_t((x >> 16) | 0x0040u);
+  const uint32_t round_bit = 0x8000u;
+  if ((x & round_bit) && (x & (3u * round_bit - 1u))) return uint16_t((x >> 16) + 1u);
+  return uint16_t(x >> 16);
+}
+inline float bf16_to_f32(uint16_t h) { return float_of(uint32_t(h) << 16); }
+
+inline uint16_t f32_to_f16(float f) {
+  uint32_t x = bits_of(f);
+  uint32_t sign = (x >> 16) & 0x8000u;
+  uint32_t exp = (x >> 23) & 0xffu;
+  uint32_t man = x & 0x7fffffu;
+  if (exp == 0xffu) {
+    if (man == 0) return uint16_t(sign | 0x7c00u);
+    return uint16_t(sign | 0x7c00u | 0x0200u | (man >> 13));
+  }
+  int e = int(exp) - 127 + 15;
+  if (e >= 0x1f) return uint16_t(sign | 0x7c00u);
+  if (e <= 0) {
+    if (e < -10) return uint16_t(sign);
+    man |= 0x800000u;
+    uint32_t shift = uint32_t(14 - e);
+    uint32_t half_man = man >> shift;
+    uint32_t round_bit = 1u << (shift - 1);
+    if ((man & round_bit) && (man & (3u * round_bit - 1u))) half_man++;
+    return uint16_t(sign | half_man);
+  }
+  uint32_t out = sign | (uint32_t(e) << 10) | (man >> 13);
+  const uint32_t round_bit = 0x1000u;
+  if ((man & round_bit) && (man & (3u * round_bit - 1u))) out++;
+  return uint16_t(out);
+}
+inline float f16_to_f32(uint16_t h) {
+  uint32_t sign = uint32_t(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  if (exp == 0x1fu) return float_of(sign | 0x7f800000u | (man << 13));
+  if (exp == 0) {
+    if (man == 0) return float_of(sign);
+    // subnormal: value = man * 2^-24, exact in f32
+    float v = float(man) * 5.9604644775390625e-08f;
+    return sign ? -v : v;
+  }
+  return float_of(sign | ((exp - 15 + 127) << 23) | (man << 13));
+}
+
+// Element access: load widens exactly, store rounds once.
+struct F32 { using S = float;
+  static float load(const void *p, size_t i) { return static_cast<const float *>(p)[i]; }
+  static void store(void *p, size_t i, float v) { static_cast<float *>(p)[i] = v; }
+  static float round(float v) { return v; } };
+struct F16 { using S = uint16_t;
+  static float load(const void *p, size_t i) { return f16_to_f32(static_cast<const uint16_t *>(p)[i]); }
+  static void store(void *p, size_t i, float v) { static_cast<uint16_t *>(p)[i] = f32_to_f16(v); }
+  static float round(float v) { return f16_to_f32(f32_to_f16(v)); } };
+struct BF16 { using S = uint16_t;
+  static float load(const void *p, size_t i) { return bf16_to_f32(static_cast<const uint16_t *>(p)[i]); }
+  static void store(void *p, size_t i, float v) { static_cast<uint16_t *>(p)[i] = f32_to_bf16(v); }
+  static float round(float v) { return bf16_to_f32(f32_to_bf16(v)); } };
+
+template <class F> int with_dtype(int dtype, F &&f) {
+  switch (dtype) {
+    case TC_F32: return f(F32{});
+    case TC_F16: return f(F16{});
+    case TC_BF16: return f(BF16{});
+    default: return int(TC_EINVAL);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Scalar semantics, src/tensors/kernels.rs.
+// ---------------------------------------------------------------------------
+// f32::min / f32::max: IEEE minNum/maxNum, a number beats a NaN.
+inline float min_num(float a, float b) { if (std::isnan(a)) return b; if (std::isnan(b)) return a; return b < a ? b : a; }
+inline float max_num(float a, float b) { if (std::isnan(a)) return b; if (std::isnan(b)) return a; return b > a ? b : a; }
+
+// Compare::value, kernels.rs:138-153.
+inline float compare_value(int op, float a, float b) {
+  switch (op) {
+    case TC_MIN: return min_num(a, b);
+    case TC_MAX: return max_num(a, b);
+    case TC_MAX_SHARE: return a > b ? 1.0f : (a < b ? 0.0f : 0.5f);
+    case TC_LESS: return a < b ? 1.0f : 0.0f;
+    case TC_LESS_EQUAL: return a <= b ? 1.0f : 0.0f;
+    case TC_GREATER: return a > b ? 1.0f : 0.0f;
+    case TC_GREATER_EQUAL: return a >= b ? 1.0f : 0.0f;
+  }
+  return NAN;
+}
+// BinaryOp as Pairwise::value computes it, kernels.rs:431-441 (Rem is the
+// truncated remainder, Rust's `%` on floats = fmod).
+inline float binary_value(int op, float a, float b) {
+  switch (op) {
+    case TC_ADD: return a + b;
+    case TC_SUB: return a - b;
+    case TC_MUL: return a * b;
+    case TC_DIV: return a / b;
+    case TC_REM: return std::fmod(a, b);
+  }
+  return NAN;
+}
+// Pairwise::Power: f32::powf (src/numbers/primitive.rs:133-153).
+inline float power_value(float a, float b) { return std::pow(a, b); }
+
+inline bool valid_binary(int op) { return op >= TC_ADD && op <= TC_REM; }
+inline bool valid_compare(int op) { return op >= TC_MIN && op <= TC_GREATER_EQUAL; }
+
+// ---------------------------------------------------------------------------
+// Layout, src/tensors/layout.rs.
+// ---------------------------------------------------------------------------
+struct Dims { uint32_t rank = 0; size_t v[TC_MAX_RANK] = {0}; };
+
+// coalesce, layout.rs:419-446: drop axes of extent 1, merge an axis into the
+// previous one wherever every operand steps across the pair as across one.
+template <int N>
+void coalesce(uint32_t rank, const size_t *shape, const size_t *const *strides, Dims &out_shape,
+              Dims *out) {
+  out_shape.rank = 0;
+  for (int o = 0; o < N; ++o) out[o].rank = 0;
+  for (uint32_t axis = 0; axis < rank; ++axis) {
+    size_t extent = shape[axis];
+    if (extent == 1) continue;
+    uint32_t r = out_shape.rank;
+    bool joins = r > 0;
+    for (int o = 0; o < N && joins; ++o) joins = out[o].v[r - 1] == strides[o][axis] * extent;
+    if (joins) {
+      out_shape.v[r - 1] *= extent;
+      for (int o = 0; o < N; ++o) out[o].v[r - 1] = strides[o][axis];
+    } else {
+      out_shape.v[r] = extent;
+      out_shape.rank++;
+      for (int o = 0; o < N; ++o) { out[o].v[r] = strides[o][axis]; out[o].rank++; }
+    }
+  }
+}
+
+// for_each_run, layout.rs:457-498: call run(starts, len, steps) for each
+// innermost run of a row-major walk.
+template <int N, class Run>
+void for_each_run(uint32_t rank, const size_t *shape, const size_t *offsets,
+                  const size_t *const *strides, Run &&run) {
+  for (uint32_t a = 0; a < rank; ++a) if (shape[a] == 0) return;
+  Dims cs; Dims cst[N];
+  coalesce<N>(rank, shape, strides, cs, cst);
+  size_t at[N];
+  for (int o = 0; o < N; ++o) at[o] = offsets[o];
+  uint32_t r = cs.rank;
+  if (r == 0) { size_t steps[N] = {0}; run(at, size_t(1), steps); return; }
+  size_t inner = cs.v[r - 1];
+  size_t steps[N];
+  for (int o = 0; o < N; ++o) steps[o] = cst[o].v[r - 1];
+  size_t index[TC_MAX_RANK] = {0};
+  for (;;) {
+    run(at, inner, steps);
+    uint32_t axis = r - 1;
+    for (;;) {
+      if (axis == 0) return;
+      axis -= 1;
+      index[axis] += 1;
+      for (int o = 0; o < N; ++o) at[o] += cst[o].v[axis];
+      if (index[axis] < cs.v[axis]) break;
+      for (int o = 0; o < N; ++o) at[o] -= cst[o].v[axis] * cs.v[axis];
+      index[axis] = 0;
+    }
+  }
+}
+
+// reach, layout.rs:136-149: one past the last element read, or 0 if none;
+// SIZE_MAX on overflow.
+size_t reach(uint32_t rank, const size_t *shape, size_t offset, const size_t *strides) {
+  for (uint32_t a = 0; a < rank; ++a) if (shape[a] == 0) return 0;
+  size_t end = offset;
+  for (uint32_t a = 0; a < rank; ++a) {
+    size_t span;
+    if (__builtin_mul_overflow(shape[a] - 1, strides[a], &span)) return SIZE_MAX;
+    if (__builtin_add_overflow(end, span, &end)) return SIZE_MAX;
+  }
+  if (end == SIZE_MAX) return SIZE_MAX;
+  return end + 1;
+}
+
+size_t element_count(uint32_t rank, const size_t *shape) {
+  size_t n = 1;
+  for (uint32_t a = 0; a < rank; ++a) n *= shape[a];
+  return n;
+}
+
+// check_strided, backend.rs:226-252.
+bool check_strided(size_t len, uint32_t rank, const size_t *shape, size_t offset,
+                   const size_t *strides) {
+  if (rank > TC_MAX_RANK) return false;
+  return reach(rank, shape, offset, strides) <= len;
+}
+
+void contiguous_strides(uint32_t rank, const size_t *shape, size_t *out) {
+  size_t step = 1;
+  for (int a = int(rank) - 1; a >= 0; --a) { out[a] = step; step *= shape[a]; }
+}
+
+// ---------------------------------------------------------------------------
+// Threads for the same-shape elementwise kernels, as simd_dispatch::split
+// (src/tensors/simd_dispatch.rs:54-76): windows of PARALLEL_GRAIN elements
+// over all host threads once the output holds at least two of them.
+// ---------------------------------------------------------------------------
+int g_threads = 0;
+constexpr size_t PARALLEL_GRAIN = 32 * 1024;
+
+template <class K> void split(size_t n, K &&kernel) {
+  int threads = g_threads > 0 ? g_threads : int(std::max(1u, std::thread::hardware_concurrency()));
+  if (n < 2 * PARALLEL_GRAIN || threads == 1) { kernel(size_t(0), n); return; }
+  size_t windows = (n + PARALLEL_GRAIN - 1) / PARALLEL_GRAIN;
+  std::atomic<size_t> next{0};
+  auto worker = [&] {
+    for (;;) {
+      size_t w = next.fetch_add(1);
+      if (w >= windows) return;
+      size_t lo = w * PARALLEL_GRAIN, hi = std::min(n, lo + PARALLEL_GRAIN);
+      kernel(lo, hi);
+    }
+  };
+  std::vector<std::thread> pool;
+  int spawn = int(std::min<size_t>(size_t(threads), windows)) - 1;
+  for (int t = 0; t < spawn; ++t) pool.emplace_back(worker);
+  worker();
+  for (auto &t : pool) t.join();
+}
+
+// ---------------------------------------------------------------------------
+// f32 products, src/simd_x86.rs.  The Host dispatches on CPU features at run
+// time; so does this.
+// ---------------------------------------------------------------------------
+bool has_avx2_fma() {
+  static int cached = -1;
+  if (cached < 0) cached = (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma")) ? 1 : 0;
+  return cached == 1;
+}
+
+// matmul_avx, simd_x86.rs:1303-1327: for i, for p, broadcast a[i,p] and FMA
+// it with b[p, j..j+8] into out[i, j..j+8]; the column tail is
+// `out += a*b`, two roundings (Rust does not contract).
+__attribute__((target("avx2,fma")))
+void matmul_avx(const float *a, const float *b, size_t, size_t k, size_t n, float *out,
+                size_t row0, size_t row1) {
+  for (size_t i = row0; i < row1; ++i) {
+    size_t arow = i * k, orow = i * n;
+    for (size_t p = 0; p < k; ++p) {
+      float value = a[arow + p];
+      __m256 broadcast = _mm256_set1_ps(value);
+      size_t brow = p * n;
+      size_t j = 0;
+      for (; j + 8 <= n; j += 8) {
+        __m256 rhs = _mm256_loadu_ps(b + brow + j);
+        __m256 cur = _mm256_loadu_ps(out + orow + j);
+        _mm256_storeu_ps(out + orow + j, _mm256_fmadd_ps(broadcast, rhs, cur));
+      }
+      for (; j < n; ++j) out[orow + j] += value * b[brow + j];
+    }
+  }
+}
+// matmul_sse, simd_x86.rs:1334-1358: the same, unfused throughout.
+void matmul_sse(const float *a, const float *b, size_t m, size_t k, size_t n, float *out,
+                size_t row0, size_t row1) {
+  (void)m;
+  for (size_t i = row0; i < row1; ++i) {
+    size_t arow = i * k, orow = i * n;
+    for (size_t p = 0; p < k; ++p) {
+      float value = a[arow + p];
+      size_t brow = p * n;
+      for (size_t j = 0; j < n; ++j) out[orow + j] = out[orow + j] + value * b[brow + j];
+    }
+  }
+}
+
+// dot_avx, simd_x86.rs:72-104: four 8-lane FMA accumulators over blocks of
+// 32, summed pairwise lane by lane, then the 8 lanes in order; then 8-lane
+// blocks of unfused products; then a scalar tail.
+__attribute__((target("avx2,fma")))
+float dot_avx(const float *a, const float *b, size_t len) {
+  size_t i = 0;
+  __m256 acc[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+  while (i + 32 <= len) {
+    for (int lane = 0; lane < 4; ++lane) {
+      size_t off = i + size_t(lane) * 8;
+      acc[lane] = _mm256_fmadd_ps(_mm256_loadu_ps(a + off), _mm256_loadu_ps(b + off), acc[lane]);
+    }
+    i += 32;
+  }
+  __m256 total = _mm256_add_ps(_mm256_add_ps(acc[0], acc[1]), _mm256_add_ps(acc[2], acc[3]));
+  float lanes[8];
+  _mm256_storeu_ps(lanes, total);
+  // Rust's `Sum for f32` folds from -0.0.
+  float sum = -0.0f;
+  for (int l = 0; l < 8; ++l) sum += lanes[l];
+  while (i + 8 <= len) {
+    _mm256_storeu_ps(lanes, _mm256_mul_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i)));
+    float part = -0.0f;
+    for (int l = 0; l < 8; ++l) part += lanes[l];
+    sum += part;
+    i += 8;
+  }
+  for (; i < len; ++i) sum += a[i] * b[i];
+  return sum;
+}
+// dot_sse, simd_x86.rs:110-135: four 4-lane unfused accumulators.
+float dot_sse(const float *a, const float *b, size_t len) {
+  size_t i = 0;
+  float acc[4][4] = {{0}};
+  while (i + 16 <= len) {
+    for (int lane = 0; lane < 4; ++lane)
+      for (int l = 0; l < 4; ++l) acc[lane][l] = acc[lane][l] + a[i + lane * 4 + l] * b[i + lane * 4 + l];
+    i += 16;
+  }
+  float sum = -0.0f;
+  for (int l = 0; l < 4; ++l) sum += (acc[0][l] + acc[1][l]) + (acc[2][l] + acc[3][l]);
+  while (i + 4 <= len) {
+    float part = -0.0f;
+    for (int l = 0; l < 4; ++l) part += a[i + l] * b[i + l];
+    sum += part;
+    i += 4;
+  }
+  for (; i < len; ++i) sum += a[i] * b[i];
+  return sum;
+}
+float dot_f32(const float *a, const float *b, size_t len) {
+  return has_avx2_fma() ? dot_avx(a, b, len) : dot_sse(a, b, len);
+}
+
+constexpr size_t MIN_MATMUL_OPS = 512;  // HOST_MATMUL_DISPATCH_OPS, src/tensors/mod.rs:167
+
+// Matrix<f32, Host>::matmul / matmul_add over output rows [row0, row1)
+// (matrix.rs:580-666): the SIMD i-p-j path at or above 512 multiply-adds,
+// else the scalar loops (i-j-p running sum for matmul, i-p-j for matmul_add).
+void matmul_f32(const float *a, const float *b, size_t m, size_t k, size_t n, float *out,
+                bool accumulate, size_t row0, size_t row1) {
+  if (m * k * n >= MIN_MATMUL_OPS) {
+    if (!accumulate)
+      for (size_t i = row0; i < row1; ++i) std::fill(out + i * n, out + (i + 1) * n, 0.0f);
+    if (has_avx2_fma()) matmul_avx(a, b, m, k, n, out, row0, row1);
+    else matmul_sse(a, b, m, k, n, out, row0, row1);
+    return;
+  }
+  if (!accumulate) {
+    for (size_t i = row0; i < row1; ++i)
+      for (size_t j = 0; j < n; ++j) {
+        float sum = 0.0f;
+        for (size_t p = 0; p < k; ++p) sum = sum + a[i * k + p] * b[p * n + j];
+        out[i * n + j] = sum;
+      }
+  } else {
+    for (size_t i = row0; i < row1; ++i)
+      for (size_t p = 0; p < k; ++p)
+        for (size_t j = 0; j < n; ++j) out[i * n + j] = out[i * n + j] + a[i * k + p] * b[p * n + j];
+  }
+}
+
+// Real::from_f64 (src/numbers/mod.rs:76-86): an f64 rounded to the element
+// type once (crate half rounds f64 -> f16/bf16 directly).  Rounding to f32 by
+// round-to-odd first keeps that single rounding exact, since f32 carries more
+// than twice the compact types' precision plus two bits.
+template <class T> float from_f64(double d) {
+  float f = float(d);
+  if (std::is_same<T, F32>::value) return f;
+  if (std::isfinite(d) && double(f) != d && std::isfinite(f)) {
+    uint32_t u = bits_of(f);
+    if (std::fabs(double(f)) > std::fabs(d)) u -= 1;
+    f = float_of(u | 1u);
+  }
+  return T::round(f);
+}
+
+template <class T> std::vector<float> widen_all(const void *p, size_t n) {
+  std::vector<float> out(n);
+  for (size_t i = 0; i < n; ++i) out[i] = T::load(p, i);
+  return out;
+}
+
+// A transposed copy, as Kernels::transpose then matmul_add is the default
+// matmul_transposed_add (kernels.rs:975-985).
+template <class T> std::vector<typename T::S> transposed_copy(const void *m, size_t rows, size_t cols) {
+  using S = typename T::S;
+  const S *src = static_cast<const S *>(m);
+  std::vector<S> out(rows * cols);
+  for (size_t i = 0; i < rows; ++i)
+    for (size_t j = 0; j < cols; ++j) out[j * rows + i] = src[i * cols + j];
+  return out;
+}
+
+template <class T>
+int matmul_rows(size_t rows, size_t inner, size_t cols, const void *a, const void *b, void *c,
+                bool accumulate, size_t row0, size_t row1) {
+  if (std::is_same<T, F32>::value) {
+    matmul_f32(static_cast<const float *>(a), static_cast<const float *>(b), rows, inner, cols,
+               static_cast<float *>(c), accumulate, row0, row1);
+    return int(TC_OK);
+  }
+  // compact::matmul, src/compact.rs:232-253: widen once, the f32 product
+  // (addend widened too when accumulating), round each output once.
+  std::vector<float> left(( row1 - row0) * inner);
+  for (size_t i = row0; i < row1; ++i)
+    for (size_t p = 0; p < inner; ++p) left[(i - row0) * inner + p] = T::load(a, i * inner + p);
+  std::vector<float> right = widen_all<T>(b, inner * cols);
+  std::vector<float> out((row1 - row0) * cols, 0.0f);
+  if (accumulate)
+    for (size_t i = row0; i < row1; ++i)
+      for (size_t j = 0; j < cols; ++j) out[(i - row0) * cols + j] = T::load(c, i * cols + j);
+  // The band is a matrix of its own; the MIN_MATMUL_OPS choice is made on
+  // the whole product, as the reference makes it.
+  size_t band = row1 - row0;
+  if (rows * inner * cols >= MIN_MATMUL_OPS) {
+    if (has_avx2_fma()) matmul_avx(left.data(), right.data(), band, inner, cols, out.data(), 0, band);
+    else matmul_sse(left.data(), right.data(), band, inner, cols, out.data(), 0, band);
+  } else {
+    matmul_f32(left.data(), right.data(), band, inner, cols, out.data(), accumulate, 0, band);
+  }
+  for (size_t i = row0; i < row1; ++i)
+    for (size_t j = 0; j < cols; ++j) T::store(c, i * cols + j, out[(i - row0) * cols + j]);
+  return int(TC_OK);
+}
+
+}  // namespace
+
+// ===========================================================================
+// exported
+// ===========================================================================
+extern "C" {
+
+void orc_set_threads(int threads) { g_threads = threads; }
+
+void orc_narrow(int dtype, const float *in, void *out, size_t n) {
+  with_dtype(dtype, [&](auto t) { using T = decltype(t); for (size_t i = 0; i < n; ++i) T::store(out, i, in[i]); return 0; });
+}
+void orc_widen(int dtype, const void *in, float *out, size_t n) {
+  with_dtype(dtype, [&](auto t) { using T = decltype(t); for (size_t i = 0; i < n; ++i) out[i] = T::load(in, i); return 0; });
+}
+
+int orc_coalesce(uint32_t rank, const size_t *shape, uint32_t n_ops, const size_t *strides,
+                 uint32_t *out_rank, size_t *out_shape, size_t *out_strides) {
+  if (rank > TC_MAX_RANK || n_ops < 1 || n_ops > 3) return int(TC_EINVAL);
+  const size_t *ops[3] = {strides, strides + rank, strides + 2 * rank};
+  Dims cs; Dims cst[3];
+  if (n_ops == 1) coalesce<1>(rank, shape, ops, cs, cst);
+  else if (n_ops == 2) coalesce<2>(rank, shape, ops, cs, cst);
+  else coalesce<3>(rank, shape, ops, cs, cst);
+  *out_rank = cs.rank;
+  for (uint32_t a = 0; a < cs.rank; ++a) out_shape[a] = cs.v[a];
+  for (uint32_t o = 0; o < n_ops; ++o)
+    for (uint32_t a = 0; a < cs.rank; ++a) out_strides[o * cs.rank + a] = cst[o].v[a];
+  return int(TC_OK);
+}
+
+// broadcast_shape, layout.rs:330-341.
+int orc_broadcast_shape(uint32_t lrank, const size_t *left, uint32_t rrank, const size_t *right,
+                        uint32_t *out_rank, size_t *out_shape) {
+  uint32_t rank = std::max(lrank, rrank);
+  if (rank > TC_MAX_RANK) return int(TC_EINVAL);
+  for (uint32_t axis = 0; axis < rank; ++axis) {
+    uint32_t from_end = rank - axis;
+    size_t l = lrank >= from_end ? left[lrank - from_end] : 1;
+    size_t r = rrank >= from_end ? right[rrank - from_end] : 1;
+    if (l == r) out_shape[axis] = l;
+    else if (l == 1) out_shape[axis] = r;
+    else if (r == 1) out_shape[axis] = l;
+    else return int(TC_EINVAL);
+  }
+  *out_rank = rank;
+  return int(TC_OK);
+}
+
+// broadcast_strides, layout.rs:347-363.
+int orc_broadcast_strides(uint32_t rank, const size_t *shape, const size_t *strides,
+                          uint32_t trank, const size_t *target, size_t *out_strides) {
+  if (trank < rank || trank > TC_MAX_RANK) return int(TC_EINVAL);
+  uint32_t added = trank - rank;
+  for (uint32_t a = 0; a < trank; ++a) out_strides[a] = 0;
+  for (uint32_t axis = 0; axis < rank; ++axis) {
+    size_t wanted = target[added + axis];
+    if (shape[axis] == wanted) out_strides[added + axis] = strides[axis];
+    else if (shape[axis] == 1) out_strides[added + axis] = 0;
+    else return int(TC_EINVAL);
+  }
+  return int(TC_OK);
+}
+
+int orc_walk(uint32_t rank, const size_t *shape, size_t offset, const size_t *strides,
+             size_t *out_positions) {
+  if (rank > TC_MAX_RANK) return int(TC_EINVAL);
+  size_t k = 0;
+  const size_t *st[1] = {strides};
+  size_t off[1] = {offset};
+  for_each_run<1>(rank, shape, off, st, [&](const size_t *at, size_t len, const size_t *steps) {
+    for (size_t i = 0; i < len; ++i) out_positions[k++] = at[0] + i * steps[0];
+  });
+  return int(TC_OK);
+}
+
+// strided_copy_slice, backend.rs:255-274.
+int orc_strided_copy(size_t elem, uint32_t rank, const size_t *shape, const void *src,
+                     size_t src_len, size_t src_offset, const size_t *src_strides, void *dst) {
+  if (!check_strided(src_len, rank, shape, src_offset, src_strides)) return int(TC_ERANGE);
+  const char *s = static_cast<const char *>(src);
+  char *d = static_cast<char *>(dst);
+  size_t k = 0;
+  const size_t *st[1] = {src_strides};
+  size_t off[1] = {src_offset};
+  for_each_run<1>(rank, shape, off, st, [&](const size_t *at, size_t len, const size_t *steps) {
+    if (steps[0] == 1) {
+      std::memcpy(d + k * elem, s + at[0] * elem, len * elem);
+      k += len;
+    } else {
+      for (size_t i = 0; i < len; ++i, ++k) std::memcpy(d + k * elem, s + (at[0] + i * steps[0]) * elem, elem);
+    }
+  });
+  return int(TC_OK);
+}
+
+// strided_write_slice, backend.rs:277-300.
+int orc_strided_write(size_t elem, void *target, size_t target_len, const tc_region *r) {
+  if (r->rank > TC_MAX_RANK) return int(TC_EINVAL);
+  if (!check_strided(r->source_len, r->rank, r->shape, r->from_offset, r->from_strides)) return int(TC_ERANGE);
+  if (!check_strided(target_len, r->rank, r->shape, r->to_offset, r->to_strides)) return int(TC_ERANGE);
+  const char *s = static_cast<const char *>(r->source);
+  char *d = static_cast<char *>(target);
+  const size_t *st[2] = {r->from_strides, r->to_strides};
+  size_t off[2] = {r->from_offset, r->to_offset};
+  for_each_run<2>(r->rank, r->shape, off, st, [&](const size_t *at, size_t len, const size_t *steps) {
+    if (steps[0] == 1 && steps[1] == 1) std::memcpy(d + at[1] * elem, s + at[0] * elem, len * elem);
+    else
+      for (size_t i = 0; i < len; ++i)
+        std::memcpy(d + (at[1] + i * steps[1]) * elem, s + (at[0] + i * steps[0]) * elem, elem);
+  });
+  return int(TC_OK);
+}
+
+// assemble_slices, backend.rs:303-323: fill with the first element of the
+// first non-empty region, then one strided write per region in order.
+int orc_assemble(size_t elem, void *dst, size_t len, const tc_region *regions, size_t n) {
+  const void *fill = nullptr;
+  for (size_t i = 0; i < n; ++i) {
+    const tc_region &r = regions[i];
+    if (r.rank > TC_MAX_RANK) return int(TC_EINVAL);
+    if (!check_strided(r.source_len, r.rank, r.shape, r.from_offset, r.from_strides)) return int(TC_ERANGE);
+    if (!fill && element_count(r.rank, r.shape) != 0)
+      fill = static_cast<const char *>(r.source) + r.from_offset * elem;
+  }
+  if (!fill) return len == 0 ? TC_OK : TC_EINVAL;
+  char *d = static_cast<char *>(dst);
+  for (size_t k = 0; k < len; ++k) std::memcpy(d + k * elem, fill, elem);
+  for (size_t i = 0; i < n; ++i) {
+    int st = orc_strided_write(elem, dst, len, &regions[i]);
+    if (st) return st;
+  }
+  return int(TC_OK);
+}
+
+// Same-shape elementwise: Host vector_elementwise (kernels.rs:1193-1206)
+// through simd_dispatch::elementwise (split across threads).
+int orc_elementwise(int dtype, int op, const void *a, const void *b, void *out, size_t n) {
+  if (!valid_binary(op)) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) T::store(out, i, binary_value(op, T::load(a, i), T::load(b, i)));
+    });
+    return int(TC_OK);
+  });
+}
+
+// vector_broadcast (kernels.rs:1208-1220): a op s, or s op a.
+int orc_broadcast_scalar(int dtype, int op, const void *a, double scalar, int scalar_left,
+                         void *out, size_t n) {
+  if (!valid_binary(op)) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    float s = float(scalar);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) {
+        float x = T::load(a, i);
+        T::store(out, i, scalar_left ? binary_value(op, s, x) : binary_value(op, x, s));
+      }
+    });
+    return int(TC_OK);
+  });
+}
+
+int orc_compare(int dtype, int cmp, const void *a, const void *b, void *out, size_t n) {
+  if (!valid_compare(cmp)) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) T::store(out, i, compare_value(cmp, T::load(a, i), T::load(b, i)));
+    });
+    return int(TC_OK);
+  });
+}
+
+int orc_compare_scalar(int dtype, int cmp, const void *a, double scalar, int scalar_left,
+                       void *out, size_t n) {
+  if (!valid_compare(cmp)) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    float s = float(scalar);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) {
+        float x = T::load(a, i);
+        T::store(out, i, scalar_left ? compare_value(cmp, s, x) : compare_value(cmp, x, s));
+      }
+    });
+    return int(TC_OK);
+  });
+}
+
+// Vector::clamp, src/tensors/vector.rs:642-652: ordered_min(ordered_max(x,
+// low), high) (src/tensors/order.rs:10-29); a NaN element becomes `low`.
+int orc_clamp(int dtype, const void *a, double low, double high, void *out, size_t n) {
+  if (!(low <= high)) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    float lo_v = float(low), hi_v = float(high);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) {
+        float x = T::load(a, i);
+        float m = std::isnan(x) ? lo_v : (x < lo_v ? lo_v : x);
+        m = m > hi_v ? hi_v : m;
+        T::store(out, i, m);
+      }
+    });
+    return int(TC_OK);
+  });
+}
+
+// Reduce::fold (kernels.rs:217-226; compact::fold, compact.rs:196-205): left
+// to right in f32 from the identity, rounded once.
+int orc_vector_reduce(int dtype, int op, const void *a, size_t n, void *out) {
+  if (op < TC_SUM || op > TC_RMAX) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    float acc = op == TC_SUM ? 0.0f : (op == TC_RMIN ? INFINITY : -INFINITY);
+    for (size_t i = 0; i < n; ++i) {
+      float x = T::load(a, i);
+      acc = op == TC_SUM ? acc + x : (op == TC_RMIN ? min_num(acc, x) : max_num(acc, x));
+    }
+    T::store(out, 0, acc);
+    return int(TC_OK);
+  });
+}
+
+// dot: f32 through simd::f32k::dot (simd_x86.rs:58-104); f16/bf16 through
+// compact::dot (compact.rs:162-178), a running f32 sum of exact products.
+int orc_dot(int dtype, const void *a, const void *b, size_t n, void *out) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    if (std::is_same<T, F32>::value) {
+      const float *x = static_cast<const float *>(a), *y = static_cast<const float *>(b);
+      float s;
+      if (n >= 16) s = dot_f32(x, y, n);
+      else { s = 0.0f; for (size_t i = 0; i < n; ++i) s = s + x[i] * y[i]; }
+      T::store(out, 0, s);
+    } else {
+      float s = 0.0f;
+      for (size_t i = 0; i < n; ++i) s = s + T::load(a, i) * T::load(b, i);
+      T::store(out, 0, s);
+    }
+    return int(TC_OK);
+  });
+}
+
+// strided::binary + zip, strided.rs:29-78: op over the common shape in
+// row-major order, each operand read through its strides.  Single-threaded,
+// as the Host runs it.
+int orc_strided_binary(int dtype, int kind, int op, uint32_t rank, const size_t *shape,
+                       const void *a, size_t a_len, size_t a_offset, const size_t *a_strides,
+                       const void *b, size_t b_len, size_t b_offset, const size_t *b_strides,
+                       void *out) {
+  if (rank > TC_MAX_RANK) return int(TC_EINVAL);
+  if (kind == TC_PAIR_ARITHMETIC && !valid_binary(op)) return int(TC_EINVAL);
+  if (kind == TC_PAIR_COMPARE && !valid_compare(op)) return int(TC_EINVAL);
+  if (kind < 0 || kind > TC_PAIR_POWER) return int(TC_EINVAL);
+  if (!check_strided(a_len, rank, shape, a_offset, a_strides)) return int(TC_ERANGE);
+  if (!check_strided(b_len, rank, shape, b_offset, b_strides)) return int(TC_ERANGE);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    auto f = [&](float x, float y) {
+      return kind == TC_PAIR_ARITHMETIC ? binary_value(op, x, y)
+           : kind == TC_PAIR_COMPARE ? compare_value(op, x, y) : power_value(x, y);
+    };
+    size_t k = 0;
+    const size_t *st[2] = {a_strides, b_strides};
+    size_t off[2] = {a_offset, b_offset};
+    for_each_run<2>(rank, shape, off, st, [&](const size_t *at, size_t len, const size_t *steps) {
+      for (size_t i = 0; i < len; ++i, ++k)
+        T::store(out, k, f(T::load(a, at[0] + i * steps[0]), T::load(b, at[1] + i * steps[1])));
+    });
+    return int(TC_OK);
+  });
+}
+
+// strided::reduce / reduce_in / fold, strided.rs:105-184: one row-major walk
+// of the input, each element (widened to f32) folded into the accumulator
+// of its result; Mean = total / depth; Variance = a second walk over squared
+// deviations from the f32 mean, divided by `divisor`; each result rounded
+// to the element type once.
+int orc_reduce_axes(int dtype, uint32_t rank, const size_t *shape, const void *input,
+                    size_t input_len, size_t offset, const size_t *strides, uint32_t n_axes,
+                    const uint32_t *axes, int kind, int op, size_t divisor, void *out) {
+  if (rank > TC_MAX_RANK || n_axes > rank) return int(TC_EINVAL);
+  if (kind < TC_AXIS_FOLD || kind > TC_AXIS_VARIANCE) return int(TC_EINVAL);
+  if (kind == TC_AXIS_FOLD && (op < TC_SUM || op > TC_RMAX)) return int(TC_EINVAL);
+  if (!check_strided(input_len, rank, shape, offset, strides)) return int(TC_ERANGE);
+  bool folded[TC_MAX_RANK] = {false};
+  for (uint32_t i = 0; i < n_axes; ++i) {
+    if (axes[i] >= rank || (i > 0 && axes[i] <= axes[i - 1])) return int(TC_EINVAL);
+    folded[axes[i]] = true;
+  }
+  // result_strides, strided.rs:83-100.
+  size_t kept[TC_MAX_RANK]; uint32_t nk = 0;
+  for (uint32_t a = 0; a < rank; ++a) if (!folded[a]) kept[nk++] = shape[a];
+  size_t kept_strides[TC_MAX_RANK];
+  contiguous_strides(nk, kept, kept_strides);
+  size_t to[TC_MAX_RANK]; uint32_t next = 0;
+  for (uint32_t a = 0; a < rank; ++a) to[a] = folded[a] ? 0 : kept_strides[next++];
+  size_t results = element_count(nk, kept);
+  size_t depth = 1;
+  for (uint32_t i = 0; i < n_axes; ++i) depth *= shape[axes[i]];
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    const size_t *st[2] = {strides, to};
+    size_t off[2] = {offset, 0};
+    auto walk = [&](auto &&combine) {
+      for_each_run<2>(rank, shape, off, st, [&](const size_t *at, size_t len, const size_t *steps) {
+        for (size_t i = 0; i < len; ++i) {
+          size_t slot = at[1] + i * steps[1];
+          combine(slot, T::load(input, at[0] + i * steps[0]));
+        }
+      });
+    };
+    std::vector<float> totals(results);
+    float count = float(depth);
+    auto means = [&] {
+      std::vector<float> m(results, 0.0f);
+      walk([&](size_t slot, float x) { m[slot] = m[slot] + x; });
+      for (auto &v : m) v = v / count;
+      return m;
+    };
+    if (kind == TC_AXIS_FOLD) {
+      float id = op == TC_SUM ? 0.0f : (op == TC_RMIN ? INFINITY : -INFINITY);
+      std::fill(totals.begin(), totals.end(), id);
+      walk([&](size_t slot, float x) {
+        totals[slot] = op == TC_SUM ? totals[slot] + x
+                     : op == TC_RMIN ? min_num(totals[slot], x) : max_num(totals[slot], x);
+      });
+    } else if (kind == TC_AXIS_MEAN) {
+      totals = means();
+    } else {
+      std::vector<float> m = means();
+      std::fill(totals.begin(), totals.end(), 0.0f);
+      walk([&](size_t slot, float x) {
+        float d = x - m[slot];
+        totals[slot] = totals[slot] + d * d;
+      });
+      float div = float(double(divisor));
+      for (auto &v : totals) v = v / div;
+    }
+    for (size_t r = 0; r < results; ++r) T::store(out, r, totals[r]);
+    return int(TC_OK);
+  });
+}
+
+// strided::arg_reduce + replaces, strided.rs:186-225.
+int orc_arg_reduce(int dtype, uint32_t rank, const size_t *shape, const void *input,
+                   size_t input_len, size_t offset, const size_t *strides, uint32_t axis, int op,
+                   uint32_t *out) {
+  if (rank > TC_MAX_RANK || axis >= rank) return int(TC_EINVAL);
+  if (op != TC_RMIN && op != TC_RMAX) return int(TC_EINVAL);
+  if (!check_strided(input_len, rank, shape, offset, strides)) return int(TC_ERANGE);
+  size_t kept[TC_MAX_RANK]; uint32_t nk = 0;
+  for (uint32_t a = 0; a < rank; ++a) if (a != axis) kept[nk++] = shape[a];
+  size_t kept_strides[TC_MAX_RANK];
+  contiguous_strides(nk, kept, kept_strides);
+  size_t to[TC_MAX_RANK]; uint32_t next = 0;
+  for (uint32_t a = 0; a < rank; ++a) to[a] = a == axis ? 0 : kept_strides[next++];
+  size_t along[TC_MAX_RANK] = {0};
+  along[axis] = 1;
+  size_t results = element_count(nk, kept);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    std::vector<float> best(results, NAN);
+    for (size_t r = 0; r < results; ++r) out[r] = 0;
+    const size_t *st[3] = {strides, to, along};
+    size_t off[3] = {offset, 0, 0};
+    for_each_run<3>(rank, shape, off, st, [&](const size_t *at, size_t len, const size_t *steps) {
+      for (size_t i = 0; i < len; ++i) {
+        size_t slot = at[1] + i * steps[1];
+        float x = T::load(input, at[0] + i * steps[0]);
+        bool replaces = !std::isnan(x) &&
+                        (std::isnan(best[slot]) || (op == TC_RMIN ? x < best[slot] : x > best[slot]));
+        if (replaces) { best[slot] = x; out[slot] = uint32_t(at[2] + i * steps[2]); }
+      }
+    });
+    return int(TC_OK);
+  });
+}
+
+int orc_matmul_rows(int dtype, size_t rows, size_t inner, size_t cols, const void *a,
+                    const void *b, void *c, int accumulate, size_t row0, size_t row1) {
+  if (row1 > rows || row0 > row1) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    return matmul_rows<decltype(t)>(rows, inner, cols, a, b, c, accumulate != 0, row0, row1);
+  });
+}
+
+// Kernels::matmul / matmul_add / matmul_transposed_add on Host
+// (kernels.rs:1441-1507): the transposed forms copy the operand transposed
+// first (the trait default, kernels.rs:975-985).
+int orc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
+               const void *a, const void *b, void *c, int accumulate) {
+  if (transposed < TC_TRANS_NONE || transposed > TC_TRANS_RIGHT) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    bool acc = accumulate != 0;
+    if (transposed == TC_TRANS_LEFT) {
+      auto at = transposed_copy<T>(a, inner, rows);
+      return matmul_rows<T>(rows, inner, cols, at.data(), b, c, acc, 0, rows);
+    }
+    if (transposed == TC_TRANS_RIGHT) {
+      auto bt = transposed_copy<T>(b, cols, inner);
+      return matmul_rows<T>(rows, inner, cols, a, bt.data(), c, acc, 0, rows);
+    }
+    return matmul_rows<T>(rows, inner, cols, a, b, c, acc, 0, rows);
+  });
+}
+
+// Matrix::matvec / matvec_add (matrix.rs:675-730): f16/bf16 through
+// compact::matmul with one column (the i-p-j tail: a running `out += a*x`
+// per row, from the widened addend when accumulating); f32 through
+// simd_dispatch::matvec (a SIMD dot per row, simd_dispatch.rs:626-660) at or
+// above 512 elements, else the scalar running sum.
+int orc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x, void *y,
+               int accumulate) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    if (!std::is_same<T, F32>::value)
+      return matmul_rows<T>(rows, cols, 1, m, x, y, accumulate != 0, 0, rows);
+    const float *mm = static_cast<const float *>(m), *xx = static_cast<const float *>(x);
+    float *yy = static_cast<float *>(y);
+    bool simd = rows * cols >= MIN_MATMUL_OPS;
+    for (size_t i = 0; i < rows; ++i) {
+      float s;
+      if (simd) s = dot_f32(mm + i * cols, xx, cols);
+      else { s = 0.0f; for (size_t p = 0; p < cols; ++p) s = s + mm[i * cols + p] * xx[p]; }
+      yy[i] = accumulate ? yy[i] + s : s;
+    }
+    return int(TC_OK);
+  });
+}
+
+// Vector::vecmat (vector.rs:491-515): compact::matmul / simd vecmat = the
+// (1 x rows)·(rows x cols) i-p-j product; else the scalar per-column sum.
+int orc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m, void *y) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    if (!std::is_same<T, F32>::value || rows * cols >= MIN_MATMUL_OPS)
+      return matmul_rows<T>(1, rows, cols, x, m, y, false, 0, 1);
+    const float *xx = static_cast<const float *>(x), *mm = static_cast<const float *>(m);
+    float *yy = static_cast<float *>(y);
+    for (size_t j = 0; j < cols; ++j) {
+      float s = 0.0f;
+      for (size_t p = 0; p < rows; ++p) s = s + xx[p] * mm[p * cols + j];
+      yy[j] = s;
+    }
+    return int(TC_OK);
+  });
+}
+
+// Matrix::transpose (matrix.rs:740-745): moves bits.
+int orc_transpose(int dtype, size_t rows, size_t cols, const void *m, void *out) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    auto tr = transposed_copy<T>(m, rows, cols);
+    std::memcpy(out, tr.data(), tr.size() * sizeof(typename T::S));
+    return int(TC_OK);
+  });
+}
+
+// Adam's program as built (optim.rs:1048-1099), every operation in the
+// element type, in the program's order:
+//   first_share = 1 - beta1; second_share = 1 - beta2      (constants)
+//   fresh_first = g*first_share; squared = g*g; fresh_second = squared*second_share
+//   resumed: first = m*beta1 + fresh_first; second = v*beta2 + fresh_second
+//   else:    first = fresh_first; second = fresh_second
+//   step = (first*c1) / (sqrt(second*c2) + eps) * rate;  p = p - step
+int orc_adam(int dtype, size_t n, void *p, const void *g, void *m, void *v, int resumed,
+             double rate, double beta1, double beta2, double eps, double c1, double c2) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    const float one = 1.0f;
+    float r = float(rate), b1 = float(beta1), b2 = float(beta2), e = float(eps);
+    float k1 = float(c1), k2 = float(c2);
+    float first_share = T::round(one - b1), second_share = T::round(one - b2);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) {
+        float gi = T::load(g, i);
+        float fresh_first = T::round(gi * first_share);
+        float squared = T::round(gi * gi);
+        float fresh_second = T::round(squared * second_share);
+        float first, second;
+        if (resumed) {
+          first = T::round(T::round(T::load(m, i) * b1) + fresh_first);
+          second = T::round(T::round(T::load(v, i) * b2) + fresh_second);
+        } else {
+          first = fresh_first;
+          second = fresh_second;
+        }
+        float cf = T::round(first * k1);
+        float cs = T::round(second * k2);
+        float root = T::round(std::sqrt(cs));
+        float den = T::round(root + e);
+        float step = T::round(T::round(cf / den) * r);
+        T::store(p, i, T::load(p, i) - step);
+        T::store(m, i, first);
+        T::store(v, i, second);
+      }
+    });
+    return int(TC_OK);
+  });
+}
+
+// Sgd's program (optim.rs:773-787): step = g·rate (Builder::scale), p - step.
+int orc_sgd(int dtype, size_t n, void *p, const void *g, double rate) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    float r = float(rate);
+    split(n, [&](size_t lo, size_t hi) {
+      for (size_t i = lo; i < hi; ++i) {
+        float step = T::round(T::load(g, i) * r);
+        T::store(p, i, T::load(p, i) - step);
+      }
+    });
+    return int(TC_OK);
+  });
+}
+
+// Adam::update's host arithmetic (optim.rs:1106-1124).  The coefficients are
+// values of the element type (Adam::new rounds 0.9/0.999/1e-8 into it,
+// optim.rs:1029-1035); `powi` is f32 powi then a rounding for f16/bf16
+// (crate half) and compiler-rt's __powisf2 square-and-multiply for f32;
+// `one - x` and `.recip()` round in the element type.
+int orc_adam_coefficients(int dtype, double rate, double beta1, double beta2, double eps,
+                          uint32_t step, double *out) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    auto powi = [](float a, int b) {
+      bool recip = b < 0;
+      float r = 1.0f;
+      for (;;) {
+        if (b & 1) r *= a;
+        b /= 2;
+        if (b == 0) break;
+        a *= a;
+      }
+      return recip ? 1.0f / r : r;
+    };
+    float r = from_f64<T>(rate), b1 = from_f64<T>(beta1), b2 = from_f64<T>(beta2);
+    float e = from_f64<T>(eps);
+    float c1 = T::round(1.0f - T::round(powi(b1, int(step))));
+    float c2 = T::round(1.0f - T::round(powi(b2, int(step))));
+    out[0] = r; out[1] = b1; out[2] = b2; out[3] = e;
+    out[4] = T::round(1.0f / c1);
+    out[5] = T::round(1.0f / c2);
+    return int(TC_OK);
+  });
+}
+
+}  // extern "C"

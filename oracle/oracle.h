@@ -1,0 +1,101 @@
+/*
+ * oracle.h — CPU restatement of tensorcrate's Host backend for the hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker the CUDA backend is
+ * compared against, and the timed CPU baseline; nothing in the product
+ * (libtccuda, the tensorcrate_b200 package) links, loads or calls it.
+ *
+ * Each function restates the reference's Host algorithm it names
+ * (file:line inside the tensorcrate crate), in the same arithmetic order, so
+ * that integer, bit and comparison work is bit-identical and floating-point
+ * work rounds where the reference rounds.  The enums, dtype codes and the
+ * region struct are the public ones of include/tccuda.h.
+ */
+#ifndef TC_ORACLE_H
+#define TC_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../include/tccuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* f16/bf16 <-> f32, as crate `half` 2.7.1 converts (round to nearest even,
+ * NaN kept quiet with its payload). */
+void orc_narrow(int dtype, const float *in, void *out, size_t n);
+void orc_widen(int dtype, const void *in, float *out, size_t n);
+
+/* layout.rs */
+int orc_coalesce(uint32_t rank, const size_t *shape, uint32_t n_ops, const size_t *strides,
+                 uint32_t *out_rank, size_t *out_shape, size_t *out_strides);
+int orc_broadcast_shape(uint32_t lrank, const size_t *left, uint32_t rrank, const size_t *right,
+                        uint32_t *out_rank, size_t *out_shape);
+int orc_broadcast_strides(uint32_t rank, const size_t *shape, const size_t *strides,
+                          uint32_t trank, const size_t *target, size_t *out_strides);
+/* The walk for_each_run makes: every storage position, in order. */
+int orc_walk(uint32_t rank, const size_t *shape, size_t offset, const size_t *strides,
+             size_t *out_positions);
+
+/* backend.rs */
+int orc_strided_copy(size_t elem_bytes, uint32_t rank, const size_t *shape, const void *src,
+                     size_t src_len, size_t src_offset, const size_t *src_strides, void *dst);
+int orc_strided_write(size_t elem_bytes, void *target, size_t target_len, const tc_region *region);
+int orc_assemble(size_t elem_bytes, void *dst, size_t len, const tc_region *regions, size_t n);
+
+/* kernels.rs / simd_dispatch.rs same-shape elementwise */
+int orc_elementwise(int dtype, int op, const void *a, const void *b, void *out, size_t n);
+int orc_broadcast_scalar(int dtype, int op, const void *a, double scalar, int scalar_left,
+                         void *out, size_t n);
+int orc_compare(int dtype, int cmp, const void *a, const void *b, void *out, size_t n);
+int orc_compare_scalar(int dtype, int cmp, const void *a, double scalar, int scalar_left,
+                       void *out, size_t n);
+int orc_clamp(int dtype, const void *a, double low, double high, void *out, size_t n);
+int orc_vector_reduce(int dtype, int op, const void *a, size_t n, void *out);
+int orc_dot(int dtype, const void *a, const void *b, size_t n, void *out);
+
+/* strided.rs */
+int orc_strided_binary(int dtype, int kind, int op, uint32_t rank, const size_t *shape,
+                       const void *a, size_t a_len, size_t a_offset, const size_t *a_strides,
+                       const void *b, size_t b_len, size_t b_offset, const size_t *b_strides,
+                       void *out);
+int orc_reduce_axes(int dtype, uint32_t rank, const size_t *shape, const void *input,
+                    size_t input_len, size_t offset, const size_t *strides, uint32_t n_axes,
+                    const uint32_t *axes, int kind, int op, size_t divisor, void *out);
+int orc_arg_reduce(int dtype, uint32_t rank, const size_t *shape, const void *input,
+                   size_t input_len, size_t offset, const size_t *strides, uint32_t axis, int op,
+                   uint32_t *out);
+
+/* matrix.rs / simd_x86.rs / compact.rs products */
+int orc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
+               const void *a, const void *b, void *c, int accumulate);
+/* The same product over a band of output rows [row0, row1) only: rows of
+ * the i-p-j loop are independent, so a band times the whole. */
+int orc_matmul_rows(int dtype, size_t rows, size_t inner, size_t cols, const void *a,
+                    const void *b, void *c, int accumulate, size_t row0, size_t row1);
+int orc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x, void *y,
+               int accumulate);
+int orc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m, void *y);
+int orc_transpose(int dtype, size_t rows, size_t cols, const void *m, void *out);
+
+/* optim.rs */
+int orc_adam(int dtype, size_t n, void *p, const void *g, void *m, void *v, int resumed,
+             double rate, double beta1, double beta2, double eps, double c1, double c2);
+int orc_sgd(int dtype, size_t n, void *p, const void *g, double rate);
+/* Adam::update's host arithmetic (optim.rs:1106-1124): for step t, the two
+ * corrections (1 - beta^t).recip() rounded in the element type, and the
+ * element-type values of the coefficients.  out[0..6] = rate, beta1, beta2,
+ * eps, c1, c2 as doubles holding element-type values. */
+int orc_adam_coefficients(int dtype, double rate, double beta1, double beta2, double eps,
+                          uint32_t step, double *out);
+
+/* Host threads the elementwise kernels may use (set_host_threads,
+ * src/parallel.rs:40); 0 = all. */
+void orc_set_threads(int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

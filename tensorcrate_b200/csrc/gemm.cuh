@@ -1,0 +1,13 @@
+// gemm.cuh — the product kernels behind tc_matmul: tcgen05 tensor-core tiles
+// for f16/bf16 (gemm_sm100.cu) and FP32 CUDA-core tiles (gemm_simt.cu).
+#pragma once
+#include "common.cuh"
+
+namespace tc {
+int gemm_simt_run(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                  void *c, bool accumulate, cudaStream_t stream);
+// TC_ENOTSUP when the shape or alignment is not one the tensor-core kernel
+// tiles; the caller then runs the SIMT kernel.
+int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                void *c, bool accumulate, cudaStream_t stream);
+}  // namespace tc

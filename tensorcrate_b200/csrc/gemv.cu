@@ -1,0 +1,142 @@
+// gemv.cu — matrix-vector products (Kernels::matvec / matvec_add,
+// kernels.rs:901-908; Kernels::vecmat, kernels.rs:899) and the tc_matmul
+// entry point that routes products to the GEMM kernels.
+//
+// Both GEMVs are HBM-bound: the matrix is read once with 128-bit loads.
+//  - matvec: a warp per row, the row streamed in packs, a shuffle tree.
+//  - vecmat: each thread owns adjacent output columns; the block's warps
+//    split the rows and combine in shared memory, so every row read is
+//    one coalesced segment.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace tc {
+namespace {
+
+template <class T> struct Pack {
+  using S = typename T::S;
+  static constexpr int N = 16 / int(sizeof(S));
+  union { uint4 raw; S v[N]; };
+};
+
+template <class T>
+__global__ void __launch_bounds__(256) matvec_rows(const typename T::S *m, const typename T::S *x,
+                                                   typename T::S *y, long long rows, long long cols,
+                                                   bool accumulate, bool vec) {
+  constexpr int N = Pack<T>::N;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const typename T::S *row = m + r * cols;
+    float s = 0.0f;
+    if (vec) {
+      for (long long p = lane; p < cols / N; p += 32) {
+        Pack<T> a, b;
+        a.raw = __ldg(reinterpret_cast<const uint4 *>(row + p * N));
+        b.raw = __ldg(reinterpret_cast<const uint4 *>(x + p * N));
+#pragma unroll
+        for (int j = 0; j < N; ++j) s = fmaf(T::load(a.v[j]), T::load(b.v[j]), s);
+      }
+    } else {
+      for (long long c = lane; c < cols; c += 32) s = fmaf(T::load(row[c]), T::load(x[c]), s);
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    if (lane == 0) {
+      if (accumulate) s = __fadd_rn(T::load(y[r]), s);
+      y[r] = T::store(s);
+    }
+  }
+}
+
+// y[j] = sum_p x[p] * m[p, j].  blockDim = (32, 8): x walks 32 adjacent
+// columns, y splits the rows.
+template <class T>
+__global__ void __launch_bounds__(256) vecmat_cols(const typename T::S *x, const typename T::S *m,
+                                                   typename T::S *y, long long rows, long long cols) {
+  __shared__ float part[8][33];
+  long long j = (long long)blockIdx.x * 32 + threadIdx.x;
+  float s = 0.0f;
+  if (j < cols) {
+    long long p = threadIdx.y;
+    for (; p + 24 < rows; p += 32) {
+      float a0 = T::load(__ldg(m + p * cols + j)), a1 = T::load(__ldg(m + (p + 8) * cols + j));
+      float a2 = T::load(__ldg(m + (p + 16) * cols + j)), a3 = T::load(__ldg(m + (p + 24) * cols + j));
+      s = fmaf(T::load(x[p]), a0, s);
+      s = fmaf(T::load(x[p + 8]), a1, s);
+      s = fmaf(T::load(x[p + 16]), a2, s);
+      s = fmaf(T::load(x[p + 24]), a3, s);
+    }
+    for (; p < rows; p += 8) s = fmaf(T::load(x[p]), T::load(__ldg(m + p * cols + j)), s);
+  }
+  part[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && j < cols) {
+    float t = part[0][threadIdx.x];
+    for (int k = 1; k < 8; ++k) t += part[k][threadIdx.x];
+    y[j] = T::store(t);
+  }
+}
+
+}  // namespace
+}  // namespace tc
+
+using namespace tc;
+
+extern "C" {
+
+int tc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x, void *y, int accumulate,
+              void *stream) {
+  if (rows == 0) return TC_OK;
+  if (!m || !x || !y) return fail(TC_EINVAL, "matvec: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    constexpr int N = Pack<T>::N;
+    bool vec = cols % N == 0 && (uintptr_t(m) & 15u) == 0 && (uintptr_t(x) & 15u) == 0;
+    unsigned grid = unsigned(std::min<long long>(((long long)rows + 7) / 8, (long long)sm_count() * 8));
+    matvec_rows<T><<<std::max(1u, grid), 256, 0, as_stream(stream)>>>(
+        static_cast<const S *>(m), static_cast<const S *>(x), static_cast<S *>(y), (long long)rows,
+        (long long)cols, accumulate != 0, vec);
+    return check_launch("matvec");
+  });
+}
+
+int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m, void *y, void *stream) {
+  if (cols == 0) return TC_OK;
+  if (!m || !x || !y) return fail(TC_EINVAL, "vecmat: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    unsigned grid = unsigned(((long long)cols + 31) / 32);
+    vecmat_cols<T><<<grid, dim3(32, 8), 0, as_stream(stream)>>>(static_cast<const S *>(x),
+                                                                 static_cast<const S *>(m), static_cast<S *>(y),
+                                                                 (long long)rows, (long long)cols);
+    return check_launch("vecmat");
+  });
+}
+
+int tc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+              void *c, int accumulate, void *stream) {
+  if (transposed < TC_TRANS_NONE || transposed > TC_TRANS_RIGHT)
+    return fail(TC_EINVAL, "matmul: bad Transposed %d", transposed);
+  if (dtype != TC_F32 && dtype != TC_F16 && dtype != TC_BF16) return fail(TC_EINVAL, "matmul: element type %d", dtype);
+  if (rows == 0 || cols == 0) return TC_OK;
+  if (!c) return fail(TC_EINVAL, "matmul: null output");
+  if (inner == 0) {
+    // An empty inner dimension: the product is zero.
+    if (accumulate) return TC_OK;
+    return check_cuda(cudaMemsetAsync(c, 0, rows * cols * dtype_bytes(dtype), as_stream(stream)), "memset");
+  }
+  if (!a || !b) return fail(TC_EINVAL, "matmul: null operand");
+  cudaStream_t s = as_stream(stream);
+  if (dtype != TC_F32) {
+    int st = gemm_tc_run(dtype, transposed, rows, inner, cols, a, b, c, accumulate != 0, s);
+    if (st != TC_ENOTSUP) return st;
+  }
+  return gemm_simt_run(dtype, transposed, rows, inner, cols, a, b, c, accumulate != 0, s);
+}
+
+}  // extern "C"

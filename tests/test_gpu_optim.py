@@ -1,0 +1,56 @@
+"""The fused Adam and SGD updates against the oracle's restatement of the
+programs (optim.rs:1048-1099, 773-787): every operation rounds to the
+element type in the program's order, so the updates agree bit for bit."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tensorcrate_b200 import cuda
+from tensorcrate_b200 import _native as N
+from util import DTYPES, normal
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("n", [1, 13, 4096 + 3, 250000])
+def test_adam_steps_match_bit_for_bit(device, dtype, n):
+    # beta2 = 0.99 keeps the bf16 run finite (0.999 rounds to 1.0 in bf16).
+    beta2 = 0.99 if dtype == "bf16" else 0.999
+    p = O.narrow(normal(n, 1), dtype)
+    dp = cuda.CudaStorage.store(p, dtype)
+    dm, dv = cuda.CudaStorage.zeros(dtype, n), cuda.CudaStorage.zeros(dtype, n)
+    m, v = np.zeros_like(p), np.zeros_like(p)
+    for step in range(1, 4):
+        g = O.narrow(normal(n, 10 + step) * 0.1, dtype)
+        dg = cuda.CudaStorage.store(g, dtype)
+        coef = O.adam_coefficients(dtype, 1e-3, 0.9, beta2, 1e-8, step)
+        resumed = int(step > 1)
+        N.call("tc_adam", N.DTYPES[dtype], n, dp.ptr, dg.ptr, dm.ptr, dv.ptr, resumed, *coef, None)
+        O.call("orc_adam", O.DTYPES[dtype], n, O.ptr(p), O.ptr(g), O.ptr(m), O.ptr(v), resumed, *coef)
+        assert np.array_equal(dp.as_slice(), p), f"p at step {step}"
+        assert np.array_equal(dm.as_slice(), m), f"m at step {step}"
+        assert np.array_equal(dv.as_slice(), v), f"v at step {step}"
+
+
+def test_bf16_adam_with_default_betas_is_nan_like_the_reference(device):
+    coef = O.adam_coefficients("bf16", 1e-3, 0.9, 0.999, 1e-8, 1)
+    p = O.narrow(normal(64, 1), "bf16")
+    g = O.narrow(normal(64, 2), "bf16")
+    dp, dg = cuda.CudaStorage.store(p, "bf16"), cuda.CudaStorage.store(g, "bf16")
+    dm, dv = cuda.CudaStorage.zeros("bf16", 64), cuda.CudaStorage.zeros("bf16", 64)
+    N.call("tc_adam", N.BF16, 64, dp.ptr, dg.ptr, dm.ptr, dv.ptr, 0, *coef, None)
+    assert np.all(np.isnan(O.widen(dp.as_slice(), "bf16")))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_sgd_matches_bit_for_bit(device, dtype):
+    n = 10007
+    p = O.narrow(normal(n, 3), dtype)
+    g = O.narrow(normal(n, 4), dtype)
+    dp, dg = cuda.CudaStorage.store(p, dtype), cuda.CudaStorage.store(g, dtype)
+    N.call("tc_sgd", N.DTYPES[dtype], n, dp.ptr, dg.ptr, 0.01, None)
+    O.call("orc_sgd", O.DTYPES[dtype], n, O.ptr(p), O.ptr(g), 0.01)
+    assert np.array_equal(dp.as_slice(), p)

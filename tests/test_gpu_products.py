@@ -1,0 +1,80 @@
+"""Products against the oracle: matmul, matmul_add and
+matmul_transposed_add in f32 (rel 1e-5*sqrt(K)) and f16/bf16 (half
+precision tolerance of the f32-accumulated, once-rounded result,
+src/compact.rs:232-253); matvec and vecmat."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tensorcrate_b200 import cuda
+from tensorcrate_b200 import _native as N
+from util import DTYPES, uniform
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 1, 1), (7, 5, 3), (96, 96, 96), (128, 64, 256), (129, 200, 257), (256, 512, 384), (300, 1024, 520),
+          (1024, 1024, 1024)]
+
+
+def _tol(dtype, k):
+    return {"f32": 1e-5 * np.sqrt(k), "f16": 2.0 ** -10 * 2, "bf16": 2.0 ** -7 * 2}[dtype]
+
+
+def _run(dtype, transposed, m, k, n, accumulate, seed):
+    a_shape = (k, m) if transposed == N.TRANS_LEFT else (m, k)
+    b_shape = (n, k) if transposed == N.TRANS_RIGHT else (k, n)
+    a = O.narrow(uniform(a_shape, seed), dtype)
+    b = O.narrow(uniform(b_shape, seed + 1), dtype)
+    c0 = O.narrow(uniform((m, n), seed + 2), dtype)
+    da, db = cuda.CudaStorage.store(a, dtype), cuda.CudaStorage.store(b, dtype)
+    dc = cuda.CudaStorage.store(c0, dtype) if accumulate else None
+    got = O.widen(cuda.Cuda.matmul(da, db, m, k, n, transposed, dc).as_slice(), dtype)
+    want = O.widen(O.matmul(dtype, transposed, m, k, n, a, b, c0 if accumulate else None, accumulate), dtype)
+    return got, want
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_matmul(device, dtype, m, k, n):
+    got, want = _run(dtype, N.TRANS_NONE, m, k, n, False, m + k + n)
+    scale = max(1.0, float(np.max(np.abs(want))))
+    assert np.max(np.abs(got - want)) <= _tol(dtype, k) * scale
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("transposed", [N.TRANS_NONE, N.TRANS_LEFT, N.TRANS_RIGHT])
+@pytest.mark.parametrize("m,k,n", [(7, 5, 3), (130, 96, 72), (256, 320, 512)])
+def test_transposed_accumulating_products(device, dtype, transposed, m, k, n):
+    """The tape's backward products (tape/mod.rs:1195-1216)."""
+    got, want = _run(dtype, transposed, m, k, n, True, 3 * m + k)
+    scale = max(1.0, float(np.max(np.abs(want))))
+    assert np.max(np.abs(got - want)) <= _tol(dtype, k) * scale
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(1, 1), (7, 13), (1024, 1024), (333, 4096)])
+def test_matvec_and_vecmat(device, dtype, rows, cols):
+    m = O.narrow(uniform((rows, cols), 1), dtype)
+    x = O.narrow(uniform(cols, 2), dtype)
+    y0 = O.narrow(uniform(rows, 3), dtype)
+    dm, dx = cuda.CudaStorage.store(m, dtype), cuda.CudaStorage.store(x, dtype)
+    got = O.widen(cuda.Cuda.matvec(dm, dx, rows, cols).as_slice(), dtype)
+    want = np.empty(rows, m.dtype)
+    O.call("orc_matvec", O.DTYPES[dtype], rows, cols, O.ptr(m), O.ptr(x), O.ptr(want), 0)
+    want = O.widen(want, dtype)
+    assert np.max(np.abs(got - want)) <= _tol(dtype, cols) * max(1.0, np.max(np.abs(want)))
+    dy = cuda.CudaStorage.store(y0, dtype)
+    got = O.widen(cuda.Cuda.matvec(dm, dx, rows, cols, addend=dy).as_slice(), dtype)
+    want = y0.copy()
+    O.call("orc_matvec", O.DTYPES[dtype], rows, cols, O.ptr(m), O.ptr(x), O.ptr(want), 1)
+    want = O.widen(want, dtype)
+    assert np.max(np.abs(got - want)) <= _tol(dtype, cols) * max(1.0, np.max(np.abs(want)))
+    v = O.narrow(uniform(rows, 4), dtype)
+    dv = cuda.CudaStorage.store(v, dtype)
+    got = O.widen(cuda.Cuda.vecmat(dv, dm, rows, cols).as_slice(), dtype)
+    want = np.empty(cols, m.dtype)
+    O.call("orc_vecmat", O.DTYPES[dtype], rows, cols, O.ptr(v), O.ptr(m), O.ptr(want))
+    want = O.widen(want, dtype)
+    assert np.max(np.abs(got - want)) <= _tol(dtype, rows) * max(1.0, np.max(np.abs(want)))
