@@ -133,9 +133,9 @@ int tc_strided_write(size_t elem_bytes, void *target, size_t target_len,
                      const tc_region *region, void *stream);
 
 /* `Backend::assemble` (src/tensors/backend.rs:157-160; Host assemble_slices
- * :303-323): a new storage of `len` elements built from `n` regions.  Every
- * region is copied in one launch; elements no region writes are left as they
- * were in `dst` (the reference leaves them unspecified). */
+ * :303-323): a new storage of `len` elements built from `n` regions, each
+ * region one copy launch; elements no region writes are left as they were in
+ * `dst` (the reference leaves them unspecified). */
 int tc_assemble(size_t elem_bytes, void *dst, size_t len, const tc_region *regions,
                 size_t n, void *stream);
 
@@ -228,6 +228,12 @@ int tc_adam(int dtype, size_t n, void *p, const void *g, void *m, void *v, int r
             double second_correction, void *stream);
 /* Sgd's fused program (optim.rs:773-787): p <- p - g·rate. */
 int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *stream);
+
+/* Status of bounded device-side waits since the library loaded: TC_ETIMEOUT
+ * (and *fault = 1) if a tensor-core GEMM gave up waiting on its pipeline
+ * and returned early; TC_OK otherwise.  No counterpart in the reference
+ * (Metal reports async errors at the next sync, src/metal/mod.rs:17-21). */
+int tc_device_status(int *fault);
 
 /* ---- layout helpers (host only; src/tensors/layout.rs) ------------------ */
 /* `coalesce` (layout.rs:419-446) for n_ops operands whose strides are

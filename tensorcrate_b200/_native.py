@@ -81,6 +81,7 @@ SIGNATURES = {
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],
     "tc_sgd": [_i, _sz, _p, _p, _d, _p],
     "tc_coalesce": [_u32, _szp, _u32, _szp, _u32p, _szp, _szp],
+    "tc_device_status": [C.POINTER(_i)],
     "tc_comm_unique_id": [C.POINTER(C.c_uint8)],
     "tc_comm_init": [_i, _i, C.POINTER(C.c_uint8), C.POINTER(_p)],
     "tc_comm_destroy": [_p],

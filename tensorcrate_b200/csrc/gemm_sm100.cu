@@ -1,7 +1,465 @@
-// placeholder until the tcgen05 kernel lands
+// gemm_sm100.cu — f16/bf16 products on the 5th-generation tensor cores:
+// Kernels::matmul / matmul_add / matmul_transposed_add (kernels.rs:956-985)
+// for the compact types, f32 accumulation, each output rounded once
+// (compact::matmul, src/compact.rs:232-253).
+//
+// One persistent CTA per SM, warp-specialised:
+//   warp 0      TMA producer: 128-byte-swizzled tiles of A and B into a ring
+//               of shared-memory stages (cp.async.bulk.tensor, no multicast).
+//   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
+//               K=16) into an f32 accumulator in TMEM and commits each stage
+//               back to the producer and each finished tile to the epilogue.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp its 32
+//               TMEM lanes), + C when accumulating, round, store.
+// Two accumulators in TMEM let the epilogue of one tile overlap the main
+// loop of the next.
+//
+// Operands are read where they lie: a row-major [M,K] A or [N,K] B is
+// "K-major"; A stored [K,M] (Transposed::Left) or B stored [K,N] (the plain
+// product) is "MN-major", which the UMMA descriptors express with their
+// leading/stride byte offsets, so no transpose copy is made.
+//
+// Every wait on an mbarrier is bounded: on expiry the kernel records the
+// failure in a device flag (read by tc_device_status), every role stops,
+// in-flight copies and MMAs are waited for (again bounded) and TMEM is freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "gemm.cuh"
+
 namespace tc {
-int gemm_tc_run(int, int, size_t, size_t, size_t, const void *, const void *, void *, bool, cudaStream_t) {
-  return TC_ENOTSUP;
+
+__device__ int g_gemm_fault = 0;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 f16/bf16 = 128 bytes: one swizzle row
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
+constexpr uint32_t WAIT_SPINS = 1u << 30;   // and never more spins than this
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase of `bar` with `parity`.  False if the CTA is aborting,
+// or if WAIT_NS pass first: that records the fault and starts the abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  for (uint32_t i = 1; i < WAIT_SPINS; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (now_ns() - t0 > WAIT_NS) break;
+    }
+  }
+  *abort_flag = 1;
+  atomicExch(&g_gemm_fault, 1);
+  return false;
+}
+// The same wait with no abort check, for draining in-flight work.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = now_ns();
+  for (uint32_t i = 0; i < WAIT_SPINS; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 63u) == 0 && now_ns() - t0 > WAIT_NS) return;
+  }
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// The shared-memory matrix descriptor: start, leading and stride byte
+// offsets (>> 4), version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct Params {
+  int M, N, K;
+  int a_mn, b_mn;  // 1 = MN-major operand
+  int accumulate;
+  void *c;
+  int elem_is_bf16;
+  int vec_store;  // rows of C start 16-byte aligned
+};
+
+// Tile t of the persistent sequence -> (m block, n block), grouped along M
+// so that concurrently resident CTAs share B panels in L2.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
+  const int GROUP = 8;
+  int group_size = GROUP * num_n;
+  int group = t / group_size;
+  int first = group * GROUP;
+  int gm = min(num_m - first, GROUP);
+  int r = t - group * group_size;
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const Params p) {
+  constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *tiles = smem;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *acc_full = empty + STAGES;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int k_blocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], EPI_WARPS * 32);
+    }
+    mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch(&map_a);
+    tma_prefetch(&map_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled = 0, fill_parity = 0;  // per stage: a fill was issued, and its phase parity
+      for (int t = blockIdx.x; t < num_tiles && !abort_flag; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, &abort_flag)) break;
+          uint8_t *sa = tiles + stage * STAGE_BYTES;
+          uint8_t *sb = sa + A_BYTES;
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (p.a_mn) {
+            tma_load_2d(sa, &map_a, &full[stage], m0, k0);
+            tma_load_2d(sa + 64 * BK * 2, &map_a, &full[stage], m0 + 64, k0);
+          } else {
+            tma_load_2d(sa, &map_a, &full[stage], k0, m0);
+          }
+          if (p.b_mn) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * BK * 2, &map_b, &full[stage], n0 + 64 * j, k0);
+          } else {
+            tma_load_2d(sb, &map_b, &full[stage], k0, n0);
+          }
+          filled |= 1u << stage;
+          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // On an abort, let every copy this thread started land before the CTA
+      // exits: the phase a fill completes is the parity it was issued in.
+      if (abort_flag) {
+        for (int s = 0; s < STAGES; ++s)
+          if (filled & (1u << s)) mbar_drain(&full[s], (fill_parity >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (uint32_t(p.elem_is_bf16) << 7) | (uint32_t(p.elem_is_bf16) << 10) |
+                             (uint32_t(p.a_mn) << 15) | (uint32_t(p.b_mn) << 16) | (uint32_t(BN >> 3) << 17) |
+                             (uint32_t(BM >> 4) << 24);
+      // K advance per 16-element MMA step inside a stage: 32 bytes along a
+      // K-major row; 16 rows of 128 bytes down an MN-major tile.
+      const uint32_t a_step = p.a_mn ? 16 * 128 : 32, b_step = p.b_mn ? 16 * 128 : 32;
+      const uint32_t a_lbo = p.a_mn ? 64 * BK * 2 : 16, b_lbo = p.b_mn ? 64 * BK * 2 : 16;
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
+        const int buf = iter & 1;
+        const uint32_t use = uint32_t(iter >> 1);
+        // The accumulator must have been drained by the epilogue.
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, &abort_flag)) { ok = false; break; }
+        fence_after();
+        const uint32_t tmem_d = tmem_base + uint32_t(buf * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, &abort_flag)) { ok = false; break; }
+          fence_after();
+          const uint32_t sa = smem_u32(tiles + stage * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t da = smem_desc(sa + kk * a_step, a_lbo, 1024);
+            uint64_t db = smem_desc(sb + kk * b_step, b_lbo, 1024);
+            umma(tmem_d, da, db, idesc, (kb | kk) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+      // Drain: every MMA issued by this thread completes before TMEM is
+      // freed, whatever happened.
+      umma_commit(drain);
+      mbar_drain(drain, 0);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int iter = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
+      const int buf = iter & 1;
+      const uint32_t use = uint32_t(iter >> 1);
+      if (!mbar_wait(&acc_full[buf], use & 1u, &abort_flag)) break;
+      fence_after();
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int row = mb * BM + q * 32 + lane;
+      const int n0 = nb * BN;
+      const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
+      uint16_t *crow = static_cast<uint16_t *>(p.c) + size_t(row) * size_t(p.N);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + uint32_t(c * 32), r);
+        const int col0 = n0 + c * 32;
+        if (row < p.M && col0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          const bool whole = col0 + 32 <= p.N && p.vec_store;
+          if (p.accumulate) {
+            if (whole) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 old = *reinterpret_cast<const uint4 *>(crow + col0 + 8 * j);
+                const uint32_t w[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  uint16_t lo = uint16_t(w[h] & 0xffffu), hi = uint16_t(w[h] >> 16);
+                  float flo = p.elem_is_bf16 ? bf16_bits_to_f32(lo) : f16_bits_to_f32(lo);
+                  float fhi = p.elem_is_bf16 ? bf16_bits_to_f32(hi) : f16_bits_to_f32(hi);
+                  v[8 * j + 2 * h] = __fadd_rn(flo, v[8 * j + 2 * h]);
+                  v[8 * j + 2 * h + 1] = __fadd_rn(fhi, v[8 * j + 2 * h + 1]);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col0 + j < p.N) {
+                  uint16_t o = crow[col0 + j];
+                  v[j] = __fadd_rn(p.elem_is_bf16 ? bf16_bits_to_f32(o) : f16_bits_to_f32(o), v[j]);
+                }
+              }
+            }
+          }
+          if (whole) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t w[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                float a = v[8 * j + 2 * h], b = v[8 * j + 2 * h + 1];
+                uint32_t lo = p.elem_is_bf16 ? f32_to_bf16_bits(a) : f32_to_f16_bits(a);
+                uint32_t hi = p.elem_is_bf16 ? f32_to_bf16_bits(b) : f32_to_f16_bits(b);
+                w[h] = lo | (hi << 16);
+              }
+              *reinterpret_cast<uint4 *>(crow + col0 + 8 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) crow[col0 + j] = p.elem_is_bf16 ? f32_to_bf16_bits(v[j]) : f32_to_f16_bits(v[j]);
+          }
+        }
+      }
+      fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---- host: tensor maps -------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A 2-D map of a row-major [outer, inner] matrix with `box` = {64, box_outer}
+// and 128-byte swizzle.
+int make_map(CUtensorMap *map, const void *base, bool bf16, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return fail(TC_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TC_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return TC_OK;
+}
+
+template <int BN, int STAGES>
+int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, cudaStream_t stream) {
+  constexpr size_t smem = size_t(STAGES) * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    if (int st = check_cuda(cudaFuncSetAttribute(gemm_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(smem)),
+                            "cudaFuncSetAttribute"))
+      return st;
+    configured[dev & 63] = true;
+  }
+  int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  int grid = std::min(tiles, sm_count());
+  gemm_tc<BN, STAGES><<<grid, THREADS, smem, stream>>>(ma, mb, p);
+  return check_launch("gemm (tcgen05)");
+}
+
+}  // namespace
+
+int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                void *c, bool accumulate, cudaStream_t stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ENOTSUP;
+  if (inner < 16 || rows > 0x7fffffffu || cols > 0x7fffffffu || inner > 0x7fffffffu) return TC_ENOTSUP;
+  const bool a_mn = transposed == TC_TRANS_LEFT;   // A stored [K, M]
+  const bool b_mn = transposed != TC_TRANS_RIGHT;  // B stored [K, N]
+  // TMA: 16-byte aligned bases and row pitches.
+  const uint64_t a_inner = a_mn ? rows : inner, b_inner = b_mn ? cols : inner;
+  if ((uintptr_t(a) & 15u) || (uintptr_t(b) & 15u) || (a_inner * 2) % 16 || (b_inner * 2) % 16) return TC_ENOTSUP;
+  const bool bf16 = dtype == TC_BF16;
+  Params p;
+  p.M = int(rows);
+  p.N = int(cols);
+  p.K = int(inner);
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.accumulate = accumulate;
+  p.c = c;
+  p.elem_is_bf16 = bf16;
+  p.vec_store = (uintptr_t(c) & 15u) == 0 && (cols * 2) % 16 == 0;
+  // 128x256 tiles when they fill the machine, else 128x128.
+  const long long tiles256 = ((long long)(rows + BM - 1) / BM) * ((long long)(cols + 255) / 256);
+  const int BN = tiles256 >= sm_count() ? 256 : 128;
+  CUtensorMap ma, mb;
+  if (int st = a_mn ? make_map(&ma, a, bf16, rows, inner, BK) : make_map(&ma, a, bf16, inner, rows, BM)) return st;
+  if (int st = b_mn ? make_map(&mb, b, bf16, cols, inner, BK) : make_map(&mb, b, bf16, inner, cols, BN)) return st;
+  return BN == 256 ? launch<256, 4>(ma, mb, p, stream) : launch<128, 6>(ma, mb, p, stream);
+}
+
 }  // namespace tc
+
+extern "C" int tc_device_status(int *fault) {
+  int h = 0;
+  if (int st = tc::check_cuda(cudaMemcpyFromSymbol(&h, tc::g_gemm_fault, sizeof(int)), "cudaMemcpyFromSymbol"))
+    return st;
+  if (fault) *fault = h;
+  if (h) return tc::fail(TC_ETIMEOUT, "a tensor-core GEMM gave up waiting on its pipeline");
+  return TC_OK;
+}

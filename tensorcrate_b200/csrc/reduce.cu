@@ -24,6 +24,7 @@
 //  - walk: anything else; a warp per result over the decomposed folded
 //    index.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -140,7 +141,7 @@ template <class T> struct Pack {
 constexpr int CACHE_PACKS = 8;
 
 template <class T, bool BLOCK>
-__global__ void __launch_bounds__(256) reduce_rows(const typename T::S *in, Layout2 L, long long results,
+__global__ void __launch_bounds__(256, 2) reduce_rows(const typename T::S *in, Layout2 L, long long results,
                                                    long long outer, long long run, int mode, float count,
                                                    float divisor, typename T::S *out, uint32_t *arg_out,
                                                    bool vec) {
@@ -158,36 +159,65 @@ __global__ void __launch_bounds__(256) reduce_rows(const typename T::S *in, Layo
   for (long long r = group0; r < results; r += group_stride) {
     const S *base = in + kept_base(L.kept, r);
     Acc a = identity(fold_mode);
-    float cached[CACHE_PACKS * N];
+    Pack<T> cached[CACHE_PACKS];  // the slice, still in its storage form
     if (cache) {
-      // Pass one from memory into registers.
+      // Pass one from memory into registers: all loads first, then the sum.
+#pragma unroll
+      for (int k = 0; k < CACHE_PACKS; ++k) {
+        long long p = (long long)k * G + lane;
+        if (p * N < run) cached[k].raw = __ldg(reinterpret_cast<const uint4 *>(base + p * N));
+      }
 #pragma unroll
       for (int k = 0; k < CACHE_PACKS; ++k) {
         long long p = (long long)k * G + lane;
         if (p * N < run) {
-          Pack<T> x;
-          x.raw = __ldg(reinterpret_cast<const uint4 *>(base + p * N));
 #pragma unroll
-          for (int j = 0; j < N; ++j) {
-            float v = T::load(x.v[j]);
-            cached[k * N + j] = v;
-            a.v = __fadd_rn(a.v, v);
-          }
+          for (int j = 0; j < N; ++j) a.v = __fadd_rn(a.v, T::load(cached[k].v[j]));
         }
       }
     } else {
-      for (long long o = 0; o < outer; ++o) {
-        const S *rp = base + (outer > 1 ? kept_base(L.folded, o) : 0);
+      // The slice as one flat run of units (packs when vectorised, else
+      // elements): `outer` runs of `per_run` units.  U independent loads are
+      // issued before any is folded, so each thread keeps U requests in
+      // flight.
+      constexpr int U = 8;
+      const long long per_run = vec ? run / N : run;
+      const long long total = outer * per_run;
+      for (long long f0 = lane; f0 < total; f0 += (long long)G * U) {
         if (vec) {
-          long long packs = run / N;
-          for (long long p = lane; p < packs; p += G) {
-            Pack<T> x;
-            x.raw = __ldg(reinterpret_cast<const uint4 *>(rp + p * N));
+          Pack<T> x[U];
+          long long at[U];
 #pragma unroll
-            for (int j = 0; j < N; ++j) push(fold_mode, a, T::load(x.v[j]), uint32_t(p * N + j));
+          for (int u = 0; u < U; ++u) {
+            long long f = f0 + (long long)u * G;
+            if (f < total) {
+              long long o = outer > 1 ? f / per_run : 0, c = f - o * per_run;
+              at[u] = c * N;
+              x[u].raw = __ldg(reinterpret_cast<const uint4 *>(base + (outer > 1 ? kept_base(L.folded, o) : 0) + c * N));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if (f0 + (long long)u * G < total) {
+#pragma unroll
+              for (int j = 0; j < N; ++j) push(fold_mode, a, T::load(x[u].v[j]), uint32_t(at[u] + j));
+            }
           }
         } else {
-          for (long long c = lane; c < run; c += G) push(fold_mode, a, T::load(rp[c]), uint32_t(c));
+          float x[U];
+          long long at[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            long long f = f0 + (long long)u * G;
+            if (f < total) {
+              long long o = outer > 1 ? f / per_run : 0, c = f - o * per_run;
+              at[u] = c;
+              x[u] = T::load(base[(outer > 1 ? kept_base(L.folded, o) : 0) + c]);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (f0 + (long long)u * G < total) push(fold_mode, a, x[u], uint32_t(at[u]));
         }
       }
     }
@@ -203,7 +233,7 @@ __global__ void __launch_bounds__(256) reduce_rows(const typename T::S *in, Layo
           if (p * N < run) {
 #pragma unroll
             for (int j = 0; j < N; ++j) {
-              float dev = __fsub_rn(cached[k * N + j], mean);
+              float dev = __fsub_rn(T::load(cached[k].v[j]), mean);
               d.v = __fadd_rn(d.v, __fmul_rn(dev, dev));
             }
           }
@@ -232,70 +262,102 @@ __global__ void __launch_bounds__(256) reduce_rows(const typename T::S *in, Layo
 
 // ---------------------------------------------------------------------------
 // columns: results r = (outer kept index) * K + k with k along the kept axis
-// of stride 1.  blockDim = (32, Y): x walks 32 adjacent results, y splits
-// the folded range into Y shares.
+// of stride 1.  blockDim = (32, Y): x walks 32*CPT adjacent results (CPT per
+// thread, one vector load each), y splits the folded range into Y shares
+// that combine in shared memory in share order.
 // ---------------------------------------------------------------------------
-template <class T>
+template <class T, int CPT> struct Cols {
+  using S = typename T::S;
+  union { typename std::conditional<CPT * sizeof(S) == 16, uint4, typename std::conditional<CPT * sizeof(S) == 8, uint2, S>::type>::type raw; S v[CPT]; };
+};
+
+template <class T, int CPT>
 __global__ void __launch_bounds__(256) reduce_cols(const typename T::S *in, Layout2 L, long long kept_outer,
                                                    long long K, long long depth, int mode, float count,
                                                    float divisor, typename T::S *out, uint32_t *arg_out) {
   using S = typename T::S;
-  __shared__ Acc part[8][33];
+  using V = Cols<T, CPT>;
+  constexpr int W = 32 * CPT;
+  constexpr int U = 8;
+  __shared__ Acc part[8][W];
   const int Y = blockDim.y;
   const int fold_mode = (mode == MEAN || mode == VARIANCE) ? FOLD_SUM : mode;
-  const long long tiles_k = (K + 31) / 32;
+  const long long tiles_k = (K + W - 1) / W;
   const long long tiles = kept_outer * tiles_k;
   const long long share = (depth + Y - 1) / Y;
   const long long f0 = (long long)threadIdx.y * share, f1 = min(depth, f0 + share);
   for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
-    long long ko = t / tiles_k, k = (t - ko * tiles_k) * 32 + threadIdx.x;
-    bool live = k < K;
+    const long long ko = t / tiles_k;
+    const long long k = (t - ko * tiles_k) * W + (long long)threadIdx.x * CPT;
+    const bool live = k < K;  // CPT divides K when CPT > 1
     const S *base = in + kept_base(L.kept, ko) + (live ? k : 0);
-    Acc a = identity(fold_mode);
+    Acc a[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) a[c] = identity(fold_mode);
     if (live) {
-      long long f = f0;
-      // Unrolled so that several independent loads are in flight.
-      for (; f + 4 <= f1; f += 4) {
-        long long p[4];
+      for (long long f = f0; f < f1; f += U) {
+        V x[U];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) p[u] = kept_base(L.folded, f + u);
-        float x[4];
+        for (int u = 0; u < U; ++u)
+          if (f + u < f1) x[u].raw = __ldg(reinterpret_cast<const decltype(V::raw) *>(base + kept_base(L.folded, f + u)));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = T::load(__ldg(base + p[u]));
+        for (int u = 0; u < U; ++u)
+          if (f + u < f1) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) push(fold_mode, a, x[u], uint32_t(f + u));
-      }
-      for (; f < f1; ++f) {
-        push(fold_mode, a, T::load(__ldg(base + kept_base(L.folded, f))), uint32_t(f));
+            for (int c = 0; c < CPT; ++c) push(fold_mode, a[c], T::load(x[u].v[c]), uint32_t(f + u));
+          }
       }
     }
-    part[threadIdx.y][threadIdx.x] = a;
+    float result[CPT];
+    Acc total[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) part[threadIdx.y][threadIdx.x * CPT + c] = a[c];
     __syncthreads();
-    Acc total = part[0][threadIdx.x];
-    for (int y = 1; y < Y; ++y) total = merge(fold_mode, total, part[y][threadIdx.x]);
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      total[c] = part[0][threadIdx.x * CPT + c];
+      for (int y = 1; y < Y; ++y) total[c] = merge(fold_mode, total[c], part[y][threadIdx.x * CPT + c]);
+    }
     __syncthreads();
-    float result;
     if (mode == VARIANCE) {
-      float mean = __fdiv_rn(total.v, count);
-      Acc d = identity(FOLD_SUM);
+      float mean[CPT];
+      Acc d[CPT];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        mean[c] = __fdiv_rn(total[c].v, count);
+        d[c] = identity(FOLD_SUM);
+      }
       if (live)
         for (long long f = f0; f < f1; ++f) {
-          float dev = __fsub_rn(T::load(__ldg(base + kept_base(L.folded, f))), mean);
-          d.v = __fadd_rn(d.v, __fmul_rn(dev, dev));
+          V x;
+          x.raw = __ldg(reinterpret_cast<const decltype(V::raw) *>(base + kept_base(L.folded, f)));
+#pragma unroll
+          for (int c = 0; c < CPT; ++c) {
+            float dev = __fsub_rn(T::load(x.v[c]), mean[c]);
+            d[c].v = __fadd_rn(d[c].v, __fmul_rn(dev, dev));
+          }
         }
-      part[threadIdx.y][threadIdx.x] = d;
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) part[threadIdx.y][threadIdx.x * CPT + c] = d[c];
       __syncthreads();
-      Acc dt = part[0][threadIdx.x];
-      for (int y = 1; y < Y; ++y) dt = merge(FOLD_SUM, dt, part[y][threadIdx.x]);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        Acc dt = part[0][threadIdx.x * CPT + c];
+        for (int y = 1; y < Y; ++y) dt = merge(FOLD_SUM, dt, part[y][threadIdx.x * CPT + c]);
+        result[c] = __fdiv_rn(dt.v, divisor);
+      }
       __syncthreads();
-      result = __fdiv_rn(dt.v, divisor);
     } else {
-      result = finish(mode, total.v, count);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) result[c] = finish(mode, total[c].v, count);
     }
     if (live && threadIdx.y == 0) {
       long long r = ko * K + k;
-      if (mode >= ARG_MIN) arg_out[r] = total.i;
-      else out[r] = T::store(result);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        if (mode >= ARG_MIN) arg_out[r + c] = total[c].i;
+        else out[r + c] = T::store(result[c]);
+      }
     }
   }
 }
@@ -413,11 +475,20 @@ int run_reduction(int dtype, uint32_t rank, const size_t *shape, const void *inp
       long long kept_outer = (long long)element_count(ko.rank, ko.v);
       fill_walk(L.kept, ko, kos, 0);
       fill_walk(L.folded, fc, fcs[0], 0);
-      long long tiles = kept_outer * ((K + 31) / 32);
+      // Four results per thread when every row of them starts 4-aligned.
+      bool four = K % 4 == 0 && (uintptr_t(in) % (4 * sizeof(S))) == 0;
+      for (uint32_t a = 0; four && a < ko.rank; ++a) four = kos.v[a] % 4 == 0;
+      for (uint32_t a = 0; four && a < fc.rank; ++a) four = fcs[0].v[a] % 4 == 0;
+      const int cpt = four ? 4 : 1;
+      long long tiles = kept_outer * ((K + 32 * cpt - 1) / (32 * cpt));
       int Y = 8;
       unsigned grid = unsigned(std::min<long long>(tiles, (long long)sm_count() * 8));
-      reduce_cols<T><<<std::max(1u, grid), dim3(32, Y), 0, stream>>>(in, L, kept_outer, K, (long long)depth, mode,
-                                                                      count, div, o, arg_out);
+      if (four)
+        reduce_cols<T, 4><<<std::max(1u, grid), dim3(32, Y), 0, stream>>>(in, L, kept_outer, K, (long long)depth,
+                                                                           mode, count, div, o, arg_out);
+      else
+        reduce_cols<T, 1><<<std::max(1u, grid), dim3(32, Y), 0, stream>>>(in, L, kept_outer, K, (long long)depth,
+                                                                           mode, count, div, o, arg_out);
       return check_launch("reduce (columns)");
     }
     fill_walk(L.folded, fc, fcs[0], 0);

@@ -78,3 +78,43 @@ def test_matvec_and_vecmat(device, dtype, rows, cols):
     O.call("orc_vecmat", O.DTYPES[dtype], rows, cols, O.ptr(v), O.ptr(m), O.ptr(want))
     want = O.widen(want, dtype)
     assert np.max(np.abs(got - want)) <= _tol(dtype, rows) * max(1.0, np.max(np.abs(want)))
+
+
+def _sampled_rows_check(dtype, m, k, n, transposed, rows, seed):
+    """Full-size products checked on a sample of output rows: the oracle's
+    i-p-j rows are independent, so a band of rows is the whole product's."""
+    a_shape = (k, m) if transposed == N.TRANS_LEFT else (m, k)
+    b_shape = (n, k) if transposed == N.TRANS_RIGHT else (k, n)
+    a = O.narrow(uniform(a_shape, seed), dtype)
+    b = O.narrow(uniform(b_shape, seed + 1), dtype)
+    da, db = cuda.CudaStorage.store(a, dtype), cuda.CudaStorage.store(b, dtype)
+    got = O.widen(cuda.Cuda.matmul(da, db, m, k, n, transposed).as_slice(), dtype).reshape(m, n)
+    a_rm = np.ascontiguousarray(a.reshape(a_shape).T) if transposed == N.TRANS_LEFT else a.reshape(m, k)
+    b_rm = np.ascontiguousarray(b.reshape(b_shape).T) if transposed == N.TRANS_RIGHT else b.reshape(k, n)
+    for r0 in rows:
+        band = np.zeros(16 * n, dtype=O.STORE[dtype])
+        O.call("orc_matmul_rows", O.DTYPES[dtype], 16, k, n, O.ptr(np.ascontiguousarray(a_rm[r0:r0 + 16])),
+               O.ptr(b_rm), O.ptr(band), 0, 0, 16)
+        want = O.widen(band, dtype).reshape(16, n)
+        assert np.max(np.abs(got[r0:r0 + 16] - want)) <= _tol(dtype, k) * max(1.0, np.max(np.abs(want))), r0
+    status = C.c_int(0)
+    N.call("tc_device_status", C.byref(status))
+
+
+import ctypes as C  # noqa: E402
+
+
+@pytest.mark.parametrize("transposed", [N.TRANS_NONE, N.TRANS_LEFT, N.TRANS_RIGHT])
+def test_bf16_2048_cubed_sampled(device, transposed):
+    _sampled_rows_check("bf16", 2048, 2048, 2048, transposed, [0, 640, 2032], 7)
+
+
+def test_bf16_config5_8192_sampled(device):
+    """Config 5's middle size, M=N=K=8192, uniform[-1,1], checked on 48 rows."""
+    _sampled_rows_check("bf16", 8192, 8192, 8192, N.TRANS_NONE, [0, 4096, 8176], 11)
+
+
+def test_no_gemm_wait_gave_up(device):
+    fault = C.c_int(0)
+    N.call("tc_device_status", C.byref(fault))
+    assert fault.value == 0
