@@ -25,7 +25,6 @@ import ctypes as C
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -51,56 +50,59 @@ def peaks() -> tuple[dict, str]:
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class Clocks:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled through NVML every ~2 ms
+    while the timed region runs (the same counters nvidia-smi reports)."""
 
-    def __init__(self, device: int):
-        self.device, self.proc, self.lines = device, None, []
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, torch_device: int):
+        self.dev, self.samples, self.max_mhz, self.error = torch_device, [], None, None
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.reader = threading.Thread(target=self._read, daemon=True)
-            self.reader.start()
-        except Exception:
-            self.proc = None
+            import pynvml as nv
+            import torch
+            nv.nvmlInit()
+            props = torch.cuda.get_device_properties(self.dev)
+            try:
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                self.h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = nv.nvmlDeviceGetHandleByIndex(self.dev)
+            self.nv = nv
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception as e:  # no NVML: report it
+            self.error = f"{type(e).__name__}: {e}"
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), int(get_reasons(self.h))))
+            except Exception as e:
+                self.error = str(e)
+                return
+            time.sleep(0.002)
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if getattr(self, "thread", None):
+            self.thread.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        loaded = [s for s in sm if s > 0.5 * mx] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0, "error": self.error}
+        mhz = [m for m, _ in self.samples]
+        reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz)}
 
 
 # ---------------------------------------------------------------------------
@@ -311,8 +313,113 @@ def cpu_c2(sample_rows: int = 16, reps: int = 1):
     scale = sample_rows / SHAPE2[0]
     step_bytes = sum(c2_ops_bytes().values()) * scale
     return {"value": round(step_bytes / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"all nine calls on a [{sample_rows},512,1024] slab ({scale:.3g} of config 2), x{reps}",
+            "sample": f"all nine calls on a [{sample_rows},512,1024] slab ({scale:.3g} of config 2), x{reps}, "
+                      "single-threaded as the Host runs strided kernels",
             "seconds": round(dt * reps, 2)}
+
+
+def timed(torch, world, fn, steps, warmup, stream, per_call=None):
+    """Run fn warmup times, then time `steps` calls with CUDA events on
+    `stream` (max over ranks).  Returns (ms per step, clocks summary)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(torch.cuda.current_device()) as clocks:
+        barrier(torch, world)
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier(torch, world)
+    return max_over_ranks(torch, world, t0.elapsed_time(t1)) / steps, clocks.summary()
+
+
+def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
+    """Config 5 (bf16, M=N=K=size) or config 1 (f32 1024^3): C = A.B through
+    tc_matmul, inputs resident.  metric TFLOP/s."""
+    from tensorcrate_b200 import _native as N
+    from tensorcrate_b200 import cuda
+    lib = N.lib()
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    m = k = n = size
+    rng = np.random.default_rng(0)
+    a = cuda.CudaStorage.store(cuda.f32_to_bits(rng.uniform(-1, 1, m * k).astype(np.float32), dtype), dtype)
+    b = cuda.CudaStorage.store(cuda.f32_to_bits(rng.uniform(-1, 1, k * n).astype(np.float32), dtype), dtype)
+    c = cuda.CudaStorage(dtype, m * n)
+    code = N.DTYPES[dtype]
+
+    def step():
+        N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a.ptr, b.ptr, c.ptr, 0, sp))
+
+    ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
+    flops = 2.0 * m * n * k
+    pk, pk_kind = peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak = pk["bf16_tflops"] if dtype != "f32" else None
+    line = {"metric": f"{dtype} GEMM TFLOP/s", "value": round(world * tflops, 1), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic uniform[-1,1], seeded",
+            "config": {"workload": f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate",
+                       "l2": "inputs resident; the working set exceeds L2 at 8192 and above"},
+            "roofline": {"bound": "tensor" if dtype != "f32" else "fp32-simt", "kernel": "gemm_tc" if dtype != "f32"
+                         else "gemm_simt", "achieved": round(tflops, 1), "peak": peak, "peak_source": pk_kind,
+                         "unit": "TFLOP/s", "frac": round(tflops / peak, 3) if peak else None, "traffic": None},
+            "gpu_launches": args.steps, "clocks": clocks}
+    return line
+
+
+def run_c3(args, torch, world, rank, comm):
+    """Config 3: f16 [8,16,128,64,32] permuted (0,3,1,4,2) and made
+    contiguous; then sliced [:, 8:, :, :32, :], split in 4 along axis 1 and
+    concatenated back (one assemble).  metric GB/s of the two copies."""
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200 import _native as N
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    shape = [8, 16, 128, 64, 32]
+    n = int(np.prod(shape))
+    x = cuda.CudaStorage.store(np.random.default_rng(3).standard_normal(n).astype(np.float16).view(np.uint16), "f16")
+    t = cuda.Tensor(x, shape)
+    perm = [0, 3, 1, 4, 2]
+    pv = t.view().permute(perm)
+    p_shape = pv.shape
+    out_p = cuda.CudaStorage("f16", n)
+    lib = N.lib()
+    sl = cuda.TensorView(out_p, p_shape, cuda.contiguous_strides(p_shape)).slice(1, 8, p_shape[1]).slice(3, 0, 32)
+    pieces = sl.chunk(1, 4)
+    cat_shape = list(sl.shape)
+    to = cuda.contiguous_strides(cat_shape)
+    regions, at = [], 0
+    for v in pieces:
+        regions.append(cuda.Cuda._region((v.storage, v.shape, v.offset, v.strides, at * to[1], to)))
+        at += v.shape[1]
+    m = int(np.prod(cat_shape))
+    out_c = cuda.CudaStorage("f16", m)
+    arr = (N.Region * len(regions))(*regions)
+    ps, pst = N.sizes(p_shape), N.sizes(pv.strides)
+
+    def step():
+        N.check("copy", lib.tc_strided_copy(2, 5, ps, x.ptr, n, 0, pst, out_p.ptr, C.c_void_p(sp)))
+        N.check("assemble", lib.tc_assemble(2, out_c.ptr, m, arr, len(regions), C.c_void_p(sp)))
+
+    ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
+    byts = 2 * n * 2 + 2 * m * 2
+    gbs = byts / (ms * 1e-3) / 1e9
+    pk, pk_kind = peaks()
+    return {"metric": "config-3 layout copy HBM throughput (GB/s)", "value": round(world * gbs, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "config3: permute(0,3,1,4,2)+contiguous, slice->split(4)->concat",
+                       "algorithmic_bytes_per_step": byts},
+            "roofline": {"bound": "hbm", "kernel": "strided copy + assemble", "achieved": round(gbs, 1),
+                         "peak": pk["hbm_gbs"], "peak_source": pk_kind, "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 3), "traffic": None},
+            "gpu_launches": 5 * args.steps, "clocks": clocks}
 
 
 def barrier(torch, world):
@@ -350,7 +457,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
+    ap.add_argument("--size", type=int, default=8192, help="config 5's M=N=K")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -359,8 +467,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        reps = max(1, args.steps // 25)
-        base = cpu_c2(sample_rows=16, reps=reps)
+        base = cpu_c2(sample_rows=64, reps=max(3, min(16, args.steps)))
         line = {"metric": "config-2 broadcast + axis-reduction HBM throughput (GB/s)", "value": base["value"],
                 "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -380,9 +487,16 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     comm = init_comm(torch, world, rank)
-    line = run_c2(args, torch, world, rank, comm)
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_c2(sample_rows=16, reps=1)
+    if args.workload == "c5":
+        line = run_gemm(args, torch, world, rank, comm, "bf16", args.size)
+    elif args.workload == "c1":
+        line = run_gemm(args, torch, world, rank, comm, "f32", 1024)
+    elif args.workload == "c3":
+        line = run_c3(args, torch, world, rank, comm)
+    else:
+        line = run_c2(args, torch, world, rank, comm)
+    if rank == 0 and not args.no_cpu_baseline and args.workload == "c2":
+        line["cpu_baseline"] = cpu_c2(sample_rows=64, reps=12)
     if comm is not None:
         N.call("tc_comm_destroy", comm)
     if world > 1:

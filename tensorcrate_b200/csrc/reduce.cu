@@ -12,18 +12,22 @@
 //
 // The host splits the layout into kept axes (one result each) and folded
 // axes (coalesced separately), then picks a kernel:
-//  - rows: the folded space ends in a contiguous run (the innermost folded
-//    axis has stride 1).  A warp (short slices) or a 256-thread block (long
-//    ones) per result, 128-bit loads along the run.  A variance whose slice
-//    fits in registers is computed from them in both passes, so the input
-//    is read from HBM once.
-//  - columns: the innermost kept axis has stride 1 (results side by side in
-//    memory).  Each thread owns one result and a share of the folded range;
-//    neighbouring threads read neighbouring addresses, so each folded step
-//    is a coalesced row read.  The shares combine in shared memory.
+//  - rows: the folded space ends in a contiguous run (innermost folded
+//    stride 1).  A warp per (result, share of its slice); each lane issues
+//    eight independent 128-bit loads before folding any.  When results are
+//    few and slices long, the slice is split into shares whose partial
+//    results land in a scratch buffer and are merged, in order, by a second
+//    small kernel.  A variance whose slice fits in registers is computed from
+//    them in both passes, so the input is read from HBM once.
+//  - columns: the innermost kept axis has stride 1 (results side by side).
+//    Each thread owns four adjacent results (one vector load each) and a
+//    share of the folded range; the shares combine in shared memory.
 //  - walk: anything else; a warp per result over the decomposed folded
 //    index.
+// Every kernel is compiled per operation, so each carries only its own
+// arithmetic.
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -31,96 +35,63 @@
 namespace tc {
 namespace {
 
-enum Mode { FOLD_SUM = 0, FOLD_MIN = 1, FOLD_MAX = 2, MEAN = 3, VARIANCE = 4, ARG_MIN = 5, ARG_MAX = 6 };
+enum Mode { M_SUM = 0, M_MIN = 1, M_MAX = 2, M_MEAN = 3, M_VAR = 4, M_ARGMIN = 5, M_ARGMAX = 6 };
 
-// ---- accumulators ---------------------------------------------------------
+template <int MODE> constexpr bool is_arg() { return MODE == M_ARGMIN || MODE == M_ARGMAX; }
+// The fold a mode accumulates with.
+template <int MODE> constexpr int fold_of() { return (MODE == M_MEAN || MODE == M_VAR) ? M_SUM : MODE; }
+
 struct Acc {
   float v;
   uint32_t i;  // position (arg-reductions only)
 };
 
-__device__ __forceinline__ Acc identity(int mode) {
-  switch (mode) {
-    case FOLD_MIN: return {INFINITY, 0};
-    case FOLD_MAX: return {-INFINITY, 0};
-    case ARG_MIN:
-    case ARG_MAX: return {__int_as_float(0x7fc00000), 0};
-    default: return {0.0f, 0};
-  }
+template <int F> __device__ __forceinline__ Acc identity() {
+  if (F == M_MIN) return {INFINITY, 0};
+  if (F == M_MAX) return {-INFINITY, 0};
+  if (is_arg<F>()) return {__int_as_float(0x7fc00000), 0};
+  return {0.0f, 0};
 }
 
-// Fold one more element (at position `pos` along an arg-reduction's axis).
-__device__ __forceinline__ void push(int mode, Acc &a, float x, uint32_t pos) {
-  switch (mode) {
-    case FOLD_MIN: a.v = fminf(a.v, x); break;
-    case FOLD_MAX: a.v = fmaxf(a.v, x); break;
-    case ARG_MIN:
-      // strided.rs:188-198 `replaces`: a number, and best is NaN or x is past it
-      if (!isnan(x) && (isnan(a.v) || x < a.v)) { a.v = x; a.i = pos; }
-      break;
-    case ARG_MAX:
-      if (!isnan(x) && (isnan(a.v) || x > a.v)) { a.v = x; a.i = pos; }
-      break;
-    default: a.v = __fadd_rn(a.v, x); break;
-  }
+// Fold one more element, at position `pos` along an arg-reduction's axis.
+template <int F> __device__ __forceinline__ void push(Acc &a, float x, uint32_t pos) {
+  if (F == M_MIN) a.v = fminf(a.v, x);
+  else if (F == M_MAX) a.v = fmaxf(a.v, x);
+  else if (F == M_ARGMIN) {
+    // strided.rs:188-198 `replaces`: a number, and best is NaN or x is past it
+    if (!isnan(x) && (isnan(a.v) || x < a.v)) { a.v = x; a.i = pos; }
+  } else if (F == M_ARGMAX) {
+    if (!isnan(x) && (isnan(a.v) || x > a.v)) { a.v = x; a.i = pos; }
+  } else a.v = __fadd_rn(a.v, x);
 }
 
-// Combine two partial results; for an arg-reduction the lower position wins
-// a tie, which is the first position overall.
-__device__ __forceinline__ Acc merge(int mode, Acc a, Acc b) {
-  switch (mode) {
-    case FOLD_MIN: return {fminf(a.v, b.v), 0};
-    case FOLD_MAX: return {fmaxf(a.v, b.v), 0};
-    case ARG_MIN:
-    case ARG_MAX: {
-      if (isnan(b.v)) return a;
-      if (isnan(a.v)) return b;
-      bool better = mode == ARG_MAX ? b.v > a.v : b.v < a.v;
-      if (better || (b.v == a.v && b.i < a.i)) return b;
-      return a;
-    }
-    default: return {__fadd_rn(a.v, b.v), 0};
+// Combine partials; for an arg-reduction the lower position wins a tie.
+template <int F> __device__ __forceinline__ Acc merge(Acc a, Acc b) {
+  if (F == M_MIN) return {fminf(a.v, b.v), 0};
+  if (F == M_MAX) return {fmaxf(a.v, b.v), 0};
+  if (is_arg<F>()) {
+    if (isnan(b.v)) return a;
+    if (isnan(a.v)) return b;
+    bool better = F == M_ARGMAX ? b.v > a.v : b.v < a.v;
+    return (better || (b.v == a.v && b.i < a.i)) ? b : a;
   }
+  return {__fadd_rn(a.v, b.v), 0};
 }
 
-__device__ __forceinline__ Acc warp_merge(int mode, Acc a) {
+template <int F> __device__ __forceinline__ Acc warp_merge(Acc a) {
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) {
     Acc b;
     b.v = __shfl_xor_sync(0xffffffffu, a.v, d);
-    b.i = __shfl_xor_sync(0xffffffffu, a.i, d);
-    a = merge(mode, a, b);
+    if (is_arg<F>()) b.i = __shfl_xor_sync(0xffffffffu, a.i, d);
+    a = merge<F>(a, b);
   }
   return a;
 }
 
-// Merge across a block of `nwarps` warps: every thread gets the result.
-__device__ __forceinline__ Acc block_merge(int mode, Acc a, Acc *scratch) {
-  a = warp_merge(mode, a);
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  __syncthreads();
-  if (lane == 0) scratch[warp] = a;
-  __syncthreads();
-  Acc r = scratch[0];
-  for (int w = 1; w < nwarps; ++w) r = merge(mode, r, scratch[w]);
-  return r;
-}
-
-// Finish one result: Mean divides, everything else is already final.
-__device__ __forceinline__ float finish(int mode, float total, float count) {
-  return mode == MEAN ? __fdiv_rn(total, count) : total;
-}
-
-// The kept walk gives each result's base offset; the folded walk (outer
-// axes) gives each run's offset within the slice.
-struct Layout2 {
-  Walk kept;    // operand 0: input strides; rank 0 = one result
-  Walk folded;  // operand 0: input strides of the folded axes except the run
-};
-
 // Storage position of flat index `r` of a one-operand walk; rank 0 and 1
 // (the common cases) skip the division.
-__device__ __forceinline__ long long kept_base(const Walk &w, long long r) {
+__device__ __forceinline__ long long walk_pos(const Walk &w, long long r) {
   if (w.rank == 0) return w.offset[0];
   if (w.rank == 1) return w.offset[0] + r * w.stride[0][0];
   long long p[1];
@@ -134,207 +105,242 @@ template <class T> struct Pack {
   union { uint4 raw; S v[N]; };
 };
 
-// ---------------------------------------------------------------------------
-// rows: G threads per result (G = 32: a warp; G = blockDim: the block).
-// The slice is `outer` runs of `run` contiguous elements.
-// ---------------------------------------------------------------------------
-constexpr int CACHE_PACKS = 8;
+struct RowsArgs {
+  Walk kept;          // result r -> slice base
+  Walk folded;        // run o -> run offset within the slice
+  long long results;  // kept results
+  long long outer;    // runs per slice
+  long long run;      // elements per run
+  int splits;         // shares per slice (1 = no partials)
+  long long share;    // runs (outer > 1) or units (outer == 1) per share
+  float count, divisor;
+  bool vec;
+};
 
-template <class T, bool BLOCK>
-__global__ void __launch_bounds__(256, 2) reduce_rows(const typename T::S *in, Layout2 L, long long results,
-                                                   long long outer, long long run, int mode, float count,
-                                                   float divisor, typename T::S *out, uint32_t *arg_out,
-                                                   bool vec) {
+template <int MODE, class T>
+__device__ __forceinline__ void write_result(const RowsArgs &a, long long r, Acc acc, typename T::S *out,
+                                             uint32_t *arg_out) {
+  if (is_arg<MODE>()) arg_out[r] = acc.i;
+  else if (MODE == M_MEAN) out[r] = T::store(__fdiv_rn(acc.v, a.count));
+  else out[r] = T::store(acc.v);
+}
+
+// ---------------------------------------------------------------------------
+// rows: a warp per (result, share).  The slice is `outer` runs of `run`
+// elements, read as units (16-byte packs when `vec`, else elements).
+// ---------------------------------------------------------------------------
+template <class T, int MODE>
+__global__ void __launch_bounds__(256, 3) reduce_rows(const typename T::S *in, const RowsArgs a,
+                                                      typename T::S *out, uint32_t *arg_out, Acc *partial) {
   using S = typename T::S;
   constexpr int N = Pack<T>::N;
-  __shared__ Acc scratch[32];
-  const int G = BLOCK ? blockDim.x : 32;
-  const int lane = BLOCK ? threadIdx.x : (threadIdx.x & 31);
-  const long long groups_per_block = BLOCK ? 1 : (blockDim.x >> 5);
-  const long long group0 = (long long)blockIdx.x * groups_per_block + (BLOCK ? 0 : (threadIdx.x >> 5));
-  const long long group_stride = (long long)gridDim.x * groups_per_block;
-  const int fold_mode = (mode == MEAN || mode == VARIANCE) ? FOLD_SUM : mode;
-  const bool cache = mode == VARIANCE && vec && outer == 1 && run <= (long long)G * N * CACHE_PACKS;
-
-  for (long long r = group0; r < results; r += group_stride) {
-    const S *base = in + kept_base(L.kept, r);
-    Acc a = identity(fold_mode);
-    Pack<T> cached[CACHE_PACKS];  // the slice, still in its storage form
-    if (cache) {
-      // Pass one from memory into registers: all loads first, then the sum.
-#pragma unroll
-      for (int k = 0; k < CACHE_PACKS; ++k) {
-        long long p = (long long)k * G + lane;
-        if (p * N < run) cached[k].raw = __ldg(reinterpret_cast<const uint4 *>(base + p * N));
-      }
-#pragma unroll
-      for (int k = 0; k < CACHE_PACKS; ++k) {
-        long long p = (long long)k * G + lane;
-        if (p * N < run) {
-#pragma unroll
-          for (int j = 0; j < N; ++j) a.v = __fadd_rn(a.v, T::load(cached[k].v[j]));
-        }
-      }
+  constexpr int F = fold_of<MODE>();
+  constexpr int U = 8;
+  const int lane = threadIdx.x & 31;
+  const long long groups = a.results * a.splits;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long per_run = a.vec ? a.run / N : a.run;
+  for (long long g = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < groups; g += warps) {
+    const long long r = g / a.splits, s = g - r * a.splits;
+    const S *base = in + walk_pos(a.kept, r);
+    // A share is a range of whole runs, or (one run per slice) a range of
+    // the run's units.
+    long long o_lo = 0, o_hi = 1, c_lo = 0, c_hi = per_run;
+    if (a.outer > 1) {
+      o_lo = s * a.share;
+      o_hi = min(a.outer, o_lo + a.share);
     } else {
-      // The slice as one flat run of units (packs when vectorised, else
-      // elements): `outer` runs of `per_run` units.  U independent loads are
-      // issued before any is folded, so each thread keeps U requests in
-      // flight.
-      constexpr int U = 8;
-      const long long per_run = vec ? run / N : run;
-      const long long total = outer * per_run;
-      for (long long f0 = lane; f0 < total; f0 += (long long)G * U) {
-        if (vec) {
+      c_lo = s * a.share;
+      c_hi = min(per_run, c_lo + a.share);
+    }
+    Acc acc = identity<F>();
+    for (long long o = o_lo; o < o_hi; ++o) {
+      const S *rp = base + walk_pos(a.folded, o);
+      for (long long c0 = c_lo + lane; c0 < c_hi; c0 += 32 * U) {
+        if (a.vec) {
           Pack<T> x[U];
-          long long at[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            long long f = f0 + (long long)u * G;
-            if (f < total) {
-              long long o = outer > 1 ? f / per_run : 0, c = f - o * per_run;
-              at[u] = c * N;
-              x[u].raw = __ldg(reinterpret_cast<const uint4 *>(base + (outer > 1 ? kept_base(L.folded, o) : 0) + c * N));
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            if (f0 + (long long)u * G < total) {
-#pragma unroll
-              for (int j = 0; j < N; ++j) push(fold_mode, a, T::load(x[u].v[j]), uint32_t(at[u] + j));
-            }
-          }
-        } else {
-          float x[U];
-          long long at[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            long long f = f0 + (long long)u * G;
-            if (f < total) {
-              long long o = outer > 1 ? f / per_run : 0, c = f - o * per_run;
-              at[u] = c;
-              x[u] = T::load(base[(outer > 1 ? kept_base(L.folded, o) : 0) + c]);
-            }
-          }
 #pragma unroll
           for (int u = 0; u < U; ++u)
-            if (f0 + (long long)u * G < total) push(fold_mode, a, x[u], uint32_t(at[u]));
-        }
-      }
-    }
-    a = BLOCK ? block_merge(fold_mode, a, scratch) : warp_merge(fold_mode, a);
-    float result;
-    if (mode == VARIANCE) {
-      float mean = __fdiv_rn(a.v, count);
-      Acc d = identity(FOLD_SUM);
-      if (cache) {
+            if (c0 + 32 * u < c_hi) x[u].raw = __ldg(reinterpret_cast<const uint4 *>(rp + (c0 + 32 * u) * N));
 #pragma unroll
-        for (int k = 0; k < CACHE_PACKS; ++k) {
-          long long p = (long long)k * G + lane;
-          if (p * N < run) {
+          for (int u = 0; u < U; ++u)
+            if (c0 + 32 * u < c_hi) {
+              const uint32_t at = uint32_t((c0 + 32 * u) * N);
 #pragma unroll
-            for (int j = 0; j < N; ++j) {
-              float dev = __fsub_rn(T::load(cached[k].v[j]), mean);
-              d.v = __fadd_rn(d.v, __fmul_rn(dev, dev));
+              for (int j = 0; j < N; ++j) push<F>(acc, T::load(x[u].v[j]), at + j);
             }
-          }
-        }
-      } else {
-        for (long long o = 0; o < outer; ++o) {
-          const S *rp = base + (outer > 1 ? kept_base(L.folded, o) : 0);
-          for (long long c = lane; c < run; c += G) {
-            float dev = __fsub_rn(T::load(rp[c]), mean);
-            d.v = __fadd_rn(d.v, __fmul_rn(dev, dev));
-          }
+        } else {
+          float x[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (c0 + 32 * u < c_hi) x[u] = T::load(rp[c0 + 32 * u]);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (c0 + 32 * u < c_hi) push<F>(acc, x[u], uint32_t(c0 + 32 * u));
         }
       }
-      d = BLOCK ? block_merge(FOLD_SUM, d, scratch) : warp_merge(FOLD_SUM, d);
-      result = __fdiv_rn(d.v, divisor);
-    } else {
-      result = finish(mode, a.v, count);
     }
+    acc = warp_merge<F>(acc);
     if (lane == 0) {
-      if (mode >= ARG_MIN) arg_out[r] = a.i;
-      else out[r] = T::store(result);
+      if (a.splits > 1) partial[g] = acc;
+      else write_result<MODE, T>(a, r, acc, out, arg_out);
     }
-    if (BLOCK) __syncthreads();
+  }
+}
+
+// Merge each result's shares in order and finish it.
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) reduce_finish(const RowsArgs a, const Acc *partial, typename T::S *out,
+                                                     uint32_t *arg_out) {
+  constexpr int F = fold_of<MODE>();
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < a.results; r += warps) {
+    Acc acc = identity<F>();
+    for (int s = lane; s < a.splits; s += 32) acc = merge<F>(acc, partial[r * a.splits + s]);
+    acc = warp_merge<F>(acc);
+    if (lane == 0) write_result<MODE, T>(a, r, acc, out, arg_out);
+  }
+}
+
+// Variance over rows: a warp per result.  When the slice is one run of at
+// most 32*CACHE_PACKS packs it is held in registers between the passes.
+constexpr int CACHE_PACKS = 8;
+template <class T>
+__global__ void __launch_bounds__(256, 2) reduce_rows_var(const typename T::S *in, const RowsArgs a,
+                                                          typename T::S *out) {
+  using S = typename T::S;
+  constexpr int N = Pack<T>::N;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const bool cache = a.vec && a.outer == 1 && a.run <= 32LL * N * CACHE_PACKS;
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < a.results; r += warps) {
+    const S *base = in + walk_pos(a.kept, r);
+    Acc sum = identity<M_SUM>(), dev = identity<M_SUM>();
+    if (cache) {
+      Pack<T> x[CACHE_PACKS];
+#pragma unroll
+      for (int k = 0; k < CACHE_PACKS; ++k)
+        if ((32LL * k + lane) * N < a.run) x[k].raw = __ldg(reinterpret_cast<const uint4 *>(base + (32LL * k + lane) * N));
+#pragma unroll
+      for (int k = 0; k < CACHE_PACKS; ++k)
+        if ((32LL * k + lane) * N < a.run) {
+#pragma unroll
+          for (int j = 0; j < N; ++j) sum.v = __fadd_rn(sum.v, T::load(x[k].v[j]));
+        }
+      sum = warp_merge<M_SUM>(sum);
+      const float mean = __fdiv_rn(sum.v, a.count);
+#pragma unroll
+      for (int k = 0; k < CACHE_PACKS; ++k)
+        if ((32LL * k + lane) * N < a.run) {
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            const float d = __fsub_rn(T::load(x[k].v[j]), mean);
+            dev.v = __fadd_rn(dev.v, __fmul_rn(d, d));
+          }
+        }
+    } else {
+      for (long long o = 0; o < a.outer; ++o) {
+        const S *rp = base + (a.outer > 1 ? walk_pos(a.folded, o) : 0);
+        for (long long c = lane; c < a.run; c += 32) sum.v = __fadd_rn(sum.v, T::load(rp[c]));
+      }
+      sum = warp_merge<M_SUM>(sum);
+      const float mean = __fdiv_rn(sum.v, a.count);
+      for (long long o = 0; o < a.outer; ++o) {
+        const S *rp = base + (a.outer > 1 ? walk_pos(a.folded, o) : 0);
+        for (long long c = lane; c < a.run; c += 32) {
+          const float d = __fsub_rn(T::load(rp[c]), mean);
+          dev.v = __fadd_rn(dev.v, __fmul_rn(d, d));
+        }
+      }
+    }
+    dev = warp_merge<M_SUM>(dev);
+    if (lane == 0) out[r] = T::store(__fdiv_rn(dev.v, a.divisor));
   }
 }
 
 // ---------------------------------------------------------------------------
-// columns: results r = (outer kept index) * K + k with k along the kept axis
-// of stride 1.  blockDim = (32, Y): x walks 32*CPT adjacent results (CPT per
-// thread, one vector load each), y splits the folded range into Y shares
-// that combine in shared memory in share order.
+// columns: results r = (outer kept index) * K + k, k along the kept axis of
+// stride 1.  blockDim = (32, 8): x walks 32*CPT adjacent results, y splits
+// the folded range into 8 shares combined in shared memory in share order.
 // ---------------------------------------------------------------------------
 template <class T, int CPT> struct Cols {
   using S = typename T::S;
-  union { typename std::conditional<CPT * sizeof(S) == 16, uint4, typename std::conditional<CPT * sizeof(S) == 8, uint2, S>::type>::type raw; S v[CPT]; };
+  using Raw = typename std::conditional<CPT * sizeof(S) == 16, uint4,
+                                        typename std::conditional<CPT * sizeof(S) == 8, uint2, S>::type>::type;
+  union { Raw raw; S v[CPT]; };
 };
 
-template <class T, int CPT>
-__global__ void __launch_bounds__(256) reduce_cols(const typename T::S *in, Layout2 L, long long kept_outer,
-                                                   long long K, long long depth, int mode, float count,
-                                                   float divisor, typename T::S *out, uint32_t *arg_out) {
+struct ColsArgs {
+  Walk kept;    // kept outer index -> base
+  Walk folded;  // folded flat index -> offset
+  long long kept_outer, K, depth;
+  float count, divisor;
+};
+
+template <class T, int MODE, int CPT>
+__global__ void __launch_bounds__(256, 3) reduce_cols(const typename T::S *in, const ColsArgs a, typename T::S *out,
+                                                      uint32_t *arg_out) {
   using S = typename T::S;
   using V = Cols<T, CPT>;
   constexpr int W = 32 * CPT;
   constexpr int U = 8;
+  constexpr int F = fold_of<MODE>();
   __shared__ Acc part[8][W];
   const int Y = blockDim.y;
-  const int fold_mode = (mode == MEAN || mode == VARIANCE) ? FOLD_SUM : mode;
-  const long long tiles_k = (K + W - 1) / W;
-  const long long tiles = kept_outer * tiles_k;
-  const long long share = (depth + Y - 1) / Y;
-  const long long f0 = (long long)threadIdx.y * share, f1 = min(depth, f0 + share);
+  const long long tiles_k = (a.K + W - 1) / W;
+  const long long tiles = a.kept_outer * tiles_k;
+  const long long share = (a.depth + Y - 1) / Y;
+  const long long f0 = (long long)threadIdx.y * share, f1 = min(a.depth, f0 + share);
   for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
     const long long ko = t / tiles_k;
     const long long k = (t - ko * tiles_k) * W + (long long)threadIdx.x * CPT;
-    const bool live = k < K;  // CPT divides K when CPT > 1
-    const S *base = in + kept_base(L.kept, ko) + (live ? k : 0);
-    Acc a[CPT];
+    const bool live = k < a.K;  // CPT divides K when CPT > 1
+    const S *base = in + walk_pos(a.kept, ko) + (live ? k : 0);
+    Acc acc[CPT];
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) a[c] = identity(fold_mode);
+    for (int c = 0; c < CPT; ++c) acc[c] = identity<F>();
     if (live) {
       for (long long f = f0; f < f1; f += U) {
         V x[U];
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (f + u < f1) x[u].raw = __ldg(reinterpret_cast<const decltype(V::raw) *>(base + kept_base(L.folded, f + u)));
+          if (f + u < f1) x[u].raw = __ldg(reinterpret_cast<const typename V::Raw *>(base + walk_pos(a.folded, f + u)));
 #pragma unroll
         for (int u = 0; u < U; ++u)
           if (f + u < f1) {
 #pragma unroll
-            for (int c = 0; c < CPT; ++c) push(fold_mode, a[c], T::load(x[u].v[c]), uint32_t(f + u));
+            for (int c = 0; c < CPT; ++c) push<F>(acc[c], T::load(x[u].v[c]), uint32_t(f + u));
           }
       }
     }
-    float result[CPT];
-    Acc total[CPT];
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) part[threadIdx.y][threadIdx.x * CPT + c] = a[c];
+    for (int c = 0; c < CPT; ++c) part[threadIdx.y][threadIdx.x * CPT + c] = acc[c];
     __syncthreads();
+    Acc total[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) {
       total[c] = part[0][threadIdx.x * CPT + c];
-      for (int y = 1; y < Y; ++y) total[c] = merge(fold_mode, total[c], part[y][threadIdx.x * CPT + c]);
+      for (int y = 1; y < Y; ++y) total[c] = merge<F>(total[c], part[y][threadIdx.x * CPT + c]);
     }
     __syncthreads();
-    if (mode == VARIANCE) {
+    float result[CPT];
+    if (MODE == M_VAR) {
       float mean[CPT];
       Acc d[CPT];
 #pragma unroll
       for (int c = 0; c < CPT; ++c) {
-        mean[c] = __fdiv_rn(total[c].v, count);
-        d[c] = identity(FOLD_SUM);
+        mean[c] = __fdiv_rn(total[c].v, a.count);
+        d[c] = identity<M_SUM>();
       }
       if (live)
         for (long long f = f0; f < f1; ++f) {
           V x;
-          x.raw = __ldg(reinterpret_cast<const decltype(V::raw) *>(base + kept_base(L.folded, f)));
+          x.raw = __ldg(reinterpret_cast<const typename V::Raw *>(base + walk_pos(a.folded, f)));
 #pragma unroll
           for (int c = 0; c < CPT; ++c) {
-            float dev = __fsub_rn(T::load(x.v[c]), mean[c]);
-            d[c].v = __fadd_rn(d[c].v, __fmul_rn(dev, dev));
+            const float dv = __fsub_rn(T::load(x.v[c]), mean[c]);
+            d[c].v = __fadd_rn(d[c].v, __fmul_rn(dv, dv));
           }
         }
 #pragma unroll
@@ -343,19 +349,19 @@ __global__ void __launch_bounds__(256) reduce_cols(const typename T::S *in, Layo
 #pragma unroll
       for (int c = 0; c < CPT; ++c) {
         Acc dt = part[0][threadIdx.x * CPT + c];
-        for (int y = 1; y < Y; ++y) dt = merge(FOLD_SUM, dt, part[y][threadIdx.x * CPT + c]);
-        result[c] = __fdiv_rn(dt.v, divisor);
+        for (int y = 1; y < Y; ++y) dt = merge<M_SUM>(dt, part[y][threadIdx.x * CPT + c]);
+        result[c] = __fdiv_rn(dt.v, a.divisor);
       }
       __syncthreads();
     } else {
 #pragma unroll
-      for (int c = 0; c < CPT; ++c) result[c] = finish(mode, total[c].v, count);
+      for (int c = 0; c < CPT; ++c) result[c] = MODE == M_MEAN ? __fdiv_rn(total[c].v, a.count) : total[c].v;
     }
     if (live && threadIdx.y == 0) {
-      long long r = ko * K + k;
+      const long long r = ko * a.K + k;
 #pragma unroll
       for (int c = 0; c < CPT; ++c) {
-        if (mode >= ARG_MIN) arg_out[r + c] = total[c].i;
+        if (is_arg<MODE>()) arg_out[r + c] = total[c].i;
         else out[r + c] = T::store(result[c]);
       }
     }
@@ -365,65 +371,185 @@ __global__ void __launch_bounds__(256) reduce_cols(const typename T::S *in, Layo
 // ---------------------------------------------------------------------------
 // walk: a warp per result over the decomposed folded index.
 // ---------------------------------------------------------------------------
-template <class T>
-__global__ void __launch_bounds__(256) reduce_walk(const typename T::S *in, Layout2 L, long long results,
-                                                   long long depth, int mode, float count, float divisor,
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) reduce_walk(const typename T::S *in, const ColsArgs a, long long results,
                                                    typename T::S *out, uint32_t *arg_out) {
+  constexpr int F = fold_of<MODE>();
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const int fold_mode = (mode == MEAN || mode == VARIANCE) ? FOLD_SUM : mode;
   for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < results; r += warps) {
-    long long base = kept_base(L.kept, r);
-    Acc a = identity(fold_mode);
-    for (long long f = lane; f < depth; f += 32) {
-      push(fold_mode, a, T::load(in[base + kept_base(L.folded, f)]), uint32_t(f));
-    }
-    a = warp_merge(fold_mode, a);
-    float result;
-    if (mode == VARIANCE) {
-      float mean = __fdiv_rn(a.v, count);
-      Acc d = identity(FOLD_SUM);
-      for (long long f = lane; f < depth; f += 32) {
-        float dev = __fsub_rn(T::load(in[base + kept_base(L.folded, f)]), mean);
-        d.v = __fadd_rn(d.v, __fmul_rn(dev, dev));
+    const long long base = walk_pos(a.kept, r);
+    Acc acc = identity<F>();
+    for (long long f = lane; f < a.depth; f += 32) push<F>(acc, T::load(in[base + walk_pos(a.folded, f)]), uint32_t(f));
+    acc = warp_merge<F>(acc);
+    float result = acc.v;
+    if (MODE == M_MEAN) result = __fdiv_rn(acc.v, a.count);
+    if (MODE == M_VAR) {
+      const float mean = __fdiv_rn(acc.v, a.count);
+      Acc d = identity<M_SUM>();
+      for (long long f = lane; f < a.depth; f += 32) {
+        const float dv = __fsub_rn(T::load(in[base + walk_pos(a.folded, f)]), mean);
+        d.v = __fadd_rn(d.v, __fmul_rn(dv, dv));
       }
-      d = warp_merge(FOLD_SUM, d);
-      result = __fdiv_rn(d.v, divisor);
-    } else {
-      result = finish(mode, a.v, count);
+      d = warp_merge<M_SUM>(d);
+      result = __fdiv_rn(d.v, a.divisor);
     }
     if (lane == 0) {
-      if (mode >= ARG_MIN) arg_out[r] = a.i;
+      if (is_arg<MODE>()) arg_out[r] = acc.i;
       else out[r] = T::store(result);
     }
   }
 }
 
-void fill_walk(Walk &w, const Dims &shape, const Dims &strides, long long offset) {
+void fill_walk(Walk &w, const Dims &shape, const Dims &strides) {
+  w = Walk{};
   w.rank = int(shape.rank);
-  w.offset[0] = offset;
   for (uint32_t a = 0; a < shape.rank; ++a) {
     w.shape[a] = (long long)shape.v[a];
     w.stride[0][a] = (long long)strides.v[a];
   }
 }
 
+// Scratch for partial results, kept per device and grown on demand.
+struct Scratch {
+  std::mutex mu;
+  void *ptr[64] = {nullptr};
+  size_t bytes[64] = {0};
+};
+Scratch &scratch() {
+  static Scratch *s = new Scratch;
+  return *s;
+}
+int scratch_get(size_t bytes, void **out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(TC_EINVAL, "device %d", dev);
+  Scratch &s = scratch();
+  std::lock_guard<std::mutex> g(s.mu);
+  if (s.bytes[dev] < bytes) {
+    if (s.ptr[dev]) {
+      // The old block may still be read by queued work: free it only once
+      // the device is idle.
+      cudaDeviceSynchronize();
+      cudaFree(s.ptr[dev]);
+      s.ptr[dev] = nullptr;
+      s.bytes[dev] = 0;
+    }
+    size_t want = std::max(bytes, size_t(1) << 20);
+    if (int st = check_cuda(cudaMalloc(&s.ptr[dev], want), "cudaMalloc (reduction scratch)")) return st;
+    s.bytes[dev] = want;
+  }
+  *out = s.ptr[dev];
+  return TC_OK;
+}
+
+template <class T, int MODE>
+int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const Dims &fc, const Dims &fcs,
+                long long results, long long depth, float count, float divisor, void *out, uint32_t *arg_out,
+                cudaStream_t stream) {
+  using S = typename T::S;
+  S *o = static_cast<S *>(out);
+  const int sms = sm_count();
+  // rows: innermost folded axis contiguous (unless the kept axis is the
+  // contiguous one and the runs are short).
+  const bool kept_inner_contig = kc.rank && kcs.v[kc.rank - 1] == 1;
+  if (fc.rank >= 1 && fcs.v[fc.rank - 1] == 1 && !(kept_inner_contig && fc.v[fc.rank - 1] < 64)) {
+    RowsArgs a{};
+    fill_walk(a.kept, kc, kcs);
+    Dims fo = fc, fos = fcs;
+    fo.rank = fos.rank = fc.rank - 1;
+    fill_walk(a.folded, fo, fos);
+    a.results = results;
+    a.outer = (long long)element_count(fo.rank, fo.v);
+    a.run = (long long)fc.v[fc.rank - 1];
+    a.count = count;
+    a.divisor = divisor;
+    constexpr int N = Pack<T>::N;
+    a.vec = a.run % N == 0 && (uintptr_t(in) & 15u) == 0;
+    for (uint32_t ax = 0; a.vec && ax < kc.rank; ++ax) a.vec = kcs.v[ax] % N == 0;
+    for (uint32_t ax = 0; a.vec && ax < fo.rank; ++ax) a.vec = fos.v[ax] % N == 0;
+    if (MODE == M_VAR) {
+      a.splits = 1;
+      unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
+      reduce_rows_var<T><<<std::max(1u, grid), 256, 0, stream>>>(in, a, o);
+      return check_launch("reduce (rows, variance)");
+    }
+    // Split each slice into shares (of whole runs, or of its one run's
+    // units) while there are fewer than ~16 warps of work per SM and a share
+    // keeps at least two batches of loads per lane.
+    const long long per_run = a.vec ? a.run / N : a.run;
+    long long splits = 1;
+    if (a.outer > 1) {
+      while (results * splits < (long long)sms * 16 && a.outer / (splits * 2) >= 1 &&
+             (a.outer / (splits * 2)) * per_run >= 32LL * 8 * 2)
+        splits *= 2;
+      a.share = (a.outer + splits - 1) / splits;
+    } else {
+      while (results * splits < (long long)sms * 16 && per_run / (splits * 2) >= 32LL * 8 * 2) splits *= 2;
+      a.share = (per_run + splits - 1) / splits;
+    }
+    a.splits = int(splits);
+    Acc *partial = nullptr;
+    if (splits > 1) {
+      void *p = nullptr;
+      if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p)) return st;
+      partial = static_cast<Acc *>(p);
+    }
+    const long long groups = results * splits;
+    unsigned grid = unsigned(std::min<long long>((groups + 7) / 8, (long long)sms * 16));
+    reduce_rows<T, MODE><<<std::max(1u, grid), 256, 0, stream>>>(in, a, o, arg_out, partial);
+    if (splits > 1) {
+      unsigned g2 = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
+      reduce_finish<T, MODE><<<std::max(1u, g2), 256, 0, stream>>>(a, partial, o, arg_out);
+    }
+    return check_launch("reduce (rows)");
+  }
+  ColsArgs a{};
+  a.depth = depth;
+  a.count = count;
+  a.divisor = divisor;
+  if (kept_inner_contig) {
+    a.K = (long long)kc.v[kc.rank - 1];
+    Dims ko = kc, kos = kcs;
+    ko.rank = kos.rank = kc.rank - 1;
+    a.kept_outer = (long long)element_count(ko.rank, ko.v);
+    fill_walk(a.kept, ko, kos);
+    fill_walk(a.folded, fc, fcs);
+    // Four results per thread when every row of them starts 4-aligned.
+    bool four = a.K % 4 == 0 && (uintptr_t(in) % (4 * sizeof(S))) == 0;
+    for (uint32_t ax = 0; four && ax < ko.rank; ++ax) four = kos.v[ax] % 4 == 0;
+    for (uint32_t ax = 0; four && ax < fc.rank; ++ax) four = fcs.v[ax] % 4 == 0;
+    const int cpt = four ? 4 : 1;
+    const long long tiles = a.kept_outer * ((a.K + 32 * cpt - 1) / (32 * cpt));
+    unsigned grid = unsigned(std::min<long long>(tiles, (long long)sms * 8));
+    if (four) reduce_cols<T, MODE, 4><<<std::max(1u, grid), dim3(32, 8), 0, stream>>>(in, a, o, arg_out);
+    else reduce_cols<T, MODE, 1><<<std::max(1u, grid), dim3(32, 8), 0, stream>>>(in, a, o, arg_out);
+    return check_launch("reduce (columns)");
+  }
+  fill_walk(a.kept, kc, kcs);
+  fill_walk(a.folded, fc, fcs);
+  unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
+  reduce_walk<T, MODE><<<std::max(1u, grid), 256, 0, stream>>>(in, a, results, o, arg_out);
+  return check_launch("reduce (walk)");
+}
+
 // The shared driver of reduce_axes and arg_reduce.
 int run_reduction(int dtype, uint32_t rank, const size_t *shape, const void *input, size_t offset,
                   const size_t *strides, const bool *folded, int mode, size_t divisor, void *out,
                   uint32_t *arg_out, cudaStream_t stream) {
-  // Split, strided.rs / layout.rs:370-414.
+  // Split, layout.rs:370-414.
   size_t ks[TC_MAX_RANK], kst[TC_MAX_RANK], fs[TC_MAX_RANK], fst[TC_MAX_RANK];
   uint32_t nk = 0, nf = 0;
   for (uint32_t a = 0; a < rank; ++a) {
     if (folded[a]) { fs[nf] = shape[a]; fst[nf++] = strides[a]; }
     else { ks[nk] = shape[a]; kst[nk++] = strides[a]; }
   }
-  size_t results = element_count(nk, ks), depth = element_count(nf, fs);
+  const long long results = (long long)element_count(nk, ks), depth = (long long)element_count(nf, fs);
   if (results == 0) return TC_OK;
   if (depth == 0) return fail(TC_EINVAL, "reduction over an empty slice");
-  // Kept axes: coalesce input strides against the contiguous result
-  // strides, so results stay in row-major order.
+  // Kept axes coalesce against the contiguous result strides, so results
+  // stay in row-major order; folded axes coalesce among themselves (an
+  // arg-reduction's one axis stays one axis).
   size_t kout[TC_MAX_RANK];
   contiguous_strides(nk, ks, kout);
   const size_t *kops[2] = {kst, kout};
@@ -432,114 +558,71 @@ int run_reduction(int dtype, uint32_t rank, const size_t *shape, const void *inp
   const size_t *fops[1] = {fst};
   Dims fc, fcs[1];
   coalesce<1>(nf, fs, fops, fc, fcs);
-  // An arg-reduction's position is the coordinate along its one axis; its
-  // folded space is that axis alone (coalesce keeps it one axis).
   const float count = float(depth), div = float(double(divisor));
-
   return with_real(dtype, [&](auto t) -> int {
     using T = decltype(t);
-    using S = typename T::S;
-    const S *in = static_cast<const S *>(input) + offset;
-    S *o = static_cast<S *>(out);
-    Layout2 L{};
-    fill_walk(L.kept, kc, kcs[0], 0);
-
-    // rows: innermost folded axis contiguous.
-    if (fc.rank >= 1 && fcs[0].v[fc.rank - 1] == 1 && !(kc.rank && kcs[0].v[kc.rank - 1] == 1 && fc.v[fc.rank - 1] < 64)) {
-      long long run = (long long)fc.v[fc.rank - 1];
-      Dims fo = fc, fos = fcs[0];
-      fo.rank = fos.rank = fc.rank - 1;
-      long long outer = (long long)element_count(fo.rank, fo.v);
-      fill_walk(L.folded, fo, fos, 0);
-      constexpr int N = Pack<T>::N;
-      bool vec = run % N == 0 && (uintptr_t(in) & 15u) == 0;
-      for (uint32_t a = 0; vec && a < kc.rank; ++a) vec = kcs[0].v[a] % N == 0;
-      for (uint32_t a = 0; vec && a < fo.rank; ++a) vec = fos.v[a] % N == 0;
-      long long warps_total = (long long)sm_count() * 64;  // resident warps
-      if ((long long)results >= warps_total / 2 || (long long)depth <= 4096) {
-        unsigned grid = unsigned(std::min<long long>(((long long)results + 7) / 8, (long long)sm_count() * 8));
-        reduce_rows<T, false><<<std::max(1u, grid), 256, 0, stream>>>(in, L, (long long)results, outer, run, mode,
-                                                                      count, div, o, arg_out, vec);
-      } else {
-        unsigned grid = unsigned(std::min<long long>((long long)results, (long long)sm_count() * 8));
-        reduce_rows<T, true><<<std::max(1u, grid), 256, 0, stream>>>(in, L, (long long)results, outer, run, mode,
-                                                                     count, div, o, arg_out, vec);
-      }
-      return check_launch("reduce (rows)");
+    const typename T::S *in = static_cast<const typename T::S *>(input) + offset;
+    switch (mode) {
+      case M_SUM: return launch_mode<T, M_SUM>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_MIN: return launch_mode<T, M_MIN>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_MAX: return launch_mode<T, M_MAX>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_MEAN: return launch_mode<T, M_MEAN>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_VAR: return launch_mode<T, M_VAR>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_ARGMIN: return launch_mode<T, M_ARGMIN>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_ARGMAX: return launch_mode<T, M_ARGMAX>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
     }
-    // columns: innermost kept axis contiguous.
-    if (kc.rank >= 1 && kcs[0].v[kc.rank - 1] == 1) {
-      long long K = (long long)kc.v[kc.rank - 1];
-      Dims ko = kc, kos = kcs[0];
-      ko.rank = kos.rank = kc.rank - 1;
-      long long kept_outer = (long long)element_count(ko.rank, ko.v);
-      fill_walk(L.kept, ko, kos, 0);
-      fill_walk(L.folded, fc, fcs[0], 0);
-      // Four results per thread when every row of them starts 4-aligned.
-      bool four = K % 4 == 0 && (uintptr_t(in) % (4 * sizeof(S))) == 0;
-      for (uint32_t a = 0; four && a < ko.rank; ++a) four = kos.v[a] % 4 == 0;
-      for (uint32_t a = 0; four && a < fc.rank; ++a) four = fcs[0].v[a] % 4 == 0;
-      const int cpt = four ? 4 : 1;
-      long long tiles = kept_outer * ((K + 32 * cpt - 1) / (32 * cpt));
-      int Y = 8;
-      unsigned grid = unsigned(std::min<long long>(tiles, (long long)sm_count() * 8));
-      if (four)
-        reduce_cols<T, 4><<<std::max(1u, grid), dim3(32, Y), 0, stream>>>(in, L, kept_outer, K, (long long)depth,
-                                                                           mode, count, div, o, arg_out);
-      else
-        reduce_cols<T, 1><<<std::max(1u, grid), dim3(32, Y), 0, stream>>>(in, L, kept_outer, K, (long long)depth,
-                                                                           mode, count, div, o, arg_out);
-      return check_launch("reduce (columns)");
-    }
-    fill_walk(L.folded, fc, fcs[0], 0);
-    unsigned grid = unsigned(std::min<long long>(((long long)results + 7) / 8, (long long)sm_count() * 8));
-    reduce_walk<T><<<std::max(1u, grid), 256, 0, stream>>>(in, L, (long long)results, (long long)depth, mode,
-                                                            count, div, o, arg_out);
-    return check_launch("reduce (walk)");
+    return fail(TC_EINVAL, "reduction mode %d", mode);
   });
 }
 
 // Whole-vector fold / dot: per-block partials, then one block folds them.
-template <class T>
+template <class T, int F>
 __global__ void __launch_bounds__(256) vector_partials(const typename T::S *a, const typename T::S *b, size_t n,
-                                                       int mode, float *partials) {
-  __shared__ Acc scratch[32];
-  Acc acc = identity(mode);
+                                                       float *partials) {
+  __shared__ Acc sh[8];
+  Acc acc = identity<F>();
   for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
     float x = T::load(a[i]);
     if (b) x = __fmul_rn(x, T::load(b[i]));
-    push(mode, acc, x, 0);
+    push<F>(acc, x, 0);
   }
-  acc = block_merge(mode, acc, scratch);
-  if (threadIdx.x == 0) partials[blockIdx.x] = acc.v;
+  acc = warp_merge<F>(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Acc r = sh[0];
+    for (int w = 1; w < int(blockDim.x >> 5); ++w) r = merge<F>(r, sh[w]);
+    partials[blockIdx.x] = r.v;
+  }
 }
-template <class T>
-__global__ void __launch_bounds__(256) vector_finish(const float *partials, int count, int mode,
-                                                     typename T::S *out) {
-  __shared__ Acc scratch[32];
-  Acc acc = identity(mode);
-  for (int i = threadIdx.x; i < count; i += blockDim.x) push(mode, acc, partials[i], 0);
-  acc = block_merge(mode, acc, scratch);
-  if (threadIdx.x == 0) out[0] = T::store(acc.v);
+template <class T, int F>
+__global__ void __launch_bounds__(256) vector_finish(const float *partials, int count, typename T::S *out) {
+  __shared__ Acc sh[8];
+  Acc acc = identity<F>();
+  for (int i = threadIdx.x; i < count; i += blockDim.x) push<F>(acc, partials[i], 0);
+  acc = warp_merge<F>(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Acc r = sh[0];
+    for (int w = 1; w < int(blockDim.x >> 5); ++w) r = merge<F>(r, sh[w]);
+    out[0] = T::store(r.v);
+  }
 }
 
-int vector_fold(int dtype, int mode, const void *a, const void *b, size_t n, void *out, cudaStream_t stream) {
+template <int F>
+int vector_fold(int dtype, const void *a, const void *b, size_t n, void *out, cudaStream_t stream) {
   if (!out) return fail(TC_EINVAL, "vector reduce: null output");
   const int max_blocks = 1024;
-  static thread_local float *partials[64] = {nullptr};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return fail(TC_EINVAL, "device %d", dev);
-  if (!partials[dev]) {
-    if (int st = check_cuda(cudaMalloc(&partials[dev], max_blocks * sizeof(float)), "cudaMalloc")) return st;
-  }
+  void *p = nullptr;
+  if (int st = scratch_get(max_blocks * sizeof(float), &p)) return st;
+  float *partials = static_cast<float *>(p);
   return with_real(dtype, [&](auto t) -> int {
     using T = decltype(t);
     using S = typename T::S;
     int blocks = int(std::min<size_t>(std::max<size_t>((n + 255) / 256, 1), size_t(max_blocks)));
-    vector_partials<T><<<blocks, 256, 0, stream>>>(static_cast<const S *>(a), static_cast<const S *>(b), n, mode,
-                                                    partials[dev]);
-    vector_finish<T><<<1, 256, 0, stream>>>(partials[dev], blocks, mode, static_cast<S *>(out));
+    vector_partials<T, F><<<blocks, 256, 0, stream>>>(static_cast<const S *>(a), static_cast<const S *>(b), n, partials);
+    vector_finish<T, F><<<1, 256, 0, stream>>>(partials, blocks, static_cast<S *>(out));
     return check_launch("vector reduce");
   });
 }
@@ -565,19 +648,18 @@ int tc_reduce_axes(int dtype, uint32_t rank, const size_t *shape, const void *in
   int mode;
   if (kind == TC_AXIS_FOLD) {
     if (op < TC_SUM || op > TC_RMAX) return fail(TC_EINVAL, "reduce_axes: bad Reduce %d", op);
-    mode = op == TC_SUM ? FOLD_SUM : (op == TC_RMIN ? FOLD_MIN : FOLD_MAX);
+    mode = op == TC_SUM ? M_SUM : (op == TC_RMIN ? M_MIN : M_MAX);
   } else if (kind == TC_AXIS_MEAN) {
-    mode = MEAN;
+    mode = M_MEAN;
   } else if (kind == TC_AXIS_VARIANCE) {
-    mode = VARIANCE;
+    mode = M_VAR;
   } else {
     return fail(TC_EINVAL, "reduce_axes: bad AxisReduction %d", kind);
   }
   if (element_count(rank, shape) == 0) {
-    // Every result folds an empty slice: the front-end never asks; a
-    // non-empty result set over an empty slice is an error.
     size_t results = 1;
-    for (uint32_t a = 0; a < rank; ++a) if (!folded[a]) results *= shape[a];
+    for (uint32_t a = 0; a < rank; ++a)
+      if (!folded[a]) results *= shape[a];
     return results == 0 ? TC_OK : fail(TC_EINVAL, "reduce_axes: slices are empty");
   }
   if (!input || !out) return fail(TC_EINVAL, "reduce_axes: null pointer");
@@ -596,21 +678,21 @@ int tc_arg_reduce(int dtype, uint32_t rank, const size_t *shape, const void *inp
   if (!input || !out) return fail(TC_EINVAL, "arg_reduce: null pointer");
   bool folded[TC_MAX_RANK] = {false};
   folded[axis] = true;
-  // A size-1 axis is dropped by coalescing; its answer is 0 everywhere.
-  return run_reduction(dtype, rank, shape, input, offset, strides, folded, op == TC_RMAX ? ARG_MAX : ARG_MIN, 0,
+  return run_reduction(dtype, rank, shape, input, offset, strides, folded, op == TC_RMAX ? M_ARGMAX : M_ARGMIN, 0,
                        nullptr, out, as_stream(stream));
 }
 
 int tc_vector_reduce(int dtype, int op, const void *a, size_t n, void *out, void *stream) {
   if (op < TC_SUM || op > TC_RMAX) return fail(TC_EINVAL, "vector_reduce: bad Reduce %d", op);
   if (n && !a) return fail(TC_EINVAL, "vector_reduce: null input");
-  int mode = op == TC_SUM ? FOLD_SUM : (op == TC_RMIN ? FOLD_MIN : FOLD_MAX);
-  return vector_fold(dtype, mode, a, nullptr, n, out, as_stream(stream));
+  if (op == TC_SUM) return vector_fold<M_SUM>(dtype, a, nullptr, n, out, as_stream(stream));
+  if (op == TC_RMIN) return vector_fold<M_MIN>(dtype, a, nullptr, n, out, as_stream(stream));
+  return vector_fold<M_MAX>(dtype, a, nullptr, n, out, as_stream(stream));
 }
 
 int tc_dot(int dtype, const void *a, const void *b, size_t n, void *out, void *stream) {
   if (n && (!a || !b)) return fail(TC_EINVAL, "dot: null input");
-  return vector_fold(dtype, FOLD_SUM, a, b, n, out, as_stream(stream));
+  return vector_fold<M_SUM>(dtype, a, b, n, out, as_stream(stream));
 }
 
 }  // extern "C"
