@@ -243,8 +243,40 @@ int tc_device_status(int *fault);
 int tc_coalesce(uint32_t rank, const size_t *shape, uint32_t n_ops, const size_t *strides,
                 uint32_t *out_rank, size_t *out_shape, size_t *out_strides);
 
-/* ---- multi-GPU (NCCL over NVLink; no counterpart in the reference) ------ */
+/* ---- the tape and the optimizer, run natively (host-side mirror) --------- */
+/* One training step of a dense ReLU network exactly as the reference's
+ * reverse-mode tape and Adam rule run it on any backend
+ * (benches/nn_ops.rs:877-921; tape rules src/tensors/tape/mod.rs:979-988,
+ * 1026-1033, 1110-1130, 1174, 1195-1216, 1286-1300; Adam src/optim.rs:
+ * 1001-1140), driven from C++ through the kernels above.  There is no
+ * single-call counterpart in the reference: it is the Rust code above the
+ * Kernels<T> boundary, restated so the path can run where no Rust toolchain
+ * exists.  dims[0..layers] are the widths, inputs first; activations are
+ * [width x batch], one column per sample.  global_batch scales the loss (the
+ * sum over ranks of a data-parallel step's gradients is then the global
+ * gradient). */
+typedef struct tc_mlp tc_mlp;
 typedef struct tc_comm tc_comm;
+int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t batch,
+                  uint32_t global_batch, double rate, double beta1, double beta2, double eps,
+                  tc_mlp **out);
+int tc_mlp_destroy(tc_mlp *mlp);
+/* dir = 0 uploads layer `layer`'s weight [dims[l+1] x dims[l]] and bias from
+ * the host, dir = 1 downloads them. */
+int tc_mlp_params(tc_mlp *mlp, uint32_t layer, void *w_host, void *b_host, int dir);
+/* The gradients the last step computed (summed over ranks when it ran with
+ * a communicator). */
+int tc_mlp_grads(tc_mlp *mlp, uint32_t layer, void *gw_host, void *gb_host);
+/* Skip the adjoints nothing reads (inputs', targets', ones'); off by
+ * default, as the tape computes them. */
+int tc_mlp_prune_leaves(tc_mlp *mlp, int prune);
+/* Forward, loss into loss_dev[0] if not NULL, backward, NCCL gradient
+ * all-reduce over `comm` if not NULL (overlapped with the backward pass),
+ * then Adam on every parameter.  x, y are device buffers. */
+int tc_mlp_step(tc_mlp *mlp, const void *x_dev, const void *y_dev, tc_comm *comm, void *loss_dev,
+                void *stream);
+
+/* ---- multi-GPU (NCCL over NVLink; no counterpart in the reference) ------ */
 /* 128 opaque bytes (ncclUniqueId) for rank 0 to share with the others. */
 int tc_comm_unique_id(uint8_t id[128]);
 int tc_comm_init(int rank, int nranks, const uint8_t id[128], tc_comm **out);

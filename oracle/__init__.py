@@ -46,6 +46,9 @@ SIGNATURES = {
     "orc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d],
     "orc_sgd": [_i, _sz, _p, _p, _d],
     "orc_adam_coefficients": [_i, _d, _d, _d, _d, _u32, C.POINTER(C.c_double)],
+    "orc_mlp_params": [_p, _u32, _p, _p, _i],
+    "orc_mlp_grads": [_p, _u32, _p, _p],
+    "orc_mlp_step": [_p, _p, _p, _p, _i],
 }
 
 DTYPES = {"f32": 0, "f16": 1, "bf16": 2}
@@ -72,6 +75,10 @@ def lib() -> C.CDLL:
         h.orc_narrow.restype = None
         h.orc_widen.argtypes = [_i, _p, _p, _sz]
         h.orc_widen.restype = None
+        h.orc_mlp_create.argtypes = [_i, _u32, _u32p, _u32, _u32, _d, _d, _d, _d]
+        h.orc_mlp_create.restype = _p
+        h.orc_mlp_destroy.argtypes = [_p]
+        h.orc_mlp_destroy.restype = None
         h.orc_set_threads.argtypes = [_i]
         h.orc_set_threads.restype = None
         _lib = h

@@ -1001,3 +1001,145 @@ int orc_adam_coefficients(int dtype, double rate, double beta1, double beta2, do
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// One MLP training step as the reference's tape runs it (benches/nn_ops.rs:
+// 877-921 with any number of layers; tape rules tape/mod.rs:979-988, 1026-
+// 1033, 1110-1130, 1174, 1195-1216, 1286-1300), through the Host functions
+// above, then Adam on every parameter (optim.rs:1106-1140).
+// ---------------------------------------------------------------------------
+struct OrcMlp {
+  int dtype;
+  size_t esz;
+  int layers;
+  std::vector<size_t> dims;
+  size_t batch, global_batch;
+  double rate, beta1, beta2, eps;
+  uint32_t steps = 0;
+  std::vector<std::vector<uint8_t>> W, b, gW, gb, mW, vW, mb, vb;
+};
+
+extern "C" {
+
+void *orc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t batch, uint32_t global_batch,
+                     double rate, double beta1, double beta2, double eps) {
+  OrcMlp *m = new OrcMlp;
+  m->dtype = dtype;
+  m->esz = dtype == TC_F32 ? 4 : 2;
+  m->layers = int(layers);
+  m->dims.assign(dims, dims + layers + 1);
+  m->batch = batch;
+  m->global_batch = global_batch ? global_batch : batch;
+  m->rate = rate; m->beta1 = beta1; m->beta2 = beta2; m->eps = eps;
+  for (int l = 0; l < m->layers; ++l) {
+    size_t nw = m->dims[l + 1] * m->dims[l], nb = m->dims[l + 1];
+    for (auto *v : {&m->W, &m->gW, &m->mW, &m->vW}) v->emplace_back(nw * m->esz, 0);
+    for (auto *v : {&m->b, &m->gb, &m->mb, &m->vb}) v->emplace_back(nb * m->esz, 0);
+  }
+  return m;
+}
+
+void orc_mlp_destroy(void *p) { delete static_cast<OrcMlp *>(p); }
+
+int orc_mlp_params(void *p, uint32_t l, void *w, void *b, int dir) {
+  OrcMlp *m = static_cast<OrcMlp *>(p);
+  if (int(l) >= m->layers) return int(TC_EINVAL);
+  if (dir == 0) {
+    if (w) std::memcpy(m->W[l].data(), w, m->W[l].size());
+    if (b) std::memcpy(m->b[l].data(), b, m->b[l].size());
+  } else {
+    if (w) std::memcpy(w, m->W[l].data(), m->W[l].size());
+    if (b) std::memcpy(b, m->b[l].data(), m->b[l].size());
+  }
+  return int(TC_OK);
+}
+
+int orc_mlp_grads(void *p, uint32_t l, void *gw, void *gb) {
+  OrcMlp *m = static_cast<OrcMlp *>(p);
+  if (int(l) >= m->layers) return int(TC_EINVAL);
+  if (gw) std::memcpy(gw, m->gW[l].data(), m->gW[l].size());
+  if (gb) std::memcpy(gb, m->gb[l].data(), m->gb[l].size());
+  return int(TC_OK);
+}
+
+// x: [dims[0] x batch], y: [dims[L] x batch]; loss_out (one element) if
+// not null.  `skip_update` leaves the parameters as they are (gradients
+// only), for checking a data-parallel gradient sum.
+int orc_mlp_step(void *p, const void *x, const void *y, void *loss_out, int skip_update) {
+  OrcMlp *m = static_cast<OrcMlp *>(p);
+  const int d = m->dtype, L = m->layers;
+  const size_t B = m->batch, e = m->esz;
+  using Bytes = std::vector<uint8_t>;
+  auto buf = [&](size_t n) { return Bytes(n * e, 0); };
+  Bytes ones = buf(B);
+  {
+    std::vector<float> one(B, 1.0f);
+    if (d == TC_F32) std::memcpy(ones.data(), one.data(), B * 4);
+    else orc_narrow(d, one.data(), ones.data(), B);
+  }
+  std::vector<Bytes> Z, O, A, H;
+  for (int l = 0; l < L; ++l) {
+    const size_t in = m->dims[l], outd = m->dims[l + 1];
+    const void *input = l == 0 ? x : H[l - 1].data();
+    Z.push_back(buf(outd * B));
+    O.push_back(buf(outd * B));
+    A.push_back(buf(outd * B));
+    H.push_back(buf(outd * B));
+    orc_matmul(d, TC_TRANS_NONE, outd, in, B, m->W[l].data(), input, Z[l].data(), 0);
+    orc_matmul(d, TC_TRANS_NONE, outd, 1, B, m->b[l].data(), ones.data(), O[l].data(), 0);
+    orc_elementwise(d, TC_ADD, Z[l].data(), O[l].data(), A[l].data(), outd * B);
+    if (l + 1 < L) orc_compare_scalar(d, TC_MAX, A[l].data(), 0.0, 0, H[l].data(), outd * B);
+  }
+  const size_t last = m->dims[L];
+  Bytes R = buf(last * B), S = buf(last * B);
+  orc_elementwise(d, TC_SUB, A[L - 1].data(), y, R.data(), last * B);
+  orc_elementwise(d, TC_MUL, R.data(), R.data(), S.data(), last * B);
+  // scale factor in the element type
+  double f = 1.0 / (double(last) * double(m->global_batch));
+  double coef[6];
+  orc_adam_coefficients(d, f, 0.5, 0.5, 0.5, 1, coef);  // coef[0] = f rounded to T
+  const double factor = coef[0];
+  if (loss_out) {
+    Bytes total = buf(1);
+    orc_vector_reduce(d, TC_SUM, S.data(), last * B, total.data());
+    orc_broadcast_scalar(d, TC_MUL, total.data(), factor, 0, loss_out, 1);
+  }
+  // backward
+  Bytes Sbar = buf(last * B), T1 = buf(last * B), T2 = buf(last * B), Rbar = buf(last * B);
+  {
+    std::vector<float> fill(last * B, float(factor));
+    if (d == TC_F32) std::memcpy(Sbar.data(), fill.data(), fill.size() * 4);
+    else orc_narrow(d, fill.data(), Sbar.data(), fill.size());
+  }
+  orc_elementwise(d, TC_MUL, Sbar.data(), R.data(), T1.data(), last * B);
+  orc_elementwise(d, TC_MUL, Sbar.data(), R.data(), T2.data(), last * B);
+  orc_elementwise(d, TC_ADD, T1.data(), T2.data(), Rbar.data(), last * B);
+  Bytes abar = Rbar;
+  for (int l = L - 1; l >= 0; --l) {
+    const size_t in = m->dims[l], outd = m->dims[l + 1];
+    const void *input = l == 0 ? x : H[l - 1].data();
+    orc_matvec(d, outd, B, abar.data(), ones.data(), m->gb[l].data(), 0);
+    orc_matmul(d, TC_TRANS_RIGHT, outd, B, in, abar.data(), input, m->gW[l].data(), 0);
+    if (l > 0) {
+      Bytes inbar = buf(in * B), share = buf(in * B), next = buf(in * B);
+      orc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].data(), abar.data(), inbar.data(), 0);
+      orc_compare_scalar(d, TC_MAX_SHARE, A[l - 1].data(), 0.0, 0, share.data(), in * B);
+      orc_elementwise(d, TC_MUL, inbar.data(), share.data(), next.data(), in * B);
+      abar.swap(next);
+    }
+  }
+  if (skip_update) return int(TC_OK);
+  m->steps += 1;
+  double k[6];
+  orc_adam_coefficients(d, m->rate, m->beta1, m->beta2, m->eps, m->steps, k);
+  const int resumed = m->steps > 1;
+  for (int l = 0; l < L; ++l) {
+    orc_adam(d, m->W[l].size() / e, m->W[l].data(), m->gW[l].data(), m->mW[l].data(), m->vW[l].data(), resumed,
+             k[0], k[1], k[2], k[3], k[4], k[5]);
+    orc_adam(d, m->b[l].size() / e, m->b[l].data(), m->gb[l].data(), m->mb[l].data(), m->vb[l].data(), resumed,
+             k[0], k[1], k[2], k[3], k[4], k[5]);
+  }
+  return int(TC_OK);
+}
+
+}  // extern "C"

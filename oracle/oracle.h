@@ -91,6 +91,14 @@ int orc_sgd(int dtype, size_t n, void *p, const void *g, double rate);
 int orc_adam_coefficients(int dtype, double rate, double beta1, double beta2, double eps,
                           uint32_t step, double *out);
 
+/* One MLP training step through the tape's rules and Adam (see oracle.cpp). */
+void *orc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t batch, uint32_t global_batch,
+                     double rate, double beta1, double beta2, double eps);
+void orc_mlp_destroy(void *mlp);
+int orc_mlp_params(void *mlp, uint32_t layer, void *w, void *b, int dir);
+int orc_mlp_grads(void *mlp, uint32_t layer, void *gw, void *gb);
+int orc_mlp_step(void *mlp, const void *x, const void *y, void *loss_out, int skip_update);
+
 /* Host threads the elementwise kernels may use (set_host_threads,
  * src/parallel.rs:40); 0 = all. */
 void orc_set_threads(int threads);

@@ -82,6 +82,12 @@ SIGNATURES = {
     "tc_sgd": [_i, _sz, _p, _p, _d, _p],
     "tc_coalesce": [_u32, _szp, _u32, _szp, _u32p, _szp, _szp],
     "tc_device_status": [C.POINTER(_i)],
+    "tc_mlp_create": [_i, _u32, _u32p, _u32, _u32, _d, _d, _d, _d, C.POINTER(_p)],
+    "tc_mlp_destroy": [_p],
+    "tc_mlp_params": [_p, _u32, _p, _p, _i],
+    "tc_mlp_grads": [_p, _u32, _p, _p],
+    "tc_mlp_prune_leaves": [_p, _i],
+    "tc_mlp_step": [_p, _p, _p, _p, _p, _p],
     "tc_comm_unique_id": [C.POINTER(C.c_uint8)],
     "tc_comm_init": [_i, _i, C.POINTER(C.c_uint8), C.POINTER(_p)],
     "tc_comm_destroy": [_p],

@@ -80,6 +80,37 @@ __global__ void __launch_bounds__(256) vecmat_cols(const typename T::S *x, const
   }
 }
 
+// An inner dimension of one: C[i, j] (+)= a[i] * b[j], one rounding (the
+// product of two stored values is exact in f32).  The tape's outer product
+// b ⊗ ones is this (tape/mod.rs:1000-1005).  Packs of 16 bytes along j.
+template <class T>
+__global__ void __launch_bounds__(256) outer_rows(const typename T::S *a, const typename T::S *b, typename T::S *c,
+                                                  long long rows, long long cols, bool accumulate, bool vec) {
+  constexpr int N = Pack<T>::N;
+  const long long per_row = vec ? cols / N : cols;
+  const long long total = rows * per_row;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / per_row, q = i - r * per_row;
+    const float ar = T::load(a[r]);
+    if (vec) {
+      Pack<T> bb, cc;
+      bb.raw = __ldg(reinterpret_cast<const uint4 *>(b + q * N));
+      if (accumulate) cc.raw = *reinterpret_cast<const uint4 *>(c + r * cols + q * N);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float v = __fmul_rn(ar, T::load(bb.v[j]));
+        if (accumulate) v = __fadd_rn(T::load(cc.v[j]), v);
+        cc.v[j] = T::store(v);
+      }
+      *reinterpret_cast<uint4 *>(c + r * cols + q * N) = cc.raw;
+    } else {
+      float v = __fmul_rn(ar, T::load(b[q]));
+      if (accumulate) v = __fadd_rn(T::load(c[r * cols + q]), v);
+      c[r * cols + q] = T::store(v);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace tc
 
@@ -132,6 +163,21 @@ int tc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
   }
   if (!a || !b) return fail(TC_EINVAL, "matmul: null operand");
   cudaStream_t s = as_stream(stream);
+  if (inner == 1) {
+    // [rows x 1]·[1 x cols]: every storage order of either operand is the same.
+    return with_real(dtype, [&](auto t) {
+      using T = decltype(t);
+      using S = typename T::S;
+      constexpr int N = Pack<T>::N;
+      const bool vec = cols % N == 0 && (uintptr_t(b) & 15u) == 0 && (uintptr_t(c) & 15u) == 0;
+      const long long work = (long long)rows * (vec ? (long long)cols / N : (long long)cols);
+      outer_rows<T><<<grid_for(size_t(work), 256, 8), 256, 0, s>>>(static_cast<const S *>(a),
+                                                                    static_cast<const S *>(b), static_cast<S *>(c),
+                                                                    (long long)rows, (long long)cols,
+                                                                    accumulate != 0, vec);
+      return check_launch("matmul (outer)");
+    });
+  }
   if (dtype != TC_F32) {
     int st = gemm_tc_run(dtype, transposed, rows, inner, cols, a, b, c, accumulate != 0, s);
     if (st != TC_ENOTSUP) return st;

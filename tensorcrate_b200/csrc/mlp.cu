@@ -1,0 +1,334 @@
+// mlp.cu — one training step of a dense ReLU network as tensorcrate's
+// reverse-mode tape runs it, replayed through this backend's kernels, and
+// the Adam rule's update of every parameter (config 4 of the benchmark).
+//
+// The network is the one benches/nn_ops.rs:877-921 builds, with any number
+// of layers: for each layer l
+//     Z = W_l · IN            (MatrixVar::matmul, tape/mod.rs:1195)
+//     O = b_l ⊗ ones          (VectorVar::outer, tape/mod.rs:979-988)
+//     A = Z + O               (MatrixVar binary Add, tape/mod.rs:1026-1033)
+//     H = relu(A)             (select_scalar Max, tape/mod.rs:1110-1130)
+// the last layer without the ReLU, then R = P - Y, S = R * R and the loss
+// sum(S) · 1/(outputs·batch) (frobenius_dot + scale, tape/mod.rs:1299,
+// 1174).  The backward pass visits the nodes in reverse order of creation
+// and applies each node's rule with the same Kernels<T> calls and operand
+// order the tape uses; copies the tape makes (`duplicate`) are elided where
+// a buffer can be shared, which cannot change a value.  Every leaf's adjoint
+// is computed, as the tape computes it, including the inputs', targets' and
+// the ones vector's.
+//
+// Under data parallelism each rank runs the step on its own batch with the
+// loss scaled by the global batch, and the parameter gradients are summed
+// with NCCL before Adam.  The reduction of each layer's gradients starts, on
+// a second stream, as soon as the backward pass has produced them.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+struct tc_comm;
+
+namespace tc {
+namespace {
+
+struct Buf {
+  void *p = nullptr;
+  size_t n = 0;
+};
+
+// Matrix::filled: every element `value` (rounded to the element type on
+// the host).
+template <class T>
+__global__ void fill_kernel(typename T::S *out, size_t n, typename T::S value) {
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    out[i] = value;
+}
+
+// Round a host value to the element type, as Real::from_f64 does (one
+// rounding from f64; round-to-odd into f32 first keeps it single).
+float round_to(int dtype, double d) {
+  float f = float(d);
+  if (dtype == TC_F32) return f;
+  if (std::isfinite(d) && double(f) != d && std::isfinite(f)) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if (std::fabs(double(f)) > std::fabs(d)) u -= 1;
+    u |= 1u;
+    memcpy(&f, &u, 4);
+  }
+  return dtype == TC_BF16 ? bf16_bits_to_f32(f32_to_bf16_bits(f)) : f16_bits_to_f32(f32_to_f16_bits(f));
+}
+float round_f32(int dtype, float f) {
+  if (dtype == TC_F32) return f;
+  return dtype == TC_BF16 ? bf16_bits_to_f32(f32_to_bf16_bits(f)) : f16_bits_to_f32(f32_to_f16_bits(f));
+}
+// f32 powi by square-and-multiply, the loop compiler-rt's __powisf2 runs
+// (what Rust's f32::powi lowers to); f16/bf16 powi is f32 powi, rounded.
+float powi(float a, int b) {
+  bool recip = b < 0;
+  float r = 1.0f;
+  for (;;) {
+    if (b & 1) r *= a;
+    b /= 2;
+    if (b == 0) break;
+    a *= a;
+  }
+  return recip ? 1.0f / r : r;
+}
+
+}  // namespace
+}  // namespace tc
+
+using namespace tc;
+
+struct tc_mlp {
+  int dtype = TC_BF16;
+  size_t esz = 2;
+  int layers = 0;
+  std::vector<size_t> dims;  // dims[0] inputs ... dims[layers] outputs
+  size_t batch = 0, global_batch = 0;
+  float rate = 0, beta1 = 0, beta2 = 0, eps = 0;  // element-type values
+  uint32_t steps = 0;
+  std::vector<Buf> W, b, gW, gb, mW, vW, mb, vb;
+  std::vector<Buf> Z, O, A, H;
+  Buf ones, R, S, T1, T2, Rbar, Ybar, Xbar, share, abar, inbar, onesbar, ovec, loss_sum;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> grad_ready;
+  cudaEvent_t reduced = nullptr;
+  bool prune = false;
+};
+
+namespace {
+
+int alloc(Buf &b, size_t n, size_t esz) {
+  b.n = n;
+  return tc_malloc(&b.p, std::max<size_t>(n * esz, 16));
+}
+
+// Adam::update's host arithmetic (optim.rs:1106-1124) in the element type.
+void adam_coefficients(const tc_mlp &m, uint32_t step, float &c1, float &c2) {
+  const int d = m.dtype;
+  float f1 = round_f32(d, 1.0f - round_f32(d, powi(m.beta1, int(step))));
+  float f2 = round_f32(d, 1.0f - round_f32(d, powi(m.beta2, int(step))));
+  c1 = round_f32(d, 1.0f / f1);
+  c2 = round_f32(d, 1.0f / f2);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t batch, uint32_t global_batch,
+                  double rate, double beta1, double beta2, double eps, tc_mlp **out) {
+  if (!out || !dims || layers == 0 || batch == 0) return fail(TC_EINVAL, "mlp_create: bad arguments");
+  if (dtype != TC_F32 && dtype != TC_F16 && dtype != TC_BF16) return fail(TC_EINVAL, "mlp_create: dtype");
+  tc_mlp *m = new tc_mlp;
+  m->dtype = dtype;
+  m->esz = dtype_bytes(dtype);
+  m->layers = int(layers);
+  m->dims.assign(dims, dims + layers + 1);
+  m->batch = batch;
+  m->global_batch = global_batch ? global_batch : batch;
+  m->rate = round_to(dtype, rate);
+  m->beta1 = round_to(dtype, beta1);
+  m->beta2 = round_to(dtype, beta2);
+  m->eps = round_to(dtype, eps);
+  const size_t B = batch, e = m->esz;
+  int st = TC_OK;
+  auto need = [&](Buf &x, size_t n) {
+    if (!st) st = alloc(x, n, e);
+  };
+  for (int l = 0; l < m->layers; ++l) {
+    const size_t in = m->dims[l], outd = m->dims[l + 1];
+    m->W.emplace_back(); m->b.emplace_back(); m->gW.emplace_back(); m->gb.emplace_back();
+    m->mW.emplace_back(); m->vW.emplace_back(); m->mb.emplace_back(); m->vb.emplace_back();
+    m->Z.emplace_back(); m->O.emplace_back(); m->A.emplace_back(); m->H.emplace_back();
+    need(m->W[l], outd * in); need(m->gW[l], outd * in); need(m->mW[l], outd * in); need(m->vW[l], outd * in);
+    need(m->b[l], outd); need(m->gb[l], outd); need(m->mb[l], outd); need(m->vb[l], outd);
+    need(m->Z[l], outd * B); need(m->O[l], outd * B); need(m->A[l], outd * B);
+    if (l + 1 < m->layers) need(m->H[l], outd * B);
+  }
+  size_t widest = 0;
+  for (size_t d : m->dims) widest = std::max(widest, d);
+  const size_t last = m->dims[m->layers];
+  need(m->ones, B); need(m->R, last * B); need(m->S, last * B); need(m->T1, last * B); need(m->T2, last * B);
+  need(m->Rbar, last * B); need(m->Ybar, last * B); need(m->Xbar, m->dims[0] * B);
+  need(m->share, widest * B); need(m->abar, widest * B); need(m->inbar, widest * B);
+  need(m->onesbar, B); need(m->ovec, B); need(m->loss_sum, 1);
+  if (st) {
+    tc_mlp_destroy(m);
+    return st;
+  }
+  // ones: the tape's constant vector of the batch's length
+  int rc = with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    fill_kernel<T><<<grid_for(B, 256), 256>>>(static_cast<typename T::S *>(m->ones.p), B, T::store(1.0f));
+    return check_launch("mlp ones");
+  });
+  if (rc || (rc = check_cuda(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking), "stream")) ||
+      (rc = check_cuda(cudaEventCreateWithFlags(&m->reduced, cudaEventDisableTiming), "event"))) {
+    tc_mlp_destroy(m);
+    return rc;
+  }
+  m->grad_ready.resize(m->layers);
+  for (auto &ev : m->grad_ready)
+    if ((rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event"))) {
+      tc_mlp_destroy(m);
+      return rc;
+    }
+  *out = m;
+  return TC_OK;
+}
+
+int tc_mlp_destroy(tc_mlp *m) {
+  if (!m) return TC_OK;
+  cudaDeviceSynchronize();
+  auto drop = [](Buf &b) {
+    if (b.p) tc_free(b.p);
+    b.p = nullptr;
+  };
+  for (auto *v : {&m->W, &m->b, &m->gW, &m->gb, &m->mW, &m->vW, &m->mb, &m->vb, &m->Z, &m->O, &m->A, &m->H})
+    for (auto &b : *v) drop(b);
+  for (Buf *b : {&m->ones, &m->R, &m->S, &m->T1, &m->T2, &m->Rbar, &m->Ybar, &m->Xbar, &m->share, &m->abar,
+                 &m->inbar, &m->onesbar, &m->ovec, &m->loss_sum})
+    drop(*b);
+  for (auto ev : m->grad_ready)
+    if (ev) cudaEventDestroy(ev);
+  if (m->reduced) cudaEventDestroy(m->reduced);
+  if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+  delete m;
+  return TC_OK;
+}
+
+// Upload (dir = 0) or download (dir = 1) layer `l`'s weight [dims[l+1] x
+// dims[l]] and bias [dims[l+1]], in the element type's storage form.
+int tc_mlp_params(tc_mlp *m, uint32_t l, void *w_host, void *b_host, int dir) {
+  if (!m || int(l) >= m->layers) return fail(TC_EINVAL, "mlp_params: layer %u", l);
+  const size_t wb = m->W[l].n * m->esz, bb = m->b[l].n * m->esz;
+  if (dir == 0) {
+    if (w_host) if (int st = tc_memcpy_h2d(m->W[l].p, w_host, wb, nullptr)) return st;
+    if (b_host) if (int st = tc_memcpy_h2d(m->b[l].p, b_host, bb, nullptr)) return st;
+    return TC_OK;
+  }
+  if (w_host) if (int st = tc_memcpy_d2h(w_host, m->W[l].p, wb, nullptr)) return st;
+  if (b_host) if (int st = tc_memcpy_d2h(b_host, m->b[l].p, bb, nullptr)) return st;
+  return TC_OK;
+}
+
+// Download layer `l`'s gradients (after a step): dW and db.
+int tc_mlp_grads(tc_mlp *m, uint32_t l, void *gw_host, void *gb_host) {
+  if (!m || int(l) >= m->layers) return fail(TC_EINVAL, "mlp_grads: layer %u", l);
+  if (gw_host) if (int st = tc_memcpy_d2h(gw_host, m->gW[l].p, m->gW[l].n * m->esz, nullptr)) return st;
+  if (gb_host) if (int st = tc_memcpy_d2h(gb_host, m->gb[l].p, m->gb[l].n * m->esz, nullptr)) return st;
+  return TC_OK;
+}
+
+// Skip the adjoints nothing reads (inputs', targets', the ones vector's).
+// Off by default: the tape computes them.
+int tc_mlp_prune_leaves(tc_mlp *m, int prune) {
+  if (!m) return fail(TC_EINVAL, "mlp: null");
+  m->prune = prune != 0;
+  return TC_OK;
+}
+
+int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void *stream);
+
+// One step: forward, loss (into loss_out, one element, if not null),
+// backward, optional gradient all-reduce over `comm`, Adam.  x: [dims[0] x
+// batch], y: [dims[L] x batch], both device buffers, column per sample.
+int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *loss_out, void *stream_v) {
+  if (!m || !x || !y) return fail(TC_EINVAL, "mlp_step: null argument");
+  cudaStream_t s = as_stream(stream_v);
+  const int d = m->dtype, L = m->layers;
+  const size_t B = m->batch;
+  void *st = stream_v;
+#define TRY(call)                   \
+  do {                              \
+    if (int rc_ = (call)) return rc_; \
+  } while (0)
+  // ---- forward ----
+  for (int l = 0; l < L; ++l) {
+    const size_t in = m->dims[l], outd = m->dims[l + 1];
+    const void *input = l == 0 ? x : m->H[l - 1].p;
+    TRY(tc_matmul(d, TC_TRANS_NONE, outd, in, B, m->W[l].p, input, m->Z[l].p, 0, st));
+    TRY(tc_matmul(d, TC_TRANS_NONE, outd, 1, B, m->b[l].p, m->ones.p, m->O[l].p, 0, st));  // b ⊗ ones
+    TRY(tc_elementwise(d, TC_ADD, m->Z[l].p, m->O[l].p, m->A[l].p, outd * B, st));
+    if (l + 1 < L) TRY(tc_compare_scalar(d, TC_MAX, m->A[l].p, 0.0, 0, m->H[l].p, outd * B, st));
+  }
+  const size_t last = m->dims[L];
+  TRY(tc_elementwise(d, TC_SUB, m->A[L - 1].p, y, m->R.p, last * B, st));
+  TRY(tc_elementwise(d, TC_MUL, m->R.p, m->R.p, m->S.p, last * B, st));
+  const float factor = round_to(d, 1.0 / (double(last) * double(m->global_batch)));
+  if (loss_out) {
+    // The lazy scalar, forced: sum of S (f32, rounded once), then `scale`.
+    TRY(tc_vector_reduce(d, TC_SUM, m->S.p, last * B, m->loss_sum.p, st));
+    TRY(tc_broadcast_scalar(d, TC_MUL, m->loss_sum.p, factor, 0, loss_out, 1, st));
+  }
+  // ---- backward ----
+  // sum's rule: S̄ = filled(adjoint), adjoint = 1 · factor (scale's rule).
+  TRY(with_real(d, [&](auto t) {
+    using T = decltype(t);
+    fill_kernel<T><<<grid_for(last * B, 256), 256, 0, s>>>(static_cast<typename T::S *>(m->T2.p), last * B,
+                                                            T::store(factor));
+    return check_launch("mlp fill");
+  }));
+  // S = R * R (binary Mul): left += S̄·right, right += S̄·left.
+  TRY(tc_elementwise(d, TC_MUL, m->T2.p, m->R.p, m->T1.p, last * B, st));
+  TRY(tc_elementwise(d, TC_MUL, m->T2.p, m->R.p, m->S.p, last * B, st));
+  TRY(tc_elementwise(d, TC_ADD, m->T1.p, m->S.p, m->Rbar.p, last * B, st));
+  // R = P - Y: P̄ += R̄ (shared), Ȳ += -R̄.
+  if (!m->prune) TRY(tc_broadcast_scalar(d, TC_MUL, m->Rbar.p, -1.0, 0, m->Ybar.p, last * B, st));
+  const void *abar = m->Rbar.p;  // Ā of the top layer = P̄
+  for (int l = L - 1; l >= 0; --l) {
+    const size_t in = m->dims[l], outd = m->dims[l + 1];
+    const void *input = l == 0 ? x : m->H[l - 1].p;
+    // A = Z + O: Z̄ = Ō = Ā (shared).  O = b ⊗ ones: b̄ += Ō·ones,
+    // ones̄ += bᵀ·Ō (vecmat), accumulated in node order.
+    TRY(tc_matvec(d, outd, B, abar, m->ones.p, m->gb[l].p, 0, st));
+    if (!m->prune) {
+      if (l == L - 1) TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, m->onesbar.p, st));
+      else {
+        TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, m->ovec.p, st));
+        TRY(tc_elementwise(d, TC_ADD, m->onesbar.p, m->ovec.p, m->onesbar.p, B, st));
+      }
+    }
+    // Z = W·IN: W̄ += Z̄·INᵀ, ĪN += Wᵀ·Z̄ (matmul_transposed_add, both
+    // adjoints starting from zero).
+    TRY(tc_matmul(d, TC_TRANS_RIGHT, outd, B, in, abar, input, m->gW[l].p, 0, st));
+    if (comm) {
+      TRY(check_cuda(cudaEventRecord(m->grad_ready[l], s), "event"));
+      TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0), "wait"));
+      TRY(tc_allreduce(comm, d, m->gW[l].p, m->gW[l].n, TC_SUM, m->comm_stream));
+      TRY(tc_allreduce(comm, d, m->gb[l].p, m->gb[l].n, TC_SUM, m->comm_stream));
+    }
+    if (l > 0) {
+      TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->inbar.p, 0, st));
+      // H = relu(A): Ā += H̄ · MaxShare(A, 0).
+      TRY(tc_compare_scalar(d, TC_MAX_SHARE, m->A[l - 1].p, 0.0, 0, m->share.p, in * B, st));
+      TRY(tc_elementwise(d, TC_MUL, m->inbar.p, m->share.p, m->abar.p, in * B, st));
+      abar = m->abar.p;
+    } else if (!m->prune) {
+      TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->Xbar.p, 0, st));
+    }
+  }
+  if (comm) {
+    TRY(check_cuda(cudaEventRecord(m->reduced, m->comm_stream), "event"));
+    TRY(check_cuda(cudaStreamWaitEvent(s, m->reduced, 0), "wait"));
+  }
+  // ---- Adam, per parameter in the order the driver updates them ----
+  m->steps += 1;
+  float c1, c2;
+  adam_coefficients(*m, m->steps, c1, c2);
+  const int resumed = m->steps > 1;
+  for (int l = 0; l < L; ++l) {
+    TRY(tc_adam(d, m->W[l].n, m->W[l].p, m->gW[l].p, m->mW[l].p, m->vW[l].p, resumed, m->rate, m->beta1, m->beta2,
+                m->eps, c1, c2, st));
+    TRY(tc_adam(d, m->b[l].n, m->b[l].p, m->gb[l].p, m->mb[l].p, m->vb[l].p, resumed, m->rate, m->beta1, m->beta2,
+                m->eps, c1, c2, st));
+  }
+#undef TRY
+  return TC_OK;
+}
+
+}  // extern "C"

@@ -118,3 +118,17 @@ def test_no_gemm_wait_gave_up(device):
     fault = C.c_int(0)
     N.call("tc_device_status", C.byref(fault))
     assert fault.value == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("transposed", [N.TRANS_NONE, N.TRANS_LEFT, N.TRANS_RIGHT])
+def test_outer_products(device, dtype, transposed):
+    """An inner dimension of one (the tape's b ⊗ ones, tape/mod.rs:1000-1005):
+    one rounding of an exact product, so f16/bf16 match bit for bit."""
+    for (m, n) in [(4096, 2048), (7, 13)]:
+        for accumulate in (False, True):
+            got, want = _run(dtype, transposed, m, 1, n, accumulate, m + n)
+            if dtype == "f32":
+                assert np.max(np.abs(got - want)) <= 2 ** -22 * max(1.0, np.max(np.abs(want)))
+            else:
+                assert np.array_equal(got, want)

@@ -1,0 +1,131 @@
+"""Config 4's training step: the reference tape's rules and Adam, run by
+libtccuda (tc_mlp_step), against the oracle's restatement of the same tape
+on the same seeded inputs; and the oracle's gradients against f64
+backpropagation."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from util import normal
+
+DIMS = [64, 128, 96, 48]
+BATCH = 80
+
+
+def _setup(dtype, seed=0, dims=DIMS, batch=BATCH):
+    from tensorcrate_b200.mlp import xavier
+    rng = np.random.default_rng(seed)
+    ws = [xavier(dims[l + 1], dims[l], rng) for l in range(len(dims) - 1)]
+    bs = [rng.uniform(-0.1, 0.1, dims[l + 1]).astype(np.float32) for l in range(len(dims) - 1)]
+    x = normal((dims[0], batch), seed + 10)
+    y = normal((dims[-1], batch), seed + 11)
+    return ws, bs, x, y
+
+
+def _oracle(dtype, ws, bs, beta2=0.999, dims=DIMS, batch=BATCH):
+    h = O.lib().orc_mlp_create(O.DTYPES[dtype], len(dims) - 1, O.u32s(dims), batch, batch, 1e-3, 0.9, beta2, 1e-8)
+    for l, (w, b) in enumerate(zip(ws, bs)):
+        wn, bn = O.narrow(w, dtype), O.narrow(b, dtype)
+        O.call("orc_mlp_params", h, l, O.ptr(wn), O.ptr(bn), 0)
+    return h
+
+
+def _grads(h, l, dtype, dims=DIMS):
+    gw = np.empty(dims[l + 1] * dims[l], O.STORE[dtype])
+    gb = np.empty(dims[l + 1], O.STORE[dtype])
+    O.call("orc_mlp_grads", h, l, O.ptr(gw), O.ptr(gb))
+    return O.widen(gw, dtype).reshape(dims[l + 1], dims[l]), O.widen(gb, dtype)
+
+
+def test_oracle_gradients_match_f64_backprop():
+    ws, bs, x, y = _setup("f32")
+    h = _oracle("f32", ws, bs)
+    loss = np.empty(1, np.float32)
+    O.call("orc_mlp_step", h, O.ptr(x), O.ptr(y), O.ptr(loss), 1)
+    # f64 reference of the same network
+    acts, pre = [x.astype(np.float64)], []
+    for l, (w, b) in enumerate(zip(ws, bs)):
+        a = w.astype(np.float64) @ acts[-1] + b.astype(np.float64)[:, None]
+        pre.append(a)
+        acts.append(np.maximum(a, 0) if l + 1 < len(ws) else a)
+    n = y.size
+    r = acts[-1] - y
+    assert abs(loss[0] - (r * r).sum() / n) <= 1e-5 * max(1.0, (r * r).sum() / n)
+    g = 2 * r / n
+    for l in range(len(ws) - 1, -1, -1):
+        gw_want, gb_want = g @ acts[l].T, g.sum(axis=1)
+        gw, gb = _grads(h, l, "f32")
+        assert np.max(np.abs(gw - gw_want)) <= 1e-4 * max(1e-3, np.max(np.abs(gw_want)))
+        assert np.max(np.abs(gb - gb_want)) <= 1e-4 * max(1e-3, np.max(np.abs(gb_want)))
+        if l:
+            g = (ws[l].astype(np.float64).T @ g) * np.where(pre[l - 1] > 0, 1.0, np.where(pre[l - 1] < 0, 0.0, 0.5))
+    O.lib().orc_mlp_destroy(h)
+
+
+def test_oracle_training_reduces_the_loss():
+    ws, bs, x, y = _setup("f32", seed=3)
+    h = _oracle("f32", ws, bs)
+    losses = []
+    for _ in range(20):
+        loss = np.empty(1, np.float32)
+        O.call("orc_mlp_step", h, O.ptr(x), O.ptr(y), O.ptr(loss), 0)
+        losses.append(float(loss[0]))
+    assert losses[-1] < 0.9 * losses[0]
+    O.lib().orc_mlp_destroy(h)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+def test_mlp_step_matches_the_oracle(device, dtype):
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp
+    # beta2 = 0.999 rounds to 1.0 in bf16 and the reference's update is NaN
+    # there; 0.99 keeps every dtype's run finite.
+    beta2 = 0.99
+    ws, bs, x, y = _setup(dtype, seed=5)
+    h = _oracle(dtype, ws, bs, beta2)
+    m = Mlp(dtype, DIMS, BATCH, beta2=beta2)
+    m.load(ws, bs)
+    xd = cuda.CudaStorage.store(O.narrow(x, dtype), dtype)
+    yd = cuda.CudaStorage.store(O.narrow(y, dtype), dtype)
+    tol = {"f32": 1e-4, "bf16": 4e-2, "f16": 8e-3}[dtype]
+    for step in range(3):
+        loss_d = cuda.CudaStorage(dtype, 1)
+        m.step(xd, yd, loss=loss_d)
+        loss_o = np.empty(1, O.STORE[dtype])
+        O.call("orc_mlp_step", h, O.ptr(O.narrow(x, dtype)), O.ptr(O.narrow(y, dtype)), O.ptr(loss_o), 0)
+        lg, lo = O.widen(loss_d.as_slice(), dtype)[0], O.widen(loss_o, dtype)[0]
+        assert abs(lg - lo) <= tol * abs(lo), (step, lg, lo)
+        for l in range(len(DIMS) - 1):
+            gw, gb = m.grads(l)
+            ow, ob = _grads(h, l, dtype)
+            gw = O.widen(gw, dtype).reshape(ow.shape)
+            assert np.max(np.abs(gw - ow)) <= tol * np.max(np.abs(ow)), (step, l)
+            assert np.max(np.abs(O.widen(gb, dtype) - ob)) <= tol * np.max(np.abs(ob)), (step, l)
+    # parameters after three Adam steps: each step moves by about the rate
+    for l in range(len(DIMS) - 1):
+        w, _ = m.params(l)
+        ow = np.empty(DIMS[l + 1] * DIMS[l], O.STORE[dtype])
+        ob = np.empty(DIMS[l + 1], O.STORE[dtype])
+        O.call("orc_mlp_params", h, l, O.ptr(ow), O.ptr(ob), 1)
+        diff = np.abs(O.widen(w, dtype) - O.widen(ow, dtype))
+        assert np.quantile(diff, 0.99) <= 1e-3 * 3 * 0.25 + {"f32": 1e-6, "bf16": 8e-3, "f16": 1e-3}[dtype]
+    O.lib().orc_mlp_destroy(h)
+
+
+@pytest.mark.gpu
+def test_bf16_mlp_with_default_adam_is_nan_like_the_reference(device):
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp
+    ws, bs, x, y = _setup("bf16", seed=6)
+    m = Mlp("bf16", DIMS, BATCH)
+    m.load(ws, bs)
+    xd = cuda.CudaStorage.store(O.narrow(x, "bf16"), "bf16")
+    yd = cuda.CudaStorage.store(O.narrow(y, "bf16"), "bf16")
+    m.step(xd, yd)
+    w, _ = m.params(0)
+    assert np.all(np.isnan(O.widen(w, "bf16")))
