@@ -39,6 +39,15 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+def traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, or
+    None if that kernel was not captured."""
+    try:
+        return json.loads((ROOT / "profiles" / "traffic.json").read_text())[workload].get(kernel)
+    except Exception:
+        return None
+
+
 def peaks() -> tuple[dict, str]:
     try:
         return json.loads(PEAKS_FILE.read_text()), "measured"
@@ -277,7 +286,7 @@ def run_c2(args, torch, world, rank, comm):
                    "algorithmic_bytes_per_step": step_bytes},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                      "peak_source": pk_kind, "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 3),
-                     "traffic": None},
+                     "traffic": traffic("c2", dom), "algorithmic_bytes": bytes_per_op[dom]},
         "ops": ops,
         "e2e": {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -422,6 +431,70 @@ def run_c3(args, torch, world, rank, comm):
             "gpu_launches": 5 * args.steps, "clocks": clocks}
 
 
+def run_c4(args, torch, world, rank, comm):
+    """Config 4: one training step of the 1024-4096-4096-1024 ReLU MLP in
+    bf16 (tape + Adam(1e-3, 0.9, 0.999, 1e-8), as the reference runs it),
+    global batch 2048 split across the ranks (strong scaling), gradients
+    summed with NCCL.  metric: steps/s."""
+    from tensorcrate_b200 import _native as N
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp, xavier
+    dtype = "bf16"
+    dims = [1024, 4096, 4096, 1024]
+    gbatch = args.batch
+    if gbatch % world:
+        raise SystemExit("global batch must divide by the number of GPUs")
+    batch = gbatch // world
+    stream = torch.cuda.current_stream()
+    rng = np.random.default_rng(6)
+    ws = [xavier(dims[l + 1], dims[l], rng) for l in range(3)]
+    bs = [np.zeros(dims[l + 1], np.float32) for l in range(3)]
+    m = Mlp(dtype, dims, batch, gbatch)
+    m.load(ws, bs)
+    xr = np.random.default_rng(4 + rank).standard_normal((dims[0], batch)).astype(np.float32)
+    yr = np.random.default_rng(5 + rank).standard_normal((dims[-1], batch)).astype(np.float32)
+    x = cuda.CudaStorage.store(cuda.f32_to_bits(xr, dtype), dtype)
+    y = cuda.CudaStorage.store(cuda.f32_to_bits(yr, dtype), dtype)
+    loss = cuda.CudaStorage(dtype, 1)
+
+    def step():
+        m.step(x, y, comm=comm, stream=stream)
+
+    ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
+    gemm_flops = 3 * 2 * gbatch * sum(dims[l] * dims[l + 1] for l in range(3))  # fwd + dW + dX
+    pk, pk_kind = peaks()
+    tflops = gemm_flops / (ms * 1e-3) / 1e12
+    # e2e: inputs and targets uploaded from pinned host memory each step, the
+    # loss read back.
+    px = torch.from_numpy(cuda.f32_to_bits(xr, dtype).view(np.int16)).pin_memory()
+    py = torch.from_numpy(cuda.f32_to_bits(yr, dtype).view(np.int16)).pin_memory()
+    pl = torch.empty(1, dtype=torch.int16).pin_memory()
+    lib = N.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def e2e_step():
+        N.check("h2d", lib.tc_memcpy_h2d(x.ptr, px.data_ptr(), px.numel() * 2, sp))
+        N.check("h2d", lib.tc_memcpy_h2d(y.ptr, py.data_ptr(), py.numel() * 2, sp))
+        m.step(x, y, comm=comm, loss=loss, stream=stream)
+        N.check("d2h", lib.tc_memcpy_d2h(pl.data_ptr(), loss.ptr, 2, sp))
+
+    e2e_ms, _ = timed(torch, world, e2e_step, max(3, args.steps // 2), 2, stream)
+    return {"metric": "config-4 MLP training steps/s", "value": round(1000.0 / ms, 2), "unit": "steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic N(0,1) inputs/targets, Xavier-uniform weights, seeded",
+            "config": {"workload": "config4: MLP 1024-4096-4096-1024 ReLU, MSE, Adam(1e-3,0.9,0.999,1e-8), bf16",
+                       "global_batch": gbatch, "per_rank_batch": batch,
+                       "parallelism": f"dp{world}" + (" (NCCL all-reduce of gradients)" if world > 1 else ""),
+                       "gemm_flops_per_step": gemm_flops},
+            "roofline": {"bound": "tensor", "kernel": "whole step (GEMM share)", "achieved": round(tflops, 1),
+                         "peak": pk["bf16_tflops_sustained"], "peak_source": pk_kind + " sustained",
+                         "unit": "TFLOP/s", "frac": round(tflops / pk["bf16_tflops_sustained"], 3), "traffic": None},
+            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "steps/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": (px.numel() + py.numel()) * 2, "d2h_bytes_per_step": 2},
+            "gpu_launches": None, "clocks": clocks}
+
+
 def barrier(torch, world):
     if world > 1:
         torch.distributed.barrier()
@@ -457,7 +530,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--batch", type=int, default=2048, help="config 4's global batch")
     ap.add_argument("--size", type=int, default=8192, help="config 5's M=N=K")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -493,6 +567,8 @@ def main():
         line = run_gemm(args, torch, world, rank, comm, "f32", 1024)
     elif args.workload == "c3":
         line = run_c3(args, torch, world, rank, comm)
+    elif args.workload == "c4":
+        line = run_c4(args, torch, world, rank, comm)
     else:
         line = run_c2(args, torch, world, rank, comm)
     if rank == 0 and not args.no_cpu_baseline and args.workload == "c2":
