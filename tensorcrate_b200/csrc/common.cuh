@@ -104,20 +104,20 @@ __host__ __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
 struct F32T {
   using S = float;
   static constexpr int code = TC_F32;
-  __device__ __forceinline__ static float load(S s) { return s; }
-  __device__ __forceinline__ static S store(float v) { return v; }
+  __host__ __device__ __forceinline__ static float load(S s) { return s; }
+  __host__ __device__ __forceinline__ static S store(float v) { return v; }
 };
 struct F16T {
   using S = uint16_t;
   static constexpr int code = TC_F16;
-  __device__ __forceinline__ static float load(S s) { return f16_bits_to_f32(s); }
-  __device__ __forceinline__ static S store(float v) { return f32_to_f16_bits(v); }
+  __host__ __device__ __forceinline__ static float load(S s) { return f16_bits_to_f32(s); }
+  __host__ __device__ __forceinline__ static S store(float v) { return f32_to_f16_bits(v); }
 };
 struct BF16T {
   using S = uint16_t;
   static constexpr int code = TC_BF16;
-  __device__ __forceinline__ static float load(S s) { return bf16_bits_to_f32(s); }
-  __device__ __forceinline__ static S store(float v) { return f32_to_bf16_bits(v); }
+  __host__ __device__ __forceinline__ static float load(S s) { return bf16_bits_to_f32(s); }
+  __host__ __device__ __forceinline__ static S store(float v) { return f32_to_bf16_bits(v); }
 };
 
 // Dispatch a functor templated on the element trait.

@@ -455,11 +455,17 @@ int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t col
 
 }  // namespace tc
 
+namespace tc {
+int reduce_fault(int *flag);
+}
+
 extern "C" int tc_device_status(int *fault) {
-  int h = 0;
+  int h = 0, r = 0;
   if (int st = tc::check_cuda(cudaMemcpyFromSymbol(&h, tc::g_gemm_fault, sizeof(int)), "cudaMemcpyFromSymbol"))
     return st;
-  if (fault) *fault = h;
+  if (int st = tc::reduce_fault(&r)) return st;
+  if (fault) *fault = h | (r << 1);
   if (h) return tc::fail(TC_ETIMEOUT, "a tensor-core GEMM gave up waiting on its pipeline");
+  if (r) return tc::fail(TC_ETIMEOUT, "a TMA-fed reduction gave up waiting on its pipeline");
   return TC_OK;
 }

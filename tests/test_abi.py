@@ -121,3 +121,16 @@ def test_empty_work_touches_nothing():
     assert _status("tc_elementwise", 0, 0, None, None, None, 0, None)[0] == N.OK
     assert _status("tc_strided_copy", 4, 2, N.sizes([0, 3]), None, 0, 0, N.sizes([3, 1]), None, None)[0] == N.OK
     assert _status("tc_matmul", 0, 0, 0, 4, 4, None, None, None, 0, None)[0] == N.OK
+
+
+def test_no_host_code_calls_a_device_only_function():
+    """nvcc compiles a __device__-only function called from host code into a
+    stand-in that exits the process; no object of the library may contain
+    one (it would end the caller without an error)."""
+    import subprocess
+    objs = sorted((Path(__file__).resolve().parents[1] / "tensorcrate_b200" / "_build").glob("*.o"))
+    if not objs:
+        pytest.skip("library objects not built here")
+    for o in objs:
+        out = subprocess.run(["nm", "-u", str(o)], capture_output=True, text=True).stdout.split()
+        assert "exit" not in out, f"{o.name} references exit"

@@ -152,3 +152,31 @@ def test_whole_vector_fold_and_dot(device, dtype):
     want = np.empty(1, x.dtype)
     O.call("orc_dot", O.DTYPES[dtype], O.ptr(x), O.ptr(y), n, O.ptr(want))
     assert np.array_equal(got, O.widen(want, dtype))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_streamed_reductions_through_tma(device, dtype):
+    """Slices of contiguous runs, more than 8 MB in all: the TMA-fed kernel,
+    including its per-run partials merged for a fold over (0, 2)."""
+    import ctypes as C
+    shape = [64, 64, 1024]
+    n = int(np.prod(shape))
+    x = O.narrow(integral(n), dtype)
+    st = cuda.contiguous_strides(shape)
+    s = cuda.CudaStorage.store(x, dtype)
+    v = cuda.TensorView(s, shape, st, 0)
+    for kind, op, axes, div in [(N.AXIS_FOLD, N.SUM, [2], 0), (N.AXIS_MEAN, 0, [2], 0),
+                                (N.AXIS_VARIANCE, 0, [2], 1023), (N.AXIS_FOLD, N.RMAX, [0, 2], 0),
+                                (N.AXIS_FOLD, N.RMIN, [0, 2], 0), (N.AXIS_FOLD, N.SUM, [0, 2], 0)]:
+        got = O.widen(cuda.Cuda.reduce_axes(v, axes, kind, op, div).as_slice(), dtype)
+        want = O.widen(O.reduce_axes(dtype, shape, x, 0, st, axes, kind, op, div), dtype)
+        if kind == N.AXIS_VARIANCE:
+            assert np.all(np.abs(got - want) <= 1e-5 * 32 * (np.abs(want) + 1)), (kind, op, axes)
+        else:
+            assert np.array_equal(got, want), (kind, op, axes)
+    for axis in (2, 1):
+        got = cuda.Cuda.arg_reduce(v, axis, N.RMAX).as_slice()
+        assert np.array_equal(got, O.arg_reduce(dtype, shape, x, 0, st, axis, N.RMAX))
+    fault = C.c_int(0)
+    N.call("tc_device_status", C.byref(fault))
+    assert fault.value == 0
