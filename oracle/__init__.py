@@ -105,8 +105,11 @@ def u32s(values):
     return (_u32 * max(1, len(values)))(*values)
 
 
-def ptr(a: np.ndarray) -> int:
-    return a.ctypes.data
+def ptr(a: np.ndarray) -> C.c_void_p:
+    """The array's address as a ctypes pointer that keeps the array alive
+    while the pointer lives (a bare integer would let a temporary array be
+    freed before the call reads it)."""
+    return a.ctypes.data_as(C.c_void_p)
 
 
 def narrow(values, dtype: str) -> np.ndarray:
