@@ -230,8 +230,8 @@ int tc_adam(int dtype, size_t n, void *p, const void *g, void *m, void *v, int r
 int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *stream);
 
 /* Status of bounded device-side waits since the library loaded: TC_ETIMEOUT
- * if a tensor-core GEMM (*fault bit 0) or a TMA-fed reduction (bit 1) gave
- * up waiting on its pipeline and returned early; TC_OK otherwise.  No counterpart in the reference
+ * (and *fault = 1) if a tensor-core GEMM gave up waiting on its pipeline
+ * and returned early; TC_OK otherwise.  No counterpart in the reference
  * (Metal reports async errors at the next sync, src/metal/mod.rs:17-21). */
 int tc_device_status(int *fault);
 

@@ -4,6 +4,8 @@
 // from.  sm_100a only.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -31,6 +33,12 @@ int check_launch(const char *what);
 
 // SMs on the current device (148 on B200), cached per device.
 int sm_count();
+
+// A device scratch buffer of at least `bytes` for partial results, one per
+// device, grown on demand and kept until the process exits.  Work that uses
+// it is ordered on the caller's stream; two such calls running at the same
+// time on different streams of one device would share it.
+int scratch(size_t bytes, void **out);
 
 // ---------------------------------------------------------------------------
 // Element types.  A kernel computes in f32; loads widen exactly and stores
@@ -101,6 +109,10 @@ __host__ __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
 #endif
 }
 
+// Device code rounds with the hardware conversions (cvt.rn.f16.f32 /
+// cvt.rn.bf16.f32: round to nearest even, subnormals kept), which agree with
+// the software conversions above on every value but a NaN's payload; host
+// code uses the software ones.
 struct F32T {
   using S = float;
   static constexpr int code = TC_F32;
@@ -110,15 +122,43 @@ struct F32T {
 struct F16T {
   using S = uint16_t;
   static constexpr int code = TC_F16;
-  __host__ __device__ __forceinline__ static float load(S s) { return f16_bits_to_f32(s); }
-  __host__ __device__ __forceinline__ static S store(float v) { return f32_to_f16_bits(v); }
+  __host__ __device__ __forceinline__ static float load(S s) {
+#ifdef __CUDA_ARCH__
+    return __half2float(__ushort_as_half(s));
+#else
+    return f16_bits_to_f32(s);
+#endif
+  }
+  __host__ __device__ __forceinline__ static S store(float v) {
+#ifdef __CUDA_ARCH__
+    return __half_as_ushort(__float2half_rn(v));
+#else
+    return f32_to_f16_bits(v);
+#endif
+  }
 };
 struct BF16T {
   using S = uint16_t;
   static constexpr int code = TC_BF16;
   __host__ __device__ __forceinline__ static float load(S s) { return bf16_bits_to_f32(s); }
-  __host__ __device__ __forceinline__ static S store(float v) { return f32_to_bf16_bits(v); }
+  __host__ __device__ __forceinline__ static S store(float v) {
+#ifdef __CUDA_ARCH__
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+#else
+    return f32_to_bf16_bits(v);
+#endif
+  }
 };
+
+// Two values rounded to the element type and packed low-first.
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&p);
+}
+__device__ __forceinline__ uint32_t pack2_f16(float lo, float hi) {
+  __half2 p = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&p);
+}
 
 // Dispatch a functor templated on the element trait.
 template <class F> int with_real(int dtype, F &&f) {

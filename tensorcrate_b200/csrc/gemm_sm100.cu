@@ -324,8 +324,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                   uint16_t lo = uint16_t(w[h] & 0xffffu), hi = uint16_t(w[h] >> 16);
-                  float flo = p.elem_is_bf16 ? bf16_bits_to_f32(lo) : f16_bits_to_f32(lo);
-                  float fhi = p.elem_is_bf16 ? bf16_bits_to_f32(hi) : f16_bits_to_f32(hi);
+                  float flo = p.elem_is_bf16 ? BF16T::load(lo) : F16T::load(lo);
+                  float fhi = p.elem_is_bf16 ? BF16T::load(hi) : F16T::load(hi);
                   v[8 * j + 2 * h] = __fadd_rn(flo, v[8 * j + 2 * h]);
                   v[8 * j + 2 * h + 1] = __fadd_rn(fhi, v[8 * j + 2 * h + 1]);
                 }
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               for (int j = 0; j < 32; ++j) {
                 if (col0 + j < p.N) {
                   uint16_t o = crow[col0 + j];
-                  v[j] = __fadd_rn(p.elem_is_bf16 ? bf16_bits_to_f32(o) : f16_bits_to_f32(o), v[j]);
+                  v[j] = __fadd_rn(p.elem_is_bf16 ? BF16T::load(o) : F16T::load(o), v[j]);
                 }
               }
             }
@@ -346,17 +346,15 @@ __global__ void __launch_bounds__(THREADS, 1)
               uint32_t w[4];
 #pragma unroll
               for (int h = 0; h < 4; ++h) {
-                float a = v[8 * j + 2 * h], b = v[8 * j + 2 * h + 1];
-                uint32_t lo = p.elem_is_bf16 ? f32_to_bf16_bits(a) : f32_to_f16_bits(a);
-                uint32_t hi = p.elem_is_bf16 ? f32_to_bf16_bits(b) : f32_to_f16_bits(b);
-                w[h] = lo | (hi << 16);
+                const float a = v[8 * j + 2 * h], b = v[8 * j + 2 * h + 1];
+                w[h] = p.elem_is_bf16 ? pack2_bf16(a, b) : pack2_f16(a, b);
               }
               *reinterpret_cast<uint4 *>(crow + col0 + 8 * j) = make_uint4(w[0], w[1], w[2], w[3]);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) crow[col0 + j] = p.elem_is_bf16 ? f32_to_bf16_bits(v[j]) : f32_to_f16_bits(v[j]);
+              if (col0 + j < p.N) crow[col0 + j] = p.elem_is_bf16 ? BF16T::store(v[j]) : F16T::store(v[j]);
           }
         }
       }
@@ -455,17 +453,11 @@ int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t col
 
 }  // namespace tc
 
-namespace tc {
-int reduce_fault(int *flag);
-}
-
 extern "C" int tc_device_status(int *fault) {
-  int h = 0, r = 0;
+  int h = 0;
   if (int st = tc::check_cuda(cudaMemcpyFromSymbol(&h, tc::g_gemm_fault, sizeof(int)), "cudaMemcpyFromSymbol"))
     return st;
-  if (int st = tc::reduce_fault(&r)) return st;
-  if (fault) *fault = h | (r << 1);
+  if (fault) *fault = h;
   if (h) return tc::fail(TC_ETIMEOUT, "a tensor-core GEMM gave up waiting on its pipeline");
-  if (r) return tc::fail(TC_ETIMEOUT, "a TMA-fed reduction gave up waiting on its pipeline");
   return TC_OK;
 }

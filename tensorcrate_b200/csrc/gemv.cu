@@ -51,31 +51,54 @@ __global__ void __launch_bounds__(256) matvec_rows(const typename T::S *m, const
   }
 }
 
-// y[j] = sum_p x[p] * m[p, j].  blockDim = (32, 8): x walks 32 adjacent
-// columns, y splits the rows.
-template <class T>
+// y[j] = sum_p x[p] * m[p, j].  blockDim = (32, 8): x walks 32*CPT
+// adjacent columns (one 16-byte load each when CPT > 1), y splits a block's
+// rows; blockIdx.y picks one of `shares` row ranges, whose f32 partial sums
+// go to `partial` when shares > 1 (merged in order by vecmat_finish).
+template <class T, int CPT>
 __global__ void __launch_bounds__(256) vecmat_cols(const typename T::S *x, const typename T::S *m,
-                                                   typename T::S *y, long long rows, long long cols) {
-  __shared__ float part[8][33];
-  long long j = (long long)blockIdx.x * 32 + threadIdx.x;
-  float s = 0.0f;
-  if (j < cols) {
-    long long p = threadIdx.y;
-    for (; p + 24 < rows; p += 32) {
-      float a0 = T::load(__ldg(m + p * cols + j)), a1 = T::load(__ldg(m + (p + 8) * cols + j));
-      float a2 = T::load(__ldg(m + (p + 16) * cols + j)), a3 = T::load(__ldg(m + (p + 24) * cols + j));
-      s = fmaf(T::load(x[p]), a0, s);
-      s = fmaf(T::load(x[p + 8]), a1, s);
-      s = fmaf(T::load(x[p + 16]), a2, s);
-      s = fmaf(T::load(x[p + 24]), a3, s);
+                                                   typename T::S *y, long long rows, long long cols,
+                                                   long long rows_per_share, float *partial) {
+  using S = typename T::S;
+  __shared__ float part[8][32 * CPT + 1];
+  const long long j0 = ((long long)blockIdx.x * 32 + threadIdx.x) * CPT;
+  const long long r0 = (long long)blockIdx.y * rows_per_share, r1 = min(rows, r0 + rows_per_share);
+  float s[CPT];
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) s[c] = 0.0f;
+  if (j0 < cols) {
+    for (long long p = r0 + threadIdx.y; p < r1; p += 8) {
+      const float xp = T::load(x[p]);
+      if (CPT > 1) {
+        union { uint4 raw; S v[16 / sizeof(S)]; } pk;
+        pk.raw = __ldg(reinterpret_cast<const uint4 *>(m + p * cols + j0));
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) s[c] = fmaf(xp, T::load(pk.v[c]), s[c]);
+      } else {
+        s[0] = fmaf(xp, T::load(__ldg(m + p * cols + j0)), s[0]);
+      }
     }
-    for (; p < rows; p += 8) s = fmaf(T::load(x[p]), T::load(__ldg(m + p * cols + j)), s);
   }
-  part[threadIdx.y][threadIdx.x] = s;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) part[threadIdx.y][threadIdx.x * CPT + c] = s[c];
   __syncthreads();
-  if (threadIdx.y == 0 && j < cols) {
-    float t = part[0][threadIdx.x];
-    for (int k = 1; k < 8; ++k) t += part[k][threadIdx.x];
+  if (threadIdx.y == 0 && j0 < cols) {
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      float t = part[0][threadIdx.x * CPT + c];
+      for (int k = 1; k < 8; ++k) t += part[k][threadIdx.x * CPT + c];
+      if (gridDim.y > 1) partial[blockIdx.y * cols + j0 + c] = t;
+      else y[j0 + c] = T::store(t);
+    }
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) vecmat_finish(const float *partial, int shares, long long cols,
+                                                     typename T::S *y) {
+  for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < cols; j += (long long)gridDim.x * blockDim.x) {
+    float t = partial[j];
+    for (int s = 1; s < shares; ++s) t += partial[s * cols + j];
     y[j] = T::store(t);
   }
 }
@@ -138,13 +161,36 @@ int tc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x,
 int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m, void *y, void *stream) {
   if (cols == 0) return TC_OK;
   if (!m || !x || !y) return fail(TC_EINVAL, "vecmat: null pointer");
-  return with_real(dtype, [&](auto t) {
+  return with_real(dtype, [&](auto t) -> int {
     using T = decltype(t);
     using S = typename T::S;
-    unsigned grid = unsigned(((long long)cols + 31) / 32);
-    vecmat_cols<T><<<grid, dim3(32, 8), 0, as_stream(stream)>>>(static_cast<const S *>(x),
-                                                                 static_cast<const S *>(m), static_cast<S *>(y),
-                                                                 (long long)rows, (long long)cols);
+    constexpr int CPT = 16 / int(sizeof(S));
+    const bool vec = cols % CPT == 0 && (uintptr_t(m) & 15u) == 0;
+    const int cpt = vec ? CPT : 1;
+    const long long col_blocks = ((long long)cols + 32 * cpt - 1) / (32 * cpt);
+    // Split the rows until there are ~4 blocks per SM, keeping 64+ rows each.
+    long long shares = 1;
+    while (col_blocks * shares < 4LL * sm_count() && (long long)rows / (shares * 2) >= 64) shares *= 2;
+    const long long per = ((long long)rows + shares - 1) / shares;
+    float *partial = nullptr;
+    if (shares > 1) {
+      void *p = nullptr;
+      if (int st = scratch(size_t(shares) * cols * sizeof(float), &p)) return st;
+      partial = static_cast<float *>(p);
+    }
+    dim3 grid((unsigned)col_blocks, (unsigned)shares);
+    cudaStream_t s = as_stream(stream);
+    if (vec)
+      vecmat_cols<T, CPT><<<grid, dim3(32, 8), 0, s>>>(static_cast<const S *>(x), static_cast<const S *>(m),
+                                                        static_cast<S *>(y), (long long)rows, (long long)cols, per,
+                                                        partial);
+    else
+      vecmat_cols<T, 1><<<grid, dim3(32, 8), 0, s>>>(static_cast<const S *>(x), static_cast<const S *>(m),
+                                                      static_cast<S *>(y), (long long)rows, (long long)cols, per,
+                                                      partial);
+    if (shares > 1)
+      vecmat_finish<T><<<grid_for(cols, 256, 4), 256, 0, s>>>(partial, int(shares), (long long)cols,
+                                                              static_cast<S *>(y));
     return check_launch("vecmat");
   });
 }

@@ -19,6 +19,9 @@
 //    results land in a scratch buffer and are merged, in order, by a second
 //    small kernel.  A variance whose slice fits in registers is computed from
 //    them in both passes, so the input is read from HBM once.
+//    (A variant fed by 1-D TMA bulk copies through a shared-memory ring was
+//    measured slower on B200 for 4 KB runs — 48 us against 30 us per
+//    134 MB — and is not used.)
 //  - columns: the innermost kept axis has stride 1 (results side by side).
 //    Each thread owns four adjacent results (one vector load each) and a
 //    share of the folded range; the shares combine in shared memory.
@@ -261,162 +264,6 @@ __global__ void __launch_bounds__(256, 2) reduce_rows_var(const typename T::S *i
 
 
 // ---------------------------------------------------------------------------
-// rows through TMA: each row to fold is one contiguous run (16-byte aligned,
-// a multiple of 16 bytes).  One producer thread streams runs with 1-D bulk
-// copies (cp.async.bulk, no multicast) into a ring of shared-memory stages,
-// eight runs per stage; eight consumer warps fold one run each from shared
-// memory.  The bytes in flight no longer depend on registers: a stage ring
-// of ~128 KB per SM keeps HBM busy.  A run's two variance passes both read
-// shared memory, so the input crosses HBM once.  When a slice has several
-// runs (outer > 1), each run's fold is a partial, merged by reduce_finish.
-// Waits are bounded by %globaltimer, as in the tensor-core GEMM.
-// ---------------------------------------------------------------------------
-constexpr int RT_WARPS = 8;
-constexpr uint64_t RT_WAIT_NS = 2000000000ull;
-
-__device__ int g_reduce_fault = 0;
-
-__device__ __forceinline__ uint32_t rt_smem(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ uint64_t rt_now() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ bool rt_try(uint64_t *bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-               : "=r"(done) : "r"(rt_smem(bar)), "r"(parity) : "memory");
-  return done != 0;
-}
-__device__ __forceinline__ bool rt_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-  if (rt_try(bar, parity)) return true;
-  const uint64_t t0 = rt_now();
-  for (uint32_t i = 1; i < (1u << 30); ++i) {
-    if (rt_try(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (rt_now() - t0 > RT_WAIT_NS) break;
-    }
-  }
-  *abort_flag = 1;
-  atomicExch(&g_reduce_fault, 1);
-  return false;
-}
-
-struct TmaArgs {
-  Walk kept, folded;
-  long long results, outer, rows;  // rows = results * outer
-  uint32_t run_bytes;              // one run, a multiple of 16
-  int run;                         // elements per run
-  int stages;
-  float count, divisor;
-};
-
-template <class T, int MODE>
-__global__ void __launch_bounds__(32 * (RT_WARPS + 1), 1)
-    reduce_rows_tma(const typename T::S *in, const TmaArgs a, typename T::S *out, uint32_t *arg_out, Acc *partial) {
-  using S = typename T::S;
-  constexpr int N = Pack<T>::N;
-  constexpr int F = fold_of<MODE>();
-  extern __shared__ __align__(128) uint8_t rt_raw[];
-  uint8_t *buf = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(rt_raw) + 127) & ~uintptr_t(127));
-  const uint32_t stage_bytes = a.run_bytes * RT_WARPS;
-  uint64_t *full = reinterpret_cast<uint64_t *>(buf + size_t(a.stages) * stage_bytes);
-  uint64_t *empty = full + a.stages;
-  __shared__ volatile int abort_flag;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long chunks = (a.rows + RT_WARPS - 1) / RT_WARPS;
-  if (threadIdx.x == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < a.stages; ++s) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(rt_smem(&full[s])), "r"(1) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(rt_smem(&empty[s])), "r"(RT_WARPS) : "memory");
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (warp == RT_WARPS) {
-    // ---- producer ----
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, filled = 0, fill_parity = 0;
-      for (long long c = blockIdx.x; c < chunks && !abort_flag; c += gridDim.x) {
-        if (!rt_wait(&empty[stage], phase ^ 1u, &abort_flag)) break;
-        const long long r0 = c * RT_WARPS;
-        const long long left = a.rows - r0;
-        const int n = left < RT_WARPS ? int(left) : RT_WARPS;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(rt_smem(&full[stage])),
-                     "r"(uint32_t(n) * a.run_bytes) : "memory");
-        for (int w = 0; w < n; ++w) {
-          const long long row = r0 + w;
-          const long long res = a.outer > 1 ? row / a.outer : row, o = a.outer > 1 ? row - res * a.outer : 0;
-          const S *src = in + walk_pos(a.kept, res) + walk_pos(a.folded, o);
-          asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                       ::"r"(rt_smem(buf + size_t(stage) * stage_bytes + size_t(w) * a.run_bytes)),
-                       "l"(reinterpret_cast<uint64_t>(src)), "r"(a.run_bytes), "r"(rt_smem(&full[stage]))
-                       : "memory");
-        }
-        filled |= 1u << stage;
-        fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == a.stages) { stage = 0; phase ^= 1u; }
-      }
-      if (abort_flag) {  // let every copy this thread started land
-        for (int s = 0; s < a.stages; ++s)
-          if (filled & (1u << s)) {
-            const uint64_t t0 = rt_now();
-            while (!rt_try(&full[s], (fill_parity >> s) & 1u) && rt_now() - t0 < RT_WAIT_NS) {}
-          }
-      }
-    }
-  } else {
-    // ---- consumers: warp w folds run w of each stage ----
-    int stage = 0;
-    uint32_t phase = 0;
-    for (long long c = blockIdx.x; c < chunks; c += gridDim.x) {
-      if (!rt_wait(&full[stage], phase, &abort_flag)) break;
-      const long long row = c * RT_WARPS + warp;
-      if (row < a.rows) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(buf + size_t(stage) * stage_bytes + size_t(warp) * a.run_bytes);
-        const int packs = int(a.run_bytes / 16);
-        Acc acc = identity<F>();
-        for (int q = lane; q < packs; q += 32) {
-          Pack<T> x;
-          x.raw = src[q];
-#pragma unroll
-          for (int j = 0; j < N; ++j) push<F>(acc, T::load(x.v[j]), uint32_t(q * N + j));
-        }
-        acc = warp_merge<F>(acc);
-        float result = acc.v;
-        if (MODE == M_VAR) {
-          const float mean = __fdiv_rn(acc.v, a.count);
-          Acc d = identity<M_SUM>();
-          for (int q = lane; q < packs; q += 32) {
-            Pack<T> x;
-            x.raw = src[q];
-#pragma unroll
-            for (int j = 0; j < N; ++j) {
-              const float dv = __fsub_rn(T::load(x.v[j]), mean);
-              d.v = __fadd_rn(d.v, __fmul_rn(dv, dv));
-            }
-          }
-          d = warp_merge<M_SUM>(d);
-          result = __fdiv_rn(d.v, a.divisor);
-        }
-        if (lane == 0) {
-          if (a.outer > 1) partial[row] = acc;
-          else if (is_arg<MODE>()) arg_out[row] = acc.i;
-          else if (MODE == M_MEAN) out[row] = T::store(__fdiv_rn(acc.v, a.count));
-          else out[row] = T::store(result);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(rt_smem(&empty[stage])) : "memory");
-      if (++stage == a.stages) { stage = 0; phase ^= 1u; }
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
 // columns: results r = (outer kept index) * K + k, k along the kept axis of
 // stride 1.  blockDim = (32, 8): x walks 32*CPT adjacent results, y splits
 // the folded range into 8 shares combined in shared memory in share order.
@@ -589,38 +436,7 @@ void fill_walk(Walk &w, const Dims &shape, const Dims &strides) {
   }
 }
 
-// Scratch for partial results, kept per device and grown on demand.
-struct Scratch {
-  std::mutex mu;
-  void *ptr[64] = {nullptr};
-  size_t bytes[64] = {0};
-};
-Scratch &scratch() {
-  static Scratch *s = new Scratch;
-  return *s;
-}
-int scratch_get(size_t bytes, void **out) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return fail(TC_EINVAL, "device %d", dev);
-  Scratch &s = scratch();
-  std::lock_guard<std::mutex> g(s.mu);
-  if (s.bytes[dev] < bytes) {
-    if (s.ptr[dev]) {
-      // The old block may still be read by queued work: free it only once
-      // the device is idle.
-      cudaDeviceSynchronize();
-      cudaFree(s.ptr[dev]);
-      s.ptr[dev] = nullptr;
-      s.bytes[dev] = 0;
-    }
-    size_t want = std::max(bytes, size_t(1) << 20);
-    if (int st = check_cuda(cudaMalloc(&s.ptr[dev], want), "cudaMalloc (reduction scratch)")) return st;
-    s.bytes[dev] = want;
-  }
-  *out = s.ptr[dev];
-  return TC_OK;
-}
+int scratch_get(size_t bytes, void **out) { return scratch(bytes, out); }
 
 template <class T, int MODE>
 int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const Dims &fc, const Dims &fcs,
@@ -647,51 +463,6 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     a.vec = a.run % N == 0 && (uintptr_t(in) & 15u) == 0;
     for (uint32_t ax = 0; a.vec && ax < kc.rank; ++ax) a.vec = kcs.v[ax] % N == 0;
     for (uint32_t ax = 0; a.vec && ax < fo.rank; ++ax) a.vec = fos.v[ax] % N == 0;
-    // Contiguous 16-byte-aligned runs of at most 8 KB, and enough of them
-    // to stream: the TMA pipeline.  (A variance over several runs per slice
-    // needs the slice's mean first, so it stays on the register kernels.)
-    const size_t run_bytes = size_t(a.run) * sizeof(S);
-    if (a.vec && run_bytes % 16 == 0 && run_bytes <= 8192 && (MODE != M_VAR || a.outer == 1) &&
-        size_t(results * a.outer) * run_bytes >= (size_t(8) << 20)) {
-      TmaArgs t{};
-      t.kept = a.kept;
-      t.folded = a.folded;
-      t.results = results;
-      t.outer = a.outer;
-      t.rows = results * a.outer;
-      t.run_bytes = uint32_t(run_bytes);
-      t.run = int(a.run);
-      t.stages = run_bytes <= 4096 ? 4 : 3;
-      t.count = count;
-      t.divisor = divisor;
-      Acc *partial = nullptr;
-      if (a.outer > 1) {
-        void *p = nullptr;
-        if (int st = scratch_get(size_t(t.rows) * sizeof(Acc), &p)) return st;
-        partial = static_cast<Acc *>(p);
-      }
-      const size_t smem = size_t(t.stages) * RT_WARPS * run_bytes + 2 * t.stages * sizeof(uint64_t) + 128;
-      static bool configured[64][7] = {};
-      int dev = 0;
-      cudaGetDevice(&dev);
-      if (!configured[dev & 63][MODE]) {
-        if (int st = check_cuda(cudaFuncSetAttribute(reduce_rows_tma<T, MODE>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
-                                "cudaFuncSetAttribute"))
-          return st;
-        configured[dev & 63][MODE] = true;
-      }
-      const long long chunks = (t.rows + RT_WARPS - 1) / RT_WARPS;
-      unsigned grid = unsigned(std::min<long long>(chunks, (long long)sms));
-      reduce_rows_tma<T, MODE><<<grid, 32 * (RT_WARPS + 1), smem, stream>>>(in, t, o, arg_out, partial);
-      if (a.outer > 1) {
-        RowsArgs f = a;
-        f.splits = int(a.outer);
-        unsigned g2 = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
-        reduce_finish<T, MODE><<<std::max(1u, g2), 256, 0, stream>>>(f, partial, o, arg_out);
-      }
-      return check_launch("reduce (rows, TMA)");
-    }
     if (MODE == M_VAR) {
       a.splits = 1;
       unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
@@ -720,7 +491,15 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       partial = static_cast<Acc *>(p);
     }
     const long long groups = results * splits;
-    unsigned grid = unsigned(std::min<long long>((groups + 7) / 8, (long long)sms * 16));
+    // As many blocks as stay resident (a persistent grid): each warp walks
+    // its groups in turn instead of the grid running in waves.
+    static int resident[7] = {0, 0, 0, 0, 0, 0, 0};
+    if (!resident[MODE]) {
+      int n = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_rows<T, MODE>, 256, 0);
+      resident[MODE] = n > 0 ? n : 2;
+    }
+    unsigned grid = unsigned(std::min<long long>((groups + 7) / 8, (long long)sms * resident[MODE]));
     reduce_rows<T, MODE><<<std::max(1u, grid), 256, 0, stream>>>(in, a, o, arg_out, partial);
     if (splits > 1) {
       unsigned g2 = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
@@ -876,10 +655,7 @@ int vector_fold(int dtype, const void *a, const void *b, size_t n, void *out, cu
 
 }  // namespace
 
-// The TMA reduction's bounded-wait flag, for tc_device_status.
-int reduce_fault(int *flag) {
-  return check_cuda(cudaMemcpyFromSymbol(flag, g_reduce_fault, sizeof(int)), "cudaMemcpyFromSymbol");
-}
+
 
 }  // namespace tc
 

@@ -64,6 +64,41 @@ int check_layout(const char *what, size_t len, uint32_t rank, const size_t *shap
   return TC_OK;
 }
 
+namespace {
+struct Scratch {
+  std::mutex mu;
+  void *ptr[64] = {nullptr};
+  size_t bytes[64] = {0};
+};
+Scratch &scratch_state() {
+  static Scratch *s = new Scratch;  // never destroyed
+  return *s;
+}
+}  // namespace
+
+int scratch(size_t bytes, void **out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(TC_EINVAL, "device %d", dev);
+  Scratch &s = scratch_state();
+  std::lock_guard<std::mutex> g(s.mu);
+  if (s.bytes[dev] < bytes) {
+    if (s.ptr[dev]) {
+      // Queued work may still read the old block: free it once the device
+      // is idle.
+      cudaDeviceSynchronize();
+      cudaFree(s.ptr[dev]);
+      s.ptr[dev] = nullptr;
+      s.bytes[dev] = 0;
+    }
+    size_t want = bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes;
+    if (int st = check_cuda(cudaMalloc(&s.ptr[dev], want), "cudaMalloc (scratch)")) return st;
+    s.bytes[dev] = want;
+  }
+  *out = s.ptr[dev];
+  return TC_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Device pool: freed blocks are kept per (device, size class) and handed to
 // the next request of that class, as Metal's buffer pool does

@@ -155,9 +155,9 @@ def test_whole_vector_fold_and_dot(device, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-def test_streamed_reductions_through_tma(device, dtype):
-    """Slices of contiguous runs, more than 8 MB in all: the TMA-fed kernel,
-    including its per-run partials merged for a fold over (0, 2)."""
+def test_streamed_reductions_of_long_runs(device, dtype):
+    """Slices of contiguous runs, more than 8 MB in all, including the split
+    shares merged for a fold over (0, 2)."""
     import ctypes as C
     shape = [64, 64, 1024]
     n = int(np.prod(shape))

