@@ -93,13 +93,22 @@ __global__ void __launch_bounds__(256) vecmat_cols(const typename T::S *x, const
   }
 }
 
+// blockDim = (32, 8): x walks 32 columns, y takes every 8th share; the
+// eight partial sums of a column then meet in shared memory.
 template <class T>
 __global__ void __launch_bounds__(256) vecmat_finish(const float *partial, int shares, long long cols,
                                                      typename T::S *y) {
-  for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < cols; j += (long long)gridDim.x * blockDim.x) {
-    float t = partial[j];
-    for (int s = 1; s < shares; ++s) t += partial[s * cols + j];
-    y[j] = T::store(t);
+  __shared__ float part[8][33];
+  const long long j = (long long)blockIdx.x * 32 + threadIdx.x;
+  float t = 0.0f;
+  if (j < cols)
+    for (int s = threadIdx.y; s < shares; s += 8) t += partial[s * cols + j];
+  part[threadIdx.y][threadIdx.x] = t;
+  __syncthreads();
+  if (threadIdx.y == 0 && j < cols) {
+    float r = part[0][threadIdx.x];
+    for (int k = 1; k < 8; ++k) r += part[k][threadIdx.x];
+    y[j] = T::store(r);
   }
 }
 
@@ -189,8 +198,8 @@ int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m,
                                                       static_cast<S *>(y), (long long)rows, (long long)cols, per,
                                                       partial);
     if (shares > 1)
-      vecmat_finish<T><<<grid_for(cols, 256, 4), 256, 0, s>>>(partial, int(shares), (long long)cols,
-                                                              static_cast<S *>(y));
+      vecmat_finish<T><<<unsigned((cols + 31) / 32), dim3(32, 8), 0, s>>>(partial, int(shares), (long long)cols,
+                                                                         static_cast<S *>(y));
     return check_launch("vecmat");
   });
 }

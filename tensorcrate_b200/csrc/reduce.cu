@@ -394,6 +394,120 @@ __global__ void __launch_bounds__(256) reduce_cols_finish(const Acc *partial, lo
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Fast paths for the common layouts (fixed strides, packs): lean kernels
+// with 32-bit loop indices so that many warps stay resident.
+//
+// rows_fast: result r's slice is `outer` runs of `per_run` 16-byte packs at
+// in + r*kept_stride + o*outer_stride; a warp per (result, share of runs).
+// ---------------------------------------------------------------------------
+struct FastRows {
+  long long kept_stride, outer_stride;  // elements
+  long long results;
+  int outer, per_run;                   // runs per slice, packs per run
+  int splits, share;                    // shares per slice, runs per share
+  float count;
+};
+
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) reduce_rows_fast(const typename T::S *in, const FastRows a, typename T::S *out,
+                                                        uint32_t *arg_out, Acc *partial) {
+  using S = typename T::S;
+  constexpr int N = Pack<T>::N;
+  constexpr int F = fold_of<MODE>();
+  constexpr int U = 8;
+  const int lane = threadIdx.x & 31;
+  const long long groups = a.results * a.splits;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long g = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < groups; g += warps) {
+    const long long r = g / a.splits;
+    const int s = int(g - r * a.splits);
+    const int o_lo = s * a.share, o_hi = min(a.outer, o_lo + a.share);
+    const uint4 *base = reinterpret_cast<const uint4 *>(in + r * a.kept_stride);
+    Acc acc = identity<F>();
+    for (int o = o_lo; o < o_hi; ++o) {
+      const uint4 *rp = base + (o * a.outer_stride) / N;
+      for (int c0 = lane; c0 < a.per_run; c0 += 32 * U) {
+        Pack<T> x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (c0 + 32 * u < a.per_run) x[u].raw = __ldg(rp + c0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (c0 + 32 * u < a.per_run) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) push<F>(acc, T::load(x[u].v[j]), uint32_t((c0 + 32 * u) * N + j));
+          }
+      }
+    }
+    acc = warp_merge<F>(acc);
+    if (lane == 0) {
+      if (a.splits > 1) partial[g] = acc;
+      else if (is_arg<MODE>()) arg_out[r] = acc.i;
+      else if (MODE == M_MEAN) out[r] = T::store(__fdiv_rn(acc.v, a.count));
+      else out[r] = T::store(acc.v);
+    }
+  }
+}
+
+// cols_fast: results r = ko*K + k (k along the stride-1 kept axis); a
+// block of 256 threads owns 256*CPT adjacent results of one kept-outer
+// index for one share of the folded rows (fixed folded stride), each thread
+// CPT of them with one vector load per row.  No shared memory: the shares
+// meet in `partial` (in order, reduce_cols_finish) when there are several.
+struct FastCols {
+  long long kept_stride, folded_stride;  // elements
+  long long kept_outer, K;
+  int depth, kshares, kchunk;
+  float count;
+};
+
+template <class T, int MODE, int CPT>
+__global__ void __launch_bounds__(256) reduce_cols_fast(const typename T::S *in, const FastCols a, typename T::S *out,
+                                                        uint32_t *arg_out, Acc *partial) {
+  using S = typename T::S;
+  using V = Cols<T, CPT>;
+  constexpr int W = 256 * CPT;
+  constexpr int U = 8;
+  constexpr int F = fold_of<MODE>();
+  const long long tiles_k = (a.K + W - 1) / W;
+  const long long items = a.kept_outer * tiles_k * a.kshares;
+  const long long results = a.kept_outer * a.K;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+    const long long t = it / a.kshares;
+    const int ks = int(it - t * a.kshares);
+    const long long ko = t / tiles_k;
+    const long long k = (t - ko * tiles_k) * W + (long long)threadIdx.x * CPT;
+    if (k >= a.K) continue;  // CPT divides K
+    const S *base = in + ko * a.kept_stride + k;
+    const int f0 = ks * a.kchunk, f1 = min(a.depth, f0 + a.kchunk);
+    Acc acc[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[c] = identity<F>();
+    for (int f = f0; f < f1; f += U) {
+      V x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (f + u < f1) x[u].raw = __ldg(reinterpret_cast<const typename V::Raw *>(base + (long long)(f + u) * a.folded_stride));
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (f + u < f1) {
+#pragma unroll
+          for (int c = 0; c < CPT; ++c) push<F>(acc[c], T::load(x[u].v[c]), uint32_t(f + u));
+        }
+    }
+    const long long r = ko * a.K + k;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      if (a.kshares > 1) partial[ks * results + r + c] = acc[c];
+      else if (is_arg<MODE>()) arg_out[r + c] = acc[c].i;
+      else if (MODE == M_MEAN) out[r + c] = T::store(__fdiv_rn(acc[c].v, a.count));
+      else out[r + c] = T::store(acc[c].v);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // walk: a warp per result over the decomposed folded index.
 // ---------------------------------------------------------------------------
@@ -463,6 +577,46 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     a.vec = a.run % N == 0 && (uintptr_t(in) & 15u) == 0;
     for (uint32_t ax = 0; a.vec && ax < kc.rank; ++ax) a.vec = kcs.v[ax] % N == 0;
     for (uint32_t ax = 0; a.vec && ax < fo.rank; ++ax) a.vec = fos.v[ax] % N == 0;
+    // The fast path: at most one kept and one outer folded axis, packs, and
+    // index ranges that fit 32 bits.
+    if (MODE != M_VAR && a.vec && kc.rank <= 1 && fo.rank <= 1 && a.outer < (1LL << 30) &&
+        a.run / N < (1LL << 30)) {
+      FastRows f{};
+      f.kept_stride = kc.rank ? (long long)kcs.v[0] : 0;
+      f.outer_stride = fo.rank ? (long long)fos.v[0] : 0;
+      f.results = results;
+      f.outer = int(a.outer);
+      f.per_run = int(a.run / N);
+      f.count = count;
+      long long splits = 1;
+      while (results * splits < (long long)sms * 32 && a.outer / (splits * 2) >= 1 &&
+             (a.outer / (splits * 2)) * f.per_run >= 32LL * 8 * 2)
+        splits *= 2;
+      f.splits = int(splits);
+      f.share = int((a.outer + splits - 1) / splits);
+      Acc *partial = nullptr;
+      if (splits > 1) {
+        void *p = nullptr;
+        if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p)) return st;
+        partial = static_cast<Acc *>(p);
+      }
+      static int resident_fast[7] = {0, 0, 0, 0, 0, 0, 0};
+      if (!resident_fast[MODE]) {
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_rows_fast<T, MODE>, 256, 0);
+        resident_fast[MODE] = n > 0 ? n : 2;
+      }
+      const long long groups = results * splits;
+      unsigned grid = unsigned(std::min<long long>((groups + 7) / 8, (long long)sms * resident_fast[MODE]));
+      reduce_rows_fast<T, MODE><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial);
+      if (splits > 1) {
+        RowsArgs fa = a;
+        fa.splits = int(splits);
+        unsigned g2 = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
+        reduce_finish<T, MODE><<<std::max(1u, g2), 256, 0, stream>>>(fa, partial, o, arg_out);
+      }
+      return check_launch("reduce (rows, fast)");
+    }
     if (MODE == M_VAR) {
       a.splits = 1;
       unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
@@ -522,6 +676,35 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     bool four = a.K % 4 == 0 && (uintptr_t(in) % (4 * sizeof(S))) == 0;
     for (uint32_t ax = 0; four && ax < ko.rank; ++ax) four = kos.v[ax] % 4 == 0;
     for (uint32_t ax = 0; four && ax < fc.rank; ++ax) four = fcs.v[ax] % 4 == 0;
+    if (MODE != M_VAR && four && ko.rank <= 1 && fc.rank <= 1 && depth < (1LL << 30)) {
+      FastCols f{};
+      f.kept_stride = ko.rank ? (long long)kos.v[0] : 0;
+      f.folded_stride = fc.rank ? (long long)fcs.v[0] : 0;
+      f.kept_outer = a.kept_outer;
+      f.K = a.K;
+      f.depth = int(depth);
+      f.count = count;
+      const long long tiles = a.kept_outer * ((a.K + 1023) / 1024);
+      int ks = 1;
+      while (tiles * ks < 2LL * sms && depth / (ks * 2) >= 32) ks *= 2;
+      f.kshares = ks;
+      f.kchunk = int((depth + ks - 1) / ks);
+      Acc *partial = nullptr;
+      if (ks > 1) {
+        void *p = nullptr;
+        if (int st = scratch_get(size_t(ks) * size_t(a.kept_outer * a.K) * sizeof(Acc), &p)) return st;
+        partial = static_cast<Acc *>(p);
+      }
+      const long long items = tiles * ks;
+      unsigned grid = unsigned(std::min<long long>(items, (long long)sms * 8));
+      reduce_cols_fast<T, MODE, 4><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial);
+      if (ks > 1) {
+        const long long results_c = a.kept_outer * a.K;
+        reduce_cols_finish<T, MODE><<<grid_for(size_t(results_c), 256, 4), 256, 0, stream>>>(partial, results_c, ks,
+                                                                                              count, o, arg_out);
+      }
+      return check_launch("reduce (columns, fast)");
+    }
     const int cpt = four ? 4 : 1;
     const long long tiles = a.kept_outer * ((a.K + 32 * cpt - 1) / (32 * cpt));
     // Split the folded range across blocks until the work items divide
