@@ -106,6 +106,60 @@ __global__ void __launch_bounds__(256) copy_transpose(const CopyDesc d, int t_ax
   }
 }
 
+
+// Tiled transpose for 2-byte elements, 64 x 64 tiles moved as 32-bit pairs:
+// a warp reads 64 source-contiguous elements (128 bytes) of one inner
+// index, and writes 64 target-contiguous elements of one t index.  Needs
+// even extents, strides and offsets along both axes.  A persistent grid
+// walks (other axes, inner tile, t tile).
+__global__ void __launch_bounds__(256) copy_transpose_pairs(const CopyDesc d, int t_axis, long long others) {
+  __shared__ uint16_t tile[64][66];  // [inner][t]
+  const uint16_t *src = reinterpret_cast<const uint16_t *>(d.src);
+  uint16_t *dst = reinterpret_cast<uint16_t *>(d.dst);
+  const int rank = d.rank;
+  const long long n_in = d.shape[rank - 1], n_t = d.shape[t_axis];
+  const long long tiles_i = (n_in + 63) / 64, tiles_t = (n_t + 63) / 64;
+  const long long total = others * tiles_i * tiles_t;
+  const long long s_in = d.stride[0][rank - 1], d_t = d.stride[1][t_axis];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (long long w = blockIdx.x; w < total; w += gridDim.x) {
+    long long o = w / (tiles_i * tiles_t);
+    const long long rem = w - o * tiles_i * tiles_t;
+    const long long i0 = (rem / tiles_t) * 64, t0 = (rem % tiles_t) * 64;
+    long long s = d.offset[0], t = d.offset[1];
+    for (int a = rank - 2; a >= 0; --a) {
+      if (a == t_axis) continue;
+      const long long e = d.shape[a], c = o % e;
+      o /= e;
+      s += c * d.stride[0][a];
+      t += c * d.stride[1][a];
+    }
+    // read: warp rows = inner indices, lanes = pairs along t
+    const long long tp = t0 + 2 * lane;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = warp + 8 * k;
+      if (i0 + i < n_in && tp < n_t) {
+        const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(src + s + (i0 + i) * s_in + tp));
+        tile[i][2 * lane] = uint16_t(v & 0xffffu);
+        tile[i][2 * lane + 1] = uint16_t(v >> 16);
+      }
+    }
+    __syncthreads();
+    // write: warp rows = t indices, lanes = pairs along inner
+    const long long ip = i0 + 2 * lane;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = warp + 8 * k;
+      if (t0 + j < n_t && ip < n_in) {
+        const uint32_t v = uint32_t(tile[2 * lane][j]) | (uint32_t(tile[2 * lane + 1][j]) << 16);
+        *reinterpret_cast<uint32_t *>(dst + t + (t0 + j) * d_t + ip) = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 int largest_unit(size_t elem, const Dims &shape, const Dims *st, const void *src, const void *dst) {
   // The innermost run must be contiguous on both sides to widen.
   uint32_t r = shape.rank;
@@ -191,6 +245,22 @@ int copy_region(size_t elem, uint32_t rank, const size_t *shape, const void *src
         d.stride[1][a] = (long long)cst[1].v[a];
       }
       d.count = (long long)element_count(r, cs.v);
+      // 2-byte elements with even extents, strides and base offsets along
+      // both tile axes move as 32-bit pairs.
+      bool pairs = elem == 2 && cs.v[r - 1] % 2 == 0 && cs.v[t_axis] % 2 == 0 &&
+                   cst[0].v[r - 1] % 2 == 0 && cst[1].v[t_axis] % 2 == 0 && (uintptr_t(s) & 3u) == 0 &&
+                   (uintptr_t(t) & 3u) == 0;
+      for (uint32_t a = 0; pairs && a + 1 < r; ++a)
+        if (int(a) != t_axis) pairs = cst[0].v[a] % 2 == 0 && cst[1].v[a] % 2 == 0;
+      if (pairs) {
+        long long others = 1;
+        for (uint32_t a = 0; a + 1 < r; ++a)
+          if (int(a) != t_axis) others *= (long long)cs.v[a];
+        const long long tiles = others * (((long long)cs.v[r - 1] + 63) / 64) * (((long long)cs.v[t_axis] + 63) / 64);
+        unsigned grid = unsigned(std::min<long long>(tiles, (long long)sm_count() * 8));
+        copy_transpose_pairs<<<std::max(1u, grid), 256, 0, stream>>>(d, t_axis, others);
+        return check_launch("strided copy (transpose pairs)");
+      }
       int st = elem == 2 ? launch_transpose<2>(d, t_axis, stream)
              : elem == 4 ? launch_transpose<4>(d, t_axis, stream)
                          : launch_transpose<8>(d, t_axis, stream);
