@@ -39,6 +39,10 @@ int sm_count();
 // it is ordered on the caller's stream; two such calls running at the same
 // time on different streams of one device would share it.
 int scratch(size_t bytes, void **out);
+// `n` zeroed device counters, one set per device, grown on demand.  A kernel
+// that takes tickets from them sets each back to zero when it is done, so
+// they are zero between launches.
+int counters(size_t n, int **out);
 
 // ---------------------------------------------------------------------------
 // Element types.  A kernel computes in f32; loads widen exactly and stores

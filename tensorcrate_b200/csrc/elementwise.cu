@@ -7,21 +7,51 @@
 // (4 f32 or 8 f16/bf16), grid-stride loops sized to the SM count, and the
 // arithmetic done in f32 and rounded once per result with the explicit _rn
 // intrinsics, so no a*b+c is ever contracted.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tc {
 namespace {
 
-// The operation a kernel applies, chosen on the host and uniform across the
-// grid (a branch every thread takes the same way).
+// The operation a kernel applies, fixed at compile time: one instantiation
+// per (Pairwise kind, operator), so the inner loops carry no branch.
+template <int KIND, int OP> struct Fn {
+  __device__ __forceinline__ float operator()(float a, float b) const {
+    if (KIND == TC_PAIR_ARITHMETIC) return binary_value(OP, a, b);
+    if (KIND == TC_PAIR_COMPARE) return compare_value(OP, a, b);
+    return powf(a, b);
+  }
+};
+
+// Call f(Fn<kind, op>{}) for a run-time (kind, op).
+template <class G> int with_fn(int kind, int op, G &&g) {
+  switch (kind) {
+    case TC_PAIR_ARITHMETIC:
+      switch (op) {
+        case TC_ADD: return g(Fn<TC_PAIR_ARITHMETIC, TC_ADD>{});
+        case TC_SUB: return g(Fn<TC_PAIR_ARITHMETIC, TC_SUB>{});
+        case TC_MUL: return g(Fn<TC_PAIR_ARITHMETIC, TC_MUL>{});
+        case TC_DIV: return g(Fn<TC_PAIR_ARITHMETIC, TC_DIV>{});
+        default: return g(Fn<TC_PAIR_ARITHMETIC, TC_REM>{});
+      }
+    case TC_PAIR_COMPARE:
+      switch (op) {
+        case TC_MIN: return g(Fn<TC_PAIR_COMPARE, TC_MIN>{});
+        case TC_MAX: return g(Fn<TC_PAIR_COMPARE, TC_MAX>{});
+        case TC_MAX_SHARE: return g(Fn<TC_PAIR_COMPARE, TC_MAX_SHARE>{});
+        case TC_LESS: return g(Fn<TC_PAIR_COMPARE, TC_LESS>{});
+        case TC_LESS_EQUAL: return g(Fn<TC_PAIR_COMPARE, TC_LESS_EQUAL>{});
+        case TC_GREATER: return g(Fn<TC_PAIR_COMPARE, TC_GREATER>{});
+        default: return g(Fn<TC_PAIR_COMPARE, TC_GREATER_EQUAL>{});
+      }
+    default: return g(Fn<TC_PAIR_POWER, 0>{});
+  }
+}
+
 struct Pair {
   int kind;  // tc_pairwise
   int op;
-  __device__ __forceinline__ float operator()(float a, float b) const {
-    if (kind == TC_PAIR_ARITHMETIC) return binary_value(op, a, b);
-    if (kind == TC_PAIR_COMPARE) return compare_value(op, a, b);
-    return powf(a, b);
-  }
 };
 
 template <class T> struct Pack {
@@ -47,9 +77,9 @@ __device__ __forceinline__ void store_pack(typename T::S *p, const Pack<T> &k) {
 bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
 
 // out[i] = f(a[i], b[i]) — both operands whole.
-template <class T>
+template <class T, class F>
 __global__ void __launch_bounds__(256) ew_same(const typename T::S *a, const typename T::S *b,
-                                               typename T::S *out, size_t n, Pair f, bool vec) {
+                                               typename T::S *out, size_t n, F f, bool vec) {
   using S = typename T::S;
   constexpr int N = Pack<T>::N;
   size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x, stride = size_t(gridDim.x) * blockDim.x;
@@ -64,9 +94,9 @@ __global__ void __launch_bounds__(256) ew_same(const typename T::S *a, const typ
 }
 
 // out[i] = f(a[i], s) or f(s, a[i]).
-template <class T>
+template <class T, class F>
 __global__ void __launch_bounds__(256) ew_scalar(const typename T::S *a, float s, bool left,
-                                                 typename T::S *out, size_t n, Pair f, bool vec) {
+                                                 typename T::S *out, size_t n, F f, bool vec) {
   constexpr int N = Pack<T>::N;
   size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x, stride = size_t(gridDim.x) * blockDim.x;
   size_t packs = vec ? n / N : 0;
@@ -106,10 +136,10 @@ __global__ void __launch_bounds__(256) ew_clamp(const typename T::S *a, float lo
 // ac, bc in {0, 1} — a [rows, inner] walk after coalescing, which is what
 // `x + bias` over [64,512,1024] x [1,1,1024] becomes.  Packs along the
 // inner axis when it allows.
-template <class T>
+template <class T, class F>
 __global__ void __launch_bounds__(256) ew_rows(const typename T::S *a, long long as, int ac,
                                                const typename T::S *b, long long bs, int bc,
-                                               typename T::S *out, long long rows, long long inner, Pair f,
+                                               typename T::S *out, long long rows, long long inner, F f,
                                                bool vec) {
   using S = typename T::S;
   constexpr int N = Pack<T>::N;
@@ -144,10 +174,51 @@ __global__ void __launch_bounds__(256) ew_rows(const typename T::S *a, long long
   }
 }
 
+// The same for long rows (a's inner step 1, packs): a block takes U rows
+// at a time and its threads stride along them, so each thread has U loads
+// in flight and no index division.
+template <class T, class F, int U>
+__global__ void __launch_bounds__(256) ew_rows_blocked(const typename T::S *a, long long as,
+                                                       const typename T::S *b, long long bs, int bc,
+                                                       typename T::S *out, long long rows, long long inner, F f) {
+  using S = typename T::S;
+  constexpr int N = Pack<T>::N;
+  const int per_row = int(inner / N);
+  for (long long r0 = (long long)blockIdx.x * U; r0 < rows; r0 += (long long)gridDim.x * U) {
+    for (int c = threadIdx.x; c < per_row; c += blockDim.x) {
+      Pack<T> x[U], y[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (r0 + u < rows) x[u] = load_pack<T>(a + (r0 + u) * as + (long long)c * N);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (r0 + u < rows) {
+          if (bc) {
+            y[u] = (u > 0 && bs == 0) ? y[0] : load_pack<T>(b + (r0 + u) * bs + (long long)c * N);
+          } else {
+            const S sb = b[(r0 + u) * bs];
+#pragma unroll
+            for (int j = 0; j < N; ++j) y[u].v[j] = sb;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (r0 + u < rows) {
+          Pack<T> z;
+#pragma unroll
+          for (int j = 0; j < N; ++j) z.v[j] = T::store(f(T::load(x[u].v[j]), T::load(y[u].v[j])));
+          store_pack<T>(out + (r0 + u) * inner + (long long)c * N, z);
+        }
+      }
+    }
+  }
+}
+
 // Any layout: one element per thread, coordinates from the flat index.
-template <class T>
+template <class T, class F>
 __global__ void __launch_bounds__(256) ew_walk(const typename T::S *a, const typename T::S *b,
-                                               typename T::S *out, Walk w, long long n, Pair f) {
+                                               typename T::S *out, Walk w, long long n, F f) {
   long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     long long pos[2];
@@ -171,11 +242,13 @@ int same(int dtype, Pair f, const void *a, const void *b, void *out, size_t n, v
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     using S = typename T::S;
-    bool vec = aligned16(a) && aligned16(b) && aligned16(out);
-    unsigned grid = grid_for((n + Pack<T>::N - 1) / Pack<T>::N, 256, 8);
-    ew_same<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const S *>(a), static_cast<const S *>(b),
-                                                    static_cast<S *>(out), n, f, vec);
-    return check_launch("elementwise");
+    return with_fn(f.kind, f.op, [&](auto fn) {
+      bool vec = aligned16(a) && aligned16(b) && aligned16(out);
+      unsigned grid = grid_for((n + Pack<T>::N - 1) / Pack<T>::N, 256, 8);
+      ew_same<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const S *>(a), static_cast<const S *>(b),
+                                                      static_cast<S *>(out), n, fn, vec);
+      return check_launch("elementwise");
+    });
   });
 }
 
@@ -186,11 +259,13 @@ int scalar(int dtype, Pair f, const void *a, double s, int left, void *out, size
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     using S = typename T::S;
-    bool vec = aligned16(a) && aligned16(out);
-    unsigned grid = grid_for((n + Pack<T>::N - 1) / Pack<T>::N, 256, 8);
-    ew_scalar<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const S *>(a), float(s), left != 0,
-                                                      static_cast<S *>(out), n, f, vec);
-    return check_launch("elementwise scalar");
+    return with_fn(f.kind, f.op, [&](auto fn) {
+      bool vec = aligned16(a) && aligned16(out);
+      unsigned grid = grid_for((n + Pack<T>::N - 1) / Pack<T>::N, 256, 8);
+      ew_scalar<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const S *>(a), float(s), left != 0,
+                                                        static_cast<S *>(out), n, fn, vec);
+      return check_launch("elementwise scalar");
+    });
   });
 }
 
@@ -264,8 +339,18 @@ int tc_strided_binary(int dtype, int kind, int op, uint32_t rank, const size_t *
                    (!bi || (aligned16(pb) && bs % N == 0));
         long long work = rows * (vec ? inner / N : inner);
         unsigned grid = grid_for(size_t(work), 256, 8);
-        ew_rows<T><<<grid, 256, 0, s>>>(pa, as, int(ai), pb, bs, int(bi), po, rows, inner, f, vec);
-        return check_launch("strided binary");
+        if (vec && ai == 1 && inner / N >= 128) {
+          unsigned g = unsigned(std::min<long long>((rows + 3) / 4, (long long)sm_count() * 8));
+          return with_fn(f.kind, f.op, [&](auto fn) {
+            ew_rows_blocked<T, decltype(fn), 4><<<std::max(1u, g), 256, 0, s>>>(pa, as, pb, bs, int(bi), po, rows,
+                                                                                  inner, fn);
+            return check_launch("strided binary (rows)");
+          });
+        }
+        return with_fn(f.kind, f.op, [&](auto fn) {
+          ew_rows<T><<<grid, 256, 0, s>>>(pa, as, int(ai), pb, bs, int(bi), po, rows, inner, fn, vec);
+          return check_launch("strided binary");
+        });
       }
     }
     Walk w{};
@@ -276,8 +361,10 @@ int tc_strided_binary(int dtype, int kind, int op, uint32_t rank, const size_t *
       w.stride[1][ax] = (long long)cst[1].v[ax];
     }
     unsigned grid = grid_for(n, 256, 8);
-    ew_walk<T><<<grid, 256, 0, s>>>(pa, pb, po, w, (long long)n, f);
-    return check_launch("strided binary (walk)");
+    return with_fn(f.kind, f.op, [&](auto fn) {
+      ew_walk<T><<<grid, 256, 0, s>>>(pa, pb, po, w, (long long)n, fn);
+      return check_launch("strided binary (walk)");
+    });
   });
 }
 

@@ -17,7 +17,7 @@
 //    eight independent 128-bit loads before folding any.  When results are
 //    few and slices long, the slice is split into shares whose partial
 //    results land in a scratch buffer and are merged, in order, by a second
-//    small kernel.  A variance whose slice fits in registers is computed from
+//    small kernel (by the share that finishes last, on the fast path).  A variance whose slice fits in registers is computed from
 //    them in both passes, so the input is read from HBM once.
 //    (A variant fed by 1-D TMA bulk copies through a shared-memory ring was
 //    measured slower on B200 for 4 KB runs — 48 us against 30 us per
@@ -410,9 +410,18 @@ struct FastRows {
   float count;
 };
 
+// An accumulator another block wrote in this launch, read past L1.
+__device__ __forceinline__ Acc load_acc(const Acc *p) {
+  const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(p));
+  return {__uint_as_float(v.x), v.y};
+}
+
+// With several shares per result, each publishes its accumulator and takes
+// a ticket; the last to arrive merges them in share order (as
+// reduce_finish does), writes the result and sets the ticket back to zero.
 template <class T, int MODE>
 __global__ void __launch_bounds__(256) reduce_rows_fast(const typename T::S *in, const FastRows a, typename T::S *out,
-                                                        uint32_t *arg_out, Acc *partial) {
+                                                        uint32_t *arg_out, Acc *partial, int *tickets) {
   using S = typename T::S;
   constexpr int N = Pack<T>::N;
   constexpr int F = fold_of<MODE>();
@@ -442,20 +451,74 @@ __global__ void __launch_bounds__(256) reduce_rows_fast(const typename T::S *in,
       }
     }
     acc = warp_merge<F>(acc);
+    if (a.splits > 1) {
+      int ticket = 0;
+      if (lane == 0) {
+        partial[g] = acc;
+        __threadfence();
+        ticket = atomicAdd(&tickets[r], 1);
+      }
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket != a.splits - 1) continue;
+      __threadfence();
+      acc = identity<F>();
+      for (int q = lane; q < a.splits; q += 32) acc = merge<F>(acc, load_acc(partial + r * a.splits + q));
+      acc = warp_merge<F>(acc);
+      if (lane == 0) tickets[r] = 0;
+    }
     if (lane == 0) {
-      if (a.splits > 1) partial[g] = acc;
-      else if (is_arg<MODE>()) arg_out[r] = acc.i;
+      if (is_arg<MODE>()) arg_out[r] = acc.i;
       else if (MODE == M_MEAN) out[r] = T::store(__fdiv_rn(acc.v, a.count));
       else out[r] = T::store(acc.v);
     }
   }
 }
 
+// var_fast: a warp per result whose slice is one run of at most 32*8 packs
+// at in + r*kept_stride, held in registers between the two passes.
+template <class T>
+__global__ void __launch_bounds__(256) reduce_rows_var_fast(const typename T::S *in, long long kept_stride,
+                                                            long long results, int per_run, float count,
+                                                            float divisor, typename T::S *out) {
+  constexpr int N = Pack<T>::N;
+  constexpr int K = CACHE_PACKS;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < results; r += warps) {
+    const uint4 *base = reinterpret_cast<const uint4 *>(in + r * kept_stride);
+    Pack<T> x[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (32 * k + lane < per_run) x[k].raw = __ldg(base + 32 * k + lane);
+    Acc sum = identity<M_SUM>();
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (32 * k + lane < per_run) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) sum.v = __fadd_rn(sum.v, T::load(x[k].v[j]));
+      }
+    sum = warp_merge<M_SUM>(sum);
+    const float mean = __fdiv_rn(sum.v, count);
+    Acc dev = identity<M_SUM>();
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (32 * k + lane < per_run) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float d = __fsub_rn(T::load(x[k].v[j]), mean);
+          dev.v = __fadd_rn(dev.v, __fmul_rn(d, d));
+        }
+      }
+    dev = warp_merge<M_SUM>(dev);
+    if (lane == 0) out[r] = T::store(__fdiv_rn(dev.v, divisor));
+  }
+}
+
 // cols_fast: results r = ko*K + k (k along the stride-1 kept axis); a
 // block of 256 threads owns 256*CPT adjacent results of one kept-outer
 // index for one share of the folded rows (fixed folded stride), each thread
-// CPT of them with one vector load per row.  No shared memory: the shares
-// meet in `partial` (in order, reduce_cols_finish) when there are several.
+// CPT of them with one vector load per row.  When there are several shares
+// they meet in `partial`, merged in share order by the tile's last block.
 struct FastCols {
   long long kept_stride, folded_stride;  // elements
   long long kept_outer, K;
@@ -465,7 +528,8 @@ struct FastCols {
 
 template <class T, int MODE, int CPT>
 __global__ void __launch_bounds__(256) reduce_cols_fast(const typename T::S *in, const FastCols a, typename T::S *out,
-                                                        uint32_t *arg_out, Acc *partial) {
+                                                        uint32_t *arg_out, Acc *partial, int *tickets) {
+  __shared__ int last;
   using S = typename T::S;
   using V = Cols<T, CPT>;
   constexpr int W = 256 * CPT;
@@ -479,9 +543,9 @@ __global__ void __launch_bounds__(256) reduce_cols_fast(const typename T::S *in,
     const int ks = int(it - t * a.kshares);
     const long long ko = t / tiles_k;
     const long long k = (t - ko * tiles_k) * W + (long long)threadIdx.x * CPT;
-    if (k >= a.K) continue;  // CPT divides K
-    const S *base = in + ko * a.kept_stride + k;
-    const int f0 = ks * a.kchunk, f1 = min(a.depth, f0 + a.kchunk);
+    const bool live = k < a.K;  // CPT divides K
+    const S *base = in + ko * a.kept_stride + (live ? k : 0);
+    const int f0 = ks * a.kchunk, f1 = live ? min(a.depth, f0 + a.kchunk) : f0;
     Acc acc[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) acc[c] = identity<F>();
@@ -498,12 +562,35 @@ __global__ void __launch_bounds__(256) reduce_cols_fast(const typename T::S *in,
         }
     }
     const long long r = ko * a.K + k;
+    if (a.kshares > 1) {
+      // Publish this share and take the tile's ticket; the block that
+      // arrives last merges the shares in share order and resets it.
+      if (live) {
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) {
-      if (a.kshares > 1) partial[ks * results + r + c] = acc[c];
-      else if (is_arg<MODE>()) arg_out[r + c] = acc[c].i;
-      else if (MODE == M_MEAN) out[r + c] = T::store(__fdiv_rn(acc[c].v, a.count));
-      else out[r + c] = T::store(acc[c].v);
+        for (int c = 0; c < CPT; ++c) partial[ks * results + r + c] = acc[c];
+      }
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) last = atomicAdd(&tickets[t], 1) == a.kshares - 1;
+      __syncthreads();
+      if (!last) continue;
+      __threadfence();
+      if (live) {
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          acc[c] = load_acc(partial + r + c);
+          for (int q = 1; q < a.kshares; ++q) acc[c] = merge<F>(acc[c], load_acc(partial + q * results + r + c));
+        }
+      }
+      if (threadIdx.x == 0) tickets[t] = 0;
+    }
+    if (live) {
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        if (is_arg<MODE>()) arg_out[r + c] = acc[c].i;
+        else if (MODE == M_MEAN) out[r + c] = T::store(__fdiv_rn(acc[c].v, a.count));
+        else out[r + c] = T::store(acc[c].v);
+      }
     }
   }
 }
@@ -595,10 +682,12 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       f.splits = int(splits);
       f.share = int((a.outer + splits - 1) / splits);
       Acc *partial = nullptr;
+      int *tickets = nullptr;
       if (splits > 1) {
         void *p = nullptr;
         if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p)) return st;
         partial = static_cast<Acc *>(p);
+        if (int st = counters(size_t(results), &tickets)) return st;
       }
       static int resident_fast[7] = {0, 0, 0, 0, 0, 0, 0};
       if (!resident_fast[MODE]) {
@@ -608,14 +697,20 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       }
       const long long groups = results * splits;
       unsigned grid = unsigned(std::min<long long>((groups + 7) / 8, (long long)sms * resident_fast[MODE]));
-      reduce_rows_fast<T, MODE><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial);
-      if (splits > 1) {
-        RowsArgs fa = a;
-        fa.splits = int(splits);
-        unsigned g2 = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
-        reduce_finish<T, MODE><<<std::max(1u, g2), 256, 0, stream>>>(fa, partial, o, arg_out);
-      }
+      reduce_rows_fast<T, MODE><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial, tickets);
       return check_launch("reduce (rows, fast)");
+    }
+    if (MODE == M_VAR && a.vec && kc.rank <= 1 && a.outer == 1 && a.run / N <= 32LL * CACHE_PACKS) {
+      static int resident_var = 0;
+      if (!resident_var) {
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_rows_var_fast<T>, 256, 0);
+        resident_var = n > 0 ? n : 2;
+      }
+      unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * resident_var));
+      reduce_rows_var_fast<T><<<std::max(1u, grid), 256, 0, stream>>>(
+          in, kc.rank ? (long long)kcs.v[0] : 0, results, int(a.run / N), count, divisor, o);
+      return check_launch("reduce (rows, variance, fast)");
     }
     if (MODE == M_VAR) {
       a.splits = 1;
@@ -690,19 +785,16 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       f.kshares = ks;
       f.kchunk = int((depth + ks - 1) / ks);
       Acc *partial = nullptr;
+      int *tickets = nullptr;
       if (ks > 1) {
         void *p = nullptr;
         if (int st = scratch_get(size_t(ks) * size_t(a.kept_outer * a.K) * sizeof(Acc), &p)) return st;
         partial = static_cast<Acc *>(p);
+        if (int st = counters(size_t(tiles), &tickets)) return st;
       }
       const long long items = tiles * ks;
       unsigned grid = unsigned(std::min<long long>(items, (long long)sms * 8));
-      reduce_cols_fast<T, MODE, 4><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial);
-      if (ks > 1) {
-        const long long results_c = a.kept_outer * a.K;
-        reduce_cols_finish<T, MODE><<<grid_for(size_t(results_c), 256, 4), 256, 0, stream>>>(partial, results_c, ks,
-                                                                                              count, o, arg_out);
-      }
+      reduce_cols_fast<T, MODE, 4><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial, tickets);
       return check_launch("reduce (columns, fast)");
     }
     const int cpt = four ? 4 : 1;

@@ -99,6 +99,40 @@ int scratch(size_t bytes, void **out) {
   return TC_OK;
 }
 
+namespace {
+struct Counters {
+  std::mutex mu;
+  int *ptr[64] = {nullptr};
+  size_t n[64] = {0};
+};
+Counters &counter_state() {
+  static Counters *c = new Counters;  // never destroyed
+  return *c;
+}
+}  // namespace
+
+int counters(size_t n, int **out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(TC_EINVAL, "device %d", dev);
+  Counters &c = counter_state();
+  std::lock_guard<std::mutex> g(c.mu);
+  if (c.n[dev] < n) {
+    if (c.ptr[dev]) {
+      cudaDeviceSynchronize();
+      cudaFree(c.ptr[dev]);
+      c.ptr[dev] = nullptr;
+      c.n[dev] = 0;
+    }
+    size_t want = n < 65536 ? 65536 : n;
+    if (int st = check_cuda(cudaMalloc(&c.ptr[dev], want * sizeof(int)), "cudaMalloc (counters)")) return st;
+    if (int st = check_cuda(cudaMemset(c.ptr[dev], 0, want * sizeof(int)), "cudaMemset (counters)")) return st;
+    c.n[dev] = want;
+  }
+  *out = c.ptr[dev];
+  return TC_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Device pool: freed blocks are kept per (device, size class) and handed to
 // the next request of that class, as Metal's buffer pool does
