@@ -215,6 +215,19 @@ int tc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x,
 /* `vecmat` (kernels.rs:899; vector.rs:491-505): y[cols] = xᵀ[rows]·M. */
 int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m,
               void *y, void *stream);
+/* tc_vecmat for callers that cannot allocate device memory.  No counterpart
+ * in the reference.  Same row split, kernels and bits as tc_vecmat, but the
+ * split's f32 partial sums (shares x cols x 4 bytes) live in a 1 MiB static
+ * device array of the library instead of an allocated buffer; the call
+ * makes no cudaMalloc, cudaFree or other allocating call (its first call on
+ * a device looks the array's address up once).  TC_ERANGE, before any
+ * launch, when a
+ * shape's partials would not fit in 1 MiB.  Every call on a device shares
+ * the array: calls that overlap on the GPU (other streams, other threads)
+ * race on it, so order them, e.g. on one stream.  Nothing in the array has
+ * to start at zero. */
+int tc_vecmat_noalloc(int dtype, size_t rows, size_t cols, const void *x,
+                      const void *m, void *y, void *stream);
 
 /* ---- optimizer updates (the fused programs of src/optim.rs) ------------- */
 /* Adam's fused program (optim.rs:1048-1099), run in place over n elements:

@@ -78,6 +78,7 @@ SIGNATURES = {
     "tc_matmul": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_matvec": [_i, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_vecmat": [_i, _sz, _sz, _p, _p, _p, _p],
+    "tc_vecmat_noalloc": [_i, _sz, _sz, _p, _p, _p, _p],
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],
     "tc_sgd": [_i, _sz, _p, _p, _d, _p],
     "tc_coalesce": [_u32, _szp, _u32, _szp, _u32p, _szp, _szp],

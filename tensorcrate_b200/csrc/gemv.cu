@@ -8,6 +8,7 @@
 //    split the rows and combine in shared memory, so every row read is
 //    one coalesced segment.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -146,6 +147,37 @@ __global__ void __launch_bounds__(256) outer_rows(const typename T::S *a, const 
 }  // namespace
 }  // namespace tc
 
+// ---------------------------------------------------------------------------
+// Static scratch for tc_vecmat_noalloc: the row split's f32 partial sums,
+// in a device array that is part of the module, so the entry point
+// allocates nothing.  Every call on a device shares it.  Nothing in it has
+// to start at zero: each partial is written before it is read.
+// ---------------------------------------------------------------------------
+constexpr size_t VECMAT_NOALLOC_SCRATCH_BYTES = size_t(1) << 20;  // 1 MiB
+static __device__ __align__(256) float vecmat_noalloc_scratch[VECMAT_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace tc {
+namespace {
+// The array's address on the current device, looked up once per device.
+int vecmat_noalloc_scratch_address(float **out) {
+  static std::mutex mu;
+  static float *address[64] = {nullptr};
+  int dev = 0;
+  if (int st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return st;
+  if (dev < 0 || dev >= 64) return fail(TC_EINVAL, "vecmat_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> g(mu);
+  if (!address[dev]) {
+    void *p = nullptr;
+    if (int st = check_cuda(cudaGetSymbolAddress(&p, vecmat_noalloc_scratch), "cudaGetSymbolAddress (vecmat scratch)"))
+      return st;
+    address[dev] = static_cast<float *>(p);
+  }
+  *out = address[dev];
+  return TC_OK;
+}
+}  // namespace
+}  // namespace tc
+
 using namespace tc;
 
 extern "C" {
@@ -201,6 +233,48 @@ int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m,
       vecmat_finish<T><<<unsigned((cols + 31) / 32), dim3(32, 8), 0, s>>>(partial, int(shares), (long long)cols,
                                                                          static_cast<S *>(y));
     return check_launch("vecmat");
+  });
+}
+
+// tc_vecmat with the same row split and kernels, so the same bits, but the
+// partial sums in the static array above instead of the allocated scratch.
+int tc_vecmat_noalloc(int dtype, size_t rows, size_t cols, const void *x, const void *m, void *y, void *stream) {
+  if (cols == 0) return TC_OK;
+  if (!m || !x || !y) return fail(TC_EINVAL, "vecmat_noalloc: null pointer");
+  return with_real(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    using S = typename T::S;
+    constexpr int CPT = 16 / int(sizeof(S));
+    const bool vec = cols % CPT == 0 && (uintptr_t(m) & 15u) == 0;
+    const int cpt = vec ? CPT : 1;
+    const long long col_blocks = ((long long)cols + 32 * cpt - 1) / (32 * cpt);
+    long long shares = 1;
+    while (col_blocks * shares < 4LL * sm_count() && (long long)rows / (shares * 2) >= 64) shares *= 2;
+    const long long per = ((long long)rows + shares - 1) / shares;
+    float *partial = nullptr;
+    if (shares > 1) {
+      const size_t need = size_t(shares) * cols * sizeof(float);
+      if (need > VECMAT_NOALLOC_SCRATCH_BYTES)
+        return fail(TC_ERANGE,
+                    "vecmat_noalloc: %zu x %zu splits into %lld row shares whose partial sums take %zu bytes, more "
+                    "than its %zu-byte static scratch",
+                    rows, cols, shares, need, VECMAT_NOALLOC_SCRATCH_BYTES);
+      if (int st = vecmat_noalloc_scratch_address(&partial)) return st;
+    }
+    dim3 grid((unsigned)col_blocks, (unsigned)shares);
+    cudaStream_t s = as_stream(stream);
+    if (vec)
+      vecmat_cols<T, CPT><<<grid, dim3(32, 8), 0, s>>>(static_cast<const S *>(x), static_cast<const S *>(m),
+                                                        static_cast<S *>(y), (long long)rows, (long long)cols, per,
+                                                        partial);
+    else
+      vecmat_cols<T, 1><<<grid, dim3(32, 8), 0, s>>>(static_cast<const S *>(x), static_cast<const S *>(m),
+                                                      static_cast<S *>(y), (long long)rows, (long long)cols, per,
+                                                      partial);
+    if (shares > 1)
+      vecmat_finish<T><<<unsigned((cols + 31) / 32), dim3(32, 8), 0, s>>>(partial, int(shares), (long long)cols,
+                                                                         static_cast<S *>(y));
+    return check_launch("vecmat_noalloc");
   });
 }
 
