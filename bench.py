@@ -356,27 +356,51 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
     sp = C.c_void_p(stream.cuda_stream)
     m = k = n = size
     rng = np.random.default_rng(0)
-    a = cuda.CudaStorage.store(cuda.f32_to_bits(rng.uniform(-1, 1, m * k).astype(np.float32), dtype), dtype)
+    a_host = cuda.f32_to_bits(rng.uniform(-1, 1, m * k).astype(np.float32), dtype)
     b = cuda.CudaStorage.store(cuda.f32_to_bits(rng.uniform(-1, 1, k * n).astype(np.float32), dtype), dtype)
-    c = cuda.CudaStorage(dtype, m * n)
     code = N.DTYPES[dtype]
+    panels = world > 1 and dtype != "f32"
+    peer = None
+    if panels:
+        # Row panels: rank r computes rows [r*m/P, (r+1)*m/P) of C with B
+        # replicated; the GEMM epilogue stores each tile into every rank's C.
+        if m % world:
+            raise SystemExit(f"M={m} does not split over {world} ranks")
+        rows = m // world
+        a = cuda.CudaStorage.store(a_host[rank * rows * k:(rank + 1) * rows * k], dtype)
+        from tensorcrate_b200.sharding import PeerBuffer
+        peer = PeerBuffer(comm, m * n * 2)
 
-    def step():
-        N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a.ptr, b.ptr, c.ptr, 0, sp))
+        def step():
+            N.check("matmul_allgather", lib.tc_matmul_allgather(comm, code, rows, k, n, a.ptr, b.ptr, peer.handle, sp))
+    else:
+        a = cuda.CudaStorage.store(a_host, dtype)
+        c = cuda.CudaStorage(dtype, m * n)
+
+        def step():
+            N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a.ptr, b.ptr, c.ptr, 0, sp))
 
     ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
+    if peer is not None:
+        peer.close()
     flops = 2.0 * m * n * k
     pk, pk_kind = peaks()
-    tflops = flops / (ms * 1e-3) / 1e12
+    # Whole-job TFLOP/s: replicas each do the whole product; panels share one.
+    total = flops / (ms * 1e-3) / 1e12 * (1 if panels else world)
+    per_gpu = total / world
     peak = pk["bf16_tflops"] if dtype != "f32" else None
-    line = {"metric": f"{dtype} GEMM TFLOP/s", "value": round(world * tflops, 1), "unit": "TFLOP/s", "n_gpus": world,
+    workload = f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate"
+    parallelism = (f"row panels x{world}, all-gather fused into the GEMM epilogue (NVLink peer stores)" if panels
+                   else (f"replicas x{world}" if world > 1 else "single GPU"))
+    line = {"metric": f"{dtype} GEMM TFLOP/s", "value": round(total, 1), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic uniform[-1,1], seeded",
-            "config": {"workload": f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate",
+            "scaling": "strong" if panels else "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic uniform[-1,1], seeded",
+            "config": {"workload": workload, "parallelism": parallelism,
                        "l2": "inputs resident; the working set exceeds L2 at 8192 and above"},
             "roofline": {"bound": "tensor" if dtype != "f32" else "fp32-simt", "kernel": "gemm_tc" if dtype != "f32"
-                         else "gemm_simt", "achieved": round(tflops, 1), "peak": peak, "peak_source": pk_kind,
-                         "unit": "TFLOP/s", "frac": round(tflops / peak, 3) if peak else None, "traffic": None},
+                         else "gemm_simt", "achieved": round(per_gpu, 1), "peak": peak, "peak_source": pk_kind,
+                         "unit": "TFLOP/s", "frac": round(per_gpu / peak, 3) if peak else None, "traffic": None},
             "gpu_launches": args.steps, "clocks": clocks}
     return line
 
@@ -510,18 +534,8 @@ def max_over_ranks(torch, world, v: float) -> float:
 
 def init_comm(torch, world, rank):
     """NCCL communicator of the library, bootstrapped over torch.distributed."""
-    from tensorcrate_b200 import _native as N
-    if world == 1:
-        return None
-    uid = (C.c_uint8 * 128)()
-    if rank == 0:
-        N.call("tc_comm_unique_id", uid)
-    t = torch.tensor(list(uid), dtype=torch.uint8, device="cuda")
-    torch.distributed.broadcast(t, 0)
-    uid = (C.c_uint8 * 128)(*t.cpu().tolist())
-    comm = C.c_void_p()
-    N.call("tc_comm_init", rank, world, uid, C.byref(comm))
-    return comm
+    from tensorcrate_b200.sharding import nccl_comm
+    return nccl_comm(torch, world, rank)
 
 
 def main():

@@ -300,6 +300,28 @@ int tc_allgather(tc_comm *comm, int dtype, const void *send, void *recv, size_t 
 /* In-place all-reduce of `count` elements; op is tc_reduce. */
 int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void *stream);
 
+/* A device buffer of `bytes` on every rank, each rank also mapping every
+ * other rank's (CUDA IPC over NVLink).  Create and destroy are collective:
+ * every rank calls them, in the same order. */
+typedef struct tc_peer_buffer tc_peer_buffer;
+int tc_peer_buffer_create(tc_comm *comm, size_t bytes, tc_peer_buffer **out);
+int tc_peer_buffer_pointer(tc_peer_buffer *buf, void **local_dev);
+int tc_peer_buffer_destroy(tc_peer_buffer *buf);
+/* Row-panel product with its all-gather fused into the GEMM (the sharded
+ * form of Kernels::matmul, kernels.rs:956, for one large f16/bf16 product).
+ * Collective: rank r passes its panel A_r [rows x inner] and the whole
+ * B [inner x cols]; the tensor-core kernel stores each tile of
+ * C_r = A_r.B into row block r of every rank's `c`, so that when the call's
+ * work on `stream` completes, every rank's `c` holds the whole
+ * C [nranks*rows x cols] (rounded once, as tc_matmul rounds).  The call ends
+ * with a collective on `stream` that every rank's product precedes.  Every
+ * rank writes every rank's `c`: a rank must be done with `c` from an earlier
+ * call before any rank starts the next.  TC_ENOTSUP for f32 or a shape the
+ * tensor-core tiles do not take (inner < 16, rows of A or B not 16-byte
+ * aligned); TC_ERANGE when `c` is smaller than nranks*rows*cols elements. */
+int tc_matmul_allgather(tc_comm *comm, int dtype, size_t rows, size_t inner, size_t cols,
+                        const void *a, const void *b, tc_peer_buffer *c, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -94,6 +94,10 @@ SIGNATURES = {
     "tc_comm_destroy": [_p],
     "tc_allgather": [_p, _i, _p, _p, _sz, _p],
     "tc_allreduce": [_p, _i, _p, _sz, _i, _p],
+    "tc_peer_buffer_create": [_p, _sz, _p],
+    "tc_peer_buffer_pointer": [_p, _p],
+    "tc_peer_buffer_destroy": [_p],
+    "tc_matmul_allgather": [_p, _i, _sz, _sz, _sz, _p, _p, _p, _p],
 }
 
 

@@ -10,8 +10,10 @@
 #include <nccl.h>
 
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
+#include "gemm.cuh"
 
 namespace tc {
 namespace {
@@ -71,6 +73,17 @@ struct tc_comm {
   int rank, nranks;
 };
 
+// One device buffer per rank, every rank holding a mapping of every other
+// rank's (CUDA IPC handles exchanged over the communicator), so a kernel can
+// store straight into the peers' copies over NVLink.
+struct tc_peer_buffer {
+  tc_comm *comm;
+  size_t bytes;
+  void *local;
+  void *remote[64];  // remote[r] = rank r's buffer (local for this rank)
+  int *token;        // one int on this device: the completion collective's operand
+};
+
 using namespace tc;
 
 extern "C" {
@@ -115,6 +128,113 @@ int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void
   ncclRedOp_t r = op == TC_SUM ? ncclSum : op == TC_RMIN ? ncclMin : op == TC_RMAX ? ncclMax : ncclNumOps;
   if (r == ncclNumOps) return fail(TC_EINVAL, "allreduce: bad Reduce %d", op);
   return check_nccl(nccl().all_reduce(buf, buf, count, t, r, comm->comm, as_stream(stream)), "ncclAllReduce");
+}
+
+// Every rank's `bytes` of scratch meet in `all` (nranks * bytes), in rank
+// order, through an all-gather on a private stream.
+static int exchange(tc_comm *comm, const void *mine, size_t bytes, void *all) {
+  cudaStream_t s = nullptr;
+  if (int st = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return st;
+  void *dev = nullptr;
+  int st = check_cuda(cudaMalloc(&dev, bytes * size_t(comm->nranks)), "cudaMalloc (handle exchange)");
+  if (!st) st = check_cuda(cudaMemcpyAsync(static_cast<uint8_t *>(dev) + bytes * comm->rank, mine, bytes,
+                                           cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+  if (!st) st = check_nccl(nccl().all_gather(static_cast<uint8_t *>(dev) + bytes * comm->rank, dev, bytes, ncclUint8,
+                                             comm->comm, s), "ncclAllGather (handles)");
+  if (!st) st = check_cuda(cudaMemcpyAsync(all, dev, bytes * size_t(comm->nranks), cudaMemcpyDeviceToHost, s),
+                           "cudaMemcpyAsync");
+  if (!st) st = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  if (dev) cudaFree(dev);
+  cudaStreamDestroy(s);
+  return st;
+}
+
+// A collective that returns on each rank's stream once every rank has
+// reached it: an all-reduce of one int.
+static int rendezvous(tc_peer_buffer *buf, cudaStream_t stream) {
+  return check_nccl(nccl().all_reduce(buf->token, buf->token, 1, ncclInt32, ncclSum, buf->comm->comm, stream),
+                    "ncclAllReduce (rendezvous)");
+}
+
+int tc_peer_buffer_create(tc_comm *comm, size_t bytes, tc_peer_buffer **out) {
+  if (!comm || !out || bytes == 0) return fail(TC_EINVAL, "tc_peer_buffer_create: bad arguments");
+  if (comm->nranks > 64) return fail(TC_EINVAL, "tc_peer_buffer_create: %d ranks, at most 64", comm->nranks);
+  *out = nullptr;
+  auto *buf = new tc_peer_buffer{};
+  buf->comm = comm;
+  buf->bytes = bytes;
+  int st = check_cuda(cudaMalloc(&buf->local, bytes), "cudaMalloc (peer buffer)");
+  if (!st) st = check_cuda(cudaMalloc(&buf->token, sizeof(int)), "cudaMalloc (peer buffer token)");
+  if (!st) st = check_cuda(cudaMemset(buf->token, 0, sizeof(int)), "cudaMemset");
+  std::vector<cudaIpcMemHandle_t> handles(size_t(comm->nranks));
+  cudaIpcMemHandle_t mine;
+  if (!st) st = check_cuda(cudaIpcGetMemHandle(&mine, buf->local), "cudaIpcGetMemHandle");
+  if (!st) st = exchange(comm, &mine, sizeof mine, handles.data());
+  for (int r = 0; !st && r < comm->nranks; ++r) {
+    if (r == comm->rank) {
+      buf->remote[r] = buf->local;
+      continue;
+    }
+    st = check_cuda(cudaIpcOpenMemHandle(&buf->remote[r], handles[size_t(r)], cudaIpcMemLazyEnablePeerAccess),
+                    "cudaIpcOpenMemHandle");
+  }
+  if (st) {
+    for (int r = 0; r < comm->nranks; ++r)
+      if (r != comm->rank && buf->remote[r]) cudaIpcCloseMemHandle(buf->remote[r]);
+    if (buf->local) cudaFree(buf->local);
+    if (buf->token) cudaFree(buf->token);
+    delete buf;
+    return st;
+  }
+  *out = buf;
+  return TC_OK;
+}
+
+int tc_peer_buffer_pointer(tc_peer_buffer *buf, void **local) {
+  if (!buf || !local) return fail(TC_EINVAL, "tc_peer_buffer_pointer: null");
+  *local = buf->local;
+  return TC_OK;
+}
+
+int tc_peer_buffer_destroy(tc_peer_buffer *buf) {
+  if (!buf) return TC_OK;
+  // No rank may still write into another's buffer, nor hold a mapping of
+  // it when it is freed: meet before unmapping and again before freeing.
+  int st = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (!st) st = rendezvous(buf, nullptr);
+  if (!st) st = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  for (int r = 0; r < buf->comm->nranks; ++r)
+    if (r != buf->comm->rank && buf->remote[r]) cudaIpcCloseMemHandle(buf->remote[r]);
+  if (!st) st = rendezvous(buf, nullptr);
+  if (!st) st = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  cudaFree(buf->local);
+  cudaFree(buf->token);
+  delete buf;
+  return st;
+}
+
+int tc_matmul_allgather(tc_comm *comm, int dtype, size_t rows, size_t inner, size_t cols, const void *a,
+                        const void *b, tc_peer_buffer *c, void *stream) {
+  if (!comm || !c || c->comm != comm) return fail(TC_EINVAL, "matmul_allgather: communicator and buffer differ");
+  if (dtype != TC_BF16 && dtype != TC_F16)
+    return fail(TC_ENOTSUP, "matmul_allgather: tensor-core element types only (f16, bf16)");
+  if (comm->nranks - 1 > 7) return fail(TC_ENOTSUP, "matmul_allgather: at most 8 ranks");
+  const size_t need = size_t(comm->nranks) * rows * cols * 2;
+  if (need > c->bytes)
+    return fail(TC_ERANGE, "matmul_allgather: C needs %zu bytes, the buffer has %zu", need, c->bytes);
+  if (rows == 0 || cols == 0) return TC_OK;
+  if (!a || !b) return fail(TC_EINVAL, "matmul_allgather: null operand");
+  const size_t at = size_t(comm->rank) * rows * cols;  // this rank's panel, in elements
+  void *peers[7];
+  int n = 0;
+  for (int r = 0; r < comm->nranks; ++r)
+    if (r != comm->rank) peers[n++] = static_cast<uint16_t *>(c->remote[r]) + at;
+  cudaStream_t s = as_stream(stream);
+  int st = gemm_tc_run_peers(dtype, TC_TRANS_NONE, rows, inner, cols, a, b, static_cast<uint16_t *>(c->local) + at,
+                             false, peers, n, s);
+  if (st == TC_ENOTSUP) return fail(TC_ENOTSUP, "matmul_allgather: shape or alignment the tensor-core tiles refuse");
+  if (st) return st;
+  return rendezvous(c, s);
 }
 
 }  // extern "C"

@@ -10,4 +10,9 @@ int gemm_simt_run(int dtype, int transposed, size_t rows, size_t inner, size_t c
 // tiles; the caller then runs the SIMT kernel.
 int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
                 void *c, bool accumulate, cudaStream_t stream);
+// The same product, each tile also stored to the `n_peers` (at most 7)
+// buffers in peer_c: C as other GPUs hold it, at the same offset.
+int gemm_tc_run_peers(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
+                      const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers,
+                      cudaStream_t stream);
 }  // namespace tc

@@ -5,7 +5,8 @@
 //
 // One persistent CTA per SM, warp-specialised:
 //   warp 0      TMA producer: 128-byte-swizzled tiles of A and B into a ring
-//               of shared-memory stages (cp.async.bulk.tensor, no multicast).
+//               of shared-memory stages (cp.async.bulk.tensor; each CTA loads
+//               its own tiles).
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
 //               K=16) into an f32 accumulator in TMEM and commits each stage
 //               back to the producer and each finished tile to the epilogue.
@@ -133,6 +134,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+constexpr int MAX_PEERS = 7;
+
 struct Params {
   int M, N, K;
   int a_mn, b_mn;  // 1 = MN-major operand
@@ -140,6 +143,11 @@ struct Params {
   void *c;
   int elem_is_bf16;
   int vec_store;  // rows of C start 16-byte aligned
+  // The same C on other GPUs (peer pointers over NVLink): every tile is
+  // stored there as well as to `c`, which fuses an all-gather of row panels
+  // into the epilogue.
+  int n_peers;
+  void *peer_c[MAX_PEERS];
 };
 
 // Tile t of the persistent sequence -> (m block, n block), grouped along M
@@ -340,6 +348,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
+          const size_t at = size_t(row) * size_t(p.N) + size_t(col0);
           if (whole) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -349,18 +358,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const float a = v[8 * j + 2 * h], b = v[8 * j + 2 * h + 1];
                 w[h] = p.elem_is_bf16 ? pack2_bf16(a, b) : pack2_f16(a, b);
               }
-              *reinterpret_cast<uint4 *>(crow + col0 + 8 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+              const uint4 q4 = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4 *>(crow + col0 + 8 * j) = q4;
+#pragma unroll
+              for (int i = 0; i < MAX_PEERS; ++i)
+                if (i < p.n_peers) *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.peer_c[i]) + at + 8 * j) = q4;
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) crow[col0 + j] = p.elem_is_bf16 ? BF16T::store(v[j]) : F16T::store(v[j]);
+              if (col0 + j < p.N) {
+                const uint16_t o = p.elem_is_bf16 ? BF16T::store(v[j]) : F16T::store(v[j]);
+                crow[col0 + j] = o;
+#pragma unroll
+                for (int i = 0; i < MAX_PEERS; ++i)
+                  if (i < p.n_peers) static_cast<uint16_t *>(p.peer_c[i])[at + j] = o;
+              }
           }
         }
       }
       fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
+    // Stores to peers are ordered before whatever this GPU does next (the
+    // collective that tells the peers the product is complete).
+    if (p.n_peers) __threadfence_system();
   }
 
   fence_before();
@@ -424,6 +446,13 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, cudaSt
 
 int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
                 void *c, bool accumulate, cudaStream_t stream) {
+  return gemm_tc_run_peers(dtype, transposed, rows, inner, cols, a, b, c, accumulate, nullptr, 0, stream);
+}
+
+int gemm_tc_run_peers(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
+                      const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers,
+                      cudaStream_t stream) {
+  if (n_peers < 0 || n_peers > MAX_PEERS) return fail(TC_EINVAL, "gemm: %d peers, at most %d", n_peers, MAX_PEERS);
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ENOTSUP;
   if (inner < 16 || rows > 0x7fffffffu || cols > 0x7fffffffu || inner > 0x7fffffffu) return TC_ENOTSUP;
   const bool a_mn = transposed == TC_TRANS_LEFT;   // A stored [K, M]
@@ -442,6 +471,11 @@ int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t col
   p.c = c;
   p.elem_is_bf16 = bf16;
   p.vec_store = (uintptr_t(c) & 15u) == 0 && (cols * 2) % 16 == 0;
+  p.n_peers = n_peers;
+  for (int i = 0; i < MAX_PEERS; ++i) {
+    p.peer_c[i] = i < n_peers ? peer_c[i] : nullptr;
+    if (i < n_peers && (uintptr_t(peer_c[i]) & 15u)) p.vec_store = 0;
+  }
   // 128x256 tiles when they fill the machine, else 128x128.
   const long long tiles256 = ((long long)(rows + BM - 1) / BM) * ((long long)(cols + 255) / 256);
   const int BN = tiles256 >= sm_count() ? 256 : 128;

@@ -33,3 +33,42 @@ def batch_split(global_batch: int, world: int) -> int:
     if global_batch % world:
         raise ValueError(f"a global batch of {global_batch} does not split over {world} ranks")
     return global_batch // world
+
+
+def nccl_comm(torch, world: int, rank: int):
+    """The library's NCCL communicator for this rank (None at world 1):
+    rank 0 draws the unique id and torch.distributed broadcasts it."""
+    import ctypes as C
+
+    from . import _native as N
+    if world == 1:
+        return None
+    uid = (C.c_uint8 * 128)()
+    if rank == 0:
+        N.call("tc_comm_unique_id", uid)
+    t = torch.tensor(list(uid), dtype=torch.uint8, device="cuda")
+    torch.distributed.broadcast(t, 0)
+    uid = (C.c_uint8 * 128)(*t.cpu().tolist())
+    comm = C.c_void_p()
+    N.call("tc_comm_init", rank, world, uid, C.byref(comm))
+    return comm
+
+
+class PeerBuffer:
+    """A tc_peer_buffer: `nbytes` on every rank, each mapping the others'."""
+
+    def __init__(self, comm, nbytes: int):
+        import ctypes as C
+
+        from . import _native as N
+        self.handle = C.c_void_p()
+        N.call("tc_peer_buffer_create", comm, nbytes, C.byref(self.handle))
+        local = C.c_void_p()
+        N.call("tc_peer_buffer_pointer", self.handle, C.byref(local))
+        self.ptr, self.nbytes = local.value, nbytes
+
+    def close(self) -> None:
+        from . import _native as N
+        if self.handle:
+            N.call("tc_peer_buffer_destroy", self.handle)
+            self.handle = None

@@ -1,0 +1,177 @@
+"""One rank of the multi-GPU parity checks, run by test_multi_gpu.py under
+torch.distributed.run (one process per GPU, NCCL).  Each check computes a
+sharded result through the library's collectives and compares it with the
+same result computed whole on this rank's GPU:
+
+- tc_matmul_allgather (row panels, all-gather fused into the GEMM epilogue
+  over NVLink peer stores) against tc_matmul of the whole product: the same
+  bits, on two calls in a row;
+- config 2's reductions over a leading-axis shard, finished by all-gather
+  (sum/mean over axis 2, argmax over axis 1) or all-reduce (max/min over
+  axes 0 and 2), against the whole tensor: the same bits (the integral
+  filler makes every sum exact in any order);
+- one data-parallel training step (global batch split over the ranks,
+  gradients all-reduced) against the whole batch on one GPU, f32.
+
+Rank 0 prints one JSON line {"failures": [...]}; the exit status is 1 when
+any check failed on any rank."""
+from __future__ import annotations
+
+import ctypes as C
+import datetime
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+import torch  # noqa: E402
+
+from tensorcrate_b200 import _native as N  # noqa: E402
+from tensorcrate_b200 import cuda  # noqa: E402
+from tensorcrate_b200.mlp import Mlp, xavier  # noqa: E402
+from tensorcrate_b200.sharding import PeerBuffer, nccl_comm, shard  # noqa: E402
+from util import integral  # noqa: E402
+
+
+def check_matmul_allgather(comm, world, rank, sp, failures):
+    lib = N.lib()
+    for rows, inner, cols in ((256, 512, 640), (200, 96, 136)):
+        b = cuda.CudaStorage.store(
+            cuda.f32_to_bits(np.random.default_rng(3).uniform(-1, 1, inner * cols).astype(np.float32), "bf16"), "bf16")
+        c = PeerBuffer(comm, world * rows * cols * 2)
+        try:
+            for call, seed in enumerate((5, 6)):
+                a_full = cuda.f32_to_bits(
+                    np.random.default_rng(seed).uniform(-1, 1, world * rows * inner).astype(np.float32), "bf16")
+                panel = cuda.CudaStorage.store(a_full[rank * rows * inner:(rank + 1) * rows * inner], "bf16")
+                N.check("matmul_allgather", lib.tc_matmul_allgather(comm, N.BF16, rows, inner, cols, panel.ptr, b.ptr,
+                                                                    c.handle, sp))
+                torch.cuda.synchronize()
+                got = np.empty(world * rows * cols, np.uint16)
+                N.call("tc_memcpy_d2h", got.ctypes.data_as(C.c_void_p), C.c_void_p(c.ptr), got.nbytes, None)
+                whole_a = cuda.CudaStorage.store(a_full, "bf16")
+                want = cuda.CudaStorage("bf16", world * rows * cols)
+                N.check("matmul", lib.tc_matmul(N.BF16, 0, world * rows, inner, cols, whole_a.ptr, b.ptr, want.ptr, 0,
+                                                sp))
+                torch.cuda.synchronize()
+                if not np.array_equal(got, want.as_slice()):
+                    bad = int(np.count_nonzero(got != want.as_slice()))
+                    failures.append(f"rank {rank}: matmul_allgather {rows}x{inner}x{cols} call {call}: "
+                                    f"{bad} elements differ from the whole product")
+                torch.distributed.barrier()
+        finally:
+            c.close()
+
+
+def check_reduction_shards(comm, world, rank, sp, failures):
+    lib = N.lib()
+    per = [4, 64, 256]
+    total = per[0] * world
+    whole = integral(total * per[1] * per[2]).reshape(total, per[1], per[2])
+    start, count = shard(total, world, rank)
+    mine = np.ascontiguousarray(whole[start:start + count])
+    sz = N.sizes
+
+    def run(x_host):
+        shape = list(x_host.shape)
+        n = x_host.size
+        x = cuda.CudaStorage.store(x_host.ravel(), "f32")
+        xs, xst = sz(shape), sz(cuda.contiguous_strides(shape))
+        out = {k: cuda.CudaStorage("f32", shape[0] * shape[1]) for k in ("sum", "mean")}
+        out.update({k: cuda.CudaStorage("f32", shape[1]) for k in ("max", "min")})
+        out["argmax"] = cuda.CudaStorage("u32", shape[0] * shape[2])
+        N.check("sum", lib.tc_reduce_axes(0, 3, xs, x.ptr, n, 0, xst, 1, N.u32s([2]), N.AXIS_FOLD, N.SUM, 0,
+                                          out["sum"].ptr, sp))
+        N.check("mean", lib.tc_reduce_axes(0, 3, xs, x.ptr, n, 0, xst, 1, N.u32s([2]), N.AXIS_MEAN, 0, 0,
+                                           out["mean"].ptr, sp))
+        for k, op in (("max", N.RMAX), ("min", N.RMIN)):
+            N.check(k, lib.tc_reduce_axes(0, 3, xs, x.ptr, n, 0, xst, 2, N.u32s([0, 2]), N.AXIS_FOLD, op, 0,
+                                          out[k].ptr, sp))
+        argp = C.cast(C.c_void_p(out["argmax"].ptr), C.POINTER(C.c_uint32))
+        N.check("argmax", lib.tc_arg_reduce(0, 3, xs, x.ptr, n, 0, xst, 1, N.RMAX, argp, sp))
+        return x, out
+
+    _, local = run(mine)
+    gathered = {}
+    for k in ("sum", "mean", "argmax"):
+        gathered[k] = cuda.CudaStorage(local[k].dtype, local[k].len * world)
+        N.check("allgather", lib.tc_allgather(comm, N.DTYPES[local[k].dtype], local[k].ptr, gathered[k].ptr,
+                                              local[k].len, sp))
+    for k, op in (("max", N.RMAX), ("min", N.RMIN)):
+        N.check("allreduce", lib.tc_allreduce(comm, N.F32, local[k].ptr, local[k].len, op, sp))
+    torch.cuda.synchronize()
+    _, ref = run(whole)
+    torch.cuda.synchronize()
+    for k in ("sum", "mean", "argmax"):
+        if not np.array_equal(gathered[k].as_slice(), ref[k].as_slice()):
+            failures.append(f"rank {rank}: sharded {k} differs from the whole tensor's")
+    for k in ("max", "min"):
+        if not np.array_equal(local[k].as_slice(), ref[k].as_slice()):
+            failures.append(f"rank {rank}: sharded {k} differs from the whole tensor's")
+
+
+def check_data_parallel_step(comm, world, rank, sp, failures):
+    dims, gbatch = [64, 128, 64], 32
+    batch = gbatch // world
+    rng = np.random.default_rng(9)
+    weights = [xavier(dims[l + 1], dims[l], rng) for l in range(len(dims) - 1)]
+    biases = [np.zeros(dims[l + 1], np.float32) for l in range(len(dims) - 1)]
+    x = rng.standard_normal((dims[0], gbatch)).astype(np.float32)
+    y = rng.standard_normal((dims[-1], gbatch)).astype(np.float32)
+    cols = slice(rank * batch, (rank + 1) * batch)
+    dp = Mlp("f32", dims, batch, gbatch, rate=1e-3, beta2=0.99, eps=1e-4)
+    one = Mlp("f32", dims, gbatch, gbatch, rate=1e-3, beta2=0.99, eps=1e-4)
+    dp.load(weights, biases)
+    one.load(weights, biases)
+    xd = cuda.CudaStorage.store(np.ascontiguousarray(x[:, cols]).ravel(), "f32")
+    yd = cuda.CudaStorage.store(np.ascontiguousarray(y[:, cols]).ravel(), "f32")
+    xw = cuda.CudaStorage.store(x.ravel(), "f32")
+    yw = cuda.CudaStorage.store(y.ravel(), "f32")
+    for _ in range(2):
+        dp.step(xd, yd, comm=comm, stream=torch.cuda.current_stream())
+        one.step(xw, yw, stream=torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    for l in range(len(dims) - 1):
+        for name, got, want in zip(("weight", "bias"), dp.params(l), one.params(l)):
+            # The gradient sums reorder over ranks: f32 rounding, then Adam.
+            err = float(np.max(np.abs(got - want)))
+            if not err <= 2e-5:
+                failures.append(f"rank {rank}: data-parallel layer {l} {name} differs by {err:.3g}")
+
+
+def main() -> int:
+    world, rank = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    N.call("tc_set_device", local)
+    torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                                         device_id=torch.device("cuda", local))
+    comm = nccl_comm(torch, world, rank)
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    failures: list[str] = []
+    for check in (check_matmul_allgather, check_reduction_shards, check_data_parallel_step):
+        try:
+            check(comm, world, rank, sp, failures)
+        except Exception as e:  # a failed call is a failed check; every rank still reaches the end
+            failures.append(f"rank {rank}: {check.__name__}: {e}")
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+    flags = torch.tensor([len(failures)], dtype=torch.int32, device="cuda")
+    torch.distributed.all_reduce(flags)
+    everyone = [None] * world
+    torch.distributed.all_gather_object(everyone, failures)
+    N.call("tc_comm_destroy", comm)
+    torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"world": world, "failures": [f for fs in everyone for f in fs]}), flush=True)
+    return 1 if int(flags.item()) else 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
