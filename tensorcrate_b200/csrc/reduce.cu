@@ -514,72 +514,93 @@ __global__ void __launch_bounds__(256) reduce_rows_var_fast(const typename T::S 
   }
 }
 
-// cols_fast: results r = ko*K + k (k along the stride-1 kept axis); a
-// block of 256 threads owns 256*CPT adjacent results of one kept-outer
-// index for one share of the folded rows (fixed folded stride), each thread
-// CPT of them with one vector load per row.  When there are several shares
-// they meet in `partial`, merged in share order by the tile's last block.
+// cols_fast: results r = ko*K + k (k along the stride-1 kept axis), in tiles
+// of W = 256*CPT adjacent results of one kept-outer index; each thread owns
+// CPT of them and reads them with one vector load per folded row (fixed
+// folded stride).  The tiles' rows, laid end to end (tile-major), are cut
+// into gridDim.x equal ranges, one per block, all resident at once, so
+// every SM streams the same number of rows.  A tile whose rows fall in
+// several blocks' ranges gets one partial from each: a block's range meets
+// at most two tiles partly (its first and its last), so each block has two
+// partial slots of W accumulators.  The last block to finish a tile merges
+// its partials in block order and resets the tile's ticket.
 struct FastCols {
   long long kept_stride, folded_stride;  // elements
-  long long kept_outer, K;
-  int depth, kshares, kchunk;
+  long long kept_outer, K, tiles_k, tiles;
+  long long rows;                        // tiles * depth
+  int depth;
   float count;
 };
 
 template <class T, int MODE, int CPT>
-__global__ void __launch_bounds__(256) reduce_cols_fast(const typename T::S *in, const FastCols a, typename T::S *out,
-                                                        uint32_t *arg_out, Acc *partial, int *tickets) {
+__global__ void __launch_bounds__(256, 3) reduce_cols_fast(const typename T::S *in, const FastCols a, typename T::S *out,
+                                                           uint32_t *arg_out, Acc *partial, int *tickets) {
+  // (Feeding the rows through a per-thread cp.async ring in shared memory,
+  // with four blocks per SM, measured slower on B200: 45.8 us against 40 us
+  // for config 2's argmax.)
   __shared__ int last;
   using S = typename T::S;
   using V = Cols<T, CPT>;
   constexpr int W = 256 * CPT;
-  constexpr int U = 8;
+  constexpr int U = sizeof(S) == 4 ? 6 : 8;  // loads in flight per thread, within 80 registers
   constexpr int F = fold_of<MODE>();
-  const long long tiles_k = (a.K + W - 1) / W;
-  const long long items = a.kept_outer * tiles_k * a.kshares;
-  const long long results = a.kept_outer * a.K;
-  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
-    const long long t = it / a.kshares;
-    const int ks = int(it - t * a.kshares);
-    const long long ko = t / tiles_k;
-    const long long k = (t - ko * tiles_k) * W + (long long)threadIdx.x * CPT;
+  const long long G = gridDim.x, b = blockIdx.x;
+  long long x = b * a.rows / G;
+  const long long x_end = (b + 1) * a.rows / G;
+  while (x < x_end) {
+    const long long t = x / a.depth;
+    const int lo = int(x - t * a.depth);
+    const int hi = int(min((long long)a.depth, (long long)lo + (x_end - x)));
+    x += hi - lo;
+    const long long ko = t / a.tiles_k;
+    const long long k = (t - ko * a.tiles_k) * W + (long long)threadIdx.x * CPT;
     const bool live = k < a.K;  // CPT divides K
     const S *base = in + ko * a.kept_stride + (live ? k : 0);
-    const int f0 = ks * a.kchunk, f1 = live ? min(a.depth, f0 + a.kchunk) : f0;
     Acc acc[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) acc[c] = identity<F>();
-    for (int f = f0; f < f1; f += U) {
-      V x[U];
+    if (live)
+      for (int f = lo; f < hi; f += U) {
+        V v[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (f + u < f1) x[u].raw = __ldg(reinterpret_cast<const typename V::Raw *>(base + (long long)(f + u) * a.folded_stride));
+        for (int u = 0; u < U; ++u)
+          if (f + u < hi)
+            v[u].raw = __ldg(reinterpret_cast<const typename V::Raw *>(base + (long long)(f + u) * a.folded_stride));
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (f + u < f1) {
+        for (int u = 0; u < U; ++u)
+          if (f + u < hi) {
 #pragma unroll
-          for (int c = 0; c < CPT; ++c) push<F>(acc[c], T::load(x[u].v[c]), uint32_t(f + u));
-        }
-    }
+            for (int c = 0; c < CPT; ++c) push<F>(acc[c], T::load(v[u].v[c]), uint32_t(f + u));
+          }
+      }
     const long long r = ko * a.K + k;
-    if (a.kshares > 1) {
-      // Publish this share and take the tile's ticket; the block that
-      // arrives last merges the shares in share order and resets it.
+    if (lo > 0 || hi < a.depth) {
+      // Blocks first..first+n-1 hold the tile's rows (block(y), the one
+      // whose range holds flat row y, is ((y + 1) * G - 1) / rows).  Block q
+      // keeps its part of tile t in slot 0 when its range starts inside t,
+      // else (t is its last tile) in slot 1.
+      const long long t0 = t * a.depth;
+      const long long first = ((t0 + 1) * G - 1) / a.rows;
+      const int n = int(((t0 + a.depth) * G - 1) / a.rows - first + 1);
+      const int side = b * a.rows / G < t0 ? 1 : 0;
       if (live) {
+        Acc *mine = partial + (b * 2 + side) * W + threadIdx.x * CPT;
 #pragma unroll
-        for (int c = 0; c < CPT; ++c) partial[ks * results + r + c] = acc[c];
+        for (int c = 0; c < CPT; ++c) mine[c] = acc[c];
       }
       __threadfence();
       __syncthreads();
-      if (threadIdx.x == 0) last = atomicAdd(&tickets[t], 1) == a.kshares - 1;
+      if (threadIdx.x == 0) last = atomicAdd(&tickets[t], 1) == n - 1;
       __syncthreads();
       if (!last) continue;
       __threadfence();
       if (live) {
+        for (int q = 0; q < n; ++q) {
+          const long long blk = first + q;
+          const int sd = blk * a.rows / G < t0 ? 1 : 0;
+          const Acc *theirs = partial + (blk * 2 + sd) * W + threadIdx.x * CPT;
 #pragma unroll
-        for (int c = 0; c < CPT; ++c) {
-          acc[c] = load_acc(partial + r + c);
-          for (int q = 1; q < a.kshares; ++q) acc[c] = merge<F>(acc[c], load_acc(partial + q * results + r + c));
+          for (int c = 0; c < CPT; ++c) acc[c] = q ? merge<F>(acc[c], load_acc(theirs + c)) : load_acc(theirs + c);
         }
       }
       if (threadIdx.x == 0) tickets[t] = 0;
@@ -779,22 +800,26 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       f.K = a.K;
       f.depth = int(depth);
       f.count = count;
-      const long long tiles = a.kept_outer * ((a.K + 1023) / 1024);
-      int ks = 1;
-      while (tiles * ks < 2LL * sms && depth / (ks * 2) >= 32) ks *= 2;
-      f.kshares = ks;
-      f.kchunk = int((depth + ks - 1) / ks);
+      f.tiles_k = (a.K + 1023) / 1024;
+      f.tiles = a.kept_outer * f.tiles_k;
+      f.rows = f.tiles * depth;
+      static int resident_cols[7] = {0, 0, 0, 0, 0, 0, 0};
+      if (!resident_cols[MODE]) {
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_cols_fast<T, MODE, 4>, 256, 0);
+        resident_cols[MODE] = std::max(1, n);
+      }
+      // One resident wave of blocks, each with at least 16 rows.
+      const long long grid = std::max(1LL, std::min((long long)sms * resident_cols[MODE], f.rows / 16));
       Acc *partial = nullptr;
       int *tickets = nullptr;
-      if (ks > 1) {
+      if (grid > 1) {
         void *p = nullptr;
-        if (int st = scratch_get(size_t(ks) * size_t(a.kept_outer * a.K) * sizeof(Acc), &p)) return st;
+        if (int st = scratch_get(size_t(grid) * 2 * 1024 * sizeof(Acc), &p)) return st;
         partial = static_cast<Acc *>(p);
-        if (int st = counters(size_t(tiles), &tickets)) return st;
+        if (int st = counters(size_t(f.tiles), &tickets)) return st;
       }
-      const long long items = tiles * ks;
-      unsigned grid = unsigned(std::min<long long>(items, (long long)sms * 8));
-      reduce_cols_fast<T, MODE, 4><<<std::max(1u, grid), 256, 0, stream>>>(in, f, o, arg_out, partial, tickets);
+      reduce_cols_fast<T, MODE, 4><<<unsigned(grid), 256, 0, stream>>>(in, f, o, arg_out, partial, tickets);
       return check_launch("reduce (columns, fast)");
     }
     const int cpt = four ? 4 : 1;

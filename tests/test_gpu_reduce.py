@@ -180,3 +180,24 @@ def test_streamed_reductions_of_long_runs(device, dtype):
     fault = C.c_int(0)
     N.call("tc_device_status", C.byref(fault))
     assert fault.value == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", [[3, 2049, 1028], [40, 300, 2048], [1, 7, 4096], [512, 4, 1024]])
+def test_column_reductions_split_across_blocks(device, dtype, shape):
+    """Folds over axis 1 with the results side by side (the columns path):
+    every block streams an equal range of rows, so a tile's rows may be
+    shared by several blocks whose partials merge in block order.  Ragged
+    tiles (1028 columns) and short slices (7 rows) included; the integral
+    filler makes every sum exact."""
+    n = int(np.prod(shape))
+    x = O.narrow(integral(n), dtype)
+    st = cuda.contiguous_strides(shape)
+    v = cuda.TensorView(cuda.CudaStorage.store(x, dtype), shape, st, 0)
+    for kind, op in [(N.AXIS_FOLD, N.SUM), (N.AXIS_FOLD, N.RMIN), (N.AXIS_FOLD, N.RMAX), (N.AXIS_MEAN, 0)]:
+        got = O.widen(cuda.Cuda.reduce_axes(v, [1], kind, op, 0).as_slice(), dtype)
+        want = O.widen(O.reduce_axes(dtype, shape, x, 0, st, [1], kind, op, 0), dtype)
+        assert np.array_equal(got, want), (kind, op)
+    for op in (N.RMAX, N.RMIN):
+        got = cuda.Cuda.arg_reduce(v, 1, op).as_slice()
+        assert np.array_equal(got, O.arg_reduce(dtype, shape, x, 0, st, 1, op)), op
