@@ -133,9 +133,12 @@ int tc_strided_write(size_t elem_bytes, void *target, size_t target_len,
                      const tc_region *region, void *stream);
 
 /* `Backend::assemble` (src/tensors/backend.rs:157-160; Host assemble_slices
- * :303-323): a new storage of `len` elements built from `n` regions, each
- * region one copy launch; elements no region writes are left as they were in
- * `dst` (the reference leaves them unspecified). */
+ * :303-323): a new storage of `len` elements built from `n` regions.
+ * Regions whose targets are disjoint boxes (a concatenation's) may share a
+ * launch; otherwise they are written in order, so where two overlap the
+ * later one's values remain, as the Host leaves them.  Elements no region
+ * writes are left as they were in `dst` (the reference leaves them
+ * unspecified). */
 int tc_assemble(size_t elem_bytes, void *dst, size_t len, const tc_region *regions,
                 size_t n, void *stream);
 
@@ -207,6 +210,21 @@ int tc_arg_reduce(int dtype, uint32_t rank, const size_t *shape, const void *inp
  * src/compact.rs:232-253). */
 int tc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
               const void *a, const void *b, void *c, int accumulate, void *stream);
+/* `matmul_epilogue` (kernels.rs:1137-1150, reached through
+ * Program::run_matmul, fused/mod.rs:1143) for the programs a dense layer's
+ * forward and backward build, applied in this order to the product P:
+ *   share_of (not null): P = P * MaxShare(share_of, 0), the ReLU's backward
+ *     rule (Compare::MaxShare, kernels.rs:138-153; tape/mod.rs:1110-1130);
+ *     share_of is laid out as c
+ *   bias (not null): P = P + bias[row] (the add of b ⊗ ones)
+ *   c = P, and relu_out (not null) = max(P, 0) (Compare::Max against 0).
+ * Each step rounds to the element type as the separate operations do: the
+ * product once (as tc_matmul), then each op; max is exact.  f16/bf16 run
+ * it inside the tensor-core GEMM's epilogue; f32, and shapes the
+ * tensor-core tiles refuse, run the product and then one pass over it. */
+int tc_matmul_epilogue(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
+                       const void *a, const void *b, const void *share_of, const void *bias,
+                       void *c, void *relu_out, void *stream);
 
 /* `matvec`/`matvec_add` (kernels.rs:901-908; matrix.rs:675-730):
  * y[rows] (+)= M[rows x cols]·x[cols]. */
@@ -239,6 +257,20 @@ int tc_vecmat_noalloc(int dtype, size_t rows, size_t cols, const void *x,
 int tc_adam(int dtype, size_t n, void *p, const void *g, void *m, void *v, int resumed,
             double rate, double beta1, double beta2, double eps, double first_correction,
             double second_correction, void *stream);
+/* The same program over several parameters in one launch, as Adam::update
+ * steps every parameter with the same coefficients (optim.rs:1106-1140);
+ * each tensor's result is the one tc_adam gives it.  At most 16 tensors go
+ * in one launch; longer lists take several. */
+typedef struct tc_adam_tensor {
+  void *p;
+  const void *g;
+  void *m;
+  void *v;
+  size_t n;
+} tc_adam_tensor;
+int tc_adam_multi(int dtype, const tc_adam_tensor *tensors, size_t count, int resumed,
+                  double rate, double beta1, double beta2, double eps, double c1, double c2,
+                  void *stream);
 /* Sgd's fused program (optim.rs:773-787): p <- p - g·rate. */
 int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *stream);
 

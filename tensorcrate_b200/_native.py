@@ -47,6 +47,12 @@ class Region(C.Structure):
     ]
 
 
+class AdamTensor(C.Structure):
+    """tc_adam_tensor: one parameter of a tc_adam_multi call."""
+
+    _fields_ = [("p", _p), ("g", _p), ("m", _p), ("v", _p), ("n", _sz)]
+
+
 # name -> argtypes; every function returns int status.
 SIGNATURES = {
     "tc_last_error": [C.c_char_p, _sz],
@@ -78,8 +84,10 @@ SIGNATURES = {
     "tc_matmul": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_matvec": [_i, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_vecmat": [_i, _sz, _sz, _p, _p, _p, _p],
+    "tc_matmul_epilogue": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p],
     "tc_vecmat_noalloc": [_i, _sz, _sz, _p, _p, _p, _p],
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],
+    "tc_adam_multi": [_i, _p, _sz, _i, _d, _d, _d, _d, _d, _d, _p],
     "tc_sgd": [_i, _sz, _p, _p, _d, _p],
     "tc_coalesce": [_u32, _szp, _u32, _szp, _u32p, _szp, _szp],
     "tc_device_status": [C.POINTER(_i)],

@@ -30,7 +30,28 @@ struct CopyDesc {
   const char *src;
   char *dst;
   long long count;  // units to copy
+  // Division by shape[a] as a multiply and shift, for 32-bit indices
+  // (n < 2^31): n / d = umulhi(n, mul) >> shift, mul = ceil(2^(31+l) / d),
+  // shift = l - 1, l = ceil(log2 d) (Granlund and Montgomery, 1994); d = 1
+  // is marked by mul = 0.
+  uint32_t mul[TC_MAX_RANK], shift[TC_MAX_RANK];
 };
+
+// Fill d.mul / d.shift from d.shape (host).
+void prepare_division(CopyDesc &d) {
+  for (int a = 0; a < d.rank; ++a) {
+    const uint64_t e = uint64_t(d.shape[a]);
+    if (e <= 1 || e >= (1ull << 31)) {
+      d.mul[a] = 0;
+      d.shift[a] = 0;
+      continue;
+    }
+    int l = 0;
+    while ((1ull << l) < e) ++l;
+    d.mul[a] = uint32_t(((1ull << (31 + l)) + e - 1) / e);
+    d.shift[a] = uint32_t(l - 1);
+  }
+}
 
 template <int W> struct Unit;
 template <> struct Unit<1> { using T = uint8_t; };
@@ -40,29 +61,88 @@ template <> struct Unit<8> { using T = uint2; };
 template <> struct Unit<16> { using T = uint4; };
 
 // Copy `d.count` units of W bytes: flat row-major index -> both positions.
-// Shapes, strides and offsets are in units.
+// Shapes, strides and offsets are in units.  Each thread issues UNROLL
+// loads (one per grid stride) before it stores any.
+constexpr int UNROLL = 4;
+
+template <typename Index>
+__device__ __forceinline__ void unit_positions(const CopyDesc &d, Index i, Index &s, Index &t) {
+  const int rank = d.rank;
+  Index rest = i;
+  s = Index(d.offset[0]);
+  t = Index(d.offset[1]);
+  for (int a = rank - 1; a >= 0; --a) {
+    const Index e = Index(d.shape[a]);
+    Index q;
+    if (sizeof(Index) == 4)
+      q = d.mul[a] ? Index(__umulhi(uint32_t(rest), d.mul[a]) >> d.shift[a]) : (e == 1 ? rest : Index(0));
+    else
+      q = rest / e;
+    const Index ca = rest - q * e;
+    rest = q;
+    s += ca * Index(d.stride[0][a]);
+    t += ca * Index(d.stride[1][a]);
+  }
+}
+
 template <int W, typename Index>
 __global__ void __launch_bounds__(256) copy_units(const CopyDesc d) {
   using U = typename Unit<W>::T;
   const U *src = reinterpret_cast<const U *>(d.src);
   U *dst = reinterpret_cast<U *>(d.dst);
-  Index stride = Index(gridDim.x) * blockDim.x;
-  const int rank = d.rank;
-  Index inner = Index(d.shape[rank - 1]);
-  Index s_in = Index(d.stride[0][rank - 1]), t_in = Index(d.stride[1][rank - 1]);
-  for (Index i = Index(blockIdx.x) * blockDim.x + threadIdx.x; i < Index(d.count); i += stride) {
-    Index rest = i / inner;
-    Index c = i - rest * inner;
-    Index s = Index(d.offset[0]) + c * s_in, t = Index(d.offset[1]) + c * t_in;
-    for (int a = rank - 2; a >= 0; --a) {
-      Index e = Index(d.shape[a]);
-      Index q = rest / e;
-      Index ca = rest - q * e;
-      rest = q;
-      s += ca * Index(d.stride[0][a]);
-      t += ca * Index(d.stride[1][a]);
+  const Index stride = Index(gridDim.x) * blockDim.x;
+  const Index count = Index(d.count);
+  for (Index i0 = Index(blockIdx.x) * blockDim.x + threadIdx.x; i0 < count; i0 += stride * UNROLL) {
+    U v[UNROLL];
+    Index t[UNROLL];
+#pragma unroll
+    for (int k = 0; k < UNROLL; ++k) {
+      const Index i = i0 + Index(k) * stride;
+      if (i < count) {
+        Index s;
+        unit_positions(d, i, s, t[k]);
+        v[k] = __ldg(src + s);
+      }
     }
-    dst[t] = __ldg(src + s);
+#pragma unroll
+    for (int k = 0; k < UNROLL; ++k)
+      if (i0 + Index(k) * stride < count) dst[t[k]] = v[k];
+  }
+}
+
+// Several regions of one unit width in one launch (an assemble of run
+// copies): region k holds flat units [start[k], start[k+1]).
+constexpr int MAX_BATCH = 8;
+struct MultiDesc {
+  int n;
+  long long start[MAX_BATCH + 1];
+  CopyDesc r[MAX_BATCH];
+};
+
+template <int W, typename Index>
+__global__ void __launch_bounds__(256) copy_units_multi(const __grid_constant__ MultiDesc m) {
+  using U = typename Unit<W>::T;
+  const Index total = Index(m.start[m.n]);
+  const Index stride = Index(gridDim.x) * blockDim.x;
+  for (Index i0 = Index(blockIdx.x) * blockDim.x + threadIdx.x; i0 < total; i0 += stride * UNROLL) {
+    U v[UNROLL];
+    U *to[UNROLL];
+#pragma unroll
+    for (int k = 0; k < UNROLL; ++k) {
+      const Index i = i0 + Index(k) * stride;
+      if (i < total) {
+        int r = 0;
+        while (r + 1 < m.n && i >= Index(m.start[r + 1])) ++r;
+        const CopyDesc &d = m.r[r];
+        Index s, t;
+        unit_positions(d, i - Index(m.start[r]), s, t);
+        v[k] = __ldg(reinterpret_cast<const U *>(d.src) + s);
+        to[k] = reinterpret_cast<U *>(d.dst) + t;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < UNROLL; ++k)
+      if (i0 + Index(k) * stride < total) *to[k] = v[k];
   }
 }
 
@@ -107,53 +187,84 @@ __global__ void __launch_bounds__(256) copy_transpose(const CopyDesc d, int t_ax
 }
 
 
-// Tiled transpose for 2-byte elements, 64 x 64 tiles moved as 32-bit pairs:
-// a warp reads 64 source-contiguous elements (128 bytes) of one inner
-// index, and writes 64 target-contiguous elements of one t index.  Needs
-// even extents, strides and offsets along both axes.  A persistent grid
-// walks (other axes, inner tile, t tile).
+// Tiled transpose for 2-byte elements moved as 32-bit pairs: tiles of 64
+// target-contiguous (inner) by TT source-contiguous (t) elements, TT = 32 or
+// 64 to fit the t extent.  A warp reads whole 2*TT-byte source rows (one
+// inner index each) and writes 128-byte target rows (one t index each).  The
+// tile sits t-major in shared memory, so the writers read 32-bit pairs
+// along the inner axis without bank conflicts.  A block loads BATCH tiles
+// before it stores any.  Needs even extents, strides and offsets along both
+// tile axes.  A persistent grid walks (other axes, inner tile, t tile).
+template <int TT, int BATCH>
 __global__ void __launch_bounds__(256) copy_transpose_pairs(const CopyDesc d, int t_axis, long long others) {
-  __shared__ uint16_t tile[64][66];  // [inner][t]
+  constexpr int ROWS_PER_PASS = 256 / (TT / 2);  // inner rows one pass of the block reads
+  constexpr int PASSES = 64 / ROWS_PER_PASS;
+  constexpr int PITCH = 64 + 2;                   // u16 per t row: 33 words
+  __shared__ __align__(16) uint16_t tile[BATCH][TT][PITCH];
+  __shared__ const uint16_t *sb[BATCH];
+  __shared__ uint16_t *tb[BATCH];
+  __shared__ int ilim[BATCH], tlim[BATCH];  // valid inner / t extent of each tile
   const uint16_t *src = reinterpret_cast<const uint16_t *>(d.src);
   uint16_t *dst = reinterpret_cast<uint16_t *>(d.dst);
   const int rank = d.rank;
   const long long n_in = d.shape[rank - 1], n_t = d.shape[t_axis];
-  const long long tiles_i = (n_in + 63) / 64, tiles_t = (n_t + 63) / 64;
+  const long long tiles_i = (n_in + 63) / 64, tiles_t = (n_t + TT - 1) / TT;
   const long long total = others * tiles_i * tiles_t;
   const long long s_in = d.stride[0][rank - 1], d_t = d.stride[1][t_axis];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (long long w = blockIdx.x; w < total; w += gridDim.x) {
-    long long o = w / (tiles_i * tiles_t);
-    const long long rem = w - o * tiles_i * tiles_t;
-    const long long i0 = (rem / tiles_t) * 64, t0 = (rem % tiles_t) * 64;
-    long long s = d.offset[0], t = d.offset[1];
-    for (int a = rank - 2; a >= 0; --a) {
-      if (a == t_axis) continue;
-      const long long e = d.shape[a], c = o % e;
-      o /= e;
-      s += c * d.stride[0][a];
-      t += c * d.stride[1][a];
-    }
-    // read: warp rows = inner indices, lanes = pairs along t
-    const long long tp = t0 + 2 * lane;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = warp + 8 * k;
-      if (i0 + i < n_in && tp < n_t) {
-        const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(src + s + (i0 + i) * s_in + tp));
-        tile[i][2 * lane] = uint16_t(v & 0xffffu);
-        tile[i][2 * lane + 1] = uint16_t(v >> 16);
+  const int rp = threadIdx.x / (TT / 2), pp = threadIdx.x % (TT / 2);  // read: row in pass, pair
+  for (long long w0 = (long long)blockIdx.x * BATCH; w0 < total; w0 += (long long)gridDim.x * BATCH) {
+    // One thread per tile of the batch decomposes its index.
+    if (threadIdx.x < BATCH) {
+      const long long w = w0 + threadIdx.x;
+      long long o = w / (tiles_i * tiles_t);
+      const long long rem = w - o * tiles_i * tiles_t;
+      long long so = d.offset[0], to = d.offset[1];
+      for (int a = rank - 2; a >= 0; --a) {
+        if (a == t_axis) continue;
+        const long long e = d.shape[a], c = o % e;
+        o /= e;
+        so += c * d.stride[0][a];
+        to += c * d.stride[1][a];
       }
+      const long long i0 = (rem / tiles_t) * 64, j0 = (rem % tiles_t) * TT;
+      sb[threadIdx.x] = src + so + i0 * s_in + j0;
+      tb[threadIdx.x] = dst + to + j0 * d_t + i0;
+      ilim[threadIdx.x] = w < total ? int(min(64LL, n_in - i0)) : 0;
+      tlim[threadIdx.x] = w < total ? int(min((long long)TT, n_t - j0)) : 0;
     }
     __syncthreads();
-    // write: warp rows = t indices, lanes = pairs along inner
-    const long long ip = i0 + 2 * lane;
+    // read every tile of the batch before storing any
+    uint32_t v[BATCH][PASSES];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int j = warp + 8 * k;
-      if (t0 + j < n_t && ip < n_in) {
-        const uint32_t v = uint32_t(tile[2 * lane][j]) | (uint32_t(tile[2 * lane + 1][j]) << 16);
-        *reinterpret_cast<uint32_t *>(dst + t + (t0 + j) * d_t + ip) = v;
+    for (int q = 0; q < BATCH; ++q) {
+      const uint16_t *base = sb[q] + 2 * pp;
+      const bool tok = 2 * pp < tlim[q];
+#pragma unroll
+      for (int k = 0; k < PASSES; ++k) {
+        const int i = rp + ROWS_PER_PASS * k;
+        v[q][k] = (tok && i < ilim[q]) ? __ldg(reinterpret_cast<const uint32_t *>(base + (long long)i * s_in)) : 0u;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q)
+#pragma unroll
+      for (int k = 0; k < PASSES; ++k) {
+        const int i = rp + ROWS_PER_PASS * k;
+        tile[q][2 * pp][i] = uint16_t(v[q][k] & 0xffffu);
+        tile[q][2 * pp + 1][i] = uint16_t(v[q][k] >> 16);
+      }
+    __syncthreads();
+    // write: warp rows = t indices, lanes = pairs along inner
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const bool iok = 2 * lane < ilim[q];
+#pragma unroll
+      for (int k = 0; k < TT / 8; ++k) {
+        const int j = warp + 8 * k;
+        if (iok && j < tlim[q])
+          *reinterpret_cast<uint32_t *>(tb[q] + (long long)j * d_t + 2 * lane) =
+              *reinterpret_cast<const uint32_t *>(&tile[q][j][2 * lane]);
       }
     }
     __syncthreads();
@@ -207,11 +318,41 @@ int launch_transpose(const CopyDesc &d, int t_axis, cudaStream_t stream) {
   return check_launch("strided copy (transpose)");
 }
 
+// The unit-copy descriptor of a coalesced region: the widest unit, shape
+// and strides counted in units.
+int units_desc(size_t elem, const Dims &cs, const Dims *cst, const char *s, char *t, CopyDesc &d) {
+  const uint32_t r = cs.rank;
+  int w = largest_unit(elem, cs, cst, s, t);
+  size_t per = size_t(w) / elem;
+  for (uint32_t a = 0; a < r; ++a) {
+    bool inner = a + 1 == r;
+    d.shape[a] = (long long)(inner ? cs.v[a] / per : cs.v[a]);
+    d.stride[0][a] = (long long)(inner ? cst[0].v[a] : cst[0].v[a] / per);
+    d.stride[1][a] = (long long)(inner ? cst[1].v[a] : cst[1].v[a] / per);
+  }
+  if (per > 1) {  // contiguous inner run counted in units
+    d.stride[0][r - 1] = 1;
+    d.stride[1][r - 1] = 1;
+  }
+  d.count = (long long)(element_count(r, cs.v) / per);
+  prepare_division(d);
+  return w;
+}
+
+// A region that copies as plain units: its width and descriptor.
+struct UnitPlan {
+  int width;
+  CopyDesc desc;
+};
+
 // Copy one region: `shape` from (src, from) to (dst, to); both layouts
-// already checked.
+// already checked.  With `plan`, a region that would run as plain units is
+// described there instead of launched (TC_OK); any other region is launched
+// and plan->width is set to 0.
 int copy_region(size_t elem, uint32_t rank, const size_t *shape, const void *src, size_t from_offset,
                 const size_t *from_strides, void *dst, size_t to_offset, const size_t *to_strides,
-                cudaStream_t stream) {
+                cudaStream_t stream, UnitPlan *plan = nullptr) {
+  if (plan) plan->width = 0;
   if (element_count(rank, shape) == 0) return TC_OK;
   const size_t *ops[2] = {from_strides, to_strides};
   Dims cs, cst[2];
@@ -256,9 +397,23 @@ int copy_region(size_t elem, uint32_t rank, const size_t *shape, const void *src
         long long others = 1;
         for (uint32_t a = 0; a + 1 < r; ++a)
           if (int(a) != t_axis) others *= (long long)cs.v[a];
-        const long long tiles = others * (((long long)cs.v[r - 1] + 63) / 64) * (((long long)cs.v[t_axis] + 63) / 64);
-        unsigned grid = unsigned(std::min<long long>(tiles, (long long)sm_count() * 8));
-        copy_transpose_pairs<<<std::max(1u, grid), 256, 0, stream>>>(d, t_axis, others);
+        // 64 x 32 tiles when the t axis is short, else 64 x 64; each
+        // block moves 32 KB per batch.
+        const bool short_t = cs.v[t_axis] <= 32;
+        const long long tt = short_t ? 32 : 64, batch = short_t ? 4 : 2;
+        const long long tiles = others * (((long long)cs.v[r - 1] + 63) / 64) * (((long long)cs.v[t_axis] + tt - 1) / tt);
+        // One resident wave of persistent blocks.
+        static int resident[2] = {0, 0};
+        if (!resident[short_t]) {
+          int n = 0;
+          if (short_t) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, copy_transpose_pairs<32, 4>, 256, 0);
+          else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, copy_transpose_pairs<64, 2>, 256, 0);
+          resident[short_t] = std::max(1, n);
+        }
+        unsigned grid = unsigned(std::max(1LL, std::min<long long>((tiles + batch - 1) / batch,
+                                                                   (long long)sm_count() * resident[short_t])));
+        if (short_t) copy_transpose_pairs<32, 4><<<grid, 256, 0, stream>>>(d, t_axis, others);
+        else copy_transpose_pairs<64, 2><<<grid, 256, 0, stream>>>(d, t_axis, others);
         return check_launch("strided copy (transpose pairs)");
       }
       int st = elem == 2 ? launch_transpose<2>(d, t_axis, stream)
@@ -268,23 +423,50 @@ int copy_region(size_t elem, uint32_t rank, const size_t *shape, const void *src
     }
   }
 
-  int w = largest_unit(elem, cs, cst, s, t);
-  size_t per = size_t(w) / elem;
-  for (uint32_t a = 0; a < r; ++a) {
-    bool inner = a + 1 == r;
-    d.shape[a] = (long long)(inner ? cs.v[a] / per : cs.v[a]);
-    d.stride[0][a] = (long long)(inner ? cst[0].v[a] : cst[0].v[a] / per);
-    d.stride[1][a] = (long long)(inner ? cst[1].v[a] : cst[1].v[a] / per);
+  int w = units_desc(elem, cs, cst, s, t, d);
+  if (plan) {
+    plan->width = w;
+    plan->desc = d;
+    return TC_OK;
   }
-  if (per > 1) {  // contiguous inner run counted in units
-    d.stride[0][r - 1] = 1;
-    d.stride[1][r - 1] = 1;
-  }
-  d.count = (long long)(element_count(r, cs.v) / per);
   return launch_width(w, d, stream);
 }
 
 bool valid_width(size_t elem) { return elem == 1 || elem == 2 || elem == 4 || elem == 8 || elem == 16; }
+
+// True when every region writes a box of one common target layout and no
+// two boxes meet: the same strides, strictly nested (each divides the one
+// before), and each region's offset decomposed into coordinates with its
+// shape inside every axis's extent.  A concatenation's regions pass.
+bool disjoint_boxes(const tc_region *regions, size_t n) {
+  const uint32_t rank = regions[0].rank;
+  const size_t *st = regions[0].to_strides;
+  if (rank == 0) return false;
+  for (uint32_t a = 0; a < rank; ++a)
+    if (st[a] == 0 || (a && (st[a - 1] <= st[a] || st[a - 1] % st[a]))) return false;
+  size_t lo[64][TC_MAX_RANK], hi[64][TC_MAX_RANK];
+  for (size_t i = 0; i < n; ++i) {
+    const tc_region &r = regions[i];
+    if (r.rank != rank) return false;
+    for (uint32_t a = 0; a < rank; ++a)
+      if (r.to_strides[a] != st[a]) return false;
+    size_t off = r.to_offset;
+    for (uint32_t a = 0; a < rank; ++a) {
+      const size_t c = a ? (off % st[a - 1]) / st[a] : off / st[0];
+      if (a && c + r.shape[a] > st[a - 1] / st[a]) return false;  // the box would wrap
+      lo[i][a] = c;
+      hi[i][a] = c + r.shape[a];
+    }
+    if (off % st[rank - 1]) return false;
+  }
+  for (size_t i = 0; i < n; ++i)
+    for (size_t j = i + 1; j < n; ++j) {
+      bool apart = false;
+      for (uint32_t a = 0; a < rank && !apart; ++a) apart = hi[i][a] <= lo[j][a] || hi[j][a] <= lo[i][a];
+      if (!apart) return false;
+    }
+  return true;
+}
 
 }  // namespace
 }  // namespace tc
@@ -328,15 +510,54 @@ int tc_assemble(size_t elem, void *dst, size_t len, const tc_region *regions, si
       return st;
     if (int st = check_layout("assemble target", len, r.rank, r.shape, r.to_offset, r.to_strides)) return st;
   }
+  // Regions that copy as plain units of one width go out together, up to
+  // MAX_BATCH per launch, when their targets are provably disjoint; any
+  // other region, and every region when they may overlap, launches on its
+  // own in order, so a later region wins where two write one element, as
+  // the Host's sequential writes do (backend.rs:303-323).
+  const bool batch = n > 1 && n <= 64 && disjoint_boxes(regions, n);
+  MultiDesc m{};
+  int width = 0;
+  auto flush = [&]() -> int {
+    if (m.n == 0) return TC_OK;
+    int st = TC_OK;
+    if (m.n == 1) {
+      st = launch_width(width, m.r[0], as_stream(stream));
+    } else {
+      const long long total = m.start[m.n];
+      unsigned grid = grid_for(size_t(total), 256, 16);
+      switch (width) {
+#define TC_MULTI(W)                                                                                      \
+  case W:                                                                                                \
+    if (total < (1LL << 31)) copy_units_multi<W, int><<<grid, 256, 0, as_stream(stream)>>>(m);          \
+    else copy_units_multi<W, long long><<<grid, 256, 0, as_stream(stream)>>>(m);                        \
+    st = check_launch("assemble");                                                                       \
+    break;
+        TC_MULTI(1) TC_MULTI(2) TC_MULTI(4) TC_MULTI(8) TC_MULTI(16)
+#undef TC_MULTI
+        default: st = fail(TC_EINVAL, "assemble: unit width %d", width);
+      }
+    }
+    m.n = 0;
+    return st;
+  };
   for (size_t i = 0; i < n; ++i) {
     const tc_region &r = regions[i];
     if (element_count(r.rank, r.shape) == 0) continue;
     if (!r.source || !dst) return fail(TC_EINVAL, "assemble: null pointer");
+    UnitPlan plan{};
     if (int st = copy_region(elem, r.rank, r.shape, r.source, r.from_offset, r.from_strides, dst, r.to_offset,
-                             r.to_strides, as_stream(stream)))
+                             r.to_strides, as_stream(stream), batch ? &plan : nullptr))
       return st;
+    if (!plan.width) continue;  // launched already
+    if (m.n == MAX_BATCH || (m.n && plan.width != width))
+      if (int st = flush()) return st;
+    width = plan.width;
+    m.r[m.n] = plan.desc;
+    m.start[m.n + 1] = m.start[m.n] + plan.desc.count;
+    m.n++;
   }
-  return TC_OK;
+  return flush();
 }
 
 }  // extern "C"

@@ -15,4 +15,19 @@ int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t col
 int gemm_tc_run_peers(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
                       const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers,
                       cudaStream_t stream);
+// What a dense layer's epilogue does to the rounded product P, in this
+// order (all optional, none with accumulate or peers):
+//   share_of: P = round(P * MaxShare(share_of[row, col], 0)), the ReLU's
+//             backward rule (share_of laid out as C)
+//   bias:     C = round(P + bias[row])
+//   relu_out: relu_out = max(C, 0)
+struct Epilogue {
+  const void *bias = nullptr;
+  void *relu_out = nullptr;
+  const void *share_of = nullptr;
+};
+// The product with an epilogue: TC_ENOTSUP as gemm_tc_run.
+int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
+                     const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers, const Epilogue &e,
+                     cudaStream_t stream);
 }  // namespace tc

@@ -148,6 +148,13 @@ struct Params {
   // into the epilogue.
   int n_peers;
   void *peer_c[MAX_PEERS];
+  // Epilogue of a dense layer, in this order on the rounded product P:
+  // P = round(P * MaxShare(share_of[row, col], 0)) (the ReLU's backward
+  // rule), C = round(P + bias[row]), relu_out = max(C, 0); each rounded as
+  // the separate operations round.
+  const void *bias;
+  void *relu_out;
+  const void *share_of;
 };
 
 // Tile t of the persistent sequence -> (m block, n block), grouped along M
@@ -313,6 +320,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int n0 = nb * BN;
       const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
       uint16_t *crow = static_cast<uint16_t *>(p.c) + size_t(row) * size_t(p.N);
+      uint16_t *hrow = static_cast<uint16_t *>(p.relu_out) + size_t(row) * size_t(p.N);
+      float bias_row = 0.0f;
+      if (p.bias && row < p.M) {
+        const uint16_t braw = static_cast<const uint16_t *>(p.bias)[row];
+        bias_row = p.elem_is_bf16 ? BF16T::load(braw) : F16T::load(braw);
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -346,6 +359,56 @@ __global__ void __launch_bounds__(THREADS, 1)
                   v[j] = __fadd_rn(p.elem_is_bf16 ? BF16T::load(o) : F16T::load(o), v[j]);
                 }
               }
+            }
+          }
+          if (p.share_of) {
+            // The ReLU's backward rule: round(round(P) * MaxShare(A, 0)).
+            const uint16_t *arow = static_cast<const uint16_t *>(p.share_of) + size_t(row) * size_t(p.N) + col0;
+            uint16_t araw[32];
+            if (whole) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4 *>(araw + 8 * j) = *reinterpret_cast<const uint4 *>(arow + 8 * j);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) araw[j] = col0 + j < p.N ? arow[j] : uint16_t(0);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float z = p.elem_is_bf16 ? BF16T::load(BF16T::store(v[j])) : F16T::load(F16T::store(v[j]));
+              const float a = p.elem_is_bf16 ? BF16T::load(araw[j]) : F16T::load(araw[j]);
+              v[j] = __fmul_rn(z, a > 0.0f ? 1.0f : (a < 0.0f ? 0.0f : 0.5f));
+            }
+          }
+          if (p.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float z = p.elem_is_bf16 ? BF16T::load(BF16T::store(v[j])) : F16T::load(F16T::store(v[j]));
+              v[j] = __fadd_rn(z, bias_row);
+            }
+          }
+          if (p.relu_out) {
+            // max(round(a), 0) is exact in the element type.
+            if (whole) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint32_t w[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const float a = v[8 * j + 2 * h], b = v[8 * j + 2 * h + 1];
+                  const float ra = p.elem_is_bf16 ? BF16T::load(BF16T::store(a)) : F16T::load(F16T::store(a));
+                  const float rb = p.elem_is_bf16 ? BF16T::load(BF16T::store(b)) : F16T::load(F16T::store(b));
+                  w[h] = p.elem_is_bf16 ? pack2_bf16(fmaxf(ra, 0.0f), fmaxf(rb, 0.0f))
+                                        : pack2_f16(fmaxf(ra, 0.0f), fmaxf(rb, 0.0f));
+                }
+                *reinterpret_cast<uint4 *>(hrow + col0 + 8 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) {
+                  const float ra = p.elem_is_bf16 ? BF16T::load(BF16T::store(v[j])) : F16T::load(F16T::store(v[j]));
+                  hrow[col0 + j] = p.elem_is_bf16 ? BF16T::store(fmaxf(ra, 0.0f)) : F16T::store(fmaxf(ra, 0.0f));
+                }
             }
           }
           const size_t at = size_t(row) * size_t(p.N) + size_t(col0);
@@ -452,7 +515,16 @@ int gemm_tc_run(int dtype, int transposed, size_t rows, size_t inner, size_t col
 int gemm_tc_run_peers(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
                       const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers,
                       cudaStream_t stream) {
+  return gemm_tc_run_full(dtype, transposed, rows, inner, cols, a, b, c, accumulate, peer_c, n_peers, Epilogue{},
+                          stream);
+}
+
+int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
+                     const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers, const Epilogue &e,
+                     cudaStream_t stream) {
   if (n_peers < 0 || n_peers > MAX_PEERS) return fail(TC_EINVAL, "gemm: %d peers, at most %d", n_peers, MAX_PEERS);
+  if ((e.bias || e.relu_out || e.share_of) && (accumulate || n_peers))
+    return fail(TC_EINVAL, "gemm: an epilogue neither accumulates nor stores to peers");
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ENOTSUP;
   if (inner < 16 || rows > 0x7fffffffu || cols > 0x7fffffffu || inner > 0x7fffffffu) return TC_ENOTSUP;
   const bool a_mn = transposed == TC_TRANS_LEFT;   // A stored [K, M]
@@ -471,6 +543,11 @@ int gemm_tc_run_peers(int dtype, int transposed, size_t rows, size_t inner, size
   p.c = c;
   p.elem_is_bf16 = bf16;
   p.vec_store = (uintptr_t(c) & 15u) == 0 && (cols * 2) % 16 == 0;
+  p.bias = e.bias;
+  p.relu_out = e.relu_out;
+  p.share_of = e.share_of;
+  if (e.relu_out && (uintptr_t(e.relu_out) & 15u)) p.vec_store = 0;
+  if (e.share_of && (uintptr_t(e.share_of) & 15u)) p.vec_store = 0;
   p.n_peers = n_peers;
   for (int i = 0; i < MAX_PEERS; ++i) {
     p.peer_c[i] = i < n_peers ? peer_c[i] : nullptr;

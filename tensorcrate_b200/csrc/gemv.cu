@@ -144,6 +144,23 @@ __global__ void __launch_bounds__(256) outer_rows(const typename T::S *a, const 
   }
 }
 
+// A dense layer's epilogue as a pass of its own, over a product already
+// rounded to T: c = round(c * MaxShare(share_of, 0)); c = round(c +
+// bias[row]); relu_out = max(c, 0).
+template <class T>
+__global__ void __launch_bounds__(256) epilogue_rows(typename T::S *c, const typename T::S *share_of,
+                                                     const typename T::S *bias, typename T::S *relu_out,
+                                                     long long rows, long long cols) {
+  const long long total = rows * cols;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    float v = T::load(c[i]);
+    if (share_of) v = T::load(T::store(__fmul_rn(v, compare_value(TC_MAX_SHARE, T::load(share_of[i]), 0.0f))));
+    if (bias) v = T::load(T::store(__fadd_rn(v, T::load(bias[i / cols]))));
+    if (share_of || bias) c[i] = T::store(v);
+    if (relu_out) relu_out[i] = T::store(fmaxf(v, 0.0f));
+  }
+}
+
 }  // namespace
 }  // namespace tc
 
@@ -275,6 +292,37 @@ int tc_vecmat_noalloc(int dtype, size_t rows, size_t cols, const void *x, const 
       vecmat_finish<T><<<unsigned((cols + 31) / 32), dim3(32, 8), 0, s>>>(partial, int(shares), (long long)cols,
                                                                          static_cast<S *>(y));
     return check_launch("vecmat_noalloc");
+  });
+}
+
+int tc_matmul_epilogue(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
+                       const void *b, const void *share_of, const void *bias, void *c, void *relu_out,
+                       void *stream) {
+  if (transposed < TC_TRANS_NONE || transposed > TC_TRANS_RIGHT)
+    return fail(TC_EINVAL, "matmul_epilogue: bad Transposed %d", transposed);
+  if (dtype != TC_F32 && dtype != TC_F16 && dtype != TC_BF16)
+    return fail(TC_EINVAL, "matmul_epilogue: element type %d", dtype);
+  if (rows == 0 || cols == 0) return TC_OK;
+  if (!c) return fail(TC_EINVAL, "matmul_epilogue: null output");
+  cudaStream_t s = as_stream(stream);
+  if (dtype != TC_F32 && inner >= 16 && a && b) {
+    Epilogue e;
+    e.share_of = share_of;
+    e.bias = bias;
+    e.relu_out = relu_out;
+    int st = gemm_tc_run_full(dtype, transposed, rows, inner, cols, a, b, c, false, nullptr, 0, e, s);
+    if (st != TC_ENOTSUP) return st;
+  }
+  // Otherwise the product, then the epilogue as its own pass (same bits).
+  if (int st = tc_matmul(dtype, transposed, rows, inner, cols, a, b, c, 0, stream)) return st;
+  if (!share_of && !bias && !relu_out) return TC_OK;
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    epilogue_rows<T><<<grid_for(rows * cols, 256, 8), 256, 0, s>>>(
+        static_cast<S *>(c), static_cast<const S *>(share_of), static_cast<const S *>(bias),
+        static_cast<S *>(relu_out), (long long)rows, (long long)cols);
+    return check_launch("matmul_epilogue");
   });
 }
 

@@ -45,6 +45,26 @@ __global__ void fill_kernel(typename T::S *out, size_t n, typename T::S value) {
     out[i] = value;
 }
 
+// The loss and its first backward steps, one pass over the outputs:
+//   R = P - Y, S = R * R                       (binary Sub, Mul)
+//   S̄ = filled(factor); R̄ = S̄ * R + S̄ * R      (Mul's rule, both operands R)
+//   Ȳ = R̄ * -1                                 (Sub's rule for the right side)
+// each operation rounded to T as the separate kernels round it.  S is
+// written only when the loss is wanted, Ȳ only when not pruned.
+template <class T>
+__global__ void __launch_bounds__(256) mse_backward(const typename T::S *pred, const typename T::S *y, float factor,
+                                                   typename T::S *s_out, typename T::S *rbar, typename T::S *ybar,
+                                                   size_t n) {
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const float r = T::load(T::store(__fsub_rn(T::load(pred[i]), T::load(y[i]))));
+    if (s_out) s_out[i] = T::store(__fmul_rn(r, r));
+    const float t = T::load(T::store(__fmul_rn(factor, r)));
+    const typename T::S rb = T::store(__fadd_rn(t, t));
+    rbar[i] = rb;
+    if (ybar) ybar[i] = T::store(__fmul_rn(T::load(rb), -1.0f));
+  }
+}
+
 // Round a host value to the element type, as Real::from_f64 does (one
 // rounding from f64; round-to-odd into f32 first keeps it single).
 float round_to(int dtype, double d) {
@@ -91,8 +111,8 @@ struct tc_mlp {
   float rate = 0, beta1 = 0, beta2 = 0, eps = 0;  // element-type values
   uint32_t steps = 0;
   std::vector<Buf> W, b, gW, gb, mW, vW, mb, vb;
-  std::vector<Buf> Z, O, A, H;
-  Buf ones, R, S, T1, T2, Rbar, Ybar, Xbar, share, abar, inbar, onesbar, ovec, loss_sum;
+  std::vector<Buf> A, H;
+  Buf ones, S, Rbar, Ybar, Xbar, abar, inbar, onesbar, ovec, loss_sum;
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> grad_ready;
   cudaEvent_t reduced = nullptr;
@@ -143,18 +163,18 @@ int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t bat
     const size_t in = m->dims[l], outd = m->dims[l + 1];
     m->W.emplace_back(); m->b.emplace_back(); m->gW.emplace_back(); m->gb.emplace_back();
     m->mW.emplace_back(); m->vW.emplace_back(); m->mb.emplace_back(); m->vb.emplace_back();
-    m->Z.emplace_back(); m->O.emplace_back(); m->A.emplace_back(); m->H.emplace_back();
+    m->A.emplace_back(); m->H.emplace_back();
     need(m->W[l], outd * in); need(m->gW[l], outd * in); need(m->mW[l], outd * in); need(m->vW[l], outd * in);
     need(m->b[l], outd); need(m->gb[l], outd); need(m->mb[l], outd); need(m->vb[l], outd);
-    need(m->Z[l], outd * B); need(m->O[l], outd * B); need(m->A[l], outd * B);
+    need(m->A[l], outd * B);
     if (l + 1 < m->layers) need(m->H[l], outd * B);
   }
   size_t widest = 0;
   for (size_t d : m->dims) widest = std::max(widest, d);
   const size_t last = m->dims[m->layers];
-  need(m->ones, B); need(m->R, last * B); need(m->S, last * B); need(m->T1, last * B); need(m->T2, last * B);
+  need(m->ones, B); need(m->S, last * B);
   need(m->Rbar, last * B); need(m->Ybar, last * B); need(m->Xbar, m->dims[0] * B);
-  need(m->share, widest * B); need(m->abar, widest * B); need(m->inbar, widest * B);
+  need(m->abar, widest * B); need(m->inbar, widest * B);
   need(m->onesbar, B); need(m->ovec, B); need(m->loss_sum, 1);
   if (st) {
     tc_mlp_destroy(m);
@@ -188,9 +208,9 @@ int tc_mlp_destroy(tc_mlp *m) {
     if (b.p) tc_free(b.p);
     b.p = nullptr;
   };
-  for (auto *v : {&m->W, &m->b, &m->gW, &m->gb, &m->mW, &m->vW, &m->mb, &m->vb, &m->Z, &m->O, &m->A, &m->H})
+  for (auto *v : {&m->W, &m->b, &m->gW, &m->gb, &m->mW, &m->vW, &m->mb, &m->vb, &m->A, &m->H})
     for (auto &b : *v) drop(b);
-  for (Buf *b : {&m->ones, &m->R, &m->S, &m->T1, &m->T2, &m->Rbar, &m->Ybar, &m->Xbar, &m->share, &m->abar,
+  for (Buf *b : {&m->ones, &m->S, &m->Rbar, &m->Ybar, &m->Xbar, &m->abar,
                  &m->inbar, &m->onesbar, &m->ovec, &m->loss_sum})
     drop(*b);
   for (auto ev : m->grad_ready)
@@ -251,34 +271,30 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   for (int l = 0; l < L; ++l) {
     const size_t in = m->dims[l], outd = m->dims[l + 1];
     const void *input = l == 0 ? x : m->H[l - 1].p;
-    TRY(tc_matmul(d, TC_TRANS_NONE, outd, in, B, m->W[l].p, input, m->Z[l].p, 0, st));
-    TRY(tc_matmul(d, TC_TRANS_NONE, outd, 1, B, m->b[l].p, m->ones.p, m->O[l].p, 0, st));  // b ⊗ ones
-    TRY(tc_elementwise(d, TC_ADD, m->Z[l].p, m->O[l].p, m->A[l].p, outd * B, st));
-    if (l + 1 < L) TRY(tc_compare_scalar(d, TC_MAX, m->A[l].p, 0.0, 0, m->H[l].p, outd * B, st));
+    // Z = W·IN, O = b ⊗ ones, A = Z + O, H = max(A, 0): one product whose
+    // epilogue adds the bias row and applies the ReLU, rounding as the
+    // separate operations do (b ⊗ ones is b exactly).
+    TRY(tc_matmul_epilogue(d, TC_TRANS_NONE, outd, in, B, m->W[l].p, input, nullptr, m->b[l].p, m->A[l].p,
+                           l + 1 < L ? m->H[l].p : nullptr, st));
   }
   const size_t last = m->dims[L];
-  TRY(tc_elementwise(d, TC_SUB, m->A[L - 1].p, y, m->R.p, last * B, st));
-  TRY(tc_elementwise(d, TC_MUL, m->R.p, m->R.p, m->S.p, last * B, st));
   const float factor = round_to(d, 1.0 / (double(last) * double(m->global_batch)));
+  // Loss and the top of the backward pass (frobenius_dot, scale, sum's and
+  // Mul's and Sub's rules) in one pass.
+  TRY(with_real(d, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    mse_backward<T><<<grid_for(last * B, 256), 256, 0, s>>>(
+        static_cast<const S *>(m->A[L - 1].p), static_cast<const S *>(y), factor,
+        loss_out ? static_cast<S *>(m->S.p) : nullptr, static_cast<S *>(m->Rbar.p),
+        m->prune ? nullptr : static_cast<S *>(m->Ybar.p), last * B);
+    return check_launch("mlp loss");
+  }));
   if (loss_out) {
     // The lazy scalar, forced: sum of S (f32, rounded once), then `scale`.
     TRY(tc_vector_reduce(d, TC_SUM, m->S.p, last * B, m->loss_sum.p, st));
     TRY(tc_broadcast_scalar(d, TC_MUL, m->loss_sum.p, factor, 0, loss_out, 1, st));
   }
-  // ---- backward ----
-  // sum's rule: S̄ = filled(adjoint), adjoint = 1 · factor (scale's rule).
-  TRY(with_real(d, [&](auto t) {
-    using T = decltype(t);
-    fill_kernel<T><<<grid_for(last * B, 256), 256, 0, s>>>(static_cast<typename T::S *>(m->T2.p), last * B,
-                                                            T::store(factor));
-    return check_launch("mlp fill");
-  }));
-  // S = R * R (binary Mul): left += S̄·right, right += S̄·left.
-  TRY(tc_elementwise(d, TC_MUL, m->T2.p, m->R.p, m->T1.p, last * B, st));
-  TRY(tc_elementwise(d, TC_MUL, m->T2.p, m->R.p, m->S.p, last * B, st));
-  TRY(tc_elementwise(d, TC_ADD, m->T1.p, m->S.p, m->Rbar.p, last * B, st));
-  // R = P - Y: P̄ += R̄ (shared), Ȳ += -R̄.
-  if (!m->prune) TRY(tc_broadcast_scalar(d, TC_MUL, m->Rbar.p, -1.0, 0, m->Ybar.p, last * B, st));
   const void *abar = m->Rbar.p;  // Ā of the top layer = P̄
   for (int l = L - 1; l >= 0; --l) {
     const size_t in = m->dims[l], outd = m->dims[l + 1];
@@ -303,11 +319,12 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
       TRY(tc_allreduce(comm, d, m->gb[l].p, m->gb[l].n, TC_SUM, m->comm_stream));
     }
     if (l > 0) {
-      TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->inbar.p, 0, st));
-      // H = relu(A): Ā += H̄ · MaxShare(A, 0).
-      TRY(tc_compare_scalar(d, TC_MAX_SHARE, m->A[l - 1].p, 0.0, 0, m->share.p, in * B, st));
-      TRY(tc_elementwise(d, TC_MUL, m->inbar.p, m->share.p, m->abar.p, in * B, st));
-      abar = m->abar.p;
+      // H̄ = Wᵀ·Z̄, then H = relu(A): Ā += H̄ · MaxShare(A, 0).  Ā of the
+      // layer below goes to the buffer this layer's Ā does not use.
+      void *next = abar == m->abar.p ? m->inbar.p : m->abar.p;
+      TRY(tc_matmul_epilogue(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->A[l - 1].p, nullptr, next,
+                             nullptr, st));
+      abar = next;
     } else if (!m->prune) {
       TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->Xbar.p, 0, st));
     }
@@ -321,12 +338,12 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   float c1, c2;
   adam_coefficients(*m, m->steps, c1, c2);
   const int resumed = m->steps > 1;
+  std::vector<tc_adam_tensor> params;
   for (int l = 0; l < L; ++l) {
-    TRY(tc_adam(d, m->W[l].n, m->W[l].p, m->gW[l].p, m->mW[l].p, m->vW[l].p, resumed, m->rate, m->beta1, m->beta2,
-                m->eps, c1, c2, st));
-    TRY(tc_adam(d, m->b[l].n, m->b[l].p, m->gb[l].p, m->mb[l].p, m->vb[l].p, resumed, m->rate, m->beta1, m->beta2,
-                m->eps, c1, c2, st));
+    params.push_back({m->W[l].p, m->gW[l].p, m->mW[l].p, m->vW[l].p, m->W[l].n});
+    params.push_back({m->b[l].p, m->gb[l].p, m->mb[l].p, m->vb[l].p, m->b[l].n});
   }
+  TRY(tc_adam_multi(d, params.data(), params.size(), resumed, m->rate, m->beta1, m->beta2, m->eps, c1, c2, st));
 #undef TRY
   return TC_OK;
 }

@@ -168,3 +168,68 @@ def test_config3_permute_slice_split_concat(device, scale):
         assert np.array_equal(p.storage.as_slice(), want)
         sl_host = want.reshape(p.shape)[:, 8:, :, :32, :]
         assert np.array_equal(joined.to_numpy(), sl_host)
+
+
+def _oracle_assemble(elem, length, regions_host):
+    """The Host's assemble (backend.rs:303-323): regions written in order."""
+    import ctypes as C
+    from tensorcrate_b200 import _native as N
+    arr = (N.Region * len(regions_host))()
+    keep = []
+    for reg, (src, shape, fo, fs, to, ts) in zip(arr, regions_host):
+        keep.append(src)
+        reg.source, reg.source_len, reg.rank = src.ctypes.data, src.size, len(shape)
+        for k in range(len(shape)):
+            reg.shape[k], reg.from_strides[k], reg.to_strides[k] = shape[k], fs[k], ts[k]
+        reg.from_offset, reg.to_offset = fo, to
+    out = np.empty(length, keep[0].dtype)
+    O.call("orc_assemble", elem, O.ptr(out), length, C.cast(arr, C.c_void_p), len(regions_host))
+    return out
+
+
+def test_assemble_overlapping_regions_keeps_the_last_write(device):
+    """Regions that overlap in the target are written in order, as the
+    Host's sequential strided writes leave them: the later region wins."""
+    a, b, c = integral(64), integral(64, 100), integral(48, 300)
+    host = [(a, [64], 0, [1], 0, [1]), (b, [8, 8], 0, [8, 1], 16, [8, 1]), (c, [48], 0, [1], 40, [1])]
+    dev = [(cuda.CudaStorage.store(s, "f32"), sh, fo, fs, to, ts) for s, sh, fo, fs, to, ts in host]
+    got = cuda.Cuda.assemble("f32", 96, dev).as_slice()
+    assert np.array_equal(got[:88], _oracle_assemble(4, 96, host)[:88])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+def test_concat_of_many_pieces_in_one_launch(device, dtype):
+    """A concatenation of up to 11 pieces of differing widths (16-byte
+    units, odd lengths that copy element by element, a transposed view):
+    the batched plain copies and the transposes together give the Host's
+    result."""
+    rng = np.random.default_rng(4)
+    widths = [8, 16, 3, 32, 5, 64, 8, 1, 24, 40, 7]
+    pieces, host = [], []
+    for i, w in enumerate(widths):
+        x = O.narrow(integral(6 * w, 50 * i), dtype).reshape(6, w)
+        if i == 3:  # a transposed piece: stored [w, 6], viewed [6, w]
+            stored = np.ascontiguousarray(x.T)
+            pieces.append(cuda.Tensor(cuda.CudaStorage.store(stored.reshape(-1), dtype), [w, 6]).view().permute([1, 0]))
+        else:
+            pieces.append(cuda.Tensor(cuda.CudaStorage.store(x.reshape(-1), dtype), [6, w]).view())
+        host.append(x)
+    got = cuda.Tensor.concat(pieces, 1).to_numpy()
+    want = np.concatenate(host, 1)
+    assert np.array_equal(got.view(np.uint8), want.view(np.uint8))
+    del rng
+
+
+@pytest.mark.parametrize("shape,perm", [([4, 6, 40, 32], [0, 2, 1, 3]), ([3, 130, 32], [1, 2, 0]),
+                                        ([5, 96, 70], [0, 2, 1]), ([2, 64, 128], [0, 2, 1]),
+                                        ([7, 30, 66], [2, 1, 0]), ([9, 2, 14, 22], [3, 0, 2, 1])])
+def test_two_byte_transposes_with_short_and_long_tiles(device, shape, perm):
+    """Permutations whose innermost target axis comes from a strided source
+    axis: 2-byte elements move as pairs through 64 x 32 or 64 x 64 tiles,
+    ragged at the edges and in the last batch of tiles."""
+    n = int(np.prod(shape))
+    x = O.narrow(normal(n, 7), "f16")
+    t = cuda.Tensor(cuda.CudaStorage.store(x, "f16"), shape)
+    got = t.view().permute(perm).contiguous().storage.as_slice()
+    want = np.ascontiguousarray(x.reshape(shape).transpose(perm)).reshape(-1)
+    assert np.array_equal(got, want)

@@ -62,3 +62,42 @@ def test_sgd_matches_bit_for_bit(device, dtype):
     N.call("tc_sgd", N.DTYPES[dtype], n, dp.ptr, dg.ptr, 0.01, None)
     O.call("orc_sgd", O.DTYPES[dtype], n, O.ptr(p), O.ptr(g), 0.01)
     assert same_bits(dp.as_slice(), p, dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_adam_over_many_tensors_in_one_launch(device, dtype):
+    """tc_adam_multi gives every tensor the bits tc_adam gives it alone:
+    18 tensors (two launches), lengths with and without whole 16-byte packs,
+    one tensor not 16-byte aligned, an empty one; a first and a resumed step."""
+    import ctypes as C
+    beta2 = 0.99 if dtype == "bf16" else 0.999
+    lengths = [1, 7, 8, 13, 4096, 4099, 0, 250000, 31, 64, 65, 1000, 3, 16, 17, 8191, 2, 9]
+    code = N.DTYPES[dtype]
+    singles, multi = [], []
+    for i, n in enumerate(lengths):
+        p = O.narrow(normal(max(n, 1) + 1, 100 + i), dtype)
+        shift = 1 if i == 5 else 0  # an operand off the 16-byte grid
+        for group in (singles, multi):
+            d = {k: cuda.CudaStorage.store(p, dtype) for k in ("p",)}
+            d["m"], d["v"] = cuda.CudaStorage.zeros(dtype, n + 1), cuda.CudaStorage.zeros(dtype, n + 1)
+            d["shift"], d["n"] = shift, n
+            group.append(d)
+    eb = 4 if dtype == "f32" else 2
+    for step in (1, 2):
+        coef = O.adam_coefficients(dtype, 1e-3, 0.9, beta2, 1e-8, step)
+        grads = [cuda.CudaStorage.store(O.narrow(normal(max(n, 1) + 1, 300 + 10 * step + i) * 0.1, dtype), dtype)
+                 for i, n in enumerate(lengths)]
+        arr = (N.AdamTensor * len(lengths))()
+        for i, (d, g) in enumerate(zip(multi, grads)):
+            o = d["shift"] * eb
+            arr[i].p, arr[i].g, arr[i].m, arr[i].v, arr[i].n = (d["p"].ptr + o, g.ptr + o, d["m"].ptr + o,
+                                                               d["v"].ptr + o, d["n"])
+        N.call("tc_adam_multi", code, arr, len(lengths), int(step > 1), *coef, None)
+        for d, g in zip(singles, grads):
+            o = d["shift"] * eb
+            N.call("tc_adam", code, d["n"], d["p"].ptr + o, g.ptr + o, d["m"].ptr + o, d["v"].ptr + o,
+                   int(step > 1), *coef, None)
+        for s, mu in zip(singles, multi):
+            for k in ("p", "m", "v"):
+                assert np.array_equal(s[k].as_slice(), mu[k].as_slice()), (s["n"], k)
+    del C

@@ -132,3 +132,38 @@ def test_outer_products(device, dtype, transposed):
                 assert np.max(np.abs(got - want)) <= 2 ** -22 * max(1.0, np.max(np.abs(want)))
             else:
                 assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,k,n", [(7, 5, 3), (130, 96, 72), (256, 320, 512), (4096, 1024, 264), (128, 8, 256)])
+@pytest.mark.parametrize("relu", [True, False])
+def test_matmul_epilogue_matches_the_separate_operations(device, dtype, m, k, n, relu):
+    """tc_matmul_epilogue (Kernels::matmul_epilogue, kernels.rs:1137-1150)
+    for a dense layer's programs: forward A = P + bias[row], H = max(A, 0);
+    backward P * MaxShare(A, 0).  It must give the bits of the separate
+    operations the tape runs: the product (tc_matmul), then each
+    elementwise operation rounded in turn."""
+    a = O.narrow(uniform((m, k), m + k), dtype)
+    b = O.narrow(uniform((k, n), n + 1), dtype)
+    bias = O.narrow(uniform(m, 9), dtype)
+    share_src = O.narrow(np.round(uniform((m, n), 4) * 2) / 2, dtype)  # negative, zero and positive entries
+    da, db, dbias, dshare = (cuda.CudaStorage.store(x, dtype) for x in (a, b, bias, share_src))
+    product = cuda.Cuda.matmul(da, db, m, k, n).as_slice()
+    pw = O.widen(product, dtype).reshape(m, n)
+    want_a = O.narrow(pw + O.widen(bias, dtype)[:, None], dtype).reshape(-1)
+    want_h = O.narrow(np.maximum(O.widen(want_a, dtype), np.float32(0)), dtype)
+    sw = O.widen(share_src, dtype).reshape(m, n)
+    share = np.where(sw > 0, 1.0, np.where(sw < 0, 0.0, 0.5)).astype(np.float32)
+    want_s = O.narrow(pw * share, dtype).reshape(-1)
+    code = N.DTYPES[dtype]
+    got = cuda.CudaStorage(dtype, m * n)
+    got_h = cuda.CudaStorage(dtype, m * n) if relu else None
+    N.call("tc_matmul_epilogue", code, N.TRANS_NONE, m, k, n, da.ptr, db.ptr, None, dbias.ptr, got.ptr,
+           got_h.ptr if relu else None, None)
+    assert np.array_equal(got.as_slice(), want_a)
+    if relu:
+        assert np.array_equal(got_h.as_slice(), want_h)
+    N.call("tc_matmul_epilogue", code, N.TRANS_NONE, m, k, n, da.ptr, db.ptr, dshare.ptr, None, got.ptr, None, None)
+    assert np.array_equal(got.as_slice(), want_s)
+    N.call("tc_matmul_epilogue", code, N.TRANS_NONE, m, k, n, da.ptr, db.ptr, None, None, got.ptr, None, None)
+    assert np.array_equal(got.as_slice(), product)
