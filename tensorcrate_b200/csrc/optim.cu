@@ -43,47 +43,75 @@ __device__ __forceinline__ void adam_one(float g, float &p, float &m, float &v, 
   v = second;
 }
 
-// Two elements at a time: each rounding to a 16-bit type is one packed
-// conversion (cvt.rn.bf16x2.f32 / cvt.rn.f16x2.f32) of the pair, which
-// rounds each half to nearest even exactly as the single conversion does.
-template <class T> __device__ __forceinline__ float2 rnd2(float x, float y) {
-  if (T::code == TC_BF16) {
-    const uint32_t u = pack2_bf16(x, y);
+// Two 16-bit elements at a time, in packed bf16x2 / f16x2 arithmetic.  A
+// packed multiply, add or subtract (the _rn forms, which the compiler may
+// not contract into a fused multiply-add) rounds the exact result once to
+// the element type; the program's f32 operation followed by a rounding to the
+// element type gives the same value, because the exact product or sum of two
+// such values either fits in f32 or lies too far from a tie of the element
+// type for the f32 rounding to move it there (the operands' exponents are
+// then more than 15 apart, 12 for f16).  The one exception is a bf16
+// product below 2^-126, which f32 itself rounds as a subnormal.  Square root
+// and division have no packed form: they run in f32 and round once, as the
+// program does.
+template <class T> struct Half2;
+template <> struct Half2<BF16T> {
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) { return op(a, b, 0); }
+  __device__ __forceinline__ static uint32_t add(uint32_t a, uint32_t b) { return op(a, b, 1); }
+  __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) { return op(a, b, 2); }
+  __device__ __forceinline__ static uint32_t op(uint32_t a, uint32_t b, int which) {
+    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162 *>(&a), y = *reinterpret_cast<__nv_bfloat162 *>(&b);
+    __nv_bfloat162 r = which == 0 ? __hmul2_rn(x, y) : which == 1 ? __hadd2_rn(x, y) : __hsub2_rn(x, y);
+    return *reinterpret_cast<uint32_t *>(&r);
+  }
+  __device__ __forceinline__ static float2 widen(uint32_t u) {
     return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
   }
-  if (T::code == TC_F16) {
-    const uint32_t u = pack2_f16(x, y);
-    __half2 h = *reinterpret_cast<const __half2 *>(&u);
-    return __half22float2(h);
+  __device__ __forceinline__ static uint32_t narrow(float2 f) { return pack2_bf16(f.x, f.y); }
+};
+template <> struct Half2<F16T> {
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) { return op(a, b, 0); }
+  __device__ __forceinline__ static uint32_t add(uint32_t a, uint32_t b) { return op(a, b, 1); }
+  __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) { return op(a, b, 2); }
+  __device__ __forceinline__ static uint32_t op(uint32_t a, uint32_t b, int which) {
+    __half2 x = *reinterpret_cast<__half2 *>(&a), y = *reinterpret_cast<__half2 *>(&b);
+    __half2 r = which == 0 ? __hmul2_rn(x, y) : which == 1 ? __hadd2_rn(x, y) : __hsub2_rn(x, y);
+    return *reinterpret_cast<uint32_t *>(&r);
   }
-  return make_float2(x, y);
-}
+  __device__ __forceinline__ static float2 widen(uint32_t u) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+  }
+  __device__ __forceinline__ static uint32_t narrow(float2 f) { return pack2_f16(f.x, f.y); }
+};
 
-#define TC_PAIR(expr_x, expr_y) rnd2<T>((expr_x), (expr_y))
+// The coefficients as packed pairs of the element type.
+struct AdamCoef2 {
+  uint32_t rate, beta1, beta2, eps, c1, c2, first_share, second_share;
+};
 
 template <class T>
-__device__ __forceinline__ void adam_pair(float2 g, float2 &p, float2 &m, float2 &v, bool resumed, const AdamCoef &k) {
-  const float2 fresh_first = TC_PAIR(__fmul_rn(g.x, k.first_share), __fmul_rn(g.y, k.first_share));
-  const float2 squared = TC_PAIR(__fmul_rn(g.x, g.x), __fmul_rn(g.y, g.y));
-  const float2 fresh_second = TC_PAIR(__fmul_rn(squared.x, k.second_share), __fmul_rn(squared.y, k.second_share));
-  float2 first = fresh_first, second = fresh_second;
+__device__ __forceinline__ void adam_pair(uint32_t g, uint32_t &p, uint32_t &m, uint32_t &v, bool resumed,
+                                          const AdamCoef2 &k) {
+  using H = Half2<T>;
+  const uint32_t fresh_first = H::mul(g, k.first_share);
+  const uint32_t squared = H::mul(g, g);
+  const uint32_t fresh_second = H::mul(squared, k.second_share);
+  uint32_t first = fresh_first, second = fresh_second;
   if (resumed) {
-    const float2 mb = TC_PAIR(__fmul_rn(m.x, k.beta1), __fmul_rn(m.y, k.beta1));
-    first = TC_PAIR(__fadd_rn(mb.x, fresh_first.x), __fadd_rn(mb.y, fresh_first.y));
-    const float2 vb = TC_PAIR(__fmul_rn(v.x, k.beta2), __fmul_rn(v.y, k.beta2));
-    second = TC_PAIR(__fadd_rn(vb.x, fresh_second.x), __fadd_rn(vb.y, fresh_second.y));
+    first = H::add(H::mul(m, k.beta1), fresh_first);
+    second = H::add(H::mul(v, k.beta2), fresh_second);
   }
-  const float2 cf = TC_PAIR(__fmul_rn(first.x, k.c1), __fmul_rn(first.y, k.c1));
-  const float2 cs = TC_PAIR(__fmul_rn(second.x, k.c2), __fmul_rn(second.y, k.c2));
-  const float2 root = TC_PAIR(__fsqrt_rn(cs.x), __fsqrt_rn(cs.y));
-  const float2 den = TC_PAIR(__fadd_rn(root.x, k.eps), __fadd_rn(root.y, k.eps));
-  const float2 q = TC_PAIR(__fdiv_rn(cf.x, den.x), __fdiv_rn(cf.y, den.y));
-  const float2 step = TC_PAIR(__fmul_rn(q.x, k.rate), __fmul_rn(q.y, k.rate));
-  p = TC_PAIR(__fsub_rn(p.x, step.x), __fsub_rn(p.y, step.y));
+  const uint32_t cf = H::mul(first, k.c1);
+  const float2 cs = H::widen(H::mul(second, k.c2));
+  const uint32_t root = H::narrow(make_float2(__fsqrt_rn(cs.x), __fsqrt_rn(cs.y)));
+  const float2 den = H::widen(H::add(root, k.eps));
+  const float2 num = H::widen(cf);
+  const uint32_t q = H::narrow(make_float2(__fdiv_rn(num.x, den.x), __fdiv_rn(num.y, den.y)));
+  const uint32_t step = H::mul(q, k.rate);
+  p = H::sub(p, step);
   m = first;
   v = second;
 }
-#undef TC_PAIR
 
 // Several parameters in one launch (Adam::update runs the same program,
 // with the same coefficients, on each parameter of a step).
@@ -100,7 +128,8 @@ struct AdamSet {
 // Each thread walks the flat pack space with a grid stride, loading the
 // next pack's four operands before it computes the current one.
 template <class T>
-__global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamSet set, bool resumed, AdamCoef k) {
+__global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamSet set, bool resumed, AdamCoef k,
+                                                   AdamCoef2 k2) {
   using S = typename T::S;
   constexpr int N = 16 / int(sizeof(S));
   union Pk { uint4 raw; S e[N]; };
@@ -137,18 +166,26 @@ __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamS
       locate(qn, tn, atn);
       load(tn, atn, pn, gn, mn, vn);
     }
+    if constexpr (sizeof(S) == 2) {
+      uint32_t *P2 = reinterpret_cast<uint32_t *>(&pp.raw), *M2 = reinterpret_cast<uint32_t *>(&mm.raw);
+      uint32_t *V2 = reinterpret_cast<uint32_t *>(&vv.raw);
+      const uint32_t *G2 = reinterpret_cast<const uint32_t *>(&gg.raw);
 #pragma unroll
-    for (int j = 0; j < N; j += 2) {
-      float2 P = make_float2(T::load(pp.e[j]), T::load(pp.e[j + 1]));
-      float2 M = resumed ? make_float2(T::load(mm.e[j]), T::load(mm.e[j + 1])) : make_float2(0.0f, 0.0f);
-      float2 V = resumed ? make_float2(T::load(vv.e[j]), T::load(vv.e[j + 1])) : make_float2(0.0f, 0.0f);
-      adam_pair<T>(make_float2(T::load(gg.e[j]), T::load(gg.e[j + 1])), P, M, V, resumed, k);
-      pp.e[j] = T::store(P.x);
-      pp.e[j + 1] = T::store(P.y);
-      mm.e[j] = T::store(M.x);
-      mm.e[j + 1] = T::store(M.y);
-      vv.e[j] = T::store(V.x);
-      vv.e[j + 1] = T::store(V.y);
+      for (int j = 0; j < 4; ++j) {
+        uint32_t m2 = resumed ? M2[j] : 0u, v2 = resumed ? V2[j] : 0u;
+        adam_pair<T>(G2[j], P2[j], m2, v2, resumed, k2);
+        M2[j] = m2;
+        V2[j] = v2;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float P = T::load(pp.e[j]), M = resumed ? T::load(mm.e[j]) : 0.0f, V = resumed ? T::load(vv.e[j]) : 0.0f;
+        adam_one<T>(T::load(gg.e[j]), P, M, V, resumed, k);
+        pp.e[j] = T::store(P);
+        mm.e[j] = T::store(M);
+        vv.e[j] = T::store(V);
+      }
     }
     *reinterpret_cast<uint4 *>(static_cast<S *>(set.p[t]) + at) = pp.raw;
     *reinterpret_cast<uint4 *>(static_cast<S *>(set.m[t]) + at) = mm.raw;
@@ -220,6 +257,14 @@ int tc_adam_multi(int dtype, const tc_adam_tensor *tensors, size_t count, int re
     };
     k.first_share = round_host(1.0f - k.beta1);
     k.second_share = round_host(1.0f - k.beta2);
+    // The same values as packed pairs (each already a value of T).
+    auto pair = [](float x) -> uint32_t {
+      if (T::code == TC_F32) return 0u;
+      const uint32_t h = T::code == TC_BF16 ? f32_to_bf16_bits(x) : f32_to_f16_bits(x);
+      return h | (h << 16);
+    };
+    const AdamCoef2 k2{pair(k.rate), pair(k.beta1), pair(k.beta2), pair(k.eps), pair(k.c1), pair(k.c2),
+                       pair(k.first_share), pair(k.second_share)};
     static int resident = 0;
     if (!resident) {
       int n = 0;
@@ -248,7 +293,7 @@ int tc_adam_multi(int dtype, const tc_adam_tensor *tensors, size_t count, int re
       const long long work = std::max(set.start[set.count], (elems + (long long)N - 1) / (long long)N);
       const unsigned grid = unsigned(std::max(1LL, std::min<long long>((work + 255) / 256,
                                                                        (long long)sm_count() * resident)));
-      adam_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(set, resumed != 0, k);
+      adam_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(set, resumed != 0, k, k2);
       if (int st = check_launch("adam")) return st;
     }
     return TC_OK;
