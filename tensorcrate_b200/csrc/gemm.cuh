@@ -30,4 +30,11 @@ struct Epilogue {
 int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a,
                      const void *b, void *c, bool accumulate, void *const *peer_c, int n_peers, const Epilogue &e,
                      cudaStream_t stream);
+// f32 products on the tensor cores as three TF32 passes: each operand split
+// into a TF32 head and a TF32 tail (hi + lo), and C = hi.hi + hi.lo + lo.hi
+// accumulated in f32, which leaves a relative error near 2^-21 per product.
+// The halves go through the per-device scratch buffer.  TC_ENOTSUP beyond
+// 32-bit tile coordinates.
+int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b, void *c,
+                  bool accumulate, cudaStream_t stream);
 }  // namespace tc

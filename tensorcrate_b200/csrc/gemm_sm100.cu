@@ -118,6 +118,11 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, ui
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
       ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -155,6 +160,10 @@ struct Params {
   const void *bias;
   void *relu_out;
   const void *share_of;
+  // f32 products (TF32 kernel): each operand is stored [rows x 2*kp] as
+  // [hi | lo] halves; the K loop runs over three kp-long segments
+  // (hi.hi, hi.lo, lo.hi) and p.K = 3 * kp.
+  int kp;
 };
 
 // Tile t of the persistent sequence -> (m block, n block), grouped along M
@@ -170,10 +179,11 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb
   nb = r / gm;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool TF32 = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const Params p) {
-  constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int KE = TF32 ? 32 : BK;  // elements in one 128-byte row of a stage
+  constexpr uint32_t A_BYTES = BM * 128, B_BYTES = BN * 128, STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -189,7 +199,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int k_blocks = (p.K + BK - 1) / BK;
+  const int k_blocks = (p.K + KE - 1) / KE;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -232,7 +242,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t *sa = tiles + stage * STAGE_BYTES;
           uint8_t *sb = sa + A_BYTES;
           mbar_expect_tx(&full[stage], STAGE_BYTES);
-          const int k0 = kb * BK;
+          int k0 = kb * KE, kb0 = k0;
+          if (TF32) {
+            // segment s of three: A half (hi, hi, lo), B half (hi, lo, hi)
+            const int seg_blocks = p.kp / KE, sgm = kb / seg_blocks, kk = (kb - sgm * seg_blocks) * KE;
+            k0 = kk + (sgm == 2 ? p.kp : 0);
+            kb0 = kk + (sgm == 1 ? p.kp : 0);
+          }
+          if (TF32) {
+            tma_load_2d(sa, &map_a, &full[stage], k0, m0);
+            tma_load_2d(sb, &map_b, &full[stage], kb0, n0);
+          } else {
           if (p.a_mn) {
             tma_load_2d(sa, &map_a, &full[stage], m0, k0);
             tma_load_2d(sa + 64 * BK * 2, &map_a, &full[stage], m0 + 64, k0);
@@ -244,6 +264,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * BK * 2, &map_b, &full[stage], n0 + 64 * j, k0);
           } else {
             tma_load_2d(sb, &map_b, &full[stage], k0, n0);
+          }
           }
           filled |= 1u << stage;
           fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
@@ -263,9 +284,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = (1u << 4) | (uint32_t(p.elem_is_bf16) << 7) | (uint32_t(p.elem_is_bf16) << 10) |
-                             (uint32_t(p.a_mn) << 15) | (uint32_t(p.b_mn) << 16) | (uint32_t(BN >> 3) << 17) |
-                             (uint32_t(BM >> 4) << 24);
+      // A/B format: F16 0, BF16 1 (kind::f16); TF32 2 (kind::tf32).
+      const uint32_t fmt = TF32 ? 2u : uint32_t(p.elem_is_bf16);
+      const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(p.a_mn) << 15) |
+                             (uint32_t(p.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
       // K advance per 16-element MMA step inside a stage: 32 bytes along a
       // K-major row; 16 rows of 128 bytes down an MN-major tile.
       const uint32_t a_step = p.a_mn ? 16 * 128 : 32, b_step = p.b_mn ? 16 * 128 : 32;
@@ -286,10 +308,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           fence_after();
           const uint32_t sa = smem_u32(tiles + stage * STAGE_BYTES), sb = sa + A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {  // 32 bytes of K per MMA: 16 f16/bf16 or 8 tf32
             uint64_t da = smem_desc(sa + kk * a_step, a_lbo, 1024);
             uint64_t db = smem_desc(sb + kk * b_step, b_lbo, 1024);
-            umma(tmem_d, da, db, idesc, (kb | kk) != 0);
+            if (TF32) umma_tf32(tmem_d, da, db, idesc, (kb | kk) != 0);
+            else umma(tmem_d, da, db, idesc, (kb | kk) != 0);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -331,6 +354,32 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32(taddr + uint32_t(c * 32), r);
         const int col0 = n0 + c * 32;
+        if (TF32) {
+          if (row < p.M && col0 < p.N) {
+            float *frow = static_cast<float *>(p.c) + size_t(row) * size_t(p.N) + col0;
+            if (col0 + 32 <= p.N && p.vec_store) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4 o = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                       __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                if (p.accumulate) {
+                  const float4 old = *reinterpret_cast<const float4 *>(frow + 4 * j);
+                  o = make_float4(__fadd_rn(old.x, o.x), __fadd_rn(old.y, o.y), __fadd_rn(old.z, o.z),
+                                  __fadd_rn(old.w, o.w));
+                }
+                *reinterpret_cast<float4 *>(frow + 4 * j) = o;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) {
+                  const float v = __uint_as_float(r[j]);
+                  frow[j] = p.accumulate ? __fadd_rn(frow[j], v) : v;
+                }
+            }
+          }
+          continue;
+        }
         if (row < p.M && col0 < p.N) {
           float v[32];
 #pragma unroll
@@ -472,36 +521,71 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // A 2-D map of a row-major [outer, inner] matrix with `box` = {64, box_outer}
 // and 128-byte swizzle.
-int make_map(CUtensorMap *map, const void *base, bool bf16, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+int make_map(CUtensorMap *map, const void *base, bool bf16, uint64_t inner, uint64_t outer, uint32_t box_outer,
+             bool f32 = false) {
   auto fn = encode_fn();
   if (!fn) return fail(TC_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  const uint64_t eb = f32 ? 4 : 2;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 2};
-  cuuint32_t box[2] = {64, box_outer};
+  cuuint64_t strides[1] = {inner * eb};
+  cuuint32_t box[2] = {cuuint32_t(128 / eb), box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                  const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUtensorMapDataType type = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TC_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return TC_OK;
 }
 
-template <int BN, int STAGES>
+// An f32 operand as TF32 halves: row r of `out` (2 * kp floats) is
+// [hi(x[r, 0..K)), zeros | lo(x[r, 0..K)), zeros] with hi = tf32(x) (round
+// to nearest, ties away) and lo = tf32(x - hi); x[r, k] is src[r*sr + k*sc].
+// A 32 x 32 tile through shared memory when the source steps by one along r.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t u;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+  return __uint_as_float(u);
+}
+__global__ void __launch_bounds__(256) split_tf32(const float *src, long long R, long long K, long long sr,
+                                                  long long sc, float *out, long long kp) {
+  __shared__ float tile[32][33];
+  const long long r0 = (long long)blockIdx.y * 32, k0 = (long long)blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  if (sc != 1) {
+    // read along r (consecutive threads, consecutive rows), write along k
+    for (int i = ty; i < 32; i += 8) {
+      const long long k = k0 + i, r = r0 + tx;
+      tile[i][tx] = (r < R && k < K) ? __ldg(src + r * sr + k * sc) : 0.0f;
+    }
+    __syncthreads();
+  }
+  for (int i = ty; i < 32; i += 8) {
+    const long long r = r0 + i, k = k0 + tx;
+    if (r >= R) continue;
+    const float x = sc != 1 ? tile[tx][i] : (k < K ? __ldg(src + r * sr + k) : 0.0f);
+    const float hi = to_tf32(x);
+    out[r * 2 * kp + k] = hi;
+    out[r * 2 * kp + kp + k] = to_tf32(__fsub_rn(x, hi));
+  }
+}
+
+template <int BN, int STAGES, bool TF32 = false>
 int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, cudaStream_t stream) {
-  constexpr size_t smem = size_t(STAGES) * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  constexpr size_t smem = size_t(STAGES) * (BM * 128 + BN * 128) + 1024 + 256;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
-    if (int st = check_cuda(cudaFuncSetAttribute(gemm_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 int(smem)),
+    if (int st = check_cuda(cudaFuncSetAttribute(gemm_tc<BN, STAGES, TF32>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
                             "cudaFuncSetAttribute"))
       return st;
     configured[dev & 63] = true;
   }
   int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   int grid = std::min(tiles, sm_count());
-  gemm_tc<BN, STAGES><<<grid, THREADS, smem, stream>>>(ma, mb, p);
+  gemm_tc<BN, STAGES, TF32><<<grid, THREADS, smem, stream>>>(ma, mb, p);
   return check_launch("gemm (tcgen05)");
 }
 
@@ -560,6 +644,42 @@ int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_
   if (int st = a_mn ? make_map(&ma, a, bf16, rows, inner, BK) : make_map(&ma, a, bf16, inner, rows, BM)) return st;
   if (int st = b_mn ? make_map(&mb, b, bf16, cols, inner, BK) : make_map(&mb, b, bf16, inner, cols, BN)) return st;
   return BN == 256 ? launch<256, 4>(ma, mb, p, stream) : launch<128, 6>(ma, mb, p, stream);
+}
+
+int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b, void *c,
+                  bool accumulate, cudaStream_t stream) {
+  if (rows > 0x7fffffffu || cols > 0x7fffffffu || inner > 0x2aaaaaa0u) return TC_ENOTSUP;
+  const long long kp = ((long long)inner + 31) / 32 * 32;
+  void *scratch_p = nullptr;
+  if (int st = scratch(size_t(rows + cols) * size_t(2 * kp) * sizeof(float), &scratch_p)) return st;
+  float *ah = static_cast<float *>(scratch_p), *bh = ah + size_t(rows) * size_t(2 * kp);
+  // A as [rows x K]: element (m, k); B as [cols x K]: element (n, k).
+  const long long a_sr = transposed == TC_TRANS_LEFT ? 1 : (long long)inner;
+  const long long a_sc = transposed == TC_TRANS_LEFT ? (long long)rows : 1;
+  const long long b_sr = transposed == TC_TRANS_RIGHT ? (long long)inner : 1;
+  const long long b_sc = transposed == TC_TRANS_RIGHT ? 1 : (long long)cols;
+  dim3 ga(unsigned(kp / 32), unsigned((rows + 31) / 32)), gb(unsigned(kp / 32), unsigned((cols + 31) / 32));
+  split_tf32<<<ga, 256, 0, stream>>>(static_cast<const float *>(a), (long long)rows, (long long)inner, a_sr, a_sc, ah,
+                                     kp);
+  split_tf32<<<gb, 256, 0, stream>>>(static_cast<const float *>(b), (long long)cols, (long long)inner, b_sr, b_sc, bh,
+                                     kp);
+  if (int st = check_launch("gemm (tf32 split)")) return st;
+  Params p{};
+  p.M = int(rows);
+  p.N = int(cols);
+  p.K = int(3 * kp);
+  p.kp = int(kp);
+  p.a_mn = 0;
+  p.b_mn = 0;
+  p.accumulate = accumulate;
+  p.c = c;
+  p.vec_store = (uintptr_t(c) & 15u) == 0 && cols % 4 == 0;
+  const long long tiles256 = ((long long)(rows + BM - 1) / BM) * ((long long)(cols + 255) / 256);
+  const int BN = tiles256 >= sm_count() ? 256 : 128;
+  CUtensorMap ma, mb;
+  if (int st = make_map(&ma, ah, false, uint64_t(2 * kp), rows, BM, true)) return st;
+  if (int st = make_map(&mb, bh, false, uint64_t(2 * kp), cols, BN, true)) return st;
+  return BN == 256 ? launch<256, 4, true>(ma, mb, p, stream) : launch<128, 6, true>(ma, mb, p, stream);
 }
 
 }  // namespace tc

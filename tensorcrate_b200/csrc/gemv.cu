@@ -358,6 +358,13 @@ int tc_matmul(int dtype, int transposed, size_t rows, size_t inner, size_t cols,
   if (dtype != TC_F32) {
     int st = gemm_tc_run(dtype, transposed, rows, inner, cols, a, b, c, accumulate != 0, s);
     if (st != TC_ENOTSUP) return st;
+  } else if (double(rows) * double(cols) * double(inner) >= double(1 << 24) && rows >= 64 && cols >= 64 &&
+             inner >= 32) {
+    // f32 products big enough to fill the machine: three TF32 passes on the
+    // tensor cores (relative error near 2^-21 per product, inside the f32
+    // parity tolerance); small ones stay on the FP32 pipe.
+    int st = gemm_tf32_run(transposed, rows, inner, cols, a, b, c, accumulate != 0, s);
+    if (st != TC_ENOTSUP) return st;
   }
   return gemm_simt_run(dtype, transposed, rows, inner, cols, a, b, c, accumulate != 0, s);
 }
