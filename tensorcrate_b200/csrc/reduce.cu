@@ -566,12 +566,37 @@ __global__ void __launch_bounds__(256, 3) reduce_cols_fast(const typename T::S *
         for (int u = 0; u < U; ++u)
           if (f + u < hi)
             v[u].raw = __ldg(reinterpret_cast<const typename V::Raw *>(base + (long long)(f + u) * a.folded_stride));
+        if (is_arg<MODE>()) {
+          // The block's extreme per column first (fmaxf / fminf pass over
+          // NaNs), then, only when it beats the running one, the first row
+          // holding it: the same first-index, NaN-skipping result as folding
+          // element by element, for about one instruction per element.
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (f + u < hi) {
+          for (int c = 0; c < CPT; ++c) {
+            float x[U];
 #pragma unroll
-            for (int c = 0; c < CPT; ++c) push<F>(acc[c], T::load(v[u].v[c]), uint32_t(f + u));
+            for (int u = 0; u < U; ++u) x[u] = f + u < hi ? T::load(v[u].v[c]) : __int_as_float(0x7fc00000);
+            float e = x[0];
+#pragma unroll
+            for (int u = 1; u < U; ++u) e = MODE == M_ARGMAX ? fmaxf(e, x[u]) : fminf(e, x[u]);
+            const bool better = MODE == M_ARGMAX ? e > acc[c].v : e < acc[c].v;
+            if (better || (isnan(acc[c].v) && !isnan(e))) {
+              int first = U - 1;
+#pragma unroll
+              for (int u = U - 1; u >= 0; --u)
+                if (x[u] == e) first = u;
+              acc[c].v = e;
+              acc[c].i = uint32_t(f + first);
+            }
           }
+        } else {
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (f + u < hi) {
+#pragma unroll
+              for (int c = 0; c < CPT; ++c) push<F>(acc[c], T::load(v[u].v[c]), uint32_t(f + u));
+            }
+        }
       }
     const long long r = ko * a.K + k;
     if (lo > 0 || hi < a.depth) {

@@ -201,3 +201,27 @@ def test_column_reductions_split_across_blocks(device, dtype, shape):
     for op in (N.RMAX, N.RMIN):
         got = cuda.Cuda.arg_reduce(v, 1, op).as_slice()
         assert np.array_equal(got, O.arg_reduce(dtype, shape, x, 0, st, 1, op)), op
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_column_arg_reductions_with_nans_ties_and_signed_zeros(device, dtype):
+    """arg_reduce down the rows (the columns path): NaNs are passed over, a
+    column of only NaNs answers 0, ties keep the first row, -0 and +0 tie,
+    and infinities count (strided.rs:186-225)."""
+    rows, cols = 700, 1024
+    x = (integral(rows * cols) % 5).reshape(rows, cols)  # many ties
+    x[::7, :] = np.nan
+    x[:, 3] = np.nan                                      # all NaN
+    x[:, 5] = 0.0
+    x[1::2, 5] = -0.0                                     # signed zeros only
+    x[:, 9] = -np.inf
+    x[650:, 9] = np.nan
+    x[:, 11] = np.inf
+    x[:, 12] = np.nan
+    x[699, 12] = -3.0                                     # the last row the only number
+    x = O.narrow(x.reshape(-1), dtype)
+    shape, st = [rows, cols], [cols, 1]
+    v = cuda.TensorView(cuda.CudaStorage.store(x, dtype), shape, st, 0)
+    for op in (N.RMAX, N.RMIN):
+        got = cuda.Cuda.arg_reduce(v, 0, op).as_slice()
+        assert np.array_equal(got, O.arg_reduce(dtype, shape, x, 0, st, 0, op)), op
