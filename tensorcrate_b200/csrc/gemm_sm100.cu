@@ -164,6 +164,12 @@ struct Params {
   // [hi | lo] halves; the K loop runs over three kp-long segments
   // (hi.hi, hi.lo, lo.hi) and p.K = 3 * kp.
   int kp;
+  // Split K: each tile's K blocks in `ksplit` ranges of `kper` blocks, one
+  // work unit each; a unit's raw f32 accumulator goes to
+  // partial[range][row][col] and a second kernel sums the ranges in order
+  // and applies the epilogue.  ksplit = 1: the epilogue here.
+  int ksplit, kper;
+  float *partial;
 };
 
 // Tile t of the persistent sequence -> (m block, n block), grouped along M
@@ -199,6 +205,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
+  const int S = p.ksplit;
+  const int num_units = num_tiles * S;
   const int k_blocks = (p.K + KE - 1) / KE;
 
   if (threadIdx.x == 0) {
@@ -233,11 +241,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t filled = 0, fill_parity = 0;  // per stage: a fill was issued, and its phase parity
-      for (int t = blockIdx.x; t < num_tiles && !abort_flag; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && !abort_flag; u += gridDim.x) {
+        const int t = u / S, ks = u - t * S;
         int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        const int kb_lo = ks * p.kper, kb_hi = min(k_blocks, kb_lo + p.kper);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, &abort_flag)) break;
           uint8_t *sa = tiles + stage * STAGE_BYTES;
           uint8_t *sb = sa + A_BYTES;
@@ -296,14 +306,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int iter = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++iter) {
         const int buf = iter & 1;
         const uint32_t use = uint32_t(iter >> 1);
+        const int ks = u - (u / S) * S;
+        const int kb_lo = ks * p.kper, kb_hi = min(k_blocks, kb_lo + p.kper);
         // The accumulator must have been drained by the epilogue.
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, &abort_flag)) { ok = false; break; }
         fence_after();
         const uint32_t tmem_d = tmem_base + uint32_t(buf * BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[stage], phase, &abort_flag)) { ok = false; break; }
           fence_after();
           const uint32_t sa = smem_u32(tiles + stage * STAGE_BYTES), sb = sa + A_BYTES;
@@ -311,8 +323,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int kk = 0; kk < 4; ++kk) {  // 32 bytes of K per MMA: 16 f16/bf16 or 8 tf32
             uint64_t da = smem_desc(sa + kk * a_step, a_lbo, 1024);
             uint64_t db = smem_desc(sb + kk * b_step, b_lbo, 1024);
-            if (TF32) umma_tf32(tmem_d, da, db, idesc, (kb | kk) != 0);
-            else umma(tmem_d, da, db, idesc, (kb | kk) != 0);
+            if (TF32) umma_tf32(tmem_d, da, db, idesc, (kb != kb_lo) || kk);
+            else umma(tmem_d, da, db, idesc, (kb != kb_lo) || kk);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -332,16 +344,43 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- epilogue ----------------
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     int iter = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++iter) {
       const int buf = iter & 1;
       const uint32_t use = uint32_t(iter >> 1);
       if (!mbar_wait(&acc_full[buf], use & 1u, &abort_flag)) break;
       fence_after();
+      const int t = u / S, ks = u - t * S;
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
       const int row = mb * BM + q * 32 + lane;
       const int n0 = nb * BN;
       const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
+      if (S > 1) {
+        // One K range of a split tile: the raw f32 accumulator.
+        float *prow = p.partial + (size_t(ks) * size_t(p.M) + size_t(row)) * size_t(p.N);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + uint32_t(c * 32), r);
+          const int col0 = n0 + c * 32;
+          if (row < p.M && col0 < p.N) {
+            if (col0 + 32 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<float4 *>(prow + col0 + 4 * j) =
+                    make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) prow[col0 + j] = __uint_as_float(r[j]);
+            }
+          }
+        }
+        fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       uint16_t *crow = static_cast<uint16_t *>(p.c) + size_t(row) * size_t(p.N);
       uint16_t *hrow = static_cast<uint16_t *>(p.relu_out) + size_t(row) * size_t(p.N);
       float bias_row = 0.0f;
@@ -583,10 +622,88 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, cudaSt
       return st;
     configured[dev & 63] = true;
   }
-  int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
-  int grid = std::min(tiles, sm_count());
+  const int units = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN) * std::max(1, p.ksplit);
+  const int grid = std::min(units, sm_count());
   gemm_tc<BN, STAGES, TF32><<<grid, THREADS, smem, stream>>>(ma, mb, p);
   return check_launch("gemm (tcgen05)");
+}
+
+// Split K, second pass: the K ranges' f32 accumulators summed in range
+// order, then what the GEMM epilogue would have done with the sum.  Four
+// adjacent columns per thread when rows are a multiple of four long.
+template <class T>
+__device__ __forceinline__ float finish_one(float v, typename T::S *c, size_t i, bool accumulate,
+                                            const typename T::S *share_of, float bias, bool has_bias,
+                                            typename T::S *relu_out) {
+  if (accumulate) v = __fadd_rn(T::load(c[i]), v);
+  if (share_of) {
+    const float a = T::load(share_of[i]);
+    v = __fmul_rn(T::load(T::store(v)), a > 0.0f ? 1.0f : (a < 0.0f ? 0.0f : 0.5f));
+  }
+  if (has_bias) v = __fadd_rn(T::load(T::store(v)), bias);
+  if (relu_out) relu_out[i] = T::store(fmaxf(T::load(T::store(v)), 0.0f));
+  return v;
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) splitk_finish(const float *partial, int ranges, long long M, long long N,
+                                                     typename T::S *c, bool accumulate, const typename T::S *share_of,
+                                                     const typename T::S *bias, typename T::S *relu_out) {
+  const long long total = M * N;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  if ((N & 3) == 0) {
+    for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < total / 4; q += stride) {
+      const size_t i = size_t(q) * 4;
+      float4 v = *reinterpret_cast<const float4 *>(partial + i);
+      for (int r = 1; r < ranges; ++r) {
+        const float4 w = *reinterpret_cast<const float4 *>(partial + size_t(r) * size_t(total) + i);
+        v = make_float4(__fadd_rn(v.x, w.x), __fadd_rn(v.y, w.y), __fadd_rn(v.z, w.z), __fadd_rn(v.w, w.w));
+      }
+      const float b = bias ? T::load(bias[i / size_t(N)]) : 0.0f;
+      const float o[4] = {finish_one<T>(v.x, c, i, accumulate, share_of, b, bias, relu_out),
+                          finish_one<T>(v.y, c, i + 1, accumulate, share_of, b, bias, relu_out),
+                          finish_one<T>(v.z, c, i + 2, accumulate, share_of, b, bias, relu_out),
+                          finish_one<T>(v.w, c, i + 3, accumulate, share_of, b, bias, relu_out)};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[i + j] = T::store(o[j]);
+    }
+    return;
+  }
+  for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += stride) {
+    const size_t i = size_t(q);
+    float v = partial[i];
+    for (int r = 1; r < ranges; ++r) v = __fadd_rn(v, partial[size_t(r) * size_t(total) + i]);
+    const float b = bias ? T::load(bias[i / size_t(N)]) : 0.0f;
+    c[i] = T::store(finish_one<T>(v, c, i, accumulate, share_of, b, bias, relu_out));
+  }
+}
+
+// Tile width and K split for an M x N product of k_blocks K blocks: 128 x 256
+// tiles when they fill the SMs; otherwise split K (2 or 4 ranges of at least
+// 16 blocks) while the units still fit in one wave; otherwise 128 x 128 tiles
+// when even twice as many of them fit in one wave.
+struct Plan {
+  int bn, ksplit, kper;
+};
+Plan plan_tiles(long long M, long long N, int k_blocks, bool may_split) {
+  const int sms = sm_count();
+  const long long t256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  if (t256 >= sms) return {256, 1, k_blocks};
+  if (may_split)
+    for (int cand : {4, 2})
+      if (t256 * cand <= sms && k_blocks / cand >= 16) return {256, cand, (k_blocks + cand - 1) / cand};
+  if (t256 * 2 <= sms) return {128, 1, k_blocks};
+  return {256, 1, k_blocks};
+}
+
+template <class T>
+int finish_split(const Params &p, const Epilogue &e, cudaStream_t stream) {
+  using S = typename T::S;
+  const long long total = (long long)p.M * p.N;
+  splitk_finish<T><<<grid_for(size_t(total), 256, 8), 256, 0, stream>>>(
+      p.partial, p.ksplit, p.M, p.N, static_cast<S *>(p.c), p.accumulate != 0, static_cast<const S *>(e.share_of),
+      static_cast<const S *>(e.bias), static_cast<S *>(e.relu_out));
+  return check_launch("gemm (split-K finish)");
 }
 
 }  // namespace
@@ -617,7 +734,7 @@ int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_
   const uint64_t a_inner = a_mn ? rows : inner, b_inner = b_mn ? cols : inner;
   if ((uintptr_t(a) & 15u) || (uintptr_t(b) & 15u) || (a_inner * 2) % 16 || (b_inner * 2) % 16) return TC_ENOTSUP;
   const bool bf16 = dtype == TC_BF16;
-  Params p;
+  Params p{};
   p.M = int(rows);
   p.N = int(cols);
   p.K = int(inner);
@@ -637,21 +754,34 @@ int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_
     p.peer_c[i] = i < n_peers ? peer_c[i] : nullptr;
     if (i < n_peers && (uintptr_t(peer_c[i]) & 15u)) p.vec_store = 0;
   }
-  // 128x256 tiles when they fill the machine, else 128x128.
-  const long long tiles256 = ((long long)(rows + BM - 1) / BM) * ((long long)(cols + 255) / 256);
-  const int BN = tiles256 >= sm_count() ? 256 : 128;
+  const int k_blocks = int((inner + BK - 1) / BK);
+  const Plan pl = plan_tiles((long long)rows, (long long)cols, k_blocks, n_peers == 0);
+  const int BN = pl.bn;
+  p.ksplit = pl.ksplit;
+  p.kper = pl.kper;
+  p.partial = nullptr;
+  if (p.ksplit > 1) {
+    void *w = nullptr;
+    if (int st = scratch(size_t(p.ksplit) * rows * cols * sizeof(float), &w)) return st;
+    p.partial = static_cast<float *>(w);
+  }
   CUtensorMap ma, mb;
   if (int st = a_mn ? make_map(&ma, a, bf16, rows, inner, BK) : make_map(&ma, a, bf16, inner, rows, BM)) return st;
   if (int st = b_mn ? make_map(&mb, b, bf16, cols, inner, BK) : make_map(&mb, b, bf16, inner, cols, BN)) return st;
-  return BN == 256 ? launch<256, 4>(ma, mb, p, stream) : launch<128, 6>(ma, mb, p, stream);
+  if (int st = BN == 256 ? launch<256, 4>(ma, mb, p, stream) : launch<128, 6>(ma, mb, p, stream)) return st;
+  if (p.ksplit == 1) return TC_OK;
+  return bf16 ? finish_split<BF16T>(p, e, stream) : finish_split<F16T>(p, e, stream);
 }
 
 int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b, void *c,
                   bool accumulate, cudaStream_t stream) {
   if (rows > 0x7fffffffu || cols > 0x7fffffffu || inner > 0x2aaaaaa0u) return TC_ENOTSUP;
   const long long kp = ((long long)inner + 31) / 32 * 32;
+  const Plan pl = plan_tiles((long long)rows, (long long)cols, int(3 * kp / 32), true);
+  const size_t operand_floats = size_t(rows + cols) * size_t(2 * kp);
+  const size_t partial_floats = pl.ksplit > 1 ? size_t(pl.ksplit) * rows * cols : 0;
   void *scratch_p = nullptr;
-  if (int st = scratch(size_t(rows + cols) * size_t(2 * kp) * sizeof(float), &scratch_p)) return st;
+  if (int st = scratch((operand_floats + partial_floats) * sizeof(float), &scratch_p)) return st;
   float *ah = static_cast<float *>(scratch_p), *bh = ah + size_t(rows) * size_t(2 * kp);
   // A as [rows x K]: element (m, k); B as [cols x K]: element (n, k).
   const long long a_sr = transposed == TC_TRANS_LEFT ? 1 : (long long)inner;
@@ -674,12 +804,17 @@ int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const 
   p.accumulate = accumulate;
   p.c = c;
   p.vec_store = (uintptr_t(c) & 15u) == 0 && cols % 4 == 0;
-  const long long tiles256 = ((long long)(rows + BM - 1) / BM) * ((long long)(cols + 255) / 256);
-  const int BN = tiles256 >= sm_count() ? 256 : 128;
+  const int BN = pl.bn;
+  p.ksplit = pl.ksplit;
+  p.kper = pl.kper;
+  p.partial = pl.ksplit > 1 ? ah + operand_floats : nullptr;
   CUtensorMap ma, mb;
   if (int st = make_map(&ma, ah, false, uint64_t(2 * kp), rows, BM, true)) return st;
   if (int st = make_map(&mb, bh, false, uint64_t(2 * kp), cols, BN, true)) return st;
-  return BN == 256 ? launch<256, 4, true>(ma, mb, p, stream) : launch<128, 6, true>(ma, mb, p, stream);
+  if (int st = BN == 256 ? launch<256, 4, true>(ma, mb, p, stream) : launch<128, 6, true>(ma, mb, p, stream))
+    return st;
+  if (p.ksplit == 1) return TC_OK;
+  return finish_split<F32T>(p, Epilogue{}, stream);
 }
 
 }  // namespace tc

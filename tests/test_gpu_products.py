@@ -15,7 +15,7 @@ from util import DTYPES, uniform
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(1, 1, 1), (7, 5, 3), (96, 96, 96), (128, 64, 256), (129, 200, 257), (256, 512, 384), (300, 1024, 520),
-          (1024, 1024, 1024)]
+          (1024, 1024, 1024), (256, 4096, 512), (130, 2048, 264)]  # the last two split K
 
 
 def _tol(dtype, k):
@@ -45,7 +45,7 @@ def test_matmul(device, dtype, m, k, n):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("transposed", [N.TRANS_NONE, N.TRANS_LEFT, N.TRANS_RIGHT])
-@pytest.mark.parametrize("m,k,n", [(7, 5, 3), (130, 96, 72), (256, 320, 512)])
+@pytest.mark.parametrize("m,k,n", [(7, 5, 3), (130, 96, 72), (256, 320, 512), (256, 2048, 512)])
 def test_transposed_accumulating_products(device, dtype, transposed, m, k, n):
     """The tape's backward products (tape/mod.rs:1195-1216)."""
     got, want = _run(dtype, transposed, m, k, n, True, 3 * m + k)
@@ -135,7 +135,8 @@ def test_outer_products(device, dtype, transposed):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("m,k,n", [(7, 5, 3), (130, 96, 72), (256, 320, 512), (4096, 1024, 264), (128, 8, 256)])
+@pytest.mark.parametrize("m,k,n", [(7, 5, 3), (130, 96, 72), (256, 320, 512), (4096, 1024, 264), (128, 8, 256),
+                                   (1024, 4096, 256)])
 @pytest.mark.parametrize("relu", [True, False])
 def test_matmul_epilogue_matches_the_separate_operations(device, dtype, m, k, n, relu):
     """tc_matmul_epilogue (Kernels::matmul_epilogue, kernels.rs:1137-1150)
