@@ -117,7 +117,14 @@ struct MultiDesc {
   int n;
   long long start[MAX_BATCH + 1];
   CopyDesc r[MAX_BATCH];
+  // Row form (every region's innermost run contiguous on both sides): work
+  // items of ROW_ITEM units along one row; region k holds items
+  // [items[k], items[k+1]), `per_row[k]` of them per row (with its
+  // multiply-shift division constants).
+  long long items[MAX_BATCH + 1];
+  uint32_t per_row[MAX_BATCH], per_row_mul[MAX_BATCH], per_row_shift[MAX_BATCH];
 };
+constexpr int ROW_ITEM = 32 * 4;  // a warp's item: 4 units per lane
 
 template <int W, typename Index>
 __global__ void __launch_bounds__(256) copy_units_multi(const __grid_constant__ MultiDesc m) {
@@ -143,6 +150,61 @@ __global__ void __launch_bounds__(256) copy_units_multi(const __grid_constant__ 
 #pragma unroll
     for (int k = 0; k < UNROLL; ++k)
       if (i0 + Index(k) * stride < total) *to[k] = v[k];
+  }
+}
+
+// Position of the start of row `row` (all axes but the innermost).
+template <typename Index>
+__device__ __forceinline__ void row_positions(const CopyDesc &d, Index row, Index &s, Index &t) {
+  Index rest = row;
+  s = Index(d.offset[0]);
+  t = Index(d.offset[1]);
+  for (int a = d.rank - 2; a >= 0; --a) {
+    const Index e = Index(d.shape[a]);
+    Index q;
+    if (sizeof(Index) == 4)
+      q = d.mul[a] ? Index(__umulhi(uint32_t(rest), d.mul[a]) >> d.shift[a]) : (e == 1 ? rest : Index(0));
+    else
+      q = rest / e;
+    const Index ca = rest - q * e;
+    rest = q;
+    s += ca * Index(d.stride[0][a]);
+    t += ca * Index(d.stride[1][a]);
+  }
+}
+
+// Regions whose innermost run is contiguous on both sides: a warp per item
+// of ROW_ITEM units along one row, each lane 4 units 32 apart (loads before
+// stores); the row's start costs one division per item, not per unit.
+template <int W, typename Index>
+__global__ void __launch_bounds__(256) copy_rows_multi(const __grid_constant__ MultiDesc m) {
+  using U = typename Unit<W>::T;
+  const Index total = Index(m.items[m.n]);
+  const int lane = threadIdx.x & 31;
+  const Index warps = Index(gridDim.x) * (blockDim.x >> 5);
+  for (Index item = Index(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < total; item += warps) {
+    int r = 0;
+    while (r + 1 < m.n && item >= Index(m.items[r + 1])) ++r;
+    const CopyDesc &d = m.r[r];
+    const Index local = item - Index(m.items[r]);
+    Index row;
+    if (sizeof(Index) == 4)
+      row = m.per_row_mul[r] ? Index(__umulhi(uint32_t(local), m.per_row_mul[r]) >> m.per_row_shift[r]) : local;
+    else
+      row = local / Index(m.per_row[r]);
+    const Index col0 = (local - row * Index(m.per_row[r])) * ROW_ITEM + lane;
+    const Index inner = Index(d.shape[d.rank - 1]);
+    Index s, t;
+    row_positions(d, row, s, t);
+    const U *src = reinterpret_cast<const U *>(d.src) + s;
+    U *dst = reinterpret_cast<U *>(d.dst) + t;
+    U v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (col0 + 32 * k < inner) v[k] = __ldg(src + col0 + 32 * k);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (col0 + 32 * k < inner) dst[col0 + 32 * k] = v[k];
   }
 }
 
@@ -200,10 +262,13 @@ __global__ void __launch_bounds__(256) copy_transpose_pairs(const CopyDesc d, in
   constexpr int ROWS_PER_PASS = 256 / (TT / 2);  // inner rows one pass of the block reads
   constexpr int PASSES = 64 / ROWS_PER_PASS;
   constexpr int PITCH = 64 + 2;                   // u16 per t row: 33 words
-  __shared__ __align__(16) uint16_t tile[BATCH][TT][PITCH];
-  __shared__ const uint16_t *sb[BATCH];
-  __shared__ uint16_t *tb[BATCH];
-  __shared__ int ilim[BATCH], tlim[BATCH];  // valid inner / t extent of each tile
+  // Two tile buffers and three descriptor slots: while a batch is written
+  // out of one buffer, the next batch's loads are in flight into registers
+  // and the one after it is being described.
+  __shared__ __align__(16) uint16_t tile[2][BATCH][TT][PITCH];
+  __shared__ const uint16_t *sb[3][BATCH];
+  __shared__ uint16_t *tb[3][BATCH];
+  __shared__ int ilim[3][BATCH], tlim[3][BATCH];  // valid inner / t extent of each tile
   const uint16_t *src = reinterpret_cast<const uint16_t *>(d.src);
   uint16_t *dst = reinterpret_cast<uint16_t *>(d.dst);
   const int rank = d.rank;
@@ -211,63 +276,78 @@ __global__ void __launch_bounds__(256) copy_transpose_pairs(const CopyDesc d, in
   const long long tiles_i = (n_in + 63) / 64, tiles_t = (n_t + TT - 1) / TT;
   const long long total = others * tiles_i * tiles_t;
   const long long s_in = d.stride[0][rank - 1], d_t = d.stride[1][t_axis];
+  const long long step = (long long)gridDim.x * BATCH;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rp = threadIdx.x / (TT / 2), pp = threadIdx.x % (TT / 2);  // read: row in pass, pair
-  for (long long w0 = (long long)blockIdx.x * BATCH; w0 < total; w0 += (long long)gridDim.x * BATCH) {
-    // One thread per tile of the batch decomposes its index.
-    if (threadIdx.x < BATCH) {
-      const long long w = w0 + threadIdx.x;
-      long long o = w / (tiles_i * tiles_t);
-      const long long rem = w - o * tiles_i * tiles_t;
-      long long so = d.offset[0], to = d.offset[1];
-      for (int a = rank - 2; a >= 0; --a) {
-        if (a == t_axis) continue;
-        const long long e = d.shape[a], c = o % e;
-        o /= e;
-        so += c * d.stride[0][a];
-        to += c * d.stride[1][a];
-      }
-      const long long i0 = (rem / tiles_t) * 64, j0 = (rem % tiles_t) * TT;
-      sb[threadIdx.x] = src + so + i0 * s_in + j0;
-      tb[threadIdx.x] = dst + to + j0 * d_t + i0;
-      ilim[threadIdx.x] = w < total ? int(min(64LL, n_in - i0)) : 0;
-      tlim[threadIdx.x] = w < total ? int(min((long long)TT, n_t - j0)) : 0;
+  // One thread per tile of a batch decomposes its index into slot `sl`.
+  auto describe = [&](long long w0, int sl) {
+    if (threadIdx.x >= BATCH) return;
+    const long long w = w0 + threadIdx.x;
+    if (w >= total) {
+      ilim[sl][threadIdx.x] = tlim[sl][threadIdx.x] = 0;
+      return;
     }
-    __syncthreads();
-    // read every tile of the batch before storing any
-    uint32_t v[BATCH][PASSES];
+    long long o = w / (tiles_i * tiles_t);
+    const long long rem = w - o * tiles_i * tiles_t;
+    long long so = d.offset[0], to = d.offset[1];
+    for (int a = rank - 2; a >= 0; --a) {
+      if (a == t_axis) continue;
+      const long long e = d.shape[a], c = o % e;
+      o /= e;
+      so += c * d.stride[0][a];
+      to += c * d.stride[1][a];
+    }
+    const long long i0 = (rem / tiles_t) * 64, j0 = (rem % tiles_t) * TT;
+    sb[sl][threadIdx.x] = src + so + i0 * s_in + j0;
+    tb[sl][threadIdx.x] = dst + to + j0 * d_t + i0;
+    ilim[sl][threadIdx.x] = int(min(64LL, n_in - i0));
+    tlim[sl][threadIdx.x] = int(min((long long)TT, n_t - j0));
+  };
+  uint32_t v[BATCH][PASSES];
+  auto load = [&](int sl) {
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
-      const uint16_t *base = sb[q] + 2 * pp;
-      const bool tok = 2 * pp < tlim[q];
+      const uint16_t *base = sb[sl][q] + 2 * pp;
+      const bool tok = 2 * pp < tlim[sl][q];
 #pragma unroll
       for (int k = 0; k < PASSES; ++k) {
         const int i = rp + ROWS_PER_PASS * k;
-        v[q][k] = (tok && i < ilim[q]) ? __ldg(reinterpret_cast<const uint32_t *>(base + (long long)i * s_in)) : 0u;
+        v[q][k] = (tok && i < ilim[sl][q]) ? __ldg(reinterpret_cast<const uint32_t *>(base + (long long)i * s_in)) : 0u;
       }
     }
+  };
+  long long w0 = (long long)blockIdx.x * BATCH;
+  if (w0 >= total) return;
+  describe(w0, 0);
+  __syncthreads();
+  load(0);
+  for (int it = 0; w0 < total; w0 += step, ++it) {
+    const int buf = it & 1, sl = it % 3, nsl = (it + 1) % 3;
+    // stage this batch (already in registers) in shared memory, t-major
 #pragma unroll
     for (int q = 0; q < BATCH; ++q)
 #pragma unroll
       for (int k = 0; k < PASSES; ++k) {
         const int i = rp + ROWS_PER_PASS * k;
-        tile[q][2 * pp][i] = uint16_t(v[q][k] & 0xffffu);
-        tile[q][2 * pp + 1][i] = uint16_t(v[q][k] >> 16);
+        tile[buf][q][2 * pp][i] = uint16_t(v[q][k] & 0xffffu);
+        tile[buf][q][2 * pp + 1][i] = uint16_t(v[q][k] >> 16);
       }
+    describe(w0 + step, nsl);
     __syncthreads();
+    // the next batch's loads go out before this batch's stores
+    if (w0 + step < total) load(nsl);
     // write: warp rows = t indices, lanes = pairs along inner
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
-      const bool iok = 2 * lane < ilim[q];
+      const bool iok = 2 * lane < ilim[sl][q];
+      uint16_t *out = tb[sl][q] + 2 * lane;
 #pragma unroll
       for (int k = 0; k < TT / 8; ++k) {
         const int j = warp + 8 * k;
-        if (iok && j < tlim[q])
-          *reinterpret_cast<uint32_t *>(tb[q] + (long long)j * d_t + 2 * lane) =
-              *reinterpret_cast<const uint32_t *>(&tile[q][j][2 * lane]);
+        if (iok && j < tlim[sl][q])
+          *reinterpret_cast<uint32_t *>(out + (long long)j * d_t) = *reinterpret_cast<const uint32_t *>(&tile[buf][q][j][2 * lane]);
       }
     }
-    __syncthreads();
   }
 }
 
@@ -285,24 +365,80 @@ int largest_unit(size_t elem, const Dims &shape, const Dims *st, const void *src
   return int(elem);
 }
 
+// True when every index a region computes (counts, and the furthest
+// position on either side) fits a signed 32-bit integer.
+bool fits32(const CopyDesc &d) {
+  if (d.count >= (1LL << 31)) return false;
+  for (int side = 0; side < 2; ++side) {
+    long long reach = d.offset[side];
+    for (int a = 0; a < d.rank; ++a) reach += (d.shape[a] - 1) * d.stride[side][a];
+    if (reach >= (1LL << 31)) return false;
+  }
+  return true;
+}
+
+// Launch the regions of `m` (one unit width): in row form when every
+// region's innermost run is contiguous on both sides, else unit by unit.
 template <int W>
-int launch_units(const CopyDesc &d, cudaStream_t stream) {
-  unsigned block = 256;
-  unsigned grid = grid_for(size_t(d.count), block, 16);
-  if (d.count < (1ll << 31)) copy_units<W, int><<<grid, block, 0, stream>>>(d);
-  else copy_units<W, long long><<<grid, block, 0, stream>>>(d);
+int launch_multi(MultiDesc &m, cudaStream_t stream) {
+  bool rows = true, narrow = true;
+  for (int k = 0; k < m.n; ++k) {
+    const CopyDesc &d = m.r[k];
+    rows = rows && d.stride[0][d.rank - 1] == 1 && d.stride[1][d.rank - 1] == 1;
+    narrow = narrow && fits32(d);
+  }
+  if (rows) {
+    m.items[0] = 0;
+    for (int k = 0; k < m.n; ++k) {
+      const CopyDesc &d = m.r[k];
+      const long long inner = d.shape[d.rank - 1];
+      const long long per_row = (inner + ROW_ITEM - 1) / ROW_ITEM;
+      m.items[k + 1] = m.items[k] + d.count / inner * per_row;
+      m.per_row[k] = uint32_t(per_row);
+      m.per_row_mul[k] = m.per_row_shift[k] = 0;
+      if (per_row > 1 && per_row < (1LL << 31)) {
+        int l = 0;
+        while ((1LL << l) < per_row) ++l;
+        m.per_row_mul[k] = uint32_t(((1ull << (31 + l)) + uint64_t(per_row) - 1) / uint64_t(per_row));
+        m.per_row_shift[k] = uint32_t(l - 1);
+      }
+    }
+    const long long items = m.items[m.n];
+    narrow = narrow && items < (1LL << 31);
+    const unsigned grid = unsigned(std::max(1LL, std::min((items + 7) / 8, (long long)sm_count() * 8)));
+    if (narrow) copy_rows_multi<W, int><<<grid, 256, 0, stream>>>(m);
+    else copy_rows_multi<W, long long><<<grid, 256, 0, stream>>>(m);
+    return check_launch("strided copy (rows)");
+  }
+  const long long total = m.start[m.n];
+  const unsigned grid = grid_for(size_t(total), 256, 16);
+  if (m.n == 1) {
+    if (narrow) copy_units<W, int><<<grid, 256, 0, stream>>>(m.r[0]);
+    else copy_units<W, long long><<<grid, 256, 0, stream>>>(m.r[0]);
+  } else {
+    if (narrow && total < (1LL << 31)) copy_units_multi<W, int><<<grid, 256, 0, stream>>>(m);
+    else copy_units_multi<W, long long><<<grid, 256, 0, stream>>>(m);
+  }
   return check_launch("strided copy");
 }
 
-int launch_width(int w, const CopyDesc &d, cudaStream_t stream) {
+int launch_multi_width(int w, MultiDesc &m, cudaStream_t stream) {
   switch (w) {
-    case 1: return launch_units<1>(d, stream);
-    case 2: return launch_units<2>(d, stream);
-    case 4: return launch_units<4>(d, stream);
-    case 8: return launch_units<8>(d, stream);
-    case 16: return launch_units<16>(d, stream);
+    case 1: return launch_multi<1>(m, stream);
+    case 2: return launch_multi<2>(m, stream);
+    case 4: return launch_multi<4>(m, stream);
+    case 8: return launch_multi<8>(m, stream);
+    case 16: return launch_multi<16>(m, stream);
   }
   return fail(TC_EINVAL, "strided copy: element width %d", w);
+}
+
+int launch_width(int w, const CopyDesc &d, cudaStream_t stream) {
+  MultiDesc m{};
+  m.n = 1;
+  m.r[0] = d;
+  m.start[1] = d.count;
+  return launch_multi_width(w, m, stream);
 }
 
 template <int W>
@@ -520,24 +656,7 @@ int tc_assemble(size_t elem, void *dst, size_t len, const tc_region *regions, si
   int width = 0;
   auto flush = [&]() -> int {
     if (m.n == 0) return TC_OK;
-    int st = TC_OK;
-    if (m.n == 1) {
-      st = launch_width(width, m.r[0], as_stream(stream));
-    } else {
-      const long long total = m.start[m.n];
-      unsigned grid = grid_for(size_t(total), 256, 16);
-      switch (width) {
-#define TC_MULTI(W)                                                                                      \
-  case W:                                                                                                \
-    if (total < (1LL << 31)) copy_units_multi<W, int><<<grid, 256, 0, as_stream(stream)>>>(m);          \
-    else copy_units_multi<W, long long><<<grid, 256, 0, as_stream(stream)>>>(m);                        \
-    st = check_launch("assemble");                                                                       \
-    break;
-        TC_MULTI(1) TC_MULTI(2) TC_MULTI(4) TC_MULTI(8) TC_MULTI(16)
-#undef TC_MULTI
-        default: st = fail(TC_EINVAL, "assemble: unit width %d", width);
-      }
-    }
+    const int st = launch_multi_width(width, m, as_stream(stream));
     m.n = 0;
     return st;
   };
