@@ -321,6 +321,51 @@ int tc_mlp_prune_leaves(tc_mlp *mlp, int prune);
 int tc_mlp_step(tc_mlp *mlp, const void *x_dev, const void *y_dev, tc_comm *comm, void *loss_dev,
                 void *stream);
 
+/* ---- fused elementwise programs (Kernels::fused, kernels.rs:1077-1082) --- */
+/* One instruction of a fused::Program (fused/mod.rs:290-313).  `code` is a
+ * tc_instr_code; registers are below 16.  Load reads place `slot` (one per
+ * distinct load of the program, in the program's order of them, as
+ * Space::places lists them); Store writes output `slot`; Const's `value` is
+ * a value of the program's type; `op` is a tc_binary_op, tc_compare or
+ * tc_analytic. */
+enum tc_instr_code {
+  TC_I_LOAD = 0, TC_I_CONST = 1, TC_I_BINARY = 2, TC_I_UNARY = 3, TC_I_CMP = 4, TC_I_STORE = 5
+};
+/* Analytic, src/tensors/kernels.rs:293-308 */
+enum tc_analytic {
+  TC_SIN = 0, TC_COS = 1, TC_TAN = 2, TC_SEC = 3, TC_CSC = 4, TC_ARCSIN = 5, TC_ARCCOS = 6,
+  TC_ARCTAN = 7, TC_EXP = 8, TC_LN = 9, TC_SINH = 10, TC_COSH = 11, TC_TANH = 12, TC_SQRT = 13
+};
+typedef struct tc_instr {
+  uint8_t code, dst, a, b, op, slot;
+  uint16_t reserved;
+  float value;
+} tc_instr;
+/* Where one load reads (fused::Place, fused/mod.rs:3229-3238): element
+ * (row, col) of the rows x cols space is data[offset + col*col_step + sum_k
+ * c_k*steps[k]], c the row index decomposed over dims[0..lead) (outermost
+ * first); `dtype` is the storage type of `data` (f32, f16 or bf16). */
+typedef struct tc_place {
+  const void *data;
+  int dtype;
+  uint32_t lead;
+  size_t offset, col_step;
+  size_t dims[TC_MAX_RANK - 1], steps[TC_MAX_RANK - 1];
+} tc_place;
+/* Run `program` (n_code instructions, at most 256) over a rows x cols space
+ * in the program's type `dtype`: every instruction's result rounds to that
+ * type, loads convert from their storage type to it, stores from it to
+ * each output's storage type (out_dtypes), as the Host's interpreter does
+ * (fused/mod.rs:4055-4260).  Outputs are row-major rows x cols.  An output
+ * may be the storage a load reads (a tensor updated in place) when that
+ * load reads it in order.  Unary functions other than Sqrt use CUDA's f32
+ * functions (within 2 ulp of the exact value for f32; sec and csc are 1/cos
+ * and 1/sin); everything else is exact.  At most 16 places and 8 outputs.
+ * TC_ENOTSUP for an f64 storage or program type. */
+int tc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
+             const tc_place *places, uint32_t n_places, void *const *outputs,
+             const int *out_dtypes, uint32_t n_outputs, void *stream);
+
 /* ---- multi-GPU (NCCL over NVLink; no counterpart in the reference) ------ */
 /* 128 opaque bytes (ncclUniqueId) for rank 0 to share with the others. */
 int tc_comm_unique_id(uint8_t id[128]);

@@ -45,6 +45,7 @@ SIGNATURES = {
     "orc_transpose": [_i, _sz, _sz, _p, _p],
     "orc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d],
     "orc_sgd": [_i, _sz, _p, _p, _d],
+    "orc_fused": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _p, _u32],
     "orc_adam_coefficients": [_i, _d, _d, _d, _d, _u32, C.POINTER(C.c_double)],
     "orc_mlp_params": [_p, _u32, _p, _p, _i],
     "orc_mlp_grads": [_p, _u32, _p, _p],

@@ -1143,3 +1143,75 @@ int orc_mlp_step(void *p, const void *x, const void *y, void *loss_out, int skip
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Fused programs: the Host's interpreter (fused/mod.rs:4055-4260), element by
+// element.  Every instruction's result rounds to the program's type; loads
+// convert from their storage type, stores to the output's.  The analytic
+// functions are the C library's f32 ones (the reference uses its own
+// vmath; both are within an ulp or two of the exact value).
+// ---------------------------------------------------------------------------
+static float orc_analytic(int op, float x) {
+  switch (op) {
+    case TC_SIN: return std::sin(x);
+    case TC_COS: return std::cos(x);
+    case TC_TAN: return std::tan(x);
+    case TC_SEC: return 1.0f / std::cos(x);
+    case TC_CSC: return 1.0f / std::sin(x);
+    case TC_ARCSIN: return std::asin(x);
+    case TC_ARCCOS: return std::acos(x);
+    case TC_ARCTAN: return std::atan(x);
+    case TC_EXP: return std::exp(x);
+    case TC_LN: return std::log(x);
+    case TC_SINH: return std::sinh(x);
+    case TC_COSH: return std::cosh(x);
+    case TC_TANH: return std::tanh(x);
+    default: return std::sqrt(x);
+  }
+}
+
+static float orc_load_as(const void *p, int dtype, size_t i) {
+  if (dtype == TC_F32) return F32::load(p, i);
+  return dtype == TC_BF16 ? BF16::load(p, i) : F16::load(p, i);
+}
+static void orc_store_as(void *p, int dtype, size_t i, float v) {
+  if (dtype == TC_F32) F32::store(p, i, v);
+  else if (dtype == TC_BF16) BF16::store(p, i, v);
+  else F16::store(p, i, v);
+}
+
+int orc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code, const tc_place *places,
+              uint32_t n_places, void *const *outputs, const int *out_dtypes, uint32_t n_outputs) {
+  (void)n_places;
+  (void)n_outputs;
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < rows * cols; ++i) {
+      const size_t row = i / cols, col = i % cols;
+      float reg[16] = {0};
+      for (uint32_t k = 0; k < n_code; ++k) {
+        const tc_instr &in = code[k];
+        float v = 0.0f;
+        switch (in.code) {
+          case TC_I_LOAD: {
+            const tc_place &pl = places[in.slot];
+            size_t at = pl.offset + col * pl.col_step, rest = row;
+            for (int a = int(pl.lead) - 1; a >= 0; --a) {
+              at += (rest % pl.dims[a]) * pl.steps[a];
+              rest /= pl.dims[a];
+            }
+            v = T::round(orc_load_as(pl.data, pl.dtype, at));
+            break;
+          }
+          case TC_I_CONST: v = T::round(in.value); break;
+          case TC_I_BINARY: v = T::round(binary_value(in.op, reg[in.a], reg[in.b])); break;
+          case TC_I_UNARY: v = T::round(orc_analytic(in.op, reg[in.a])); break;
+          case TC_I_CMP: v = compare_value(in.op, reg[in.a], reg[in.b]); break;
+          default: orc_store_as(outputs[in.slot], out_dtypes[in.slot], i, reg[in.a]); continue;
+        }
+        reg[in.dst] = v;
+      }
+    }
+    return int(TC_OK);
+  });
+}

@@ -103,6 +103,12 @@ int orc_mlp_step(void *mlp, const void *x, const void *y, void *loss_out, int sk
  * src/parallel.rs:40); 0 = all. */
 void orc_set_threads(int threads);
 
+/* Fused program (Kernels::fused; Host interpreter, fused/mod.rs:4055-4260)
+ * over host buffers, as tc_fused takes them. */
+int orc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
+              const tc_place *places, uint32_t n_places, void *const *outputs, const int *out_dtypes,
+              uint32_t n_outputs);
+
 #ifdef __cplusplus
 }
 #endif

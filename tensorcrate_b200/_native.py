@@ -47,6 +47,24 @@ class Region(C.Structure):
     ]
 
 
+class Instr(C.Structure):
+    """tc_instr: one instruction of a fused program."""
+
+    _fields_ = [("code", C.c_uint8), ("dst", C.c_uint8), ("a", C.c_uint8), ("b", C.c_uint8), ("op", C.c_uint8),
+                ("slot", C.c_uint8), ("reserved", C.c_uint16), ("value", C.c_float)]
+
+
+class Place(C.Structure):
+    """tc_place: where one load of a fused program reads."""
+
+    _fields_ = [("data", _p), ("dtype", C.c_int), ("lead", _u32), ("offset", _sz), ("col_step", _sz),
+                ("dims", _sz * (MAX_RANK - 1)), ("steps", _sz * (MAX_RANK - 1))]
+
+
+I_LOAD, I_CONST, I_BINARY, I_UNARY, I_CMP, I_STORE = range(6)
+(SIN, COS, TAN, SEC, CSC, ARCSIN, ARCCOS, ARCTAN, EXP, LN, SINH, COSH, TANH, SQRT) = range(14)
+
+
 class AdamTensor(C.Structure):
     """tc_adam_tensor: one parameter of a tc_adam_multi call."""
 
@@ -84,6 +102,7 @@ SIGNATURES = {
     "tc_matmul": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_matvec": [_i, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_vecmat": [_i, _sz, _sz, _p, _p, _p, _p],
+    "tc_fused": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _p, _u32, _p],
     "tc_matmul_epilogue": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p],
     "tc_vecmat_noalloc": [_i, _sz, _sz, _p, _p, _p, _p],
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],

@@ -1,0 +1,224 @@
+"""Fused elementwise programs (Kernels::fused, kernels.rs:1077-1082; the
+bytecode of fused/mod.rs:290-313) through tc_fused, against the oracle's
+restatement of the Host interpreter (fused/mod.rs:4055-4260).  The oracle's
+interpreter is pinned first against the oracle's own unfused kernels (the
+Sgd and Adam programs, elementwise and broadcast programs) on the CPU."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tensorcrate_b200 import _native as N
+from util import DTYPES, normal, uniform
+
+I = N
+
+
+def ins(code, dst=0, a=0, b=0, op=0, slot=0, value=0.0):
+    x = N.Instr()
+    x.code, x.dst, x.a, x.b, x.op, x.slot, x.value = code, dst, a, b, op, slot, value
+    return x
+
+
+def load(dst, slot):
+    return ins(N.I_LOAD, dst=dst, slot=slot)
+
+
+def const(dst, value):
+    return ins(N.I_CONST, dst=dst, value=value)
+
+
+def binary(dst, op, a, b):
+    return ins(N.I_BINARY, dst=dst, a=a, b=b, op=op)
+
+
+def unary(dst, op, a):
+    return ins(N.I_UNARY, dst=dst, a=a, op=op)
+
+
+def cmp(dst, op, a, b):
+    return ins(N.I_CMP, dst=dst, a=a, b=b, op=op)
+
+
+def store(src, slot):
+    return ins(N.I_STORE, a=src, slot=slot)
+
+
+def place(ptr, dtype, rows, cols, offset=0, col_step=1, row_step=None):
+    """A place reading `rows` rows `row_step` apart (default: in order)."""
+    p = N.Place()
+    p.data, p.dtype, p.lead, p.offset, p.col_step = ptr, N.DTYPES[dtype], 1, offset, col_step
+    p.dims[0], p.steps[0] = rows, cols if row_step is None else row_step
+    return p
+
+
+def run_oracle(dtype, rows, cols, code, places_host, outs_host, out_dtypes):
+    """orc_fused over host arrays: places_host = [(array, dtype, offset, col_step, row_step)]."""
+    pl = (N.Place * len(places_host))(*[place(a.ctypes.data, d, rows, cols, o, cs, rs)
+                                         for a, d, o, cs, rs in places_host])
+    code_arr = (N.Instr * len(code))(*code)
+    outs = (C.c_void_p * len(outs_host))(*[o.ctypes.data for o in outs_host])
+    dts = (C.c_int * len(out_dtypes))(*[N.DTYPES[d] for d in out_dtypes])
+    O.call("orc_fused", O.DTYPES[dtype], rows, cols, C.cast(code_arr, C.c_void_p), len(code), C.cast(pl, C.c_void_p),
+           len(places_host), C.cast(outs, C.c_void_p), C.cast(dts, C.c_void_p), len(outs_host))
+
+
+def test_oracle_interpreter_matches_the_oracle_sgd_and_adam():
+    """The oracle's interpreter, fed the programs Sgd and Adam build
+    (optim.rs:773-787, 1048-1099), gives the oracle's optimizer results."""
+    for dtype in DTYPES:
+        n = 1000
+        p0 = O.narrow(normal(n, 1), dtype)
+        g = O.narrow(normal(n, 2) * 0.1, dtype)
+        rate = float(O.widen(O.narrow(np.array([1e-2], np.float32), dtype), dtype)[0])
+        want = p0.copy()
+        O.call("orc_sgd", O.DTYPES[dtype], n, O.ptr(want), O.ptr(g), rate)
+        got = np.empty_like(p0)
+        code = [load(0, 0), load(1, 1), const(2, rate), binary(3, N.MUL, 1, 2), binary(4, N.SUB, 0, 3), store(4, 0)]
+        run_oracle(dtype, 1, n, code, [(p0, dtype, 0, 1, n), (g, dtype, 0, 1, n)], [got], [dtype])
+        assert np.array_equal(got, want)
+        beta2 = 0.99 if dtype == "bf16" else 0.999
+        coef = O.adam_coefficients(dtype, 1e-3, 0.9, beta2, 1e-8, 2)
+        m0, v0 = O.narrow(normal(n, 3) * 0.01, dtype), O.narrow(np.abs(normal(n, 4)) * 1e-4, dtype)
+        wp, wm, wv = p0.copy(), m0.copy(), v0.copy()
+        O.call("orc_adam", O.DTYPES[dtype], n, O.ptr(wp), O.ptr(g), O.ptr(wm), O.ptr(wv), 1, *coef)
+        outs = [np.empty_like(p0) for _ in range(3)]
+        run_oracle(dtype, 1, n, adam_program(dtype, coef),
+                   [(p0, dtype, 0, 1, n), (g, dtype, 0, 1, n), (m0, dtype, 0, 1, n), (v0, dtype, 0, 1, n)],
+                   outs, [dtype] * 3)
+        for got_x, want_x in zip(outs, (wp, wm, wv)):
+            assert np.array_equal(got_x, want_x), dtype
+
+
+def adam_program(dtype, coef):
+    """Adam's resumed-step program in the order optim.rs:1048-1099 builds it."""
+    rate, b1, b2, eps, c1, c2 = coef
+    one = lambda x: float(O.widen(O.narrow(np.array([x], np.float32), dtype), dtype)[0])
+    s1, s2 = one(1.0 - np.float32(b1)), one(1.0 - np.float32(b2))
+    return [load(0, 0), load(1, 1), load(2, 2), load(3, 3),
+            const(4, s1), binary(5, N.MUL, 1, 4),            # fresh_first = g*(1-b1)
+            binary(6, N.MUL, 1, 1),                          # squared
+            const(7, s2), binary(8, N.MUL, 6, 7),            # fresh_second
+            const(9, b1), binary(10, N.MUL, 2, 9), binary(11, N.ADD, 10, 5),   # first
+            const(9, b2), binary(10, N.MUL, 3, 9), binary(12, N.ADD, 10, 8),   # second
+            const(9, c1), binary(13, N.MUL, 11, 9),          # first*c1
+            const(9, c2), binary(14, N.MUL, 12, 9), unary(14, N.SQRT, 14),
+            const(9, eps), binary(14, N.ADD, 14, 9), binary(13, N.DIV, 13, 14),
+            const(9, rate), binary(13, N.MUL, 13, 9), binary(0, N.SUB, 0, 13),
+            store(0, 0), store(11, 1), store(12, 2)]
+
+
+def test_oracle_interpreter_matches_elementwise_and_broadcast():
+    rows, cols = 7, 300
+    for dtype in DTYPES:
+        x = O.narrow(normal(rows * cols, 5), dtype)
+        bias = O.narrow(normal(cols, 6), dtype)
+        want = np.empty_like(x)
+        O.call("orc_strided_binary", O.DTYPES[dtype], N.PAIR_ARITHMETIC, N.MUL, 2, O.sizes([rows, cols]), O.ptr(x),
+               x.size, 0, O.sizes([cols, 1]), O.ptr(bias), bias.size, 0, O.sizes([0, 1]), O.ptr(want))
+        got = np.empty_like(x)
+        run_oracle(dtype, rows, cols, [load(0, 0), load(1, 1), binary(2, N.MUL, 0, 1), store(2, 0)],
+                   [(x, dtype, 0, 1, cols), (bias, dtype, 0, 1, 0)], [got], [dtype])
+        assert np.array_equal(got, want)
+
+
+# ---------------------------------------------------------------------------
+# GPU: tc_fused against the oracle
+# ---------------------------------------------------------------------------
+def run_gpu(dtype, rows, cols, code, places_dev, out_dev, out_dtypes):
+    from tensorcrate_b200 import cuda
+    pl = (N.Place * len(places_dev))(*[place(s.ptr, d, rows, cols, o, cs, rs) for s, d, o, cs, rs in places_dev])
+    code_arr = (N.Instr * len(code))(*code)
+    outs = (C.c_void_p * len(out_dev))(*[o.ptr for o in out_dev])
+    dts = (C.c_int * len(out_dtypes))(*[N.DTYPES[d] for d in out_dtypes])
+    N.call("tc_fused", N.DTYPES[dtype], rows, cols, code_arr, len(code), pl, len(places_dev), outs, dts,
+           len(out_dev), None)
+    cuda.synchronize()
+
+
+def same_bits(a, b, dtype):
+    wa, wb = O.widen(a, dtype), O.widen(b, dtype)
+    return bool(np.all((a == b) | (np.isnan(wa) & np.isnan(wb))))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_fused_programs_match_the_oracle(device, dtype):
+    """Arithmetic, remainders, comparisons, min/max, a row-broadcast load, a
+    permuted (transposed) load, a second storage type (an f32 input and an
+    f32 output of a 16-bit program), square roots: bit for bit."""
+    from tensorcrate_b200 import cuda
+    rows, cols = 96, 130
+    x = O.narrow(normal(rows * cols, 11), dtype)
+    y = O.narrow(uniform(rows * cols, 12) * 3, dtype)
+    bias = O.narrow(normal(cols, 13), dtype)
+    xt = np.ascontiguousarray(x.reshape(rows, cols).T).reshape(-1)   # read back through a transposed place
+    w32 = normal(rows * cols, 14)                                     # an f32 storage
+    code = [load(0, 0), load(1, 1), load(2, 2), load(3, 3), load(4, 4),
+            binary(5, N.ADD, 0, 2), binary(5, N.MUL, 5, 1), binary(6, N.DIV, 5, 1), binary(7, N.REM, 6, 1),
+            cmp(8, N.GREATER, 0, 1), cmp(9, N.MAX, 7, 3), cmp(10, N.MAX_SHARE, 0, 4), cmp(11, N.MIN, 9, 4),
+            binary(12, N.SUB, 3, 0),                                   # the transposed load equals x: exact zeros
+            unary(13, N.SQRT, 1), const(14, 0.75), binary(13, N.MUL, 13, 14), binary(13, N.ADD, 13, 4),
+            store(5, 0), store(7, 1), store(8, 2), store(11, 3), store(10, 4), store(12, 5), store(13, 6)]
+    out_dtypes = [dtype, dtype, dtype, dtype, dtype, dtype, "f32"]
+    host_places = [(x, dtype, 0, 1, cols), (y, dtype, 0, 1, cols), (bias, dtype, 0, 1, 0),
+                   (xt, dtype, 0, rows, 1), (w32, "f32", 0, 1, cols)]
+    want = [np.empty(rows * cols, O.STORE[d] if d != "f32" else np.float32) for d in out_dtypes]
+    run_oracle(dtype, rows, cols, code, host_places, want, out_dtypes)
+    dev_places = [(cuda.CudaStorage.store(a, d), d, o, cs, rs) for a, d, o, cs, rs in host_places]
+    got = [cuda.CudaStorage(d, rows * cols) for d in out_dtypes]
+    run_gpu(dtype, rows, cols, code, dev_places, got, out_dtypes)
+    for k, (g, w, d) in enumerate(zip(got, want, out_dtypes)):
+        assert same_bits(g.as_slice(), w, d), k
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_fused_adam_program_matches_the_adam_kernel(device, dtype):
+    """Adam's program run by the interpreter, updating p, m and v in place,
+    gives the bits of tc_adam (the dedicated kernel)."""
+    from tensorcrate_b200 import cuda
+    n = 5000
+    beta2 = 0.99 if dtype == "bf16" else 0.999
+    coef = O.adam_coefficients(dtype, 1e-3, 0.9, beta2, 1e-8, 2)
+    p0 = O.narrow(normal(n, 21), dtype)
+    g = O.narrow(normal(n, 22) * 0.1, dtype)
+    m0, v0 = O.narrow(normal(n, 23) * 0.01, dtype), O.narrow(np.abs(normal(n, 24)) * 1e-4, dtype)
+    a = {k: cuda.CudaStorage.store(v, dtype) for k, v in (("p", p0), ("g", g), ("m", m0), ("v", v0))}
+    b = {k: cuda.CudaStorage.store(v, dtype) for k, v in (("p", p0), ("g", g), ("m", m0), ("v", v0))}
+    N.call("tc_adam", N.DTYPES[dtype], n, a["p"].ptr, a["g"].ptr, a["m"].ptr, a["v"].ptr, 1, *coef, None)
+    places = [(b[k], dtype, 0, 1, n) for k in ("p", "g", "m", "v")]
+    run_gpu(dtype, 1, n, adam_program(dtype, coef), places, [b["p"], b["m"], b["v"]], [dtype] * 3)
+    for k in ("p", "m", "v"):
+        assert same_bits(a[k].as_slice(), b[k].as_slice(), dtype), k
+
+
+@pytest.mark.gpu
+def test_fused_transcendentals_within_two_ulp(device):
+    """Unary Analytic functions of an f32 program: within 2 ulp of the
+    exactly rounded value (f64), sec and csc within 3 (two roundings)."""
+    from tensorcrate_b200 import cuda
+    n = 4096
+    x = uniform(n, 31).astype(np.float32) * 0.9
+    funcs = [(N.SIN, np.sin), (N.COS, np.cos), (N.TAN, np.tan), (N.SEC, lambda v: 1 / np.cos(v)),
+             (N.CSC, lambda v: 1 / np.sin(v)), (N.ARCSIN, np.arcsin), (N.ARCCOS, np.arccos),
+             (N.ARCTAN, np.arctan), (N.EXP, np.exp), (N.LN, lambda v: np.log(np.abs(v) + 0.1)),
+             (N.SINH, np.sinh), (N.COSH, np.cosh), (N.TANH, np.tanh), (N.SQRT, lambda v: np.sqrt(np.abs(v)))]
+    xs = cuda.CudaStorage.store(x, "f32")
+    absx = cuda.CudaStorage.store(np.abs(x) + np.float32(0.1), "f32")
+    for op, f in funcs:
+        src = absx if op == N.LN else xs
+        arg = np.abs(x) + np.float32(0.1) if op == N.LN else x
+        if op == N.SQRT:
+            src, arg = cuda.CudaStorage.store(np.abs(x), "f32"), np.abs(x)
+        out = cuda.CudaStorage("f32", n)
+        run_gpu("f32", 1, n, [load(0, 0), unary(1, op, 0), store(1, 0)], [(src, "f32", 0, 1, n)], [out], ["f32"])
+        got = out.as_slice().astype(np.float64)
+        exact = (np.log(arg.astype(np.float64)) if op == N.LN else f(arg.astype(np.float64)))
+        ulp = np.spacing(np.abs(exact).astype(np.float32)).astype(np.float64)
+        limit = 0.0 if op == N.SQRT else (3.0 if op in (N.SEC, N.CSC) else 2.0)
+        err = np.abs(got - exact) / ulp
+        assert np.max(err) <= limit + 0.5, (op, float(np.max(err)))
