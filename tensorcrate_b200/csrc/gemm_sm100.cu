@@ -664,8 +664,16 @@ __global__ void __launch_bounds__(256) splitk_finish(const float *partial, int r
                           finish_one<T>(v.y, c, i + 1, accumulate, share_of, b, bias, relu_out),
                           finish_one<T>(v.z, c, i + 2, accumulate, share_of, b, bias, relu_out),
                           finish_one<T>(v.w, c, i + 3, accumulate, share_of, b, bias, relu_out)};
+      if (sizeof(typename T::S) == 2 && (reinterpret_cast<uintptr_t>(c) & 7u) == 0) {
+        // the four results in one 8-byte store
+        union { uint2 raw; typename T::S e[4]; } w;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) c[i + j] = T::store(o[j]);
+        for (int j = 0; j < 4; ++j) w.e[j] = T::store(o[j]);
+        *reinterpret_cast<uint2 *>(c + i) = w.raw;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[i + j] = T::store(o[j]);
+      }
     }
     return;
   }

@@ -33,12 +33,23 @@ __global__ void __launch_bounds__(256) matvec_rows(const typename T::S *m, const
     const typename T::S *row = m + r * cols;
     float s = 0.0f;
     if (vec) {
-      for (long long p = lane; p < cols / N; p += 32) {
-        Pack<T> a, b;
-        a.raw = __ldg(reinterpret_cast<const uint4 *>(row + p * N));
-        b.raw = __ldg(reinterpret_cast<const uint4 *>(x + p * N));
+      // Four packs in flight per lane, folded in the same order as one at a time.
+      constexpr int U = 4;
+      const long long packs = cols / N;
+      for (long long p0 = lane; p0 < packs; p0 += 32 * U) {
+        Pack<T> a[U], b[U];
 #pragma unroll
-        for (int j = 0; j < N; ++j) s = fmaf(T::load(a.v[j]), T::load(b.v[j]), s);
+        for (int u = 0; u < U; ++u)
+          if (p0 + 32 * u < packs) {
+            a[u].raw = __ldg(reinterpret_cast<const uint4 *>(row + (p0 + 32 * u) * N));
+            b[u].raw = __ldg(reinterpret_cast<const uint4 *>(x + (p0 + 32 * u) * N));
+          }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (p0 + 32 * u < packs) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) s = fmaf(T::load(a[u].v[j]), T::load(b[u].v[j]), s);
+          }
       }
     } else {
       for (long long c = lane; c < cols; c += 32) s = fmaf(T::load(row[c]), T::load(x[c]), s);
@@ -68,15 +79,27 @@ __global__ void __launch_bounds__(256) vecmat_cols(const typename T::S *x, const
 #pragma unroll
   for (int c = 0; c < CPT; ++c) s[c] = 0.0f;
   if (j0 < cols) {
-    for (long long p = r0 + threadIdx.y; p < r1; p += 8) {
-      const float xp = T::load(x[p]);
+    // Four rows in flight per thread, folded in row order as one at a time.
+    constexpr int U = 4;
+    for (long long p0 = r0 + threadIdx.y; p0 < r1; p0 += 8 * U) {
       if (CPT > 1) {
-        union { uint4 raw; S v[16 / sizeof(S)]; } pk;
-        pk.raw = __ldg(reinterpret_cast<const uint4 *>(m + p * cols + j0));
+        union Pk { uint4 raw; S v[16 / sizeof(S)]; } pk[U];
+        float xp[U];
 #pragma unroll
-        for (int c = 0; c < CPT; ++c) s[c] = fmaf(xp, T::load(pk.v[c]), s[c]);
+        for (int u = 0; u < U; ++u)
+          if (p0 + 8 * u < r1) {
+            xp[u] = T::load(x[p0 + 8 * u]);
+            pk[u].raw = __ldg(reinterpret_cast<const uint4 *>(m + (p0 + 8 * u) * cols + j0));
+          }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (p0 + 8 * u < r1) {
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) s[c] = fmaf(xp[u], T::load(pk[u].v[c]), s[c]);
+          }
       } else {
-        s[0] = fmaf(xp, T::load(__ldg(m + p * cols + j0)), s[0]);
+        for (int u = 0; u < U; ++u)
+          if (p0 + 8 * u < r1) s[0] = fmaf(T::load(x[p0 + 8 * u]), T::load(__ldg(m + (p0 + 8 * u) * cols + j0)), s[0]);
       }
     }
   }

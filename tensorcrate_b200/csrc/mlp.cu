@@ -116,6 +116,10 @@ struct tc_mlp {
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> grad_ready;
   cudaEvent_t reduced = nullptr;
+  // The bias adjoints (matvec, vecmat: memory-bound) run on a side stream,
+  // beside each layer's products.
+  cudaStream_t side = nullptr;
+  std::vector<cudaEvent_t> abar_ready, side_done;
   bool prune = false;
 };
 
@@ -191,12 +195,19 @@ int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t bat
     tc_mlp_destroy(m);
     return rc;
   }
+  if ((rc = check_cuda(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking), "stream"))) {
+    tc_mlp_destroy(m);
+    return rc;
+  }
   m->grad_ready.resize(m->layers);
-  for (auto &ev : m->grad_ready)
-    if ((rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event"))) {
-      tc_mlp_destroy(m);
-      return rc;
-    }
+  m->abar_ready.resize(m->layers);
+  m->side_done.resize(m->layers);
+  for (auto *evs : {&m->grad_ready, &m->abar_ready, &m->side_done})
+    for (auto &ev : *evs)
+      if ((rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event"))) {
+        tc_mlp_destroy(m);
+        return rc;
+      }
   *out = m;
   return TC_OK;
 }
@@ -213,10 +224,12 @@ int tc_mlp_destroy(tc_mlp *m) {
   for (Buf *b : {&m->ones, &m->S, &m->Rbar, &m->Ybar, &m->Xbar, &m->abar,
                  &m->inbar, &m->onesbar, &m->ovec, &m->loss_sum})
     drop(*b);
-  for (auto ev : m->grad_ready)
-    if (ev) cudaEventDestroy(ev);
+  for (auto *evs : {&m->grad_ready, &m->abar_ready, &m->side_done})
+    for (auto ev : *evs)
+      if (ev) cudaEventDestroy(ev);
   if (m->reduced) cudaEventDestroy(m->reduced);
   if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+  if (m->side) cudaStreamDestroy(m->side);
   delete m;
   return TC_OK;
 }
@@ -300,28 +313,46 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     const size_t in = m->dims[l], outd = m->dims[l + 1];
     const void *input = l == 0 ? x : m->H[l - 1].p;
     // A = Z + O: Z̄ = Ō = Ā (shared).  O = b ⊗ ones: b̄ += Ō·ones,
-    // ones̄ += bᵀ·Ō (vecmat), accumulated in node order.
-    TRY(tc_matvec(d, outd, B, abar, m->ones.p, m->gb[l].p, 0, st));
+    // ones̄ += bᵀ·Ō (vecmat), accumulated in node order.  These read Ā
+    // only, so they run on the side stream while the products below run
+    // here; the side stream's vecmat keeps its partial sums in the static
+    // array of tc_vecmat_noalloc (the per-device scratch belongs to this
+    // stream's split-K products), and a shape too large for it runs here.
+    TRY(check_cuda(cudaEventRecord(m->abar_ready[l], s), "event"));
+    TRY(check_cuda(cudaStreamWaitEvent(m->side, m->abar_ready[l], 0), "wait"));
+    TRY(tc_matvec(d, outd, B, abar, m->ones.p, m->gb[l].p, 0, m->side));
     if (!m->prune) {
-      if (l == L - 1) TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, m->onesbar.p, st));
-      else {
-        TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, m->ovec.p, st));
-        TRY(tc_elementwise(d, TC_ADD, m->onesbar.p, m->ovec.p, m->onesbar.p, B, st));
+      void *dst = l == L - 1 ? m->onesbar.p : m->ovec.p;
+      int vst = tc_vecmat_noalloc(d, outd, B, m->b[l].p, abar, dst, m->side);
+      if (vst == TC_ERANGE) {
+        // Too large for the static array: join, and run it on this stream.
+        TRY(check_cuda(cudaEventRecord(m->side_done[l], m->side), "event"));
+        TRY(check_cuda(cudaStreamWaitEvent(s, m->side_done[l], 0), "wait"));
+        TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, dst, st));
+        TRY(check_cuda(cudaEventRecord(m->abar_ready[l], s), "event"));
+        TRY(check_cuda(cudaStreamWaitEvent(m->side, m->abar_ready[l], 0), "wait"));
+      } else if (vst) {
+        return vst;
       }
+      if (l != L - 1) TRY(tc_elementwise(d, TC_ADD, m->onesbar.p, m->ovec.p, m->onesbar.p, B, m->side));
     }
+    TRY(check_cuda(cudaEventRecord(m->side_done[l], m->side), "event"));
     // Z = W·IN: W̄ += Z̄·INᵀ, ĪN += Wᵀ·Z̄ (matmul_transposed_add, both
     // adjoints starting from zero).
     TRY(tc_matmul(d, TC_TRANS_RIGHT, outd, B, in, abar, input, m->gW[l].p, 0, st));
     if (comm) {
       TRY(check_cuda(cudaEventRecord(m->grad_ready[l], s), "event"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0), "wait"));
+      TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->side_done[l], 0), "wait"));
       TRY(tc_allreduce(comm, d, m->gW[l].p, m->gW[l].n, TC_SUM, m->comm_stream));
       TRY(tc_allreduce(comm, d, m->gb[l].p, m->gb[l].n, TC_SUM, m->comm_stream));
     }
     if (l > 0) {
       // H̄ = Wᵀ·Z̄, then H = relu(A): Ā += H̄ · MaxShare(A, 0).  Ā of the
-      // layer below goes to the buffer this layer's Ā does not use.
+      // layer below goes to the buffer this layer's Ā does not use, which
+      // the layer above's side work read: wait for that first.
       void *next = abar == m->abar.p ? m->inbar.p : m->abar.p;
+      if (l + 1 < L) TRY(check_cuda(cudaStreamWaitEvent(s, m->side_done[l + 1], 0), "wait"));
       TRY(tc_matmul_epilogue(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->A[l - 1].p, nullptr, next,
                              nullptr, st));
       abar = next;
@@ -329,6 +360,9 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
       TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->Xbar.p, 0, st));
     }
   }
+  // Every side-stream result (b̄, ones̄) is complete before Adam and the
+  // caller see them.
+  TRY(check_cuda(cudaStreamWaitEvent(s, m->side_done[0], 0), "wait"));
   if (comm) {
     TRY(check_cuda(cudaEventRecord(m->reduced, m->comm_stream), "event"));
     TRY(check_cuda(cudaStreamWaitEvent(s, m->reduced, 0), "wait"));
