@@ -4,6 +4,10 @@
 #include "common.cuh"
 
 namespace tc {
+// SMs the persistent tensor-core kernels leave free on this thread's
+// launches (for kernels that must run beside them, such as a collective's).
+void gemm_reserve_sms(int n);
+int reserved_sms();
 int gemm_simt_run(int dtype, int transposed, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
                   void *c, bool accumulate, cudaStream_t stream);
 // TC_ENOTSUP when the shape or alignment is not one the tensor-core kernel

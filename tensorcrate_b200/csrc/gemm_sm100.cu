@@ -36,6 +36,12 @@ namespace tc {
 __device__ int g_gemm_fault = 0;
 
 namespace {
+thread_local int t_reserved_sms = 0;
+}
+void gemm_reserve_sms(int n) { t_reserved_sms = n < 0 ? 0 : n; }
+int reserved_sms() { return t_reserved_sms; }
+
+namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 f16/bf16 = 128 bytes: one swizzle row
@@ -199,6 +205,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *acc_full = empty + STAGES;
   uint64_t *acc_empty = acc_full + 2;
   uint64_t *drain = acc_empty + 2;
+  // Epilogue staging for stores to peers: per epilogue warp, 32 rows of 64
+  // 16-bit values (128 bytes, padded to 144), after the barrier block.
+  uint16_t *epi_stage = reinterpret_cast<uint16_t *>(smem + STAGES * STAGE_BYTES + 256);
   __shared__ uint32_t tmem_base_slot;
   __shared__ volatile int abort_flag;
 
@@ -355,6 +364,52 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = mb * BM + q * 32 + lane;
       const int n0 = nb * BN;
       const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
+      if (!TF32 && p.n_peers) {
+        // Stores to peers: each 32-row x 64-column piece goes through
+        // shared memory, so the warp writes whole 128-byte row segments
+        // (four rows per instruction) to C and to every peer's C, rather
+        // than 16 bytes per row per lane.  N is a multiple of 8 here.
+        constexpr int PITCH = 72;  // 16-bit values per staged row
+        uint16_t *stage = epi_stage + q * 32 * PITCH;
+#pragma unroll 1
+        for (int c2 = 0; c2 < BN / 64; ++c2) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[32];
+            tmem_ld32(taddr + uint32_t(c2 * 64 + h * 32), r);
+            uint4 *dstp = reinterpret_cast<uint4 *>(stage + lane * PITCH + h * 32);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float a = __uint_as_float(r[8 * k + 2 * e]), b = __uint_as_float(r[8 * k + 2 * e + 1]);
+                w[e] = p.elem_is_bf16 ? pack2_bf16(a, b) : pack2_f16(a, b);
+              }
+              dstp[k] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+          __syncwarp();
+          const int col0 = n0 + c2 * 64;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3), seg = lane & 7;
+            const int grow = mb * BM + q * 32 + rr, gcol = col0 + seg * 8;
+            const uint4 val = *reinterpret_cast<const uint4 *>(stage + rr * PITCH + seg * 8);
+            if (grow < p.M && gcol < p.N) {
+              const size_t off = size_t(grow) * size_t(p.N) + size_t(gcol);
+              *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.c) + off) = val;
+#pragma unroll
+              for (int i = 0; i < MAX_PEERS; ++i)
+                if (i < p.n_peers) *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.peer_c[i]) + off) = val;
+            }
+          }
+          __syncwarp();
+        }
+        fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       if (S > 1) {
         // One K range of a split tile: the raw f32 accumulator.
         float *prow = p.partial + (size_t(ks) * size_t(p.M) + size_t(row)) * size_t(p.N);
@@ -611,7 +666,9 @@ __global__ void __launch_bounds__(256) split_tf32(const float *src, long long R,
 
 template <int BN, int STAGES, bool TF32 = false>
 int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, cudaStream_t stream) {
-  constexpr size_t smem = size_t(STAGES) * (BM * 128 + BN * 128) + 1024 + 256;
+  // tiles, 1024 bytes of alignment slack, the barriers (256), the epilogue
+  // staging (4 warps x 32 rows x 144 bytes)
+  constexpr size_t smem = size_t(STAGES) * (BM * 128 + BN * 128) + 1024 + 256 + 4 * 32 * 144;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -623,7 +680,7 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, cudaSt
     configured[dev & 63] = true;
   }
   const int units = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN) * std::max(1, p.ksplit);
-  const int grid = std::min(units, sm_count());
+  const int grid = std::min(units, std::max(1, sm_count() - reserved_sms()));
   gemm_tc<BN, STAGES, TF32><<<grid, THREADS, smem, stream>>>(ma, mb, p);
   return check_launch("gemm (tcgen05)");
 }
@@ -762,6 +819,8 @@ int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_
     p.peer_c[i] = i < n_peers ? peer_c[i] : nullptr;
     if (i < n_peers && (uintptr_t(peer_c[i]) & 15u)) p.vec_store = 0;
   }
+  // The peer epilogue stores 16-byte segments: rows of C 16-byte aligned.
+  if (n_peers && (!p.vec_store || cols % 8)) return TC_ENOTSUP;
   const int k_blocks = int((inner + BK - 1) / BK);
   const Plan pl = plan_tiles((long long)rows, (long long)cols, k_blocks, n_peers == 0);
   const int BN = pl.bn;

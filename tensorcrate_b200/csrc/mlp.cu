@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm.cuh"
 
 struct tc_comm;
 
@@ -292,6 +293,12 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   }
   const size_t last = m->dims[L];
   const float factor = round_to(d, 1.0 / (double(last) * double(m->global_batch)));
+  // With a communicator, the gradient all-reduces run beside the backward
+  // products: leave them SMs (the products' CTAs fill an SM's shared memory).
+  struct Reserve {
+    explicit Reserve(bool on) { gemm_reserve_sms(on ? 16 : 0); }
+    ~Reserve() { gemm_reserve_sms(0); }
+  } reserve(comm != nullptr);
   // Loss and the top of the backward pass (frobenius_dot, scale, sum's and
   // Mul's and Sub's rules) in one pass.
   TRY(with_real(d, [&](auto t) {
