@@ -316,8 +316,9 @@ int tc_mlp_grads(tc_mlp *mlp, uint32_t layer, void *gw_host, void *gb_host);
  * default, as the tape computes them. */
 int tc_mlp_prune_leaves(tc_mlp *mlp, int prune);
 /* Forward, loss into loss_dev[0] if not NULL, backward, NCCL gradient
- * all-reduce over `comm` if not NULL (overlapped with the backward pass),
- * then Adam on every parameter.  x, y are device buffers. */
+ * all-reduce over `comm` if not NULL (each layer's as soon as the backward
+ * pass has produced it, beside the rest of the pass), then Adam on every
+ * parameter.  x, y are device buffers. */
 int tc_mlp_step(tc_mlp *mlp, const void *x_dev, const void *y_dev, tc_comm *comm, void *loss_dev,
                 void *stream);
 
@@ -376,6 +377,13 @@ int tc_allgather(tc_comm *comm, int dtype, const void *send, void *recv, size_t 
                  void *stream);
 /* In-place all-reduce of `count` elements; op is tc_reduce. */
 int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void *stream);
+/* Reduce nranks*count elements of `send` over the ranks, rank r keeping
+ * elements [r*count, (r+1)*count) of the result in `recv` (which may be
+ * send + r*count); op is tc_reduce. */
+int tc_reducescatter(tc_comm *comm, int dtype, const void *send, void *recv, size_t count, int op,
+                     void *stream);
+/* This rank and the number of ranks. */
+int tc_comm_rank(tc_comm *comm, int *rank, int *nranks);
 
 /* A device buffer of `bytes` on every rank, each rank also mapping every
  * other rank's (CUDA IPC over NVLink).  Create and destroy are collective:

@@ -121,6 +121,8 @@ SIGNATURES = {
     "tc_comm_destroy": [_p],
     "tc_allgather": [_p, _i, _p, _p, _sz, _p],
     "tc_allreduce": [_p, _i, _p, _sz, _i, _p],
+    "tc_reducescatter": [_p, _i, _p, _p, _sz, _i, _p],
+    "tc_comm_rank": [_p, _p, _p],
     "tc_peer_buffer_create": [_p, _sz, _p],
     "tc_peer_buffer_pointer": [_p, _p],
     "tc_peer_buffer_destroy": [_p],

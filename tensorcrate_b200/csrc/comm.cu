@@ -28,6 +28,8 @@ struct Nccl {
   ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*reduce_scatter)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                                 cudaStream_t) = nullptr;
 };
 
 Nccl &nccl() {
@@ -45,7 +47,9 @@ Nccl &nccl() {
     n.abort = (ncclResult_t(*)(ncclComm_t))dlsym(h, "ncclCommAbort");
     n.all_gather = (decltype(n.all_gather))dlsym(h, "ncclAllGather");
     n.all_reduce = (decltype(n.all_reduce))dlsym(h, "ncclAllReduce");
-    n.ok = n.error_string && n.get_unique_id && n.init_rank && n.destroy && n.abort && n.all_gather && n.all_reduce;
+    n.reduce_scatter = (decltype(n.reduce_scatter))dlsym(h, "ncclReduceScatter");
+    n.ok = n.error_string && n.get_unique_id && n.init_rank && n.destroy && n.abort && n.all_gather && n.all_reduce &&
+           n.reduce_scatter;
   });
   return n;
 }
@@ -119,6 +123,23 @@ int tc_allgather(tc_comm *comm, int dtype, const void *send, void *recv, size_t 
   ncclDataType_t t = ncclFloat32;
   if (int st = nccl_type(dtype, &t)) return st;
   return check_nccl(nccl().all_gather(send, recv, count, t, comm->comm, as_stream(stream)), "ncclAllGather");
+}
+
+int tc_comm_rank(tc_comm *comm, int *rank, int *nranks) {
+  if (!comm || !rank || !nranks) return fail(TC_EINVAL, "tc_comm_rank: null");
+  *rank = comm->rank;
+  *nranks = comm->nranks;
+  return TC_OK;
+}
+
+int tc_reducescatter(tc_comm *comm, int dtype, const void *send, void *recv, size_t count, int op, void *stream) {
+  if (!comm) return fail(TC_EINVAL, "reducescatter: null communicator");
+  ncclDataType_t t = ncclFloat32;
+  if (int st = nccl_type(dtype, &t)) return st;
+  ncclRedOp_t r = op == TC_SUM ? ncclSum : op == TC_RMIN ? ncclMin : op == TC_RMAX ? ncclMax : ncclNumOps;
+  if (r == ncclNumOps) return fail(TC_EINVAL, "reducescatter: bad Reduce %d", op);
+  return check_nccl(nccl().reduce_scatter(send, recv, count, t, r, comm->comm, as_stream(stream)),
+                    "ncclReduceScatter");
 }
 
 int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void *stream) {

@@ -114,6 +114,11 @@ struct tc_mlp {
   std::vector<Buf> W, b, gW, gb, mW, vW, mb, vb;
   std::vector<Buf> A, H;
   Buf ones, S, Rbar, Ybar, Xbar, abar, inbar, onesbar, ovec, loss_sum;
+  // Every layer's gradients in one allocation, [gW_l | gb_l] side by side
+  // (each 16-byte aligned, the gap zeroed), so that one all-reduce moves a
+  // layer's gradients: gW[l].p and gb[l].p point into it.
+  Buf grads;
+  std::vector<size_t> layer_span;  // elements from gW[l].p to the end of gb[l]
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> grad_ready;
   cudaEvent_t reduced = nullptr;
@@ -169,10 +174,32 @@ int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t bat
     m->W.emplace_back(); m->b.emplace_back(); m->gW.emplace_back(); m->gb.emplace_back();
     m->mW.emplace_back(); m->vW.emplace_back(); m->mb.emplace_back(); m->vb.emplace_back();
     m->A.emplace_back(); m->H.emplace_back();
-    need(m->W[l], outd * in); need(m->gW[l], outd * in); need(m->mW[l], outd * in); need(m->vW[l], outd * in);
-    need(m->b[l], outd); need(m->gb[l], outd); need(m->mb[l], outd); need(m->vb[l], outd);
+    need(m->W[l], outd * in); need(m->mW[l], outd * in); need(m->vW[l], outd * in);
+    need(m->b[l], outd); need(m->mb[l], outd); need(m->vb[l], outd);
     need(m->A[l], outd * B);
     if (l + 1 < m->layers) need(m->H[l], outd * B);
+  }
+  {
+    const size_t align = 16 / e;  // elements per 16 bytes
+    auto up = [&](size_t n) { return (n + align - 1) / align * align; };
+    size_t total = 0;
+    std::vector<size_t> at_w(layers), at_b(layers);
+    for (uint32_t l = 0; l < layers; ++l) {
+      at_w[l] = total;
+      total += up(m->dims[l + 1] * m->dims[l]);
+      at_b[l] = total;
+      total += up(m->dims[l + 1]);
+    }
+    need(m->grads, total);
+    if (!st) st = check_cuda(cudaMemset(m->grads.p, 0, total * e), "cudaMemset");
+    m->layer_span.resize(layers);
+    for (uint32_t l = 0; l < layers && !st; ++l) {
+      m->gW[l].p = static_cast<char *>(m->grads.p) + at_w[l] * e;
+      m->gW[l].n = m->dims[l + 1] * m->dims[l];
+      m->gb[l].p = static_cast<char *>(m->grads.p) + at_b[l] * e;
+      m->gb[l].n = m->dims[l + 1];
+      m->layer_span[l] = at_b[l] + m->dims[l + 1] - at_w[l];
+    }
   }
   size_t widest = 0;
   for (size_t d : m->dims) widest = std::max(widest, d);
@@ -220,8 +247,9 @@ int tc_mlp_destroy(tc_mlp *m) {
     if (b.p) tc_free(b.p);
     b.p = nullptr;
   };
-  for (auto *v : {&m->W, &m->b, &m->gW, &m->gb, &m->mW, &m->vW, &m->mb, &m->vb, &m->A, &m->H})
+  for (auto *v : {&m->W, &m->b, &m->mW, &m->vW, &m->mb, &m->vb, &m->A, &m->H})
     for (auto &b : *v) drop(b);
+  drop(m->grads);  // gW and gb point into it
   for (Buf *b : {&m->ones, &m->S, &m->Rbar, &m->Ybar, &m->Xbar, &m->abar,
                  &m->inbar, &m->onesbar, &m->ovec, &m->loss_sum})
     drop(*b);
@@ -351,8 +379,8 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
       TRY(check_cuda(cudaEventRecord(m->grad_ready[l], s), "event"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0), "wait"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->side_done[l], 0), "wait"));
-      TRY(tc_allreduce(comm, d, m->gW[l].p, m->gW[l].n, TC_SUM, m->comm_stream));
-      TRY(tc_allreduce(comm, d, m->gb[l].p, m->gb[l].n, TC_SUM, m->comm_stream));
+      // the layer's weight and bias gradients in one call
+      TRY(tc_allreduce(comm, d, m->gW[l].p, m->layer_span[l], TC_SUM, m->comm_stream));
     }
     if (l > 0) {
       // H̄ = Wᵀ·Z̄, then H = relu(A): Ā += H̄ · MaxShare(A, 0).  Ā of the
