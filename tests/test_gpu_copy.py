@@ -233,3 +233,16 @@ def test_two_byte_transposes_with_short_and_long_tiles(device, shape, perm):
     got = t.view().permute(perm).contiguous().storage.as_slice()
     want = np.ascontiguousarray(x.reshape(shape).transpose(perm)).reshape(-1)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("shape,perm", [([3, 8, 200, 12], [0, 3, 1, 2]), ([2, 5, 4, 132, 32], [0, 4, 2, 1, 3]),
+                                        ([8, 16, 128, 64, 32], [0, 3, 1, 4, 2])])
+def test_two_byte_transposes_with_short_source_runs(device, shape, perm):
+    """Permutations whose source-contiguous axis is short (at most 32) and
+    whose other axes step in multiples of 4, ragged along the inner axis."""
+    n = int(np.prod(shape))
+    x = O.narrow(normal(n, 8), "f16")
+    t = cuda.Tensor(cuda.CudaStorage.store(x, "f16"), shape)
+    got = t.view().permute(perm).contiguous().storage.as_slice()
+    want = np.ascontiguousarray(x.reshape(shape).transpose(perm)).reshape(-1)
+    assert np.array_equal(got, want)
