@@ -399,12 +399,37 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
     ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
     if peer is not None:
         peer.close()
+    matvec = None
+    if dtype == "f32" and size == 1024:
+        # Config 1's matvec: y = M.x over 64 different [1024 x 1024] f32
+        # matrices in turn (268 MB, more than L2), so every call reads HBM.
+        mats = [cuda.CudaStorage.store(rng.uniform(-1, 1, m * k).astype(np.float32), "f32") for _ in range(64)]
+        xv = cuda.CudaStorage.store(rng.uniform(-1, 1, k).astype(np.float32), "f32")
+        yv = cuda.CudaStorage("f32", m)
+        # The 64 launches are captured in one CUDA graph, so the time is the
+        # device's and not the host's launch rate through ctypes.
+        graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+        cap.wait_stream(stream)
+        with torch.cuda.graph(graph, stream=cap):
+            csp = C.c_void_p(cap.cuda_stream)
+            for M in mats:
+                N.check("matvec", lib.tc_matvec(N.F32, m, k, M.ptr, xv.ptr, yv.ptr, 0, csp))
+        ms_mv, _ = timed(torch, world, graph.replay, 8, 3, stream)
+        ms_mv /= len(mats)
+        mv_bytes = m * k * 4 + k * 4 + m * 4
+        mv_gbs = mv_bytes / (ms_mv * 1e-3) / 1e9
+        matvec = {"us": round(ms_mv * 1e3, 2), "gbs": round(mv_gbs, 1), "frac": round(mv_gbs / peaks()[0]["hbm_gbs"], 3),
+                  "bytes": mv_bytes, "l2": "64 matrices in turn, 268 MB"}
     flops = 2.0 * m * n * k
     pk, pk_kind = peaks()
     # Whole-job TFLOP/s: replicas each do the whole product; panels share one.
     total = flops / (ms * 1e-3) / 1e12 * (1 if panels else world)
     per_gpu = total / world
-    peak = pk["bf16_tflops"] if dtype != "f32" else None
+    # f32 runs as three TF32 tensor-core passes (hi.hi + hi.lo + lo.hi): the
+    # roofline counts those passes' flops against half the bf16 rate, the
+    # tensor cores' TF32 throughput.
+    passes = 3 if dtype == "f32" else 1
+    peak = pk["bf16_tflops"] / (2 if dtype == "f32" else 1)
     workload = f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate"
     parallelism = (f"row panels x{world}, all-gather fused into the GEMM epilogue (NVLink peer stores)" if panels
                    else (f"replicas x{world}" if world > 1 else "single GPU"))
@@ -414,10 +439,14 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
             "data": "synthetic uniform[-1,1], seeded",
             "config": {"workload": workload, "parallelism": parallelism,
                        "l2": "inputs resident; the working set exceeds L2 at 8192 and above"},
-            "roofline": {"bound": "tensor" if dtype != "f32" else "fp32-simt", "kernel": "gemm_tc" if dtype != "f32"
-                         else "gemm_simt", "achieved": round(per_gpu, 1), "peak": peak, "peak_source": pk_kind,
-                         "unit": "TFLOP/s", "frac": round(per_gpu / peak, 3) if peak else None, "traffic": None},
-            "gpu_launches": args.steps, "clocks": clocks}
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc" if dtype != "f32" else "gemm_tc<tf32> x3 passes",
+                         "achieved": round(per_gpu * passes, 1), "peak": round(peak, 1),
+                         "peak_source": pk_kind if dtype != "f32" else f"{pk_kind} bf16 / 2 (TF32 rate)",
+                         "unit": "TFLOP/s", "frac": round(per_gpu * passes / peak, 3), "traffic": None},
+            # f32: two operand splits, the TF32 product, the split-K finish; bf16: the product
+            "gpu_launches": (4 if dtype == "f32" else 1) * args.steps, "clocks": clocks}
+    if matvec is not None:
+        line["config"]["matvec"] = matvec
     return line
 
 
@@ -459,16 +488,43 @@ def run_c3(args, torch, world, rank, comm):
     byts = 2 * n * 2 + 2 * m * 2
     gbs = byts / (ms * 1e-3) / 1e9
     pk, pk_kind = peaks()
+
+    # Interpretation B: the slice's indices on the original axes,
+    # x[:, 8:, :, :32, :] = [8, 8, 128, 32, 32], split in 4 along axis 1 and
+    # concatenated back (one assemble of four regions).
+    slb = t.view().slice(1, 8, shape[1]).slice(3, 0, 32)
+    cat_b = list(slb.shape)
+    to_b = cuda.contiguous_strides(cat_b)
+    regions_b, at = [], 0
+    for v in slb.chunk(1, 4):
+        regions_b.append(cuda.Cuda._region((v.storage, v.shape, v.offset, v.strides, at * to_b[1], to_b)))
+        at += v.shape[1]
+    m_b = int(np.prod(cat_b))
+    out_b = cuda.CudaStorage("f16", m_b)
+    arr_b = (N.Region * len(regions_b))(*regions_b)
+
+    def step_b():
+        N.check("assemble", lib.tc_assemble(2, out_b.ptr, m_b, arr_b, len(regions_b), C.c_void_p(sp)))
+
+    ms_b, _ = timed(torch, world, step_b, args.steps, args.warmup, stream)
+    gbs_b = 2 * m_b * 2 / (ms_b * 1e-3) / 1e9
     return {"metric": "config-3 layout copy HBM throughput (GB/s)", "value": round(world * gbs, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic N(0,1), seeded",
-            "config": {"workload": "config3: permute(0,3,1,4,2)+contiguous, slice->split(4)->concat",
-                       "algorithmic_bytes_per_step": byts},
+            "config": {"workload": "config3: permute(0,3,1,4,2)+contiguous, slice->split(4)->concat "
+                                   "(interpretation A: slice of the permuted tensor)",
+                       "algorithmic_bytes_per_step": byts,
+                       "l2": "no flush: the permute moves 134 MB, more than the 126 MB L2",
+                       "interpretation_b": {"workload": "x[:, 8:, :, :32, :] on the original axes -> [8,8,128,32,32], "
+                                                        "split(4) along axis 1 -> concat",
+                                            "ms": round(ms_b, 4), "gbs": round(gbs_b, 1),
+                                            "frac": round(gbs_b / pk["hbm_gbs"], 3),
+                                            "l2": "33.6 MB of traffic per step: L2-resident between steps"}},
             "roofline": {"bound": "hbm", "kernel": "strided copy + assemble", "achieved": round(gbs, 1),
                          "peak": pk["hbm_gbs"], "peak_source": pk_kind, "unit": "GB/s",
                          "frac": round(gbs / pk["hbm_gbs"], 3), "traffic": None},
-            "gpu_launches": 5 * args.steps, "clocks": clocks}
+            "gpu_launches": 2 * args.steps, "clocks": clocks}
 
 
 def run_c4(args, torch, world, rank, comm):
@@ -532,7 +588,10 @@ def run_c4(args, torch, world, rank, comm):
                          "unit": "TFLOP/s", "frac": round(tflops / pk["bf16_tflops_sustained"], 3), "traffic": None},
             "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "steps/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": (px.numel() + py.numel()) * 2, "d2h_bytes_per_step": 2},
-            "gpu_launches": None, "clocks": clocks}
+            # per step: 3 forward products + 1 split-K finish, the loss pass, per layer the bias
+            # adjoints (matvec, vecmat + finish, an add below the top) and 2 products (+1 finish
+            # for the split input-gradient product of layer 1), Adam: 24 (ncu launch list)
+            "gpu_launches": 24 * args.steps, "clocks": clocks}
 
 
 def barrier(torch, world):

@@ -22,43 +22,64 @@ template <class T> struct Pack {
   union { uint4 raw; S v[N]; };
 };
 
-template <class T>
+// y[r] (+)= M[r, :] . x.  WPR warps per row (a block holds 8 / WPR rows),
+// each over every WPR-th group of 32 packs of the row, four packs in flight
+// per lane; the warps' partial sums meet in shared memory in warp order.
+template <class T, int WPR>
 __global__ void __launch_bounds__(256) matvec_rows(const typename T::S *m, const typename T::S *x,
                                                    typename T::S *y, long long rows, long long cols,
                                                    bool accumulate, bool vec) {
   constexpr int N = Pack<T>::N;
-  const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const typename T::S *row = m + r * cols;
+  constexpr int RPB = 8 / WPR;  // rows per block
+  __shared__ float part[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = warp / WPR, wr = warp - g * WPR;  // row in block, warp in row
+  for (long long r0 = (long long)blockIdx.x * RPB; r0 < rows; r0 += (long long)gridDim.x * RPB) {
+    const long long r = r0 + g;
     float s = 0.0f;
-    if (vec) {
-      // Four packs in flight per lane, folded in the same order as one at a time.
-      constexpr int U = 4;
-      const long long packs = cols / N;
-      for (long long p0 = lane; p0 < packs; p0 += 32 * U) {
-        Pack<T> a[U], b[U];
+    if (r < rows) {
+      const typename T::S *row = m + r * cols;
+      if (vec) {
+        constexpr int U = 4;
+        const long long packs = cols / N;
+        for (long long p0 = (long long)wr * 32 + lane; p0 < packs; p0 += 32LL * WPR * U) {
+          Pack<T> a[U], b[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (p0 + 32 * u < packs) {
-            a[u].raw = __ldg(reinterpret_cast<const uint4 *>(row + (p0 + 32 * u) * N));
-            b[u].raw = __ldg(reinterpret_cast<const uint4 *>(x + (p0 + 32 * u) * N));
-          }
+          for (int u = 0; u < U; ++u)
+            if (p0 + 32LL * WPR * u < packs) {
+              a[u].raw = __ldg(reinterpret_cast<const uint4 *>(row + (p0 + 32LL * WPR * u) * N));
+              b[u].raw = __ldg(reinterpret_cast<const uint4 *>(x + (p0 + 32LL * WPR * u) * N));
+            }
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (p0 + 32 * u < packs) {
+          for (int u = 0; u < U; ++u)
+            if (p0 + 32LL * WPR * u < packs) {
 #pragma unroll
-            for (int j = 0; j < N; ++j) s = fmaf(T::load(a[u].v[j]), T::load(b[u].v[j]), s);
-          }
+              for (int j = 0; j < N; ++j) s = fmaf(T::load(a[u].v[j]), T::load(b[u].v[j]), s);
+            }
+        }
+      } else {
+        for (long long c = (long long)wr * 32 + lane; c < cols; c += 32LL * WPR)
+          s = fmaf(T::load(row[c]), T::load(x[c]), s);
+      }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    }
+    if (WPR == 1) {
+      if (lane == 0 && r < rows) {
+        if (accumulate) s = __fadd_rn(T::load(y[r]), s);
+        y[r] = T::store(s);
       }
     } else {
-      for (long long c = lane; c < cols; c += 32) s = fmaf(T::load(row[c]), T::load(x[c]), s);
-    }
+      if (lane == 0) part[warp] = s;
+      __syncthreads();
+      if (wr == 0 && lane == 0 && r < rows) {
+        float t = part[warp];
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
-    if (lane == 0) {
-      if (accumulate) s = __fadd_rn(T::load(y[r]), s);
-      y[r] = T::store(s);
+        for (int k = 1; k < WPR; ++k) t += part[warp + k];
+        if (accumulate) t = __fadd_rn(T::load(y[r]), t);
+        y[r] = T::store(t);
+      }
+      __syncthreads();
     }
   }
 }
@@ -231,10 +252,22 @@ int tc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x,
     using S = typename T::S;
     constexpr int N = Pack<T>::N;
     bool vec = cols % N == 0 && (uintptr_t(m) & 15u) == 0 && (uintptr_t(x) & 15u) == 0;
-    unsigned grid = unsigned(std::min<long long>(((long long)rows + 7) / 8, (long long)sm_count() * 8));
-    matvec_rows<T><<<std::max(1u, grid), 256, 0, as_stream(stream)>>>(
-        static_cast<const S *>(m), static_cast<const S *>(x), static_cast<S *>(y), (long long)rows,
-        (long long)cols, accumulate != 0, vec);
+    // Warps per row: enough warps in all to cover the SMs (32 each), while
+    // every warp still has a group of 32 units of its row.
+    const long long units = vec ? (long long)cols / N : (long long)cols;
+    int wpr = 1;
+    while (wpr < 8 && (long long)rows * wpr < 32LL * sm_count() && units >= 32LL * wpr * 2) wpr *= 2;
+    const long long rpb = 8 / wpr;
+    unsigned grid = unsigned(std::max(1LL, std::min<long long>(((long long)rows + rpb - 1) / rpb, (long long)sm_count() * 8)));
+    auto go = [&](auto kernel) {
+      kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const S *>(m), static_cast<const S *>(x),
+                                                  static_cast<S *>(y), (long long)rows, (long long)cols,
+                                                  accumulate != 0, vec);
+    };
+    if (wpr == 8) go(matvec_rows<T, 8>);
+    else if (wpr == 4) go(matvec_rows<T, 4>);
+    else if (wpr == 2) go(matvec_rows<T, 2>);
+    else go(matvec_rows<T, 1>);
     return check_launch("matvec");
   });
 }
