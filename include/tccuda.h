@@ -168,6 +168,100 @@ int tc_vector_reduce(int dtype, int op, const void *a, size_t n, void *out_dev,
 int tc_dot(int dtype, const void *a, const void *b, size_t n, void *out_dev,
            void *stream);
 
+/* ---- the other vector/matrix methods (kernels.rs:870-891, 941-1070) ----- */
+/* SortOrder, src/tensors/kernels.rs:252-255 */
+enum tc_sort_order { TC_ASCENDING = 0, TC_DESCENDING = 1 };
+/* `vector_prefix_sum` (kernels.rs:870; Host vector.rs:578-589,
+ * compact::prefix_sum): out[i] = a[0] + ... + a[i], an f32 running total
+ * rounded once per output to `dtype`.  Three launches; uses the per-device
+ * scratch block. */
+int tc_prefix_sum(int dtype, const void *a, void *out, size_t n, void *stream);
+/* `vector_sort` (kernels.rs:873; Host vector.rs:874-886): the n values in
+ * SortOrder's total order (f32::total_cmp / half's total_cmp: -NaN < -inf <
+ * ... < -0 < +0 < ... < +inf < +NaN).  TC_EINVAL beyond 2^31-1 elements.
+ * Uses the per-device scratch block. */
+int tc_sort(int dtype, int order, const void *a, void *out, size_t n, void *stream);
+/* `vector_unary`/`matrix_unary` (kernels.rs:876, 941; Host 1257-1268):
+ * out = f(a), f a tc_analytic, computed in f32 and rounded once. */
+int tc_unary(int dtype, int f, const void *a, void *out, size_t n, void *stream);
+/* `vector_unary_dual`/`matrix_unary_dual` (kernels.rs:891, 950; Host
+ * 1284-1304): out_value = f(value), out_tangent = f'(value) * tangent,
+ * the derivative's rule (Analytic::derivative, kernels.rs:357-387) and the
+ * product each rounded to `dtype` per operation. */
+int tc_unary_dual(int dtype, int f, const void *value, const void *tangent, void *out_value,
+                  void *out_tangent, size_t n, void *stream);
+/* `vector_power`/`matrix_power` (kernels.rs:884, 944; Host
+ * pow_elementwise): out = powf(a, b), rounded once. */
+int tc_power(int dtype, const void *a, const void *b, void *out, size_t n, void *stream);
+/* `vector_power_scalar`/`matrix_power_scalar` (kernels.rs:888, 947):
+ * out = powf(a, scalar), or powf(scalar, a) when scalar_left. */
+int tc_power_scalar(int dtype, const void *a, double scalar, int scalar_left, void *out,
+                    size_t n, void *stream);
+
+/* ---- windowed matrix methods (kernels.rs:998-1028) ----------------------- */
+/* `correlate` (kernels.rs:998; Host correlate_values, kernels.rs:1720-1751):
+ * the valid cross-correlation of the rows x cols `input` with the
+ * window_rows x window_cols `window` (reversed in both axes when `flip`),
+ * into the (rows-window_rows+1) x (cols-window_cols+1) `out`.  Each output
+ * sums its taps in row-major order with a rounded product and a rounded sum
+ * per tap, in f32 for f16/bf16 with one rounding at the end: the Host's
+ * bits, except when the taps number 4096 or more and the outputs are few,
+ * where a block shares each output's sum (deterministic, within an f32
+ * sum's rounding).  TC_EINVAL unless the window fits and is not empty. */
+int tc_correlate(int dtype, size_t rows, size_t cols, size_t window_rows, size_t window_cols,
+                 int flip, const void *input, const void *window, void *out, void *stream);
+/* `correlate_window_gradient` (kernels.rs:1008, 1544-1551): correlate of
+ * the input with the adjoint as the window, no flip; `out` has the
+ * window's shape (rows-adjoint_rows+1) x (cols-adjoint_cols+1). */
+int tc_correlate_window_gradient(int dtype, size_t rows, size_t cols, size_t adjoint_rows,
+                                 size_t adjoint_cols, const void *input, const void *adjoint,
+                                 void *out, void *stream);
+/* `correlate_input_gradient` (kernels.rs:1017; Host 1754-1788): the full
+ * correlation of the adjoint with the window, the taps reversed when the
+ * forward pass did not reverse them, into the (adjoint_rows+window_rows-1)
+ * x (adjoint_cols+window_cols-1) `out`; taps whose adjoint index falls
+ * outside are skipped, as on the Host, so the bits are the Host's. */
+int tc_correlate_input_gradient(int dtype, size_t adjoint_rows, size_t adjoint_cols,
+                                size_t window_rows, size_t window_cols, int forward_flip,
+                                const void *adjoint, const void *window, void *out, void *stream);
+/* `pad` (kernels.rs:1025; Host 1575-1601): `input` surrounded by pad_rows
+ * and pad_cols zeros on every side, (rows+2*pad_rows) x (cols+2*pad_cols). */
+int tc_pad(int dtype, size_t rows, size_t cols, size_t pad_rows, size_t pad_cols,
+           const void *input, void *out, void *stream);
+/* `flip` (kernels.rs:1028; Host 1531-1542): both axes reversed. */
+int tc_flip(int dtype, size_t rows, size_t cols, const void *input, void *out, void *stream);
+
+/* ---- moments and distributions (kernels.rs:1035-1070) -------------------- */
+/* Axis, src/tensors/kernels.rs:482-487: Rows folds each row (one result per
+ * row), Columns each column. */
+enum tc_axis { TC_ROWS = 0, TC_COLUMNS = 1 };
+/* Family and Statistic, src/tensors/kernels.rs:536-576. */
+enum tc_family { TC_NORMAL = 0, TC_INVERSE_GAUSSIAN = 1 };
+enum tc_statistic { TC_PDF = 0, TC_CDF = 1, TC_PPF = 2 };
+/* `vector_moments`/`matrix_moments` (kernels.rs:1035-1038; Host
+ * statistics/mod.rs:419-441): out_dev[0] = the mean of the n elements,
+ * out_dev[1] = the sum of their squared deviations from it (two passes, f32
+ * for every type, each rounded once to `dtype`); NaNs when n is 0. */
+int tc_moments(int dtype, const void *a, size_t n, void *out_dev, void *stream);
+/* `matrix_axis_moments` (kernels.rs:1042; Host statistics/mod.rs:451-520):
+ * one mean and one deviation sum per row (TC_ROWS, `rows` results) or per
+ * column (TC_COLUMNS, `cols` results) of the row-major rows x cols `a`. */
+int tc_axis_moments(int dtype, size_t rows, size_t cols, int axis, const void *a, void *means,
+                    void *deviations, void *stream);
+/* `vector_distribution`/`matrix_distribution` (kernels.rs:1046-1061; Host
+ * Distribution::evaluate, statistics/mod.rs:285-303): the pdf, cdf or ppf
+ * of the Normal(first = mean, second = stddev) or InverseGaussian(first =
+ * mean, second = shape) distribution at each element, evaluated in f64
+ * (statistics/special.rs) and rounded once to `dtype`.  first and second are
+ * element-type values. */
+int tc_distribution(int dtype, int family, int statistic, const void *a, size_t n, double first,
+                    double second, void *out, void *stream);
+/* `matrix_axis_distribution` (kernels.rs:1063): the same with one parameter
+ * pair per row (TC_ROWS) or per column (TC_COLUMNS), read from the device
+ * vectors `first` and `second` of the element type. */
+int tc_axis_distribution(int dtype, size_t rows, size_t cols, int axis, int family, int statistic,
+                         const void *a, const void *first, const void *second, void *out, void *stream);
+
 /* ---- strided kernels (src/tensors/kernels.rs:1162-1187) ------------------ */
 /* `strided_binary` (kernels.rs:1162; Host strided::binary, strided.rs:29):
  * op(a, b) over the common `shape`, each operand read through its own

@@ -46,6 +46,20 @@ SIGNATURES = {
     "orc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d],
     "orc_sgd": [_i, _sz, _p, _p, _d],
     "orc_fused": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _p, _u32],
+    "orc_unary": [_i, _i, _p, _p, _sz],
+    "orc_unary_dual": [_i, _i, _p, _p, _p, _p, _sz],
+    "orc_prefix_sum": [_i, _p, _p, _sz],
+    "orc_sort": [_i, _i, _p, _p, _sz],
+    "orc_power": [_i, _p, _p, _p, _sz],
+    "orc_power_scalar": [_i, _p, _d, _i, _p, _sz],
+    "orc_correlate": [_i, _sz, _sz, _sz, _sz, _i, _p, _p, _p],
+    "orc_correlate_input_gradient": [_i, _sz, _sz, _sz, _sz, _i, _p, _p, _p],
+    "orc_pad": [_i, _sz, _sz, _sz, _sz, _p, _p],
+    "orc_flip": [_i, _sz, _sz, _p, _p],
+    "orc_moments": [_i, _p, _sz, _p],
+    "orc_axis_moments": [_i, _sz, _sz, _i, _p, _p, _p],
+    "orc_distribution": [_i, _i, _i, _p, _sz, _d, _d, _p],
+    "orc_axis_distribution": [_i, _sz, _sz, _i, _i, _i, _p, _p, _p, _p],
     "orc_adam_coefficients": [_i, _d, _d, _d, _d, _u32, C.POINTER(C.c_double)],
     "orc_mlp_params": [_p, _u32, _p, _p, _i],
     "orc_mlp_grads": [_p, _u32, _p, _p],
@@ -66,7 +80,8 @@ def build() -> Path:
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
+        sources = [HERE / "oracle.cpp", HERE / "oracle.h", HERE / "Makefile"]
+        if not LIB_PATH.exists() or any(f.stat().st_mtime > LIB_PATH.stat().st_mtime for f in sources if f.exists()):
             build()
         h = C.CDLL(str(LIB_PATH))
         for name, args in SIGNATURES.items():
@@ -80,6 +95,8 @@ def lib() -> C.CDLL:
         h.orc_mlp_create.restype = _p
         h.orc_mlp_destroy.argtypes = [_p]
         h.orc_mlp_destroy.restype = None
+        h.orc_evaluate_f64.argtypes = [_i, _i, _d, _d, _d]
+        h.orc_evaluate_f64.restype = _d
         h.orc_set_threads.argtypes = [_i]
         h.orc_set_threads.restype = None
         _lib = h

@@ -1215,3 +1215,458 @@ int orc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_
     return int(TC_OK);
   });
 }
+
+// ---- the other vector methods (kernels.rs:870-891) -------------------------
+
+// Analytic::derivative (kernels.rs:357-387) in T: each operation of the rule
+// rounded to T, as the Host's Real arithmetic on T rounds.
+template <class T> static float orc_derivative(int op, float x) {
+  auto r = [](float v) { return T::round(v); };
+  auto recip = [&](float v) { return r(1.0f / v); };
+  auto val = [&](int g) { return r(orc_analytic(g, x)); };
+  switch (op) {
+    case TC_SIN: return val(TC_COS);
+    case TC_COS: return -val(TC_SIN);
+    case TC_TAN: { float c = val(TC_COS); return recip(r(c * c)); }
+    case TC_SEC: { float c = val(TC_COS); return r(val(TC_SIN) / r(c * c)); }
+    case TC_CSC: { float s = val(TC_SIN); return r(-val(TC_COS) / r(s * s)); }
+    case TC_ARCSIN: return recip(r(std::sqrt(r(1.0f - r(x * x)))));
+    case TC_ARCCOS: return -recip(r(std::sqrt(r(1.0f - r(x * x)))));
+    case TC_ARCTAN: return recip(r(1.0f + r(x * x)));
+    case TC_EXP: return val(TC_EXP);
+    case TC_LN: return recip(x);
+    case TC_SINH: return val(TC_COSH);
+    case TC_COSH: return val(TC_SINH);
+    case TC_TANH: { float t = val(TC_TANH); return r(1.0f - r(t * t)); }
+    default: return recip(r(2.0f * r(std::sqrt(x))));
+  }
+}
+
+// vector_unary (kernels.rs:1257-1268): vmath's f32 function rounded once to
+// T.  The restatement calls the C library's f32 functions, which agree with
+// vmath's within their 2-ulp bound (parity for transcendentals is 2 ulp).
+int orc_unary(int dtype, int f, const void *a, void *out, size_t n) {
+  if (f < TC_SIN || f > TC_SQRT) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < n; ++i) T::store(out, i, orc_analytic(f, T::load(a, i)));
+    return int(TC_OK);
+  });
+}
+
+// vector_unary_dual (kernels.rs:1284-1304): (f(x), f'(x) * d), the product
+// rounded in T.
+int orc_unary_dual(int dtype, int f, const void *value, const void *tangent, void *out_value, void *out_tangent,
+                   size_t n) {
+  if (f < TC_SIN || f > TC_SQRT) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < n; ++i) {
+      const float x = T::load(value, i);
+      T::store(out_value, i, orc_analytic(f, x));
+      T::store(out_tangent, i, orc_derivative<T>(f, x) * T::load(tangent, i));
+    }
+    return int(TC_OK);
+  });
+}
+
+// Vector::prefix_sum (vector.rs:578-589) and compact::prefix_sum
+// (compact.rs:209-221): a serial f32 running total, each output rounded to T.
+int orc_prefix_sum(int dtype, const void *a, void *out, size_t n) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    float running = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+      running = running + T::load(a, i);
+      T::store(out, i, running);
+    }
+    return int(TC_OK);
+  });
+}
+
+// Vector::sorted (vector.rs:874-886): sort_unstable_by the SortOrder
+// comparator, total_cmp (kernels.rs:257-269): the values' bits compared as
+// signed integers after flipping the magnitude bits of negative values.
+template <class U, class I> static I total_key(U bits) {
+  const I s = I(bits);
+  constexpr int shift = int(sizeof(U) * 8 - 1);
+  return I(s ^ I(U(U(s >> shift) >> 1)));
+}
+int orc_sort(int dtype, int order, const void *a, void *out, size_t n) {
+  if (order != TC_ASCENDING && order != TC_DESCENDING) return int(TC_EINVAL);
+  auto run = [&](auto unsigned_zero, auto signed_zero) {
+    using U = decltype(unsigned_zero);
+    using I = decltype(signed_zero);
+    const U *in = static_cast<const U *>(a);
+    std::vector<U> v(in, in + n);
+    auto less = [](U x, U y) { return total_key<U, I>(x) < total_key<U, I>(y); };
+    if (order == TC_ASCENDING) std::sort(v.begin(), v.end(), less);
+    else std::sort(v.begin(), v.end(), [&](U x, U y) { return less(y, x); });
+    std::memcpy(out, v.data(), n * sizeof(U));
+    return int(TC_OK);
+  };
+  if (dtype == TC_F32) return run(uint32_t(0), int32_t(0));
+  if (dtype == TC_F16 || dtype == TC_BF16) return run(uint16_t(0), int16_t(0));
+  return int(TC_EINVAL);
+}
+
+// pow_elementwise / power_scalar (kernels.rs:1270-1282): powf per element,
+// f16/bf16 through f32 and rounded once.
+int orc_power(int dtype, const void *a, const void *b, void *out, size_t n) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < n; ++i) T::store(out, i, power_value(T::load(a, i), T::load(b, i)));
+    return int(TC_OK);
+  });
+}
+int orc_power_scalar(int dtype, const void *a, double scalar, int scalar_left, void *out, size_t n) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    const float s = float(scalar);
+    for (size_t i = 0; i < n; ++i) {
+      const float x = T::load(a, i);
+      T::store(out, i, scalar_left ? power_value(s, x) : power_value(x, s));
+    }
+    return int(TC_OK);
+  });
+}
+
+// ---- windowed matrix methods (kernels.rs:998-1028) -------------------------
+
+// correlate_values (kernels.rs:1720-1751), through widened() / narrowed()
+// for f16/bf16 (kernels.rs:1514-1529): per output, the taps in row-major
+// order, sum = sum + x*k with both operations rounded in f32.
+int orc_correlate(int dtype, size_t rows, size_t cols, size_t wrows, size_t wcols, int flip, const void *input,
+                  const void *window, void *out) {
+  if (wrows > rows || wcols > cols || wrows == 0 || wcols == 0) return int(TC_EINVAL);
+  const size_t orows = rows - wrows + 1, ocols = cols - wcols + 1;
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t r = 0; r < orows; ++r)
+      for (size_t c = 0; c < ocols; ++c) {
+        float sum = 0.0f;
+        for (size_t a = 0; a < wrows; ++a)
+          for (size_t b = 0; b < wcols; ++b) {
+            const size_t tr = flip ? wrows - 1 - a : a, tc = flip ? wcols - 1 - b : b;
+            const float prod = T::load(input, (r + a) * cols + c + b) * T::load(window, tr * wcols + tc);
+            sum = sum + prod;
+          }
+        T::store(out, r * ocols + c, sum);
+      }
+    return int(TC_OK);
+  });
+}
+
+// correlate_input_gradient_values (kernels.rs:1754-1788): the full
+// correlation, out-of-range adjoint indices skipped.
+int orc_correlate_input_gradient(int dtype, size_t arows, size_t acols, size_t wrows, size_t wcols, int forward_flip,
+                                 const void *adjoint, const void *window, void *out) {
+  if (wrows == 0 || wcols == 0 || arows == 0 || acols == 0) return int(TC_EINVAL);
+  const size_t rows = arows + wrows - 1, cols = acols + wcols - 1;
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t r = 0; r < rows; ++r)
+      for (size_t c = 0; c < cols; ++c) {
+        float sum = 0.0f;
+        for (size_t a = 0; a < wrows; ++a)
+          for (size_t b = 0; b < wcols; ++b) {
+            if (r < a || c < b) continue;
+            const size_t sr = r - a, sc = c - b;
+            if (sr >= arows || sc >= acols) continue;
+            const size_t tr = forward_flip ? wrows - 1 - a : a, tc = forward_flip ? wcols - 1 - b : b;
+            const float prod = T::load(adjoint, sr * acols + sc) * T::load(window, tr * wcols + tc);
+            sum = sum + prod;
+          }
+        T::store(out, r * cols + c, sum);
+      }
+    return int(TC_OK);
+  });
+}
+
+// pad (kernels.rs:1575-1601) and flip (kernels.rs:1531-1542): bits moved.
+int orc_pad(int dtype, size_t rows, size_t cols, size_t pr, size_t pc, const void *input, void *out) {
+  const size_t e = dtype == TC_F32 ? 4 : 2, ocols = cols + 2 * pc, orows = rows + 2 * pr;
+  const char *in = static_cast<const char *>(input);
+  char *o = static_cast<char *>(out);
+  for (size_t r = 0; r < orows; ++r)
+    for (size_t c = 0; c < ocols; ++c) {
+      const bool inside = r >= pr && r < pr + rows && c >= pc && c < pc + cols;
+      if (inside) std::memcpy(o + (r * ocols + c) * e, in + ((r - pr) * cols + c - pc) * e, e);
+      else std::memset(o + (r * ocols + c) * e, 0, e);
+    }
+  return int(TC_OK);
+}
+int orc_flip(int dtype, size_t rows, size_t cols, const void *input, void *out) {
+  const size_t e = dtype == TC_F32 ? 4 : 2;
+  const char *in = static_cast<const char *>(input);
+  char *o = static_cast<char *>(out);
+  for (size_t r = 0; r < rows; ++r)
+    for (size_t c = 0; c < cols; ++c)
+      std::memcpy(o + (r * cols + c) * e, in + ((rows - 1 - r) * cols + cols - 1 - c) * e, e);
+  return int(TC_OK);
+}
+
+// ---- moments and distributions (kernels.rs:1035-1070) -----------------------
+
+// moments_of / axis_moments_of (statistics/mod.rs:419-500): f32 for the
+// compact types (widened), the mean as sum / count, then the sum of squared
+// deviations from that mean; both rounded to T.  An empty slice gives NaNs.
+static void orc_moments_of(const std::vector<float> &v, float &mean, float &dev) {
+  if (v.empty()) {
+    mean = dev = std::nanf("");
+    return;
+  }
+  float s = 0.0f;
+  for (float x : v) s = s + x;
+  mean = s / float(v.size());
+  float d = 0.0f;
+  for (float x : v) {
+    const float e = x - mean;
+    d = d + e * e;
+  }
+  dev = d;
+}
+
+int orc_moments(int dtype, const void *a, size_t n, void *out) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    std::vector<float> v(n);
+    for (size_t i = 0; i < n; ++i) v[i] = T::load(a, i);
+    float mean, dev;
+    orc_moments_of(v, mean, dev);
+    T::store(out, 0, mean);
+    T::store(out, 1, dev);
+    return int(TC_OK);
+  });
+}
+
+int orc_axis_moments(int dtype, size_t rows, size_t cols, int axis, const void *a, void *means, void *devs) {
+  if (axis != TC_ROWS && axis != TC_COLUMNS) return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    const size_t extent = axis == TC_ROWS ? rows : cols, depth = axis == TC_ROWS ? cols : rows;
+    for (size_t k = 0; k < extent; ++k) {
+      std::vector<float> v(depth);
+      for (size_t j = 0; j < depth; ++j) v[j] = T::load(a, axis == TC_ROWS ? k * cols + j : j * cols + k);
+      float mean, dev;
+      orc_moments_of(v, mean, dev);
+      T::store(means, k, mean);
+      T::store(devs, k, dev);
+    }
+    return int(TC_OK);
+  });
+}
+
+// The special functions of statistics/special.rs, in f64: Cody's rational
+// Chebyshev erf/erfc (split at 0.46875 and 4) and Wichura's AS 241 normal
+// quantile, with the published coefficients.
+namespace special {
+const double FRAC_1_SQRT_PI = 0.5641895835477563, SQRT_2PI = 2.5066282746310002;
+const double FRAC_1_SQRT_2 = 0.70710678118654752440, LN_2 = 0.69314718055994530942, PI = 3.14159265358979323846;
+
+static double erf_central(double x) {
+  static const double A[5] = {3.1611237438705656, 113.864154151050156, 377.485237685302021, 3209.37758913846947,
+                              0.185777706184603153};
+  static const double B[4] = {23.6012909523441209, 244.024637934444173, 1282.61652607737228, 2844.23683343917062};
+  const double z = x * x;
+  double num = A[4] * z, den = z;
+  for (int i = 0; i < 3; ++i) {
+    num = (num + A[i]) * z;
+    den = (den + B[i]) * z;
+  }
+  return x * (num + A[3]) / (den + B[3]);
+}
+static double erfc_scaled(double x) {
+  static const double C[9] = {0.564188496988670089, 8.88314979438837594, 66.1191906371416295, 298.635138197400131,
+                              881.95222124176909, 1712.04761263407058, 2051.07837782607147, 1230.33935479799725,
+                              2.15311535474403846e-8};
+  static const double D[8] = {15.7449261107098347, 117.693950891312499, 537.181101862009858, 1621.38957456669019,
+                              3290.79923573345963, 4362.61909014324716, 3439.36767414372164, 1230.33935480374942};
+  static const double P[6] = {0.305326634961232344, 0.360344899949804439, 0.125781726111229246,
+                              0.0160837851487422766, 0.000658749161529837803, 0.0163153871373020978};
+  static const double Q[5] = {2.56852019228982242, 1.87295284992346047, 0.527905102951428412,
+                              0.0605183413124413191, 0.00233520497626869185};
+  if (x <= 4.0) {
+    double num = C[8] * x, den = x;
+    for (int i = 0; i < 7; ++i) {
+      num = (num + C[i]) * x;
+      den = (den + D[i]) * x;
+    }
+    return (num + C[7]) / (den + D[7]);
+  }
+  const double z = 1.0 / (x * x);
+  double num = P[5] * z, den = z;
+  for (int i = 0; i < 4; ++i) {
+    num = (num + P[i]) * z;
+    den = (den + Q[i]) * z;
+  }
+  const double correction = z * (num + P[4]) / (den + Q[4]);
+  return (FRAC_1_SQRT_PI - correction) / x;
+}
+static double erfc_positive(double x) {
+  if (x > 27.25) return 0.0;
+  const double leading = std::trunc(x * 16.0) / 16.0;
+  const double correction = (x - leading) * (x + leading);
+  return std::exp(-leading * leading) * std::exp(-correction) * erfc_scaled(x);
+}
+static double erfc(double x) {
+  if (std::isnan(x)) return x;
+  if (x < -0.46875) return 2.0 - erfc_positive(-x);
+  if (x <= 0.46875) return 1.0 - erf_central(x);
+  return erfc_positive(x);
+}
+static double ln_erfc(double x) {
+  if (std::isnan(x)) return x;
+  if (x <= 0.46875) return std::log(erfc(x));
+  return std::log(erfc_scaled(x)) - x * x;
+}
+static double polynomial(const double *c, int n, double x) {
+  double total = 0.0;
+  for (int i = n - 1; i >= 0; --i) total = total * x + c[i];
+  return total;
+}
+static double std_pdf(double z) { return std::exp(-0.5 * z * z) / SQRT_2PI; }
+static double std_cdf(double z) { return 0.5 * erfc(-z * FRAC_1_SQRT_2); }
+static double std_ln_cdf(double z) { return ln_erfc(-z * FRAC_1_SQRT_2) - LN_2; }
+static double std_ppf(double p) {
+  if (std::isnan(p) || !(p >= 0.0 && p <= 1.0)) return std::nan("");
+  if (p == 0.0) return -INFINITY;
+  if (p == 1.0) return INFINITY;
+  const double q = p - 0.5;
+  if (std::fabs(q) <= 0.425) {
+    static const double A[8] = {3.3871328727963666080, 133.14166789178437745, 1971.5909503065514427,
+                                13731.693765509461125, 45921.953931549871457, 67265.770927008700853,
+                                33430.575583588128105, 2509.0809287301226727};
+    static const double B[7] = {42.313330701600911252, 687.18700749205790830, 5394.1960214247511077,
+                                21213.794301586595867, 39307.895800092710610, 28729.085735721942674,
+                                5226.4952788528545610};
+    const double r = 0.180625 - q * q;
+    return q * polynomial(A, 8, r) / (polynomial(B, 7, r) * r + 1.0);
+  }
+  const double tail = q < 0.0 ? p : 1.0 - p;
+  double r = std::sqrt(-std::log(tail));
+  double value;
+  if (r <= 5.0) {
+    static const double C[8] = {1.42343711074968357734, 4.63033784615654529590, 5.76949722146069140550,
+                                3.64784832476320460504, 1.27045825245236838258, 0.241780725177450611770,
+                                0.0227238449892691845833, 0.000774545014278341407640};
+    static const double D[7] = {2.05319162663775882187, 1.67638483018380384940, 0.689767334985100004550,
+                                0.148103976427480074590, 0.0151986665636164571966, 0.000547593808499534494600,
+                                1.05075007164441684324e-9};
+    r = r - 1.6;
+    value = polynomial(C, 8, r) / (polynomial(D, 7, r) * r + 1.0);
+  } else {
+    static const double E[8] = {6.65790464350110377720, 5.46378491116411436990, 1.78482653991729133580,
+                                0.296560571828504891230, 0.0265321895265761230930, 0.00124266094738807843860,
+                                0.0000271155556874348757815, 2.01033439929228813265e-7};
+    static const double F[7] = {0.599832206555887937690, 0.136929880922735805310, 0.0148753612908506148525,
+                                0.000786869131145613259100, 0.0000184631831751005468180,
+                                1.42151175831644588870e-7, 2.04426310338993978564e-15};
+    r = r - 5.0;
+    value = polynomial(E, 8, r) / (polynomial(F, 7, r) * r + 1.0);
+  }
+  return q < 0.0 ? -value : value;
+}
+static bool positive(double v) { return v > 0.0; }
+static double ig_pdf(double x, double mean, double shape) {
+  if (!positive(mean) || !positive(shape)) return std::nan("");
+  if (x <= 0.0) return 0.0;
+  const double deviation = x - mean;
+  const double exponent = -shape * deviation * deviation / (2.0 * mean * mean * x);
+  return std::sqrt(shape / (2.0 * PI * x * x * x)) * std::exp(exponent);
+}
+static double ig_cdf(double x, double mean, double shape) {
+  if (!positive(mean) || !positive(shape)) return std::nan("");
+  if (x <= 0.0) return 0.0;
+  const double scale = std::sqrt(shape / x), ratio = x / mean;
+  const double lower = scale * (ratio - 1.0), upper = scale * (ratio + 1.0);
+  const double tail = 2.0 * shape / mean + std_ln_cdf(-upper);
+  return std::fmin(std_cdf(lower) + std::exp(tail), 1.0);
+}
+static double ig_ppf(double p, double mean, double shape) {
+  if (!positive(mean) || !positive(shape) || std::isnan(p) || !(p >= 0.0 && p <= 1.0)) return std::nan("");
+  if (p == 0.0) return 0.0;
+  if (p == 1.0) return INFINITY;
+  double low = 0.0, high = mean;
+  while (ig_cdf(high, mean, shape) < p) {
+    low = high;
+    high *= 2.0;
+    if (std::isinf(high)) return INFINITY;
+  }
+  double guess = 0.5 * (low + high);
+  for (int k = 0; k < 60; ++k) {
+    const double error = ig_cdf(guess, mean, shape) - p;
+    if (error > 0.0) high = guess;
+    else low = guess;
+    const double density = ig_pdf(guess, mean, shape);
+    const double step = density > 0.0 ? guess - error / density : std::nan("");
+    const double next = (std::isfinite(step) && step > low && step < high) ? step : 0.5 * (low + high);
+    if (next == guess) break;
+    guess = next;
+  }
+  return guess;
+}
+// Distribution::evaluate (statistics/mod.rs:285-303).
+static double evaluate(int family, int statistic, double x, double first, double second) {
+  if (family == TC_NORMAL) {
+    if (std::isnan(second) || second <= 0.0) return std::nan("");
+    if (statistic == TC_PDF) return std_pdf((x - first) / second) / second;
+    if (statistic == TC_CDF) return std_cdf((x - first) / second);
+    return first + second * std_ppf(x);
+  }
+  if (statistic == TC_PDF) return ig_pdf(x, first, second);
+  if (statistic == TC_CDF) return ig_cdf(x, first, second);
+  return ig_ppf(x, first, second);
+}
+}  // namespace special
+
+// f64 rounded once to T: the f32 cast, or crate half's direct f64
+// conversion (round to odd into f32, then to nearest even into 16 bits,
+// which is the correctly rounded result).
+template <class T> static void store_f64(void *out, size_t i, double d) {
+  float f = float(d);
+  if (!std::is_same<T, F32>::value && std::isfinite(d) && double(f) != d) {
+    // round toward zero into f32, then make the last bit odd
+    float z = float(d);
+    if (std::fabs(double(z)) > std::fabs(d)) z = std::nextafter(z, 0.0f);
+    uint32_t b;
+    std::memcpy(&b, &z, 4);
+    b |= 1u;
+    std::memcpy(&f, &b, 4);
+  }
+  T::store(out, i, f);
+}
+
+int orc_distribution(int dtype, int family, int statistic, const void *a, size_t n, double first, double second,
+                     void *out) {
+  if (family < TC_NORMAL || family > TC_INVERSE_GAUSSIAN || statistic < TC_PDF || statistic > TC_PPF)
+    return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < n; ++i)
+      store_f64<T>(out, i, special::evaluate(family, statistic, double(T::load(a, i)), first, second));
+    return int(TC_OK);
+  });
+}
+
+int orc_axis_distribution(int dtype, size_t rows, size_t cols, int axis, int family, int statistic, const void *a,
+                          const void *first, const void *second, void *out) {
+  if (family < TC_NORMAL || family > TC_INVERSE_GAUSSIAN || statistic < TC_PDF || statistic > TC_PPF ||
+      (axis != TC_ROWS && axis != TC_COLUMNS))
+    return int(TC_EINVAL);
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < rows * cols; ++i) {
+      const size_t along = axis == TC_ROWS ? i / cols : i % cols;
+      store_f64<T>(out, i, special::evaluate(family, statistic, double(T::load(a, i)),
+                                             double(T::load(first, along)), double(T::load(second, along))));
+    }
+    return int(TC_OK);
+  });
+}
+
+// Distribution::evaluate in f64 before any rounding to the element type,
+// for pinning the special functions against published values.
+double orc_evaluate_f64(int family, int statistic, double x, double first, double second) {
+  return special::evaluate(family, statistic, x, first, second);
+}

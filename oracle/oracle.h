@@ -109,6 +109,36 @@ int orc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_
               const tc_place *places, uint32_t n_places, void *const *outputs, const int *out_dtypes,
               uint32_t n_outputs);
 
+/* The other vector methods, as tc_unary, tc_unary_dual, tc_prefix_sum,
+ * tc_sort, tc_power and tc_power_scalar take them (kernels.rs:870-891). */
+int orc_unary(int dtype, int f, const void *a, void *out, size_t n);
+int orc_unary_dual(int dtype, int f, const void *value, const void *tangent, void *out_value,
+                   void *out_tangent, size_t n);
+int orc_prefix_sum(int dtype, const void *a, void *out, size_t n);
+int orc_sort(int dtype, int order, const void *a, void *out, size_t n);
+int orc_power(int dtype, const void *a, const void *b, void *out, size_t n);
+int orc_power_scalar(int dtype, const void *a, double scalar, int scalar_left, void *out, size_t n);
+
+/* Windowed matrix methods, as tc_correlate, tc_correlate_input_gradient,
+ * tc_pad and tc_flip take them (kernels.rs:998-1028). */
+int orc_correlate(int dtype, size_t rows, size_t cols, size_t window_rows, size_t window_cols, int flip,
+                  const void *input, const void *window, void *out);
+int orc_correlate_input_gradient(int dtype, size_t adjoint_rows, size_t adjoint_cols, size_t window_rows,
+                                 size_t window_cols, int forward_flip, const void *adjoint, const void *window,
+                                 void *out);
+int orc_pad(int dtype, size_t rows, size_t cols, size_t pad_rows, size_t pad_cols, const void *input, void *out);
+int orc_flip(int dtype, size_t rows, size_t cols, const void *input, void *out);
+
+/* Moments and distributions, as tc_moments, tc_axis_moments,
+ * tc_distribution and tc_axis_distribution take them (host buffers). */
+int orc_moments(int dtype, const void *a, size_t n, void *out);
+int orc_axis_moments(int dtype, size_t rows, size_t cols, int axis, const void *a, void *means, void *devs);
+int orc_distribution(int dtype, int family, int statistic, const void *a, size_t n, double first, double second,
+                     void *out);
+double orc_evaluate_f64(int family, int statistic, double x, double first, double second);
+int orc_axis_distribution(int dtype, size_t rows, size_t cols, int axis, int family, int statistic, const void *a,
+                          const void *first, const void *second, void *out);
+
 #ifdef __cplusplus
 }
 #endif

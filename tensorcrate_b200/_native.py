@@ -63,6 +63,10 @@ class Place(C.Structure):
 
 I_LOAD, I_CONST, I_BINARY, I_UNARY, I_CMP, I_STORE = range(6)
 (SIN, COS, TAN, SEC, CSC, ARCSIN, ARCCOS, ARCTAN, EXP, LN, SINH, COSH, TANH, SQRT) = range(14)
+ASCENDING, DESCENDING = range(2)
+ROWS, COLUMNS = range(2)
+NORMAL, INVERSE_GAUSSIAN = range(2)
+PDF, CDF, PPF = range(3)
 
 
 class AdamTensor(C.Structure):
@@ -96,6 +100,21 @@ SIGNATURES = {
     "tc_clamp": [_i, _p, _d, _d, _p, _sz, _p],
     "tc_vector_reduce": [_i, _i, _p, _sz, _p, _p],
     "tc_dot": [_i, _p, _p, _sz, _p, _p],
+    "tc_prefix_sum": [_i, _p, _p, _sz, _p],
+    "tc_sort": [_i, _i, _p, _p, _sz, _p],
+    "tc_unary": [_i, _i, _p, _p, _sz, _p],
+    "tc_unary_dual": [_i, _i, _p, _p, _p, _p, _sz, _p],
+    "tc_power": [_i, _p, _p, _p, _sz, _p],
+    "tc_power_scalar": [_i, _p, _d, _i, _p, _sz, _p],
+    "tc_correlate": [_i, _sz, _sz, _sz, _sz, _i, _p, _p, _p, _p],
+    "tc_correlate_window_gradient": [_i, _sz, _sz, _sz, _sz, _p, _p, _p, _p],
+    "tc_correlate_input_gradient": [_i, _sz, _sz, _sz, _sz, _i, _p, _p, _p, _p],
+    "tc_pad": [_i, _sz, _sz, _sz, _sz, _p, _p, _p],
+    "tc_flip": [_i, _sz, _sz, _p, _p, _p],
+    "tc_moments": [_i, _p, _sz, _p, _p],
+    "tc_axis_moments": [_i, _sz, _sz, _i, _p, _p, _p, _p],
+    "tc_distribution": [_i, _i, _i, _p, _sz, _d, _d, _p, _p],
+    "tc_axis_distribution": [_i, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p],
     "tc_strided_binary": [_i, _i, _i, _u32, _szp, _p, _sz, _sz, _szp, _p, _sz, _sz, _szp, _p, _p],
     "tc_reduce_axes": [_i, _u32, _szp, _p, _sz, _sz, _szp, _u32, _u32p, _i, _i, _sz, _p, _p],
     "tc_arg_reduce": [_i, _u32, _szp, _p, _sz, _sz, _szp, _u32, _i, _u32p, _p],

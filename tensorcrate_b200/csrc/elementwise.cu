@@ -289,6 +289,15 @@ int tc_compare_scalar(int dtype, int cmp, const void *a, double s, int left, voi
   return scalar(dtype, Pair{TC_PAIR_COMPARE, cmp}, a, s, left, out, n, stream);
 }
 
+// vector_power / vector_power_scalar (kernels.rs:884-888; Host
+// pow_elementwise, power_scalar): Pairwise::Power's powf.
+int tc_power(int dtype, const void *a, const void *b, void *out, size_t n, void *stream) {
+  return same(dtype, Pair{TC_PAIR_POWER, 0}, a, b, out, n, stream);
+}
+int tc_power_scalar(int dtype, const void *a, double s, int left, void *out, size_t n, void *stream) {
+  return scalar(dtype, Pair{TC_PAIR_POWER, 0}, a, s, left, out, n, stream);
+}
+
 int tc_clamp(int dtype, const void *a, double low, double high, void *out, size_t n, void *stream) {
   if (!(low <= high)) return fail(TC_EINVAL, "clamp: low %g is not <= high %g", low, high);
   if (n == 0) return TC_OK;

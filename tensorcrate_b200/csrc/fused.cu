@@ -15,7 +15,7 @@
 // optimizers' programs have kernels of their own (optim.cu).
 #include <algorithm>
 
-#include "common.cuh"
+#include "analytic.cuh"
 
 namespace tc {
 namespace {
@@ -50,26 +50,6 @@ __device__ __forceinline__ void store_as(void *p, int dtype, long long i, float 
   if (dtype == TC_F32) static_cast<float *>(p)[i] = v;
   else if (dtype == TC_BF16) static_cast<uint16_t *>(p)[i] = BF16T::store(v);
   else static_cast<uint16_t *>(p)[i] = F16T::store(v);
-}
-
-// Analytic::value in f32 (kernels.rs:329-388); Sqrt is the IEEE square root.
-__device__ __forceinline__ float analytic(int op, float x) {
-  switch (op) {
-    case TC_SIN: return sinf(x);
-    case TC_COS: return cosf(x);
-    case TC_TAN: return tanf(x);
-    case TC_SEC: return __fdiv_rn(1.0f, cosf(x));
-    case TC_CSC: return __fdiv_rn(1.0f, sinf(x));
-    case TC_ARCSIN: return asinf(x);
-    case TC_ARCCOS: return acosf(x);
-    case TC_ARCTAN: return atanf(x);
-    case TC_EXP: return expf(x);
-    case TC_LN: return logf(x);
-    case TC_SINH: return sinhf(x);
-    case TC_COSH: return coshf(x);
-    case TC_TANH: return tanhf(x);
-    default: return __fsqrt_rn(x);
-  }
 }
 
 template <class T>

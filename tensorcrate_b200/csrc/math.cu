@@ -1,0 +1,356 @@
+// math.cu — the vector methods of Kernels<T> that are neither elementwise
+// arithmetic nor reductions: the Analytic functions and their forward-mode
+// step (vector_unary / matrix_unary, vector_unary_dual / matrix_unary_dual,
+// kernels.rs:876, 891, 941, 950), the inclusive prefix sum
+// (vector_prefix_sum, kernels.rs:870) and the total-order sort (vector_sort,
+// kernels.rs:873).
+//
+// All of it is HBM-bound: 16-byte packs per thread, grids sized to the SMs.
+#include <algorithm>
+#include <climits>
+
+#include <cub/device/device_radix_sort.cuh>
+
+#include "analytic.cuh"
+
+namespace tc {
+namespace {
+
+template <class T> struct Pack {
+  using S = typename T::S;
+  static constexpr int N = 16 / int(sizeof(S));
+  union {
+    uint4 raw;
+    S v[N];
+  };
+};
+
+bool aligned16(const void *p) { return (uintptr_t(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Analytic functions.  vector_unary: vmath's f32 function, rounded once to T
+// (Host kernels.rs:1257-1268; Sqrt is compact::sqrt, the f32 root rounded).
+// vector_unary_dual: (f(x), f'(x)·t), the derivative and the product each in
+// T (kernels.rs:1284-1304).
+// ---------------------------------------------------------------------------
+template <class T>
+__global__ void __launch_bounds__(256) unary_kernel(const typename T::S *a, typename T::S *out, long long n, int f,
+                                                    bool vec) {
+  constexpr int N = Pack<T>::N;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec) {
+    const long long packs = n / N;
+    for (long long p = i; p < packs; p += stride) {
+      Pack<T> x, y;
+      x.raw = __ldg(reinterpret_cast<const uint4 *>(a) + p);
+#pragma unroll
+      for (int j = 0; j < N; ++j) y.v[j] = T::store(analytic(f, T::load(x.v[j])));
+      reinterpret_cast<uint4 *>(out)[p] = y.raw;
+    }
+    i += packs * N;
+  }
+  for (; i < n; i += stride) out[i] = T::store(analytic(f, T::load(a[i])));
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) unary_dual_kernel(const typename T::S *value, const typename T::S *tangent,
+                                                         typename T::S *out_value, typename T::S *out_tangent,
+                                                         long long n, int f, bool vec) {
+  constexpr int N = Pack<T>::N;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec) {
+    const long long packs = n / N;
+    for (long long p = i; p < packs; p += stride) {
+      Pack<T> x, t, y, d;
+      x.raw = __ldg(reinterpret_cast<const uint4 *>(value) + p);
+      t.raw = __ldg(reinterpret_cast<const uint4 *>(tangent) + p);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const float xv = T::load(x.v[j]);
+        y.v[j] = T::store(analytic(f, xv));
+        d.v[j] = T::store(__fmul_rn(analytic_derivative<T>(f, xv), T::load(t.v[j])));
+      }
+      reinterpret_cast<uint4 *>(out_value)[p] = y.raw;
+      reinterpret_cast<uint4 *>(out_tangent)[p] = d.raw;
+    }
+    i += packs * N;
+  }
+  for (; i < n; i += stride) {
+    const float xv = T::load(value[i]);
+    out_value[i] = T::store(analytic(f, xv));
+    out_tangent[i] = T::store(__fmul_rn(analytic_derivative<T>(f, xv), T::load(tangent[i])));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Inclusive prefix sum, reduce-then-scan (three launches, deterministic):
+//   1. each of G blocks sums its chunk of `per` elements (a multiple of the
+//      2048-element tile);
+//   2. one block turns the G chunk sums into exclusive chunk offsets;
+//   3. each block scans its chunk tile by tile from its offset: 8 elements
+//      per thread in registers, warp and block scans of the thread totals.
+// The running total is f32 and each output is rounded once to T, as the
+// Host keeps an f32 running total for every type (vector.rs:578-589,
+// compact::prefix_sum).  The association differs from the Host's serial
+// chain, so f32 results agree within a sum's rounding, and exactly whenever
+// the partial sums are exact (integral values below 2^24).
+// ---------------------------------------------------------------------------
+constexpr int SCAN_THREADS = 256, SCAN_ITEMS = 8, SCAN_TILE = SCAN_THREADS * SCAN_ITEMS, MAX_CHUNKS = 1024;
+
+template <class T>
+__device__ __forceinline__ void load_items(const typename T::S *a, long long at, long long n, bool vec, float v[8]) {
+  using S = typename T::S;
+  if (vec && at + SCAN_ITEMS <= n) {
+    if (sizeof(S) == 2) {
+      Pack<T> k;
+      k.raw = __ldg(reinterpret_cast<const uint4 *>(a + at));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = T::load(k.v[j]);
+    } else {
+      Pack<T> k0, k1;
+      k0.raw = __ldg(reinterpret_cast<const uint4 *>(a + at));
+      k1.raw = __ldg(reinterpret_cast<const uint4 *>(a + at) + 1);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = T::load(k0.v[j]);
+        v[4 + j] = T::load(k1.v[j]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = at + j < n ? T::load(a[at + j]) : 0.0f;
+  }
+}
+
+// Inclusive scan of one value per thread across the block; `total` gets the
+// block's sum.  Every thread of the block calls it.
+__device__ __forceinline__ float block_inclusive(float x, float *warp_sums, float &total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x = __fadd_rn(x, y);
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < warps ? warp_sums[lane] : 0.0f;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w = __fadd_rn(w, y);
+    }
+    if (lane < warps) warp_sums[lane] = w;
+  }
+  __syncthreads();
+  if (warp > 0) x = __fadd_rn(x, warp_sums[warp - 1]);
+  total = warp_sums[warps - 1];
+  __syncthreads();
+  return x;
+}
+
+template <class T>
+__global__ void __launch_bounds__(SCAN_THREADS) chunk_sums(const typename T::S *a, long long n, long long per,
+                                                           bool vec, float *sums) {
+  __shared__ float warp_sums[32];
+  const long long begin = (long long)blockIdx.x * per, end = min(n, begin + per);
+  float s = 0.0f;
+  for (long long t = begin; t < end; t += SCAN_TILE) {
+    float v[8];
+    load_items<T>(a, t + (long long)threadIdx.x * SCAN_ITEMS, end, vec, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[j]);
+  }
+  float total;
+  block_inclusive(s, warp_sums, total);
+  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+// offsets[b] = sums[0] + ... + sums[b-1], for b < chunks <= 1024.
+__global__ void __launch_bounds__(MAX_CHUNKS) chunk_offsets(float *sums, int chunks) {
+  __shared__ float warp_sums[32];
+  const int t = threadIdx.x;
+  const float x = t > 0 && t <= chunks ? sums[t - 1] : 0.0f;
+  float total;
+  const float incl = block_inclusive(x, warp_sums, total);
+  __syncthreads();
+  if (t < chunks) sums[t] = incl;
+}
+
+template <class T>
+__global__ void __launch_bounds__(SCAN_THREADS) scan_chunks(const typename T::S *a, typename T::S *out, long long n,
+                                                            long long per, bool vec, const float *offsets) {
+  using S = typename T::S;
+  __shared__ float warp_sums[32];
+  const long long begin = (long long)blockIdx.x * per, end = min(n, begin + per);
+  float carry = offsets[blockIdx.x];
+  for (long long t = begin; t < end; t += SCAN_TILE) {
+    const long long at = t + (long long)threadIdx.x * SCAN_ITEMS;
+    float v[8];
+    load_items<T>(a, at, end, vec, v);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) v[j] = __fadd_rn(v[j - 1], v[j]);
+    float tile_total;
+    const float incl = block_inclusive(v[7], warp_sums, tile_total);
+    // This thread's exclusive prefix within the tile: the inclusive scan of
+    // the thread before it.
+    float before = __shfl_up_sync(0xffffffffu, incl, 1);
+    if ((threadIdx.x & 31) == 0) before = threadIdx.x == 0 ? 0.0f : warp_sums[(threadIdx.x >> 5) - 1];
+    const float base = threadIdx.x == 0 ? carry : __fadd_rn(carry, before);
+    S r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = T::store(__fadd_rn(base, v[j]));
+    if (vec && at + SCAN_ITEMS <= end) {
+      if (sizeof(S) == 2) {
+        Pack<T> k;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) k.v[j] = r[j];
+        *reinterpret_cast<uint4 *>(out + at) = k.raw;
+      } else {
+        Pack<T> k0, k1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          k0.v[j] = r[j];
+          k1.v[j] = r[4 + j];
+        }
+        reinterpret_cast<uint4 *>(out + at)[0] = k0.raw;
+        reinterpret_cast<uint4 *>(out + at)[1] = k1.raw;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (at + j < end) out[at + j] = r[j];
+    }
+    carry = __fadd_rn(carry, tile_total);
+    __syncthreads();  // warp_sums is read above and rewritten by the next tile
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Sort in the total order of f32::total_cmp / half's total_cmp (the
+// comparator of SortOrder, kernels.rs:252-269; Host vector.rs:874-886):
+// -NaN < -inf < ... < -0 < +0 < ... < +inf < +NaN, ordered within the NaNs by
+// payload.  Mapping each value's bits to an unsigned key (every bit flipped
+// for a negative sign, the sign bit set otherwise) turns that order into
+// the keys' unsigned order, so a radix sort of the keys sorts the values;
+// equal keys are equal bits, so the result is the unique sorted sequence.
+// ---------------------------------------------------------------------------
+template <class K> __device__ __forceinline__ K order_key(K bits) {
+  constexpr K sign = K(K(1) << (sizeof(K) * 8 - 1));
+  return (bits & sign) ? K(~bits) : K(bits | sign);
+}
+template <class K> __device__ __forceinline__ K key_bits(K key) {
+  constexpr K sign = K(K(1) << (sizeof(K) * 8 - 1));
+  return (key & sign) ? K(key ^ sign) : K(~key);
+}
+
+template <class K> __global__ void __launch_bounds__(256) to_keys(const K *a, K *keys, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    keys[i] = order_key(a[i]);
+}
+template <class K> __global__ void __launch_bounds__(256) from_keys(const K *keys, K *out, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = key_bits(keys[i]);
+}
+
+template <class K> int sort_keys(const void *a, void *out, size_t n, bool descending, cudaStream_t s) {
+  if (n > size_t(INT_MAX)) return fail(TC_EINVAL, "sort: %zu elements exceed the radix sort's 2^31-1", n);
+  const int count = int(n);
+  // Keys go into `out`; the sort's second buffer and its temporary storage
+  // come from the per-device scratch block.
+  K *keys = static_cast<K *>(out);
+  size_t temp = 0;
+  cub::DoubleBuffer<K> buffers(keys, nullptr);
+  cudaError_t e = descending ? cub::DeviceRadixSort::SortKeysDescending(nullptr, temp, buffers, count, 0,
+                                                                        int(sizeof(K) * 8), s)
+                             : cub::DeviceRadixSort::SortKeys(nullptr, temp, buffers, count, 0, int(sizeof(K) * 8), s);
+  if (int st = check_cuda(e, "sort (temporary size)")) return st;
+  const size_t alt_bytes = (n * sizeof(K) + 255) & ~size_t(255);
+  void *block = nullptr;
+  if (int st = scratch(alt_bytes + temp, &block)) return st;
+  buffers = cub::DoubleBuffer<K>(keys, static_cast<K *>(block));
+  void *temp_ptr = static_cast<char *>(block) + alt_bytes;
+  const unsigned grid = grid_for(n, 256, 8);
+  to_keys<K><<<grid, 256, 0, s>>>(static_cast<const K *>(a), keys, (long long)n);
+  if (int st = check_launch("sort (keys)")) return st;
+  e = descending ? cub::DeviceRadixSort::SortKeysDescending(temp_ptr, temp, buffers, count, 0, int(sizeof(K) * 8), s)
+                 : cub::DeviceRadixSort::SortKeys(temp_ptr, temp, buffers, count, 0, int(sizeof(K) * 8), s);
+  if (int st = check_cuda(e, "sort (radix)")) return st;
+  from_keys<K><<<grid, 256, 0, s>>>(buffers.Current(), keys, (long long)n);
+  return check_launch("sort (values)");
+}
+
+}  // namespace
+}  // namespace tc
+
+using namespace tc;
+
+extern "C" {
+
+int tc_unary(int dtype, int f, const void *a, void *out, size_t n, void *stream) {
+  if (f < TC_SIN || f > TC_SQRT) return fail(TC_EINVAL, "bad Analytic %d", f);
+  if (n == 0) return TC_OK;
+  if (!a || !out) return fail(TC_EINVAL, "unary: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    const bool vec = aligned16(a) && aligned16(out);
+    unary_kernel<T><<<grid_for((n + Pack<T>::N - 1) / Pack<T>::N, 256, 8), 256, 0, as_stream(stream)>>>(
+        static_cast<const S *>(a), static_cast<S *>(out), (long long)n, f, vec);
+    return check_launch("unary");
+  });
+}
+
+int tc_unary_dual(int dtype, int f, const void *value, const void *tangent, void *out_value, void *out_tangent,
+                  size_t n, void *stream) {
+  if (f < TC_SIN || f > TC_SQRT) return fail(TC_EINVAL, "bad Analytic %d", f);
+  if (n == 0) return TC_OK;
+  if (!value || !tangent || !out_value || !out_tangent) return fail(TC_EINVAL, "unary_dual: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    const bool vec = aligned16(value) && aligned16(tangent) && aligned16(out_value) && aligned16(out_tangent);
+    unary_dual_kernel<T><<<grid_for((n + Pack<T>::N - 1) / Pack<T>::N, 256, 8), 256, 0, as_stream(stream)>>>(
+        static_cast<const S *>(value), static_cast<const S *>(tangent), static_cast<S *>(out_value),
+        static_cast<S *>(out_tangent), (long long)n, f, vec);
+    return check_launch("unary_dual");
+  });
+}
+
+int tc_prefix_sum(int dtype, const void *a, void *out, size_t n, void *stream) {
+  if (n == 0) return TC_OK;
+  if (!a || !out) return fail(TC_EINVAL, "prefix_sum: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    cudaStream_t s = as_stream(stream);
+    const long long tiles = ((long long)n + SCAN_TILE - 1) / SCAN_TILE;
+    const long long want = std::min<long long>(MAX_CHUNKS, (long long)sm_count() * 4);
+    const long long per = ((tiles + want - 1) / want) * SCAN_TILE;
+    const int chunks = int(((long long)n + per - 1) / per);
+    float *sums = nullptr;
+    if (int st = scratch(MAX_CHUNKS * sizeof(float), reinterpret_cast<void **>(&sums))) return st;
+    const bool vec = aligned16(a) && aligned16(out);
+    chunk_sums<T><<<chunks, SCAN_THREADS, 0, s>>>(static_cast<const S *>(a), (long long)n, per, vec, sums);
+    if (int st = check_launch("prefix_sum (chunks)")) return st;
+    chunk_offsets<<<1, MAX_CHUNKS, 0, s>>>(sums, chunks);
+    if (int st = check_launch("prefix_sum (offsets)")) return st;
+    scan_chunks<T><<<chunks, SCAN_THREADS, 0, s>>>(static_cast<const S *>(a), static_cast<S *>(out), (long long)n,
+                                                   per, vec, sums);
+    return check_launch("prefix_sum (scan)");
+  });
+}
+
+int tc_sort(int dtype, int order, const void *a, void *out, size_t n, void *stream) {
+  if (order != TC_ASCENDING && order != TC_DESCENDING) return fail(TC_EINVAL, "bad SortOrder %d", order);
+  if (n == 0) return TC_OK;
+  if (!a || !out) return fail(TC_EINVAL, "sort: null pointer");
+  if (dtype == TC_F32) return sort_keys<uint32_t>(a, out, n, order == TC_DESCENDING, as_stream(stream));
+  if (dtype == TC_F16 || dtype == TC_BF16)
+    return sort_keys<uint16_t>(a, out, n, order == TC_DESCENDING, as_stream(stream));
+  return fail(TC_EINVAL, "unknown element type %d", dtype);
+}
+
+}  // extern "C"

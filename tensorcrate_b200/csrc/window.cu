@@ -1,0 +1,212 @@
+// window.cu — the windowed matrix methods of Kernels<T>: valid correlation
+// and its two gradients (correlate, correlate_window_gradient,
+// correlate_input_gradient, kernels.rs:998-1023), pad and flip
+// (kernels.rs:1025-1028).
+//
+// Correlation follows the Host's loops (kernels.rs:1720-1788): each output
+// is a sum over the window's taps in row-major tap order, `sum = sum + x*k`
+// with the product and the sum each rounded (Rust does not contract), in
+// f32 for f16/bf16 (widened exactly, the output rounded once).  A thread
+// that owns an output and walks the taps in that order with __fmul_rn /
+// __fadd_rn reproduces the Host's bits.  When the taps are many and the
+// outputs few (the window gradient, whose "window" is the whole adjoint),
+// a block shares one output instead: each thread sums its own stride of
+// the taps in order and the partial sums meet in a fixed tree, which keeps
+// the result deterministic but rounds within a sum's bound of the Host's.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace tc {
+namespace {
+
+struct Window {
+  long long in_rows, in_cols;    // the input read (correlate) or the adjoint (input gradient)
+  long long win_rows, win_cols;  // the taps
+  long long out_rows, out_cols;
+  bool flip;
+};
+
+// The tap (wr, wc) of the sum, flipped or not, as the Host indexes it.
+__device__ __forceinline__ long long tap_index(const Window &w, long long wr, long long wc) {
+  return w.flip ? (w.win_rows - 1 - wr) * w.win_cols + (w.win_cols - 1 - wc) : wr * w.win_cols + wc;
+}
+
+// One thread per output, the taps in the Host's order.
+template <class T>
+__global__ void __launch_bounds__(256) correlate_direct(const typename T::S *in, const typename T::S *win,
+                                                        typename T::S *out, Window w) {
+  const long long total = w.out_rows * w.out_cols;
+  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (long long)gridDim.x * blockDim.x) {
+    const long long row = o / w.out_cols, col = o - row * w.out_cols;
+    float sum = 0.0f;
+    for (long long wr = 0; wr < w.win_rows; ++wr) {
+      const typename T::S *x = in + (row + wr) * w.in_cols + col;
+      for (long long wc = 0; wc < w.win_cols; ++wc)
+        sum = __fadd_rn(sum, __fmul_rn(T::load(__ldg(x + wc)), T::load(__ldg(win + tap_index(w, wr, wc)))));
+    }
+    out[o] = T::store(sum);
+  }
+}
+
+// One block per output: thread t sums taps t, t+B, t+2B, ... in order; the
+// partial sums meet in a fixed tree.
+template <class T>
+__global__ void __launch_bounds__(256) correlate_shared(const typename T::S *in, const typename T::S *win,
+                                                        typename T::S *out, Window w) {
+  __shared__ float part[8];
+  const long long taps = w.win_rows * w.win_cols;
+  for (long long o = blockIdx.x; o < w.out_rows * w.out_cols; o += gridDim.x) {
+    const long long row = o / w.out_cols, col = o - row * w.out_cols;
+    float sum = 0.0f;
+    for (long long t = threadIdx.x; t < taps; t += blockDim.x) {
+      const long long wr = t / w.win_cols, wc = t - wr * w.win_cols;
+      sum = __fadd_rn(sum, __fmul_rn(T::load(__ldg(in + (row + wr) * w.in_cols + col + wc)),
+                                     T::load(__ldg(win + tap_index(w, wr, wc)))));
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, d));
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = part[0];
+      for (int k = 1; k < int(blockDim.x >> 5); ++k) s = __fadd_rn(s, part[k]);
+      out[o] = T::store(s);
+    }
+    __syncthreads();
+  }
+}
+
+// The input gradient (kernels.rs:1754-1788): output (p, q) sums adjoint
+// (p-u, q-v) times tap (u, v) over the taps whose adjoint index is in range,
+// in tap order, skipping the rest (they are not added as zeros).
+template <class T>
+__global__ void __launch_bounds__(256) correlate_input_gradient_direct(const typename T::S *adj,
+                                                                       const typename T::S *win, typename T::S *out,
+                                                                       Window w) {
+  const long long total = w.out_rows * w.out_cols;
+  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (long long)gridDim.x * blockDim.x) {
+    const long long row = o / w.out_cols, col = o - row * w.out_cols;
+    float sum = 0.0f;
+    const long long wr0 = max(0LL, row - (w.in_rows - 1)), wr1 = min(w.win_rows - 1, row);
+    const long long wc0 = max(0LL, col - (w.in_cols - 1)), wc1 = min(w.win_cols - 1, col);
+    for (long long wr = wr0; wr <= wr1; ++wr) {
+      const typename T::S *a = adj + (row - wr) * w.in_cols + col;
+      for (long long wc = wc0; wc <= wc1; ++wc)
+        sum = __fadd_rn(sum, __fmul_rn(T::load(__ldg(a - wc)), T::load(__ldg(win + tap_index(w, wr, wc)))));
+    }
+    out[o] = T::store(sum);
+  }
+}
+
+// pad (kernels.rs:1575-1601): zeros around the input, one thread per
+// output element, bits moved as they are.
+template <class E>
+__global__ void __launch_bounds__(256) pad_kernel(const E *in, E *out, long long rows, long long cols,
+                                                  long long pr, long long pc) {
+  const long long ocols = cols + 2 * pc, total = (rows + 2 * pr) * ocols;
+  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (long long)gridDim.x * blockDim.x) {
+    const long long r = o / ocols - pr, c = o % ocols - pc;
+    out[o] = (r >= 0 && r < rows && c >= 0 && c < cols) ? in[r * cols + c] : E(0);
+  }
+}
+
+// flip (kernels.rs:1531-1542): out[r][c] = in[rows-1-r][cols-1-c], which is
+// the whole matrix reversed in storage order.
+template <class E>
+__global__ void __launch_bounds__(256) flip_kernel(const E *in, E *out, long long n) {
+  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < n; o += (long long)gridDim.x * blockDim.x)
+    out[o] = __ldg(in + (n - 1 - o));
+}
+
+int run_correlate(int dtype, const Window &w, const void *in, const void *win, void *out, cudaStream_t s) {
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    const long long outputs = w.out_rows * w.out_cols, taps = w.win_rows * w.win_cols;
+    if (taps >= 4096 && outputs < (long long)sm_count() * 64) {
+      const unsigned grid = unsigned(std::min<long long>(outputs, (long long)sm_count() * 8));
+      correlate_shared<T><<<grid, 256, 0, s>>>(static_cast<const S *>(in), static_cast<const S *>(win),
+                                               static_cast<S *>(out), w);
+    } else {
+      correlate_direct<T><<<grid_for(outputs, 256, 8), 256, 0, s>>>(static_cast<const S *>(in),
+                                                                      static_cast<const S *>(win),
+                                                                      static_cast<S *>(out), w);
+    }
+    return check_launch("correlate");
+  });
+}
+
+}  // namespace
+}  // namespace tc
+
+using namespace tc;
+
+extern "C" {
+
+int tc_correlate(int dtype, size_t rows, size_t cols, size_t window_rows, size_t window_cols, int flip,
+                 const void *input, const void *window, void *out, void *stream) {
+  if (window_rows > rows || window_cols > cols)
+    return fail(TC_EINVAL, "correlate: a %zux%zu window does not fit in a %zux%zu input", window_rows, window_cols,
+                rows, cols);
+  if (window_rows == 0 || window_cols == 0)
+    return fail(TC_EINVAL, "correlate: the window is empty");
+  Window w{(long long)rows, (long long)cols, (long long)window_rows, (long long)window_cols,
+           (long long)(rows - window_rows + 1), (long long)(cols - window_cols + 1), flip != 0};
+  if (!input || !window || !out) return fail(TC_EINVAL, "correlate: null pointer");
+  return run_correlate(dtype, w, input, window, out, as_stream(stream));
+}
+
+int tc_correlate_window_gradient(int dtype, size_t rows, size_t cols, size_t adjoint_rows, size_t adjoint_cols,
+                                 const void *input, const void *adjoint, void *out, void *stream) {
+  return tc_correlate(dtype, rows, cols, adjoint_rows, adjoint_cols, 0, input, adjoint, out, stream);
+}
+
+int tc_correlate_input_gradient(int dtype, size_t adjoint_rows, size_t adjoint_cols, size_t window_rows,
+                                size_t window_cols, int forward_flip, const void *adjoint, const void *window,
+                                void *out, void *stream) {
+  if (window_rows == 0 || window_cols == 0 || adjoint_rows == 0 || adjoint_cols == 0)
+    return fail(TC_EINVAL, "correlate_input_gradient: empty operand");
+  Window w{(long long)adjoint_rows, (long long)adjoint_cols, (long long)window_rows, (long long)window_cols,
+           (long long)(adjoint_rows + window_rows - 1), (long long)(adjoint_cols + window_cols - 1),
+           forward_flip != 0};
+  if (!adjoint || !window || !out) return fail(TC_EINVAL, "correlate_input_gradient: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    correlate_input_gradient_direct<T><<<grid_for(w.out_rows * w.out_cols, 256, 8), 256, 0, as_stream(stream)>>>(
+        static_cast<const S *>(adjoint), static_cast<const S *>(window), static_cast<S *>(out), w);
+    return check_launch("correlate_input_gradient");
+  });
+}
+
+int tc_pad(int dtype, size_t rows, size_t cols, size_t pad_rows, size_t pad_cols, const void *input, void *out,
+           void *stream) {
+  const size_t total = (rows + 2 * pad_rows) * (cols + 2 * pad_cols);
+  if (total == 0) return TC_OK;
+  if ((rows * cols && !input) || !out) return fail(TC_EINVAL, "pad: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using S = typename decltype(t)::S;
+    pad_kernel<S><<<grid_for(total, 256, 8), 256, 0, as_stream(stream)>>>(
+        static_cast<const S *>(input), static_cast<S *>(out), (long long)rows, (long long)cols,
+        (long long)pad_rows, (long long)pad_cols);
+    return check_launch("pad");
+  });
+}
+
+int tc_flip(int dtype, size_t rows, size_t cols, const void *input, void *out, void *stream) {
+  const size_t n = rows * cols;
+  if (n == 0) return TC_OK;
+  if (!input || !out) return fail(TC_EINVAL, "flip: null pointer");
+  return with_real(dtype, [&](auto t) {
+    using S = typename decltype(t)::S;
+    flip_kernel<S><<<grid_for(n, 256, 8), 256, 0, as_stream(stream)>>>(static_cast<const S *>(input),
+                                                                        static_cast<S *>(out), (long long)n);
+    return check_launch("flip");
+  });
+}
+
+}  // extern "C"

@@ -535,6 +535,50 @@ class Cuda:
         N.call("tc_dot", N.DTYPES[a.dtype], a.ptr, b.ptr, a.len, out.ptr, _stream(stream))
         return out
 
+    @staticmethod
+    def vector_prefix_sum(a: CudaStorage, stream=None) -> CudaStorage:
+        out = CudaStorage(a.dtype, a.len)
+        N.call("tc_prefix_sum", N.DTYPES[a.dtype], a.ptr, out.ptr, a.len, _stream(stream))
+        return out
+
+    @staticmethod
+    def vector_sort(a: CudaStorage, order: int, stream=None) -> CudaStorage:
+        out = CudaStorage(a.dtype, a.len)
+        N.call("tc_sort", N.DTYPES[a.dtype], order, a.ptr, out.ptr, a.len, _stream(stream))
+        return out
+
+    @staticmethod
+    def vector_unary(a: CudaStorage, f: int, stream=None) -> CudaStorage:
+        """vector_unary / matrix_unary: f an Analytic."""
+        out = CudaStorage(a.dtype, a.len)
+        N.call("tc_unary", N.DTYPES[a.dtype], f, a.ptr, out.ptr, a.len, _stream(stream))
+        return out
+
+    @staticmethod
+    def vector_unary_dual(value: CudaStorage, tangent: CudaStorage, f: int,
+                          stream=None) -> tuple[CudaStorage, CudaStorage]:
+        if value.len != tangent.len:
+            raise ValueError("unary_dual: value and tangent lengths differ")
+        out_v, out_t = CudaStorage(value.dtype, value.len), CudaStorage(value.dtype, value.len)
+        N.call("tc_unary_dual", N.DTYPES[value.dtype], f, value.ptr, tangent.ptr, out_v.ptr, out_t.ptr, value.len,
+               _stream(stream))
+        return out_v, out_t
+
+    @staticmethod
+    def vector_power(a: CudaStorage, b: CudaStorage, stream=None) -> CudaStorage:
+        if a.len != b.len:
+            raise ValueError(f"pow: lengths {a.len} and {b.len} differ")
+        out = CudaStorage(a.dtype, a.len)
+        N.call("tc_power", N.DTYPES[a.dtype], a.ptr, b.ptr, out.ptr, a.len, _stream(stream))
+        return out
+
+    @staticmethod
+    def vector_power_scalar(a: CudaStorage, scalar: float, scalar_left: bool, stream=None) -> CudaStorage:
+        out = CudaStorage(a.dtype, a.len)
+        N.call("tc_power_scalar", N.DTYPES[a.dtype], a.ptr, float(scalar), int(scalar_left), out.ptr, a.len,
+               _stream(stream))
+        return out
+
     # --- products (kernels.rs:899-985) ---
     @staticmethod
     def matmul(a: CudaStorage, b: CudaStorage, rows: int, inner: int, cols: int, transposed: int = N.TRANS_NONE,

@@ -161,6 +161,83 @@ def kats():
     for mag in (0.01, 1.0, 100.0):
         k.append(dict(id=f"adam_first_step_{mag}", source="tests/optim.rs:95-100", kind="adam_first", dtype="f32",
                       rate=0.1, g=[mag], p=[0.0], expect=[-0.1], tol=2e-3 * 1.1))
+
+    # tests/math_macro.rs:507-513: prefix_sum and sorted of small literals
+    k.append(dict(id="prefix_sum_literal", source="tests/math_macro.rs:507-508", kind="prefix_sum", dtype="f32",
+                  input=[1.0, 2.0, 3.0, 4.0], expect=[1.0, 3.0, 6.0, 10.0]))
+    for order, want in ((0, [-1.0, 2.0, 3.0]), (1, [3.0, 2.0, -1.0])):
+        k.append(dict(id=f"sorted_literal_{order}", source="tests/math_macro.rs:510-513", kind="sort", dtype="f32",
+                      order=order, input_bits=None, input=[3.0, -1.0, 2.0], expect=want))
+    # tests/dtypes.rs:110-116: a bf16 vector sorted descending through the trait
+    k.append(dict(id="bf16_sorted_descending", source="tests/dtypes.rs:110-116", kind="sort", dtype="bf16", order=1,
+                  input_bits=None, input=[1.0, 3.0, 2.0], expect=[3.0, 2.0, 1.0]))
+    # tests/ordering.rs:122-135: the total order puts -NaN first, -0.0 before
+    # +0.0 and +NaN last (f32::NAN is 0x7fc00000, -f32::NAN 0xffc00000)
+    k.append(dict(id="sort_awkward_total_order", source="tests/ordering.rs:122-135", kind="sort", dtype="f32",
+                  order=0, input_bits=[0x7FC00000, 0x00000000, 0x80000000, 0xFFC00000, 0x3F800000, 0xFF800000],
+                  expect_bits={"0": 0xFFC00000, "1": 0xFF800000, "2": 0x80000000, "3": 0x00000000,
+                               "5": 0x7FC00000}))
+
+    # tests/conv.rs:54-69: correlation and convolution worked out by hand
+    i33 = [1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0, 8.0, 9.0]
+    taps = [1.0, 10.0, 100.0, 1000.0]
+    k.append(dict(id="correlate_by_hand", source="tests/conv.rs:54-66", kind="correlate", dtype="f32",
+                  shape=[3, 3], window_shape=[2, 2], flip=0, input=i33, window=taps,
+                  expect=[5421.0, 6532.0, 8754.0, 9865.0]))
+    k.append(dict(id="convolve_by_hand", source="tests/conv.rs:68-69", kind="correlate", dtype="f32",
+                  shape=[3, 3], window_shape=[2, 2], flip=1, input=i33, window=taps,
+                  expect=[1245.0, 2356.0, 4578.0, 5689.0]))
+    for flip in (0, 1):
+        k.append(dict(id=f"correlate_unit_window_{flip}", source="tests/conv.rs:71-80", kind="correlate",
+                      dtype="f32", shape=[3, 3], window_shape=[1, 1], flip=flip, input=i33, window=[3.0],
+                      expect=[3.0 * v for v in i33]))
+    # tests/conv.rs:95-117: padding and flipping
+    i22 = [1.0, 2.0, 3.0, 4.0]
+    k.append(dict(id="pad_1_1", source="tests/conv.rs:98-106", kind="pad", dtype="f32", shape=[2, 2], pad=[1, 1],
+                  input=i22, expect=[0, 0, 0, 0, 0, 1, 2, 0, 0, 3, 4, 0, 0, 0, 0, 0]))
+    k.append(dict(id="pad_0_2", source="tests/conv.rs:108-113", kind="pad", dtype="f32", shape=[2, 2], pad=[0, 2],
+                  input=i22, expect=[0, 0, 1, 2, 0, 0, 0, 0, 3, 4, 0, 0]))
+    k.append(dict(id="pad_0_0", source="tests/conv.rs:114", kind="pad", dtype="f32", shape=[2, 2], pad=[0, 0],
+                  input=i22, expect=i22))
+    k.append(dict(id="flip_2x2", source="tests/conv.rs:116", kind="flip", dtype="f32", shape=[2, 2], input=i22,
+                  expect=[4.0, 3.0, 2.0, 1.0]))
+
+    # tests/statistics.rs:198-233: moments over every element; an empty
+    # vector has NaN moments
+    k.append(dict(id="moments_eight", source="tests/statistics.rs:199-209", kind="moments", dtype="f32",
+                  input=[2.0, 4.0, 4.0, 4.0, 5.0, 5.0, 7.0, 9.0], expect=[5.0, 32.0]))
+    k.append(dict(id="moments_matrix_2x2", source="tests/statistics.rs:211-212", kind="moments", dtype="f32",
+                  input=[1.0, 2.0, 3.0, 4.0], expect=[2.5, 5.0]))
+    k.append(dict(id="moments_single", source="tests/statistics.rs:227-229", kind="moments", dtype="f32",
+                  input=[7.0], expect=[7.0, 0.0]))
+    k.append(dict(id="moments_empty", source="tests/statistics.rs:232-234", kind="moments", dtype="f32",
+                  input=[], expect=[NAN, NAN]))
+    # tests/statistics.rs:238-252: axis moments fold the axis they name
+    m34 = [1.0, 2.0, 3.0, 4.0, 10.0, 20.0, 30.0, 40.0, -1.0, -2.0, -3.0, -4.0]
+    k.append(dict(id="axis_means_rows", source="tests/statistics.rs:245", kind="axis_moments", dtype="f32",
+                  shape=[3, 4], axis=0, input=m34, expect_means=[2.5, 25.0, -2.5]))
+    k.append(dict(id="axis_means_columns", source="tests/statistics.rs:246-249", kind="axis_moments", dtype="f32",
+                  shape=[3, 4], axis=1, input=m34, expect_means_f64=[10.0 / 3.0, 20.0 / 3.0, 10.0, 40.0 / 3.0]))
+    # tests/statistics.rs:82-118: published values of the standard normal
+    # cdf and quantile (mean 0, stddev 1), and the quantile's edges
+    for z, want in ((0.0, 0.5), (1.0, 0.8413447460685429), (-1.0, 0.1586552539314571), (1.96, 0.9750021048517795),
+                    (-3.0, 0.001349898031630095)):
+        k.append(dict(id=f"normal_cdf_{z}", source="tests/statistics.rs:84-99", kind="distribution", family=0,
+                      statistic=1, params=[0.0, 1.0], x=z, expect_f64=want))
+    for p, want in ((0.95, 1.6448536269514722), (0.975, 1.959963984540054), (0.99, 2.326347874040841),
+                    (0.5, 0.0), (0.0, NINF), (1.0, INF), (1.5, NAN), (-0.5, NAN)):
+        k.append(dict(id=f"normal_ppf_{p}", source="tests/statistics.rs:101-118", kind="distribution", family=0,
+                      statistic=2, params=[0.0, 1.0], x=p, expect_f64=want))
+    # tests/statistics.rs:182-194: the inverse Gaussian's edges
+    for id_, stat, x, params, want in (("ig_cdf_at_zero", 1, 0.0, [1.0, 1.0], 0.0),
+                                       ("ig_pdf_below_zero", 0, -1.0, [1.0, 1.0], 0.0),
+                                       ("ig_ppf_at_zero", 2, 0.0, [1.0, 1.0], 0.0),
+                                       ("ig_ppf_at_one", 2, 1.0, [1.0, 1.0], INF),
+                                       ("ig_cdf_negative_mean", 1, 1.0, [-1.0, 1.0], NAN)):
+        k.append(dict(id=id_, source="tests/statistics.rs:182-186", kind="distribution", family=1, statistic=stat,
+                      params=params, x=x, expect_f64=want))
+    k.append(dict(id="ig_cdf_extreme_shape", source="tests/statistics.rs:188-193", kind="distribution", family=1,
+                  statistic=1, params=[1.0, 1e6], x=1.0, expect_f64=0.5, tol=1e-3))
     return k
 
 

@@ -1,0 +1,134 @@
+"""The windowed matrix methods through the C ABI: correlate and its two
+gradients (kernels.rs:998-1023; Host 1514-1573, 1720-1788), pad and flip
+(kernels.rs:1025-1028; Host 1531-1542, 1575-1601), against the oracle.
+
+Parity: a thread per output walks the taps in the Host's order with
+rounded products and sums, so those results are the Host's bits; the
+shared-output path (4096 taps or more, few outputs) is held to an f32 sum's
+rounding; pad and flip move bits.  The worked examples of tests/conv.rs
+run through the GPU as well."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tensorcrate_b200 import _native as N
+from tensorcrate_b200 import cuda
+from util import DTYPES, kats, uniform
+
+pytestmark = pytest.mark.gpu
+
+
+def _store(x, dtype):
+    return cuda.CudaStorage.store(x, dtype)
+
+
+def correlate_gpu(x, w, shape, wshape, flip, dtype):
+    (r, c), (wr, wc) = shape, wshape
+    out = cuda.CudaStorage(dtype, (r - wr + 1) * (c - wc + 1))
+    dx, dw = _store(x, dtype), _store(w, dtype)  # held until the result is read
+    N.call("tc_correlate", N.DTYPES[dtype], r, c, wr, wc, int(flip), dx.ptr, dw.ptr, out.ptr, None)
+    return out.as_slice()
+
+
+def correlate_oracle(x, w, shape, wshape, flip, dtype):
+    (r, c), (wr, wc) = shape, wshape
+    out = np.empty((r - wr + 1) * (c - wc + 1), x.dtype)
+    O.call("orc_correlate", O.DTYPES[dtype], r, c, wr, wc, int(flip), O.ptr(x), O.ptr(w), O.ptr(out))
+    return out
+
+
+@pytest.mark.parametrize("k", kats("correlate"), ids=lambda k: k["id"])
+def test_correlate_worked_examples(device, k):
+    x, w = np.array(k["input"], np.float32), np.array(k["window"], np.float32)
+    got = correlate_gpu(x, w, k["shape"], k["window_shape"], k["flip"], "f32")
+    assert list(got) == k["expect"]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape,wshape", [((8, 9), (3, 2)), ((64, 100), (5, 7)), ((1, 1), (1, 1)),
+                                          ((33, 257), (33, 1)), ((300, 40), (1, 40)), ((60, 60), (60, 60))])
+@pytest.mark.parametrize("flip", [False, True])
+def test_correlate_is_the_hosts_bits(device, dtype, shape, wshape, flip):
+    x = O.narrow(uniform(shape[0] * shape[1], 1), dtype)
+    w = O.narrow(uniform(wshape[0] * wshape[1], 2), dtype)
+    got = correlate_gpu(x, w, shape, wshape, flip, dtype)
+    want = correlate_oracle(x, w, shape, wshape, flip, dtype)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_window_gradient_with_many_taps_within_sum_rounding(device, dtype):
+    """The window gradient of a 300x300 input (a 298x298 adjoint, 88804
+    taps per output): a block per output, a tree of partial sums."""
+    r = c = 300
+    ar = ac = 298
+    x = O.narrow(uniform(r * c, 3), dtype)
+    adj = O.narrow(uniform(ar * ac, 4), dtype)
+    out = cuda.CudaStorage(dtype, 9)
+    dx, dadj = _store(x, dtype), _store(adj, dtype)
+    N.call("tc_correlate_window_gradient", N.DTYPES[dtype], r, c, ar, ac, dx.ptr, dadj.ptr, out.ptr, None)
+    got = O.widen(out.as_slice(), dtype).astype(np.float64)
+    want = O.widen(correlate_oracle(x, adj, (r, c), (ar, ac), False, dtype), dtype).astype(np.float64)
+    xs, ads = O.widen(x, dtype).reshape(r, c), O.widen(adj, dtype).reshape(ar, ac)
+    scale = np.array([np.sum(np.abs(xs[a:a + ar, b:b + ac] * ads)) for a in range(3) for b in range(3)])
+    taps = ar * ac
+    tol = 2.0 * np.sqrt(taps) * 2.0 ** -24 * scale * 8
+    half = 0.0 if dtype == "f32" else (2.0 ** -7 if dtype == "bf16" else 2.0 ** -10) * np.abs(want)
+    assert np.all(np.abs(got - want) <= tol + half)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("ashape,wshape", [((30, 40), (3, 5)), ((2, 3), (5, 4)), ((17, 1), (1, 1)),
+                                           ((64, 64), (7, 7))])
+@pytest.mark.parametrize("forward_flip", [False, True])
+def test_correlate_input_gradient_is_the_hosts_bits(device, dtype, ashape, wshape, forward_flip):
+    (ar, ac), (wr, wc) = ashape, wshape
+    adj = O.narrow(uniform(ar * ac, 5), dtype)
+    w = O.narrow(uniform(wr * wc, 6), dtype)
+    rows, cols = ar + wr - 1, ac + wc - 1
+    out = cuda.CudaStorage(dtype, rows * cols)
+    dadj, dw = _store(adj, dtype), _store(w, dtype)
+    N.call("tc_correlate_input_gradient", N.DTYPES[dtype], ar, ac, wr, wc, int(forward_flip), dadj.ptr, dw.ptr,
+           out.ptr, None)
+    want = np.empty(rows * cols, adj.dtype)
+    O.call("orc_correlate_input_gradient", O.DTYPES[dtype], ar, ac, wr, wc, int(forward_flip), O.ptr(adj), O.ptr(w),
+           O.ptr(want))
+    assert np.array_equal(out.as_slice(), want)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape,pad", [((2, 2), (1, 1)), ((7, 5), (2, 3)), ((7, 5), (0, 0)), ((0, 4), (2, 1)),
+                                       ((1000, 1000), (3, 9))])
+def test_pad_moves_bits(device, dtype, shape, pad):
+    (r, c), (pr, pc) = shape, pad
+    x = O.narrow(uniform(max(1, r * c), 7)[: r * c], dtype)
+    out = cuda.CudaStorage(dtype, (r + 2 * pr) * (c + 2 * pc))
+    src = _store(x, dtype) if r * c else None
+    N.call("tc_pad", N.DTYPES[dtype], r, c, pr, pc, src.ptr if src else None, out.ptr, None)
+    want = np.empty((r + 2 * pr) * (c + 2 * pc), x.dtype)
+    O.call("orc_pad", O.DTYPES[dtype], r, c, pr, pc, O.ptr(x), O.ptr(want))
+    assert np.array_equal(out.as_slice(), want)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", [(2, 2), (1, 1), (7, 5), (1000, 1001)])
+def test_flip_moves_bits_and_is_an_involution(device, dtype, shape):
+    r, c = shape
+    x = O.narrow(uniform(r * c, 8), dtype)
+    once = cuda.CudaStorage(dtype, r * c)
+    dx = _store(x, dtype)
+    N.call("tc_flip", N.DTYPES[dtype], r, c, dx.ptr, once.ptr, None)
+    want = np.empty_like(x)
+    O.call("orc_flip", O.DTYPES[dtype], r, c, O.ptr(x), O.ptr(want))
+    assert np.array_equal(once.as_slice(), want)
+    twice = cuda.CudaStorage(dtype, r * c)
+    N.call("tc_flip", N.DTYPES[dtype], r, c, once.ptr, twice.ptr, None)
+    assert np.array_equal(twice.as_slice(), x)
+
+
+def test_correlate_rejects_a_window_that_does_not_fit(device):
+    x = _store(np.zeros(6, np.float32), "f32")
+    out = cuda.CudaStorage("f32", 1)
+    assert N.lib().tc_correlate(N.F32, 2, 3, 3, 1, 0, x.ptr, x.ptr, out.ptr, None) == N.EINVAL

@@ -134,6 +134,174 @@ def test_elementwise_kats(k):
     assert same_floats(O.widen(out, k["dtype"]), expand(k["expect"]))
 
 
+@pytest.mark.parametrize("k", kats("prefix_sum"), ids=lambda k: k["id"])
+def test_prefix_sum_kats(k):
+    a = O.narrow(expand(k["input"]), k["dtype"])
+    out = np.empty_like(a)
+    O.call("orc_prefix_sum", O.DTYPES[k["dtype"]], O.ptr(a), O.ptr(out), a.size)
+    assert same_floats(O.widen(out, k["dtype"]), expand(k["expect"]))
+
+
+@pytest.mark.parametrize("k", kats("sort"), ids=lambda k: k["id"])
+def test_sort_kats(k):
+    if k["input_bits"] is not None:
+        a = np.array(k["input_bits"], np.uint32).view(np.float32)
+    else:
+        a = O.narrow(expand(k["input"]), k["dtype"])
+    out = np.empty_like(a)
+    O.call("orc_sort", O.DTYPES[k["dtype"]], k["order"], O.ptr(a), O.ptr(out), a.size)
+    if "expect_bits" in k:
+        bits = out.view(np.uint32)
+        for i, want in k["expect_bits"].items():
+            assert int(bits[int(i)]) == want, i
+    else:
+        assert same_floats(O.widen(out, k["dtype"]), expand(k["expect"]))
+
+
+def test_sort_matches_numpy_on_distinct_values():
+    """Away from NaNs and signed zeros the total order is the numeric one."""
+    a = normal(10000, 5)
+    for order in (0, 1):
+        out = np.empty_like(a)
+        O.call("orc_sort", O.DTYPES["f32"], order, O.ptr(a), O.ptr(out), a.size)
+        want = np.sort(a) if order == 0 else np.sort(a)[::-1]
+        assert np.array_equal(out, want)
+
+
+def test_prefix_sum_of_the_integral_filler_is_exact():
+    a = integral(100000)
+    out = np.empty_like(a)
+    O.call("orc_prefix_sum", O.DTYPES["f32"], O.ptr(a), O.ptr(out), a.size)
+    assert np.array_equal(out, np.cumsum(a.astype(np.float64)).astype(np.float32))
+
+
+@pytest.mark.parametrize("k", kats("correlate"), ids=lambda k: k["id"])
+def test_correlate_kats(k):
+    x, w = np.array(k["input"], np.float32), np.array(k["window"], np.float32)
+    (r, c), (wr, wc) = k["shape"], k["window_shape"]
+    out = np.empty((r - wr + 1) * (c - wc + 1), np.float32)
+    O.call("orc_correlate", O.DTYPES["f32"], r, c, wr, wc, k["flip"], O.ptr(x), O.ptr(w), O.ptr(out))
+    assert list(out) == k["expect"]
+
+
+@pytest.mark.parametrize("k", kats("pad") + kats("flip"), ids=lambda k: k["id"])
+def test_pad_and_flip_kats(k):
+    x = np.array(k["input"], np.float32)
+    r, c = k["shape"]
+    if k["kind"] == "pad":
+        pr, pc = k["pad"]
+        out = np.empty((r + 2 * pr) * (c + 2 * pc), np.float32)
+        O.call("orc_pad", O.DTYPES["f32"], r, c, pr, pc, O.ptr(x), O.ptr(out))
+    else:
+        out = np.empty(r * c, np.float32)
+        O.call("orc_flip", O.DTYPES["f32"], r, c, O.ptr(x), O.ptr(out))
+    assert list(out) == list(map(float, k["expect"]))
+
+
+def test_convolution_is_correlation_with_the_window_flipped():
+    """tests/conv.rs:118-126."""
+    x, w = uniform(4 * 5, 3), uniform(2 * 3, 4)
+    conv, flipped, corr = np.empty(3 * 3, np.float32), np.empty(6, np.float32), np.empty(3 * 3, np.float32)
+    O.call("orc_correlate", O.DTYPES["f32"], 4, 5, 2, 3, 1, O.ptr(x), O.ptr(w), O.ptr(conv))
+    O.call("orc_flip", O.DTYPES["f32"], 2, 3, O.ptr(w), O.ptr(flipped))
+    O.call("orc_correlate", O.DTYPES["f32"], 4, 5, 2, 3, 0, O.ptr(x), O.ptr(flipped), O.ptr(corr))
+    assert np.array_equal(conv, corr)
+
+
+def test_correlate_gradients_match_numpy():
+    """The window gradient is the input correlated with the adjoint, and the
+    input gradient the full correlation: both against f64 numpy sums."""
+    x, w, adj = uniform((6, 7), 5), uniform((3, 2), 6), uniform((4, 6), 7)
+    got = np.empty((6, 7), np.float32)
+    O.call("orc_correlate_input_gradient", O.DTYPES["f32"], 4, 6, 3, 2, 0, O.ptr(adj), O.ptr(w), O.ptr(got))
+    want = np.zeros((6, 7))
+    for i in range(4):
+        for j in range(6):
+            want[i:i + 3, j:j + 2] += adj[i, j] * w.astype(np.float64)
+    assert np.allclose(got, want, atol=1e-5)
+    gw = np.empty((3, 2), np.float32)
+    O.call("orc_correlate", O.DTYPES["f32"], 6, 7, 4, 6, 0, O.ptr(x), O.ptr(adj), O.ptr(gw))
+    want_w = np.array([[np.sum(x[a:a + 4, b:b + 6].astype(np.float64) * adj) for b in range(2)] for a in range(3)])
+    assert np.allclose(gw, want_w, atol=1e-5)
+
+
+@pytest.mark.parametrize("k", kats("moments"), ids=lambda k: k["id"])
+def test_moments_kats(k):
+    a = np.array(expand(k["input"]), np.float32)
+    out = np.empty(2, np.float32)
+    O.call("orc_moments", O.DTYPES["f32"], O.ptr(a), a.size, O.ptr(out))
+    assert same_floats(out, expand(k["expect"]))
+
+
+@pytest.mark.parametrize("k", kats("axis_moments"), ids=lambda k: k["id"])
+def test_axis_moments_kats(k):
+    a = np.array(k["input"], np.float32)
+    r, c = k["shape"]
+    extent = r if k["axis"] == 0 else c
+    means, devs = np.empty(extent, np.float32), np.empty(extent, np.float32)
+    O.call("orc_axis_moments", O.DTYPES["f32"], r, c, k["axis"], O.ptr(a), O.ptr(means), O.ptr(devs))
+    want = k.get("expect_means") or [np.float32(v) for v in k["expect_means_f64"]]
+    assert list(means) == list(np.array(want, np.float32))
+
+
+@pytest.mark.parametrize("k", kats("distribution"), ids=lambda k: k["id"])
+def test_distribution_kats(k):
+    """In f64, as tests/statistics.rs checks them: within 1e-14 relative
+    (max(|want|, 1)) of the published value, or the stated tolerance."""
+    got = O.lib().orc_evaluate_f64(k["family"], k["statistic"], _value_of(k["x"]), k["params"][0], k["params"][1])
+    want = _value_of(k["expect_f64"])
+    if np.isnan(want) or np.isinf(want):
+        assert (np.isnan(got) and np.isnan(want)) or got == want
+    else:
+        assert abs(got - want) <= k.get("tol", 1e-14) * max(abs(want), 1.0)
+
+
+def test_distribution_rounds_the_f64_value_once():
+    """The f32/f16/bf16 results are the f64 value rounded once, to nearest."""
+    x = np.array([0.5, 0.95, 0.975, 0.99, 0.001, 0.999, 0.3, 0.7], np.float32)
+    for dtype in ("f32", "f16", "bf16"):
+        xs = O.narrow(x, dtype)
+        out = np.empty_like(xs)
+        O.call("orc_distribution", O.DTYPES[dtype], 0, 2, O.ptr(xs), xs.size, 0.0, 1.0, O.ptr(out))
+        exact = np.array([O.lib().orc_evaluate_f64(0, 2, float(v), 0.0, 1.0) for v in O.widen(xs, dtype)])
+        if dtype == "f32":
+            assert np.array_equal(out, exact.astype(np.float32))
+        elif dtype == "f16":
+            assert np.array_equal(out.view(np.float16), exact.astype(np.float16))
+        else:
+            got = O.widen(out, dtype).astype(np.float64)
+            assert np.array_equal(np.isinf(got), np.isinf(exact))
+            nz = (got != 0) & np.isfinite(got)
+            ulp = np.exp2(np.floor(np.log2(np.abs(got[nz]))) - 7)
+            assert np.all(np.abs(got[nz] - exact[nz]) <= 0.5 * ulp)
+
+
+def test_normal_quantile_inverts_the_cdf():
+    """tests/statistics.rs:120-143: cdf(ppf(p)) = p within 1e-13 across the
+    interval and 1e-12 far into the tail."""
+    ev = O.lib().orc_evaluate_f64
+    for i in range(1, 10000, 7):
+        p = i / 10000.0
+        assert abs(ev(0, 1, ev(0, 2, p, 0.0, 1.0), 0.0, 1.0) - p) <= 1e-13 * max(p, 1.0)
+    for p in (1e-300, 1e-100, 1e-20, 1e-8, 1e-3):
+        assert abs(ev(0, 1, ev(0, 2, p, 0.0, 1.0), 0.0, 1.0) - p) <= 1e-12 * max(p, 1.0)
+
+
+def test_inverse_gaussian_quantile_inverts_its_cdf():
+    """tests/statistics.rs:146-165: the solved quantile round-trips within
+    1e-12 for the reference's five parameter pairs."""
+    ev = O.lib().orc_evaluate_f64
+    for mean, shape in ((1.0, 1.0), (1.0, 3.0), (2.0, 0.5), (0.5, 20.0), (1.0, 100.0)):
+        for i in range(1, 500, 3):
+            p = i / 500.0
+            x = ev(1, 2, p, mean, shape)
+            assert abs(ev(1, 1, x, mean, shape) - p) <= 1e-12 * max(p, 1.0), (mean, shape, p)
+
+
+def _value_of(v):
+    return expand([v])[0]
+
+
 def test_sgd_kat():
     (k,) = kats("sgd")
     p, g = np.array(k["p"], np.float32), np.array(k["g"], np.float32)

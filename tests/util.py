@@ -47,3 +47,24 @@ def same_floats(got: np.ndarray, want: np.ndarray) -> bool:
     """Equal, with NaN equal to NaN (positions must agree)."""
     got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
     return got.shape == want.shape and bool(np.all((got == want) | (np.isnan(got) & np.isnan(want))))
+
+
+def bits_of(values, dtype):
+    return np.asarray(values).view(np.uint32 if dtype == "f32" else np.uint16).astype(np.int64)
+
+
+def steps(got, want, dtype):
+    """How many representable values of `dtype` lie between got and want
+    (0 = same bits; NaNs compare equal to NaNs)."""
+    width = 32 if dtype == "f32" else 16
+    sign = 1 << (width - 1)
+
+    def ordered(b):
+        return np.where(b & sign, -(b & (sign - 1)), b)
+
+    g, w = bits_of(got, dtype), bits_of(want, dtype)
+    d = np.abs(ordered(g) - ordered(w))
+    import oracle as O
+
+    gf, wf = O.widen(np.asarray(got), dtype), O.widen(np.asarray(want), dtype)
+    return np.where(np.isnan(gf) & np.isnan(wf), 0, d)
