@@ -460,6 +460,40 @@ typedef struct tc_place {
 int tc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
              const tc_place *places, uint32_t n_places, void *const *outputs,
              const int *out_dtypes, uint32_t n_outputs, void *stream);
+/* RowStatistic, src/tensors/fused/mod.rs:544-553. */
+enum tc_row_statistic_kind { TC_ROW_MEAN = 0, TC_ROW_DEVIATIONS = 1 };
+/* One statistic a program reads (Builder::row_statistic,
+ * fused/mod.rs:1832): loads of place `into_place` read, for each row of the
+ * space, the mean or the sum of squared deviations of that row of place
+ * `of_place` (as Kernels::row_moments gives them, rounded to the program's
+ * type).  `into_place` needs no data. */
+typedef struct tc_row_statistic {
+  uint32_t of_place, into_place;
+  int statistic;
+} tc_row_statistic;
+/* `fused_with_statistics` (kernels.rs:1103-1117): `program` with its row
+ * statistics computed in the same launch, one warp per row: the warp reduces
+ * the row's statistics (two passes, f32, as row_moments), then runs the
+ * program over the row's elements, which read them.  At most 8 places may
+ * be the source of statistics. */
+int tc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr *code,
+                             uint32_t n_code, const tc_place *places, uint32_t n_places,
+                             const tc_row_statistic *stats, uint32_t n_stats,
+                             void *const *outputs, const int *out_dtypes, uint32_t n_outputs,
+                             void *stream);
+/* `fused_sum` (kernels.rs:1120-1135; Program::run_sum, fused/mod.rs:1048):
+ * a program with one output of its own type, that output summed along
+ * `axis` (TC_ROWS: one sum per row, `rows` results; TC_COLUMNS: one per
+ * column) without being stored: each value rounded to the type, the sums
+ * in f32, rounded once.  Columns with many rows use the per-device scratch
+ * block for their bands' partial sums. */
+int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
+                 const tc_place *places, uint32_t n_places, int axis, void *sums, void *stream);
+/* `row_moments` (kernels.rs:1090-1101; Host fused/mod.rs:4030-4043): the
+ * mean and sum of squared deviations of each row of the rows x cols matrix
+ * `place` reads, converted to `dtype`, in f32, each rounded once. */
+int tc_row_moments(int dtype, const tc_place *place, size_t rows, size_t cols, void *means,
+                   void *deviations, void *stream);
 
 /* ---- multi-GPU (NCCL over NVLink; no counterpart in the reference) ------ */
 /* 128 opaque bytes (ncclUniqueId) for rank 0 to share with the others. */

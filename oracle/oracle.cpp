@@ -1670,3 +1670,79 @@ int orc_axis_distribution(int dtype, size_t rows, size_t cols, int axis, int fam
 double orc_evaluate_f64(int family, int statistic, double x, double first, double second) {
   return special::evaluate(family, statistic, x, first, second);
 }
+
+// ---- fused programs with row statistics and sums (kernels.rs:1090-1135) ----
+
+// host_row_moments (fused/mod.rs:4030-4043): the rows x cols matrix `place`
+// reads, converted to T (input_matrix), then axis_moments_of along Rows.
+int orc_row_moments(int dtype, const tc_place *place, size_t rows, size_t cols, void *means, void *devs) {
+  return with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    std::vector<float> m(rows * cols);
+    for (size_t i = 0; i < rows * cols; ++i) {
+      const size_t row = i / cols, col = i % cols;
+      size_t at = place->offset + col * place->col_step, rest = row;
+      for (int a = int(place->lead) - 1; a >= 0; --a) {
+        at += (rest % place->dims[a]) * place->steps[a];
+        rest /= place->dims[a];
+      }
+      m[i] = T::round(orc_load_as(place->data, place->dtype, at));
+    }
+    for (size_t r = 0; r < rows; ++r) {
+      std::vector<float> v(m.begin() + r * cols, m.begin() + (r + 1) * cols);
+      float mean, dev;
+      orc_moments_of(v, mean, dev);
+      T::store(means, r, mean);
+      T::store(devs, r, dev);
+    }
+    return int(TC_OK);
+  });
+}
+
+// Kernels::fused_with_statistics' default (kernels.rs:1103-1117): the
+// statistics computed first by row_moments, then passed to the program as
+// inputs read one value per row.
+int orc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
+                              const tc_place *places, uint32_t n_places, const tc_row_statistic *stats,
+                              uint32_t n_stats, void *const *outputs, const int *out_dtypes, uint32_t n_outputs) {
+  const size_t e = dtype == TC_F32 ? 4 : 2;
+  std::vector<tc_place> all(places, places + n_places);
+  std::vector<std::vector<char>> vectors;
+  for (uint32_t s = 0; s < n_stats; ++s) {
+    std::vector<char> means(rows * e), devs(rows * e);
+    if (int st = orc_row_moments(dtype, &places[stats[s].of_place], rows, cols, means.data(), devs.data())) return st;
+    vectors.push_back(stats[s].statistic == TC_ROW_MEAN ? means : devs);
+  }
+  for (uint32_t s = 0; s < n_stats; ++s) {
+    tc_place q{};
+    q.data = vectors[s].data();
+    q.dtype = dtype;
+    q.lead = 1;
+    q.dims[0] = rows;
+    q.steps[0] = 1;
+    q.col_step = 0;
+    all[stats[s].into_place] = q;
+  }
+  return orc_fused(dtype, rows, cols, code, n_code, all.data(), n_places, outputs, out_dtypes, n_outputs);
+}
+
+// Program::run_sum's unfused definition (fused/mod.rs:1081-1084, axis_sum at
+// 4045-4052): the program's one output of type T, then matvec with ones
+// (Rows) or vecmat (Columns).
+int orc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code, const tc_place *places,
+                  uint32_t n_places, int axis, void *sums) {
+  if (axis != TC_ROWS && axis != TC_COLUMNS) return int(TC_EINVAL);
+  const size_t e = dtype == TC_F32 ? 4 : 2;
+  std::vector<char> out(rows * cols * e);
+  void *outs[1] = {out.data()};
+  const int dts[1] = {dtype};
+  if (int st = orc_fused(dtype, rows, cols, code, n_code, places, n_places, outs, dts, 1)) return st;
+  std::vector<char> ones(std::max(rows, cols) * e);
+  with_dtype(dtype, [&](auto t) {
+    using T = decltype(t);
+    for (size_t i = 0; i < std::max(rows, cols); ++i) T::store(ones.data(), i, 1.0f);
+    return 0;
+  });
+  if (axis == TC_ROWS) return orc_matvec(dtype, rows, cols, out.data(), ones.data(), sums, 0);
+  return orc_vecmat(dtype, rows, cols, ones.data(), out.data(), sums);
+}

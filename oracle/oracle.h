@@ -139,6 +139,15 @@ double orc_evaluate_f64(int family, int statistic, double x, double first, doubl
 int orc_axis_distribution(int dtype, size_t rows, size_t cols, int axis, int family, int statistic, const void *a,
                           const void *first, const void *second, void *out);
 
+/* Fused programs with row statistics and sums, as tc_row_moments,
+ * tc_fused_with_statistics and tc_fused_sum take them (host buffers). */
+int orc_row_moments(int dtype, const tc_place *place, size_t rows, size_t cols, void *means, void *devs);
+int orc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
+                              const tc_place *places, uint32_t n_places, const tc_row_statistic *stats,
+                              uint32_t n_stats, void *const *outputs, const int *out_dtypes, uint32_t n_outputs);
+int orc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
+                  const tc_place *places, uint32_t n_places, int axis, void *sums);
+
 #ifdef __cplusplus
 }
 #endif

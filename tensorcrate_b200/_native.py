@@ -69,6 +69,16 @@ NORMAL, INVERSE_GAUSSIAN = range(2)
 PDF, CDF, PPF = range(3)
 
 
+class RowStatistic(C.Structure):
+    """tc_row_statistic: loads of `into_place` read a statistic of each row
+    of `of_place`."""
+
+    _fields_ = [("of_place", _u32), ("into_place", _u32), ("statistic", C.c_int)]
+
+
+ROW_MEAN, ROW_DEVIATIONS = range(2)
+
+
 class AdamTensor(C.Structure):
     """tc_adam_tensor: one parameter of a tc_adam_multi call."""
 
@@ -122,6 +132,9 @@ SIGNATURES = {
     "tc_matvec": [_i, _sz, _sz, _p, _p, _p, _i, _p],
     "tc_vecmat": [_i, _sz, _sz, _p, _p, _p, _p],
     "tc_fused": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _p, _u32, _p],
+    "tc_fused_with_statistics": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _u32, _p, _p, _u32, _p],
+    "tc_fused_sum": [_i, _sz, _sz, _p, _u32, _p, _u32, _i, _p, _p],
+    "tc_row_moments": [_i, _p, _sz, _sz, _p, _p, _p],
     "tc_matmul_epilogue": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p],
     "tc_vecmat_noalloc": [_i, _sz, _sz, _p, _p, _p, _p],
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],

@@ -222,3 +222,132 @@ def test_fused_transcendentals_within_two_ulp(device):
         limit = 0.0 if op == N.SQRT else (3.0 if op in (N.SEC, N.CSC) else 2.0)
         err = np.abs(got - exact) / ulp
         assert np.max(err) <= limit + 0.5, (op, float(np.max(err)))
+
+
+# ---- row statistics, sums and row moments (kernels.rs:1090-1135) -----------
+
+def layer_norm_program():
+    """(x - mean) / sqrt(deviations * 0.5) of each row: the doc example of
+    Builder::row_statistic (fused/mod.rs:1808-1827).  Place 0 is x, places
+    1 and 2 its row mean and deviations."""
+    return [load(0, 0), load(1, 1), load(2, 2), const(3, 0.5), binary(4, N.MUL, 2, 3), unary(5, N.SQRT, 4),
+            binary(6, N.SUB, 0, 1), binary(7, N.DIV, 6, 5), store(7, 0)]
+
+
+def _stats_places(ptr, dtype, rows, cols):
+    x = place(ptr, dtype, rows, cols)
+    blank = N.Place()
+    return (N.Place * 3)(x, blank, blank)
+
+
+STATS = (N.RowStatistic * 2)(N.RowStatistic(0, 1, N.ROW_MEAN), N.RowStatistic(0, 2, N.ROW_DEVIATIONS))
+
+
+def _with_statistics_oracle(dtype, x, rows, cols, code):
+    out = np.empty(rows * cols, x.dtype)
+    pl = _stats_places(x.ctypes.data, dtype, rows, cols)
+    code_arr = (N.Instr * len(code))(*code)
+    outs = (C.c_void_p * 1)(out.ctypes.data)
+    dts = (C.c_int * 1)(N.DTYPES[dtype])
+    O.call("orc_fused_with_statistics", O.DTYPES[dtype], rows, cols, C.cast(code_arr, C.c_void_p), len(code),
+           C.cast(pl, C.c_void_p), 3, C.cast(STATS, C.c_void_p), 2, C.cast(outs, C.c_void_p), C.cast(dts, C.c_void_p), 1)
+    return out
+
+
+def test_oracle_layer_norm_doc_example():
+    """fused/mod.rs:1822-1826: [[1, 3], [10, 20]] normalizes to [[-1, 1], [-1, 1]]."""
+    x = np.array([1.0, 3.0, 10.0, 20.0], np.float32)
+    assert list(_with_statistics_oracle("f32", x, 2, 2, layer_norm_program())) == [-1.0, 1.0, -1.0, 1.0]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(2, 2), (64, 1000), (1000, 64), (7, 1), (3, 4099)])
+def test_fused_with_statistics_matches_the_oracle(device, dtype, rows, cols):
+    """The row statistics are sums in another order (rel 1e-5·√cols), so
+    the normalized values agree within that for f32, and within a step of
+    the element type for f16/bf16; the 2x2 doc example is exact."""
+    from tensorcrate_b200 import cuda
+    x_host = np.array([1.0, 3.0, 10.0, 20.0], np.float32) if (rows, cols) == (2, 2) else normal(rows * cols, 12)
+    x = O.narrow(x_host * np.float32(3.0) + np.float32(1.0) if (rows, cols) != (2, 2) else x_host, dtype)
+    dx, out = cuda.CudaStorage.store(x, dtype), cuda.CudaStorage(dtype, rows * cols)
+    code = layer_norm_program()
+    code_arr = (N.Instr * len(code))(*code)
+    pl = _stats_places(dx.ptr, dtype, rows, cols)
+    outs = (C.c_void_p * 1)(out.ptr)
+    dts = (C.c_int * 1)(N.DTYPES[dtype])
+    N.call("tc_fused_with_statistics", N.DTYPES[dtype], rows, cols, C.cast(code_arr, C.c_void_p), len(code),
+           C.cast(pl, C.c_void_p), 3, C.cast(STATS, C.c_void_p), 2, C.cast(outs, C.c_void_p),
+           C.cast(dts, C.c_void_p), 1, None)
+    want = _with_statistics_oracle(dtype, x, rows, cols, code)
+    got = out.as_slice()
+    if (rows, cols) == (2, 2):
+        assert list(O.widen(got, dtype)) == [-1.0, 1.0, -1.0, 1.0]
+    if cols == 1:
+        # one element per row: zero deviation, 0/0
+        assert np.all(np.isnan(O.widen(got, dtype)))
+        return
+    g, w = O.widen(got, dtype).astype(np.float64), O.widen(want, dtype).astype(np.float64)
+    if dtype == "f32":
+        assert np.all(np.abs(g - w) <= 1e-5 * np.sqrt(cols) * np.maximum(np.abs(w), 1.0))
+    else:
+        from util import steps
+        assert int(np.max(steps(got, want, dtype))) <= 2
+
+
+def sum_program():
+    """x * y + 1: place 0 is x, place 1 is y."""
+    return [load(0, 0), load(1, 1), binary(2, N.MUL, 0, 1), const(3, 1.0), binary(4, N.ADD, 2, 3), store(4, 0)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(100, 300), (3000, 7), (1, 5000), (5000, 1), (2048, 1024)])
+@pytest.mark.parametrize("axis", [N.ROWS, N.COLUMNS])
+def test_fused_sum_matches_the_oracle(device, dtype, rows, cols, axis):
+    """A program's output summed along an axis without being stored, against
+    the Host's definition (the output, then matvec/vecmat with ones): sums in
+    another order, rel 1e-5·√K, plus a step of the element type."""
+    from tensorcrate_b200 import cuda
+    n = rows * cols
+    x, y = O.narrow(uniform(n, 13), dtype), O.narrow(uniform(n, 14), dtype)
+    dx, dy = cuda.CudaStorage.store(x, dtype), cuda.CudaStorage.store(y, dtype)
+    results = rows if axis == N.ROWS else cols
+    out = cuda.CudaStorage(dtype, results)
+    code = sum_program()
+    code_arr = (N.Instr * len(code))(*code)
+    pl = (N.Place * 2)(place(dx.ptr, dtype, rows, cols), place(dy.ptr, dtype, rows, cols))
+    N.call("tc_fused_sum", N.DTYPES[dtype], rows, cols, C.cast(code_arr, C.c_void_p), len(code),
+           C.cast(pl, C.c_void_p), 2, axis, out.ptr, None)
+    want = np.empty(results, x.dtype)
+    hpl = (N.Place * 2)(place(x.ctypes.data, dtype, rows, cols), place(y.ctypes.data, dtype, rows, cols))
+    O.call("orc_fused_sum", O.DTYPES[dtype], rows, cols, C.cast(code_arr, C.c_void_p), len(code),
+           C.cast(hpl, C.c_void_p), 2, axis, O.ptr(want))
+    depth = cols if axis == N.ROWS else rows
+    g, w = O.widen(out.as_slice(), dtype).astype(np.float64), O.widen(want, dtype).astype(np.float64)
+    rel = 1e-5 * np.sqrt(depth) + (0 if dtype == "f32" else (2.0 ** -7 if dtype == "bf16" else 2.0 ** -10))
+    assert np.all(np.abs(g - w) <= rel * np.maximum(np.abs(w), 1.0))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("stored", ["f32", "bf16"])
+def test_row_moments_through_a_transposing_place(device, dtype, stored):
+    """row_moments of the transpose of a stored [cols x rows] matrix, read
+    through a place (col_step = rows, row step 1), converting the storage
+    type to the program's type first."""
+    from tensorcrate_b200 import cuda
+    rows, cols = 300, 517
+    src = O.narrow(normal(rows * cols, 15) + np.float32(0.5), stored)
+    dsrc = cuda.CudaStorage.store(src, stored)
+    pl = place(dsrc.ptr, stored, rows, cols, col_step=rows, row_step=1)
+    means, devs = cuda.CudaStorage(dtype, rows), cuda.CudaStorage(dtype, rows)
+    N.call("tc_row_moments", N.DTYPES[dtype], C.byref(pl), rows, cols, means.ptr, devs.ptr, None)
+    hpl = place(src.ctypes.data, stored, rows, cols, col_step=rows, row_step=1)
+    store_t = np.float32 if dtype == "f32" else np.uint16
+    wm, wd = np.empty(rows, store_t), np.empty(rows, store_t)
+    O.call("orc_row_moments", O.DTYPES[dtype], C.byref(hpl), rows, cols, O.ptr(wm), O.ptr(wd))
+    rel = 1e-5 * np.sqrt(cols) + (0 if dtype == "f32" else (2.0 ** -7 if dtype == "bf16" else 2.0 ** -10))
+    for got, want in ((means, wm), (devs, wd)):
+        g, w = O.widen(got.as_slice(), dtype).astype(np.float64), O.widen(want, dtype).astype(np.float64)
+        assert np.all(np.abs(g - w) <= rel * np.maximum(np.abs(w), 1.0))
