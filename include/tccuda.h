@@ -489,6 +489,16 @@ int tc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr
  * block for their bands' partial sums. */
 int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
                  const tc_place *places, uint32_t n_places, int axis, void *sums, void *stream);
+/* `matmul_epilogue` for any program (kernels.rs:1137-1150; Host
+ * host_matmul, fused/mod.rs:4754-4764): C = a.b (rows x inner by inner x
+ * cols, rounded once to `dtype`, as tc_matmul), then `program` over the
+ * rows x cols space with C as its input 0: places[0] says how input 0 is
+ * read and its data is ignored (the product goes there).  The dense-layer
+ * programs (bias, ReLU, ReLU's backward rule) run inside the GEMM's
+ * epilogue instead: tc_matmul_epilogue. */
+int tc_matmul_program(int dtype, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                      const tc_instr *code, uint32_t n_code, const tc_place *places, uint32_t n_places,
+                      void *const *outputs, const int *out_dtypes, uint32_t n_outputs, void *stream);
 /* `row_moments` (kernels.rs:1090-1101; Host fused/mod.rs:4030-4043): the
  * mean and sum of squared deviations of each row of the rows x cols matrix
  * `place` reads, converted to `dtype`, in f32, each rounded once. */

@@ -63,6 +63,7 @@ SIGNATURES = {
     "orc_row_moments": [_i, _p, _sz, _sz, _p, _p],
     "orc_fused_with_statistics": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _u32, _p, _p, _u32],
     "orc_fused_sum": [_i, _sz, _sz, _p, _u32, _p, _u32, _i, _p],
+    "orc_matmul_program": [_i, _sz, _sz, _sz, _p, _p, _p, _u32, _p, _u32, _p, _p, _u32],
     "orc_adam_coefficients": [_i, _d, _d, _d, _d, _u32, C.POINTER(C.c_double)],
     "orc_mlp_params": [_p, _u32, _p, _p, _i],
     "orc_mlp_grads": [_p, _u32, _p, _p],

@@ -1746,3 +1746,17 @@ int orc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
   if (axis == TC_ROWS) return orc_matvec(dtype, rows, cols, out.data(), ones.data(), sums, 0);
   return orc_vecmat(dtype, rows, cols, ones.data(), out.data(), sums);
 }
+
+// host_matmul (fused/mod.rs:4754-4764): the product a.matmul(b), rounded to
+// T, then the program with it as input 0.
+int orc_matmul_program(int dtype, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                       const tc_instr *code, uint32_t n_code, const tc_place *places, uint32_t n_places,
+                       void *const *outputs, const int *out_dtypes, uint32_t n_outputs) {
+  const size_t e = dtype == TC_F32 ? 4 : 2;
+  std::vector<char> product(rows * cols * e);
+  if (int st = orc_matmul(dtype, TC_TRANS_NONE, rows, inner, cols, a, b, product.data(), 0)) return st;
+  std::vector<tc_place> all(places, places + n_places);
+  all[0].data = product.data();
+  all[0].dtype = dtype;
+  return orc_fused(dtype, rows, cols, code, n_code, all.data(), n_places, outputs, out_dtypes, n_outputs);
+}

@@ -148,6 +148,10 @@ int orc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_inst
 int orc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
                   const tc_place *places, uint32_t n_places, int axis, void *sums);
 
+int orc_matmul_program(int dtype, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                       const tc_instr *code, uint32_t n_code, const tc_place *places, uint32_t n_places,
+                       void *const *outputs, const int *out_dtypes, uint32_t n_outputs);
+
 #ifdef __cplusplus
 }
 #endif

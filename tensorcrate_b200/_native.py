@@ -135,6 +135,7 @@ SIGNATURES = {
     "tc_fused_with_statistics": [_i, _sz, _sz, _p, _u32, _p, _u32, _p, _u32, _p, _p, _u32, _p],
     "tc_fused_sum": [_i, _sz, _sz, _p, _u32, _p, _u32, _i, _p, _p],
     "tc_row_moments": [_i, _p, _sz, _sz, _p, _p, _p],
+    "tc_matmul_program": [_i, _sz, _sz, _sz, _p, _p, _p, _u32, _p, _u32, _p, _p, _u32, _p],
     "tc_matmul_epilogue": [_i, _i, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p],
     "tc_vecmat_noalloc": [_i, _sz, _sz, _p, _p, _p, _p],
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],

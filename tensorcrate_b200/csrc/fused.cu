@@ -396,6 +396,30 @@ int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint
   });
 }
 
+int tc_matmul_program(int dtype, size_t rows, size_t inner, size_t cols, const void *a, const void *b,
+                      const tc_instr *code, uint32_t n_code, const tc_place *places, uint32_t n_places,
+                      void *const *outputs, const int *out_dtypes, uint32_t n_outputs, void *stream) {
+  if (n_places == 0 || !places) return fail(TC_EINVAL, "matmul_program: place 0 (the product) is missing");
+  if (n_places > uint32_t(MAX_PLACES)) return fail(TC_EINVAL, "matmul_program: %u places", n_places);
+  if (!storage_type(dtype)) return fail(TC_ENOTSUP, "matmul_program: type %d", dtype);
+  if (rows == 0 || cols == 0) return TC_OK;
+  // The product, rounded once to T (a.matmul(b)), in a pooled block that
+  // the program reads as its input 0 and that goes back to the pool after
+  // the launch (later work on this stream is ordered after it).
+  void *product = nullptr;
+  if (int st = tc_malloc(&product, rows * cols * dtype_bytes(dtype))) return st;
+  int st = tc_matmul(dtype, TC_TRANS_NONE, rows, inner, cols, a, b, product, 0, stream);
+  if (st == TC_OK) {
+    tc_place all[MAX_PLACES];
+    for (uint32_t j = 0; j < n_places; ++j) all[j] = places[j];
+    all[0].data = product;
+    all[0].dtype = dtype;
+    st = tc_fused(dtype, rows, cols, code, n_code, all, n_places, outputs, out_dtypes, n_outputs, stream);
+  }
+  tc_free(product);
+  return st;
+}
+
 int tc_row_moments(int dtype, const tc_place *place, size_t rows, size_t cols, void *means, void *deviations,
                    void *stream) {
   if (!storage_type(dtype)) return fail(TC_ENOTSUP, "row_moments: type %d", dtype);

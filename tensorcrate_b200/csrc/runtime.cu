@@ -178,7 +178,9 @@ int tc_last_error(char *buf, size_t len) {
 
 const char *tc_build_info(void) {
   return "tensorcrate_b200 0.1 sm_100a: strided copy/assemble/write, elementwise, strided binary, "
-         "axis reduce, arg reduce, tcgen05 bf16/f16 GEMM, f32 SIMT GEMM, gemv, Adam/SGD, NCCL";
+         "axis reduce, arg reduce, tcgen05 bf16/f16 GEMM and 3xTF32 f32 GEMM with epilogues, gemv, "
+         "Adam/SGD, fused programs (statistics, sums, GEMM epilogues), analytic unary and dual, power, "
+         "prefix sum, sort, correlation, pad, flip, moments, distributions, NCCL and NVLink peer stores";
 }
 
 int tc_set_device(int device) { return check_cuda(cudaSetDevice(device), "cudaSetDevice"); }

@@ -579,6 +579,78 @@ class Cuda:
                _stream(stream))
         return out
 
+    # --- windowed matrices (kernels.rs:998-1028) ---
+    @staticmethod
+    def correlate(input: CudaStorage, shape, window: CudaStorage, window_shape, flip: bool,
+                  stream=None) -> CudaStorage:
+        (r, c), (wr, wc) = shape, window_shape
+        if wr > r or wc > c:
+            raise ValueError(f"correlate: a {wr}x{wc} window does not fit in a {r}x{c} input")
+        out = CudaStorage(input.dtype, (r - wr + 1) * (c - wc + 1))
+        N.call("tc_correlate", N.DTYPES[input.dtype], r, c, wr, wc, int(flip), input.ptr, window.ptr, out.ptr,
+               _stream(stream))
+        return out
+
+    @staticmethod
+    def correlate_window_gradient(input: CudaStorage, shape, adjoint: CudaStorage, adjoint_shape,
+                                  stream=None) -> CudaStorage:
+        return Cuda.correlate(input, shape, adjoint, adjoint_shape, False, stream)
+
+    @staticmethod
+    def correlate_input_gradient(adjoint: CudaStorage, adjoint_shape, window: CudaStorage, window_shape,
+                                 forward_flip: bool, stream=None) -> CudaStorage:
+        (ar, ac), (wr, wc) = adjoint_shape, window_shape
+        out = CudaStorage(adjoint.dtype, (ar + wr - 1) * (ac + wc - 1))
+        N.call("tc_correlate_input_gradient", N.DTYPES[adjoint.dtype], ar, ac, wr, wc, int(forward_flip),
+               adjoint.ptr, window.ptr, out.ptr, _stream(stream))
+        return out
+
+    @staticmethod
+    def pad(input: CudaStorage, shape, pad_rows: int, pad_cols: int, stream=None) -> CudaStorage:
+        r, c = shape
+        out = CudaStorage(input.dtype, (r + 2 * pad_rows) * (c + 2 * pad_cols))
+        N.call("tc_pad", N.DTYPES[input.dtype], r, c, pad_rows, pad_cols, input.ptr, out.ptr, _stream(stream))
+        return out
+
+    @staticmethod
+    def flip(input: CudaStorage, shape, stream=None) -> CudaStorage:
+        r, c = shape
+        out = CudaStorage(input.dtype, r * c)
+        N.call("tc_flip", N.DTYPES[input.dtype], r, c, input.ptr, out.ptr, _stream(stream))
+        return out
+
+    # --- moments and distributions (kernels.rs:1035-1070) ---
+    @staticmethod
+    def vector_moments(a: CudaStorage, stream=None) -> CudaStorage:
+        """(mean, deviations) as a 2-element device vector."""
+        out = CudaStorage(a.dtype, 2)
+        N.call("tc_moments", N.DTYPES[a.dtype], a.ptr, a.len, out.ptr, _stream(stream))
+        return out
+
+    @staticmethod
+    def matrix_axis_moments(a: CudaStorage, shape, axis: int, stream=None) -> tuple[CudaStorage, CudaStorage]:
+        r, c = shape
+        extent = r if axis == N.ROWS else c
+        means, devs = CudaStorage(a.dtype, extent), CudaStorage(a.dtype, extent)
+        N.call("tc_axis_moments", N.DTYPES[a.dtype], r, c, axis, a.ptr, means.ptr, devs.ptr, _stream(stream))
+        return means, devs
+
+    @staticmethod
+    def vector_distribution(a: CudaStorage, family: int, statistic: int, parameters, stream=None) -> CudaStorage:
+        out = CudaStorage(a.dtype, a.len)
+        N.call("tc_distribution", N.DTYPES[a.dtype], family, statistic, a.ptr, a.len, float(parameters[0]),
+               float(parameters[1]), out.ptr, _stream(stream))
+        return out
+
+    @staticmethod
+    def matrix_axis_distribution(a: CudaStorage, shape, axis: int, family: int, statistic: int,
+                                 first: CudaStorage, second: CudaStorage, stream=None) -> CudaStorage:
+        r, c = shape
+        out = CudaStorage(a.dtype, r * c)
+        N.call("tc_axis_distribution", N.DTYPES[a.dtype], r, c, axis, family, statistic, a.ptr, first.ptr,
+               second.ptr, out.ptr, _stream(stream))
+        return out
+
     # --- products (kernels.rs:899-985) ---
     @staticmethod
     def matmul(a: CudaStorage, b: CudaStorage, rows: int, inner: int, cols: int, transposed: int = N.TRANS_NONE,

@@ -351,3 +351,35 @@ def test_row_moments_through_a_transposing_place(device, dtype, stored):
     for got, want in ((means, wm), (devs, wd)):
         g, w = O.widen(got.as_slice(), dtype).astype(np.float64), O.widen(want, dtype).astype(np.float64)
         assert np.all(np.abs(g - w) <= rel * np.maximum(np.abs(w), 1.0))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,k,n", [(128, 256, 192), (33, 70, 17), (512, 1024, 768)])
+def test_matmul_program_matches_the_oracle(device, dtype, m, k, n):
+    """Kernels::matmul_epilogue with a program of its own: tanh(P) * 0.5 +
+    bias[col], the product as input 0 and a per-column bias as input 1 (a
+    place that repeats one row).  The product itself is a GEMM (half-
+    precision tolerance for f16/bf16, the 3xTF32 bound for f32), which the
+    program carries through."""
+    from tensorcrate_b200 import cuda
+    a, b = O.narrow(uniform(m * k, 21), dtype), O.narrow(uniform(k * n, 22), dtype)
+    bias = O.narrow(uniform(n, 23), dtype)
+    da, db, dbias = (cuda.CudaStorage.store(x, dtype) for x in (a, b, bias))
+    out = cuda.CudaStorage(dtype, m * n)
+    code = [load(0, 0), unary(1, N.TANH, 0), const(2, 0.5), binary(3, N.MUL, 1, 2), load(4, 1),
+            binary(5, N.ADD, 3, 4), store(5, 0)]
+    code_arr = (N.Instr * len(code))(*code)
+    pl = (N.Place * 2)(place(None, dtype, m, n), place(dbias.ptr, dtype, m, n, row_step=0))
+    outs = (C.c_void_p * 1)(out.ptr)
+    dts = (C.c_int * 1)(N.DTYPES[dtype])
+    N.call("tc_matmul_program", N.DTYPES[dtype], m, k, n, da.ptr, db.ptr, C.cast(code_arr, C.c_void_p), len(code),
+           C.cast(pl, C.c_void_p), 2, C.cast(outs, C.c_void_p), C.cast(dts, C.c_void_p), 1, None)
+    want = np.empty(m * n, a.dtype)
+    hpl = (N.Place * 2)(place(None, dtype, m, n), place(bias.ctypes.data, dtype, m, n, row_step=0))
+    houts = (C.c_void_p * 1)(want.ctypes.data)
+    O.call("orc_matmul_program", O.DTYPES[dtype], m, k, n, O.ptr(a), O.ptr(b), C.cast(code_arr, C.c_void_p),
+           len(code), C.cast(hpl, C.c_void_p), 2, C.cast(houts, C.c_void_p), C.cast(dts, C.c_void_p), 1)
+    g, w = O.widen(out.as_slice(), dtype).astype(np.float64), O.widen(want, dtype).astype(np.float64)
+    tol = 1e-5 * np.sqrt(k) if dtype == "f32" else (2.0 ** -6 if dtype == "bf16" else 2.0 ** -9)
+    assert np.all(np.abs(g - w) <= tol * np.maximum(np.abs(w), 1.0))

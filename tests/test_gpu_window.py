@@ -132,3 +132,31 @@ def test_correlate_rejects_a_window_that_does_not_fit(device):
     x = _store(np.zeros(6, np.float32), "f32")
     out = cuda.CudaStorage("f32", 1)
     assert N.lib().tc_correlate(N.F32, 2, 3, 3, 1, 0, x.ptr, x.ptr, out.ptr, None) == N.EINVAL
+
+
+def test_trait_surface_matches_the_oracle(device):
+    """The Cuda mirror of the trait methods (cuda.Cuda.correlate, pad, flip,
+    the gradients, moments and distributions) on one small case each."""
+    x = np.arange(20, dtype=np.float32).reshape(4, 5) / 7
+    w = np.array([[1.0, -2.0], [0.5, 3.0]], np.float32)
+    dx, dw = _store(x.ravel(), "f32"), _store(w.ravel(), "f32")
+    got = cuda.Cuda.correlate(dx, (4, 5), dw, (2, 2), True).as_slice()
+    assert np.array_equal(got, correlate_oracle(x.ravel(), w.ravel(), (4, 5), (2, 2), True, "f32"))
+    adj = _store(np.ones(12, np.float32), "f32")
+    gw = cuda.Cuda.correlate_window_gradient(dx, (4, 5), adj, (3, 4)).as_slice()
+    assert np.array_equal(gw, correlate_oracle(x.ravel(), np.ones(12, np.float32), (4, 5), (3, 4), False, "f32"))
+    gi = cuda.Cuda.correlate_input_gradient(adj, (3, 4), dw, (2, 2), False).as_slice()
+    want = np.empty(20, np.float32)
+    O.call("orc_correlate_input_gradient", O.DTYPES["f32"], 3, 4, 2, 2, 0, O.ptr(np.ones(12, np.float32)),
+           O.ptr(w.ravel()), O.ptr(want))
+    assert np.array_equal(gi, want)
+    assert np.array_equal(cuda.Cuda.flip(dx, (4, 5)).as_slice(), x.ravel()[::-1])
+    assert np.array_equal(cuda.Cuda.pad(dx, (4, 5), 1, 2).as_slice().reshape(6, 9), np.pad(x, ((1, 1), (2, 2))))
+    m = cuda.Cuda.vector_moments(dx).as_slice()
+    assert abs(m[0] - x.mean()) <= 1e-6 and abs(m[1] - ((x - x.mean()) ** 2).sum()) <= 1e-4
+    means, devs = cuda.Cuda.matrix_axis_moments(dx, (4, 5), N.COLUMNS)
+    assert np.allclose(means.as_slice(), x.mean(axis=0), atol=1e-6)
+    cdf = cuda.Cuda.vector_distribution(dx, N.NORMAL, N.CDF, (1.0, 2.0)).as_slice()
+    want = np.empty(20, np.float32)
+    O.call("orc_distribution", O.DTYPES["f32"], N.NORMAL, N.CDF, O.ptr(x.ravel()), 20, 1.0, 2.0, O.ptr(want))
+    assert np.array_equal(cdf, want)
