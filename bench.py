@@ -15,7 +15,8 @@ locally and are all-gathered; max/min over (0,2) reduce across the sharded
 axis, so their [512] partials are all-reduced (NCCL).
 
 Other workloads (--workload): c1 (f32 1024^3 GEMM + matvec), c3 (f16 layout
-copies), c5 (bf16 GEMM, --size).  --impl reference times the reference's
+copies), c4 (MLP training step), c5 (bf16 GEMM, --size), trait (the other
+Kernels<T> methods, each timed alone).  --impl reference times the reference's
 Host path restated in C++ (oracle/) on the host cores.
 """
 from __future__ import annotations
@@ -527,6 +528,124 @@ def run_c3(args, torch, world, rank, comm):
             "gpu_launches": 2 * args.steps, "clocks": clocks}
 
 
+def run_trait(args, torch, world, rank, comm):
+    """The Kernels<T> methods beyond the configs' hot path,
+    each on an input larger than L2, timed alone: scan, sort, analytic
+    unary and its dual, power, correlation, pad, flip, moments, a
+    distribution function, and fused programs (plain, with row statistics,
+    summed).  metric: algorithmic bytes of the HBM-bound calls / their time;
+    "ops" gives each call against its own bound."""
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200 import _native as N
+    lib = N.lib()
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    pk, pk_kind = peaks()
+    hbm = pk["hbm_gbs"]
+    rng = np.random.default_rng(7)
+    n = 64 << 20
+    x = cuda.CudaStorage.store(rng.standard_normal(n, dtype=np.float32), "f32")
+    y = cuda.CudaStorage.store(rng.uniform(0.5, 2.0, n).astype(np.float32), "f32")
+    o1, o2 = cuda.CudaStorage("f32", n), cuda.CudaStorage("f32", n)
+    ops, hbm_bytes, hbm_ms = {}, 0, 0.0
+
+    def measure(name, fn, byts, flops=None, bound="hbm", peak=None, steps=None):
+        nonlocal hbm_bytes, hbm_ms
+        ms, _ = timed(torch, world, fn, steps or args.steps, args.warmup, stream)
+        entry = {"ms": round(ms, 4), "bound": bound}
+        if byts:
+            gbs = byts / (ms * 1e-3) / 1e9
+            entry.update(gbs=round(gbs, 1), bytes=byts)
+            if bound == "hbm":
+                entry["frac"] = round(gbs / hbm, 3)
+                hbm_bytes += byts
+                hbm_ms += ms
+        if flops:
+            tf = flops / (ms * 1e-3) / 1e12
+            entry["tflops"] = round(tf, 2)
+            if peak:
+                entry["frac"] = round(tf / peak, 3)
+        ops[name] = entry
+
+    f32 = N.F32
+    measure("prefix_sum", lambda: N.check("scan", lib.tc_prefix_sum(f32, x.ptr, o1.ptr, n, sp)), 2 * 4 * n)
+    ns = 32 << 20
+    measure("sort", lambda: N.check("sort", lib.tc_sort(f32, N.ASCENDING, x.ptr, o1.ptr, ns, sp)), 2 * 4 * ns)
+    measure("unary_exp", lambda: N.check("unary", lib.tc_unary(f32, N.EXP, x.ptr, o1.ptr, n, sp)), 2 * 4 * n)
+    measure("unary_dual_tanh",
+            lambda: N.check("dual", lib.tc_unary_dual(f32, N.TANH, x.ptr, y.ptr, o1.ptr, o2.ptr, n, sp)), 4 * 4 * n)
+    measure("power", lambda: N.check("pow", lib.tc_power(f32, y.ptr, x.ptr, o1.ptr, n, sp)), 3 * 4 * n)
+    r = c = 8192
+    w = cuda.CudaStorage.store(rng.uniform(-1, 1, 25).astype(np.float32), "f32")
+    out_rc = (r - 4) * (c - 4)
+    # FP32 pipe without FMA: one multiply and one add per tap, 128 lanes per SM
+    fp32_peak = 148 * 128 * 1.965e9 / 1e12
+    measure("correlate_5x5", lambda: N.check("corr", lib.tc_correlate(f32, r, c, 5, 5, 0, x.ptr, w.ptr, o1.ptr, sp)),
+            4 * (r * c + out_rc), flops=2 * 25 * out_rc, bound="fp32 (mul + add per tap)", peak=fp32_peak)
+    measure("pad_16", lambda: N.check("pad", lib.tc_pad(f32, r, c, 16, 16, x.ptr, o1.ptr, sp)),
+            4 * (r * c + (r + 32) * (c + 32)))
+    measure("flip", lambda: N.check("flip", lib.tc_flip(f32, r, c, x.ptr, o1.ptr, sp)), 2 * 4 * r * c)
+    mom = cuda.CudaStorage("f32", 2)
+    measure("moments", lambda: N.check("moments", lib.tc_moments(f32, x.ptr, n, mom.ptr, sp)), 4 * n)
+    rows, cols = 16384, 4096
+    means, devs = cuda.CudaStorage("f32", rows), cuda.CudaStorage("f32", rows)
+    measure("axis_moments_rows",
+            lambda: N.check("axis", lib.tc_axis_moments(f32, rows, cols, N.ROWS, x.ptr, means.ptr, devs.ptr, sp)),
+            4 * rows * cols)
+    nd = 16 << 20
+    measure("normal_cdf", lambda: N.check("dist", lib.tc_distribution(f32, N.NORMAL, N.CDF, x.ptr, nd, 0.0, 1.0,
+                                                                      o1.ptr, sp)),
+            2 * 4 * nd, bound="fp64 (Cody erfc per element)")
+
+    def ins(code, dst=0, a=0, b=0, op=0, slot=0, value=0.0):
+        i = N.Instr()
+        i.code, i.dst, i.a, i.b, i.op, i.slot, i.value = code, dst, a, b, op, slot, value
+        return i
+
+    def place(ptr):
+        p = N.Place()
+        p.data, p.dtype, p.lead, p.offset, p.col_step = ptr, f32, 1, 0, 1
+        p.dims[0], p.steps[0] = rows, cols
+        return p
+
+    prog = [ins(N.I_LOAD, 0, slot=0), ins(N.I_LOAD, 1, slot=1), ins(N.I_BINARY, 2, 0, 1, op=2),
+            ins(N.I_CONST, 3, value=1.0), ins(N.I_BINARY, 4, 2, 3, op=0), ins(N.I_STORE, a=4, slot=0)]
+    code = (N.Instr * len(prog))(*prog)
+    pl2 = (N.Place * 2)(place(x.ptr), place(y.ptr))
+    outs = (C.c_void_p * 1)(o1.ptr)
+    dts = (C.c_int * 1)(f32)
+    measure("fused_xy_plus_1", lambda: N.check("fused", lib.tc_fused(f32, rows, cols, code, len(prog), pl2, 2, outs,
+                                                                      dts, 1, sp)), 3 * 4 * rows * cols)
+    sums = cuda.CudaStorage("f32", rows)
+    measure("fused_sum_rows", lambda: N.check("fsum", lib.tc_fused_sum(f32, rows, cols, code, len(prog), pl2, 2,
+                                                                        N.ROWS, sums.ptr, sp)), 2 * 4 * rows * cols)
+    ln = [ins(N.I_LOAD, 0, slot=0), ins(N.I_LOAD, 1, slot=1), ins(N.I_LOAD, 2, slot=2), ins(N.I_CONST, 3, value=1.0 / cols),
+          ins(N.I_BINARY, 4, 2, 3, op=2), ins(N.I_UNARY, 5, 4, op=N.SQRT), ins(N.I_BINARY, 6, 0, 1, op=1),
+          ins(N.I_BINARY, 7, 6, 5, op=3), ins(N.I_STORE, a=7, slot=0)]
+    ln_code = (N.Instr * len(ln))(*ln)
+    pl3 = (N.Place * 3)(place(x.ptr), N.Place(), N.Place())
+    st = (N.RowStatistic * 2)(N.RowStatistic(0, 1, N.ROW_MEAN), N.RowStatistic(0, 2, N.ROW_DEVIATIONS))
+    measure("layer_norm_with_statistics",
+            lambda: N.check("stats", lib.tc_fused_with_statistics(f32, rows, cols, ln_code, len(ln), pl3, 3, st, 2,
+                                                                  outs, dts, 1, sp)), 2 * 4 * rows * cols)
+    gbs = hbm_bytes / (hbm_ms * 1e-3) / 1e9
+    return {"metric": "8(f) trait-method kernels HBM throughput (GB/s)", "value": round(gbs, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(hbm_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1) / uniform, seeded",
+            "config": {"workload": "each 8(f) kernel alone: 64M-element vectors (sort: 32M, distribution: 16M), "
+                                   "8192x8192 matrices, 16384x4096 programs",
+                       "l2": "no flush: every input is 256 MB or more, above the 126 MB L2 (sort: 128 MB)",
+                       "value": "algorithmic bytes of the HBM-bound calls / the sum of their times"},
+            "roofline": {"bound": "hbm", "kernel": "all HBM-bound 8(f) calls", "achieved": round(gbs, 1), "peak": hbm,
+                         "peak_source": pk_kind, "unit": "GB/s", "frac": round(gbs / hbm, 3), "traffic": None},
+            # our kernels per call (sort: the key maps; CUB's radix passes are not counted)
+            "ops": ops, "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.get(k, 1) for k in ops)}
+
+
+LAUNCHES_PER_CALL = {"prefix_sum": 3, "sort": 2, "moments": 2, "axis_moments_rows": 2}
+
+
 def run_c4(args, torch, world, rank, comm):
     """Config 4: one training step of the 1024-4096-4096-1024 ReLU MLP in
     bf16 (tape + Adam(1e-3, 0.9, 0.999, 1e-8), as the reference runs it),
@@ -619,7 +738,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "trait"])
     ap.add_argument("--batch", type=int, default=2048, help="config 4's global batch")
     ap.add_argument("--size", type=int, default=8192, help="config 5's M=N=K")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -658,6 +777,8 @@ def main():
         line = run_c3(args, torch, world, rank, comm)
     elif args.workload == "c4":
         line = run_c4(args, torch, world, rank, comm)
+    elif args.workload == "trait":
+        line = run_trait(args, torch, world, rank, comm)
     else:
         line = run_c2(args, torch, world, rank, comm)
     if rank == 0 and not args.no_cpu_baseline and args.workload == "c2":
