@@ -676,6 +676,84 @@ __global__ void __launch_bounds__(256) reduce_walk(const typename T::S *in, cons
   }
 }
 
+// var_split: a variance whose slices are few and long, in chunks that fill
+// the machine (a warp per slice would leave it nearly idle).  Pass 1 sums
+// each (slice, chunk) with a block; the chunk sums, added in chunk order,
+// give the f32 mean; pass 2 sums the squared deviations from it the same
+// way; the chunk sums, added in order and divided, give the result.  The
+// innermost folded axis is walked as a run (a step of run_stride), the
+// others through their walk, recomputed only when the run changes.
+struct VarSplit {
+  Walk kept, outer;            // result -> base; folded outer index -> offset
+  long long run, run_stride;   // the innermost folded axis
+  long long results, depth, chunk;
+  int chunks;
+  float count, divisor;
+};
+
+template <class T, bool DEV>
+__global__ void __launch_bounds__(256) var_split_pass(const typename T::S *in, const VarSplit a, const float *means,
+                                                      float *partial) {
+  __shared__ float warp_part[8];
+  const long long groups = a.results * a.chunks;
+  for (long long g = blockIdx.x; g < groups; g += gridDim.x) {
+    const long long r = g / a.chunks;
+    const long long f0 = (g - r * a.chunks) * a.chunk, f1 = min(a.depth, f0 + a.chunk);
+    const typename T::S *base = in + walk_pos(a.kept, r);
+    const float mean = DEV ? means[r] : 0.0f;
+    float s = 0.0f;
+    long long f = f0 + threadIdx.x;
+    if (f < f1) {
+      long long o = f / a.run, j = f - o * a.run;
+      const long long so = 256 / a.run, sj = 256 - so * a.run;
+      long long last_o = o, opos = walk_pos(a.outer, o);
+      for (; f < f1; f += 256) {
+        if (o != last_o) {
+          last_o = o;
+          opos = walk_pos(a.outer, o);
+        }
+        const float x = T::load(base[opos + j * a.run_stride]);
+        if (DEV) {
+          const float d = __fsub_rn(x, mean);
+          s = __fadd_rn(s, __fmul_rn(d, d));
+        } else {
+          s = __fadd_rn(s, x);
+        }
+        j += sj;
+        o += so;
+        if (j >= a.run) {
+          j -= a.run;
+          ++o;
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, d));
+    if ((threadIdx.x & 31) == 0) warp_part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = warp_part[0];
+      for (int w = 1; w < 8; ++w) t = __fadd_rn(t, warp_part[w]);
+      partial[g] = t;
+    }
+    __syncthreads();
+  }
+}
+
+// The chunk sums of each slice in chunk order: the f32 mean (into means),
+// or the variance rounded to T (into out).
+template <class T, bool DEV>
+__global__ void __launch_bounds__(256) var_split_finish(const VarSplit a, const float *partial, float *means,
+                                                        typename T::S *out) {
+  for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < a.results;
+       r += (long long)gridDim.x * blockDim.x) {
+    float t = 0.0f;
+    for (int c = 0; c < a.chunks; ++c) t = __fadd_rn(t, partial[r * a.chunks + c]);
+    if (DEV) out[r] = T::store(__fdiv_rn(t, a.divisor));
+    else means[r] = __fdiv_rn(t, a.count);
+  }
+}
+
 void fill_walk(Walk &w, const Dims &shape, const Dims &strides) {
   w = Walk{};
   w.rank = int(shape.rank);
@@ -697,6 +775,34 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
   // rows: innermost folded axis contiguous (unless the kept axis is the
   // contiguous one and the runs are short).
   const bool kept_inner_contig = kc.rank && kcs.v[kc.rank - 1] == 1;
+  if (MODE == M_VAR && fc.rank >= 1 && results < (long long)sms * 16 && depth >= 16384) {
+    VarSplit v{};
+    fill_walk(v.kept, kc, kcs);
+    Dims fo = fc, fos = fcs;
+    fo.rank = fos.rank = fc.rank - 1;
+    fill_walk(v.outer, fo, fos);
+    v.run = (long long)fc.v[fc.rank - 1];
+    v.run_stride = (long long)fcs.v[fc.rank - 1];
+    v.results = results;
+    v.depth = depth;
+    // chunks of at least 4096 elements, about 8 blocks' worth per SM in all
+    const long long want = std::max(1LL, (long long)sms * 8 / results);
+    v.chunk = std::max(4096LL, ((depth + want - 1) / want + 255) / 256 * 256);
+    v.chunks = int((depth + v.chunk - 1) / v.chunk);
+    v.count = count;
+    v.divisor = divisor;
+    void *p = nullptr;
+    const size_t groups = size_t(results) * size_t(v.chunks);
+    if (int st = scratch_get((groups + size_t(results)) * sizeof(float), &p)) return st;
+    float *partial = static_cast<float *>(p), *means = partial + groups;
+    const unsigned grid = unsigned(std::min<long long>((long long)groups, (long long)sms * 8));
+    const unsigned fgrid = unsigned((results + 255) / 256);
+    var_split_pass<T, false><<<grid, 256, 0, stream>>>(in, v, nullptr, partial);
+    var_split_finish<T, false><<<fgrid, 256, 0, stream>>>(v, partial, means, o);
+    var_split_pass<T, true><<<grid, 256, 0, stream>>>(in, v, means, partial);
+    var_split_finish<T, true><<<fgrid, 256, 0, stream>>>(v, partial, means, o);
+    return check_launch("reduce (variance, split)");
+  }
   if (fc.rank >= 1 && fcs.v[fc.rank - 1] == 1 && !(kept_inner_contig && fc.v[fc.rank - 1] < 64)) {
     RowsArgs a{};
     fill_walk(a.kept, kc, kcs);
@@ -714,8 +820,11 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     for (uint32_t ax = 0; a.vec && ax < fo.rank; ++ax) a.vec = fos.v[ax] % N == 0;
     // The fast path: at most one kept and one outer folded axis, packs, and
     // index ranges that fit 32 bits.
+    // (A few long single-run slices go to the general kernel, which splits
+    // a run between warps; this one splits only across runs.)
+    const bool few_long_runs = a.outer == 1 && results < (long long)sms * 16 && a.run / N >= 32LL * 8 * 4;
     if (MODE != M_VAR && a.vec && kc.rank <= 1 && fo.rank <= 1 && a.outer < (1LL << 30) &&
-        a.run / N < (1LL << 30)) {
+        a.run / N < (1LL << 30) && !few_long_runs) {
       FastRows f{};
       f.kept_stride = kc.rank ? (long long)kcs.v[0] : 0;
       f.outer_stride = fo.rank ? (long long)fos.v[0] : 0;

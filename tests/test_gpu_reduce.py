@@ -225,3 +225,40 @@ def test_column_arg_reductions_with_nans_ties_and_signed_zeros(device, dtype):
     for op in (N.RMAX, N.RMIN):
         got = cuda.Cuda.arg_reduce(v, 0, op).as_slice()
         assert np.array_equal(got, O.arg_reduce(dtype, shape, x, 0, st, 0, op)), op
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape,axes,offset_perm", [
+    ([1 << 22], [0], None),            # one long slice: the split variance, the run-splitting sum
+    ([100000, 3], [0], None),          # three long strided columns
+    ([7, 8, 4096], [0, 2], None),      # eight slices, each 7 runs of 4096
+    ([8, 4096, 6], [0, 1], [1, 2, 0]),  # a permuted view: 8 slices of 24576 over two folded axes
+])
+def test_few_long_slices(device, dtype, shape, axes, offset_perm):
+    """Few slices of 16384+ elements: the variance splits each slice into
+    chunks over the whole machine (two passes, chunk sums in order) and a
+    single long run's sum is split between warps; both against the oracle
+    within the f32 sum bound (the integral filler makes folds and means
+    exact)."""
+    n = int(np.prod(shape))
+    for fill, exact in ((integral(n), True), (normal(n, 17) + np.float32(3.0), False)):
+        x = O.narrow(fill, dtype)
+        strides = cuda.contiguous_strides(shape)
+        view_shape = shape
+        if offset_perm is not None:
+            view_shape = [shape[a] for a in offset_perm]
+            strides = [strides[a] for a in offset_perm]
+        s = cuda.CudaStorage.store(x, dtype)
+        view = cuda.TensorView(s, list(view_shape), list(strides), 0)
+        depth = int(np.prod([view_shape[a] for a in axes]))
+        for kind, op in ((N.AXIS_FOLD, N.SUM), (N.AXIS_MEAN, 0), (N.AXIS_VARIANCE, 0), (N.AXIS_FOLD, N.RMAX)):
+            divisor = depth - 1 if kind == N.AXIS_VARIANCE else 0
+            got = O.widen(cuda.Cuda.reduce_axes(view, axes, kind, op, divisor).as_slice(), dtype)
+            want = O.widen(O.reduce_axes(dtype, view_shape, x, 0, strides, axes, kind, op, divisor), dtype)
+            if (exact and kind != N.AXIS_VARIANCE) or op == N.RMAX:
+                assert np.array_equal(got, want), (kind, op)
+            else:
+                half = 0 if dtype == "f32" else (2.0 ** -7 if dtype == "bf16" else 2.0 ** -10)
+                scale = np.abs(want) + 1.0
+                same_inf = np.isinf(got) & (got == want)  # f16 sums of millions overflow on both sides
+                assert np.all(same_inf | (np.abs(got - want) <= (1e-5 * np.sqrt(depth) + half) * scale)), (kind, op)
