@@ -36,12 +36,14 @@ struct Place {
   int lead;
   int in_order;  // element (row, col) is data[offset + row*cols + col]
   int stat;      // -1: read from memory; else 2*k + (0 mean, 1 deviations) of statistic source k
+  int packs;     // in order, offset a multiple of 4, data aligned for 4-element vector loads
   long long offset, col_step;
   long long dims[TC_MAX_RANK - 1], steps[TC_MAX_RANK - 1];
 };
 
 struct Program {
   int n_code, n_places, n_outputs, n_stat_sources;
+  int needs_rc;  // some place is read out of order: elements need their (row, col)
   long long rows, cols;
   tc_instr code[MAX_CODE];
   Place places[MAX_PLACES];
@@ -81,42 +83,231 @@ __device__ __forceinline__ float load_place(const Place &pl, long long i, long l
   return T::load(T::store(load_as(pl.data, pl.dtype, place_at(pl, i, row, col))));
 }
 
-// Run the program on element i = (row, col).  `stats` holds the row's
-// statistics (2 per source) for places that read one; `sink(slot, value)`
-// receives every store.
-template <class T, class Sink>
-__device__ __forceinline__ void run_element(const Program &p, long long i, long long row, long long col,
-                                            const float *stats, Sink &&sink) {
-  float reg[REGISTERS];
+// E elements of the space run through the program together: flat indices
+// i0 .. i0+n-1 (n <= E), each with its (row, col).  Registers hold E values;
+// a load of an in-order place whose E elements are 16-byte (f32) or 8-byte
+// (f16/bf16) aligned is one vector load, and so is the store of a group.
+template <int E> struct Group {
+  long long i0;
+  int n;
+  long long row[E], col[E];
+};
+
+template <int E>
+__device__ __forceinline__ Group<E> make_group(long long i0, int n, long long cols, bool with_rc = true) {
+  Group<E> g;
+  g.i0 = i0;
+  g.n = n;
+  if (!with_rc) return g;
+  long long r = i0 / cols, c = i0 - r * cols;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    g.row[e] = r;
+    g.col[e] = c;
+    if (++c == cols) {
+      c = 0;
+      ++r;
+    }
+  }
+  return g;
+}
+
+__device__ __forceinline__ bool aligned_to(const void *p, unsigned bytes) {
+  return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0;
+}
+
+template <class T, int E>
+__device__ __forceinline__ void load_group(const Place &pl, const Group<E> &g, float v[E]) {
+  if (pl.in_order) {
+    const long long at = pl.offset + g.i0;
+    if (E % 4 == 0 && pl.packs && g.n == E && (g.i0 & 3) == 0) {
+      if (pl.dtype == TC_F32) {
+        const float4 *src = reinterpret_cast<const float4 *>(pl.data) + at / 4;
+        float4 q[E / 4 > 0 ? E / 4 : 1];
+#pragma unroll
+        for (int k = 0; k < E / 4; ++k) q[k] = __ldg(src + k);
+#pragma unroll
+        for (int k = 0; k < E / 4; ++k) {
+          v[4 * k] = q[k].x;
+          v[4 * k + 1] = q[k].y;
+          v[4 * k + 2] = q[k].z;
+          v[4 * k + 3] = q[k].w;
+        }
+        goto convert;
+      }
+      {
+        const uint2 *src = reinterpret_cast<const uint2 *>(pl.data) + at / 4;
+        uint2 q[E / 4 > 0 ? E / 4 : 1];
+#pragma unroll
+        for (int k = 0; k < E / 4; ++k) q[k] = __ldg(src + k);
+#pragma unroll
+        for (int k = 0; k < E / 4; ++k) {
+          const uint16_t h[4] = {uint16_t(q[k].x), uint16_t(q[k].x >> 16), uint16_t(q[k].y), uint16_t(q[k].y >> 16)};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[4 * k + j] = pl.dtype == TC_BF16 ? BF16T::load(h[j]) : F16T::load(h[j]);
+        }
+        goto convert;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      if (e < g.n) v[e] = load_as(pl.data, pl.dtype, at + e);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      if (e < g.n) v[e] = load_as(pl.data, pl.dtype, place_at(pl, g.i0 + e, g.row[e], g.col[e]));
+  }
+convert:
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = T::load(T::store(v[e]));
+}
+
+// Store a group's values of one output (laid out as the space, in order).
+template <int E>
+__device__ __forceinline__ void store_group(void *out, int dtype, const Group<E> &g, const float v[E]) {
+  if (E % 4 == 0 && g.n == E && (g.i0 & 3) == 0) {
+    if (dtype == TC_F32 && aligned_to(out, 16)) {
+#pragma unroll
+      for (int k = 0; k < E / 4; ++k)
+        reinterpret_cast<float4 *>(out)[g.i0 / 4 + k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      return;
+    }
+    if (dtype != TC_F32 && aligned_to(out, 8)) {
+#pragma unroll
+      for (int k = 0; k < E / 4; ++k) {
+        uint16_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = dtype == TC_BF16 ? BF16T::store(v[4 * k + j]) : F16T::store(v[4 * k + j]);
+        reinterpret_cast<uint2 *>(out)[g.i0 / 4 + k] =
+            make_uint2(uint32_t(h[0]) | (uint32_t(h[1]) << 16), uint32_t(h[2]) | (uint32_t(h[3]) << 16));
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+    if (e < g.n) store_as(out, dtype, g.i0 + e, v[e]);
+}
+
+// Run the program on a group.  `stats` holds the row's statistics (2 per
+// source) for places that read one (every element of the group is in that
+// row); `sink(slot, values)` receives every store.
+// The interpreter's blocks are INTERP_BLOCK threads; each thread's
+// registers live in shared memory, register r's element e of thread t at
+// rf_base[(r * E + e) * INTERP_BLOCK + t] (consecutive threads, consecutive
+// banks), since registers indexed by the program cannot be machine
+// registers and would otherwise go to local memory.
+constexpr int INTERP_BLOCK = 128;
+
+template <int E> struct RegFile {
+  float *base;  // this thread's register 0, element 0
+  __device__ __forceinline__ float &at(int r, int e) const { return base[(r * E + e) * INTERP_BLOCK]; }
+};
+
+template <int E> __device__ __forceinline__ RegFile<E> thread_registers() {
+  __shared__ float file[REGISTERS * E * INTERP_BLOCK];
+  return RegFile<E>{file + threadIdx.x};
+}
+
+template <class T, int E, class Sink>
+__device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, const float *stats, Sink &&sink) {
+  const RegFile<E> reg = thread_registers<E>();
   for (int k = 0; k < p.n_code; ++k) {
     const tc_instr in = p.code[k];
-    float v;
+    float v[E];
     switch (in.code) {
       case TC_I_LOAD: {
         const Place &pl = p.places[in.slot];
-        v = pl.stat >= 0 ? stats[pl.stat] : load_place<T>(pl, i, row, col);
+        if (pl.stat >= 0) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) v[e] = stats[pl.stat];
+        } else {
+          load_group<T, E>(pl, g, v);
+        }
         break;
       }
-      case TC_I_CONST: v = T::load(T::store(in.value)); break;
-      case TC_I_BINARY: v = T::load(T::store(binary_value(in.op, reg[in.a], reg[in.b]))); break;
-      case TC_I_UNARY: v = T::load(T::store(analytic(in.op, reg[in.a]))); break;
-      case TC_I_CMP: v = compare_value(in.op, reg[in.a], reg[in.b]); break;
-      default:  // store
-        sink(in.slot, reg[in.a]);
+      case TC_I_CONST: {
+        const float c = T::load(T::store(in.value));
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = c;
+        break;
+      }
+      case TC_I_BINARY: {
+        float x[E], y[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = reg.at(in.a, e), y[e] = reg.at(in.b, e);
+        // one branch per instruction, not per element
+        switch (in.op) {
+          case TC_ADD:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = __fadd_rn(x[e], y[e]);
+            break;
+          case TC_SUB:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = __fsub_rn(x[e], y[e]);
+            break;
+          case TC_MUL:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = __fmul_rn(x[e], y[e]);
+            break;
+          case TC_DIV:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = __fdiv_rn(x[e], y[e]);
+            break;
+          default:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = fmodf(x[e], y[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = T::load(T::store(v[e]));
+        break;
+      }
+      case TC_I_UNARY:
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = T::load(T::store(analytic(in.op, reg.at(in.a, e))));
+        break;
+      case TC_I_CMP: {
+        float x[E], y[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = reg.at(in.a, e), y[e] = reg.at(in.b, e);
+        switch (in.op) {
+          case TC_MIN:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = fminf(x[e], y[e]);
+            break;
+          case TC_MAX:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = fmaxf(x[e], y[e]);
+            break;
+          default:
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = compare_value(in.op, x[e], y[e]);
+        }
+        break;
+      }
+      default: {  // store
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = reg.at(in.a, e);
+        sink(int(in.slot), v);
         continue;
+      }
     }
-    reg[in.dst] = v;
+#pragma unroll
+    for (int e = 0; e < E; ++e) reg.at(in.dst, e) = v[e];
   }
 }
 
+constexpr int GROUP = 4;
+
 template <class T>
-__global__ void __launch_bounds__(256) fused_kernel(const __grid_constant__ Program p) {
+__global__ void __launch_bounds__(INTERP_BLOCK) fused_kernel(const __grid_constant__ Program p) {
   const long long total = p.rows * p.cols;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / p.cols, col = i - row * p.cols;
-    run_element<T>(p, i, row, col, nullptr,
-                   [&](int slot, float v) { store_as(p.out[slot], p.out_dtype[slot], i, v); });
+  const long long groups = (total + GROUP - 1) / GROUP;
+  for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < groups;
+       q += (long long)gridDim.x * blockDim.x) {
+    const long long i0 = q * GROUP;
+    const Group<GROUP> g = make_group<GROUP>(i0, int(min((long long)GROUP, total - i0)), p.cols, p.needs_rc != 0);
+    run_group<T, GROUP>(p, g, nullptr, [&](int slot, const float *v) { store_group<GROUP>(p.out[slot], p.out_dtype[slot], g, v); });
   }
 }
 
@@ -135,21 +326,36 @@ __device__ __forceinline__ void row_moments_of(const Place &pl, long long row, l
                                                float &dev) {
   const int lane = threadIdx.x & 31;
   float s = 0.0f;
-  for (long long c = lane; c < cols; c += 32) s = __fadd_rn(s, load_place<T>(pl, row * cols + c, row, c));
+  for (long long c0 = (long long)lane * GROUP; c0 < cols; c0 += 32 * GROUP) {
+    Group<GROUP> g = make_group<GROUP>(row * cols + c0, int(min((long long)GROUP, cols - c0)), cols);
+    float v[GROUP];
+    load_group<T, GROUP>(pl, g, v);
+#pragma unroll
+    for (int e = 0; e < GROUP; ++e)
+      if (e < g.n) s = __fadd_rn(s, v[e]);
+  }
   const float m = __fdiv_rn(warp_sum(s), float(cols));
   float d = 0.0f;
-  for (long long c = lane; c < cols; c += 32) {
-    const float e = __fsub_rn(load_place<T>(pl, row * cols + c, row, c), m);
-    d = __fadd_rn(d, __fmul_rn(e, e));
+  for (long long c0 = (long long)lane * GROUP; c0 < cols; c0 += 32 * GROUP) {
+    Group<GROUP> g = make_group<GROUP>(row * cols + c0, int(min((long long)GROUP, cols - c0)), cols);
+    float v[GROUP];
+    load_group<T, GROUP>(pl, g, v);
+#pragma unroll
+    for (int e = 0; e < GROUP; ++e)
+      if (e < g.n) {
+        const float x = __fsub_rn(v[e], m);
+        d = __fadd_rn(d, __fmul_rn(x, x));
+      }
   }
   mean = T::load(T::store(m));
   dev = T::load(T::store(warp_sum(d)));
 }
 
-// One warp per row.  SUM: the row's values of output 0 are added (f32,
-// rounded once to T) into sums[row] instead of stored.
+// One warp per row, each lane GROUP consecutive elements at a time.  SUM:
+// the row's values of output 0 are added (f32, rounded once to T) into
+// sums[row] instead of stored.
 template <class T, bool SUM>
-__global__ void __launch_bounds__(256) fused_rows_kernel(const __grid_constant__ Program p, void *sums) {
+__global__ void __launch_bounds__(INTERP_BLOCK) fused_rows_kernel(const __grid_constant__ Program p, void *sums) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.rows; row += warps) {
@@ -157,13 +363,17 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(const __grid_constant__
     for (int k = 0; k < p.n_stat_sources; ++k)
       row_moments_of<T>(p.places[p.stat_source[k]], row, p.cols, stats[2 * k], stats[2 * k + 1]);
     float acc = 0.0f;
-    for (long long col = lane; col < p.cols; col += 32) {
-      const long long i = row * p.cols + col;
+    for (long long c0 = (long long)lane * GROUP; c0 < p.cols; c0 += 32 * GROUP) {
+      const Group<GROUP> g = make_group<GROUP>(row * p.cols + c0, int(min((long long)GROUP, p.cols - c0)), p.cols);
       if (SUM) {
-        run_element<T>(p, i, row, col, stats, [&](int, float v) { acc = __fadd_rn(acc, v); });
+        run_group<T, GROUP>(p, g, stats, [&](int, const float *v) {
+#pragma unroll
+          for (int e = 0; e < GROUP; ++e)
+            if (e < g.n) acc = __fadd_rn(acc, v[e]);
+        });
       } else {
-        run_element<T>(p, i, row, col, stats,
-                       [&](int slot, float v) { store_as(p.out[slot], p.out_dtype[slot], i, v); });
+        run_group<T, GROUP>(p, g, stats,
+                            [&](int slot, const float *v) { store_group<GROUP>(p.out[slot], p.out_dtype[slot], g, v); });
       }
     }
     if (SUM) {
@@ -176,14 +386,20 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(const __grid_constant__
 // fused_sum along columns: thread = column, block row = a band of `band`
 // rows; partial[band][col] in f32 (or the rounded sum itself with one band).
 template <class T>
-__global__ void __launch_bounds__(256) fused_cols_kernel(const __grid_constant__ Program p, long long band,
+__global__ void __launch_bounds__(INTERP_BLOCK) fused_cols_kernel(const __grid_constant__ Program p, long long band,
                                                          float *partial, void *sums) {
   const long long col = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= p.cols) return;
   const long long r0 = (long long)blockIdx.y * band, r1 = min(p.rows, r0 + band);
   float acc = 0.0f;
-  for (long long row = r0; row < r1; ++row)
-    run_element<T>(p, row * p.cols + col, row, col, nullptr, [&](int, float v) { acc = __fadd_rn(acc, v); });
+  for (long long row = r0; row < r1; ++row) {
+    Group<1> g;
+    g.i0 = row * p.cols + col;
+    g.n = 1;
+    g.row[0] = row;
+    g.col[0] = col;
+    run_group<T, 1>(p, g, nullptr, [&](int, const float *v) { acc = __fadd_rn(acc, v[0]); });
+  }
   if (gridDim.y == 1) static_cast<typename T::S *>(sums)[col] = T::store(acc);
   else partial[(long long)blockIdx.y * p.cols + col] = acc;
 }
@@ -242,6 +458,8 @@ int take_place(const tc_place &q, uint32_t j, size_t rows, size_t cols, Place &p
     step *= pl.dims[a];
   }
   pl.in_order = in_order;
+  const uintptr_t align = q.dtype == TC_F32 ? 16 : 8;
+  pl.packs = in_order && q.offset % 4 == 0 && (reinterpret_cast<uintptr_t>(q.data) & (align - 1)) == 0;
   return TC_OK;
 }
 
@@ -294,6 +512,7 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
       continue;
     }
     if (int st = take_place(places[j], j, rows, cols, p.places[j])) return st;
+    if (!p.places[j].in_order) p.needs_rc = 1;
   }
   for (uint32_t s = 0; s < n_stats; ++s) {
     const uint32_t of = stats[s].of_place;
@@ -312,6 +531,13 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     p.out_dtype[j] = out_dtypes[j];
   }
   return TC_OK;
+}
+
+// Warps per row for the interpreter's row kernels: INTERP_BLOCK / 32 rows
+// per block, at most 6 blocks per SM (their register files).
+unsigned interp_row_grid(long long rows) {
+  constexpr int W = INTERP_BLOCK / 32;
+  return unsigned(std::max(1LL, std::min<long long>((rows + W - 1) / W, (long long)sm_count() * 6)));
 }
 
 unsigned row_grid(long long rows) {
@@ -334,7 +560,9 @@ int tc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t
   if (rows == 0 || cols == 0) return TC_OK;
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
-    fused_kernel<T><<<grid_for(rows * cols, 256, 8), 256, 0, as_stream(stream)>>>(p);
+    // 32 KB of register file per block: 6 blocks per SM
+    fused_kernel<T><<<grid_for((rows * cols + GROUP - 1) / GROUP, INTERP_BLOCK, 6), INTERP_BLOCK, 0,
+                      as_stream(stream)>>>(p);
     return check_launch("fused program");
   });
 }
@@ -350,7 +578,7 @@ int tc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr
   if (rows == 0 || cols == 0) return TC_OK;
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
-    fused_rows_kernel<T, false><<<row_grid((long long)rows), 256, 0, as_stream(stream)>>>(p, nullptr);
+    fused_rows_kernel<T, false><<<interp_row_grid((long long)rows), INTERP_BLOCK, 0, as_stream(stream)>>>(p, nullptr);
     return check_launch("fused program with statistics");
   });
 }
@@ -376,17 +604,17 @@ int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     if (axis == TC_ROWS) {
-      fused_rows_kernel<T, true><<<row_grid((long long)rows), 256, 0, s>>>(p, sums);
+      fused_rows_kernel<T, true><<<interp_row_grid((long long)rows), INTERP_BLOCK, 0, s>>>(p, sums);
       return check_launch("fused sum (rows)");
     }
-    const long long col_blocks = ((long long)cols + 255) / 256;
+    const long long col_blocks = ((long long)cols + INTERP_BLOCK - 1) / INTERP_BLOCK;
     const long long want = std::max(1LL, (long long)sm_count() * 8 / col_blocks);
     const long long band = std::max(16LL, ((long long)rows + want - 1) / want);
     const long long bands = ((long long)rows + band - 1) / band;
     float *partial = nullptr;
     if (bands > 1)
       if (int st = scratch(size_t(bands) * cols * sizeof(float), reinterpret_cast<void **>(&partial))) return st;
-    fused_cols_kernel<T><<<dim3(unsigned(col_blocks), unsigned(bands)), 256, 0, s>>>(p, band, partial, sums);
+    fused_cols_kernel<T><<<dim3(unsigned(col_blocks), unsigned(bands)), INTERP_BLOCK, 0, s>>>(p, band, partial, sums);
     if (int st = check_launch("fused sum (columns)")) return st;
     if (bands > 1) {
       cols_finish<T><<<grid_for(cols, 256, 4), 256, 0, s>>>(partial, bands, (long long)cols, sums);

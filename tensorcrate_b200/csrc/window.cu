@@ -32,21 +32,39 @@ __device__ __forceinline__ long long tap_index(const Window &w, long long wr, lo
   return w.flip ? (w.win_rows - 1 - wr) * w.win_cols + (w.win_cols - 1 - wc) : wr * w.win_cols + wc;
 }
 
-// One thread per output, the taps in the Host's order.
+// Four adjacent outputs of a row per thread, each summing its taps in the
+// Host's order: for each window row the thread slides a register window of
+// four input values along the row, so a tap costs one input load and one
+// window load for four products (instead of two loads for one).
 template <class T>
 __global__ void __launch_bounds__(256) correlate_direct(const typename T::S *in, const typename T::S *win,
                                                         typename T::S *out, Window w) {
-  const long long total = w.out_rows * w.out_cols;
+  const long long quads = (w.out_cols + 3) / 4, total = w.out_rows * quads;
   for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
        o += (long long)gridDim.x * blockDim.x) {
-    const long long row = o / w.out_cols, col = o - row * w.out_cols;
-    float sum = 0.0f;
+    const long long row = o / quads, c0 = (o - row * quads) * 4;
+    const int n = int(min(4LL, w.out_cols - c0));
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (long long wr = 0; wr < w.win_rows; ++wr) {
-      const typename T::S *x = in + (row + wr) * w.in_cols + col;
-      for (long long wc = 0; wc < w.win_cols; ++wc)
-        sum = __fadd_rn(sum, __fmul_rn(T::load(__ldg(x + wc)), T::load(__ldg(win + tap_index(w, wr, wc)))));
+      const typename T::S *x = in + (row + wr) * w.in_cols + c0;
+      const long long room = w.in_cols - c0;  // readable elements from x
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) v[j] = j < room ? T::load(__ldg(x + j)) : 0.0f;
+      for (long long wc = 0; wc < w.win_cols; ++wc) {
+        v[3] = wc + 3 < room ? T::load(__ldg(x + wc + 3)) : 0.0f;
+        const float k = T::load(__ldg(win + tap_index(w, wr, wc)));
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j < n) sum[j] = __fadd_rn(sum[j], __fmul_rn(v[j], k));
+        v[0] = v[1];
+        v[1] = v[2];
+        v[2] = v[3];
+      }
     }
-    out[o] = T::store(sum);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < n) out[row * w.out_cols + c0 + j] = T::store(sum[j]);
   }
 }
 
@@ -101,16 +119,19 @@ __global__ void __launch_bounds__(256) correlate_input_gradient_direct(const typ
   }
 }
 
-// pad (kernels.rs:1575-1601): zeros around the input, one thread per
-// output element, bits moved as they are.
+// pad (kernels.rs:1575-1601): zeros around the input, bits moved; a block
+// per output row in turn, its threads along the row (no division).
 template <class E>
 __global__ void __launch_bounds__(256) pad_kernel(const E *in, E *out, long long rows, long long cols,
                                                   long long pr, long long pc) {
-  const long long ocols = cols + 2 * pc, total = (rows + 2 * pr) * ocols;
-  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
-       o += (long long)gridDim.x * blockDim.x) {
-    const long long r = o / ocols - pr, c = o % ocols - pc;
-    out[o] = (r >= 0 && r < rows && c >= 0 && c < cols) ? in[r * cols + c] : E(0);
+  const long long ocols = cols + 2 * pc, orows = rows + 2 * pr;
+  for (long long orow = blockIdx.x; orow < orows; orow += gridDim.x) {
+    const long long r = orow - pr;
+    const bool inside_row = r >= 0 && r < rows;
+    E *dst = out + orow * ocols;
+    const E *src = in + (inside_row ? r * cols : 0) - pc;
+    for (long long c = threadIdx.x; c < ocols; c += blockDim.x)
+      dst[c] = (inside_row && c >= pc && c < pc + cols) ? src[c] : E(0);
   }
 }
 
@@ -132,7 +153,7 @@ int run_correlate(int dtype, const Window &w, const void *in, const void *win, v
       correlate_shared<T><<<grid, 256, 0, s>>>(static_cast<const S *>(in), static_cast<const S *>(win),
                                                static_cast<S *>(out), w);
     } else {
-      correlate_direct<T><<<grid_for(outputs, 256, 8), 256, 0, s>>>(static_cast<const S *>(in),
+      correlate_direct<T><<<grid_for((outputs + 3) / 4, 256, 8), 256, 0, s>>>(static_cast<const S *>(in),
                                                                       static_cast<const S *>(win),
                                                                       static_cast<S *>(out), w);
     }
@@ -190,7 +211,8 @@ int tc_pad(int dtype, size_t rows, size_t cols, size_t pad_rows, size_t pad_cols
   if ((rows * cols && !input) || !out) return fail(TC_EINVAL, "pad: null pointer");
   return with_real(dtype, [&](auto t) {
     using S = typename decltype(t)::S;
-    pad_kernel<S><<<grid_for(total, 256, 8), 256, 0, as_stream(stream)>>>(
+    const unsigned grid = unsigned(std::min<long long>((long long)(rows + 2 * pad_rows), (long long)sm_count() * 16));
+    pad_kernel<S><<<grid, 256, 0, as_stream(stream)>>>(
         static_cast<const S *>(input), static_cast<S *>(out), (long long)rows, (long long)cols,
         (long long)pad_rows, (long long)pad_cols);
     return check_launch("pad");
