@@ -43,6 +43,12 @@ int scratch(size_t bytes, void **out);
 // that takes tickets from them sets each back to zero when it is done, so
 // they are zero between launches.
 int counters(size_t n, int **out);
+// The means and sums of squared deviations (in the element type) of the
+// slices of `input` folded over `axes`, in as few passes as the layout
+// allows (reduce.cu).
+int reduce_moments(int dtype, uint32_t rank, const size_t *shape, const void *input, size_t offset,
+                   const size_t *strides, uint32_t n_axes, const uint32_t *axes, void *means, void *deviations,
+                   cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Element types.  A kernel computes in f32; loads widen exactly and stores

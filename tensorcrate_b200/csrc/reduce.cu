@@ -479,7 +479,8 @@ __global__ void __launch_bounds__(256) reduce_rows_fast(const typename T::S *in,
 template <class T>
 __global__ void __launch_bounds__(256) reduce_rows_var_fast(const typename T::S *in, long long kept_stride,
                                                             long long results, int per_run, float count,
-                                                            float divisor, typename T::S *out) {
+                                                            float divisor, typename T::S *out,
+                                                            typename T::S *mean_out) {
   constexpr int N = Pack<T>::N;
   constexpr int K = CACHE_PACKS;
   const int lane = threadIdx.x & 31;
@@ -510,7 +511,10 @@ __global__ void __launch_bounds__(256) reduce_rows_var_fast(const typename T::S 
         }
       }
     dev = warp_merge<M_SUM>(dev);
-    if (lane == 0) out[r] = T::store(__fdiv_rn(dev.v, divisor));
+    if (lane == 0) {
+      out[r] = T::store(__fdiv_rn(dev.v, divisor));
+      if (mean_out) mean_out[r] = T::store(mean);
+    }
   }
 }
 
@@ -702,28 +706,51 @@ __global__ void __launch_bounds__(256) var_split_pass(const typename T::S *in, c
     const typename T::S *base = in + walk_pos(a.kept, r);
     const float mean = DEV ? means[r] : 0.0f;
     float s = 0.0f;
-    long long f = f0 + threadIdx.x;
-    if (f < f1) {
-      long long o = f / a.run, j = f - o * a.run;
-      const long long so = 256 / a.run, sj = 256 - so * a.run;
-      long long last_o = o, opos = walk_pos(a.outer, o);
-      for (; f < f1; f += 256) {
-        if (o != last_o) {
-          last_o = o;
-          opos = walk_pos(a.outer, o);
+    auto add = [&](float x) {
+      if (DEV) {
+        const float d = __fsub_rn(x, mean);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+      } else {
+        s = __fadd_rn(s, x);
+      }
+    };
+    using P = Pack<T>;
+    constexpr int N = P::N;
+    if (a.outer.rank == 0 && a.run_stride == 1 && (reinterpret_cast<uintptr_t>(base + f0) & 15u) == 0) {
+      // One contiguous run: 16-byte packs, two per thread in flight.
+      const long long packs = (f1 - f0) / N;
+      const uint4 *src = reinterpret_cast<const uint4 *>(base + f0);
+      for (long long q = threadIdx.x; q < packs; q += 512) {
+        P x0, x1;
+        x0.raw = __ldg(src + q);
+        const bool two = q + 256 < packs;
+        if (two) x1.raw = __ldg(src + q + 256);
+#pragma unroll
+        for (int e = 0; e < N; ++e) add(T::load(x0.v[e]));
+        if (two) {
+#pragma unroll
+          for (int e = 0; e < N; ++e) add(T::load(x1.v[e]));
         }
-        const float x = T::load(base[opos + j * a.run_stride]);
-        if (DEV) {
-          const float d = __fsub_rn(x, mean);
-          s = __fadd_rn(s, __fmul_rn(d, d));
-        } else {
-          s = __fadd_rn(s, x);
-        }
-        j += sj;
-        o += so;
-        if (j >= a.run) {
-          j -= a.run;
-          ++o;
+      }
+      for (long long f = f0 + packs * N + threadIdx.x; f < f1; f += 256) add(T::load(base[f]));
+    } else {
+      long long f = f0 + threadIdx.x;
+      if (f < f1) {
+        long long o = f / a.run, j = f - o * a.run;
+        const long long so = 256 / a.run, sj = 256 - so * a.run;
+        long long last_o = o, opos = walk_pos(a.outer, o);
+        for (; f < f1; f += 256) {
+          if (o != last_o) {
+            last_o = o;
+            opos = walk_pos(a.outer, o);
+          }
+          add(T::load(base[opos + j * a.run_stride]));
+          j += sj;
+          o += so;
+          if (j >= a.run) {
+            j -= a.run;
+            ++o;
+          }
         }
       }
     }
@@ -749,8 +776,12 @@ __global__ void __launch_bounds__(256) var_split_finish(const VarSplit a, const 
        r += (long long)gridDim.x * blockDim.x) {
     float t = 0.0f;
     for (int c = 0; c < a.chunks; ++c) t = __fadd_rn(t, partial[r * a.chunks + c]);
-    if (DEV) out[r] = T::store(__fdiv_rn(t, a.divisor));
-    else means[r] = __fdiv_rn(t, a.count);
+    if (DEV) {
+      out[r] = T::store(__fdiv_rn(t, a.divisor));
+    } else {
+      means[r] = __fdiv_rn(t, a.count);
+      if (out) out[r] = T::store(means[r]);  // the mean in T, for moments
+    }
   }
 }
 
@@ -765,12 +796,20 @@ void fill_walk(Walk &w, const Dims &shape, const Dims &strides) {
 
 int scratch_get(size_t bytes, void **out) { return scratch(bytes, out); }
 
+// A variance's slices' means in T, when the path computing the variance
+// can write them too (`written` says whether it did).
+struct MeanOut {
+  void *ptr = nullptr;
+  bool written = false;
+};
+
 template <class T, int MODE>
 int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const Dims &fc, const Dims &fcs,
                 long long results, long long depth, float count, float divisor, void *out, uint32_t *arg_out,
-                cudaStream_t stream) {
+                cudaStream_t stream, MeanOut *mean_out = nullptr) {
   using S = typename T::S;
   S *o = static_cast<S *>(out);
+  S *mo = mean_out ? static_cast<S *>(mean_out->ptr) : nullptr;
   const int sms = sm_count();
   // rows: innermost folded axis contiguous (unless the kept axis is the
   // contiguous one and the runs are short).
@@ -798,7 +837,8 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     const unsigned grid = unsigned(std::min<long long>((long long)groups, (long long)sms * 8));
     const unsigned fgrid = unsigned((results + 255) / 256);
     var_split_pass<T, false><<<grid, 256, 0, stream>>>(in, v, nullptr, partial);
-    var_split_finish<T, false><<<fgrid, 256, 0, stream>>>(v, partial, means, o);
+    var_split_finish<T, false><<<fgrid, 256, 0, stream>>>(v, partial, means, mo);
+    if (mean_out) mean_out->written = true;
     var_split_pass<T, true><<<grid, 256, 0, stream>>>(in, v, means, partial);
     var_split_finish<T, true><<<fgrid, 256, 0, stream>>>(v, partial, means, o);
     return check_launch("reduce (variance, split)");
@@ -866,7 +906,8 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       }
       unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * resident_var));
       reduce_rows_var_fast<T><<<std::max(1u, grid), 256, 0, stream>>>(
-          in, kc.rank ? (long long)kcs.v[0] : 0, results, int(a.run / N), count, divisor, o);
+          in, kc.rank ? (long long)kcs.v[0] : 0, results, int(a.run / N), count, divisor, o, mo);
+      if (mean_out) mean_out->written = true;
       return check_launch("reduce (rows, variance, fast)");
     }
     if (MODE == M_VAR) {
@@ -998,7 +1039,7 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
 // The shared driver of reduce_axes and arg_reduce.
 int run_reduction(int dtype, uint32_t rank, const size_t *shape, const void *input, size_t offset,
                   const size_t *strides, const bool *folded, int mode, size_t divisor, void *out,
-                  uint32_t *arg_out, cudaStream_t stream) {
+                  uint32_t *arg_out, cudaStream_t stream, MeanOut *mean_out = nullptr) {
   // Split, layout.rs:370-414.
   size_t ks[TC_MAX_RANK], kst[TC_MAX_RANK], fs[TC_MAX_RANK], fst[TC_MAX_RANK];
   uint32_t nk = 0, nf = 0;
@@ -1029,7 +1070,9 @@ int run_reduction(int dtype, uint32_t rank, const size_t *shape, const void *inp
       case M_MIN: return launch_mode<T, M_MIN>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
       case M_MAX: return launch_mode<T, M_MAX>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
       case M_MEAN: return launch_mode<T, M_MEAN>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
-      case M_VAR: return launch_mode<T, M_VAR>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
+      case M_VAR:
+        return launch_mode<T, M_VAR>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream,
+                                     mean_out);
       case M_ARGMIN: return launch_mode<T, M_ARGMIN>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
       case M_ARGMAX: return launch_mode<T, M_ARGMAX>(in, kc, kcs[0], fc, fcs[0], results, depth, count, div, out, arg_out, stream);
     }
@@ -1092,6 +1135,23 @@ int vector_fold(int dtype, const void *a, const void *b, size_t n, void *out, cu
 }  // namespace
 
 
+
+// Means and sums of squared deviations of the slices of `input` folded over
+// `axes` (both in T): the variance kernel with divisor 1, which writes the
+// means too where it can; otherwise a mean reduction beside it.
+int reduce_moments(int dtype, uint32_t rank, const size_t *shape, const void *input, size_t offset,
+                   const size_t *strides, uint32_t n_axes, const uint32_t *axes, void *means, void *deviations,
+                   cudaStream_t stream) {
+  bool folded[TC_MAX_RANK] = {false};
+  for (uint32_t i = 0; i < n_axes; ++i) folded[axes[i]] = true;
+  MeanOut m;
+  m.ptr = means;
+  if (int st = run_reduction(dtype, rank, shape, input, offset, strides, folded, M_VAR, 1, deviations, nullptr, stream,
+                             &m))
+    return st;
+  if (m.written) return TC_OK;
+  return run_reduction(dtype, rank, shape, input, offset, strides, folded, M_MEAN, 0, means, nullptr, stream);
+}
 
 }  // namespace tc
 

@@ -3,10 +3,9 @@
 // vector_distribution, matrix_distribution, matrix_axis_distribution;
 // kernels.rs:1035-1070).
 //
-// Moments are the reductions' two passes: the mean (f32 sum / count) and
-// the variance kernel with divisor 1, which is the sum of squared
-// deviations from the f32 mean (statistics/mod.rs:419-441), each rounded
-// once to T.
+// Moments are the variance kernels with divisor 1, which is the sum of
+// squared deviations from the f32 mean (statistics/mod.rs:419-441); those
+// kernels write the mean (f32 sum / count) as well, each rounded once to T.
 //
 // The distribution functions are evaluated in f64 per element, as the Host
 // does (statistics/special.rs), with the products, sums and quotients
@@ -300,9 +299,7 @@ int tc_moments(int dtype, const void *a, size_t n, void *out_dev, void *stream) 
   const size_t shape[1] = {n}, strides[1] = {1};
   const uint32_t axes[1] = {0};
   char *out = static_cast<char *>(out_dev);
-  if (int st = tc_reduce_axes(dtype, 1, shape, a, n, 0, strides, 1, axes, TC_AXIS_MEAN, 0, 0, out, stream)) return st;
-  return tc_reduce_axes(dtype, 1, shape, a, n, 0, strides, 1, axes, TC_AXIS_VARIANCE, 0, 1, out + dtype_bytes(dtype),
-                        stream);
+  return reduce_moments(dtype, 1, shape, a, 0, strides, 1, axes, out, out + dtype_bytes(dtype), s);
 }
 
 int tc_axis_moments(int dtype, size_t rows, size_t cols, int axis, const void *a, void *means, void *deviations,
@@ -320,10 +317,7 @@ int tc_axis_moments(int dtype, size_t rows, size_t cols, int axis, const void *a
   if (!a) return fail(TC_EINVAL, "axis_moments: null input");
   const size_t shape[2] = {rows, cols}, strides[2] = {cols, 1};
   const uint32_t axes[1] = {axis == TC_ROWS ? 1u : 0u};
-  if (int st = tc_reduce_axes(dtype, 2, shape, a, rows * cols, 0, strides, 1, axes, TC_AXIS_MEAN, 0, 0, means, stream))
-    return st;
-  return tc_reduce_axes(dtype, 2, shape, a, rows * cols, 0, strides, 1, axes, TC_AXIS_VARIANCE, 0, 1, deviations,
-                        stream);
+  return reduce_moments(dtype, 2, shape, a, 0, strides, 1, axes, means, deviations, s);
 }
 
 int tc_distribution(int dtype, int family, int statistic, const void *a, size_t n, double first, double second,
