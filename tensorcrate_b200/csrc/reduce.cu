@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(256) reduce_finish(const RowsArgs a, const Acc
 constexpr int CACHE_PACKS = 8;
 template <class T>
 __global__ void __launch_bounds__(256, 2) reduce_rows_var(const typename T::S *in, const RowsArgs a,
-                                                          typename T::S *out) {
+                                                          typename T::S *out, typename T::S *mean_out) {
   using S = typename T::S;
   constexpr int N = Pack<T>::N;
   const int lane = threadIdx.x & 31;
@@ -243,22 +243,53 @@ __global__ void __launch_bounds__(256, 2) reduce_rows_var(const typename T::S *i
           }
         }
     } else {
-      for (long long o = 0; o < a.outer; ++o) {
-        const S *rp = base + (a.outer > 1 ? walk_pos(a.folded, o) : 0);
-        for (long long c = lane; c < a.run; c += 32) sum.v = __fadd_rn(sum.v, T::load(rp[c]));
-      }
-      sum = warp_merge<M_SUM>(sum);
-      const float mean = __fdiv_rn(sum.v, a.count);
-      for (long long o = 0; o < a.outer; ++o) {
-        const S *rp = base + (a.outer > 1 ? walk_pos(a.folded, o) : 0);
-        for (long long c = lane; c < a.run; c += 32) {
-          const float d = __fsub_rn(T::load(rp[c]), mean);
-          dev.v = __fadd_rn(dev.v, __fmul_rn(d, d));
+      // Each pass: packs of the runs, four per lane in flight (the second
+      // pass finds the slice in L2); element by element without packs.
+      constexpr int U = 4;
+      float mean = 0.0f;
+      for (int pass = 0; pass < 2; ++pass) {
+        Acc &acc = pass ? dev : sum;
+        auto add = [&](float x) {
+          if (pass) {
+            const float d = __fsub_rn(x, mean);
+            acc.v = __fadd_rn(acc.v, __fmul_rn(d, d));
+          } else {
+            acc.v = __fadd_rn(acc.v, x);
+          }
+        };
+        for (long long o = 0; o < a.outer; ++o) {
+          const S *rp = base + (a.outer > 1 ? walk_pos(a.folded, o) : 0);
+          if (a.vec) {
+            const long long packs = a.run / N;
+            const uint4 *pp = reinterpret_cast<const uint4 *>(rp);
+            for (long long c0 = lane; c0 < packs; c0 += 32 * U) {
+              Pack<T> x[U];
+#pragma unroll
+              for (int u = 0; u < U; ++u)
+                if (c0 + 32 * u < packs) x[u].raw = __ldg(pp + c0 + 32 * u);
+#pragma unroll
+              for (int u = 0; u < U; ++u)
+                if (c0 + 32 * u < packs) {
+#pragma unroll
+                  for (int j = 0; j < N; ++j) add(T::load(x[u].v[j]));
+                }
+            }
+          } else {
+            for (long long c = lane; c < a.run; c += 32) add(T::load(rp[c]));
+          }
+        }
+        if (!pass) {
+          sum = warp_merge<M_SUM>(sum);
+          mean = __fdiv_rn(sum.v, a.count);
         }
       }
+      if (lane == 0 && mean_out) mean_out[r] = T::store(mean);
     }
     dev = warp_merge<M_SUM>(dev);
-    if (lane == 0) out[r] = T::store(__fdiv_rn(dev.v, a.divisor));
+    if (lane == 0) {
+      out[r] = T::store(__fdiv_rn(dev.v, a.divisor));
+      if (cache && mean_out) mean_out[r] = T::store(__fdiv_rn(sum.v, a.count));
+    }
   }
 }
 
@@ -913,7 +944,8 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     if (MODE == M_VAR) {
       a.splits = 1;
       unsigned grid = unsigned(std::min<long long>((results + 7) / 8, (long long)sms * 8));
-      reduce_rows_var<T><<<std::max(1u, grid), 256, 0, stream>>>(in, a, o);
+      reduce_rows_var<T><<<std::max(1u, grid), 256, 0, stream>>>(in, a, o, mo);
+      if (mean_out) mean_out->written = true;
       return check_launch("reduce (rows, variance)");
     }
     // Split each slice into shares (of whole runs, or of its one run's
