@@ -798,21 +798,31 @@ __global__ void __launch_bounds__(256) var_split_pass(const typename T::S *in, c
   }
 }
 
-// The chunk sums of each slice in chunk order: the f32 mean (into means),
-// or the variance rounded to T (into out).
+// The chunk sums of each slice (a block per slice: thread t adds chunks t,
+// t+256, ... in order, then a fixed tree): the f32 mean (into means, and in
+// T into out when asked), or the variance rounded to T (into out).
 template <class T, bool DEV>
 __global__ void __launch_bounds__(256) var_split_finish(const VarSplit a, const float *partial, float *means,
                                                         typename T::S *out) {
-  for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < a.results;
-       r += (long long)gridDim.x * blockDim.x) {
+  __shared__ float warp_part[8];
+  for (long long r = blockIdx.x; r < a.results; r += gridDim.x) {
     float t = 0.0f;
-    for (int c = 0; c < a.chunks; ++c) t = __fadd_rn(t, partial[r * a.chunks + c]);
-    if (DEV) {
-      out[r] = T::store(__fdiv_rn(t, a.divisor));
-    } else {
-      means[r] = __fdiv_rn(t, a.count);
-      if (out) out[r] = T::store(means[r]);  // the mean in T, for moments
+    for (int c = threadIdx.x; c < a.chunks; c += 256) t = __fadd_rn(t, partial[r * a.chunks + c]);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, d));
+    if ((threadIdx.x & 31) == 0) warp_part[threadIdx.x >> 5] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float total = warp_part[0];
+      for (int w = 1; w < 8; ++w) total = __fadd_rn(total, warp_part[w]);
+      if (DEV) {
+        out[r] = T::store(__fdiv_rn(total, a.divisor));
+      } else {
+        means[r] = __fdiv_rn(total, a.count);
+        if (out) out[r] = T::store(means[r]);  // the mean in T, for moments
+      }
     }
+    __syncthreads();
   }
 }
 
@@ -866,7 +876,7 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     if (int st = scratch_get((groups + size_t(results)) * sizeof(float), &p)) return st;
     float *partial = static_cast<float *>(p), *means = partial + groups;
     const unsigned grid = unsigned(std::min<long long>((long long)groups, (long long)sms * 8));
-    const unsigned fgrid = unsigned((results + 255) / 256);
+    const unsigned fgrid = unsigned(std::min<long long>(results, (long long)sms * 8));
     var_split_pass<T, false><<<grid, 256, 0, stream>>>(in, v, nullptr, partial);
     var_split_finish<T, false><<<fgrid, 256, 0, stream>>>(v, partial, means, mo);
     if (mean_out) mean_out->written = true;
