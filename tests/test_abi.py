@@ -134,3 +134,34 @@ def test_no_host_code_calls_a_device_only_function():
     for o in objs:
         out = subprocess.run(["nm", "-u", str(o)], capture_output=True, text=True).stdout.split()
         assert "exit" not in out, f"{o.name} references exit"
+
+
+def test_other_methods_refuse_bad_arguments_on_the_host():
+    """The trait methods beyond the configs check their enums and shapes
+    before any device call: a bad Analytic, SortOrder, Axis, Family or
+    Statistic, a window larger than its input, a place missing."""
+    fake = C.c_void_p(0x1000)
+    assert _status("tc_unary", N.F32, 14, fake, fake, 4, None)[0] == N.EINVAL
+    assert _status("tc_unary_dual", N.F32, 99, fake, fake, fake, fake, 4, None)[0] == N.EINVAL
+    assert _status("tc_sort", N.F32, 2, fake, fake, 4, None)[0] == N.EINVAL
+    assert _status("tc_sort", 9, N.ASCENDING, fake, fake, 4, None)[0] == N.EINVAL
+    assert _status("tc_correlate", N.F32, 2, 3, 3, 1, 0, fake, fake, fake, None)[0] == N.EINVAL
+    assert _status("tc_correlate", N.F32, 2, 3, 0, 1, 0, fake, fake, fake, None)[0] == N.EINVAL
+    assert _status("tc_correlate_input_gradient", N.F32, 0, 3, 1, 1, 0, fake, fake, fake, None)[0] == N.EINVAL
+    assert _status("tc_axis_moments", N.F32, 2, 3, 2, fake, fake, fake, None)[0] == N.EINVAL
+    assert _status("tc_distribution", N.F32, 2, N.PDF, fake, 4, 0.0, 1.0, fake, None)[0] == N.EINVAL
+    assert _status("tc_distribution", N.F32, N.NORMAL, 3, fake, 4, 0.0, 1.0, fake, None)[0] == N.EINVAL
+    assert _status("tc_axis_distribution", N.F32, 2, 2, 5, N.NORMAL, N.CDF, fake, fake, fake, fake, None)[0] == N.EINVAL
+    assert _status("tc_row_moments", N.F32, None, 4, 4, fake, fake, None)[0] == N.EINVAL
+    assert _status("tc_fused_sum", N.F32, 2, 2, None, 0, None, 0, 7, fake, None)[0] == N.EINVAL
+    assert _status("tc_matmul_program", N.F32, 2, 2, 2, fake, fake, None, 0, None, 0, None, None, 0, None)[0] == N.EINVAL
+
+
+def test_empty_inputs_of_the_other_methods_touch_nothing():
+    assert _status("tc_prefix_sum", N.F32, None, None, 0, None)[0] == N.OK
+    assert _status("tc_sort", N.F32, N.DESCENDING, None, None, 0, None)[0] == N.OK
+    assert _status("tc_unary", N.BF16, N.EXP, None, None, 0, None)[0] == N.OK
+    assert _status("tc_power", N.F16, None, None, None, 0, None)[0] == N.OK
+    assert _status("tc_flip", N.F32, 0, 5, None, None, None)[0] == N.OK
+    assert _status("tc_distribution", N.F32, N.NORMAL, N.PPF, None, 0, 0.0, 1.0, None, None)[0] == N.OK
+    assert _status("tc_axis_moments", N.F32, 0, 4, N.ROWS, None, None, None, None)[0] == N.OK
