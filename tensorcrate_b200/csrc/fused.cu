@@ -44,6 +44,8 @@ struct Place {
 struct Program {
   int n_code, n_places, n_outputs, n_stat_sources;
   int needs_rc;  // some place is read out of order: elements need their (row, col)
+  int n_ahead;   // places read in order, whose next group is requested into L2 ahead
+  int ahead[4];
   long long rows, cols;
   tc_instr code[MAX_CODE];
   Place places[MAX_PLACES];
@@ -299,6 +301,16 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
 
 constexpr int GROUP = 4;
 
+// Ask L2 for the group at flat index i0 of each in-order place the program
+// loads: a thread's next group arrives while it runs the current one.
+__device__ __forceinline__ void request_ahead(const Program &p, long long i0) {
+  for (int k = 0; k < p.n_ahead; ++k) {
+    const Place &pl = p.places[p.ahead[k]];
+    const char *at = static_cast<const char *>(pl.data) + (pl.offset + i0) * (pl.dtype == TC_F32 ? 4 : 2);
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(at));
+  }
+}
+
 template <class T>
 __global__ void __launch_bounds__(INTERP_BLOCK) fused_kernel(const __grid_constant__ Program p) {
   const long long total = p.rows * p.cols;
@@ -306,6 +318,8 @@ __global__ void __launch_bounds__(INTERP_BLOCK) fused_kernel(const __grid_consta
   for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < groups;
        q += (long long)gridDim.x * blockDim.x) {
     const long long i0 = q * GROUP;
+    const long long next = i0 + (long long)gridDim.x * blockDim.x * GROUP;
+    if (next < total) request_ahead(p, next);
     const Group<GROUP> g = make_group<GROUP>(i0, int(min((long long)GROUP, total - i0)), p.cols, p.needs_rc != 0);
     run_group<T, GROUP>(p, g, nullptr, [&](int slot, const float *v) { store_group<GROUP>(p.out[slot], p.out_dtype[slot], g, v); });
   }
@@ -364,6 +378,7 @@ __global__ void __launch_bounds__(INTERP_BLOCK) fused_rows_kernel(const __grid_c
       row_moments_of<T>(p.places[p.stat_source[k]], row, p.cols, stats[2 * k], stats[2 * k + 1]);
     float acc = 0.0f;
     for (long long c0 = (long long)lane * GROUP; c0 < p.cols; c0 += 32 * GROUP) {
+      if (c0 + 2 * 32 * GROUP < p.cols) request_ahead(p, row * p.cols + c0 + 2 * 32 * GROUP);
       const Group<GROUP> g = make_group<GROUP>(row * p.cols + c0, int(min((long long)GROUP, p.cols - c0)), p.cols);
       if (SUM) {
         run_group<T, GROUP>(p, g, stats, [&](int, const float *v) {
@@ -513,6 +528,7 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     }
     if (int st = take_place(places[j], j, rows, cols, p.places[j])) return st;
     if (!p.places[j].in_order) p.needs_rc = 1;
+    else if (p.n_ahead < 4) p.ahead[p.n_ahead++] = int(j);
   }
   for (uint32_t s = 0; s < n_stats; ++s) {
     const uint32_t of = stats[s].of_place;
