@@ -450,6 +450,8 @@ __device__ __forceinline__ Acc load_acc(const Acc *p) {
 // With several shares per result, each publishes its accumulator and takes
 // a ticket; the last to arrive merges them in share order (as
 // reduce_finish does), writes the result and sets the ticket back to zero.
+// (Requesting each warp's next 4 KB run into L2 before reading the current
+// one measured slower on B200: config 2's sum 0.58 of HBM against 0.62.)
 template <class T, int MODE>
 __global__ void __launch_bounds__(256) reduce_rows_fast(const typename T::S *in, const FastRows a, typename T::S *out,
                                                         uint32_t *arg_out, Acc *partial, int *tickets) {
