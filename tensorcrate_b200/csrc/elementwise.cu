@@ -71,6 +71,7 @@ __device__ __forceinline__ Pack<T> load_pack(const typename T::S *p) {
 }
 template <class T>
 __device__ __forceinline__ void store_pack(typename T::S *p, const Pack<T> &k) {
+  // (Cache-streaming stores, __stcs, measured no different on config 2.)
   *reinterpret_cast<uint4 *>(p) = k.raw;
 }
 
