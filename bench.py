@@ -634,6 +634,10 @@ def run_trait(args, torch, world, rank, comm):
     measure("pad_16", lambda: N.check("pad", lib.tc_pad(f32, r, c, 16, 16, x.ptr, o1.ptr, sp)),
             4 * (r * c + (r + 32) * (c + 32)))
     measure("flip", lambda: N.check("flip", lib.tc_flip(f32, r, c, x.ptr, o1.ptr, sp)), 2 * 4 * r * c)
+    scalar = cuda.CudaStorage("f32", 1)
+    measure("sgd", lambda: N.check("sgd", lib.tc_sgd(f32, n, o1.ptr, y.ptr, 1e-3, sp)), 3 * 4 * n)
+    measure("dot", lambda: N.check("dot", lib.tc_dot(f32, x.ptr, y.ptr, n, scalar.ptr, sp)), 2 * 4 * n)
+    measure("vector_sum", lambda: N.check("sum", lib.tc_vector_reduce(f32, N.SUM, x.ptr, n, scalar.ptr, sp)), 4 * n)
     mom = cuda.CudaStorage("f32", 2)
     measure("moments", lambda: N.check("moments", lib.tc_moments(f32, x.ptr, n, mom.ptr, sp)), 4 * n)
     rows, cols = 16384, 4096
@@ -692,7 +696,7 @@ def run_trait(args, torch, world, rank, comm):
             "ops": ops, "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.get(k, 1) for k in ops)}
 
 
-LAUNCHES_PER_CALL = {"prefix_sum": 3, "sort": 2, "moments": 2, "axis_moments_rows": 2}
+LAUNCHES_PER_CALL = {"prefix_sum": 3, "sort": 2, "moments": 4, "axis_moments_rows": 1, "dot": 2, "vector_sum": 2}
 
 
 def run_c4(args, torch, world, rank, comm):

@@ -1128,10 +1128,35 @@ int run_reduction(int dtype, uint32_t rank, const size_t *shape, const void *inp
 // Whole-vector fold / dot: per-block partials, then one block folds them.
 template <class T, int F>
 __global__ void __launch_bounds__(256) vector_partials(const typename T::S *a, const typename T::S *b, size_t n,
-                                                       float *partials) {
+                                                       float *partials, bool vec) {
+  // 16-byte packs, U of them (and of b's) in flight per thread; the tail
+  // element by element.  Each thread's order and the block's tree are fixed.
   __shared__ Acc sh[8];
+  constexpr int N = Pack<T>::N, U = 4;
   Acc acc = identity<F>();
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+  const size_t stride = size_t(gridDim.x) * blockDim.x, tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t packs = vec ? n / N : 0;
+  const uint4 *pa = reinterpret_cast<const uint4 *>(a), *pb = reinterpret_cast<const uint4 *>(b);
+  for (size_t p0 = tid; p0 < packs; p0 += stride * U) {
+    Pack<T> x[U], y[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (p0 + u * stride < packs) {
+        x[u].raw = __ldg(pa + p0 + u * stride);
+        if (b) y[u].raw = __ldg(pb + p0 + u * stride);
+      }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (p0 + u * stride < packs) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          float v = T::load(x[u].v[j]);
+          if (b) v = __fmul_rn(v, T::load(y[u].v[j]));
+          push<F>(acc, v, 0);
+        }
+      }
+  }
+  for (size_t i = packs * N + tid; i < n; i += stride) {
     float x = T::load(a[i]);
     if (b) x = __fmul_rn(x, T::load(b[i]));
     push<F>(acc, x, 0);
@@ -1163,15 +1188,20 @@ __global__ void __launch_bounds__(256) vector_finish(const float *partials, int 
 template <int F>
 int vector_fold(int dtype, const void *a, const void *b, size_t n, void *out, cudaStream_t stream) {
   if (!out) return fail(TC_EINVAL, "vector reduce: null output");
-  const int max_blocks = 1024;
+  const int max_blocks = 2048;
   void *p = nullptr;
   if (int st = scratch_get(max_blocks * sizeof(float), &p)) return st;
   float *partials = static_cast<float *>(p);
   return with_real(dtype, [&](auto t) -> int {
     using T = decltype(t);
     using S = typename T::S;
-    int blocks = int(std::min<size_t>(std::max<size_t>((n + 255) / 256, 1), size_t(max_blocks)));
-    vector_partials<T, F><<<blocks, 256, 0, stream>>>(static_cast<const S *>(a), static_cast<const S *>(b), n, partials);
+    constexpr size_t N = size_t(Pack<T>::N);
+    const bool vec = (uintptr_t(a) & 15u) == 0 && (!b || (uintptr_t(b) & 15u) == 0);
+    const size_t units = vec ? (n + N - 1) / N : n;
+    int blocks = int(std::min<size_t>(std::max<size_t>((units + 255) / 256, 1),
+                                      std::min<size_t>(size_t(max_blocks), size_t(sm_count()) * 8)));
+    vector_partials<T, F><<<blocks, 256, 0, stream>>>(static_cast<const S *>(a), static_cast<const S *>(b), n, partials,
+                                                      vec);
     vector_finish<T, F><<<1, 256, 0, stream>>>(partials, blocks, static_cast<S *>(out));
     return check_launch("vector reduce");
   });
