@@ -216,9 +216,30 @@ __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamS
 
 // Sgd: step = g * rate (Builder::scale), p = p - step.
 template <class T>
-__global__ void __launch_bounds__(256) sgd_kernel(typename T::S *p, const typename T::S *g, size_t n, float rate) {
-  size_t stride = size_t(gridDim.x) * blockDim.x;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+__global__ void __launch_bounds__(256) sgd_kernel(typename T::S *p, const typename T::S *g, size_t n, float rate,
+                                                  bool vec) {
+  // 16-byte packs of p and g when both are aligned, the tail (or all of an
+  // unaligned update) element by element; the same operations either way.
+  using S = typename T::S;
+  constexpr int N = 16 / int(sizeof(S));
+  union Pk {
+    uint4 raw;
+    S v[N];
+  };
+  const size_t stride = size_t(gridDim.x) * blockDim.x, tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t packs = vec ? n / N : 0;
+  for (size_t q = tid; q < packs; q += stride) {
+    Pk pp, gg;
+    pp.raw = reinterpret_cast<const uint4 *>(p)[q];
+    gg.raw = __ldg(reinterpret_cast<const uint4 *>(g) + q);
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float step = rnd<T>(__fmul_rn(T::load(gg.v[j]), rate));
+      pp.v[j] = T::store(__fsub_rn(T::load(pp.v[j]), step));
+    }
+    reinterpret_cast<uint4 *>(p)[q] = pp.raw;
+  }
+  for (size_t i = packs * N + tid; i < n; i += stride) {
     float step = rnd<T>(__fmul_rn(T::load(g[i]), rate));
     p[i] = T::store(__fsub_rn(T::load(p[i]), step));
   }
@@ -314,9 +335,10 @@ int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *strea
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     using S = typename T::S;
-    unsigned grid = grid_for(n, 256, 8);
+    const bool vec = aligned16(p) && aligned16(g);
+    unsigned grid = grid_for(vec ? (n + 15 / sizeof(S)) / (16 / sizeof(S)) : n, 256, 8);
     sgd_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<S *>(p), static_cast<const S *>(g), n,
-                                                       float(rate));
+                                                       float(rate), vec);
     return check_launch("sgd");
   });
 }
