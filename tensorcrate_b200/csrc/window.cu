@@ -135,6 +135,28 @@ __global__ void __launch_bounds__(256) pad_kernel(const E *in, E *out, long long
   }
 }
 
+// pad in 16-byte packs: the same rows when the padding, the row length and
+// both buffers are whole packs (element size E, P = 16 / E per pack).
+template <class E>
+__global__ void __launch_bounds__(256) pad_packs(const E *in, E *out, long long rows, long long cols, long long pr,
+                                                 long long pc) {
+  constexpr long long P = 16 / sizeof(E);
+  const long long ocols = cols + 2 * pc, orows = rows + 2 * pr;
+  const long long oq = ocols / P, pq = pc / P, cq = cols / P;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (long long orow = blockIdx.x; orow < orows; orow += gridDim.x) {
+    const long long r = orow - pr;
+    uint4 *dst = reinterpret_cast<uint4 *>(out + orow * ocols);
+    if (r < 0 || r >= rows) {
+      for (long long q = threadIdx.x; q < oq; q += blockDim.x) dst[q] = zero;
+      continue;
+    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(in + r * cols);
+    for (long long q = threadIdx.x; q < oq; q += blockDim.x)
+      dst[q] = (q >= pq && q < pq + cq) ? __ldg(src + (q - pq)) : zero;
+  }
+}
+
 // flip (kernels.rs:1531-1542): out[r][c] = in[rows-1-r][cols-1-c], which is
 // the whole matrix reversed in storage order.
 template <class E>
@@ -212,6 +234,13 @@ int tc_pad(int dtype, size_t rows, size_t cols, size_t pad_rows, size_t pad_cols
   return with_real(dtype, [&](auto t) {
     using S = typename decltype(t)::S;
     const unsigned grid = unsigned(std::min<long long>((long long)(rows + 2 * pad_rows), (long long)sm_count() * 16));
+    constexpr size_t P = 16 / sizeof(S);
+    if ((uintptr_t(input) & 15u) == 0 && (uintptr_t(out) & 15u) == 0 && cols % P == 0 && pad_cols % P == 0) {
+      pad_packs<S><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const S *>(input), static_cast<S *>(out),
+                                                        (long long)rows, (long long)cols, (long long)pad_rows,
+                                                        (long long)pad_cols);
+      return check_launch("pad");
+    }
     pad_kernel<S><<<grid, 256, 0, as_stream(stream)>>>(
         static_cast<const S *>(input), static_cast<S *>(out), (long long)rows, (long long)cols,
         (long long)pad_rows, (long long)pad_cols);

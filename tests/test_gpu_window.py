@@ -100,7 +100,8 @@ def test_correlate_input_gradient_is_the_hosts_bits(device, dtype, ashape, wshap
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("shape,pad", [((2, 2), (1, 1)), ((7, 5), (2, 3)), ((7, 5), (0, 0)), ((0, 4), (2, 1)),
-                                       ((1000, 1000), (3, 9))])
+                                       ((1000, 1000), (3, 9)), ((64, 256), (5, 8)), ((0, 16), (2, 8)),
+                                       ((33, 1024), (0, 16))])
 def test_pad_moves_bits(device, dtype, shape, pad):
     (r, c), (pr, pc) = shape, pad
     x = O.narrow(uniform(max(1, r * c), 7)[: r * c], dtype)
