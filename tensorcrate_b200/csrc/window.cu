@@ -32,38 +32,49 @@ __device__ __forceinline__ long long tap_index(const Window &w, long long wr, lo
   return w.flip ? (w.win_rows - 1 - wr) * w.win_cols + (w.win_cols - 1 - wc) : wr * w.win_cols + wc;
 }
 
-// Four adjacent outputs of a row per thread, each summing its taps in the
+// OUTS adjacent outputs of a row per thread, each summing its taps in the
 // Host's order: for each window row the thread slides a register window of
-// four input values along the row, so a tap costs one input load and one
-// window load for four products (instead of two loads for one).
+// OUTS input values along the row, so a tap costs one input load and one
+// (shared-memory, broadcast) tap read for OUTS products.  The taps are
+// staged in shared memory when they fit (SMEM_TAPS), else read through L1.
+constexpr int OUTS = 8, SMEM_TAPS = 4096;
+
 template <class T>
 __global__ void __launch_bounds__(256) correlate_direct(const typename T::S *in, const typename T::S *win,
                                                         typename T::S *out, Window w) {
-  const long long quads = (w.out_cols + 3) / 4, total = w.out_rows * quads;
+  __shared__ float taps_sh[SMEM_TAPS];
+  const long long taps = w.win_rows * w.win_cols;
+  const bool staged = taps <= SMEM_TAPS;
+  if (staged)
+    for (long long t = threadIdx.x; t < taps; t += blockDim.x) taps_sh[t] = T::load(win[t]);
+  __syncthreads();
+  const long long groups = (w.out_cols + OUTS - 1) / OUTS, total = w.out_rows * groups;
   for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
        o += (long long)gridDim.x * blockDim.x) {
-    const long long row = o / quads, c0 = (o - row * quads) * 4;
-    const int n = int(min(4LL, w.out_cols - c0));
-    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const long long row = o / groups, c0 = (o - row * groups) * OUTS;
+    const int n = int(min((long long)OUTS, w.out_cols - c0));
+    float sum[OUTS];
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j) sum[j] = 0.0f;
     for (long long wr = 0; wr < w.win_rows; ++wr) {
       const typename T::S *x = in + (row + wr) * w.in_cols + c0;
       const long long room = w.in_cols - c0;  // readable elements from x
-      float v[4];
+      float v[OUTS];
 #pragma unroll
-      for (int j = 0; j < 3; ++j) v[j] = j < room ? T::load(__ldg(x + j)) : 0.0f;
+      for (int j = 0; j < OUTS - 1; ++j) v[j] = j < room ? T::load(__ldg(x + j)) : 0.0f;
       for (long long wc = 0; wc < w.win_cols; ++wc) {
-        v[3] = wc + 3 < room ? T::load(__ldg(x + wc + 3)) : 0.0f;
-        const float k = T::load(__ldg(win + tap_index(w, wr, wc)));
+        v[OUTS - 1] = wc + OUTS - 1 < room ? T::load(__ldg(x + wc + OUTS - 1)) : 0.0f;
+        const long long ti = tap_index(w, wr, wc);
+        const float k = staged ? taps_sh[ti] : T::load(__ldg(win + ti));
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < OUTS; ++j)
           if (j < n) sum[j] = __fadd_rn(sum[j], __fmul_rn(v[j], k));
-        v[0] = v[1];
-        v[1] = v[2];
-        v[2] = v[3];
+#pragma unroll
+        for (int j = 0; j < OUTS - 1; ++j) v[j] = v[j + 1];
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < OUTS; ++j)
       if (j < n) out[row * w.out_cols + c0 + j] = T::store(sum[j]);
   }
 }
@@ -175,7 +186,7 @@ int run_correlate(int dtype, const Window &w, const void *in, const void *win, v
       correlate_shared<T><<<grid, 256, 0, s>>>(static_cast<const S *>(in), static_cast<const S *>(win),
                                                static_cast<S *>(out), w);
     } else {
-      correlate_direct<T><<<grid_for((outputs + 3) / 4, 256, 8), 256, 0, s>>>(static_cast<const S *>(in),
+      correlate_direct<T><<<grid_for((outputs + OUTS - 1) / OUTS, 256, 8), 256, 0, s>>>(static_cast<const S *>(in),
                                                                       static_cast<const S *>(win),
                                                                       static_cast<S *>(out), w);
     }
