@@ -186,10 +186,16 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_chunks(const typename T::S 
   __shared__ float warp_sums[32];
   const long long begin = (long long)blockIdx.x * per, end = min(n, begin + per);
   float carry = offsets[blockIdx.x];
+  // The next tile's items are loaded before this tile is scanned, so its
+  // reads are in flight during the scan and the stores.
+  float nv[8];
+  if (begin < end) load_items<T>(a, begin + (long long)threadIdx.x * SCAN_ITEMS, end, vec, nv);
   for (long long t = begin; t < end; t += SCAN_TILE) {
     const long long at = t + (long long)threadIdx.x * SCAN_ITEMS;
     float v[8];
-    load_items<T>(a, at, end, vec, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = nv[j];
+    if (t + SCAN_TILE < end) load_items<T>(a, at + SCAN_TILE, end, vec, nv);
 #pragma unroll
     for (int j = 1; j < 8; ++j) v[j] = __fadd_rn(v[j - 1], v[j]);
     float tile_total;
