@@ -631,6 +631,12 @@ def run_trait(args, torch, world, rank, comm):
     fp32_peak = 148 * 128 * 1.965e9 / 1e12
     measure("correlate_5x5", lambda: N.check("corr", lib.tc_correlate(f32, r, c, 5, 5, 0, x.ptr, w.ptr, o1.ptr, sp)),
             4 * (r * c + out_rc), flops=2 * 25 * out_rc, bound="fp32 (mul + add per tap)", peak=fp32_peak)
+    # the input gradient of that correlation: the 8188x8188 adjoint against
+    # the 5x5 window back to 8192x8192 (each adjoint element meets each tap once)
+    measure("correlate_input_gradient_5x5",
+            lambda: N.check("cig", lib.tc_correlate_input_gradient(f32, r - 4, c - 4, 5, 5, 0, x.ptr, w.ptr, o1.ptr,
+                                                                   sp)),
+            4 * (out_rc + r * c), flops=2 * 25 * out_rc, bound="fp32 (mul + add per tap)", peak=fp32_peak)
     measure("pad_16", lambda: N.check("pad", lib.tc_pad(f32, r, c, 16, 16, x.ptr, o1.ptr, sp)),
             4 * (r * c + (r + 32) * (c + 32)))
     measure("flip", lambda: N.check("flip", lib.tc_flip(f32, r, c, x.ptr, o1.ptr, sp)), 2 * 4 * r * c)

@@ -109,24 +109,52 @@ __global__ void __launch_bounds__(256) correlate_shared(const typename T::S *in,
 
 // The input gradient (kernels.rs:1754-1788): output (p, q) sums adjoint
 // (p-u, q-v) times tap (u, v) over the taps whose adjoint index is in range,
-// in tap order, skipping the rest (they are not added as zeros).
+// in tap order, skipping the rest (they are not added as zeros).  OUTS
+// adjacent outputs of a row per thread: for each window row the thread
+// slides a register window of adjoint values (column q-v) leftwards as v
+// grows, and each output adds a tap only where its column is in range.
 template <class T>
 __global__ void __launch_bounds__(256) correlate_input_gradient_direct(const typename T::S *adj,
                                                                        const typename T::S *win, typename T::S *out,
                                                                        Window w) {
-  const long long total = w.out_rows * w.out_cols;
+  __shared__ float taps_sh[SMEM_TAPS];
+  const long long taps = w.win_rows * w.win_cols;
+  const bool staged = taps <= SMEM_TAPS;
+  if (staged)
+    for (long long t = threadIdx.x; t < taps; t += blockDim.x) taps_sh[t] = T::load(win[t]);
+  __syncthreads();
+  const long long groups = (w.out_cols + OUTS - 1) / OUTS, total = w.out_rows * groups;
   for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
        o += (long long)gridDim.x * blockDim.x) {
-    const long long row = o / w.out_cols, col = o - row * w.out_cols;
-    float sum = 0.0f;
+    const long long row = o / groups, c0 = (o - row * groups) * OUTS;
+    const int n = int(min((long long)OUTS, w.out_cols - c0));
+    float sum[OUTS];
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j) sum[j] = 0.0f;
     const long long wr0 = max(0LL, row - (w.in_rows - 1)), wr1 = min(w.win_rows - 1, row);
-    const long long wc0 = max(0LL, col - (w.in_cols - 1)), wc1 = min(w.win_cols - 1, col);
     for (long long wr = wr0; wr <= wr1; ++wr) {
-      const typename T::S *a = adj + (row - wr) * w.in_cols + col;
-      for (long long wc = wc0; wc <= wc1; ++wc)
-        sum = __fadd_rn(sum, __fmul_rn(T::load(__ldg(a - wc)), T::load(__ldg(win + tap_index(w, wr, wc)))));
+      const typename T::S *a = adj + (row - wr) * w.in_cols;
+      // v[j] holds the adjoint at column c0 + j - wc (0 outside the row)
+      auto at = [&](long long col) { return col >= 0 && col < w.in_cols ? T::load(__ldg(a + col)) : 0.0f; };
+      float v[OUTS];
+#pragma unroll
+      for (int j = 1; j < OUTS; ++j) v[j] = at(c0 + j);
+      for (long long wc = 0; wc < w.win_cols; ++wc) {
+#pragma unroll
+        for (int j = OUTS - 1; j > 0; --j) v[j] = wc ? v[j - 1] : v[j];
+        v[0] = at(c0 - wc);
+        const long long ti = tap_index(w, wr, wc);
+        const float k = staged ? taps_sh[ti] : T::load(__ldg(win + ti));
+#pragma unroll
+        for (int j = 0; j < OUTS; ++j) {
+          const long long col = c0 + j - wc;
+          if (j < n && col >= 0 && col < w.in_cols) sum[j] = __fadd_rn(sum[j], __fmul_rn(v[j], k));
+        }
+      }
     }
-    out[o] = T::store(sum);
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j)
+      if (j < n) out[row * w.out_cols + c0 + j] = T::store(sum[j]);
   }
 }
 
@@ -231,7 +259,8 @@ int tc_correlate_input_gradient(int dtype, size_t adjoint_rows, size_t adjoint_c
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     using S = typename T::S;
-    correlate_input_gradient_direct<T><<<grid_for(w.out_rows * w.out_cols, 256, 8), 256, 0, as_stream(stream)>>>(
+    correlate_input_gradient_direct<T><<<grid_for(w.out_rows * ((w.out_cols + OUTS - 1) / OUTS), 256, 8), 256, 0,
+                                         as_stream(stream)>>>(
         static_cast<const S *>(adjoint), static_cast<const S *>(window), static_cast<S *>(out), w);
     return check_launch("correlate_input_gradient");
   });
