@@ -1,29 +1,49 @@
 """Benchmark of the tensorcrate CUDA backend's hot path on B200.
 
-Default workload ("config 2", the headline benchmark's configuration): one step is the
-nine broadcast and reduction calls the reference's config names, on f32
-x[64,512,1024] ~ N(0,1) and bias[1,1,1024] ~ N(0,1):
+One JSON line.  Its headline (`value`) is config 2, the configuration the
+reference's broadcast + axis-reduction path is quoted on: one step is the
+nine calls that config names, on f32 x[64,512,1024] ~ N(0,1) and
+bias[1,1,1024] ~ N(0,1):
     x + bias, x * bias, x > bias          (Kernels::strided_binary)
     sum, mean, var over axis 2           (Kernels::reduce_axes)
     max, min over axes (0, 2)            (Kernels::reduce_axes)
     argmax over axis 1                   (Kernels::arg_reduce)
 metric: HBM GB/s = algorithmic bytes of the nine calls / step time.
 
-Under torchrun each rank holds its own [64,512,1024] slab of a
-[64*P,512,1024] tensor (weak scaling): the per-slab results are final
-locally and are all-gathered; max/min over (0,2) reduce across the sharded
-axis, so their [512] partials are all-reduced (NCCL).
+The same line carries the other configurations as sub-records, each with
+its own timing, clocks, roofline, end-to-end figure and parity check:
+  c4  the MLP training step (1024-4096-4096-1024, bf16, Adam), steps/s;
+  c5  the bf16 GEMM, M=N=K=8192, TFLOP/s;
+  c1  the f32 GEMM 1024^3 and matvec;
+  c3  the f16 layout copies (permute, slice-split-concatenate).
 
-Other workloads (--workload): c1 (f32 1024^3 GEMM + matvec), c3 (f16 layout
-copies), c4 (MLP training step), c5 (bf16 GEMM, --size), trait (the other
-Kernels<T> methods, each timed alone).  --impl reference times the reference's
-Host path restated in C++ (oracle/) on the host cores.
+Under torchrun (one process per GPU, NCCL):
+  c2  each rank owns its own [64,512,1024] slab of a [64*P,512,1024] tensor
+      (weak scaling); the per-slab results are all-gathered and the [512]
+      max/min partials folded over ranks;
+  c4  data parallel over the global batch of 2048 (strong scaling), the
+      optimizer sharded over the ranks (reduce-scatter, Adam on 1/P,
+      all-gather);
+  c5  row panels: rank r computes rows [r*M/P, (r+1)*M/P) of C and the GEMM
+      epilogue stores every tile into every rank's C over NVLink (strong);
+  c1, c3  replicas (each rank its own copy of the work).
+
+Timing: W warm-up steps, then blocks of K timed steps (CUDA events on the
+launching stream, max over ranks) repeated until at least --min-seconds of
+device time has passed; ms_per_step is the median block's, with the spread.
+Every sub-record checks its results against the oracle (the reference's
+Host path restated in C++) outside the timed region and reports "parity".
+
+--workload c1|c2|c3|c4|c5|trait runs one workload alone as the headline.
+--impl reference times the reference's Host path restated in C++ (oracle/)
+on the host cores.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes as C
 import json
+import math
 import os
 import statistics
 import sys
@@ -38,6 +58,7 @@ sys.path.insert(0, str(ROOT))
 
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+ORACLE_FLAGS = "g++ -O3 -ffp-contract=off -fno-fast-math (oracle/Makefile), AVX2/FMA dispatched at run time"
 
 
 def traffic(workload: str, kernel: str):
@@ -125,11 +146,181 @@ def dist_env():
     return world, rank, local
 
 
+def barrier(torch, world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(torch, world, v):
+    """Max over ranks of a float or a list of floats."""
+    if world == 1:
+        return v
+    t = torch.tensor(v if isinstance(v, list) else [v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    out = [float(a) for a in t.cpu().tolist()]
+    return out if isinstance(v, list) else out[0]
+
+
+def sum_over_ranks(torch, world, v: int) -> int:
+    if world == 1:
+        return int(v)
+    t = torch.tensor([int(v)], dtype=torch.int64, device="cuda")
+    torch.distributed.all_reduce(t)
+    return int(t.item())
+
+
+def init_comm(torch, world, rank):
+    """NCCL communicator of the library, bootstrapped over torch.distributed."""
+    from tensorcrate_b200.sharding import nccl_comm
+    return nccl_comm(torch, world, rank)
+
+
+def timed(torch, world, fn, args, stream):
+    """W warm-up calls of fn, then blocks of K timed calls (CUDA events on
+    `stream`) until at least args.min_seconds of device time has passed
+    (at least 3 blocks), bracketed by a barrier and a synchronize.  Each
+    block's time is the max over ranks.  Returns (ms per step of the median
+    block, {blocks, spread, seconds}, clocks summary)."""
+    steps = args.steps
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    blocks = []
+    n_blocks = None
+    with Clocks(torch.cuda.current_device()) as clocks:
+        barrier(torch, world)
+        torch.cuda.synchronize()
+        while n_blocks is None or len(blocks) < n_blocks:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            blocks.append(e0.elapsed_time(e1))
+            if n_blocks is None:
+                first = max_over_ranks(torch, world, blocks[0])
+                n_blocks = max(3, math.ceil(args.min_seconds * 1e3 / max(first, 1e-3)))
+        torch.cuda.synchronize()
+        barrier(torch, world)
+    blocks = max_over_ranks(torch, world, blocks)
+    per_step = sorted(b / steps for b in blocks)
+    med = statistics.median(per_step)
+    info = {"blocks": len(blocks), "steps_per_block": steps, "seconds": round(sum(blocks) / 1e3, 3),
+            "ms_per_step_min": round(per_step[0], 5), "ms_per_step_max": round(per_step[-1], 5),
+            "spread": round((per_step[-1] - per_step[0]) / med, 4)}
+    return med, info, clocks.summary()
+
+
+def pinned(torch, nbytes: int):
+    return torch.empty(max(1, nbytes), dtype=torch.uint8).pin_memory()
+
+
+class Pipeline:
+    """End-to-end steps as a streaming caller runs them through the C ABI
+    with host buffers: every step uploads its inputs from pinned host memory,
+    runs, and reads its results back into pinned host memory.  Two device
+    sets of inputs and results: step k+1's uploads (copy stream) and step
+    k-1's read-backs (a second copy stream) overlap step k's kernels.  Each
+    upload waits for the kernels that last read its buffers; each step waits
+    for its uploads and for the read-back of the results it overwrites."""
+
+    def __init__(self, torch, lib, stream, uploads, readbacks, run):
+        # uploads: [(host pinned tensor, [dev ptr set 0, set 1], nbytes)]
+        # readbacks: [([dev ptr set 0, set 1], host pinned tensor, nbytes)]
+        # run(b, stream pointer): enqueue the step on input/result set b
+        self.torch, self.lib, self.stream = torch, lib, stream
+        self.uploads, self.readbacks, self.run = uploads, readbacks, run
+        self.up, self.down = torch.cuda.Stream(), torch.cuda.Stream()
+        self.copied = [torch.cuda.Event(), torch.cuda.Event()]
+        self.computed = [torch.cuda.Event(), torch.cuda.Event()]
+        self.drained = [torch.cuda.Event(), torch.cuda.Event()]
+        self.h2d = sum(n for _, _, n in uploads)
+        self.d2h = sum(n for _, _, n in readbacks)
+
+    def _upload(self, k):
+        from tensorcrate_b200 import _native as N
+        b = k % 2
+        if k >= 2:
+            self.up.wait_event(self.computed[b])
+        usp = C.c_void_p(self.up.cuda_stream)
+        for host, dev, n in self.uploads:
+            N.check("h2d", self.lib.tc_memcpy_h2d(dev[b], host.data_ptr(), n, usp))
+        self.copied[b].record(self.up)
+
+    def steps(self, count):
+        from tensorcrate_b200 import _native as N
+        sp = C.c_void_p(self.stream.cuda_stream)
+        dsp = C.c_void_p(self.down.cuda_stream)
+        self.up.wait_stream(self.stream)
+        self.down.wait_stream(self.stream)
+        self._upload(0)
+        for k in range(count):
+            b = k % 2
+            if k + 1 < count:
+                self._upload(k + 1)
+            self.stream.wait_event(self.copied[b])
+            if k >= 2:
+                self.stream.wait_event(self.drained[b])
+            self.run(b, sp)
+            self.computed[b].record(self.stream)
+            self.down.wait_event(self.computed[b])
+            for dev, host, n in self.readbacks:
+                N.check("d2h", self.lib.tc_memcpy_d2h(host.data_ptr(), dev[b], n, dsp))
+            self.drained[b].record(self.down)
+        self.stream.wait_stream(self.down)
+        self.stream.wait_stream(self.up)
+
+    def measure(self, world, steps):
+        """ms per end-to-end step, pipelined (max over ranks)."""
+        torch = self.torch
+        self.steps(2)
+        torch.cuda.synchronize()
+        barrier(torch, world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        self.steps(steps)
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(torch, world, e0.elapsed_time(e1) / steps)
+
+    def measure_serial(self, world, steps):
+        """ms per end-to-end step with uploads, kernels and read-backs in
+        turn on one stream (input/result set 0)."""
+        from tensorcrate_b200 import _native as N
+        torch = self.torch
+        sp = C.c_void_p(self.stream.cuda_stream)
+
+        def one():
+            for host, dev, n in self.uploads:
+                N.check("h2d", self.lib.tc_memcpy_h2d(dev[0], host.data_ptr(), n, sp))
+            self.run(0, sp)
+            for dev, host, n in self.readbacks:
+                N.check("d2h", self.lib.tc_memcpy_d2h(host.data_ptr(), dev[0], n, sp))
+        one()
+        torch.cuda.synchronize()
+        barrier(torch, world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for _ in range(steps):
+            one()
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(torch, world, e0.elapsed_time(e1) / steps)
+
+
+def parity_record(torch, world, failures: list[str], checked: str) -> dict | str:
+    """'ok', or the number of failures over all ranks and this rank's first."""
+    total = sum_over_ranks(torch, world, len(failures))
+    if total == 0:
+        return {"status": "ok", "checked": checked}
+    return {"status": "failed", "failures": total, "first_on_this_rank": failures[:1], "checked": checked}
+
+
 # ---------------------------------------------------------------------------
-# config 2 on the GPU
+# config 2
 # ---------------------------------------------------------------------------
 SHAPE2 = [64, 512, 1024]
-MB = 1e6
 
 
 def c2_ops_bytes():
@@ -143,6 +334,17 @@ def c2_ops_bytes():
     }
 
 
+def c2_slab(rank: int) -> np.ndarray:
+    """Rank `rank`'s [64,512,1024] slab of the global config-2 tensor."""
+    return np.random.default_rng(1 + rank).standard_normal(int(np.prod(SHAPE2)), dtype=np.float32)
+
+
+C2_BIAS_SEED = 2
+C2_FIELDS = [("sum", "f32", SHAPE2[0] * SHAPE2[1]), ("mean", "f32", SHAPE2[0] * SHAPE2[1]),
+             ("var", "f32", SHAPE2[0] * SHAPE2[1]), ("argmax", "u32", SHAPE2[0] * SHAPE2[2]),
+             ("max", "f32", 512), ("min", "f32", 512)]
+
+
 def run_c2(args, torch, world, rank, comm):
     from tensorcrate_b200 import _native as N
     from tensorcrate_b200 import cuda
@@ -152,72 +354,77 @@ def run_c2(args, torch, world, rank, comm):
     sp = C.c_void_p(stream.cuda_stream)
     shape = SHAPE2
     n = int(np.prod(shape))
-    rng = np.random.default_rng(1 + rank)
-    x_host = rng.standard_normal(n, dtype=np.float32)
-    bias_host = np.random.default_rng(2).standard_normal(1024, dtype=np.float32)
-    x = cuda.CudaStorage.store(x_host, "f32")
-    bias = cuda.CudaStorage.store(bias_host, "f32")
-    rows = shape[0] * shape[1]
-    outs = {k: cuda.CudaStorage("f32", n) for k in ("add", "mul", "greater")}
-    # The reductions' results sit side by side in one block of 4-byte
-    # elements, so that one all-gather carries all of them when P > 1.
-    fields = [("sum", "f32", rows), ("mean", "f32", rows), ("var", "f32", rows),
-              ("argmax", "u32", shape[0] * shape[2]), ("max", "f32", 512), ("min", "f32", 512)]
-    pack_len = sum(c for _, _, c in fields)
-    pack = cuda.CudaStorage("u32", pack_len)
-    at = {}
-    offset = 0
-    for k, dt, count in fields:
-        outs[k] = cuda.CudaStorage(dt, count, ptr=pack.ptr + 4 * offset)
+    x_host = c2_slab(rank)
+    bias_host = np.random.default_rng(C2_BIAS_SEED).standard_normal(1024, dtype=np.float32)
+    xs_dev = [cuda.CudaStorage.store(x_host, "f32"), cuda.CudaStorage("f32", n)]
+    biases = [cuda.CudaStorage.store(bias_host, "f32"), cuda.CudaStorage.store(bias_host, "f32")]
+    pack_len = sum(c for _, _, c in C2_FIELDS)
+    at, offset = {}, 0
+    for k, _, count in C2_FIELDS:
         at[k] = offset
         offset += count
 
+    def result_set():
+        # The reductions' results sit side by side in one block of 4-byte
+        # elements, so that one all-gather carries all of them when P > 1.
+        outs = {k: cuda.CudaStorage("f32", n) for k in ("add", "mul", "greater")}
+        pack = cuda.CudaStorage("u32", pack_len)
+        for k, dt, count in C2_FIELDS:
+            outs[k] = cuda.CudaStorage(dt, count, ptr=pack.ptr + 4 * at[k])
+        outs["pack"] = pack
+        if world > 1:
+            outs["gathered"] = cuda.CudaStorage("u32", pack_len * world)
+            outs["final_max"] = cuda.CudaStorage("f32", 512)
+            outs["final_min"] = cuda.CudaStorage("f32", 512)
+        return outs
+
+    sets = [result_set(), result_set()]
     sz = N.sizes
     xs, xst = sz(shape), sz(cuda.contiguous_strides(shape))
     bst = sz([0, 0, 1])
     ax2, ax02 = N.u32s([2]), N.u32s([0, 2])
-    argp = C.cast(C.c_void_p(outs["argmax"].ptr), C.POINTER(C.c_uint32))
+    g_shape, g_strides = sz([world, 512]), sz([pack_len, 1])
 
-    def calls_on(x):
-        """The nine calls of a step on the input at `x`."""
+    def calls_on(b, sp):
+        """The nine calls of a step on input set b into result set b."""
+        x, o, bias = xs_dev[b], sets[b], biases[b]
+        argp = C.cast(C.c_void_p(o["argmax"].ptr), C.POINTER(C.c_uint32))
         return [
-            ("add", lib.tc_strided_binary, (0, N.PAIR_ARITHMETIC, N.ADD, 3, xs, x.ptr, n, 0, xst, bias.ptr, 1024, 0, bst,
-                                            outs["add"].ptr, sp)),
-            ("mul", lib.tc_strided_binary, (0, N.PAIR_ARITHMETIC, N.MUL, 3, xs, x.ptr, n, 0, xst, bias.ptr, 1024, 0, bst,
-                                            outs["mul"].ptr, sp)),
-            ("greater", lib.tc_strided_binary, (0, N.PAIR_COMPARE, N.GREATER, 3, xs, x.ptr, n, 0, xst, bias.ptr, 1024, 0,
-                                                bst, outs["greater"].ptr, sp)),
-            ("sum", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 1, ax2, N.AXIS_FOLD, N.SUM, 0, outs["sum"].ptr, sp)),
-            ("mean", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 1, ax2, N.AXIS_MEAN, 0, 0, outs["mean"].ptr, sp)),
-            ("var", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 1, ax2, N.AXIS_VARIANCE, 0, 1024, outs["var"].ptr,
+            ("add", lib.tc_strided_binary, (0, N.PAIR_ARITHMETIC, N.ADD, 3, xs, x.ptr, n, 0, xst, bias.ptr, 1024, 0,
+                                            bst, o["add"].ptr, sp)),
+            ("mul", lib.tc_strided_binary, (0, N.PAIR_ARITHMETIC, N.MUL, 3, xs, x.ptr, n, 0, xst, bias.ptr, 1024, 0,
+                                            bst, o["mul"].ptr, sp)),
+            ("greater", lib.tc_strided_binary, (0, N.PAIR_COMPARE, N.GREATER, 3, xs, x.ptr, n, 0, xst, bias.ptr, 1024,
+                                                0, bst, o["greater"].ptr, sp)),
+            ("sum", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 1, ax2, N.AXIS_FOLD, N.SUM, 0, o["sum"].ptr, sp)),
+            ("mean", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 1, ax2, N.AXIS_MEAN, 0, 0, o["mean"].ptr, sp)),
+            ("var", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 1, ax2, N.AXIS_VARIANCE, 0, 1024, o["var"].ptr,
                                          sp)),
-            ("max", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 2, ax02, N.AXIS_FOLD, N.RMAX, 0, outs["max"].ptr, sp)),
-            ("min", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 2, ax02, N.AXIS_FOLD, N.RMIN, 0, outs["min"].ptr, sp)),
+            ("max", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 2, ax02, N.AXIS_FOLD, N.RMAX, 0, o["max"].ptr,
+                                         sp)),
+            ("min", lib.tc_reduce_axes, (0, 3, xs, x.ptr, n, 0, xst, 2, ax02, N.AXIS_FOLD, N.RMIN, 0, o["min"].ptr,
+                                         sp)),
             ("argmax", lib.tc_arg_reduce, (0, 3, xs, x.ptr, n, 0, xst, 1, N.RMAX, argp, sp)),
         ]
 
-    calls = calls_on(x)
-
-    # Collectives for P > 1: one all-gather of every rank's block of results
-    # (the slab results are then final, rank after rank); the [512] extremes
-    # fold the sharded leading axis, so each is finished by reducing the P
-    # gathered partials ([P, 512] with a stride of one block), exactly.
-    gathered = cuda.CudaStorage("u32", pack_len * world) if world > 1 else None
-    finals = {k: cuda.CudaStorage("f32", 512) for k in ("max", "min")} if world > 1 else {}
-    g_shape, g_strides = sz([world, 512]), sz([pack_len, 1])
-
-    def collectives():
+    def collectives(o, sp):
+        # P > 1: one all-gather of every rank's block of results (the slab
+        # results are then final, rank after rank); the [512] extremes fold
+        # the sharded leading axis, so each is finished by reducing the P
+        # gathered partials ([P, 512] with a stride of one block), exactly.
         if world == 1:
             return
-        N.check("allgather", lib.tc_allgather(comm, N.U32, pack.ptr, gathered.ptr, pack_len, sp))
+        N.check("allgather", lib.tc_allgather(comm, N.U32, o["pack"].ptr, o["gathered"].ptr, pack_len, sp))
         for k, op in (("max", N.RMAX), ("min", N.RMIN)):
-            N.check("fold", lib.tc_reduce_axes(0, 2, g_shape, gathered.ptr, pack_len * world, at[k], g_strides, 1,
-                                               N.u32s([0]), N.AXIS_FOLD, op, 0, finals[k].ptr, sp))
+            N.check("fold", lib.tc_reduce_axes(0, 2, g_shape, o["gathered"].ptr, pack_len * world, at[k], g_strides,
+                                               1, N.u32s([0]), N.AXIS_FOLD, op, 0, o["final_" + k].ptr, sp))
 
-    events = {name: [] for name, _, _ in calls}
+    calls = [calls_on(0, sp), calls_on(1, sp)]
+    events = {name: [] for name, _, _ in calls[0]}
 
-    def step(record=False, on=None):
-        for name, fn, a in (on or calls):
+    def step(b=0, record=False, on_sp=None):
+        todo = calls[b] if on_sp is None else calls_on(b, on_sp)
+        for name, fn, a in todo:
             if record:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
@@ -228,28 +435,11 @@ def run_c2(args, torch, world, rank, comm):
                 st = fn(*a)
             if st:
                 N.check(name, st)
-        collectives()
+        collectives(sets[b], sp if on_sp is None else on_sp)
 
     bytes_per_op = c2_ops_bytes()
     step_bytes = sum(bytes_per_op.values())
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-
-    # device-timed region
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(torch.cuda.current_device()) as clocks:
-        barrier(torch, world)
-        torch.cuda.synchronize()
-        t0.record(stream)
-        for _ in range(args.steps):
-            step()
-        t1.record(stream)
-        torch.cuda.synchronize()
-        barrier(torch, world)
-    ms = t0.elapsed_time(t1)
-    ms = max_over_ranks(torch, world, ms)
+    ms_per_step, blocks, clocks = timed(torch, world, step, args, stream)
     # Per-operation times, from events around each call, in a pass of their
     # own (events between the calls would sit inside the timed region).
     for _ in range(min(args.steps, 50)):
@@ -257,76 +447,28 @@ def run_c2(args, torch, world, rank, comm):
     torch.cuda.synchronize()
     per_op_ms = {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in events.items()}
 
-    # e2e: through the public API with host buffers (pinned), copies inside.
-    pinned_x = torch.from_numpy(x_host).pin_memory()
-    pinned_b = torch.from_numpy(bias_host).pin_memory()
-    out_host = {k: torch.empty(o.nbytes, dtype=torch.uint8).pin_memory() for k, o in outs.items()
-                if k not in ("add", "mul", "greater")}
-    h2d = pinned_x.numel() * 4 + pinned_b.numel() * 4
-    d2h = sum(v.numel() for v in out_host.values())
+    # ---- parity against the oracle, outside the timed region ----
+    failures = parity_c2(torch, world, rank, x_host, bias_host, sets[0], at, pack_len, failures=[])
+    parity = parity_record(torch, world, failures,
+                           "sampled rows of add/mul/greater (bit-exact), sum/mean/var (rel 1e-5*sqrt(K)) and argmax "
+                           "(bit-exact) of this rank's slab and of the next rank's slab as gathered here; max/min over "
+                           "(0,2) of the whole tensor (bit-exact), against oracle/ on the same seeded input")
 
-    def e2e_step():
-        N.check("h2d", lib.tc_memcpy_h2d(x.ptr, pinned_x.data_ptr(), pinned_x.numel() * 4, sp))
-        N.check("h2d", lib.tc_memcpy_h2d(bias.ptr, pinned_b.data_ptr(), pinned_b.numel() * 4, sp))
-        step()
-        for k, h in out_host.items():
-            N.check("d2h", lib.tc_memcpy_d2h(h.data_ptr(), outs[k].ptr, h.numel(), sp))
+    # ---- end to end: host buffers through the C ABI, every result read back ----
+    h_x, h_b = pinned(torch, n * 4), pinned(torch, 4096)
+    h_x.numpy().view(np.float32)[:] = x_host
+    h_b.numpy().view(np.float32)[:] = bias_host
+    read_keys = [("add", n * 4), ("mul", n * 4), ("greater", n * 4), ("pack", pack_len * 4)]
+    hosts = {k: pinned(torch, nb) for k, nb in read_keys}
+    pipe = Pipeline(torch, lib, stream,
+                    uploads=[(h_x, [xs_dev[0].ptr, xs_dev[1].ptr], n * 4),
+                             (h_b, [biases[0].ptr, biases[1].ptr], 4096)],
+                    readbacks=[([sets[0][k].ptr, sets[1][k].ptr], hosts[k], nb) for k, nb in read_keys],
+                    run=lambda b, s: step(b, on_sp=s))
+    e2e_steps = max(5, args.steps // 2)
+    e2e_ms = pipe.measure(world, e2e_steps)
+    serial_ms = pipe.measure_serial(world, max(3, e2e_steps // 2))
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(torch, world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    e2e_steps = max(3, args.steps // 4)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    serial_ms = max_over_ranks(torch, world, e0.elapsed_time(e1) / e2e_steps)
-
-    # The same steps as a streaming caller runs them: two device copies of
-    # the input, step k+1's upload on a copy stream while step k's kernels
-    # run (each upload waits for the step that last read its buffer; each
-    # step waits for its own upload).  Every step still uploads its input
-    # and reads its results back inside the timed region.
-    x2 = cuda.CudaStorage("f32", n)
-    bufs, on = [x, x2], [calls, calls_on(x2)]
-    copy_stream = torch.cuda.Stream()
-    csp = C.c_void_p(copy_stream.cuda_stream)
-    copied = [torch.cuda.Event(), torch.cuda.Event()]
-    consumed = [torch.cuda.Event(), torch.cuda.Event()]
-
-    def upload(k):
-        b = k % 2
-        if k >= 2:
-            copy_stream.wait_event(consumed[b])
-        N.check("h2d", lib.tc_memcpy_h2d(bufs[b].ptr, pinned_x.data_ptr(), pinned_x.numel() * 4, csp))
-        copied[b].record(copy_stream)
-
-    def pipelined(steps):
-        copy_stream.wait_stream(stream)
-        upload(0)
-        for k in range(steps):
-            if k + 1 < steps:
-                upload(k + 1)
-            stream.wait_event(copied[k % 2])
-            N.check("h2d", lib.tc_memcpy_h2d(bias.ptr, pinned_b.data_ptr(), pinned_b.numel() * 4, sp))
-            step(on=on[k % 2])
-            consumed[k % 2].record(stream)
-            for kk, h in out_host.items():
-                N.check("d2h", lib.tc_memcpy_d2h(h.data_ptr(), outs[kk].ptr, h.numel(), sp))
-
-    pipelined(2)
-    torch.cuda.synchronize()
-    barrier(torch, world)
-    e0.record(stream)
-    pipelined(e2e_steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(torch, world, e0.elapsed_time(e1) / e2e_steps)
-
-    ms_per_step = ms / args.steps
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
     # Dominant kernel: the largest share of the step.
     dom = max(per_op_ms, key=lambda k: per_op_ms[k])
@@ -334,7 +476,8 @@ def run_c2(args, torch, world, rank, comm):
     achieved = bytes_per_op[dom] / (per_op_ms[dom] * 1e-3) / 1e9
     ops = {k: {"ms": round(v, 5), "gbs": round(bytes_per_op[k] / (v * 1e-3) / 1e9, 1),
                "frac": round(bytes_per_op[k] / (v * 1e-3) / 1e9 / pk["hbm_gbs"], 3)} for k, v in per_op_ms.items()}
-    line = {
+    launches = len(calls[0]) + (2 if world > 1 else 0)
+    return {
         "metric": "config-2 broadcast + axis-reduction HBM throughput (GB/s)",
         "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -342,29 +485,93 @@ def run_c2(args, torch, world, rank, comm):
         "config": {"workload": "config2: f32 x[64,512,1024] with bias[1,1,1024]: add, mul, greater; sum/mean/var ax2; "
                                "max/min ax(0,2); argmax ax1",
                    "per_rank_shape": SHAPE2, "global_shape": [64 * world, 512, 1024],
-                   "parallelism": f"leading-axis shards x{world}" + (" (one NCCL all-gather of every result, "
-                                                                     "then max/min folded over ranks)" if world > 1
-                                                                     else ""),
+                   "parallelism": f"leading-axis shards x{world}" + (" (one NCCL all-gather of every result, then "
+                                                                     "max/min folded over ranks)" if world > 1 else ""),
                    "l2": "no flush: every call reads the 134.2 MB input, larger than the 126 MB L2",
                    "algorithmic_bytes_per_step": step_bytes},
+        "timing": blocks,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                      "peak_source": pk_kind, "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 3),
                      "traffic": traffic("c2", dom), "algorithmic_bytes": bytes_per_op[dom]},
         "ops": ops,
         "e2e": {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "pipelined": "each step's input upload overlaps the previous step's kernels (two device buffers, "
-                             "a copy stream)",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": pipe.h2d, "d2h_bytes_per_step": pipe.d2h,
+                "reads_back": "all nine results: the three [64,512,1024] broadcast outputs and the six reductions' "
+                              "block, every step",
+                "pipelined": "step k+1's upload and step k-1's read-back overlap step k's kernels (two device sets "
+                             "of inputs and results, one copy stream each way)",
                 "serial_ms_per_step": round(serial_ms, 4)},
-        "gpu_launches": (len(calls) + (2 if world > 1 else 0)) * args.steps,
-        "clocks": clocks.summary(),
+        "parity": parity,
+        "gpu_launches_per_step": launches,
+        "gpu_launches": launches * args.steps * blocks["blocks"],
+        "clocks": clocks,
     }
-    return line
 
 
-# ---------------------------------------------------------------------------
-# CPU: the reference's Host path (oracle restatement) on a bounded sample
-# ---------------------------------------------------------------------------
+def parity_c2(torch, world, rank, x_host, bias_host, o, at, pack_len, failures):
+    """Config 2's results against the oracle on sampled leading rows of this
+    rank's slab and, when sharded, of the next rank's slab as the all-gather
+    delivered it here; the max/min over (0,2) of the whole global tensor."""
+    import oracle as O
+    from tensorcrate_b200 import _native as N
+    lib = N.lib()
+    torch.cuda.synchronize()
+    rows = [0, 37, 63]
+    st = [512 * 1024, 1024, 1]
+    sub_shape = [len(rows), 512, 1024]
+    slab = x_host.reshape(SHAPE2)
+
+    def tol_ok(got, want, k):
+        return bool(np.all(np.abs(got - want) <= 1e-5 * np.sqrt(k) * (np.abs(want) + 1.0)))
+
+    def check_reductions(sub, pack, who):
+        want = {"sum": O.reduce_axes("f32", sub_shape, sub, 0, st, [2], N.AXIS_FOLD, N.SUM, 0),
+                "mean": O.reduce_axes("f32", sub_shape, sub, 0, st, [2], N.AXIS_MEAN, 0, 0),
+                "var": O.reduce_axes("f32", sub_shape, sub, 0, st, [2], N.AXIS_VARIANCE, 0, 1024)}
+        for k, w in want.items():
+            got = np.concatenate([pack[at[k] + r * 512: at[k] + (r + 1) * 512].view(np.float32) for r in rows])
+            if not tol_ok(got, w, 1024):
+                failures.append(f"{who}: {k} differs from the oracle")
+        arg = O.arg_reduce("f32", sub_shape, sub, 0, st, 1, N.RMAX)
+        got = np.concatenate([pack[at["argmax"] + r * 1024: at["argmax"] + (r + 1) * 1024] for r in rows])
+        if not np.array_equal(got, arg):
+            failures.append(f"{who}: argmax differs from the oracle")
+
+    sub = np.ascontiguousarray(slab[rows]).reshape(-1)
+    pack = o["pack"].as_slice()
+    check_reductions(sub, pack, f"rank {rank}")
+    for k, kind, op in (("add", 0, N.ADD), ("mul", 0, N.MUL), ("greater", 1, N.GREATER)):
+        want = O.strided_binary("f32", kind, op, sub_shape, sub, 0, st, bias_host, 0, [0, 0, 1])
+        got = np.empty(len(rows) * 512 * 1024, np.float32)
+        for i, r in enumerate(rows):
+            N.check("d2h", lib.tc_memcpy_d2h(got[i * 512 * 1024:].ctypes.data, o[k].ptr + r * 512 * 1024 * 4,
+                                             512 * 1024 * 4, None))
+        if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
+            failures.append(f"rank {rank}: {k} differs from the oracle")
+    # max/min over (0, 2): this slab's partial by the oracle, folded over
+    # every rank's partial (exact), against the result every rank holds.
+    part = {k: O.reduce_axes("f32", SHAPE2, x_host, 0, st, [0, 2], N.AXIS_FOLD, op, 0)
+            for k, op in (("max", N.RMAX), ("min", N.RMIN))}
+    if world > 1:
+        gathered = o["gathered"].as_slice()
+        nxt = (rank + 1) % world
+        nsub = np.ascontiguousarray(c2_slab(nxt).reshape(SHAPE2)[rows]).reshape(-1)
+        check_reductions(nsub, gathered[nxt * pack_len:(nxt + 1) * pack_len], f"rank {nxt}'s slab on rank {rank}")
+        for k in ("max", "min"):
+            t = torch.tensor(part[k], device="cuda")
+            every = [torch.empty_like(t) for _ in range(world)]
+            torch.distributed.all_gather(every, t)
+            stacked = np.stack([e.cpu().numpy() for e in every])
+            want = stacked.max(axis=0) if k == "max" else stacked.min(axis=0)
+            if not np.array_equal(o["final_" + k].as_slice(), want):
+                failures.append(f"rank {rank}: global {k} differs from the oracle")
+    else:
+        for k in ("max", "min"):
+            if not np.array_equal(pack[at[k]:at[k] + 512].view(np.float32), part[k]):
+                failures.append(f"rank {rank}: {k} differs from the oracle")
+    return failures
+
+
 def cpu_c2(sample_rows: int = 16, reps: int = 1):
     import oracle as O
 
@@ -373,6 +580,7 @@ def cpu_c2(sample_rows: int = 16, reps: int = 1):
     x = np.random.default_rng(1).standard_normal(n, dtype=np.float32)
     bias = np.random.default_rng(2).standard_normal(1024, dtype=np.float32)
     st = [512 * 1024, 1024, 1]
+    O.set_matmul_threads(1)
     t = time.perf_counter()
     for _ in range(reps):
         O.strided_binary("f32", 0, 0, shape, x, 0, st, bias, 0, [0, 0, 1])
@@ -389,32 +597,18 @@ def cpu_c2(sample_rows: int = 16, reps: int = 1):
     step_bytes = sum(c2_ops_bytes().values()) * scale
     return {"value": round(step_bytes / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
             "sample": f"all nine calls on a [{sample_rows},512,1024] slab ({scale:.3g} of config 2), x{reps}, "
-                      "single-threaded as the Host runs strided kernels",
-            "seconds": round(dt * reps, 2)}
+                      "single-threaded: the Host runs strided binaries and axis reductions on one thread "
+                      "(src/parallel.rs:12-14), so one core is all this path can use",
+            "build": ORACLE_FLAGS, "seconds": round(dt * reps, 2), "host_cores": os.cpu_count()}
 
 
-def timed(torch, world, fn, steps, warmup, stream, per_call=None):
-    """Run fn warmup times, then time `steps` calls with CUDA events on
-    `stream` (max over ranks).  Returns (ms per step, clocks summary)."""
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(torch.cuda.current_device()) as clocks:
-        barrier(torch, world)
-        torch.cuda.synchronize()
-        t0.record(stream)
-        for _ in range(steps):
-            fn()
-        t1.record(stream)
-        torch.cuda.synchronize()
-        barrier(torch, world)
-    return max_over_ranks(torch, world, t0.elapsed_time(t1)) / steps, clocks.summary()
-
-
+# ---------------------------------------------------------------------------
+# GEMMs: config 5 (bf16) and config 1 (f32)
+# ---------------------------------------------------------------------------
 def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
     """Config 5 (bf16, M=N=K=size) or config 1 (f32 1024^3): C = A.B through
-    tc_matmul, inputs resident.  metric TFLOP/s."""
+    tc_matmul, inputs resident; at P > 1 config 5 runs row panels with the
+    all-gather fused into the GEMM (tc_matmul_allgather).  metric TFLOP/s."""
     from tensorcrate_b200 import _native as N
     from tensorcrate_b200 import cuda
     lib = N.lib()
@@ -423,8 +617,10 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
     m = k = n = size
     rng = np.random.default_rng(0)
     a_host = cuda.f32_to_bits(rng.uniform(-1, 1, m * k).astype(np.float32), dtype)
-    b = cuda.CudaStorage.store(cuda.f32_to_bits(rng.uniform(-1, 1, k * n).astype(np.float32), dtype), dtype)
+    b_host = cuda.f32_to_bits(rng.uniform(-1, 1, k * n).astype(np.float32), dtype)
+    b = cuda.CudaStorage.store(b_host, dtype)
     code = N.DTYPES[dtype]
+    esz = 4 if dtype == "f32" else 2
     panels = world > 1 and dtype != "f32"
     peer = None
     if panels:
@@ -433,28 +629,72 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
         if m % world:
             raise SystemExit(f"M={m} does not split over {world} ranks")
         rows = m // world
-        a = cuda.CudaStorage.store(a_host[rank * rows * k:(rank + 1) * rows * k], dtype)
+        a_rows = a_host[rank * rows * k:(rank + 1) * rows * k]
+        a = cuda.CudaStorage.store(a_rows, dtype)
         from tensorcrate_b200.sharding import PeerBuffer
         peer = PeerBuffer(comm, m * n * 2)
+        c_ptr = peer.ptr
 
-        def step():
-            N.check("matmul_allgather", lib.tc_matmul_allgather(comm, code, rows, k, n, a.ptr, b.ptr, peer.handle, sp))
+        def run(a_ptr, b_ptr, s):
+            N.check("matmul_allgather", lib.tc_matmul_allgather(comm, code, rows, k, n, a_ptr, b_ptr, peer.handle, s))
     else:
+        rows = m
+        a_rows = a_host
         a = cuda.CudaStorage.store(a_host, dtype)
         c = cuda.CudaStorage(dtype, m * n)
+        c_ptr = c.ptr
 
-        def step():
-            N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a.ptr, b.ptr, c.ptr, 0, sp))
+        def run(a_ptr, b_ptr, s):
+            N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a_ptr, b_ptr, c_ptr, 0, s))
 
-    ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
+    ms, blocks, clocks = timed(torch, world, lambda: run(a.ptr, b.ptr, sp), args, stream)
+
+    # parity: sampled rows of every panel of C against the oracle
+    import oracle as O
+    torch.cuda.synchronize()
+    failures = []
+    sample = [(p * (m // max(world, 1)) + 17) for p in range(world if panels else 1)] + [m - 3]
+    O.set_matmul_threads(os.cpu_count() or 1)
+    try:
+        for r0 in sample:
+            band = 4 if r0 + 4 <= m else m - r0
+            want = O.widen(O.matmul(dtype, 0, band, k, n, a_host[r0 * k:(r0 + band) * k], b_host), dtype)
+            got_bits = np.empty(band * n, dtype=np.float32 if dtype == "f32" else np.uint16)
+            N.check("d2h", lib.tc_memcpy_d2h(got_bits.ctypes.data, c_ptr + r0 * n * esz, band * n * esz, None))
+            got = O.widen(got_bits, dtype)
+            tol = 1e-5 * np.sqrt(k) if dtype == "f32" else 2.0 ** -7 * 2
+            if not np.max(np.abs(got - want)) <= tol * max(1.0, float(np.max(np.abs(want)))):
+                failures.append(f"rank {rank}: rows {r0}..{r0 + band} of C differ from the oracle")
+    finally:
+        O.set_matmul_threads(1)
+    parity = parity_record(torch, world, failures,
+                           f"rows {sample} (4 each) of the whole C on every rank against oracle/ "
+                           + ("(f32 1e-5*sqrt(K))" if dtype == "f32" else "(2 bf16 ulp of the f32-accumulated result)"))
+
+    # e2e: A (this rank's rows) and B uploaded, the whole C read back, every
+    # step, on one stream (the row-panel product writes every rank's C, so a
+    # second C would need every rank's read-back ordered before it).
+    h_a, h_b, h_c = pinned(torch, a_rows.nbytes), pinned(torch, b_host.nbytes), pinned(torch, m * n * esz)
+    h_a.numpy()[:] = a_rows.view(np.uint8)
+    h_b.numpy()[:] = b_host.view(np.uint8)
+    pipe = Pipeline(torch, lib, stream, uploads=[(h_a, [a.ptr, a.ptr], a_rows.nbytes), (h_b, [b.ptr, b.ptr],
+                                                                                        b_host.nbytes)],
+                    readbacks=[([c_ptr, c_ptr], h_c, m * n * esz)], run=lambda bb, s: run(a.ptr, b.ptr, s))
+    e2e_ms = pipe.measure_serial(world, max(3, args.steps // 4))
     if peer is not None:
+        torch.cuda.synchronize()
+        barrier(torch, world)
         peer.close()
+
     matvec = None
     if dtype == "f32" and size == 1024:
         # Config 1's matvec: y = M.x over 64 different [1024 x 1024] f32
         # matrices in turn (268 MB, more than L2), so every call reads HBM.
-        mats = [cuda.CudaStorage.store(rng.uniform(-1, 1, m * k).astype(np.float32), "f32") for _ in range(64)]
-        xv = cuda.CudaStorage.store(rng.uniform(-1, 1, k).astype(np.float32), "f32")
+        mats_host = [rng.uniform(-1, 1, m * k).astype(np.float32) for _ in range(64)]
+        mats = [cuda.CudaStorage.store(h, "f32") for h in mats_host]
+        last_host = mats_host[-1]
+        xv_host = rng.uniform(-1, 1, k).astype(np.float32)
+        xv = cuda.CudaStorage.store(xv_host, "f32")
         yv = cuda.CudaStorage("f32", m)
         # The 64 launches are captured in one CUDA graph, so the time is the
         # device's and not the host's launch rate through ctypes.
@@ -464,12 +704,23 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
             csp = C.c_void_p(cap.cuda_stream)
             for M in mats:
                 N.check("matvec", lib.tc_matvec(N.F32, m, k, M.ptr, xv.ptr, yv.ptr, 0, csp))
-        ms_mv, _ = timed(torch, world, graph.replay, 8, 3, stream)
+        mv_args = argparse.Namespace(steps=8, warmup=3, min_seconds=0.2)
+        ms_mv, _, _ = timed(torch, world, graph.replay, mv_args, stream)
         ms_mv /= len(mats)
         mv_bytes = m * k * 4 + k * 4 + m * 4
         mv_gbs = mv_bytes / (ms_mv * 1e-3) / 1e9
-        matvec = {"us": round(ms_mv * 1e3, 2), "gbs": round(mv_gbs, 1), "frac": round(mv_gbs / peaks()[0]["hbm_gbs"], 3),
-                  "bytes": mv_bytes, "l2": "64 matrices in turn, 268 MB"}
+        # the last product of the replay against the oracle's dot per row
+        torch.cuda.synchronize()
+        want_y = np.empty(m, np.float32)
+        O.call("orc_matvec", N.F32, m, k, O.ptr(last_host), O.ptr(xv_host), O.ptr(want_y), 0)
+        got_y = yv.as_slice()
+        if not np.max(np.abs(got_y - want_y)) <= 1e-5 * np.sqrt(k) * max(1.0, float(np.max(np.abs(want_y)))):
+            failures.append(f"rank {rank}: matvec differs from the oracle")
+        parity = parity_record(torch, world, failures, parity["checked"] + "; the matvec's y (1e-5*sqrt(K))")
+        matvec = {"us": round(ms_mv * 1e3, 2), "gbs": round(mv_gbs, 1),
+                  "frac": round(mv_gbs / peaks()[0]["hbm_gbs"], 3), "bytes": mv_bytes,
+                  "l2": "64 matrices in turn, 268 MB"}
+        del graph
     flops = 2.0 * m * n * k
     pk, pk_kind = peaks()
     # Whole-job TFLOP/s: replicas each do the whole product; panels share one.
@@ -480,68 +731,88 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
     # tensor cores' TF32 throughput.
     passes = 3 if dtype == "f32" else 1
     peak = pk["bf16_tflops"] / (2 if dtype == "f32" else 1)
-    workload = f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate"
-    parallelism = (f"row panels x{world}, all-gather fused into the GEMM epilogue (NVLink peer stores)" if panels
-                   else (f"replicas x{world}" if world > 1 else "single GPU"))
-    line = {"metric": f"{dtype} GEMM TFLOP/s", "value": round(total, 1), "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong" if panels else "weak", "vs_baseline": None, "dtype": dtype,
-            "data": "synthetic uniform[-1,1], seeded",
-            "config": {"workload": workload, "parallelism": parallelism,
-                       "l2": "inputs resident; the working set exceeds L2 at 8192 and above"},
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc" if dtype != "f32" else "gemm_tc<tf32> x3 passes",
-                         "achieved": round(per_gpu * passes, 1), "peak": round(peak, 1),
-                         "peak_source": pk_kind if dtype != "f32" else f"{pk_kind} bf16 / 2 (TF32 rate)",
-                         "unit": "TFLOP/s", "frac": round(per_gpu * passes / peak, 3), "traffic": None},
-            # f32: two operand splits, the TF32 product, the split-K finish; bf16: the product
-            "gpu_launches": (4 if dtype == "f32" else 1) * args.steps, "clocks": clocks}
+    e2e_total = flops / (e2e_ms * 1e-3) / 1e12 * (1 if panels else world)
+    rec = {"metric": f"{dtype} GEMM TFLOP/s", "value": round(total, 1), "unit": "TFLOP/s", "n_gpus": world,
+           "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong" if panels else "weak",
+           "dtype": dtype, "data": "synthetic uniform[-1,1], seeded",
+           "config": {"workload": f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate",
+                      "parallelism": (f"row panels x{world}, all-gather fused into the GEMM epilogue (NVLink peer "
+                                      "stores)" if panels else (f"replicas x{world}" if world > 1 else "single GPU")),
+                      "l2": "inputs resident; no flush: the operands and C exceed L2 at 8192"
+                      if size >= 8192 else "inputs resident; A, B, C (12.6 MB) fit in L2: the figure is L2-warm"},
+           "timing": blocks,
+           "roofline": {"bound": "tensor", "kernel": "gemm_tc" if dtype != "f32" else "gemm_tc<tf32> x3 passes",
+                        "achieved": round(per_gpu * passes, 1), "peak": round(peak, 1),
+                        "peak_source": (pk_kind + " burst") if dtype != "f32" else f"{pk_kind} bf16 / 2 (TF32 rate)",
+                        "unit": "TFLOP/s", "frac": round(per_gpu * passes / peak, 3),
+                        "frac_of_sustained": round(per_gpu * passes / (pk["bf16_tflops_sustained"] /
+                                                                       (2 if dtype == "f32" else 1)), 3),
+                        "traffic": None},
+           "e2e": {"value": round(e2e_total, 1), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": pipe.h2d, "d2h_bytes_per_step": pipe.d2h,
+                   "how": "this rank's rows of A and all of B uploaded, the whole C read back, every step, in turn "
+                          "on one stream"},
+           "parity": parity,
+           # f32: two operand splits, the TF32 product, the split-K finish; bf16: the product
+           "gpu_launches_per_step": 4 if dtype == "f32" else 1,
+           "clocks": clocks}
+    rec["gpu_launches"] = rec["gpu_launches_per_step"] * args.steps * blocks["blocks"]
     if matvec is not None:
-        line["config"]["matvec"] = matvec
-    return line
+        rec["config"]["matvec"] = matvec
+    return rec
 
 
+# ---------------------------------------------------------------------------
+# config 3: layout copies
+# ---------------------------------------------------------------------------
 def run_c3(args, torch, world, rank, comm):
     """Config 3: f16 [8,16,128,64,32] permuted (0,3,1,4,2) and made
     contiguous; then sliced [:, 8:, :, :32, :], split in 4 along axis 1 and
     concatenated back (one assemble).  metric GB/s of the two copies."""
     from tensorcrate_b200 import cuda
     from tensorcrate_b200 import _native as N
+    import oracle as O
     stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
+    sp = C.c_void_p(stream.cuda_stream)
+    lib = N.lib()
     shape = [8, 16, 128, 64, 32]
     n = int(np.prod(shape))
-    x = cuda.CudaStorage.store(np.random.default_rng(3).standard_normal(n).astype(np.float16).view(np.uint16), "f16")
-    t = cuda.Tensor(x, shape)
+    x_host = np.random.default_rng(3).standard_normal(n).astype(np.float16).view(np.uint16)
+    xs = [cuda.CudaStorage.store(x_host, "f16"), cuda.CudaStorage("f16", n)]
     perm = [0, 3, 1, 4, 2]
-    pv = t.view().permute(perm)
+    pv = cuda.Tensor(xs[0], shape).view().permute(perm)
     p_shape = pv.shape
-    out_p = cuda.CudaStorage("f16", n)
-    lib = N.lib()
-    sl = cuda.TensorView(out_p, p_shape, cuda.contiguous_strides(p_shape)).slice(1, 8, p_shape[1]).slice(3, 0, 32)
-    pieces = sl.chunk(1, 4)
-    cat_shape = list(sl.shape)
-    to = cuda.contiguous_strides(cat_shape)
-    regions, at = [], 0
-    for v in pieces:
-        regions.append(cuda.Cuda._region((v.storage, v.shape, v.offset, v.strides, at * to[1], to)))
-        at += v.shape[1]
-    m = int(np.prod(cat_shape))
-    out_c = cuda.CudaStorage("f16", m)
-    arr = (N.Region * len(regions))(*regions)
+
+    def plan(out_p):
+        sl = cuda.TensorView(out_p, p_shape, cuda.contiguous_strides(p_shape)).slice(1, 8, p_shape[1]).slice(3, 0, 32)
+        cat_shape = list(sl.shape)
+        to = cuda.contiguous_strides(cat_shape)
+        regions, at = [], 0
+        for v in sl.chunk(1, 4):
+            regions.append(cuda.Cuda._region((v.storage, v.shape, v.offset, v.strides, at * to[1], to)))
+            at += v.shape[1]
+        return sl, cat_shape, (N.Region * len(regions))(*regions), len(regions)
+
+    outs_p = [cuda.CudaStorage("f16", n), cuda.CudaStorage("f16", n)]
+    plans = [plan(o) for o in outs_p]
+    cat_shape = plans[0][1]
+    mcat = int(np.prod(cat_shape))
+    outs_c = [cuda.CudaStorage("f16", mcat), cuda.CudaStorage("f16", mcat)]
     ps, pst = N.sizes(p_shape), N.sizes(pv.strides)
 
-    def step():
-        N.check("copy", lib.tc_strided_copy(2, 5, ps, x.ptr, n, 0, pst, out_p.ptr, C.c_void_p(sp)))
-        N.check("assemble", lib.tc_assemble(2, out_c.ptr, m, arr, len(regions), C.c_void_p(sp)))
+    def step(b=0, s=sp):
+        N.check("copy", lib.tc_strided_copy(2, 5, ps, xs[b].ptr, n, 0, pst, outs_p[b].ptr, s))
+        N.check("assemble", lib.tc_assemble(2, outs_c[b].ptr, mcat, plans[b][2], plans[b][3], s))
 
-    ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
-    byts = 2 * n * 2 + 2 * m * 2
+    ms, blocks, clocks = timed(torch, world, step, args, stream)
+    byts = 2 * n * 2 + 2 * mcat * 2
     gbs = byts / (ms * 1e-3) / 1e9
     pk, pk_kind = peaks()
 
     # Interpretation B: the slice's indices on the original axes,
     # x[:, 8:, :, :32, :] = [8, 8, 128, 32, 32], split in 4 along axis 1 and
     # concatenated back (one assemble of four regions).
+    t = cuda.Tensor(xs[0], shape)
     slb = t.view().slice(1, 8, shape[1]).slice(3, 0, 32)
     cat_b = list(slb.shape)
     to_b = cuda.contiguous_strides(cat_b)
@@ -554,29 +825,249 @@ def run_c3(args, torch, world, rank, comm):
     arr_b = (N.Region * len(regions_b))(*regions_b)
 
     def step_b():
-        N.check("assemble", lib.tc_assemble(2, out_b.ptr, m_b, arr_b, len(regions_b), C.c_void_p(sp)))
+        N.check("assemble", lib.tc_assemble(2, out_b.ptr, m_b, arr_b, len(regions_b), sp))
 
-    ms_b, _ = timed(torch, world, step_b, args.steps, args.warmup, stream)
+    ms_b, _, _ = timed(torch, world, step_b, argparse.Namespace(steps=args.steps, warmup=args.warmup,
+                                                                min_seconds=0.3), stream)
     gbs_b = 2 * m_b * 2 / (ms_b * 1e-3) / 1e9
-    return {"metric": "config-3 layout copy HBM throughput (GB/s)", "value": round(world * gbs, 1), "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic N(0,1), seeded",
-            "config": {"workload": "config3: permute(0,3,1,4,2)+contiguous, slice->split(4)->concat "
-                                   "(interpretation A: slice of the permuted tensor)",
-                       "algorithmic_bytes_per_step": byts,
-                       "l2": "no flush: the permute moves 134 MB, more than the 126 MB L2",
-                       "interpretation_b": {"workload": "x[:, 8:, :, :32, :] on the original axes -> [8,8,128,32,32], "
-                                                        "split(4) along axis 1 -> concat",
-                                            "ms": round(ms_b, 4), "gbs": round(gbs_b, 1),
-                                            "frac": round(gbs_b / pk["hbm_gbs"], 3),
-                                            "l2": "33.6 MB of traffic per step: L2-resident between steps"}},
-            "roofline": {"bound": "hbm", "kernel": "strided copy + assemble", "achieved": round(gbs, 1),
-                         "peak": pk["hbm_gbs"], "peak_source": pk_kind, "unit": "GB/s",
-                         "frac": round(gbs / pk["hbm_gbs"], 3), "traffic": None},
-            "gpu_launches": 2 * args.steps, "clocks": clocks}
+
+    # parity: the whole permuted copy, the concatenation and interpretation
+    # B, bit for bit against the oracle's strided copies of the same views.
+    torch.cuda.synchronize()
+    failures = []
+    want_p = O.strided_copy(x_host, p_shape, 0, pv.strides)
+    if not np.array_equal(outs_p[0].as_slice(), want_p):
+        failures.append(f"rank {rank}: the permuted copy differs from the oracle")
+    sl = plans[0][0]
+    want_c = O.strided_copy(want_p, sl.shape, sl.offset, sl.strides)
+    if not np.array_equal(outs_c[0].as_slice(), want_c):
+        failures.append(f"rank {rank}: the concatenation differs from the oracle's contiguous slice")
+    want_b = O.strided_copy(x_host, slb.shape, slb.offset, slb.strides)
+    if not np.array_equal(out_b.as_slice(), want_b):
+        failures.append(f"rank {rank}: interpretation B differs from the oracle")
+    parity = parity_record(torch, world, failures, "all of the permuted copy, the concatenation (= the contiguous "
+                                                   "slice) and interpretation B, bit-exact against oracle/")
+
+    h_x, h_p, h_c = pinned(torch, n * 2), pinned(torch, n * 2), pinned(torch, mcat * 2)
+    h_x.numpy()[:] = x_host.view(np.uint8)
+    pipe = Pipeline(torch, lib, stream, uploads=[(h_x, [xs[0].ptr, xs[1].ptr], n * 2)],
+                    readbacks=[([outs_p[0].ptr, outs_p[1].ptr], h_p, n * 2),
+                               ([outs_c[0].ptr, outs_c[1].ptr], h_c, mcat * 2)],
+                    run=lambda b, s: step(b, s))
+    e2e_ms = pipe.measure(world, max(5, args.steps // 2))
+    rec = {"metric": "config-3 layout copy HBM throughput (GB/s)", "value": round(world * gbs, 1), "unit": "GB/s",
+           "n_gpus": world, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "dtype": "f16",
+           "data": "synthetic N(0,1), seeded",
+           "config": {"workload": "config3: permute(0,3,1,4,2)+contiguous, slice->split(4)->concat "
+                                  "(interpretation A: slice of the permuted tensor)",
+                      "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                      "algorithmic_bytes_per_step": byts,
+                      "l2": "no flush: the permute moves 134 MB, more than the 126 MB L2",
+                      "interpretation_b": {"workload": "x[:, 8:, :, :32, :] on the original axes -> [8,8,128,32,32], "
+                                                       "split(4) along axis 1 -> concat",
+                                           "ms": round(ms_b, 4), "gbs": round(gbs_b, 1),
+                                           "frac": round(gbs_b / pk["hbm_gbs"], 3),
+                                           "l2": "33.6 MB of traffic per step: L2-resident between steps"}},
+           "timing": blocks,
+           "roofline": {"bound": "hbm", "kernel": "strided copy + assemble", "achieved": round(gbs, 1),
+                        "peak": pk["hbm_gbs"], "peak_source": pk_kind, "unit": "GB/s",
+                        "frac": round(gbs / pk["hbm_gbs"], 3), "traffic": None},
+           "e2e": {"value": round(world * byts / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                   "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": pipe.h2d, "d2h_bytes_per_step": pipe.d2h,
+                   "how": "the input uploaded, the permuted copy and the concatenation read back, every step; "
+                          "pipelined over two device sets"},
+           "parity": parity, "gpu_launches_per_step": 2, "clocks": clocks}
+    rec["gpu_launches"] = 2 * args.steps * blocks["blocks"]
+    return rec
 
 
+# ---------------------------------------------------------------------------
+# config 4: the MLP training step
+# ---------------------------------------------------------------------------
+C4_DIMS = [1024, 4096, 4096, 1024]
+
+
+def run_c4(args, torch, world, rank, comm):
+    """Config 4: one training step of the 1024-4096-4096-1024 ReLU MLP in
+    bf16 (tape + Adam(1e-3, 0.9, 0.999, 1e-8), as the reference runs it),
+    global batch 2048 split across the ranks (strong scaling), the optimizer
+    sharded over the ranks.  metric: steps/s."""
+    from tensorcrate_b200 import _native as N
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp, xavier
+    lib = N.lib()
+    dtype = "bf16"
+    dims = C4_DIMS
+    gbatch = args.batch
+    if gbatch % world:
+        raise SystemExit("global batch must divide by the number of GPUs")
+    batch = gbatch // world
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    rng = np.random.default_rng(6)
+    ws = [xavier(dims[l + 1], dims[l], rng) for l in range(3)]
+    bs = [np.zeros(dims[l + 1], np.float32) for l in range(3)]
+    m = Mlp(dtype, dims, batch, gbatch)
+    m.load(ws, bs)
+    # The global batch (seeds 4, 5), rank r's columns.
+    x_all = np.random.default_rng(4).standard_normal((dims[0], gbatch)).astype(np.float32)
+    y_all = np.random.default_rng(5).standard_normal((dims[-1], gbatch)).astype(np.float32)
+    cols = slice(rank * batch, (rank + 1) * batch)
+    xr = cuda.f32_to_bits(np.ascontiguousarray(x_all[:, cols]), dtype)
+    yr = cuda.f32_to_bits(np.ascontiguousarray(y_all[:, cols]), dtype)
+    xs = [cuda.CudaStorage.store(xr, dtype), cuda.CudaStorage(dtype, xr.size)]
+    ys = [cuda.CudaStorage.store(yr, dtype), cuda.CudaStorage(dtype, yr.size)]
+    losses = [cuda.CudaStorage(dtype, 1), cuda.CudaStorage(dtype, 1)]
+
+    def step():
+        m.step(xs[0], ys[0], comm=comm, stream=stream)
+
+    ms, blocks, clocks = timed(torch, world, step, args, stream)
+    gemm_flops = 3 * 2 * gbatch * sum(dims[l] * dims[l + 1] for l in range(3))  # fwd + dW + dX
+    pk, pk_kind = peaks()
+    tflops = gemm_flops / (ms * 1e-3) / 1e12
+
+    # Phases, each timed alone (CUDA events, max over ranks): the step
+    # without the exchange (products, loss, adjoints and the whole Adam pass
+    # on this rank's batch), the Adam pass alone over all and over 1/P of the
+    # parameters, and the collectives over the whole flat gradient.
+    phase_args = argparse.Namespace(steps=args.steps, warmup=3, min_seconds=0.2)
+    solo = Mlp(dtype, dims, batch, gbatch)
+    solo.load(ws, bs)
+    phases = {}
+    phases["step_without_exchange_ms"] = round(timed(torch, world, lambda: solo.step(xs[0], ys[0], stream=stream),
+                                                     phase_args, stream)[0], 4)
+    total = sum(solo.block(l)[0] for l in range(3))
+    flat = [cuda.CudaStorage(dtype, total) for _ in range(4)]
+    for f in flat:
+        N.check("memset", lib.tc_memset(f.ptr, 0, f.nbytes, None))
+    adam = lambda n_el: N.check("adam", lib.tc_adam(N.BF16, n_el, flat[0].ptr, flat[1].ptr, flat[2].ptr, flat[3].ptr,
+                                                    1, 1e-3, 0.8984375, 0.98828125, 0.0, 10.0, 100.0, sp))
+    phases["adam_all_ms"] = round(timed(torch, world, lambda: adam(total), phase_args, stream)[0], 4)
+    if world > 1:
+        phases["adam_shard_ms"] = round(timed(torch, world, lambda: adam(total // world), phase_args, stream)[0], 4)
+        count = total // world
+        g = flat[1]
+        phases["reduce_scatter_ms"] = round(timed(
+            torch, world, lambda: N.check("rs", lib.tc_reducescatter(comm, N.BF16, g.ptr, g.ptr + rank * count * 2,
+                                                                     count, N.SUM, sp)), phase_args, stream)[0], 4)
+        phases["all_gather_ms"] = round(timed(
+            torch, world, lambda: N.check("ag", lib.tc_allgather(comm, N.BF16, g.ptr + rank * count * 2, g.ptr, count,
+                                                                 sp)), phase_args, stream)[0], 4)
+        phases["exchange_bytes_per_rank"] = 2 * (world - 1) * count * 2
+    del solo, flat
+
+    # parity: one fresh data-parallel step (beta2 = 0.99: the configured
+    # 0.999 rounds to 1.0 in bf16 and makes the reference's update NaN)
+    # against the oracle's whole-batch step, on rank 0.
+    parity = parity_c4(torch, world, rank, comm, ws, bs, x_all, y_all, batch, gbatch)
+
+    # e2e: inputs and targets uploaded from pinned host memory each step, the
+    # loss read back (parameters and optimizer state stay on the device).
+    h_x, h_y, h_l = pinned(torch, xr.nbytes), pinned(torch, yr.nbytes), pinned(torch, 2)
+    h_x.numpy()[:] = xr.reshape(-1).view(np.uint8)
+    h_y.numpy()[:] = yr.reshape(-1).view(np.uint8)
+    pipe = Pipeline(torch, lib, stream, uploads=[(h_x, [xs[0].ptr, xs[1].ptr], xr.nbytes),
+                                                 (h_y, [ys[0].ptr, ys[1].ptr], yr.nbytes)],
+                    readbacks=[([losses[0].ptr, losses[1].ptr], h_l, 2)],
+                    run=lambda b, s: N.check("mlp", lib.tc_mlp_step(m.handle, xs[b].ptr, ys[b].ptr, comm,
+                                                                    losses[b].ptr, s)))
+    e2e_steps = max(5, args.steps // 2)
+    e2e_ms = pipe.measure(world, e2e_steps)
+    serial_ms = pipe.measure_serial(world, max(3, e2e_steps // 2))
+    launches = 24 + (0 if world == 1 else 3 - 1)  # sharded: 3 Adam launches on shards instead of one
+    rec = {"metric": "config-4 MLP training steps/s", "value": round(1000.0 / ms, 2), "unit": "steps/s",
+           "n_gpus": world, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+           "dtype": dtype, "data": "synthetic N(0,1) inputs/targets, Xavier-uniform weights, seeded",
+           "config": {"workload": "config4: MLP 1024-4096-4096-1024 ReLU, MSE, Adam(1e-3,0.9,0.999,1e-8), bf16",
+                      "global_batch": gbatch, "per_rank_batch": batch,
+                      "parallelism": f"dp{world}" + (" (per layer: NCCL reduce-scatter of the gradient block, Adam "
+                                                     "on this rank's 1/P, all-gather of the parameters, beside the "
+                                                     "backward pass)" if world > 1 else ""),
+                      "l2": "no flush: a step touches 50 MB of weights, 150 MB of Adam state and ~100 MB of "
+                            "activations, more than the 126 MB L2",
+                      "gemm_flops_per_step": gemm_flops},
+           "timing": blocks,
+           "phases": phases,
+           "roofline": {"bound": "tensor", "kernel": "whole step (GEMM share)", "achieved": round(tflops / world, 1),
+                        "peak": pk["bf16_tflops_sustained"], "peak_source": pk_kind + " sustained", "unit": "TFLOP/s",
+                        "frac": round(tflops / world / pk["bf16_tflops_sustained"], 3), "traffic": None,
+                        "note": "GEMM flops per GPU per second over the whole step"},
+           "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "steps/s", "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": pipe.h2d, "d2h_bytes_per_step": pipe.d2h,
+                   "how": "inputs and targets uploaded and the loss read back every step; pipelined over two device "
+                          "sets", "serial_ms_per_step": round(serial_ms, 4)},
+           "parity": parity,
+           # per step: 3 forward products + 1 split-K finish, the loss pass, per layer the bias
+           # adjoints (matvec, vecmat + finish, an add below the top) and 2 products (+1 finish
+           # for the split input-gradient product of layer 1), Adam
+           "gpu_launches_per_step": launches, "clocks": clocks}
+    rec["gpu_launches"] = launches * args.steps * blocks["blocks"]
+    return rec
+
+
+def parity_c4(torch, world, rank, comm, ws, bs, x_all, y_all, batch, gbatch):
+    import oracle as O
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp
+    dtype, dims = "bf16", C4_DIMS
+    cols = slice(rank * batch, (rank + 1) * batch)
+    dp = Mlp(dtype, dims, batch, gbatch, beta2=0.99)
+    dp.load(ws, bs)
+    x = cuda.CudaStorage.store(O.narrow(np.ascontiguousarray(x_all[:, cols]), dtype), dtype)
+    y = cuda.CudaStorage.store(O.narrow(np.ascontiguousarray(y_all[:, cols]), dtype), dtype)
+    dp.step(x, y, comm=comm, stream=torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    failures = []
+    got = [dp.params(l) for l in range(3)]
+    blocks = [dp.block(l) for l in range(3)]
+    grads = [dp.grads(l) for l in range(3)]
+    if rank == 0:
+        O.set_matmul_threads(os.cpu_count() or 1)
+        try:
+            h = O.lib().orc_mlp_create(O.DTYPES[dtype], 3, O.u32s(dims), gbatch, gbatch, 1e-3, 0.9, 0.99, 1e-8)
+            for l, (w, b) in enumerate(zip(ws, bs)):
+                O.call("orc_mlp_params", h, l, O.ptr(O.narrow(w, dtype)), O.ptr(O.narrow(b, dtype)), 0)
+            loss = np.empty(1, O.STORE[dtype])
+            O.call("orc_mlp_step", h, O.ptr(O.narrow(x_all, dtype)), O.ptr(O.narrow(y_all, dtype)), O.ptr(loss), 0)
+        finally:
+            O.set_matmul_threads(1)
+        for l in range(3):
+            ow = np.empty(dims[l + 1] * dims[l], O.STORE[dtype])
+            ob = np.empty(dims[l + 1], O.STORE[dtype])
+            O.call("orc_mlp_params", h, l, O.ptr(ow), O.ptr(ob), 1)
+            for name, g, o in (("weight", got[l][0], ow), ("bias", got[l][1], ob)):
+                diff = np.abs(O.widen(g, dtype) - O.widen(o, dtype))
+                if not (np.max(diff) <= 2e-3 + 8e-3 and np.median(diff) <= 4e-3):
+                    failures.append(f"layer {l} {name}s after one step: max {np.max(diff):.3g}, "
+                                    f"median {np.median(diff):.3g} off the oracle")
+            # this rank's shard of the gradient block holds the sum over ranks
+            gw = np.empty(dims[l + 1] * dims[l], O.STORE[dtype])
+            gb = np.empty(dims[l + 1], O.STORE[dtype])
+            O.call("orc_mlp_grads", h, l, O.ptr(gw), O.ptr(gb))
+            length, at = blocks[l]
+
+            def block(w, b):
+                out = np.zeros(length, np.float32)
+                out[:w.size] = O.widen(w, dtype)
+                out[at:at + b.size] = O.widen(b, dtype)
+                return out
+            mine, want = block(*grads[l]), block(gw, gb)
+            hi = length // world
+            err, scale = float(np.linalg.norm(mine[:hi] - want[:hi])), float(np.linalg.norm(want[:hi]))
+            if not err <= max(1e-2, world * 2.0 ** -7) * scale:
+                failures.append(f"layer {l} gradient (rank 0's shard) off the oracle by {err:.3g} of {scale:.3g}")
+        O.lib().orc_mlp_destroy(h)
+    del dp
+    return parity_record(torch, world, failures,
+                         "one data-parallel step (beta2 0.99) from the bench's weights: every parameter against the "
+                         "oracle's whole-batch step (max <= 2 rates + 1 bf16 step, median <= 4e-3), rank 0's gradient "
+                         "shard within max(1e-2, P*2^-7) in norm")
+
+
+# ---------------------------------------------------------------------------
+# the other Kernels<T> methods, each alone (--workload trait)
+# ---------------------------------------------------------------------------
 def run_trait(args, torch, world, rank, comm):
     """The Kernels<T> methods beyond the configs' hot path, each on an
     input larger than L2, timed alone: scan, sort, analytic
@@ -597,10 +1088,11 @@ def run_trait(args, torch, world, rank, comm):
     y = cuda.CudaStorage.store(rng.uniform(0.5, 2.0, n).astype(np.float32), "f32")
     o1, o2 = cuda.CudaStorage("f32", n), cuda.CudaStorage("f32", n)
     ops, hbm_bytes, hbm_ms = {}, 0, 0.0
+    t_args = argparse.Namespace(steps=args.steps, warmup=args.warmup, min_seconds=0.2)
 
-    def measure(name, fn, byts, flops=None, bound="hbm", peak=None, steps=None):
+    def measure(name, fn, byts, flops=None, bound="hbm", peak=None):
         nonlocal hbm_bytes, hbm_ms
-        ms, _ = timed(torch, world, fn, steps or args.steps, args.warmup, stream)
+        ms, _, _ = timed(torch, world, fn, t_args, stream)
         entry = {"ms": round(ms, 4), "bound": bound}
         if byts:
             gbs = byts / (ms * 1e-3) / 1e9
@@ -696,154 +1188,35 @@ def run_trait(args, torch, world, rank, comm):
                                    "8192x8192 matrices, 16384x4096 programs",
                        "l2": "no flush: every input is 256 MB or more, above the 126 MB L2 (sort: 128 MB)",
                        "value": "algorithmic bytes of the HBM-bound calls / the sum of their times"},
-            "roofline": {"bound": "hbm", "kernel": "all HBM-bound trait-method calls", "achieved": round(gbs, 1), "peak": hbm,
-                         "peak_source": pk_kind, "unit": "GB/s", "frac": round(gbs / hbm, 3), "traffic": None},
-            # our kernels per call (sort: the key maps; CUB's radix passes are not counted)
+            "roofline": {"bound": "hbm", "kernel": "all HBM-bound trait-method calls", "achieved": round(gbs, 1),
+                         "peak": hbm, "peak_source": pk_kind, "unit": "GB/s", "frac": round(gbs / hbm, 3),
+                         "traffic": None},
             "ops": ops, "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.get(k, 1) for k in ops)}
 
 
-LAUNCHES_PER_CALL = {"prefix_sum": 3, "sort": 2, "moments": 4, "axis_moments_rows": 1, "dot": 2, "vector_sum": 2}
+LAUNCHES_PER_CALL = {"prefix_sum": 3, "sort": 10, "moments": 4, "axis_moments_rows": 1, "dot": 2, "vector_sum": 2}
 
 
-def run_c4(args, torch, world, rank, comm):
-    """Config 4: one training step of the 1024-4096-4096-1024 ReLU MLP in
-    bf16 (tape + Adam(1e-3, 0.9, 0.999, 1e-8), as the reference runs it),
-    global batch 2048 split across the ranks (strong scaling), gradients
-    summed with NCCL.  metric: steps/s."""
-    from tensorcrate_b200 import _native as N
-    from tensorcrate_b200 import cuda
-    from tensorcrate_b200.mlp import Mlp, xavier
-    dtype = "bf16"
-    dims = [1024, 4096, 4096, 1024]
-    gbatch = args.batch
-    if gbatch % world:
-        raise SystemExit("global batch must divide by the number of GPUs")
-    batch = gbatch // world
-    stream = torch.cuda.current_stream()
-    rng = np.random.default_rng(6)
-    ws = [xavier(dims[l + 1], dims[l], rng) for l in range(3)]
-    bs = [np.zeros(dims[l + 1], np.float32) for l in range(3)]
-    m = Mlp(dtype, dims, batch, gbatch)
-    m.load(ws, bs)
-    xr = np.random.default_rng(4 + rank).standard_normal((dims[0], batch)).astype(np.float32)
-    yr = np.random.default_rng(5 + rank).standard_normal((dims[-1], batch)).astype(np.float32)
-    x = cuda.CudaStorage.store(cuda.f32_to_bits(xr, dtype), dtype)
-    y = cuda.CudaStorage.store(cuda.f32_to_bits(yr, dtype), dtype)
-    loss = cuda.CudaStorage(dtype, 1)
-
-    def step():
-        m.step(x, y, comm=comm, stream=stream)
-
-    ms, clocks = timed(torch, world, step, args.steps, args.warmup, stream)
-    gemm_flops = 3 * 2 * gbatch * sum(dims[l] * dims[l + 1] for l in range(3))  # fwd + dW + dX
-    pk, pk_kind = peaks()
-    tflops = gemm_flops / (ms * 1e-3) / 1e12
-    # e2e: inputs and targets uploaded from pinned host memory each step, the
-    # loss read back.
-    px = torch.from_numpy(cuda.f32_to_bits(xr, dtype).view(np.int16)).pin_memory()
-    py = torch.from_numpy(cuda.f32_to_bits(yr, dtype).view(np.int16)).pin_memory()
-    pl = torch.empty(1, dtype=torch.int16).pin_memory()
-    lib = N.lib()
-    sp = C.c_void_p(stream.cuda_stream)
-
-    def e2e_step():
-        N.check("h2d", lib.tc_memcpy_h2d(x.ptr, px.data_ptr(), px.numel() * 2, sp))
-        N.check("h2d", lib.tc_memcpy_h2d(y.ptr, py.data_ptr(), py.numel() * 2, sp))
-        m.step(x, y, comm=comm, loss=loss, stream=stream)
-        N.check("d2h", lib.tc_memcpy_d2h(pl.data_ptr(), loss.ptr, 2, sp))
-
-    serial_ms, _ = timed(torch, world, e2e_step, max(3, args.steps // 2), 2, stream)
-
-    # As a streaming caller runs it: two device copies of the inputs and
-    # targets, step k+1's uploads on a copy stream while step k trains (each
-    # upload waits for the step that last read its buffers; each step waits
-    # for its own uploads).  Every step still uploads its batch and reads its
-    # loss back inside the timed region.
-    x2, y2 = cuda.CudaStorage(dtype, x.len), cuda.CudaStorage(dtype, y.len)
-    bufs = [(x, y), (x2, y2)]
-    copy_stream = torch.cuda.Stream()
-    csp = C.c_void_p(copy_stream.cuda_stream)
-    copied = [torch.cuda.Event(), torch.cuda.Event()]
-    consumed = [torch.cuda.Event(), torch.cuda.Event()]
-
-    def upload(k):
-        b = k % 2
-        if k >= 2:
-            copy_stream.wait_event(consumed[b])
-        N.check("h2d", lib.tc_memcpy_h2d(bufs[b][0].ptr, px.data_ptr(), px.numel() * 2, csp))
-        N.check("h2d", lib.tc_memcpy_h2d(bufs[b][1].ptr, py.data_ptr(), py.numel() * 2, csp))
-        copied[b].record(copy_stream)
-
-    def pipelined(steps):
-        copy_stream.wait_stream(stream)
-        upload(0)
-        for k in range(steps):
-            if k + 1 < steps:
-                upload(k + 1)
-            stream.wait_event(copied[k % 2])
-            m.step(bufs[k % 2][0], bufs[k % 2][1], comm=comm, loss=loss, stream=stream)
-            consumed[k % 2].record(stream)
-            N.check("d2h", lib.tc_memcpy_d2h(pl.data_ptr(), loss.ptr, 2, sp))
-
-    e2e_steps = max(3, args.steps // 2)
-    pipelined(2)
-    torch.cuda.synchronize()
-    barrier(torch, world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    pipelined(e2e_steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(torch, world, e0.elapsed_time(e1) / e2e_steps)
-    return {"metric": "config-4 MLP training steps/s", "value": round(1000.0 / ms, 2), "unit": "steps/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype,
-            "data": "synthetic N(0,1) inputs/targets, Xavier-uniform weights, seeded",
-            "config": {"workload": "config4: MLP 1024-4096-4096-1024 ReLU, MSE, Adam(1e-3,0.9,0.999,1e-8), bf16",
-                       "global_batch": gbatch, "per_rank_batch": batch,
-                       "parallelism": f"dp{world}" + (" (NCCL all-reduce of gradients)" if world > 1 else ""),
-                       "gemm_flops_per_step": gemm_flops},
-            "roofline": {"bound": "tensor", "kernel": "whole step (GEMM share)", "achieved": round(tflops, 1),
-                         "peak": pk["bf16_tflops_sustained"], "peak_source": pk_kind + " sustained",
-                         "unit": "TFLOP/s", "frac": round(tflops / pk["bf16_tflops_sustained"], 3), "traffic": None},
-            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "steps/s", "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": (px.numel() + py.numel()) * 2, "d2h_bytes_per_step": 2,
-                    "pipelined": "each step's uploads overlap the previous step (two device buffers, a copy stream)",
-                    "serial_ms_per_step": round(serial_ms, 4)},
-            # per step: 3 forward products + 1 split-K finish, the loss pass, per layer the bias
-            # adjoints (matvec, vecmat + finish, an add below the top) and 2 products (+1 finish
-            # for the split input-gradient product of layer 1), Adam: 24 (ncu launch list)
-            "gpu_launches": 24 * args.steps, "clocks": clocks}
-
-
-def barrier(torch, world):
-    if world > 1:
-        torch.distributed.barrier()
-
-
-def max_over_ranks(torch, world, v: float) -> float:
-    if world == 1:
-        return v
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
-
-
-def init_comm(torch, world, rank):
-    """NCCL communicator of the library, bootstrapped over torch.distributed."""
-    from tensorcrate_b200.sharding import nccl_comm
-    return nccl_comm(torch, world, rank)
+# ---------------------------------------------------------------------------
+def headline_keys(rec: dict, args) -> dict:
+    """A sub-record as the headline line of a single-workload run."""
+    out = dict(rec)
+    out.setdefault("steps", args.steps)
+    out.setdefault("warmup", args.warmup)
+    out.setdefault("vs_baseline", None)
+    return out
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "trait"])
+    ap.add_argument("--workload", default="all", choices=["all", "c1", "c2", "c3", "c4", "c5", "trait"])
     ap.add_argument("--batch", type=int, default=2048, help="config 4's global batch")
     ap.add_argument("--size", type=int, default=8192, help="config 5's M=N=K")
+    ap.add_argument("--min-seconds", type=float, default=1.0, help="device time each timed region lasts at least")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -869,24 +1242,30 @@ def main():
     N.call("tc_set_device", local)
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                              device_id=torch.device("cuda", local))
     comm = init_comm(torch, world, rank)
-    if args.workload == "c5":
-        line = run_gemm(args, torch, world, rank, comm, "bf16", args.size)
-    elif args.workload == "c1":
-        line = run_gemm(args, torch, world, rank, comm, "f32", 1024)
-    elif args.workload == "c3":
-        line = run_c3(args, torch, world, rank, comm)
-    elif args.workload == "c4":
-        line = run_c4(args, torch, world, rank, comm)
-    elif args.workload == "trait":
-        line = run_trait(args, torch, world, rank, comm)
-    else:
+    runners = {"c1": lambda: run_gemm(args, torch, world, rank, comm, "f32", 1024),
+               "c2": lambda: run_c2(args, torch, world, rank, comm),
+               "c3": lambda: run_c3(args, torch, world, rank, comm),
+               "c4": lambda: run_c4(args, torch, world, rank, comm),
+               "c5": lambda: run_gemm(args, torch, world, rank, comm, "bf16", args.size),
+               "trait": lambda: run_trait(args, torch, world, rank, comm)}
+    if args.workload == "all":
         line = run_c2(args, torch, world, rank, comm)
-    if rank == 0 and not args.no_cpu_baseline and args.workload == "c2":
+        for key in ("c4", "c5", "c1", "c3"):
+            line[key] = runners[key]()
+        statuses = [line["parity"]] + [line[k]["parity"] for k in ("c4", "c5", "c1", "c3")]
+        bad = [s for s in statuses if s["status"] != "ok"]
+        line["parity_all"] = "ok" if not bad else {"failed": len(bad)}
+        line["gpu_launches_all"] = line["gpu_launches"] + sum(line[k]["gpu_launches"] for k in ("c4", "c5", "c1", "c3"))
+    else:
+        line = headline_keys(runners[args.workload](), args)
+    if rank == 0 and not args.no_cpu_baseline and args.workload in ("all", "c2"):
         line["cpu_baseline"] = cpu_c2(sample_rows=64, reps=12)
+    torch.cuda.synchronize()
     if comm is not None:
+        barrier(torch, world)
         N.call("tc_comm_destroy", comm)
     if world > 1:
         torch.distributed.destroy_process_group()

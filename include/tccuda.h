@@ -13,9 +13,22 @@
  *    as `require_metal` does for Metal (src/tensors/backend.rs:418-426).
  *  - Pointers named `*_dev` / device buffers come from tc_malloc (or any
  *    cudaMalloc'd memory); `stream` is a cudaStream_t passed as void*
- *    (NULL = the per-thread default stream).  Every compute call is
+ *    (NULL = the legacy default stream).  Every compute call is
  *    asynchronous on `stream`; nothing synchronises except tc_stream_sync and
  *    the tc_memcpy_* calls given a NULL stream.
+ *  - Threads and streams.  Calls that keep partial results between kernels
+ *    (split reductions, vecmat, split-K products, scans, sorts, fused sums)
+ *    take that scratch, and the ticket counters some of them use, from
+ *    blocks owned by the (device, stream) pair they are called with.  Calls
+ *    on different streams, from any threads, therefore share nothing and may
+ *    run at the same time.  A stream belongs to one host thread at a time,
+ *    as Metal's per-thread device and queue do (src/tensors/backend.rs:
+ *    410-412): two threads enqueueing on one stream could interleave one
+ *    call's kernels with another's.  tc_ctx_create gives a thread a stream
+ *    of its own; tc_ctx_destroy frees that stream's blocks.  The scratch of
+ *    a stream grows on demand with cudaMalloc, which must not happen while
+ *    the stream is being captured into a CUDA graph: make one call of each
+ *    size before capturing.
  *  - Sizes, offsets and strides count ELEMENTS (as `Strided` does,
  *    src/tensors/backend.rs:196-203), never bytes, except where named `bytes`.
  *  - Shapes have at most TC_MAX_RANK axes (src/tensors/layout.rs:16).
@@ -95,12 +108,41 @@ const char *tc_build_info(void);
 int tc_set_device(int device);
 int tc_device_count(int *count);
 
+/* SMs of the current device (148 on B200): the launch geometry's unit. */
+int tc_sm_count(int *count);
+
+/* A device and a stream of its own for one host thread (Metal's per-thread
+ * device and command queue, src/tensors/backend.rs:391-412 and
+ * src/metal/device.rs).  Pass the stream tc_ctx_stream gives to every call
+ * the thread makes; the stream keys its own scratch, ticket counters and
+ * stream-ordered pool frees.  tc_ctx_destroy waits for the stream, frees its
+ * scratch and counters, and destroys it. */
+typedef struct tc_ctx tc_ctx;
+int tc_ctx_create(int device, tc_ctx **out);
+int tc_ctx_stream(tc_ctx *ctx, void **stream);
+int tc_ctx_device(tc_ctx *ctx, int *device);
+int tc_ctx_destroy(tc_ctx *ctx);
+
 /* Device storage: `Backend::Storage<T>` (src/tensors/backend.rs:84).
- * Served from a per-device caching pool, as Metal's src/metal/pool.rs. */
+ * Served from a per-device caching pool, as Metal's src/metal/pool.rs.
+ * tc_free returns a block for immediate reuse: no queued work may still use
+ * it.  tc_free_async returns it in `stream`'s order (work queued on `stream`
+ * before the call may still use it): a later tc_malloc_async on the same
+ * stream may take it at once, a request on another stream only with that
+ * stream made to wait for the freeing stream's work, and tc_malloc only once
+ * that work has completed.  This is how a storage dropped while its
+ * kernels are queued (Drop of `CudaStorage`) goes back to the pool. */
 int tc_malloc(void **out_dev, size_t bytes);
+int tc_malloc_async(void **out_dev, size_t bytes, void *stream);
 int tc_free(void *dev);
+int tc_free_async(void *dev, void *stream);
 /* Release every cached block back to CUDA. */
 int tc_pool_trim(void);
+/* Counters since the library loaded: cudaMalloc calls the library made
+ * (pool misses, scratch and counter growth, peer buffers), and requests for
+ * a stream's scratch.  The counterpart of the reference's allocation
+ * counters (src/counters.rs:100-160). */
+int tc_alloc_counts(uint64_t *device_allocations, uint64_t *scratch_requests);
 /* Pinned host staging, for the lazily filled host mirror behind
  * `Backend::as_slice` (src/tensors/backend.rs:96-99). */
 int tc_host_alloc(void **out_host, size_t bytes);
@@ -173,13 +215,13 @@ int tc_dot(int dtype, const void *a, const void *b, size_t n, void *out_dev,
 enum tc_sort_order { TC_ASCENDING = 0, TC_DESCENDING = 1 };
 /* `vector_prefix_sum` (kernels.rs:870; Host vector.rs:578-589,
  * compact::prefix_sum): out[i] = a[0] + ... + a[i], an f32 running total
- * rounded once per output to `dtype`.  Three launches; uses the per-device
- * scratch block. */
+ * rounded once per output to `dtype`.  Three launches; uses the stream's
+ * scratch. */
 int tc_prefix_sum(int dtype, const void *a, void *out, size_t n, void *stream);
 /* `vector_sort` (kernels.rs:873; Host vector.rs:874-886): the n values in
  * SortOrder's total order (f32::total_cmp / half's total_cmp: -NaN < -inf <
  * ... < -0 < +0 < ... < +inf < +NaN).  TC_EINVAL beyond 2^31-1 elements.
- * Uses the per-device scratch block. */
+ * Uses the stream's scratch. */
 int tc_sort(int dtype, int order, const void *a, void *out, size_t n, void *stream);
 /* `vector_unary`/`matrix_unary` (kernels.rs:876, 941; Host 1257-1268):
  * out = f(a), f a tc_analytic, computed in f32 and rounded once. */
@@ -328,16 +370,22 @@ int tc_matvec(int dtype, size_t rows, size_t cols, const void *m, const void *x,
 int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m,
               void *y, void *stream);
 /* tc_vecmat for callers that cannot allocate device memory.  No counterpart
- * in the reference.  Same row split, kernels and bits as tc_vecmat, but the
- * split's f32 partial sums (shares x cols x 4 bytes) live in a 1 MiB static
- * device array of the library instead of an allocated buffer; the call
- * makes no cudaMalloc, cudaFree or other allocating call (its first call on
- * a device looks the array's address up once).  TC_ERANGE, before any
- * launch, when a
- * shape's partials would not fit in 1 MiB.  Every call on a device shares
- * the array: calls that overlap on the GPU (other streams, other threads)
- * race on it, so order them, e.g. on one stream.  Nothing in the array has
- * to start at zero. */
+ * in the reference.  Some callers' device memory is already claimed by
+ * another allocator (a framework's caching allocator that holds the GPU's
+ * memory, or a fixed arena sized at start-up), so a cudaMalloc from this
+ * library would fail or break that allocator's budget; others run under a
+ * hard latency budget, where cudaMalloc may block and synchronise the
+ * device.  Same row split, kernels and bits as tc_vecmat, but the split's
+ * f32 partial sums (shares x cols x 4 bytes) live in a 1 MiB static device
+ * array of the library, which every GPU that loads the library holds until
+ * exit, instead of the stream's scratch; the call makes no cudaMalloc,
+ * cudaFree or other allocating call (its first call on a device looks the
+ * array's address up once, with cudaGetSymbolAddress).  TC_ERANGE, before
+ * any launch, when a shape's partials would not fit in 1 MiB.  Every call on
+ * a device shares the array and it keeps the last call's partials: calls
+ * that overlap on the GPU (other streams, other threads) race on it, so
+ * order them, e.g. on one stream.  Nothing in the array has to start at
+ * zero: each partial is written before it is read. */
 int tc_vecmat_noalloc(int dtype, size_t rows, size_t cols, const void *x,
                       const void *m, void *y, void *stream);
 
@@ -403,16 +451,28 @@ int tc_mlp_destroy(tc_mlp *mlp);
 /* dir = 0 uploads layer `layer`'s weight [dims[l+1] x dims[l]] and bias from
  * the host, dir = 1 downloads them. */
 int tc_mlp_params(tc_mlp *mlp, uint32_t layer, void *w_host, void *b_host, int dir);
-/* The gradients the last step computed (summed over ranks when it ran with
- * a communicator). */
+/* The gradients the last step computed.  After a step with a communicator
+ * of more than 8 ranks they are summed over the ranks; after a sharded step
+ * (2-8 ranks) only this rank's shard of each layer's block holds the sum
+ * (tc_mlp_block says where), the rest this rank's own part of it. */
 int tc_mlp_grads(tc_mlp *mlp, uint32_t layer, void *gw_host, void *gb_host);
+/* Layer `layer`'s block of the flat parameter, gradient and moment buffers:
+ * [W (row-major) | b], b starting at element *bias_at, the block *len
+ * elements long (padding zero).  Rank r of P (P <= 8) owns elements
+ * [r*len/P, (r+1)*len/P) of it in a sharded step. */
+int tc_mlp_block(tc_mlp *mlp, uint32_t layer, size_t *len, size_t *bias_at);
 /* Skip the adjoints nothing reads (inputs', targets', ones'); off by
  * default, as the tape computes them. */
 int tc_mlp_prune_leaves(tc_mlp *mlp, int prune);
-/* Forward, loss into loss_dev[0] if not NULL, backward, NCCL gradient
- * all-reduce over `comm` if not NULL (each layer's as soon as the backward
- * pass has produced it, beside the rest of the pass), then Adam on every
- * parameter.  x, y are device buffers. */
+/* Forward, loss into loss_dev[0] if not NULL, backward, then Adam.  With a
+ * communicator of 2-8 ranks the optimizer is sharded: as soon as the
+ * backward pass has produced a layer's gradients, a second stream
+ * reduce-scatters the layer's block, runs Adam on this rank's shard and
+ * all-gathers the updated parameters (NCCL), beside the rest of the pass.
+ * With more ranks each layer's gradients are all-reduced and every rank
+ * runs Adam on everything.  x, y are device buffers.  The products' split-K
+ * partials, vecmat's row split and the loss's sum use the scratch of
+ * `stream` and of the handle's own side stream. */
 int tc_mlp_step(tc_mlp *mlp, const void *x_dev, const void *y_dev, tc_comm *comm, void *loss_dev,
                 void *stream);
 
@@ -485,8 +545,8 @@ int tc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr
  * a program with one output of its own type, that output summed along
  * `axis` (TC_ROWS: one sum per row, `rows` results; TC_COLUMNS: one per
  * column) without being stored: each value rounded to the type, the sums
- * in f32, rounded once.  Columns with many rows use the per-device scratch
- * block for their bands' partial sums. */
+ * in f32, rounded once.  Columns with many rows use the stream's scratch
+ * for their bands' partial sums. */
 int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
                  const tc_place *places, uint32_t n_places, int axis, void *sums, void *stream);
 /* `matmul_epilogue` for any program (kernels.rs:1137-1150; Host

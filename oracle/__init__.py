@@ -103,6 +103,8 @@ def lib() -> C.CDLL:
         h.orc_evaluate_f64.restype = _d
         h.orc_set_threads.argtypes = [_i]
         h.orc_set_threads.restype = None
+        h.orc_set_matmul_threads.argtypes = [_i]
+        h.orc_set_matmul_threads.restype = None
         _lib = h
     return _lib
 
@@ -155,6 +157,12 @@ def widen(values, dtype: str) -> np.ndarray:
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(int(n))
+
+
+def set_matmul_threads(n: int) -> None:
+    """Threads for the oracle's large products (tests only: the same bits as
+    the Host's single thread, in a cache-blocked loop nest)."""
+    lib().orc_set_matmul_threads(int(n))
 
 
 # --- convenience wrappers returning numpy arrays ---------------------------

@@ -287,6 +287,55 @@ void matmul_avx(const float *a, const float *b, size_t, size_t k, size_t n, floa
     }
   }
 }
+void matmul_sse(const float *a, const float *b, size_t m, size_t k, size_t n, float *out, size_t row0, size_t row1);
+// The same products per output element, for the tests' large cases only:
+// each out[i, j] still runs p = 0..k in order with the same FMA (or, in the
+// column tail, the same unfused multiply-add), so the bits are matmul_avx's.
+// Only the loop nest differs (column blocks that stay in cache across rows,
+// row bands over threads).  The timed CPU baseline never takes this path.
+int g_matmul_threads = 1;
+__attribute__((target("avx2,fma")))
+void matmul_avx_blocked(const float *a, const float *b, size_t k, size_t n, float *out, size_t row0,
+                        size_t row1) {
+  constexpr size_t JB = 64;
+  const size_t body = n / 8 * 8;
+  for (size_t j0 = 0; j0 < body; j0 += JB) {
+    const size_t j1 = std::min(body, j0 + JB);
+    for (size_t i = row0; i < row1; ++i) {
+      const size_t arow = i * k, orow = i * n;
+      __m256 acc[JB / 8];
+      const size_t lanes = (j1 - j0) / 8;
+      for (size_t q = 0; q < lanes; ++q) acc[q] = _mm256_loadu_ps(out + orow + j0 + 8 * q);
+      for (size_t p = 0; p < k; ++p) {
+        const __m256 broadcast = _mm256_set1_ps(a[arow + p]);
+        const float *brow = b + p * n + j0;
+        for (size_t q = 0; q < lanes; ++q) acc[q] = _mm256_fmadd_ps(broadcast, _mm256_loadu_ps(brow + 8 * q), acc[q]);
+      }
+      for (size_t q = 0; q < lanes; ++q) _mm256_storeu_ps(out + orow + j0 + 8 * q, acc[q]);
+    }
+  }
+  if (body < n)
+    for (size_t i = row0; i < row1; ++i)
+      for (size_t p = 0; p < k; ++p) {
+        const float value = a[i * k + p];
+        for (size_t j = body; j < n; ++j) out[i * n + j] += value * b[p * n + j];
+      }
+}
+// Rows [row0, row1) of the SIMD product: matmul_avx as the Host runs it, or,
+// when the tests asked for threads, the blocked form over row bands.
+void matmul_simd_rows(const float *a, const float *b, size_t m, size_t k, size_t n, float *out, size_t row0,
+                      size_t row1) {
+  if (!has_avx2_fma()) { matmul_sse(a, b, m, k, n, out, row0, row1); return; }
+  const size_t rows = row1 - row0;
+  if (g_matmul_threads <= 1 || rows < 2) { matmul_avx(a, b, m, k, n, out, row0, row1); return; }
+  const size_t bands = std::min<size_t>(size_t(g_matmul_threads), rows);
+  std::vector<std::thread> pool;
+  for (size_t t = 0; t < bands; ++t) {
+    const size_t lo = row0 + rows * t / bands, hi = row0 + rows * (t + 1) / bands;
+    pool.emplace_back([=] { matmul_avx_blocked(a, b, k, n, out, lo, hi); });
+  }
+  for (auto &t : pool) t.join();
+}
 // matmul_sse, simd_x86.rs:1334-1358: the same, unfused throughout.
 void matmul_sse(const float *a, const float *b, size_t m, size_t k, size_t n, float *out,
                 size_t row0, size_t row1) {
@@ -365,8 +414,7 @@ void matmul_f32(const float *a, const float *b, size_t m, size_t k, size_t n, fl
   if (m * k * n >= MIN_MATMUL_OPS) {
     if (!accumulate)
       for (size_t i = row0; i < row1; ++i) std::fill(out + i * n, out + (i + 1) * n, 0.0f);
-    if (has_avx2_fma()) matmul_avx(a, b, m, k, n, out, row0, row1);
-    else matmul_sse(a, b, m, k, n, out, row0, row1);
+    matmul_simd_rows(a, b, m, k, n, out, row0, row1);
     return;
   }
   if (!accumulate) {
@@ -437,8 +485,7 @@ int matmul_rows(size_t rows, size_t inner, size_t cols, const void *a, const voi
   // the whole product, as the reference makes it.
   size_t band = row1 - row0;
   if (rows * inner * cols >= MIN_MATMUL_OPS) {
-    if (has_avx2_fma()) matmul_avx(left.data(), right.data(), band, inner, cols, out.data(), 0, band);
-    else matmul_sse(left.data(), right.data(), band, inner, cols, out.data(), 0, band);
+    matmul_simd_rows(left.data(), right.data(), band, inner, cols, out.data(), 0, band);
   } else {
     matmul_f32(left.data(), right.data(), band, inner, cols, out.data(), accumulate, 0, band);
   }
@@ -455,6 +502,9 @@ int matmul_rows(size_t rows, size_t inner, size_t cols, const void *a, const voi
 extern "C" {
 
 void orc_set_threads(int threads) { g_threads = threads; }
+// Threads for the large products of the tests (same bits; see
+// matmul_avx_blocked).  1, the default, is the Host's single thread.
+void orc_set_matmul_threads(int threads) { g_matmul_threads = threads < 1 ? 1 : threads; }
 
 void orc_narrow(int dtype, const float *in, void *out, size_t n) {
   with_dtype(dtype, [&](auto t) { using T = decltype(t); for (size_t i = 0; i < n; ++i) T::store(out, i, in[i]); return 0; });
@@ -744,7 +794,7 @@ int orc_reduce_axes(int dtype, uint32_t rank, const size_t *shape, const void *i
   // result_strides, strided.rs:83-100.
   size_t kept[TC_MAX_RANK]; uint32_t nk = 0;
   for (uint32_t a = 0; a < rank; ++a) if (!folded[a]) kept[nk++] = shape[a];
-  size_t kept_strides[TC_MAX_RANK];
+  size_t kept_strides[TC_MAX_RANK] = {0, 0, 0, 0, 0, 0};
   contiguous_strides(nk, kept, kept_strides);
   size_t to[TC_MAX_RANK]; uint32_t next = 0;
   for (uint32_t a = 0; a < rank; ++a) to[a] = folded[a] ? 0 : kept_strides[next++];

@@ -102,6 +102,7 @@ int orc_mlp_step(void *mlp, const void *x, const void *y, void *loss_out, int sk
 /* Host threads the elementwise kernels may use (set_host_threads,
  * src/parallel.rs:40); 0 = all. */
 void orc_set_threads(int threads);
+void orc_set_matmul_threads(int threads);
 
 /* Fused program (Kernels::fused; Host interpreter, fused/mod.rs:4055-4260)
  * over host buffers, as tc_fused takes them. */

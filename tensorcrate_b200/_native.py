@@ -90,8 +90,16 @@ SIGNATURES = {
     "tc_last_error": [C.c_char_p, _sz],
     "tc_set_device": [_i],
     "tc_device_count": [C.POINTER(_i)],
+    "tc_sm_count": [C.POINTER(_i)],
+    "tc_ctx_create": [_i, C.POINTER(_p)],
+    "tc_ctx_stream": [_p, C.POINTER(_p)],
+    "tc_ctx_device": [_p, C.POINTER(_i)],
+    "tc_ctx_destroy": [_p],
     "tc_malloc": [C.POINTER(_p), _sz],
+    "tc_malloc_async": [C.POINTER(_p), _sz, _p],
     "tc_free": [_p],
+    "tc_free_async": [_p, _p],
+    "tc_alloc_counts": [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)],
     "tc_pool_trim": [],
     "tc_host_alloc": [C.POINTER(_p), _sz],
     "tc_host_free": [_p],
@@ -147,6 +155,7 @@ SIGNATURES = {
     "tc_mlp_destroy": [_p],
     "tc_mlp_params": [_p, _u32, _p, _p, _i],
     "tc_mlp_grads": [_p, _u32, _p, _p],
+    "tc_mlp_block": [_p, _u32, C.POINTER(_sz), C.POINTER(_sz)],
     "tc_mlp_prune_leaves": [_p, _i],
     "tc_mlp_step": [_p, _p, _p, _p, _p, _p],
     "tc_comm_unique_id": [C.POINTER(C.c_uint8)],

@@ -157,7 +157,7 @@ static int exchange(tc_comm *comm, const void *mine, size_t bytes, void *all) {
   cudaStream_t s = nullptr;
   if (int st = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return st;
   void *dev = nullptr;
-  int st = check_cuda(cudaMalloc(&dev, bytes * size_t(comm->nranks)), "cudaMalloc (handle exchange)");
+  int st = device_malloc(&dev, bytes * size_t(comm->nranks), "cudaMalloc (handle exchange)");
   if (!st) st = check_cuda(cudaMemcpyAsync(static_cast<uint8_t *>(dev) + bytes * comm->rank, mine, bytes,
                                            cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
   if (!st) st = check_nccl(nccl().all_gather(static_cast<uint8_t *>(dev) + bytes * comm->rank, dev, bytes, ncclUint8,
@@ -184,8 +184,8 @@ int tc_peer_buffer_create(tc_comm *comm, size_t bytes, tc_peer_buffer **out) {
   auto *buf = new tc_peer_buffer{};
   buf->comm = comm;
   buf->bytes = bytes;
-  int st = check_cuda(cudaMalloc(&buf->local, bytes), "cudaMalloc (peer buffer)");
-  if (!st) st = check_cuda(cudaMalloc(&buf->token, sizeof(int)), "cudaMalloc (peer buffer token)");
+  int st = device_malloc(&buf->local, bytes, "cudaMalloc (peer buffer)");
+  if (!st) st = device_malloc(reinterpret_cast<void **>(&buf->token), sizeof(int), "cudaMalloc (peer buffer token)");
   if (!st) st = check_cuda(cudaMemset(buf->token, 0, sizeof(int)), "cudaMemset");
   std::vector<cudaIpcMemHandle_t> handles(size_t(comm->nranks));
   cudaIpcMemHandle_t mine;

@@ -35,14 +35,17 @@ int check_launch(const char *what);
 int sm_count();
 
 // A device scratch buffer of at least `bytes` for partial results, one per
-// device, grown on demand and kept until the process exits.  Work that uses
-// it is ordered on the caller's stream; two such calls running at the same
-// time on different streams of one device would share it.
-int scratch(size_t bytes, void **out);
-// `n` zeroed device counters, one set per device, grown on demand.  A kernel
-// that takes tickets from them sets each back to zero when it is done, so
-// they are zero between launches.
-int counters(size_t n, int **out);
+// (device, stream), grown on demand.  Work that uses it is ordered on that
+// stream, so calls on other streams never share it.  A stream belongs to one
+// host thread at a time: two threads that enqueue multi-kernel calls on the
+// same stream could interleave them.
+int scratch(size_t bytes, void **out, cudaStream_t stream);
+// `n` zeroed device counters per (device, stream), grown on demand.  A
+// kernel that takes tickets from them sets each back to zero when it is
+// done, so they are zero between launches.
+int counters(size_t n, int **out, cudaStream_t stream);
+// cudaMalloc, counted (tc_alloc_counts).
+int device_malloc(void **ptr, size_t bytes, const char *what);
 // The means and sums of squared deviations (in the element type) of the
 // slices of `input` folded over `axes`, in as few passes as the layout
 // allows (reduce.cu).

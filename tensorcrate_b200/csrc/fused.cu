@@ -629,7 +629,7 @@ int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint
     const long long bands = ((long long)rows + band - 1) / band;
     float *partial = nullptr;
     if (bands > 1)
-      if (int st = scratch(size_t(bands) * cols * sizeof(float), reinterpret_cast<void **>(&partial))) return st;
+      if (int st = scratch(size_t(bands) * cols * sizeof(float), reinterpret_cast<void **>(&partial), s)) return st;
     fused_cols_kernel<T><<<dim3(unsigned(col_blocks), unsigned(bands)), INTERP_BLOCK, 0, s>>>(p, band, partial, sums);
     if (int st = check_launch("fused sum (columns)")) return st;
     if (bands > 1) {

@@ -829,7 +829,7 @@ int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_
   p.partial = nullptr;
   if (p.ksplit > 1) {
     void *w = nullptr;
-    if (int st = scratch(size_t(p.ksplit) * rows * cols * sizeof(float), &w)) return st;
+    if (int st = scratch(size_t(p.ksplit) * rows * cols * sizeof(float), &w, stream)) return st;
     p.partial = static_cast<float *>(w);
   }
   CUtensorMap ma, mb;
@@ -848,7 +848,7 @@ int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const 
   const size_t operand_floats = size_t(rows + cols) * size_t(2 * kp);
   const size_t partial_floats = pl.ksplit > 1 ? size_t(pl.ksplit) * rows * cols : 0;
   void *scratch_p = nullptr;
-  if (int st = scratch((operand_floats + partial_floats) * sizeof(float), &scratch_p)) return st;
+  if (int st = scratch((operand_floats + partial_floats) * sizeof(float), &scratch_p, stream)) return st;
   float *ah = static_cast<float *>(scratch_p), *bh = ah + size_t(rows) * size_t(2 * kp);
   // A as [rows x K]: element (m, k); B as [cols x K]: element (n, k).
   const long long a_sr = transposed == TC_TRANS_LEFT ? 1 : (long long)inner;

@@ -289,7 +289,7 @@ int tc_vecmat(int dtype, size_t rows, size_t cols, const void *x, const void *m,
     float *partial = nullptr;
     if (shares > 1) {
       void *p = nullptr;
-      if (int st = scratch(size_t(shares) * cols * sizeof(float), &p)) return st;
+      if (int st = scratch(size_t(shares) * cols * sizeof(float), &p, as_stream(stream))) return st;
       partial = static_cast<float *>(p);
     }
     dim3 grid((unsigned)col_blocks, (unsigned)shares);

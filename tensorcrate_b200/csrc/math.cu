@@ -286,7 +286,7 @@ template <class K> int sort_keys(const void *a, void *out, size_t n, bool descen
   if (int st = check_cuda(e, "sort (temporary size)")) return st;
   const size_t alt_bytes = (n * sizeof(K) + 255) & ~size_t(255);
   void *block = nullptr;
-  if (int st = scratch(alt_bytes + temp, &block)) return st;
+  if (int st = scratch(alt_bytes + temp, &block, s)) return st;
   buffers = cub::DoubleBuffer<K>(keys, static_cast<K *>(block));
   void *temp_ptr = static_cast<char *>(block) + alt_bytes;
   const unsigned grid = grid_for((n * sizeof(K) + 15) / 16, 256, 8);
@@ -350,7 +350,7 @@ int tc_prefix_sum(int dtype, const void *a, void *out, size_t n, void *stream) {
     const long long per = ((tiles + want - 1) / want) * SCAN_TILE;
     const int chunks = int(((long long)n + per - 1) / per);
     float *sums = nullptr;
-    if (int st = scratch(MAX_CHUNKS * sizeof(float), reinterpret_cast<void **>(&sums))) return st;
+    if (int st = scratch(MAX_CHUNKS * sizeof(float), reinterpret_cast<void **>(&sums), s)) return st;
     const bool vec = aligned16(a) && aligned16(out);
     chunk_sums<T><<<chunks, SCAN_THREADS, 0, s>>>(static_cast<const S *>(a), (long long)n, per, vec, sums);
     if (int st = check_launch("prefix_sum (chunks)")) return st;

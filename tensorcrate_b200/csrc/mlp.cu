@@ -18,9 +18,15 @@
 // the ones vector's.
 //
 // Under data parallelism each rank runs the step on its own batch with the
-// loss scaled by the global batch, and the parameter gradients are summed
-// with NCCL before Adam.  The reduction of each layer's gradients starts, on
-// a second stream, as soon as the backward pass has produced them.
+// loss scaled by the global batch, so the sum of the ranks' gradients is the
+// gradient of the whole batch.  Each layer's gradients are exchanged on a
+// second stream as soon as the backward pass has produced them.  With 2-8
+// ranks the optimizer is sharded (ZeRO stage 1 style): the layer's
+// gradient block is reduce-scattered, each rank runs Adam on its 1/P of the
+// block, and the updated parameters are all-gathered, so the Adam pass
+// shrinks with P and the collectives move the same bytes an all-reduce
+// would.  With more ranks the gradients are all-reduced and every rank runs
+// the whole Adam pass.
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -114,13 +120,18 @@ struct tc_mlp {
   std::vector<Buf> W, b, gW, gb, mW, vW, mb, vb;
   std::vector<Buf> A, H;
   Buf ones, S, Rbar, Ybar, Xbar, abar, inbar, onesbar, ovec, loss_sum;
-  // Every layer's gradients in one allocation, [gW_l | gb_l] side by side
-  // (each 16-byte aligned, the gap zeroed), so that one all-reduce moves a
-  // layer's gradients: gW[l].p and gb[l].p point into it.
-  Buf grads;
-  std::vector<size_t> layer_span;  // elements from gW[l].p to the end of gb[l]
+  // Parameters, their gradients and Adam's two moments each in one flat
+  // allocation with the same layout: layer l's block starts at element
+  // block_at[l] and holds [W_l | b_l] (b_l 16-byte aligned, gaps zero),
+  // padded to block_len[l], a multiple of SHARD_UNIT elements.  W[l], b[l],
+  // gW[l], ... point into them.  One collective moves a layer's block, and
+  // every rank count P <= 8 cuts a block into P equal, 16-byte-aligned
+  // shards.
+  Buf params, grads, mom1, mom2;
+  std::vector<size_t> block_at, block_len;
+  size_t total = 0;
   cudaStream_t comm_stream = nullptr;
-  std::vector<cudaEvent_t> grad_ready;
+  std::vector<cudaEvent_t> grad_ready, params_free;
   cudaEvent_t reduced = nullptr;
   // The bias adjoints (matvec, vecmat: memory-bound) run on a side stream,
   // beside each layer's products.
@@ -135,6 +146,11 @@ int alloc(Buf &b, size_t n, size_t esz) {
   b.n = n;
   return tc_malloc(&b.p, std::max<size_t>(n * esz, 16));
 }
+
+// 840 = lcm(1, ..., 8): a block of a multiple of 840 16-byte groups splits
+// into P equal shards of whole groups for every P <= 8.
+constexpr size_t SHARD_UNIT_GROUPS = 840;
+constexpr int MAX_SHARDS = 8;
 
 // Adam::update's host arithmetic (optim.rs:1106-1124) in the element type.
 void adam_coefficients(const tc_mlp &m, uint32_t step, float &c1, float &c2) {
@@ -174,31 +190,40 @@ int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t bat
     m->W.emplace_back(); m->b.emplace_back(); m->gW.emplace_back(); m->gb.emplace_back();
     m->mW.emplace_back(); m->vW.emplace_back(); m->mb.emplace_back(); m->vb.emplace_back();
     m->A.emplace_back(); m->H.emplace_back();
-    need(m->W[l], outd * in); need(m->mW[l], outd * in); need(m->vW[l], outd * in);
-    need(m->b[l], outd); need(m->mb[l], outd); need(m->vb[l], outd);
     need(m->A[l], outd * B);
     if (l + 1 < m->layers) need(m->H[l], outd * B);
   }
   {
-    const size_t align = 16 / e;  // elements per 16 bytes
-    auto up = [&](size_t n) { return (n + align - 1) / align * align; };
+    const size_t group = 16 / e;  // elements per 16 bytes
+    const size_t unit = SHARD_UNIT_GROUPS * group;
+    auto up = [](size_t n, size_t to) { return (n + to - 1) / to * to; };
     size_t total = 0;
-    std::vector<size_t> at_w(layers), at_b(layers);
+    std::vector<size_t> at_b(layers);
+    m->block_at.resize(layers);
+    m->block_len.resize(layers);
     for (uint32_t l = 0; l < layers; ++l) {
-      at_w[l] = total;
-      total += up(m->dims[l + 1] * m->dims[l]);
-      at_b[l] = total;
-      total += up(m->dims[l + 1]);
+      const size_t nw = size_t(m->dims[l + 1]) * m->dims[l], nb = m->dims[l + 1];
+      m->block_at[l] = total;
+      at_b[l] = total + up(nw, group);
+      m->block_len[l] = up(up(nw, group) + nb, unit);
+      total += m->block_len[l];
     }
-    need(m->grads, total);
-    if (!st) st = check_cuda(cudaMemset(m->grads.p, 0, total * e), "cudaMemset");
-    m->layer_span.resize(layers);
+    m->total = total;
+    need(m->params, total); need(m->grads, total); need(m->mom1, total); need(m->mom2, total);
+    for (Buf *f : {&m->params, &m->grads, &m->mom1, &m->mom2})
+      if (!st) st = check_cuda(cudaMemset(f->p, 0, total * e), "cudaMemset");
     for (uint32_t l = 0; l < layers && !st; ++l) {
-      m->gW[l].p = static_cast<char *>(m->grads.p) + at_w[l] * e;
-      m->gW[l].n = m->dims[l + 1] * m->dims[l];
-      m->gb[l].p = static_cast<char *>(m->grads.p) + at_b[l] * e;
-      m->gb[l].n = m->dims[l + 1];
-      m->layer_span[l] = at_b[l] + m->dims[l + 1] - at_w[l];
+      const size_t nw = size_t(m->dims[l + 1]) * m->dims[l], nb = m->dims[l + 1];
+      auto at = [&](Buf &f, size_t off, size_t n) {
+        Buf v;
+        v.p = static_cast<char *>(f.p) + off * e;
+        v.n = n;
+        return v;
+      };
+      m->W[l] = at(m->params, m->block_at[l], nw); m->b[l] = at(m->params, at_b[l], nb);
+      m->gW[l] = at(m->grads, m->block_at[l], nw); m->gb[l] = at(m->grads, at_b[l], nb);
+      m->mW[l] = at(m->mom1, m->block_at[l], nw); m->mb[l] = at(m->mom1, at_b[l], nb);
+      m->vW[l] = at(m->mom2, m->block_at[l], nw); m->vb[l] = at(m->mom2, at_b[l], nb);
     }
   }
   size_t widest = 0;
@@ -228,9 +253,10 @@ int tc_mlp_create(int dtype, uint32_t layers, const uint32_t *dims, uint32_t bat
     return rc;
   }
   m->grad_ready.resize(m->layers);
+  m->params_free.resize(m->layers);
   m->abar_ready.resize(m->layers);
   m->side_done.resize(m->layers);
-  for (auto *evs : {&m->grad_ready, &m->abar_ready, &m->side_done})
+  for (auto *evs : {&m->grad_ready, &m->params_free, &m->abar_ready, &m->side_done})
     for (auto &ev : *evs)
       if ((rc = check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event"))) {
         tc_mlp_destroy(m);
@@ -247,13 +273,14 @@ int tc_mlp_destroy(tc_mlp *m) {
     if (b.p) tc_free(b.p);
     b.p = nullptr;
   };
-  for (auto *v : {&m->W, &m->b, &m->mW, &m->vW, &m->mb, &m->vb, &m->A, &m->H})
+  for (auto *v : {&m->A, &m->H})
     for (auto &b : *v) drop(b);
-  drop(m->grads);  // gW and gb point into it
+  // W, b, their gradients and moments point into these
+  for (Buf *f : {&m->params, &m->grads, &m->mom1, &m->mom2}) drop(*f);
   for (Buf *b : {&m->ones, &m->S, &m->Rbar, &m->Ybar, &m->Xbar, &m->abar,
                  &m->inbar, &m->onesbar, &m->ovec, &m->loss_sum})
     drop(*b);
-  for (auto *evs : {&m->grad_ready, &m->abar_ready, &m->side_done})
+  for (auto *evs : {&m->grad_ready, &m->params_free, &m->abar_ready, &m->side_done})
     for (auto ev : *evs)
       if (ev) cudaEventDestroy(ev);
   if (m->reduced) cudaEventDestroy(m->reduced);
@@ -286,6 +313,18 @@ int tc_mlp_grads(tc_mlp *m, uint32_t l, void *gw_host, void *gb_host) {
   return TC_OK;
 }
 
+// Where layer `l`'s parameters sit in its block of the flat buffers: the
+// block's length in elements (a multiple of every rank count up to 8 times
+// 16 bytes) and the element at which b_l starts (W_l starts at 0).  Rank r
+// of P owns elements [r*len/P, (r+1)*len/P) of every block in a sharded
+// step.
+int tc_mlp_block(tc_mlp *m, uint32_t l, size_t *len, size_t *bias_at) {
+  if (!m || int(l) >= m->layers || !len || !bias_at) return fail(TC_EINVAL, "mlp_block: layer %u", l);
+  *len = m->block_len[l];
+  *bias_at = size_t(static_cast<char *>(m->b[l].p) - static_cast<char *>(m->W[l].p)) / m->esz;
+  return TC_OK;
+}
+
 // Skip the adjoints nothing reads (inputs', targets', the ones vector's).
 // Off by default: the tape computes them.
 int tc_mlp_prune_leaves(tc_mlp *m, int prune) {
@@ -295,20 +334,42 @@ int tc_mlp_prune_leaves(tc_mlp *m, int prune) {
 }
 
 int tc_allreduce(tc_comm *comm, int dtype, void *buf, size_t count, int op, void *stream);
+int tc_allgather(tc_comm *comm, int dtype, const void *send, void *recv, size_t count, void *stream);
+int tc_reducescatter(tc_comm *comm, int dtype, const void *send, void *recv, size_t count, int op, void *stream);
+int tc_comm_rank(tc_comm *comm, int *rank, int *nranks);
 
 // One step: forward, loss (into loss_out, one element, if not null),
-// backward, optional gradient all-reduce over `comm`, Adam.  x: [dims[0] x
+// backward, optional gradient exchange over `comm`, Adam.  x: [dims[0] x
 // batch], y: [dims[L] x batch], both device buffers, column per sample.
 int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *loss_out, void *stream_v) {
   if (!m || !x || !y) return fail(TC_EINVAL, "mlp_step: null argument");
   cudaStream_t s = as_stream(stream_v);
   const int d = m->dtype, L = m->layers;
-  const size_t B = m->batch;
+  const size_t B = m->batch, e = m->esz;
   void *st = stream_v;
 #define TRY(call)                   \
   do {                              \
     if (int rc_ = (call)) return rc_; \
   } while (0)
+  int rank = 0, nranks = 1;
+  if (comm) TRY(tc_comm_rank(comm, &rank, &nranks));
+  if (nranks == 1) comm = nullptr;
+  // With 2-8 ranks the optimizer is sharded: each layer's gradient block is
+  // reduce-scattered, every rank runs Adam on its own shard of the block,
+  // and the updated parameters are all-gathered.  More ranks all-reduce the
+  // gradients and run Adam on everything.
+  const bool sharded = comm && nranks <= MAX_SHARDS;
+  // Adam's coefficients for this step (Adam::update, optim.rs:1106-1124).
+  m->steps += 1;
+  float c1, c2;
+  adam_coefficients(*m, m->steps, c1, c2);
+  const int resumed = m->steps > 1;
+  auto adam_range = [&](size_t at, size_t n, cudaStream_t on) {
+    char *p = static_cast<char *>(m->params.p), *g = static_cast<char *>(m->grads.p);
+    char *m1 = static_cast<char *>(m->mom1.p), *m2 = static_cast<char *>(m->mom2.p);
+    return tc_adam(d, n, p + at * e, g + at * e, m1 + at * e, m2 + at * e, resumed, m->rate, m->beta1, m->beta2,
+                   m->eps, c1, c2, on);
+  };
   // ---- forward ----
   for (int l = 0; l < L; ++l) {
     const size_t in = m->dims[l], outd = m->dims[l + 1];
@@ -321,8 +382,9 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   }
   const size_t last = m->dims[L];
   const float factor = round_to(d, 1.0 / (double(last) * double(m->global_batch)));
-  // With a communicator, the gradient all-reduces run beside the backward
-  // products: leave them SMs (the products' CTAs fill an SM's shared memory).
+  // With a communicator, the collectives (and, sharded, the Adam shards)
+  // run beside the backward products: leave them SMs (the products' CTAs
+  // fill an SM's shared memory).
   struct Reserve {
     explicit Reserve(bool on) { gemm_reserve_sms(on ? 16 : 0); }
     ~Reserve() { gemm_reserve_sms(0); }
@@ -350,25 +412,14 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     // A = Z + O: Z̄ = Ō = Ā (shared).  O = b ⊗ ones: b̄ += Ō·ones,
     // ones̄ += bᵀ·Ō (vecmat), accumulated in node order.  These read Ā
     // only, so they run on the side stream while the products below run
-    // here; the side stream's vecmat keeps its partial sums in the static
-    // array of tc_vecmat_noalloc (the per-device scratch belongs to this
-    // stream's split-K products), and a shape too large for it runs here.
+    // here; the side stream's calls keep their partial sums in that
+    // stream's own scratch.
     TRY(check_cuda(cudaEventRecord(m->abar_ready[l], s), "event"));
     TRY(check_cuda(cudaStreamWaitEvent(m->side, m->abar_ready[l], 0), "wait"));
     TRY(tc_matvec(d, outd, B, abar, m->ones.p, m->gb[l].p, 0, m->side));
     if (!m->prune) {
       void *dst = l == L - 1 ? m->onesbar.p : m->ovec.p;
-      int vst = tc_vecmat_noalloc(d, outd, B, m->b[l].p, abar, dst, m->side);
-      if (vst == TC_ERANGE) {
-        // Too large for the static array: join, and run it on this stream.
-        TRY(check_cuda(cudaEventRecord(m->side_done[l], m->side), "event"));
-        TRY(check_cuda(cudaStreamWaitEvent(s, m->side_done[l], 0), "wait"));
-        TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, dst, st));
-        TRY(check_cuda(cudaEventRecord(m->abar_ready[l], s), "event"));
-        TRY(check_cuda(cudaStreamWaitEvent(m->side, m->abar_ready[l], 0), "wait"));
-      } else if (vst) {
-        return vst;
-      }
+      TRY(tc_vecmat(d, outd, B, m->b[l].p, abar, dst, m->side));
       if (l != L - 1) TRY(tc_elementwise(d, TC_ADD, m->onesbar.p, m->ovec.p, m->onesbar.p, B, m->side));
     }
     TRY(check_cuda(cudaEventRecord(m->side_done[l], m->side), "event"));
@@ -379,8 +430,14 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
       TRY(check_cuda(cudaEventRecord(m->grad_ready[l], s), "event"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0), "wait"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->side_done[l], 0), "wait"));
-      // the layer's weight and bias gradients in one call
-      TRY(tc_allreduce(comm, d, m->gW[l].p, m->layer_span[l], TC_SUM, m->comm_stream));
+      char *block = static_cast<char *>(m->grads.p) + m->block_at[l] * e;
+      if (sharded) {
+        // The layer's summed gradient, rank r's shard only.
+        const size_t count = m->block_len[l] / size_t(nranks);
+        TRY(tc_reducescatter(comm, d, block, block + size_t(rank) * count * e, count, TC_SUM, m->comm_stream));
+      } else {
+        TRY(tc_allreduce(comm, d, block, m->block_len[l], TC_SUM, m->comm_stream));
+      }
     }
     if (l > 0) {
       // H̄ = Wᵀ·Z̄, then H = relu(A): Ā += H̄ · MaxShare(A, 0).  Ā of the
@@ -394,6 +451,18 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     } else if (!m->prune) {
       TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->Xbar.p, 0, st));
     }
+    if (sharded) {
+      // Nothing of this step reads W_l or b_l any more (the side stream's
+      // vecmat read b_l before side_done[l]): update this rank's shard of
+      // the layer and gather every rank's.
+      TRY(check_cuda(cudaEventRecord(m->params_free[l], s), "event"));
+      TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->params_free[l], 0), "wait"));
+      const size_t count = m->block_len[l] / size_t(nranks);
+      const size_t mine = m->block_at[l] + size_t(rank) * count;
+      TRY(adam_range(mine, count, m->comm_stream));
+      char *block = static_cast<char *>(m->params.p) + m->block_at[l] * e;
+      TRY(tc_allgather(comm, d, block + size_t(rank) * count * e, block, count, m->comm_stream));
+    }
   }
   // Every side-stream result (b̄, ones̄) is complete before Adam and the
   // caller see them.
@@ -402,17 +471,9 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     TRY(check_cuda(cudaEventRecord(m->reduced, m->comm_stream), "event"));
     TRY(check_cuda(cudaStreamWaitEvent(s, m->reduced, 0), "wait"));
   }
-  // ---- Adam, per parameter in the order the driver updates them ----
-  m->steps += 1;
-  float c1, c2;
-  adam_coefficients(*m, m->steps, c1, c2);
-  const int resumed = m->steps > 1;
-  std::vector<tc_adam_tensor> params;
-  for (int l = 0; l < L; ++l) {
-    params.push_back({m->W[l].p, m->gW[l].p, m->mW[l].p, m->vW[l].p, m->W[l].n});
-    params.push_back({m->b[l].p, m->gb[l].p, m->mb[l].p, m->vb[l].p, m->b[l].n});
-  }
-  TRY(tc_adam_multi(d, params.data(), params.size(), resumed, m->rate, m->beta1, m->beta2, m->eps, c1, c2, st));
+  // ---- Adam over every parameter (one launch over the flat blocks; the
+  // padding between tensors is zero and is read by nothing) ----
+  if (!sharded) TRY(adam_range(0, m->total, s));
 #undef TRY
   return TC_OK;
 }

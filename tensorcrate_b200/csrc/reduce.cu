@@ -838,7 +838,7 @@ void fill_walk(Walk &w, const Dims &shape, const Dims &strides) {
   }
 }
 
-int scratch_get(size_t bytes, void **out) { return scratch(bytes, out); }
+int scratch_get(size_t bytes, void **out, cudaStream_t stream) { return scratch(bytes, out, stream); }
 
 // A variance's slices' means in T, when the path computing the variance
 // can write them too (`written` says whether it did).
@@ -876,7 +876,7 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     v.divisor = divisor;
     void *p = nullptr;
     const size_t groups = size_t(results) * size_t(v.chunks);
-    if (int st = scratch_get((groups + size_t(results)) * sizeof(float), &p)) return st;
+    if (int st = scratch_get((groups + size_t(results)) * sizeof(float), &p, stream)) return st;
     float *partial = static_cast<float *>(p), *means = partial + groups;
     const unsigned grid = unsigned(std::min<long long>((long long)groups, (long long)sms * 8));
     const unsigned fgrid = unsigned(std::min<long long>(results, (long long)sms * 8));
@@ -926,9 +926,9 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       int *tickets = nullptr;
       if (splits > 1) {
         void *p = nullptr;
-        if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p)) return st;
+        if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p, stream)) return st;
         partial = static_cast<Acc *>(p);
-        if (int st = counters(size_t(results), &tickets)) return st;
+        if (int st = counters(size_t(results), &tickets, stream)) return st;
       }
       static int resident_fast[7] = {0, 0, 0, 0, 0, 0, 0};
       if (!resident_fast[MODE]) {
@@ -979,7 +979,7 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     Acc *partial = nullptr;
     if (splits > 1) {
       void *p = nullptr;
-      if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p)) return st;
+      if (int st = scratch_get(size_t(results * splits) * sizeof(Acc), &p, stream)) return st;
       partial = static_cast<Acc *>(p);
     }
     const long long groups = results * splits;
@@ -1037,9 +1037,9 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
       int *tickets = nullptr;
       if (grid > 1) {
         void *p = nullptr;
-        if (int st = scratch_get(size_t(grid) * 2 * 1024 * sizeof(Acc), &p)) return st;
+        if (int st = scratch_get(size_t(grid) * 2 * 1024 * sizeof(Acc), &p, stream)) return st;
         partial = static_cast<Acc *>(p);
-        if (int st = counters(size_t(f.tiles), &tickets)) return st;
+        if (int st = counters(size_t(f.tiles), &tickets, stream)) return st;
       }
       reduce_cols_fast<T, MODE, 4><<<unsigned(grid), 256, 0, stream>>>(in, f, o, arg_out, partial, tickets);
       return check_launch("reduce (columns, fast)");
@@ -1062,7 +1062,7 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     Acc *partial = nullptr;
     if (ks > 1) {
       void *p = nullptr;
-      if (int st = scratch_get(size_t(ks) * size_t(a.kept_outer * a.K) * sizeof(Acc), &p)) return st;
+      if (int st = scratch_get(size_t(ks) * size_t(a.kept_outer * a.K) * sizeof(Acc), &p, stream)) return st;
       partial = static_cast<Acc *>(p);
     }
     if (four) reduce_cols<T, MODE, 4><<<grid, dim3(32, 8), 0, stream>>>(in, a, o, arg_out, partial);
@@ -1190,7 +1190,7 @@ int vector_fold(int dtype, const void *a, const void *b, size_t n, void *out, cu
   if (!out) return fail(TC_EINVAL, "vector reduce: null output");
   const int max_blocks = 2048;
   void *p = nullptr;
-  if (int st = scratch_get(max_blocks * sizeof(float), &p)) return st;
+  if (int st = scratch_get(max_blocks * sizeof(float), &p, stream)) return st;
   float *partials = static_cast<float *>(p);
   return with_real(dtype, [&](auto t) -> int {
     using T = decltype(t);

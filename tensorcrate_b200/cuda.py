@@ -75,7 +75,11 @@ def _stream(stream) -> C.c_void_p:
 # storage
 # ---------------------------------------------------------------------------
 class CudaStorage:
-    """A flat run of `len` elements of `dtype` in device memory."""
+    """A flat run of `len` elements of `dtype` in device memory.  Its block
+    comes from the library's pool in the default stream's order and goes
+    back in that order when the storage is dropped (tc_free_async), so a
+    storage dropped while kernels that use it are queued is not handed out
+    before they ran."""
 
     __slots__ = ("ptr", "len", "dtype", "_owned", "__weakref__")
 
@@ -85,7 +89,7 @@ class CudaStorage:
         self.dtype, self.len = dtype, int(length)
         if ptr is None:
             out = C.c_void_p()
-            N.call("tc_malloc", C.byref(out), max(1, self.len * ELEM[dtype][1]))
+            N.call("tc_malloc_async", C.byref(out), max(1, self.len * ELEM[dtype][1]), None)
             self.ptr, self._owned = out.value, True
         else:
             self.ptr, self._owned = int(ptr), False
@@ -136,7 +140,7 @@ class CudaStorage:
     def __del__(self):
         try:
             if self._owned and self.ptr and N._lib is not None:
-                N._lib.tc_free(self.ptr)
+                N._lib.tc_free_async(self.ptr, None)
         except Exception:  # interpreter shutdown
             pass
 

@@ -43,6 +43,12 @@ class Mlp:
         N.call("tc_mlp_grads", self.handle, l, w.ctypes.data, b.ctypes.data)
         return w, b
 
+    def block(self, l: int) -> tuple[int, int]:
+        """(length, bias offset) of layer l's block of the flat buffers."""
+        n, at = C.c_size_t(), C.c_size_t()
+        N.call("tc_mlp_block", self.handle, l, C.byref(n), C.byref(at))
+        return n.value, at.value
+
     def prune_leaves(self, prune: bool) -> None:
         N.call("tc_mlp_prune_leaves", self.handle, int(prune))
 

@@ -145,6 +145,58 @@ def check_data_parallel_step(comm, world, rank, sp, failures):
                 failures.append(f"rank {rank}: data-parallel layer {l} {name} differs by {err:.3g}")
 
 
+def check_data_parallel_bf16(comm, world, rank, sp, failures):
+    """bf16, the config's type: each rank's partial gradient is rounded to
+    bf16 by its own products, and NCCL adds the partials in bf16 with a
+    rounding per hop, so the data-parallel gradient is not the whole batch's
+    bit for bit.  Bound the difference on this rank's shard of every layer
+    block (the shard the sharded optimizer updates), then check the updated
+    parameters: the same bits on every rank, and within Adam's first-step
+    bounds of the whole-batch step."""
+    dims, gbatch = [256, 512, 256], 64
+    batch = gbatch // world
+    rng = np.random.default_rng(11)
+    weights = [xavier(dims[l + 1], dims[l], rng) for l in range(len(dims) - 1)]
+    biases = [rng.uniform(-0.05, 0.05, dims[l + 1]).astype(np.float32) for l in range(len(dims) - 1)]
+    x = rng.standard_normal((dims[0], gbatch)).astype(np.float32)
+    y = rng.standard_normal((dims[-1], gbatch)).astype(np.float32)
+    cols = slice(rank * batch, (rank + 1) * batch)
+    dp = Mlp("bf16", dims, batch, gbatch, beta2=0.99)
+    one = Mlp("bf16", dims, gbatch, gbatch, beta2=0.99)
+    dp.load(weights, biases)
+    one.load(weights, biases)
+    bits = lambda a: cuda.CudaStorage.store(cuda.f32_to_bits(np.ascontiguousarray(a).ravel(), "bf16"), "bf16")
+    dp.step(bits(x[:, cols]), bits(y[:, cols]), comm=comm, stream=torch.cuda.current_stream())
+    one.step(bits(x), bits(y), stream=torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    widen = lambda a: cuda.bits_to_f32(a, "bf16")
+    for l in range(len(dims) - 1):
+        length, at = dp.block(l)
+
+        def block(w, b):
+            out = np.zeros(length, np.float32)
+            out[:w.size] = widen(w)
+            out[at:at + b.size] = widen(b)
+            return out
+        got, want = block(*dp.grads(l)), block(*one.grads(l))
+        lo, hi = rank * length // world, (rank + 1) * length // world
+        err, scale = float(np.linalg.norm(got[lo:hi] - want[lo:hi])), float(np.linalg.norm(want[lo:hi]))
+        if not err <= world * 2.0 ** -7 * scale:
+            failures.append(f"rank {rank}: bf16 data-parallel layer {l} gradient shard off by {err:.3g} "
+                            f"(norm {scale:.3g})")
+        for name, p, q in zip(("weight", "bias"), dp.params(l), one.params(l)):
+            mine = torch.tensor(p.view(np.int16).astype(np.int64).sum(), device="cuda")
+            lowest, highest = mine.clone(), mine.clone()
+            torch.distributed.all_reduce(lowest, op=torch.distributed.ReduceOp.MIN)
+            torch.distributed.all_reduce(highest, op=torch.distributed.ReduceOp.MAX)
+            if int(lowest.item()) != int(highest.item()):
+                failures.append(f"rank {rank}: bf16 data-parallel layer {l} {name}s differ between ranks")
+            diff = np.abs(widen(p) - widen(q))
+            if not (np.max(diff) <= 2e-3 + 8e-3 and np.median(diff) <= 4e-3):
+                failures.append(f"rank {rank}: bf16 data-parallel layer {l} {name} off the whole-batch step by "
+                                f"max {np.max(diff):.3g}, median {np.median(diff):.3g}")
+
+
 def main() -> int:
     world, rank = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -155,7 +207,7 @@ def main() -> int:
     comm = nccl_comm(torch, world, rank)
     sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     failures: list[str] = []
-    for check in (check_matmul_allgather, check_reduction_shards, check_data_parallel_step):
+    for check in (check_matmul_allgather, check_reduction_shards, check_data_parallel_step, check_data_parallel_bf16):
         try:
             check(comm, world, rank, sp, failures)
         except Exception as e:  # a failed call is a failed check; every rank still reaches the end

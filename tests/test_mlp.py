@@ -150,3 +150,83 @@ def test_bf16_mlp_with_default_adam_is_nan_like_the_reference(device):
     m.step(xd, yd)
     w, _ = m.params(0)
     assert np.all(np.isnan(O.widen(w, "bf16")))
+
+
+CONFIG4 = [1024, 4096, 4096, 1024]
+CONFIG4_BATCH = 2048
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_mlp_step_matches_the_oracle_at_config_4(device, dtype):
+    """One training step at config 4's own size (1024-4096-4096-1024, batch
+    2048), which takes the tile plans, split-K products and row splits the
+    small network never reaches.  beta2 = 0.99: the configured 0.999 rounds
+    to 1.0 in bf16 and turns the reference's update into NaN.  The oracle's
+    products run on all host threads (same bits as its single thread)."""
+    import os
+
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp, xavier
+    dims, batch, beta2 = CONFIG4, CONFIG4_BATCH, 0.99
+    rng = np.random.default_rng(6)
+    ws = [xavier(dims[l + 1], dims[l], rng) for l in range(3)]
+    bs = [rng.uniform(-0.05, 0.05, dims[l + 1]).astype(np.float32) for l in range(3)]
+    x = normal((dims[0], batch), 4)
+    y = normal((dims[-1], batch), 5)
+    O.set_matmul_threads(os.cpu_count() or 1)
+    try:
+        h = _oracle(dtype, ws, bs, beta2, dims=dims, batch=batch)
+        loss_o = np.empty(1, O.STORE[dtype])
+        O.call("orc_mlp_step", h, O.ptr(O.narrow(x, dtype)), O.ptr(O.narrow(y, dtype)), O.ptr(loss_o), 0)
+    finally:
+        O.set_matmul_threads(1)
+    m = Mlp(dtype, dims, batch, beta2=beta2)
+    m.load(ws, bs)
+    loss_d = cuda.CudaStorage(dtype, 1)
+    m.step(cuda.CudaStorage.store(O.narrow(x, dtype), dtype), cuda.CudaStorage.store(O.narrow(y, dtype), dtype),
+           loss=loss_d)
+    tol = {"f32": 1e-4, "bf16": 4e-2}[dtype]
+    lg, lo = O.widen(loss_d.as_slice(), dtype)[0], O.widen(loss_o, dtype)[0]
+    # The loss sums 2M squares: the Host's running f32 sum drifts by about
+    # 1e-3 over that many terms, the device's tree by far less; the sums'
+    # contract is rel 1e-5*sqrt(K).
+    assert abs(lg - lo) <= max(tol, 1e-5 * np.sqrt(dims[-1] * batch)) * abs(lo), (lg, lo)
+    report = {}
+    for l in range(3):
+        gw, gb = m.grads(l)
+        ow, ob = _grads(h, l, dtype, dims=dims)
+        gw, gb = O.widen(gw, dtype).reshape(ow.shape), O.widen(gb, dtype)
+        w, b = m.params(l)
+        pw = np.empty(dims[l + 1] * dims[l], O.STORE[dtype])
+        pb = np.empty(dims[l + 1], O.STORE[dtype])
+        O.call("orc_mlp_params", h, l, O.ptr(pw), O.ptr(pb), 1)
+        diff = np.abs(O.widen(w, dtype) - O.widen(pw, dtype))
+        report[l] = {"max_rel": float(np.max(np.abs(gw - ow)) / np.max(np.abs(ow))),
+                     "norm_rel": float(np.linalg.norm(gw - ow) / np.linalg.norm(ow)),
+                     "bias_max_rel": float(np.max(np.abs(gb - ob)) / np.max(np.abs(ob))),
+                     "param_max": float(np.max(diff)), "param_median": float(np.median(diff)),
+                     # Adam's first step moves a parameter by about the rate either
+                     # way: parameters more than one rate apart moved opposite ways
+                     "opposite_moves": float(np.mean(diff > 1e-3))}
+    # A ReLU whose input sits within rounding of zero takes the other branch
+    # on one side (MaxShare is 1, 0.5 or 0): that sample's whole contribution
+    # to the gradients below it differs, about 1/sqrt(batch) of a gradient
+    # element.  The top layer's gradients see such flips only through the
+    # forward activations and are held element by element; the lower layers
+    # are held in norm.  After Adam's first step every
+    # parameter is within two rates (a gradient of the other sign moves it
+    # the other way), and few move opposite ways.
+    # (Measured on B200, f32: top layer 1.4e-4 of the largest element, the
+    # lower layers 2e-3 and 3e-4 in norm; bf16: 4e-3, 4e-3 and 1e-3.)
+    top = report[2]
+    top_tol = {"f32": 1e-3, "bf16": 4e-2}[dtype]
+    assert top["max_rel"] <= top_tol and top["bias_max_rel"] <= top_tol, report
+    for l in range(2):
+        assert report[l]["norm_rel"] <= 2e-2, report
+    ulp = {"f32": 1e-6, "bf16": 8e-3}[dtype]
+    for l in range(3):
+        assert report[l]["param_max"] <= 2 * 1e-3 + ulp, report
+        assert report[l]["param_median"] <= {"f32": 1e-6, "bf16": 4e-3}[dtype], report
+        assert report[l]["opposite_moves"] <= 1e-2, report
+    O.lib().orc_mlp_destroy(h)

@@ -1,10 +1,16 @@
-"""tc_vecmat_noalloc: the vecmat whose row-split partial sums live in a
-static device array, so that the call allocates nothing.  It must give the
-same bits as tc_vecmat on the same inputs, on two calls in a row (the second
-with other inputs, so stale partials would show), and refuse a shape whose
-partials do not fit the array.  This file is named to be collected last, so
-that the suite also runs it after every other test has used the library;
-run alone, it is the first user of the library in its process."""
+"""tc_vecmat_noalloc: the vecmat for callers that cannot allocate device
+memory -- those whose GPU memory another allocator has already claimed (a
+framework's caching allocator, a fixed arena), where a cudaMalloc from the
+library would fail or break that allocator's budget, and those under a hard
+latency budget, where cudaMalloc may block and synchronise the device.  Its
+row-split partial sums live in a static device array instead.  It must give
+the same bits as tc_vecmat on the same inputs, on two calls in a row (the
+second with other inputs, so stale partials would show), make no allocation
+and ask for no scratch while it runs (the library's own counters), and
+refuse a shape whose partials do not fit the array.  This file is named to
+be collected last, so that the suite also runs it after every other test has
+used the library; run alone, it is the first user of the library in its
+process."""
 from __future__ import annotations
 
 import ctypes as C
@@ -54,8 +60,23 @@ class Buffer:
         N.call("tc_free", self.ptr)
 
 
-def _shares(rows: int, cols: int, dtype: str, sms: int = 148) -> int:
-    """The row split tc_vecmat picks for a 16-byte-aligned matrix."""
+def _sm_count() -> int:
+    n = C.c_int(0)
+    N.call("tc_sm_count", C.byref(n))
+    return n.value
+
+
+def _alloc_counts() -> tuple[int, int]:
+    """(cudaMalloc calls the library made, scratch requests) so far."""
+    a, s = C.c_uint64(0), C.c_uint64(0)
+    N.call("tc_alloc_counts", C.byref(a), C.byref(s))
+    return a.value, s.value
+
+
+def _shares(rows: int, cols: int, dtype: str, sms: int | None = None) -> int:
+    """The row split tc_vecmat picks for a 16-byte-aligned matrix on a GPU
+    with `sms` SMs (the current device's when not given)."""
+    sms = _sm_count() if sms is None else sms
     cpt = 16 // (4 if dtype == "f32" else 2)
     if cols % cpt:
         cpt = 1
@@ -88,8 +109,13 @@ def test_matches_vecmat_on_two_calls_in_a_row(device, dtype, rows, cols):
     want = [Buffer(y_like.nbytes) for _ in xs]
     try:
         # Two calls in a row on one stream, then the allocating entry point.
+        # The library allocates nothing and asks for no scratch meanwhile
+        # (its first call on a device only looks the array's address up).
+        before = _alloc_counts()
         for x, y in zip(dx, got):
             N.call("tc_vecmat_noalloc", code, rows, cols, x.ptr, dm.ptr, y.ptr, None)
+        N.call("tc_stream_sync", None)
+        assert _alloc_counts() == before
         for x, y in zip(dx, want):
             N.call("tc_vecmat", code, rows, cols, x.ptr, dm.ptr, y.ptr, None)
         for g, w in zip(got, want):
