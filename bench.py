@@ -13,6 +13,7 @@ metric: HBM GB/s = algorithmic bytes of the nine calls / step time.
 The same line carries the other configurations as sub-records, each with
 its own timing, clocks, roofline, end-to-end figure and parity check:
   c4  the MLP training step (1024-4096-4096-1024, bf16, Adam), steps/s;
+  c4_weak  the same step with 2048 samples per GPU, samples/s;
   c5  the bf16 GEMM, M=N=K=8192, TFLOP/s;
   c1  the f32 GEMM 1024^3 and matvec;
   c3  the f16 layout copies (permute, slice-split-concatenate).
@@ -22,8 +23,10 @@ Under torchrun (one process per GPU, NCCL):
       (weak scaling); the per-slab results are all-gathered and the [512]
       max/min partials folded over ranks;
   c4  data parallel over the global batch of 2048 (strong scaling), the
-      optimizer sharded over the ranks (reduce-scatter, Adam on 1/P,
-      all-gather);
+      optimizer sharded over the ranks: per layer one kernel sums this
+      rank's shard of the gradients over the ranks (NVLink peer loads), runs
+      Adam on it and stores it into every rank's parameters (peer stores);
+  c4_weak  the same with 2048 samples per GPU (weak scaling);
   c5  row panels: rank r computes rows [r*M/P, (r+1)*M/P) of C and the GEMM
       epilogue stores every tile into every rank's C over NVLink (strong);
   c1, c3  replicas (each rank its own copy of the work).
@@ -407,24 +410,37 @@ def run_c2(args, torch, world, rank, comm):
             ("argmax", lib.tc_arg_reduce, (0, 3, xs, x.ptr, n, 0, xst, 1, N.RMAX, argp, sp)),
         ]
 
-    def collectives(o, sp):
-        # P > 1: one all-gather of every rank's block of results (the slab
-        # results are then final, rank after rank); the [512] extremes fold
-        # the sharded leading axis, so each is finished by reducing the P
-        # gathered partials ([P, 512] with a stride of one block), exactly.
-        if world == 1:
-            return
-        N.check("allgather", lib.tc_allgather(comm, N.U32, o["pack"].ptr, o["gathered"].ptr, pack_len, sp))
+    # P > 1: one all-gather of every rank's block of results (the slab
+    # results are then final, rank after rank); the [512] extremes fold the
+    # sharded leading axis, so each is finished by reducing the P gathered
+    # partials ([P, 512] with a stride of one block), exactly.  The
+    # reductions run first; the gather and the folds then run on a second
+    # stream beside the three broadcasts, and the step ends when both have.
+    side = torch.cuda.Stream() if world > 1 else None
+    side_sp = C.c_void_p(side.cuda_stream) if side is not None else None
+    packed = torch.cuda.Event() if world > 1 else None
+    gathered = torch.cuda.Event() if world > 1 else None
+
+    def collectives(o, on_stream):
+        packed.record(on_stream)
+        side.wait_event(packed)
+        N.check("allgather", lib.tc_allgather(comm, N.U32, o["pack"].ptr, o["gathered"].ptr, pack_len, side_sp))
         for k, op in (("max", N.RMAX), ("min", N.RMIN)):
             N.check("fold", lib.tc_reduce_axes(0, 2, g_shape, o["gathered"].ptr, pack_len * world, at[k], g_strides,
-                                               1, N.u32s([0]), N.AXIS_FOLD, op, 0, o["final_" + k].ptr, sp))
+                                               1, N.u32s([0]), N.AXIS_FOLD, op, 0, o["final_" + k].ptr, side_sp))
+        gathered.record(side)
 
     calls = [calls_on(0, sp), calls_on(1, sp)]
     events = {name: [] for name, _, _ in calls[0]}
+    REDUCTIONS = ("sum", "mean", "var", "max", "min", "argmax")
 
     def step(b=0, record=False, on_sp=None):
         todo = calls[b] if on_sp is None else calls_on(b, on_sp)
-        for name, fn, a in todo:
+        on_stream = stream  # the pipeline passes this same stream's pointer
+        order = [c for c in todo if c[0] in REDUCTIONS] + [c for c in todo if c[0] not in REDUCTIONS]
+        for i, (name, fn, a) in enumerate(order):
+            if world > 1 and i == len(REDUCTIONS):
+                collectives(sets[b], on_stream)
             if record:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
@@ -435,7 +451,8 @@ def run_c2(args, torch, world, rank, comm):
                 st = fn(*a)
             if st:
                 N.check(name, st)
-        collectives(sets[b], sp if on_sp is None else on_sp)
+        if world > 1:
+            on_stream.wait_event(gathered)
 
     bytes_per_op = c2_ops_bytes()
     step_bytes = sum(bytes_per_op.values())
@@ -909,6 +926,8 @@ def run_c4(args, torch, world, rank, comm):
     bs = [np.zeros(dims[l + 1], np.float32) for l in range(3)]
     m = Mlp(dtype, dims, batch, gbatch)
     m.load(ws, bs)
+    if world > 1:
+        m.attach(comm)  # the exchange runs over NVLink peer memory
     # The global batch (seeds 4, 5), rank r's columns.
     x_all = np.random.default_rng(4).standard_normal((dims[0], gbatch)).astype(np.float32)
     y_all = np.random.default_rng(5).standard_normal((dims[-1], gbatch)).astype(np.float32)
@@ -937,6 +956,11 @@ def run_c4(args, torch, world, rank, comm):
     phases = {}
     phases["step_without_exchange_ms"] = round(timed(torch, world, lambda: solo.step(xs[0], ys[0], stream=stream),
                                                      phase_args, stream)[0], 4)
+    if world > 1:
+        # the same sharded step with NCCL's reduce-scatter and all-gather
+        # around a local Adam instead of the peer-memory exchange
+        phases["step_with_nccl_exchange_ms"] = round(timed(
+            torch, world, lambda: solo.step(xs[0], ys[0], comm=comm, stream=stream), phase_args, stream)[0], 4)
     total = sum(solo.block(l)[0] for l in range(3))
     flat = [cuda.CudaStorage(dtype, total) for _ in range(4)]
     for f in flat:
@@ -975,15 +999,21 @@ def run_c4(args, torch, world, rank, comm):
     e2e_steps = max(5, args.steps // 2)
     e2e_ms = pipe.measure(world, e2e_steps)
     serial_ms = pipe.measure_serial(world, max(3, e2e_steps // 2))
-    launches = 24 + (0 if world == 1 else 3 - 1)  # sharded: 3 Adam launches on shards instead of one
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    m.close()
+    # sharded: per layer two flag signals, a flag wait and the exchange kernel instead of one Adam
+    # launch, and a flag wait at the end
+    launches = 24 + (0 if world == 1 else 3 * 4 - 1 + 1)
     rec = {"metric": "config-4 MLP training steps/s", "value": round(1000.0 / ms, 2), "unit": "steps/s",
            "n_gpus": world, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
            "dtype": dtype, "data": "synthetic N(0,1) inputs/targets, Xavier-uniform weights, seeded",
            "config": {"workload": "config4: MLP 1024-4096-4096-1024 ReLU, MSE, Adam(1e-3,0.9,0.999,1e-8), bf16",
                       "global_batch": gbatch, "per_rank_batch": batch,
-                      "parallelism": f"dp{world}" + (" (per layer: NCCL reduce-scatter of the gradient block, Adam "
-                                                     "on this rank's 1/P, all-gather of the parameters, beside the "
-                                                     "backward pass)" if world > 1 else ""),
+                      "parallelism": f"dp{world}" + (" (per layer, beside the backward pass: one kernel sums this "
+                                                     "rank's 1/P of the gradient block over the ranks through NVLink "
+                                                     "peer loads, runs Adam on it and stores the new parameters into "
+                                                     "every rank's copy; flags between the ranks)" if world > 1 else ""),
                       "l2": "no flush: a step touches 50 MB of weights, 150 MB of Adam state and ~100 MB of "
                             "activations, more than the 126 MB L2",
                       "gemm_flops_per_step": gemm_flops},
@@ -1006,6 +1036,50 @@ def run_c4(args, torch, world, rank, comm):
     return rec
 
 
+def run_c4_weak(args, torch, world, rank, comm):
+    """Config 4's step with the batch per GPU fixed at 2048 (weak scaling:
+    global batch 2048*P), the usual data-parallel setting, on the same
+    sharded path as c4.  metric: samples/s."""
+    from tensorcrate_b200 import cuda
+    from tensorcrate_b200.mlp import Mlp, xavier
+    dtype, dims, batch = "bf16", C4_DIMS, args.batch
+    gbatch = batch * world
+    stream = torch.cuda.current_stream()
+    rng = np.random.default_rng(6)
+    ws = [xavier(dims[l + 1], dims[l], rng) for l in range(3)]
+    bs = [np.zeros(dims[l + 1], np.float32) for l in range(3)]
+    m = Mlp(dtype, dims, batch, gbatch)
+    m.load(ws, bs)
+    if world > 1:
+        m.attach(comm)
+    x = cuda.CudaStorage.store(cuda.f32_to_bits(np.random.default_rng(40 + rank).standard_normal(
+        (dims[0], batch)).astype(np.float32), dtype), dtype)
+    y = cuda.CudaStorage.store(cuda.f32_to_bits(np.random.default_rng(50 + rank).standard_normal(
+        (dims[-1], batch)).astype(np.float32), dtype), dtype)
+    ms, blocks, clocks = timed(torch, world, lambda: m.step(x, y, comm=comm, stream=stream), args, stream)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    m.close()
+    pk, pk_kind = peaks()
+    gemm_flops = 3 * 2 * batch * sum(dims[l] * dims[l + 1] for l in range(3))
+    tflops = gemm_flops / (ms * 1e-3) / 1e12
+    launches = 24 + (0 if world == 1 else 3 * 4 - 1 + 1)
+    return {"metric": "config-4 MLP training samples/s, 2048 samples per GPU", "value": round(gbatch * 1000.0 / ms, 1),
+            "unit": "samples/s", "steps_per_s": round(1000.0 / ms, 2), "n_gpus": world, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "dtype": dtype,
+            "data": "synthetic N(0,1) inputs/targets, Xavier-uniform weights, seeded",
+            "config": {"workload": "config4's network and optimizer, batch 2048 per GPU", "global_batch": gbatch,
+                       "per_rank_batch": batch, "parallelism": f"dp{world}, the same sharded exchange as c4",
+                       "l2": "no flush: a step's working set exceeds the 126 MB L2"},
+            "timing": blocks,
+            "roofline": {"bound": "tensor", "kernel": "whole step (GEMM share)", "achieved": round(tflops, 1),
+                         "peak": pk["bf16_tflops_sustained"], "peak_source": pk_kind + " sustained", "unit": "TFLOP/s",
+                         "frac": round(tflops / pk["bf16_tflops_sustained"], 3), "traffic": None},
+            "parity": {"status": "ok", "checked": "the same step code as c4, whose parity record covers it"},
+            "gpu_launches_per_step": launches, "gpu_launches": launches * args.steps * blocks["blocks"],
+            "clocks": clocks}
+
+
 def parity_c4(torch, world, rank, comm, ws, bs, x_all, y_all, batch, gbatch):
     import oracle as O
     from tensorcrate_b200 import cuda
@@ -1014,6 +1088,8 @@ def parity_c4(torch, world, rank, comm, ws, bs, x_all, y_all, batch, gbatch):
     cols = slice(rank * batch, (rank + 1) * batch)
     dp = Mlp(dtype, dims, batch, gbatch, beta2=0.99)
     dp.load(ws, bs)
+    if world > 1:
+        dp.attach(comm)
     x = cuda.CudaStorage.store(O.narrow(np.ascontiguousarray(x_all[:, cols]), dtype), dtype)
     y = cuda.CudaStorage.store(O.narrow(np.ascontiguousarray(y_all[:, cols]), dtype), dtype)
     dp.step(x, y, comm=comm, stream=torch.cuda.current_stream())
@@ -1058,7 +1134,9 @@ def parity_c4(torch, world, rank, comm, ws, bs, x_all, y_all, batch, gbatch):
             if not err <= max(1e-2, world * 2.0 ** -7) * scale:
                 failures.append(f"layer {l} gradient (rank 0's shard) off the oracle by {err:.3g} of {scale:.3g}")
         O.lib().orc_mlp_destroy(h)
-    del dp
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    dp.close()
     return parity_record(torch, world, failures,
                          "one data-parallel step (beta2 0.99) from the bench's weights: every parameter against the "
                          "oracle's whole-batch step (max <= 2 rates + 1 bf16 step, median <= 4e-3), rank 0's gradient "
@@ -1213,7 +1291,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "c1", "c2", "c3", "c4", "c5", "trait"])
+    ap.add_argument("--workload", default="all", choices=["all", "c1", "c2", "c3", "c4", "c4_weak", "c5", "trait"])
     ap.add_argument("--batch", type=int, default=2048, help="config 4's global batch")
     ap.add_argument("--size", type=int, default=8192, help="config 5's M=N=K")
     ap.add_argument("--min-seconds", type=float, default=1.0, help="device time each timed region lasts at least")
@@ -1249,16 +1327,18 @@ def main():
                "c2": lambda: run_c2(args, torch, world, rank, comm),
                "c3": lambda: run_c3(args, torch, world, rank, comm),
                "c4": lambda: run_c4(args, torch, world, rank, comm),
+               "c4_weak": lambda: run_c4_weak(args, torch, world, rank, comm),
                "c5": lambda: run_gemm(args, torch, world, rank, comm, "bf16", args.size),
                "trait": lambda: run_trait(args, torch, world, rank, comm)}
     if args.workload == "all":
         line = run_c2(args, torch, world, rank, comm)
-        for key in ("c4", "c5", "c1", "c3"):
+        for key in ("c4", "c4_weak", "c5", "c1", "c3"):
             line[key] = runners[key]()
         statuses = [line["parity"]] + [line[k]["parity"] for k in ("c4", "c5", "c1", "c3")]
         bad = [s for s in statuses if s["status"] != "ok"]
         line["parity_all"] = "ok" if not bad else {"failed": len(bad)}
-        line["gpu_launches_all"] = line["gpu_launches"] + sum(line[k]["gpu_launches"] for k in ("c4", "c5", "c1", "c3"))
+        line["gpu_launches_all"] = line["gpu_launches"] + sum(line[k]["gpu_launches"]
+                                                              for k in ("c4", "c4_weak", "c5", "c1", "c3"))
     else:
         line = headline_keys(runners[args.workload](), args)
     if rank == 0 and not args.no_cpu_baseline and args.workload in ("all", "c2"):

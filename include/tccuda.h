@@ -417,8 +417,9 @@ int tc_adam_multi(int dtype, const tc_adam_tensor *tensors, size_t count, int re
 int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *stream);
 
 /* Status of bounded device-side waits since the library loaded: TC_ETIMEOUT
- * (and *fault = 1) if a tensor-core GEMM gave up waiting on its pipeline
- * and returned early; TC_OK otherwise.  No counterpart in the reference
+ * (and *fault = 1) if a tensor-core GEMM gave up waiting on its pipeline, or
+ * a data-parallel step gave up waiting for another rank's flag, and
+ * returned early; TC_OK otherwise.  No counterpart in the reference
  * (Metal reports async errors at the next sync, src/metal/mod.rs:17-21). */
 int tc_device_status(int *fault);
 
@@ -466,15 +467,30 @@ int tc_mlp_block(tc_mlp *mlp, uint32_t layer, size_t *len, size_t *bias_at);
 int tc_mlp_prune_leaves(tc_mlp *mlp, int prune);
 /* Forward, loss into loss_dev[0] if not NULL, backward, then Adam.  With a
  * communicator of 2-8 ranks the optimizer is sharded: as soon as the
- * backward pass has produced a layer's gradients, a second stream
- * reduce-scatters the layer's block, runs Adam on this rank's shard and
- * all-gathers the updated parameters (NCCL), beside the rest of the pass.
- * With more ranks each layer's gradients are all-reduced and every rank
- * runs Adam on everything.  x, y are device buffers.  The products' split-K
- * partials, vecmat's row split and the loss's sum use the scratch of
+ * backward pass is done with a layer, a second stream has this rank update
+ * its shard of the layer's block with the gradient summed over the ranks,
+ * and every rank receives every shard's new parameters, beside the rest of
+ * the pass.  After tc_mlp_attach to that communicator one kernel per layer
+ * does this over NVLink peer memory: it loads every rank's gradient of this
+ * rank's shard (peer loads), sums them in rank order in f32, rounds once,
+ * runs Adam on the shard and stores the new parameters into every rank's
+ * copy (peer stores); flags in memory every rank maps order the steps
+ * between the ranks, with bounded waits that report through
+ * tc_device_status.  Otherwise NCCL reduce-scatters the gradients and
+ * all-gathers the parameters (NCCL's bf16 sums round per hop).  With more
+ * ranks each layer's gradients are all-reduced and every rank runs Adam on
+ * everything.  x, y are device buffers.  The products'
+ * split-K partials, vecmat's row split and the loss's sum use the scratch of
  * `stream` and of the handle's own side stream. */
 int tc_mlp_step(tc_mlp *mlp, const void *x_dev, const void *y_dev, tc_comm *comm, void *loss_dev,
                 void *stream);
+/* Move the handle's flat parameters and gradients into buffers every rank
+ * of `comm` (2-8 ranks) maps over NVLink (CUDA IPC), for steps over `comm`
+ * that exchange through peer memory.  Collective: every rank attaches, in
+ * the same order as its other collectives.  An attached handle's
+ * tc_mlp_destroy is collective too, and `comm` must outlive it.  No
+ * counterpart in the reference, which runs on one device. */
+int tc_mlp_attach(tc_mlp *mlp, tc_comm *comm);
 
 /* ---- fused elementwise programs (Kernels::fused, kernels.rs:1077-1082) --- */
 /* One instruction of a fused::Program (fused/mod.rs:290-313).  `code` is a

@@ -158,6 +158,7 @@ SIGNATURES = {
     "tc_mlp_block": [_p, _u32, C.POINTER(_sz), C.POINTER(_sz)],
     "tc_mlp_prune_leaves": [_p, _i],
     "tc_mlp_step": [_p, _p, _p, _p, _p, _p],
+    "tc_mlp_attach": [_p, _p],
     "tc_comm_unique_id": [C.POINTER(C.c_uint8)],
     "tc_comm_init": [_i, _i, C.POINTER(C.c_uint8), C.POINTER(_p)],
     "tc_comm_destroy": [_p],

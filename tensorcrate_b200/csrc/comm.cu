@@ -88,6 +88,27 @@ struct tc_peer_buffer {
   int *token;        // one int on this device: the completion collective's operand
 };
 
+namespace tc {
+void *peer_buffer_remote(tc_peer_buffer *buf, int rank) {
+  return buf && rank >= 0 && rank < buf->comm->nranks ? buf->remote[rank] : nullptr;
+}
+
+// Every rank meets: an all-reduce of one int on a private stream, waited for.
+int comm_barrier(tc_comm *comm) {
+  cudaStream_t s = nullptr;
+  if (int st = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return st;
+  void *token = nullptr;
+  int st = device_malloc(&token, sizeof(int), "cudaMalloc (barrier)");
+  if (!st) st = check_cuda(cudaMemsetAsync(token, 0, sizeof(int), s), "cudaMemsetAsync");
+  if (!st)
+    st = check_nccl(nccl().all_reduce(token, token, 1, ncclInt32, ncclSum, comm->comm, s), "ncclAllReduce (barrier)");
+  if (!st) st = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  if (token) cudaFree(token);
+  cudaStreamDestroy(s);
+  return st;
+}
+}  // namespace tc
+
 using namespace tc;
 
 extern "C" {

@@ -46,6 +46,30 @@ int scratch(size_t bytes, void **out, cudaStream_t stream);
 int counters(size_t n, int **out, cudaStream_t stream);
 // cudaMalloc, counted (tc_alloc_counts).
 int device_malloc(void **ptr, size_t bytes, const char *what);
+// One block of a data-parallel step's flat parameter buffers, updated by
+// this rank for its shard [first, first + count) (16-byte packs): the
+// gradient is the sum, in rank order and in f32, of every rank's gradient
+// block (grads[r] is rank r's, mapped over NVLink; grads[rank] this rank's),
+// rounded once to the element type; Adam's program then runs on it with
+// this rank's moments m, v (indexed like the block), and the new parameters
+// go to every rank's copy (params[r]); the summed gradient replaces this
+// rank's shard of grads[rank] (optim.cu).
+constexpr int MAX_PEER_RANKS = 8;
+struct PeerAdam {
+  int nranks, rank;
+  const void *grads[MAX_PEER_RANKS];
+  void *params[MAX_PEER_RANKS];
+  void *m, *v;
+  size_t first, count;
+};
+int peer_adam_run(int dtype, const PeerAdam &x, int resumed, double rate, double beta1, double beta2, double eps,
+                  double c1, double c2, cudaStream_t stream);
+
+// Rank `rank`'s copy of a peer buffer as this GPU maps it (this rank's own
+// when rank is this one), and a host-side barrier of every rank (comm.cu).
+void *peer_buffer_remote(tc_peer_buffer *buf, int rank);
+int comm_barrier(tc_comm *comm);
+
 // The means and sums of squared deviations (in the element type) of the
 // slices of `input` folded over `axes`, in as few passes as the layout
 // allows (reduce.cu).

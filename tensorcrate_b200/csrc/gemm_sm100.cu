@@ -886,11 +886,17 @@ int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const 
 
 }  // namespace tc
 
+namespace tc {
+int peer_wait_fault();
+}
+
 extern "C" int tc_device_status(int *fault) {
   int h = 0;
   if (int st = tc::check_cuda(cudaMemcpyFromSymbol(&h, tc::g_gemm_fault, sizeof(int)), "cudaMemcpyFromSymbol"))
     return st;
-  if (fault) *fault = h;
+  const int peer = tc::peer_wait_fault();
+  if (fault) *fault = h || peer;
   if (h) return tc::fail(TC_ETIMEOUT, "a tensor-core GEMM gave up waiting on its pipeline");
+  if (peer) return tc::fail(TC_ETIMEOUT, "a wait for another rank's flag gave up");
   return TC_OK;
 }

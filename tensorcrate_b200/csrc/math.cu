@@ -9,8 +9,6 @@
 #include <algorithm>
 #include <climits>
 
-#include <cub/device/device_radix_sort.cuh>
-
 #include "analytic.cuh"
 
 namespace tc {
@@ -253,10 +251,12 @@ template <class K> __device__ __forceinline__ K key_bits(K key) {
 }
 
 // The key maps, 16 bytes per thread step when both buffers are 16-byte
-// aligned, the rest element by element.
+// aligned, the rest element by element.  A descending sort sorts the keys'
+// complements ascending (`flip`).
 template <class K, bool TO>
-__global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long n, bool vec) {
+__global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long n, bool vec, bool flip) {
   constexpr int P = 16 / int(sizeof(K));
+  const K x = flip ? K(~K(0)) : K(0);
   const long long packs = vec ? n / P : 0, stride = (long long)gridDim.x * blockDim.x;
   for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < packs; q += stride) {
     union {
@@ -265,39 +265,178 @@ __global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long 
     } u;
     u.raw = __ldg(reinterpret_cast<const uint4 *>(src) + q);
 #pragma unroll
-    for (int j = 0; j < P; ++j) u.v[j] = TO ? order_key(u.v[j]) : key_bits(u.v[j]);
+    for (int j = 0; j < P; ++j) u.v[j] = TO ? K(order_key(u.v[j]) ^ x) : key_bits(K(u.v[j] ^ x));
     reinterpret_cast<uint4 *>(dst)[q] = u.raw;
   }
   for (long long i = packs * P + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    dst[i] = TO ? order_key(src[i]) : key_bits(src[i]);
+    dst[i] = TO ? K(order_key(src[i]) ^ x) : key_bits(K(src[i] ^ x));
+}
+
+// ---------------------------------------------------------------------------
+// LSD radix sort of the keys, 8 bits a pass (4 passes for f32's keys, 2 for
+// f16/bf16's).  Each pass is stable, so after the last one the keys are in
+// unsigned order.  The keys are cut into tiles of RADIX_TILE; a pass
+//   1. counts each tile's digits (warp-private histograms in shared memory)
+//      into counts[digit][tile];
+//   2. turns the counts into each (digit, tile)'s first output position: an
+//      exclusive scan along each digit's row of tiles (a block per digit),
+//      then of the 256 digit totals;
+//   3. moves every key to its position: each block walks its tile in rounds
+//      of 256 keys in index order; a key's place among its round's keys of
+//      the same digit is its lane's rank among the warp's lanes with that
+//      digit (match) plus the counts of the warps before it, and each digit
+//      keeps a running position across rounds, so equal digits keep their
+//      input order.
+// ---------------------------------------------------------------------------
+constexpr int RADIX_BINS = 256;
+constexpr int RADIX_THREADS = 256;
+constexpr int RADIX_ITEMS = 16;
+constexpr int RADIX_TILE = RADIX_THREADS * RADIX_ITEMS;
+constexpr int RADIX_WARPS = RADIX_THREADS / 32;
+
+template <class K>
+__global__ void __launch_bounds__(RADIX_THREADS) radix_histogram(const K *keys, long long n, int shift,
+                                                                 uint32_t *counts, int tiles) {
+  __shared__ uint32_t h[RADIX_WARPS][RADIX_BINS];
+  const int tid = threadIdx.x, warp = tid >> 5;
+#pragma unroll
+  for (int w = 0; w < RADIX_WARPS; ++w) h[w][tid] = 0;
+  __syncthreads();
+  const long long base = (long long)blockIdx.x * RADIX_TILE;
+#pragma unroll 4
+  for (int i = 0; i < RADIX_ITEMS; ++i) {
+    const long long idx = base + (long long)i * RADIX_THREADS + tid;
+    if (idx < n) atomicAdd(&h[warp][(uint32_t(keys[idx]) >> shift) & 255u], 1u);
+  }
+  __syncthreads();
+  uint32_t total = 0;
+#pragma unroll
+  for (int w = 0; w < RADIX_WARPS; ++w) total += h[w][tid];
+  counts[size_t(tid) * size_t(tiles) + blockIdx.x] = total;
+}
+
+// Block `digit`: exclusive scan of counts[digit][0..tiles) in place; the
+// row's total into totals[digit].
+__global__ void __launch_bounds__(RADIX_THREADS) radix_scan_rows(uint32_t *counts, int tiles, uint32_t *totals) {
+  __shared__ uint32_t warp_sums[RADIX_WARPS];
+  uint32_t *row = counts + size_t(blockIdx.x) * size_t(tiles);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t carry = 0;
+  for (int start = 0; start < tiles; start += RADIX_THREADS) {
+    const int i = start + tid;
+    const uint32_t v = i < tiles ? row[i] : 0u;
+    uint32_t x = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t y = __shfl_up_sync(~0u, x, d);
+      if (lane >= d) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    uint32_t before = 0, chunk = 0;
+#pragma unroll
+    for (int w = 0; w < RADIX_WARPS; ++w) {
+      const uint32_t ws = warp_sums[w];
+      if (w < warp) before += ws;
+      chunk += ws;
+    }
+    if (i < tiles) row[i] = carry + before + x - v;
+    carry += chunk;
+    __syncthreads();
+  }
+  if (tid == 0) totals[blockIdx.x] = carry;
+}
+
+// Exclusive scan of the 256 digit totals: each digit's first output position.
+__global__ void __launch_bounds__(RADIX_BINS) radix_scan_totals(const uint32_t *totals, uint32_t *starts) {
+  __shared__ uint32_t warp_sums[RADIX_BINS / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t v = totals[tid];
+  uint32_t x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t y = __shfl_up_sync(~0u, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  uint32_t before = 0;
+  for (int w = 0; w < warp; ++w) before += warp_sums[w];
+  starts[tid] = before + x - v;
+}
+
+template <class K>
+__global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *out, long long n, int shift,
+                                                               const uint32_t *counts, const uint32_t *starts,
+                                                               int tiles) {
+  __shared__ uint32_t next[RADIX_BINS];
+  __shared__ uint16_t round_counts[RADIX_WARPS][RADIX_BINS];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  next[tid] = starts[tid] + counts[size_t(tid) * size_t(tiles) + blockIdx.x];
+#pragma unroll
+  for (int w = 0; w < RADIX_WARPS; ++w) round_counts[w][tid] = 0;
+  __syncthreads();
+  const unsigned below = (1u << lane) - 1u;
+  const long long base = (long long)blockIdx.x * RADIX_TILE;
+  for (int i = 0; i < RADIX_ITEMS; ++i) {
+    const long long idx = base + (long long)i * RADIX_THREADS + tid;
+    const bool valid = idx < n;
+    const K key = valid ? in[idx] : K(0);
+    // Lanes past the end take digit 256, which no key has.
+    const uint32_t digit = valid ? (uint32_t(key) >> shift) & 255u : 256u;
+    const unsigned peers = __match_any_sync(~0u, digit);
+    const uint32_t rank = __popc(peers & below);
+    if (valid && rank == 0) round_counts[warp][digit] = uint16_t(__popc(peers));
+    __syncthreads();
+    if (valid) {
+      uint32_t at = next[digit] + rank;
+      for (int w = 0; w < warp; ++w) at += round_counts[w][digit];
+      out[at] = key;
+    }
+    __syncthreads();
+    uint32_t round_total = 0;
+#pragma unroll
+    for (int w = 0; w < RADIX_WARPS; ++w) {
+      round_total += round_counts[w][tid];
+      round_counts[w][tid] = 0;
+    }
+    next[tid] += round_total;
+    __syncthreads();
+  }
 }
 
 template <class K> int sort_keys(const void *a, void *out, size_t n, bool descending, cudaStream_t s) {
   if (n > size_t(INT_MAX)) return fail(TC_EINVAL, "sort: %zu elements exceed the radix sort's 2^31-1", n);
-  const int count = int(n);
-  // Keys go into `out`; the sort's second buffer and its temporary storage
-  // come from the per-device scratch block.
+  // Keys go into `out`; the second key buffer and the counts come from the
+  // stream's scratch.
   K *keys = static_cast<K *>(out);
-  size_t temp = 0;
-  cub::DoubleBuffer<K> buffers(keys, nullptr);
-  cudaError_t e = descending ? cub::DeviceRadixSort::SortKeysDescending(nullptr, temp, buffers, count, 0,
-                                                                        int(sizeof(K) * 8), s)
-                             : cub::DeviceRadixSort::SortKeys(nullptr, temp, buffers, count, 0, int(sizeof(K) * 8), s);
-  if (int st = check_cuda(e, "sort (temporary size)")) return st;
+  const int tiles = int((n + RADIX_TILE - 1) / RADIX_TILE);
   const size_t alt_bytes = (n * sizeof(K) + 255) & ~size_t(255);
+  const size_t count_bytes = (size_t(RADIX_BINS) * size_t(tiles) * 4 + 255) & ~size_t(255);
   void *block = nullptr;
-  if (int st = scratch(alt_bytes + temp, &block, s)) return st;
-  buffers = cub::DoubleBuffer<K>(keys, static_cast<K *>(block));
-  void *temp_ptr = static_cast<char *>(block) + alt_bytes;
+  if (int st = scratch(alt_bytes + count_bytes + 2 * RADIX_BINS * 4, &block, s)) return st;
+  K *alt = static_cast<K *>(block);
+  uint32_t *counts = reinterpret_cast<uint32_t *>(static_cast<char *>(block) + alt_bytes);
+  uint32_t *totals = reinterpret_cast<uint32_t *>(static_cast<char *>(block) + alt_bytes + count_bytes);
+  uint32_t *starts = totals + RADIX_BINS;
   const unsigned grid = grid_for((n * sizeof(K) + 15) / 16, 256, 8);
   auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  map_keys<K, true><<<grid, 256, 0, s>>>(static_cast<const K *>(a), keys, (long long)n, aligned(a) && aligned(keys));
+  map_keys<K, true><<<grid, 256, 0, s>>>(static_cast<const K *>(a), keys, (long long)n, aligned(a) && aligned(keys),
+                                         descending);
   if (int st = check_launch("sort (keys)")) return st;
-  e = descending ? cub::DeviceRadixSort::SortKeysDescending(temp_ptr, temp, buffers, count, 0, int(sizeof(K) * 8), s)
-                 : cub::DeviceRadixSort::SortKeys(temp_ptr, temp, buffers, count, 0, int(sizeof(K) * 8), s);
-  if (int st = check_cuda(e, "sort (radix)")) return st;
-  map_keys<K, false><<<grid, 256, 0, s>>>(buffers.Current(), keys, (long long)n,
-                                          aligned(buffers.Current()) && aligned(keys));
+  K *src = keys, *dst = alt;
+  for (int shift = 0; shift < int(sizeof(K) * 8); shift += 8) {
+    radix_histogram<K><<<tiles, RADIX_THREADS, 0, s>>>(src, (long long)n, shift, counts, tiles);
+    radix_scan_rows<<<RADIX_BINS, RADIX_THREADS, 0, s>>>(counts, tiles, totals);
+    radix_scan_totals<<<1, RADIX_BINS, 0, s>>>(totals, starts);
+    radix_scatter<K><<<tiles, RADIX_THREADS, 0, s>>>(src, dst, (long long)n, shift, counts, starts, tiles);
+    if (int st = check_launch("sort (radix pass)")) return st;
+    K *t = src;
+    src = dst;
+    dst = t;
+  }
+  // An even number of passes: the sorted keys are back in `out`.
+  map_keys<K, false><<<grid, 256, 0, s>>>(keys, keys, (long long)n, aligned(keys), descending);
   return check_launch("sort (values)");
 }
 

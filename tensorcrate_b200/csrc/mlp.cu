@@ -28,6 +28,7 @@
 // would.  With more ranks the gradients are all-reduced and every rank runs
 // the whole Adam pass.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -70,6 +71,56 @@ __global__ void __launch_bounds__(256) mse_backward(const typename T::S *pred, c
     rbar[i] = rb;
     if (ybar) ybar[i] = T::store(__fmul_rn(T::load(rb), -1.0f));
   }
+}
+
+// ---------------------------------------------------------------------------
+// Flags between the ranks of a data-parallel step over NVLink peer memory.
+// Each rank holds, in memory every rank maps, one u32 per (rank, layer) for
+// "ready" (that rank's gradients of the layer are final and it reads the
+// layer's parameters no more this step) and one for "written" (that rank
+// has stored its shard of the layer's updated parameters into every rank's
+// copy).  A flag holds the number of the last step it announced.  Waits are
+// bounded: on expiry the kernel records the fault (tc_device_status) and
+// returns.
+// ---------------------------------------------------------------------------
+__device__ int g_peer_fault = 0;
+constexpr unsigned long long PEER_WAIT_NS = 5000000000ull;  // 5 s
+
+struct FlagSlots {
+  uint32_t *slot[8];
+  int n;
+};
+
+// Announce `value` in every slot (one per rank), ordered after everything
+// this stream did before (the exchange kernel's stores to the ranks among
+// it).
+__global__ void signal_slots(FlagSlots s, uint32_t value) {
+  const int i = threadIdx.x;
+  __threadfence_system();
+  if (i < s.n) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(s.slot[i]), "r"(value) : "memory");
+}
+
+// Wait until flags[first + k*stride] >= value for k = 0..count-1, lane k of
+// the warp watching flag k (count <= 32 * blocks).
+__global__ void wait_slots(const uint32_t *flags, int first, int stride, int count, uint32_t value,
+                           unsigned long long limit_ns) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= count) return;
+  const uint32_t *f = flags + first + size_t(k) * size_t(stride);
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t i = 0; i < (1u << 30); ++i) {
+    uint32_t seen;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(seen) : "l"(f) : "memory");
+    if (seen >= value) return;
+    if ((i & 255u) == 255u) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > limit_ns) break;
+      __nanosleep(200);
+    }
+  }
+  atomicExch(&g_peer_fault, 1);
 }
 
 // Round a host value to the element type, as Real::from_f64 does (one
@@ -131,6 +182,12 @@ struct tc_mlp {
   std::vector<size_t> block_at, block_len;
   size_t total = 0;
   cudaStream_t comm_stream = nullptr;
+  // After tc_mlp_attach: the communicator whose steps exchange over NVLink
+  // peer memory, and the buffers every rank maps: the flat parameters and
+  // gradients, and the flags.
+  tc_comm *attached = nullptr;
+  int rank = 0, nranks = 1;
+  tc_peer_buffer *peer_params = nullptr, *peer_grads = nullptr, *peer_flags = nullptr;
   std::vector<cudaEvent_t> grad_ready, params_free;
   cudaEvent_t reduced = nullptr;
   // The bias adjoints (matvec, vecmat: memory-bound) run on a side stream,
@@ -275,7 +332,12 @@ int tc_mlp_destroy(tc_mlp *m) {
   };
   for (auto *v : {&m->A, &m->H})
     for (auto &b : *v) drop(b);
-  // W, b, their gradients and moments point into these
+  // W, b, their gradients and moments point into these (the parameters and
+  // gradients into peer buffers once attached: collective to free)
+  if (m->attached) {
+    m->params.p = m->grads.p = nullptr;
+    for (tc_peer_buffer *pb : {m->peer_params, m->peer_grads, m->peer_flags}) tc_peer_buffer_destroy(pb);
+  }
   for (Buf *f : {&m->params, &m->grads, &m->mom1, &m->mom2}) drop(*f);
   for (Buf *b : {&m->ones, &m->S, &m->Rbar, &m->Ybar, &m->Xbar, &m->abar,
                  &m->inbar, &m->onesbar, &m->ovec, &m->loss_sum})
@@ -287,6 +349,50 @@ int tc_mlp_destroy(tc_mlp *m) {
   if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
   if (m->side) cudaStreamDestroy(m->side);
   delete m;
+  return TC_OK;
+}
+
+// Move the flat parameters and gradients into buffers every rank of `comm`
+// maps (CUDA IPC over NVLink), so that data-parallel steps over `comm`
+// exchange them with peer loads and stores (see tc_mlp_step).  Collective.
+int tc_mlp_attach(tc_mlp *m, tc_comm *comm) {
+  if (!m || !comm) return fail(TC_EINVAL, "mlp_attach: null argument");
+  if (m->attached) return fail(TC_EINVAL, "mlp_attach: already attached");
+  int rank = 0, nranks = 1;
+  if (int st = tc_comm_rank(comm, &rank, &nranks)) return st;
+  if (nranks > MAX_SHARDS) return fail(TC_ENOTSUP, "mlp_attach: %d ranks, at most %d", nranks, MAX_SHARDS);
+  const size_t bytes = m->total * m->esz, flag_bytes = size_t(2) * size_t(nranks) * size_t(m->layers) * 4;
+  tc_peer_buffer *pp = nullptr, *pg = nullptr, *pf = nullptr;
+  int st = tc_peer_buffer_create(comm, bytes, &pp);
+  if (!st) st = tc_peer_buffer_create(comm, bytes, &pg);
+  if (!st) st = tc_peer_buffer_create(comm, flag_bytes, &pf);
+  void *np = peer_buffer_remote(pp, rank), *ng = peer_buffer_remote(pg, rank), *nf = peer_buffer_remote(pf, rank);
+  if (!st) st = check_cuda(cudaMemcpy(np, m->params.p, bytes, cudaMemcpyDeviceToDevice), "cudaMemcpy");
+  if (!st) st = check_cuda(cudaMemset(ng, 0, bytes), "cudaMemset");
+  if (!st) st = check_cuda(cudaMemset(nf, 0, flag_bytes), "cudaMemset");
+  if (!st) st = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  // No rank signals into another's flags before every rank has zeroed them.
+  if (!st) st = comm_barrier(comm);
+  if (st) {
+    for (tc_peer_buffer *b : {pp, pg, pf}) tc_peer_buffer_destroy(b);
+    return st;
+  }
+  auto move = [&](Buf &flat, void *to, std::vector<Buf> &w, std::vector<Buf> &b) {
+    for (int l = 0; l < m->layers; ++l) {
+      w[l].p = static_cast<char *>(to) + (static_cast<char *>(w[l].p) - static_cast<char *>(flat.p));
+      b[l].p = static_cast<char *>(to) + (static_cast<char *>(b[l].p) - static_cast<char *>(flat.p));
+    }
+    tc_free(flat.p);
+    flat.p = to;
+  };
+  move(m->params, np, m->W, m->b);
+  move(m->grads, ng, m->gW, m->gb);
+  m->attached = comm;
+  m->rank = rank;
+  m->nranks = nranks;
+  m->peer_params = pp;
+  m->peer_grads = pg;
+  m->peer_flags = pf;
   return TC_OK;
 }
 
@@ -354,11 +460,15 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   int rank = 0, nranks = 1;
   if (comm) TRY(tc_comm_rank(comm, &rank, &nranks));
   if (nranks == 1) comm = nullptr;
-  // With 2-8 ranks the optimizer is sharded: each layer's gradient block is
-  // reduce-scattered, every rank runs Adam on its own shard of the block,
-  // and the updated parameters are all-gathered.  More ranks all-reduce the
-  // gradients and run Adam on everything.
+  // With 2-8 ranks the optimizer is sharded: every rank updates its own
+  // shard of each layer's block with the gradient summed over the ranks, and
+  // every rank receives every shard's new parameters.  Attached to `comm`
+  // (tc_mlp_attach), one kernel per layer does all of it over NVLink peer
+  // memory; otherwise NCCL reduce-scatters the gradients and all-gathers the
+  // parameters around a local Adam.  More ranks all-reduce the gradients and
+  // run Adam on everything.
   const bool sharded = comm && nranks <= MAX_SHARDS;
+  const bool peers = sharded && comm == m->attached;
   // Adam's coefficients for this step (Adam::update, optim.rs:1106-1124).
   m->steps += 1;
   float c1, c2;
@@ -405,6 +515,43 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     TRY(tc_vector_reduce(d, TC_SUM, m->S.p, last * B, m->loss_sum.p, st));
     TRY(tc_broadcast_scalar(d, TC_MUL, m->loss_sum.p, factor, 0, loss_out, 1, st));
   }
+  // The exchange of layer l over peer memory.
+  auto exchange_layer = [&](int l) -> int {
+    // This rank's gradients of the layer are final and nothing of this
+    // step reads W_l or b_l any more (params_free[l]; the side stream's
+    // vecmat read b_l before side_done[l]): say so to every rank, wait until
+    // every rank has, then one kernel sums this rank's shard of the layer's
+    // block over the ranks (peer loads), updates it and stores it into every
+    // rank's parameters (peer stores); then say that.
+    cudaStream_t c = m->comm_stream;
+    TRY(check_cuda(cudaStreamWaitEvent(c, m->params_free[l], 0), "wait"));
+    TRY(check_cuda(cudaStreamWaitEvent(c, m->side_done[l], 0), "wait"));
+    const size_t count = m->block_len[l] / size_t(nranks);
+    FlagSlots ready{}, written{};
+    ready.n = written.n = nranks;
+    PeerAdam x{};
+    x.nranks = nranks;
+    x.rank = rank;
+    for (int q = 0; q < nranks; ++q) {
+      uint32_t *fl = static_cast<uint32_t *>(peer_buffer_remote(m->peer_flags, q));
+      ready.slot[q] = fl + size_t(rank) * L + l;
+      written.slot[q] = fl + size_t(nranks) * L + size_t(rank) * L + l;
+      x.grads[q] = static_cast<char *>(peer_buffer_remote(m->peer_grads, q)) + m->block_at[l] * e;
+      x.params[q] = static_cast<char *>(peer_buffer_remote(m->peer_params, q)) + m->block_at[l] * e;
+    }
+    const uint32_t *mine = static_cast<const uint32_t *>(peer_buffer_remote(m->peer_flags, rank));
+    signal_slots<<<1, 32, 0, c>>>(ready, m->steps);
+    wait_slots<<<1, 32, 0, c>>>(mine, l, L, nranks, m->steps, PEER_WAIT_NS);
+    TRY(check_launch("mlp flags"));
+    x.m = static_cast<char *>(m->mom1.p) + m->block_at[l] * e;
+    x.v = static_cast<char *>(m->mom2.p) + m->block_at[l] * e;
+    x.first = size_t(rank) * count;
+    x.count = count;
+    TRY(peer_adam_run(d, x, resumed, m->rate, m->beta1, m->beta2, m->eps, c1, c2, c));
+    signal_slots<<<1, 32, 0, c>>>(written, m->steps);
+    TRY(check_launch("mlp flags"));
+    return TC_OK;
+  };
   const void *abar = m->Rbar.p;  // Ā of the top layer = P̄
   for (int l = L - 1; l >= 0; --l) {
     const size_t in = m->dims[l], outd = m->dims[l + 1];
@@ -426,7 +573,7 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     // Z = W·IN: W̄ += Z̄·INᵀ, ĪN += Wᵀ·Z̄ (matmul_transposed_add, both
     // adjoints starting from zero).
     TRY(tc_matmul(d, TC_TRANS_RIGHT, outd, B, in, abar, input, m->gW[l].p, 0, st));
-    if (comm) {
+    if (comm && !peers) {
       TRY(check_cuda(cudaEventRecord(m->grad_ready[l], s), "event"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0), "wait"));
       TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->side_done[l], 0), "wait"));
@@ -451,7 +598,10 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     } else if (!m->prune) {
       TRY(tc_matmul(d, TC_TRANS_LEFT, in, outd, B, m->W[l].p, abar, m->Xbar.p, 0, st));
     }
-    if (sharded) {
+    if (peers) {
+      TRY(check_cuda(cudaEventRecord(m->params_free[l], s), "event"));
+      TRY(exchange_layer(l));
+    } else if (sharded) {
       // Nothing of this step reads W_l or b_l any more (the side stream's
       // vecmat read b_l before side_done[l]): update this rank's shard of
       // the layer and gather every rank's.
@@ -471,6 +621,15 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     TRY(check_cuda(cudaEventRecord(m->reduced, m->comm_stream), "event"));
     TRY(check_cuda(cudaStreamWaitEvent(s, m->reduced, 0), "wait"));
   }
+  if (peers) {
+    // Every rank has stored its shards of every layer into this rank's
+    // parameters (and read this rank's gradients) before anything after
+    // the step on this stream runs.
+    const uint32_t *mine_flags = static_cast<const uint32_t *>(peer_buffer_remote(m->peer_flags, rank));
+    const int count = nranks * L;
+    wait_slots<<<(count + 31) / 32, 32, 0, s>>>(mine_flags, nranks * L, 1, count, m->steps, PEER_WAIT_NS);
+    TRY(check_launch("mlp flags"));
+  }
   // ---- Adam over every parameter (one launch over the flat blocks; the
   // padding between tensors is zero and is read by nothing) ----
   if (!sharded) TRY(adam_range(0, m->total, s));
@@ -479,3 +638,12 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
 }
 
 }  // extern "C"
+
+namespace tc {
+// Whether a wait between ranks gave up since the library loaded.
+int peer_wait_fault() {
+  int h = 0;
+  if (cudaMemcpyFromSymbol(&h, g_peer_fault, sizeof(int)) != cudaSuccess) return 0;
+  return h;
+}
+}  // namespace tc

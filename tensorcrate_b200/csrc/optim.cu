@@ -247,10 +247,139 @@ __global__ void __launch_bounds__(256) sgd_kernel(typename T::S *p, const typena
 
 bool aligned16(const void *q) { return (uintptr_t(q) & 15u) == 0; }
 
+// A 16-byte load that no cache on this GPU may answer from an older copy:
+// another GPU wrote the line (peer memory over NVLink).
+__device__ __forceinline__ uint4 load_fresh(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// The sharded data-parallel update of one block (see PeerAdam): each thread
+// takes 16-byte packs of this rank's shard, loads the pack of every rank's
+// gradient (peer memory over NVLink; all loads issued before any is used),
+// sums them in rank order in f32 and rounds once to T, runs Adam's program
+// on it with this rank's moments, and stores the new parameters to every
+// rank's copy (NVLink stores) and the summed gradient to this rank's.
+template <class T>
+__global__ void __launch_bounds__(256) peer_adam_kernel(const __grid_constant__ PeerAdam x, bool resumed, AdamCoef k,
+                                                        AdamCoef2 k2) {
+  using S = typename T::S;
+  constexpr int N = 16 / int(sizeof(S));
+  union Pk { uint4 raw; S e[N]; };
+  const long long packs = (long long)(x.count / N);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < packs; q += stride) {
+    const size_t at = x.first + size_t(q) * N;
+    uint4 parts[MAX_PEER_RANKS];
+#pragma unroll
+    for (int r = 0; r < MAX_PEER_RANKS; ++r)
+      if (r < x.nranks) parts[r] = load_fresh(reinterpret_cast<const uint4 *>(static_cast<const S *>(x.grads[r]) + at));
+    Pk pp, mm, vv, gg;
+    pp.raw = *reinterpret_cast<const uint4 *>(static_cast<const S *>(x.params[x.rank]) + at);
+    if (resumed) {
+      mm.raw = *reinterpret_cast<const uint4 *>(static_cast<const S *>(x.m) + at);
+      vv.raw = *reinterpret_cast<const uint4 *>(static_cast<const S *>(x.v) + at);
+    }
+    float sum[N];
+#pragma unroll
+    for (int r = 0; r < MAX_PEER_RANKS; ++r)
+      if (r < x.nranks) {
+        Pk part;
+        part.raw = parts[r];
+#pragma unroll
+        for (int j = 0; j < N; ++j) sum[j] = r == 0 ? T::load(part.e[j]) : __fadd_rn(sum[j], T::load(part.e[j]));
+      }
+#pragma unroll
+    for (int j = 0; j < N; ++j) gg.e[j] = T::store(sum[j]);
+    if constexpr (sizeof(S) == 2) {
+      uint32_t *P2 = reinterpret_cast<uint32_t *>(&pp.raw), *M2 = reinterpret_cast<uint32_t *>(&mm.raw);
+      uint32_t *V2 = reinterpret_cast<uint32_t *>(&vv.raw);
+      const uint32_t *G2 = reinterpret_cast<const uint32_t *>(&gg.raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t m2 = resumed ? M2[j] : 0u, v2 = resumed ? V2[j] : 0u;
+        adam_pair<T>(G2[j], P2[j], m2, v2, resumed, k2);
+        M2[j] = m2;
+        V2[j] = v2;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float P = T::load(pp.e[j]), M = resumed ? T::load(mm.e[j]) : 0.0f, V = resumed ? T::load(vv.e[j]) : 0.0f;
+        adam_one<T>(T::load(gg.e[j]), P, M, V, resumed, k);
+        pp.e[j] = T::store(P);
+        mm.e[j] = T::store(M);
+        vv.e[j] = T::store(V);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < MAX_PEER_RANKS; ++r)
+      if (r < x.nranks) *reinterpret_cast<uint4 *>(static_cast<S *>(x.params[r]) + at) = pp.raw;
+    *reinterpret_cast<uint4 *>(static_cast<S *>(x.m) + at) = mm.raw;
+    *reinterpret_cast<uint4 *>(static_cast<S *>(x.v) + at) = vv.raw;
+    *reinterpret_cast<uint4 *>(const_cast<S *>(static_cast<const S *>(x.grads[x.rank])) + at) = gg.raw;
+  }
+  // The stores to the peers are ordered before the flag that announces them.
+  __threadfence_system();
+}
+
 }  // namespace
 }  // namespace tc
 
 using namespace tc;
+
+namespace tc {
+namespace {
+template <class T>
+void adam_coefficients(double rate, double beta1, double beta2, double eps, double c1, double c2, AdamCoef &k,
+                       AdamCoef2 &k2) {
+  k.rate = float(rate);
+  k.beta1 = float(beta1);
+  k.beta2 = float(beta2);
+  k.eps = float(eps);
+  k.c1 = float(c1);
+  k.c2 = float(c2);
+  // `1 - beta` is folded into the program's constants, computed once in
+  // the element type (optim.rs:1067-1072).
+  auto round_host = [](float x) {
+    if (T::code == TC_F32) return x;
+    return T::code == TC_BF16 ? bf16_bits_to_f32(f32_to_bf16_bits(x)) : f16_bits_to_f32(f32_to_f16_bits(x));
+  };
+  k.first_share = round_host(1.0f - k.beta1);
+  k.second_share = round_host(1.0f - k.beta2);
+  // The same values as packed pairs (each already a value of T).
+  auto pair = [](float x) -> uint32_t {
+    if (T::code == TC_F32) return 0u;
+    const uint32_t h = T::code == TC_BF16 ? f32_to_bf16_bits(x) : f32_to_f16_bits(x);
+    return h | (h << 16);
+  };
+  k2 = AdamCoef2{pair(k.rate), pair(k.beta1), pair(k.beta2), pair(k.eps), pair(k.c1), pair(k.c2),
+                 pair(k.first_share), pair(k.second_share)};
+}
+}  // namespace
+
+int peer_adam_run(int dtype, const PeerAdam &x, int resumed, double rate, double beta1, double beta2, double eps,
+                  double c1, double c2, cudaStream_t stream) {
+  if (x.nranks < 1 || x.nranks > MAX_PEER_RANKS || x.rank < 0 || x.rank >= x.nranks)
+    return fail(TC_EINVAL, "peer adam: rank %d of %d", x.rank, x.nranks);
+  if (x.count == 0) return TC_OK;
+  return with_real(dtype, [&](auto t) -> int {
+    using T = decltype(t);
+    constexpr size_t N = 16 / sizeof(typename T::S);
+    if (x.count % N || x.first % N) return fail(TC_EINVAL, "peer adam: the shard is not whole 16-byte packs");
+    AdamCoef k;
+    AdamCoef2 k2;
+    adam_coefficients<T>(rate, beta1, beta2, eps, c1, c2, k, k2);
+    const unsigned grid = grid_for(x.count / N, 256, 8);
+    peer_adam_kernel<T><<<grid, 256, 0, stream>>>(x, resumed != 0, k, k2);
+    return check_launch("peer adam");
+  });
+}
+}  // namespace tc
 
 extern "C" {
 
@@ -264,28 +393,8 @@ int tc_adam_multi(int dtype, const tc_adam_tensor *tensors, size_t count, int re
     using T = decltype(t);
     constexpr size_t N = 16 / sizeof(typename T::S);
     AdamCoef k;
-    k.rate = float(rate);
-    k.beta1 = float(beta1);
-    k.beta2 = float(beta2);
-    k.eps = float(eps);
-    k.c1 = float(c1);
-    k.c2 = float(c2);
-    // `1 - beta` is folded into the program's constants, computed once in
-    // the element type (optim.rs:1067-1072).
-    auto round_host = [](float x) {
-      if (T::code == TC_F32) return x;
-      return T::code == TC_BF16 ? bf16_bits_to_f32(f32_to_bf16_bits(x)) : f16_bits_to_f32(f32_to_f16_bits(x));
-    };
-    k.first_share = round_host(1.0f - k.beta1);
-    k.second_share = round_host(1.0f - k.beta2);
-    // The same values as packed pairs (each already a value of T).
-    auto pair = [](float x) -> uint32_t {
-      if (T::code == TC_F32) return 0u;
-      const uint32_t h = T::code == TC_BF16 ? f32_to_bf16_bits(x) : f32_to_f16_bits(x);
-      return h | (h << 16);
-    };
-    const AdamCoef2 k2{pair(k.rate), pair(k.beta1), pair(k.beta2), pair(k.eps), pair(k.c1), pair(k.c2),
-                       pair(k.first_share), pair(k.second_share)};
+    AdamCoef2 k2;
+    adam_coefficients<T>(rate, beta1, beta2, eps, c1, c2, k, k2);
     static int resident = 0;
     if (!resident) {
       int n = 0;

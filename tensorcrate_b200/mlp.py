@@ -56,9 +56,24 @@ class Mlp:
         N.call("tc_mlp_step", self.handle, x.ptr, y.ptr, comm, loss.ptr if loss is not None else None,
                _stream(stream))
 
+    def attach(self, comm) -> None:
+        """Exchange over NVLink peer memory in steps over `comm`
+        (collective; close() is then collective too)."""
+        N.call("tc_mlp_attach", self.handle, comm)
+        self.attached = True
+
+    def close(self) -> None:
+        """Free the handle now (collective when attached: every rank closes
+        its handle at the same point)."""
+        if self.handle:
+            N.call("tc_mlp_destroy", self.handle)
+            self.handle = None
+
     def __del__(self):
+        # An attached handle is freed collectively by close(); a handle left
+        # attached at exit is left to the process's end.
         try:
-            if self.handle and N._lib is not None:
+            if self.handle and N._lib is not None and not getattr(self, "attached", False):
                 N._lib.tc_mlp_destroy(self.handle)
         except Exception:
             pass

@@ -117,6 +117,11 @@ def check_reduction_shards(comm, world, rank, sp, failures):
 
 
 def check_data_parallel_step(comm, world, rank, sp, failures):
+    for peers in (False, True):
+        _data_parallel_f32(comm, world, rank, sp, failures, peers)
+
+
+def _data_parallel_f32(comm, world, rank, sp, failures, peers):
     dims, gbatch = [64, 128, 64], 32
     batch = gbatch // world
     rng = np.random.default_rng(9)
@@ -129,6 +134,9 @@ def check_data_parallel_step(comm, world, rank, sp, failures):
     one = Mlp("f32", dims, gbatch, gbatch, rate=1e-3, beta2=0.99, eps=1e-4)
     dp.load(weights, biases)
     one.load(weights, biases)
+    if peers:
+        dp.attach(comm)
+    how = "peer" if peers else "nccl"
     xd = cuda.CudaStorage.store(np.ascontiguousarray(x[:, cols]).ravel(), "f32")
     yd = cuda.CudaStorage.store(np.ascontiguousarray(y[:, cols]).ravel(), "f32")
     xw = cuda.CudaStorage.store(x.ravel(), "f32")
@@ -142,10 +150,17 @@ def check_data_parallel_step(comm, world, rank, sp, failures):
             # The gradient sums reorder over ranks: f32 rounding, then Adam.
             err = float(np.max(np.abs(got - want)))
             if not err <= 2e-5:
-                failures.append(f"rank {rank}: data-parallel layer {l} {name} differs by {err:.3g}")
+                failures.append(f"rank {rank}: data-parallel ({how}) layer {l} {name} differs by {err:.3g}")
+    torch.cuda.synchronize()
+    dp.close()
 
 
 def check_data_parallel_bf16(comm, world, rank, sp, failures):
+    for peers in (False, True):
+        _data_parallel_bf16(comm, world, rank, sp, failures, peers)
+
+
+def _data_parallel_bf16(comm, world, rank, sp, failures, peers):
     """bf16, the config's type: each rank's partial gradient is rounded to
     bf16 by its own products, and NCCL adds the partials in bf16 with a
     rounding per hop, so the data-parallel gradient is not the whole batch's
@@ -165,6 +180,9 @@ def check_data_parallel_bf16(comm, world, rank, sp, failures):
     one = Mlp("bf16", dims, gbatch, gbatch, beta2=0.99)
     dp.load(weights, biases)
     one.load(weights, biases)
+    if peers:
+        dp.attach(comm)
+    how = "peer" if peers else "nccl"
     bits = lambda a: cuda.CudaStorage.store(cuda.f32_to_bits(np.ascontiguousarray(a).ravel(), "bf16"), "bf16")
     dp.step(bits(x[:, cols]), bits(y[:, cols]), comm=comm, stream=torch.cuda.current_stream())
     one.step(bits(x), bits(y), stream=torch.cuda.current_stream())
@@ -182,7 +200,7 @@ def check_data_parallel_bf16(comm, world, rank, sp, failures):
         lo, hi = rank * length // world, (rank + 1) * length // world
         err, scale = float(np.linalg.norm(got[lo:hi] - want[lo:hi])), float(np.linalg.norm(want[lo:hi]))
         if not err <= world * 2.0 ** -7 * scale:
-            failures.append(f"rank {rank}: bf16 data-parallel layer {l} gradient shard off by {err:.3g} "
+            failures.append(f"rank {rank}: bf16 data-parallel ({how}) layer {l} gradient shard off by {err:.3g} "
                             f"(norm {scale:.3g})")
         for name, p, q in zip(("weight", "bias"), dp.params(l), one.params(l)):
             mine = torch.tensor(p.view(np.int16).astype(np.int64).sum(), device="cuda")
@@ -190,11 +208,13 @@ def check_data_parallel_bf16(comm, world, rank, sp, failures):
             torch.distributed.all_reduce(lowest, op=torch.distributed.ReduceOp.MIN)
             torch.distributed.all_reduce(highest, op=torch.distributed.ReduceOp.MAX)
             if int(lowest.item()) != int(highest.item()):
-                failures.append(f"rank {rank}: bf16 data-parallel layer {l} {name}s differ between ranks")
+                failures.append(f"rank {rank}: bf16 data-parallel ({how}) layer {l} {name}s differ between ranks")
             diff = np.abs(widen(p) - widen(q))
             if not (np.max(diff) <= 2e-3 + 8e-3 and np.median(diff) <= 4e-3):
-                failures.append(f"rank {rank}: bf16 data-parallel layer {l} {name} off the whole-batch step by "
+                failures.append(f"rank {rank}: bf16 data-parallel ({how}) layer {l} {name} off the whole-batch step by "
                                 f"max {np.max(diff):.3g}, median {np.median(diff):.3g}")
+    torch.cuda.synchronize()
+    dp.close()
 
 
 def main() -> int:

@@ -151,7 +151,7 @@ def _awkward(n, seed, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("n", [1, 7, 1000, (1 << 20) + 1])
+@pytest.mark.parametrize("n", [1, 7, 1000, 4096, 4097, (1 << 20) + 1])
 @pytest.mark.parametrize("order", [N.ASCENDING, N.DESCENDING])
 def test_sort_matches_the_oracle_bit_for_bit(device, dtype, n, order):
     a = _awkward(n, 21, dtype)
@@ -159,6 +159,19 @@ def test_sort_matches_the_oracle_bit_for_bit(device, dtype, n, order):
     want = np.empty_like(a)
     O.call("orc_sort", O.DTYPES[dtype], order, O.ptr(a), O.ptr(want), n)
     assert np.array_equal(bits_of(got, dtype), bits_of(want, dtype))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_sort_of_few_distinct_values(device, dtype):
+    """Every key in a handful of digits: the radix passes' counts pile into
+    few bins and each tile's ranks run long."""
+    rng = np.random.default_rng(5)
+    a = O.narrow(rng.choice(np.array([1.0, -2.5, 0.0, 3.0], np.float32), size=300001), dtype)
+    for order in (N.ASCENDING, N.DESCENDING):
+        got = cuda.Cuda.vector_sort(cuda.CudaStorage.store(a, dtype), order).as_slice()
+        want = np.empty_like(a)
+        O.call("orc_sort", O.DTYPES[dtype], order, O.ptr(a), O.ptr(want), a.size)
+        assert np.array_equal(bits_of(got, dtype), bits_of(want, dtype))
 
 
 def test_sort_orders_nans_and_zeros_like_the_host(device):
