@@ -14,7 +14,8 @@ The same line carries the other configurations as sub-records, each with
 its own timing, clocks, roofline, end-to-end figure and parity check:
   c4  the MLP training step (1024-4096-4096-1024, bf16, Adam), steps/s;
   c4_weak  the same step with 2048 samples per GPU, samples/s;
-  c5  the bf16 GEMM, M=N=K=8192, TFLOP/s;
+  c5  the bf16 GEMM, M=N=K=8192, TFLOP/s (c5_16384, c5_4096: the config's
+      other sizes);
   c1  the f32 GEMM 1024^3 and matvec;
   c3  the f16 layout copies (permute, slice-split-concatenate).
 
@@ -664,13 +665,44 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
         def run(a_ptr, b_ptr, s):
             N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a_ptr, b_ptr, c_ptr, 0, s))
 
-    ms, blocks, clocks = timed(torch, world, lambda: run(a.ptr, b.ptr, sp), args, stream)
+    # Small products fit in L2: the timed steps then rotate over enough
+    # copies of A and B (and, on one GPU, C) that one pass over them
+    # exceeds twice the 126 MB L2, so every step reads its operands from HBM.
+    set_bytes = (rows * k + k * n + (0 if panels else m * n)) * esz
+    copies = max(1, math.ceil(2 * 126e6 / set_bytes)) if 3 * size * size * esz <= 126e6 else 1
+    rot = [(a, b, c_ptr)]
+    for _ in range(copies - 1):
+        a2 = cuda.CudaStorage(dtype, rows * k)
+        b2 = cuda.CudaStorage(dtype, k * n)
+        N.check("d2d", lib.tc_memcpy_d2d(a2.ptr, a.ptr, a2.nbytes, None))
+        N.check("d2d", lib.tc_memcpy_d2d(b2.ptr, b.ptr, b2.nbytes, None))
+        c2 = c_ptr if panels else cuda.CudaStorage(dtype, m * n)
+        rot.append((a2, b2, c2))
+    turn = [0]
+
+    def rotating_step():
+        a_i, b_i, c_i = rot[turn[0] % len(rot)]
+        turn[0] += 1
+        if panels:
+            run(a_i.ptr, b_i.ptr, sp)
+        else:
+            N.check("matmul", lib.tc_matmul(code, 0, m, k, n, a_i.ptr, b_i.ptr,
+                                            c_i if isinstance(c_i, int) else c_i.ptr, 0, sp))
+
+    ms, blocks, clocks = timed(torch, world, rotating_step, args, stream)
+    torch.cuda.synchronize()
+    del rot[1:]
+    # the parity check reads C from the first set: run it once more there
+    run(a.ptr, b.ptr, sp)
 
     # parity: sampled rows of every panel of C against the oracle
     import oracle as O
     torch.cuda.synchronize()
     failures = []
     sample = [(p * (m // max(world, 1)) + 17) for p in range(world if panels else 1)] + [m - 3]
+    if size > 8192:
+        # every band widens all of B in the oracle: three bands at most
+        sample = sorted({sample[0], sample[len(sample) // 2], m - 3})
     O.set_matmul_threads(os.cpu_count() or 1)
     try:
         for r0 in sample:
@@ -755,8 +787,11 @@ def run_gemm(args, torch, world, rank, comm, dtype="bf16", size=8192):
            "config": {"workload": f"config{'5' if dtype != 'f32' else '1'}: C = A.B, M=N=K={size}, f32 accumulate",
                       "parallelism": (f"row panels x{world}, all-gather fused into the GEMM epilogue (NVLink peer "
                                       "stores)" if panels else (f"replicas x{world}" if world > 1 else "single GPU")),
-                      "l2": "inputs resident; no flush: the operands and C exceed L2 at 8192"
-                      if size >= 8192 else "inputs resident; A, B, C (12.6 MB) fit in L2: the figure is L2-warm"},
+                      "l2": (f"inputs resident; no flush: A, B and C ({3 * size * size * esz / 1e6:.0f} MB) exceed "
+                             "the 126 MB L2") if copies == 1 else
+                            (f"inputs resident; A, B and C ({3 * size * size * esz / 1e6:.1f} MB) fit in the 126 MB "
+                             f"L2, so the steps rotate over {copies} copies of them ({copies * set_bytes / 1e6:.0f} MB "
+                             "per rank), more than twice L2")},
            "timing": blocks,
            "roofline": {"bound": "tensor", "kernel": "gemm_tc" if dtype != "f32" else "gemm_tc<tf32> x3 passes",
                         "achieved": round(per_gpu * passes, 1), "peak": round(peak, 1),
@@ -1329,16 +1364,19 @@ def main():
                "c4": lambda: run_c4(args, torch, world, rank, comm),
                "c4_weak": lambda: run_c4_weak(args, torch, world, rank, comm),
                "c5": lambda: run_gemm(args, torch, world, rank, comm, "bf16", args.size),
+               "c5_16384": lambda: run_gemm(args, torch, world, rank, comm, "bf16", 16384),
+               "c5_4096": lambda: run_gemm(args, torch, world, rank, comm, "bf16", 4096),
                "trait": lambda: run_trait(args, torch, world, rank, comm)}
     if args.workload == "all":
         line = run_c2(args, torch, world, rank, comm)
-        for key in ("c4", "c4_weak", "c5", "c1", "c3"):
+        for key in ("c4", "c4_weak", "c5", "c5_16384", "c5_4096", "c1", "c3"):
             line[key] = runners[key]()
-        statuses = [line["parity"]] + [line[k]["parity"] for k in ("c4", "c5", "c1", "c3")]
+        statuses = [line["parity"]] + [line[k]["parity"] for k in ("c4", "c5", "c5_16384", "c5_4096", "c1", "c3")]
         bad = [s for s in statuses if s["status"] != "ok"]
         line["parity_all"] = "ok" if not bad else {"failed": len(bad)}
         line["gpu_launches_all"] = line["gpu_launches"] + sum(line[k]["gpu_launches"]
-                                                              for k in ("c4", "c4_weak", "c5", "c1", "c3"))
+                                                              for k in ("c4", "c4_weak", "c5", "c5_16384", "c5_4096",
+                                                                        "c1", "c3"))
     else:
         line = headline_keys(runners[args.workload](), args)
     if rank == 0 and not args.no_cpu_baseline and args.workload in ("all", "c2"):

@@ -422,6 +422,13 @@ int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *strea
  * returned early; TC_OK otherwise.  No counterpart in the reference
  * (Metal reports async errors at the next sync, src/metal/mod.rs:17-21). */
 int tc_device_status(int *fault);
+/* Clear those records.  No counterpart in the reference. */
+int tc_device_status_reset(void);
+/* How long a pipeline wait of the tensor-core GEMM lasts before its CTA
+ * gives up (ns; 0 restores the default of 2 s).  Waits for in-flight copies
+ * and products while giving up always allow 2 s.  Lets a test make a wait
+ * run out on purpose; no counterpart in the reference. */
+int tc_set_wait_limit(unsigned long long ns);
 
 /* ---- layout helpers (host only; src/tensors/layout.rs) ------------------ */
 /* `coalesce` (layout.rs:419-446) for n_ops operands whose strides are

@@ -151,6 +151,8 @@ SIGNATURES = {
     "tc_sgd": [_i, _sz, _p, _p, _d, _p],
     "tc_coalesce": [_u32, _szp, _u32, _szp, _u32p, _szp, _szp],
     "tc_device_status": [C.POINTER(_i)],
+    "tc_device_status_reset": [],
+    "tc_set_wait_limit": [C.c_ulonglong],
     "tc_mlp_create": [_i, _u32, _u32p, _u32, _u32, _d, _d, _d, _d, C.POINTER(_p)],
     "tc_mlp_destroy": [_p],
     "tc_mlp_params": [_p, _u32, _p, _p, _i],

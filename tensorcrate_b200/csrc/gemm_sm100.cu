@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -37,6 +38,7 @@ __device__ int g_gemm_fault = 0;
 
 namespace {
 thread_local int t_reserved_sms = 0;
+std::atomic<unsigned long long> g_wait_ns{2000000000ull};
 }
 void gemm_reserve_sms(int n) { t_reserved_sms = n < 0 ? 0 : n; }
 int reserved_sms() { return t_reserved_sms; }
@@ -47,7 +49,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 f16/bf16 = 128 bytes: one swizzle row
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
-constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait (drains always wait this long)
 constexpr uint32_t WAIT_SPINS = 1u << 30;   // and never more spins than this
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -78,15 +80,15 @@ __device__ __forceinline__ uint64_t now_ns() {
   return t;
 }
 // Wait for the phase of `bar` with `parity`.  False if the CTA is aborting,
-// or if WAIT_NS pass first: that records the fault and starts the abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+// or if `limit_ns` pass first: that records the fault and starts the abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = now_ns();
   for (uint32_t i = 1; i < WAIT_SPINS; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
+    if ((i & 63u) == 1) {  // after the first retry, then every 64
       if (*abort_flag) return false;
-      if (now_ns() - t0 > WAIT_NS) break;
+      if (now_ns() - t0 > limit_ns) break;
     }
   }
   *abort_flag = 1;
@@ -148,6 +150,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 constexpr int MAX_PEERS = 7;
 
 struct Params {
+  // How long a pipeline wait lasts before the CTA gives up (drains of
+  // in-flight work always allow WAIT_NS).
+  unsigned long long wait_ns;
   int M, N, K;
   int a_mn, b_mn;  // 1 = MN-major operand
   int accumulate;
@@ -257,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int m0 = mb * BM, n0 = nb * BN;
         const int kb_lo = ks * p.kper, kb_hi = min(k_blocks, kb_lo + p.kper);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, &abort_flag)) break;
+          if (!mbar_wait(&empty[stage], phase ^ 1u, &abort_flag, p.wait_ns)) break;
           uint8_t *sa = tiles + stage * STAGE_BYTES;
           uint8_t *sb = sa + A_BYTES;
           mbar_expect_tx(&full[stage], STAGE_BYTES);
@@ -321,11 +326,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int ks = u - (u / S) * S;
         const int kb_lo = ks * p.kper, kb_hi = min(k_blocks, kb_lo + p.kper);
         // The accumulator must have been drained by the epilogue.
-        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, &abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, &abort_flag, p.wait_ns)) { ok = false; break; }
         fence_after();
         const uint32_t tmem_d = tmem_base + uint32_t(buf * BN);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait(&full[stage], phase, &abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, &abort_flag, p.wait_ns)) { ok = false; break; }
           fence_after();
           const uint32_t sa = smem_u32(tiles + stage * STAGE_BYTES), sb = sa + A_BYTES;
 #pragma unroll
@@ -356,7 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++iter) {
       const int buf = iter & 1;
       const uint32_t use = uint32_t(iter >> 1);
-      if (!mbar_wait(&acc_full[buf], use & 1u, &abort_flag)) break;
+      if (!mbar_wait(&acc_full[buf], use & 1u, &abort_flag, p.wait_ns)) break;
       fence_after();
       const int t = u / S, ks = u - t * S;
       int mb, nb;
@@ -800,6 +805,7 @@ int gemm_tc_run_full(int dtype, int transposed, size_t rows, size_t inner, size_
   if ((uintptr_t(a) & 15u) || (uintptr_t(b) & 15u) || (a_inner * 2) % 16 || (b_inner * 2) % 16) return TC_ENOTSUP;
   const bool bf16 = dtype == TC_BF16;
   Params p{};
+  p.wait_ns = g_wait_ns.load();
   p.M = int(rows);
   p.N = int(cols);
   p.K = int(inner);
@@ -862,6 +868,7 @@ int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const 
                                      kp);
   if (int st = check_launch("gemm (tf32 split)")) return st;
   Params p{};
+  p.wait_ns = g_wait_ns.load();
   p.M = int(rows);
   p.N = int(cols);
   p.K = int(3 * kp);
@@ -888,6 +895,22 @@ int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const 
 
 namespace tc {
 int peer_wait_fault();
+int peer_wait_fault_reset();
+}
+
+// How long the tensor-core GEMM's pipeline waits last before a CTA gives up
+// (default 2 s); 0 restores the default.  For tests of the failure path.
+extern "C" int tc_set_wait_limit(unsigned long long ns) {
+  tc::g_wait_ns.store(ns ? ns : 2000000000ull);
+  return TC_OK;
+}
+
+// Clear the records of waits that gave up.
+extern "C" int tc_device_status_reset(void) {
+  const int zero = 0;
+  if (int st = tc::check_cuda(cudaMemcpyToSymbol(tc::g_gemm_fault, &zero, sizeof(int)), "cudaMemcpyToSymbol"))
+    return st;
+  return tc::peer_wait_fault_reset();
 }
 
 extern "C" int tc_device_status(int *fault) {

@@ -640,10 +640,15 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
 }  // extern "C"
 
 namespace tc {
-// Whether a wait between ranks gave up since the library loaded.
+// Whether a wait between ranks gave up since the library loaded (or the
+// last reset).
 int peer_wait_fault() {
   int h = 0;
   if (cudaMemcpyFromSymbol(&h, g_peer_fault, sizeof(int)) != cudaSuccess) return 0;
   return h;
+}
+int peer_wait_fault_reset() {
+  const int zero = 0;
+  return check_cuda(cudaMemcpyToSymbol(g_peer_fault, &zero, sizeof(int)), "cudaMemcpyToSymbol");
 }
 }  // namespace tc

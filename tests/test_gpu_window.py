@@ -58,6 +58,38 @@ def test_correlate_is_the_hosts_bits(device, dtype, shape, wshape, flip):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_correlate_with_more_taps_than_shared_memory_holds(device, dtype):
+    """A 65x65 window (4225 taps, more than the 4096 staged in shared memory)
+    over enough outputs (136 x 939) for the thread-per-outputs kernel, which
+    then reads the taps through L1: still the Host's bits.  The output rows
+    are not a multiple of the 8 outputs a thread takes."""
+    shape, wshape = (200, 1003), (65, 65)
+    x = O.narrow(uniform(shape[0] * shape[1], 11), dtype)
+    w = O.narrow(uniform(wshape[0] * wshape[1], 12), dtype)
+    assert np.array_equal(correlate_gpu(x, w, shape, wshape, False, dtype),
+                          correlate_oracle(x, w, shape, wshape, False, dtype))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("forward_flip", [False, True])
+def test_correlate_input_gradient_with_more_taps_than_shared_memory_holds(device, dtype, forward_flip):
+    """The input gradient through a 65x65 window (taps read through L1):
+    the Host's bits, out-of-range taps skipped as the Host skips them."""
+    (ar, ac), (wr, wc) = (70, 83), (65, 65)
+    adj = O.narrow(uniform(ar * ac, 13), dtype)
+    w = O.narrow(uniform(wr * wc, 14), dtype)
+    rows, cols = ar + wr - 1, ac + wc - 1
+    out = cuda.CudaStorage(dtype, rows * cols)
+    dadj, dw = _store(adj, dtype), _store(w, dtype)
+    N.call("tc_correlate_input_gradient", N.DTYPES[dtype], ar, ac, wr, wc, int(forward_flip), dadj.ptr, dw.ptr,
+           out.ptr, None)
+    want = np.empty(rows * cols, adj.dtype)
+    O.call("orc_correlate_input_gradient", O.DTYPES[dtype], ar, ac, wr, wc, int(forward_flip), O.ptr(adj), O.ptr(w),
+           O.ptr(want))
+    assert np.array_equal(out.as_slice(), want)
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 def test_window_gradient_with_many_taps_within_sum_rounding(device, dtype):
     """The window gradient of a 300x300 input (a 298x298 adjoint, 88804
