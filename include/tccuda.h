@@ -499,6 +499,49 @@ int tc_mlp_step(tc_mlp *mlp, const void *x_dev, const void *y_dev, tc_comm *comm
  * counterpart in the reference, which runs on one device. */
 int tc_mlp_attach(tc_mlp *mlp, tc_comm *comm);
 
+/* ---- a reverse-mode tape over device tensors (src/tensors/tape) --------- */
+/* The tensor-level rules of tensorcrate's tape, recorded in creation order
+ * and replayed backwards through the kernels above, for callers that drive
+ * the backend without the Rust tape (Tape, tape/mod.rs:349-549).  Every var
+ * is a tensor of the tape's element type; values and adjoints are device
+ * buffers the tape owns (a leaf's value is the caller's), all work on the
+ * tape's stream.  Shapes broadcast as layout.rs:330-363 (right-aligned,
+ * extents equal or one).  Each call returns its result's var id in *out. */
+typedef struct tc_tape tc_tape;
+int tc_tape_create(int dtype, void *stream, tc_tape **out);
+int tc_tape_destroy(tc_tape *tape);
+/* A leaf (a parameter or an input): the tape reads `dev` in place. */
+int tc_tape_leaf(tc_tape *tape, const void *dev, uint32_t rank, const size_t *shape, uint32_t *out);
+/* a op b, op = TC_ADD/SUB/MUL/DIV, broadcast; backward sums each operand's
+ * share to its shape (TensorVar::binary and sum_to_shape, tape/tensor.rs:
+ * 23-37, 128-160). */
+int tc_tape_binary(tc_tape *tape, int op, uint32_t a, uint32_t b, uint32_t *out);
+/* max(a, 0); backward weights the adjoint by MaxShare(a, 0): 1, 1/2 at 0,
+ * 0 (relu / select_scalar, tape/tensor.rs:272-300). */
+int tc_tape_relu(tc_tape *tape, uint32_t a, uint32_t *out);
+/* a * factor, factor a value of the element type (tape/tensor.rs:317). */
+int tc_tape_scale(tc_tape *tape, uint32_t a, double factor, uint32_t *out);
+/* The sum (mean != 0: the mean) over `axes` (distinct, ascending), the
+ * folded axes dropped or kept at one; backward spreads the adjoint over each
+ * slice, a mean's scaled first by `share` = 1/count as a value of the
+ * element type (sum_axes / mean_axes, tape/tensor.rs:581-620). */
+int tc_tape_sum_axes(tc_tape *tape, uint32_t a, uint32_t n_axes, const uint32_t *axes, int mean, int keep_dims,
+                     double share, uint32_t *out);
+/* [m x k]·[k x n]; backward Ā += C̄·Bᵀ, B̄ += Aᵀ·C̄ into the current adjoint
+ * or zeros (MatrixVar::matmul, tape/mod.rs:1190-1216). */
+int tc_tape_matmul(tc_tape *tape, uint32_t a, uint32_t b, uint32_t *out);
+/* The sum of every element, a one-element var; backward fills (MatrixVar::
+ * sum, tape/mod.rs:1286-1296). */
+int tc_tape_sum(tc_tape *tape, uint32_t a, uint32_t *out);
+/* A var's value: device pointer, rank and shape (shape may be NULL). */
+int tc_tape_value(tc_tape *tape, uint32_t var, const void **dev, uint32_t *rank, size_t *shape);
+/* Clear every adjoint, seed the one-element `var` with one and apply every
+ * rule from it back to the first node (Var::backward_with, tape/mod.rs:
+ * 507-521). */
+int tc_tape_backward(tc_tape *tape, uint32_t var);
+/* A var's adjoint after backward; NULL when no contribution reached it. */
+int tc_tape_adjoint(tc_tape *tape, uint32_t var, const void **dev);
+
 /* ---- fused elementwise programs (Kernels::fused, kernels.rs:1077-1082) --- */
 /* One instruction of a fused::Program (fused/mod.rs:290-313).  `code` is a
  * tc_instr_code; registers are below 16.  Load reads place `slot` (one per

@@ -161,6 +161,18 @@ SIGNATURES = {
     "tc_mlp_prune_leaves": [_p, _i],
     "tc_mlp_step": [_p, _p, _p, _p, _p, _p],
     "tc_mlp_attach": [_p, _p],
+    "tc_tape_create": [_i, _p, C.POINTER(_p)],
+    "tc_tape_destroy": [_p],
+    "tc_tape_leaf": [_p, _p, _u32, _szp, _u32p],
+    "tc_tape_binary": [_p, _i, _u32, _u32, _u32p],
+    "tc_tape_relu": [_p, _u32, _u32p],
+    "tc_tape_scale": [_p, _u32, _d, _u32p],
+    "tc_tape_sum_axes": [_p, _u32, _u32, _u32p, _i, _i, _d, _u32p],
+    "tc_tape_matmul": [_p, _u32, _u32, _u32p],
+    "tc_tape_sum": [_p, _u32, _u32p],
+    "tc_tape_value": [_p, _u32, C.POINTER(_p), _u32p, _szp],
+    "tc_tape_backward": [_p, _u32],
+    "tc_tape_adjoint": [_p, _u32, C.POINTER(_p)],
     "tc_comm_unique_id": [C.POINTER(C.c_uint8)],
     "tc_comm_init": [_i, _i, C.POINTER(C.c_uint8), C.POINTER(_p)],
     "tc_comm_destroy": [_p],
