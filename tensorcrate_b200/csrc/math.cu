@@ -303,16 +303,10 @@ __global__ void __launch_bounds__(RADIX_THREADS) radix_histogram(const K *keys, 
   for (int w = 0; w < RADIX_WARPS; ++w) h[w][tid] = 0;
   __syncthreads();
   const long long base = (long long)blockIdx.x * RADIX_TILE;
-  const unsigned below = (1u << (tid & 31)) - 1u;
 #pragma unroll 4
   for (int i = 0; i < RADIX_ITEMS; ++i) {
     const long long idx = base + (long long)i * RADIX_THREADS + tid;
-    // One shared-memory add per distinct digit of the warp's 32 keys (keys
-    // with few distinct top bytes would otherwise serialise on one bin).
-    const uint32_t digit = idx < n ? (uint32_t(keys[idx]) >> shift) & 255u : 256u;
-    const unsigned peers = __match_any_sync(~0u, digit);
-    if (digit < 256u && __popc(peers & below) == 0) h[warp][digit] += __popc(peers);
-    __syncwarp();
+    if (idx < n) atomicAdd(&h[warp][(uint32_t(keys[idx]) >> shift) & 255u], 1u);
   }
   __syncthreads();
   uint32_t total = 0;
