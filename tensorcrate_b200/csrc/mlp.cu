@@ -469,6 +469,10 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   // run Adam on everything.
   const bool sharded = comm && nranks <= MAX_SHARDS;
   const bool peers = sharded && comm == m->attached;
+  // On one GPU each layer's Adam runs on the second stream as soon as the
+  // backward pass is done with the layer, beside the products of the layers
+  // below it (Adam is bound by memory, the products by the tensor cores).
+  const bool layered = !comm;
   // Adam's coefficients for this step (Adam::update, optim.rs:1106-1124).
   m->steps += 1;
   float c1, c2;
@@ -492,13 +496,13 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   }
   const size_t last = m->dims[L];
   const float factor = round_to(d, 1.0 / (double(last) * double(m->global_batch)));
-  // With a communicator, the collectives (and, sharded, the Adam shards)
-  // run beside the backward products: leave them SMs (the products' CTAs
-  // fill an SM's shared memory).
+  // The second stream's work (collectives, exchanges, Adam) runs beside
+  // the backward products: leave it SMs (the products' CTAs fill an SM's
+  // shared memory).
   struct Reserve {
     explicit Reserve(bool on) { gemm_reserve_sms(on ? 16 : 0); }
     ~Reserve() { gemm_reserve_sms(0); }
-  } reserve(comm != nullptr);
+  } reserve(comm != nullptr || layered);
   // Loss and the top of the backward pass (frobenius_dot, scale, sum's and
   // Mul's and Sub's rules) in one pass.
   TRY(with_real(d, [&](auto t) {
@@ -612,12 +616,17 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
       TRY(adam_range(mine, count, m->comm_stream));
       char *block = static_cast<char *>(m->params.p) + m->block_at[l] * e;
       TRY(tc_allgather(comm, d, block + size_t(rank) * count * e, block, count, m->comm_stream));
+    } else if (layered) {
+      TRY(check_cuda(cudaEventRecord(m->params_free[l], s), "event"));
+      TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->params_free[l], 0), "wait"));
+      TRY(check_cuda(cudaStreamWaitEvent(m->comm_stream, m->side_done[l], 0), "wait"));
+      TRY(adam_range(m->block_at[l], m->block_len[l], m->comm_stream));
     }
   }
   // Every side-stream result (b̄, ones̄) is complete before Adam and the
   // caller see them.
   TRY(check_cuda(cudaStreamWaitEvent(s, m->side_done[0], 0), "wait"));
-  if (comm) {
+  if (comm || layered) {
     TRY(check_cuda(cudaEventRecord(m->reduced, m->comm_stream), "event"));
     TRY(check_cuda(cudaStreamWaitEvent(s, m->reduced, 0), "wait"));
   }
@@ -632,7 +641,7 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
   }
   // ---- Adam over every parameter (one launch over the flat blocks; the
   // padding between tensors is zero and is read by nothing) ----
-  if (!sharded) TRY(adam_range(0, m->total, s));
+  if (!sharded && !layered) TRY(adam_range(0, m->total, s));
 #undef TRY
   return TC_OK;
 }
