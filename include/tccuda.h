@@ -429,6 +429,11 @@ int tc_device_status_reset(void);
  * and products while giving up always allow 2 s.  Lets a test make a wait
  * run out on purpose; no counterpart in the reference. */
 int tc_set_wait_limit(unsigned long long ns);
+/* How long a data-parallel step's kernels wait for another rank's flag
+ * (ns; 0 restores the default of 5 s); on expiry they record the fault and
+ * return, and the step's results are not valid.  Lets a test make a wait
+ * run out on purpose; no counterpart in the reference. */
+int tc_set_peer_wait_limit(unsigned long long ns);
 
 /* ---- layout helpers (host only; src/tensors/layout.rs) ------------------ */
 /* `coalesce` (layout.rs:419-446) for n_ops operands whose strides are

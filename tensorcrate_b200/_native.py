@@ -153,6 +153,7 @@ SIGNATURES = {
     "tc_device_status": [C.POINTER(_i)],
     "tc_device_status_reset": [],
     "tc_set_wait_limit": [C.c_ulonglong],
+    "tc_set_peer_wait_limit": [C.c_ulonglong],
     "tc_mlp_create": [_i, _u32, _u32p, _u32, _u32, _d, _d, _d, _d, C.POINTER(_p)],
     "tc_mlp_destroy": [_p],
     "tc_mlp_params": [_p, _u32, _p, _p, _i],

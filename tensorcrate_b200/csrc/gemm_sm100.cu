@@ -896,12 +896,20 @@ int gemm_tf32_run(int transposed, size_t rows, size_t inner, size_t cols, const 
 namespace tc {
 int peer_wait_fault();
 int peer_wait_fault_reset();
+void set_peer_wait_limit(unsigned long long ns);
 }
 
 // How long the tensor-core GEMM's pipeline waits last before a CTA gives up
 // (default 2 s); 0 restores the default.  For tests of the failure path.
 extern "C" int tc_set_wait_limit(unsigned long long ns) {
   tc::g_wait_ns.store(ns ? ns : 2000000000ull);
+  return TC_OK;
+}
+
+// How long a data-parallel step waits for another rank's flag (default 5
+// s); 0 restores the default.  For tests of the failure path.
+extern "C" int tc_set_peer_wait_limit(unsigned long long ns) {
+  tc::set_peer_wait_limit(ns);
   return TC_OK;
 }
 

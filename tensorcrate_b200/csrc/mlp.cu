@@ -27,6 +27,7 @@
 // shrinks with P and the collectives move the same bytes an all-reduce
 // would.  With more ranks the gradients are all-reduced and every rank runs
 // the whole Adam pass.
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -84,7 +85,8 @@ __global__ void __launch_bounds__(256) mse_backward(const typename T::S *pred, c
 // returns.
 // ---------------------------------------------------------------------------
 __device__ int g_peer_fault = 0;
-constexpr unsigned long long PEER_WAIT_NS = 5000000000ull;  // 5 s
+constexpr unsigned long long PEER_WAIT_NS = 5000000000ull;  // 5 s by default
+std::atomic<unsigned long long> g_peer_wait_ns{PEER_WAIT_NS};
 
 struct FlagSlots {
   uint32_t *slot[8];
@@ -545,7 +547,7 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     }
     const uint32_t *mine = static_cast<const uint32_t *>(peer_buffer_remote(m->peer_flags, rank));
     signal_slots<<<1, 32, 0, c>>>(ready, m->steps);
-    wait_slots<<<1, 32, 0, c>>>(mine, l, L, nranks, m->steps, PEER_WAIT_NS);
+    wait_slots<<<1, 32, 0, c>>>(mine, l, L, nranks, m->steps, g_peer_wait_ns.load());
     TRY(check_launch("mlp flags"));
     x.m = static_cast<char *>(m->mom1.p) + m->block_at[l] * e;
     x.v = static_cast<char *>(m->mom2.p) + m->block_at[l] * e;
@@ -636,7 +638,7 @@ int tc_mlp_step(tc_mlp *m, const void *x, const void *y, tc_comm *comm, void *lo
     // the step on this stream runs.
     const uint32_t *mine_flags = static_cast<const uint32_t *>(peer_buffer_remote(m->peer_flags, rank));
     const int count = nranks * L;
-    wait_slots<<<(count + 31) / 32, 32, 0, s>>>(mine_flags, nranks * L, 1, count, m->steps, PEER_WAIT_NS);
+    wait_slots<<<(count + 31) / 32, 32, 0, s>>>(mine_flags, nranks * L, 1, count, m->steps, g_peer_wait_ns.load());
     TRY(check_launch("mlp flags"));
   }
   // ---- Adam over every parameter (one launch over the flat blocks; the
@@ -656,6 +658,7 @@ int peer_wait_fault() {
   if (cudaMemcpyFromSymbol(&h, g_peer_fault, sizeof(int)) != cudaSuccess) return 0;
   return h;
 }
+void set_peer_wait_limit(unsigned long long ns) { g_peer_wait_ns.store(ns ? ns : PEER_WAIT_NS); }
 int peer_wait_fault_reset() {
   const int zero = 0;
   return check_cuda(cudaMemcpyToSymbol(g_peer_fault, &zero, sizeof(int)), "cudaMemcpyToSymbol");

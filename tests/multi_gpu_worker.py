@@ -217,6 +217,43 @@ def _data_parallel_bf16(comm, world, rank, sp, failures, peers):
     dp.close()
 
 
+def check_peer_wait_gives_up(comm, world, rank, sp, failures):
+    """A rank that stops stepping, between steps and with nothing of its own
+    in flight, while the others step: their waits for its flags run out
+    (the limit shortened to 50 ms), record the fault and return, and the
+    context stays usable.  No GPU faults; the step's results are not used."""
+    import time
+    dims, batch = [64, 128, 64], 16
+    rng = np.random.default_rng(13)
+    m = Mlp("f32", dims, batch, batch * world, beta2=0.99, eps=1e-4)
+    m.load([xavier(dims[l + 1], dims[l], rng) for l in range(2)], [np.zeros(dims[l + 1], np.float32) for l in range(2)])
+    m.attach(comm)
+    x = cuda.CudaStorage.store(rng.standard_normal(dims[0] * batch).astype(np.float32), "f32")
+    y = cuda.CudaStorage.store(rng.standard_normal(dims[-1] * batch).astype(np.float32), "f32")
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    if rank == 0:
+        N.call("tc_set_peer_wait_limit", 50_000_000)
+        try:
+            m.step(x, y, comm=comm, stream=torch.cuda.current_stream())
+            torch.cuda.synchronize()  # the step's kernels returned
+            fault = C.c_int(0)
+            st = N.lib().tc_device_status(C.byref(fault))
+            if st != N.ETIMEOUT or fault.value != 1:
+                failures.append(f"rank 0: a wait for a silent rank did not report (status {st}, fault {fault.value})")
+        finally:
+            N.call("tc_set_peer_wait_limit", 0)
+            N.call("tc_device_status_reset")
+        a = cuda.CudaStorage.store(np.eye(4, dtype=np.float32).ravel(), "f32")
+        if not np.array_equal(cuda.Cuda.matmul(a, a, 4, 4, 4).as_slice(), np.eye(4, dtype=np.float32).ravel()):
+            failures.append("rank 0: the context is not usable after the wait gave up")
+    else:
+        time.sleep(1.0)  # on the host, nothing in flight on this GPU
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    m.close()
+
+
 def main() -> int:
     world, rank = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -227,7 +264,8 @@ def main() -> int:
     comm = nccl_comm(torch, world, rank)
     sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     failures: list[str] = []
-    for check in (check_matmul_allgather, check_reduction_shards, check_data_parallel_step, check_data_parallel_bf16):
+    for check in (check_matmul_allgather, check_reduction_shards, check_data_parallel_step, check_data_parallel_bf16,
+                  check_peer_wait_gives_up):
         try:
             check(comm, world, rank, sp, failures)
         except Exception as e:  # a failed call is a failed check; every rank still reaches the end
