@@ -36,6 +36,7 @@ struct Place {
   int lead;
   int in_order;  // element (row, col) is data[offset + row*cols + col]
   int stat;      // -1: read from memory; else 2*k + (0 mean, 1 deviations) of statistic source k
+  int source;    // -1, or k when this place is statistic source k (its row may be staged on chip)
   int packs;     // in order, offset a multiple of 4, data aligned for 4-element vector loads
   long long offset, col_step;
   long long dims[TC_MAX_RANK - 1], steps[TC_MAX_RANK - 1];
@@ -43,6 +44,7 @@ struct Place {
 
 struct Program {
   int n_code, n_places, n_outputs, n_stat_sources;
+  int n_regs;    // registers the program writes (1 + the highest index): the register file's height
   int needs_rc;  // some place is read out of order: elements need their (row, col)
   int n_ahead;   // places read in order, whose next group is requested into L2 ahead
   int ahead[4];
@@ -86,13 +88,15 @@ __device__ __forceinline__ float load_place(const Place &pl, long long i, long l
 }
 
 // E elements of the space run through the program together: flat indices
-// i0 .. i0+n-1 (n <= E), each with its (row, col).  Registers hold E values;
-// a load of an in-order place whose E elements are 16-byte (f32) or 8-byte
-// (f16/bf16) aligned is one vector load, and so is the store of a group.
+// i0 .. i0+n-1 (n <= E), the first at (row, col) of a space `cols` wide
+// (row and col are set only for programs that read a place out of order).
+// Registers hold E values; a load of an in-order place whose E elements are
+// 16-byte (f32) or 8-byte (f16/bf16) aligned is one vector load per 4, and
+// so is the store of a group.
 template <int E> struct Group {
   long long i0;
   int n;
-  long long row[E], col[E];
+  long long row, col, cols;
 };
 
 template <int E>
@@ -100,16 +104,10 @@ __device__ __forceinline__ Group<E> make_group(long long i0, int n, long long co
   Group<E> g;
   g.i0 = i0;
   g.n = n;
-  if (!with_rc) return g;
-  long long r = i0 / cols, c = i0 - r * cols;
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    g.row[e] = r;
-    g.col[e] = c;
-    if (++c == cols) {
-      c = 0;
-      ++r;
-    }
+  g.cols = cols;
+  if (with_rc) {
+    g.row = i0 / cols;
+    g.col = i0 - g.row * cols;
   }
   return g;
 }
@@ -155,9 +153,12 @@ __device__ __forceinline__ void load_group(const Place &pl, const Group<E> &g, f
     for (int e = 0; e < E; ++e)
       if (e < g.n) v[e] = load_as(pl.data, pl.dtype, at + e);
   } else {
+    long long r = g.row, c = g.col;
 #pragma unroll
-    for (int e = 0; e < E; ++e)
-      if (e < g.n) v[e] = load_as(pl.data, pl.dtype, place_at(pl, g.i0 + e, g.row[e], g.col[e]));
+    for (int e = 0; e < E; ++e) {
+      if (e < g.n) v[e] = load_as(pl.data, pl.dtype, place_at(pl, g.i0 + e, r, c));
+      if (++c == g.cols) c = 0, ++r;
+    }
   }
 convert:
 #pragma unroll
@@ -191,28 +192,81 @@ __device__ __forceinline__ void store_group(void *out, int dtype, const Group<E>
     if (e < g.n) store_as(out, dtype, g.i0 + e, v[e]);
 }
 
-// Run the program on a group.  `stats` holds the row's statistics (2 per
-// source) for places that read one (every element of the group is in that
-// row); `sink(slot, values)` receives every store.
+// What a group's loads may read on chip instead of from memory (the row
+// kernels): the row's statistics, 2 per source (mean, deviations), and the
+// row of each statistic source staged in shared memory, `stage_cols` floats
+// apart, with the group's first element at column `col0` (a multiple of 4).
+struct OnChip {
+  const float *stats;
+  const float *stage;  // null: nothing staged
+  int stage_cols;
+  int col0;
+};
+
+// Run the program on a group; `sink(slot, values)` receives every store.
 // The interpreter's blocks are INTERP_BLOCK threads; each thread's
-// registers live in shared memory, register r's element e of thread t at
-// rf_base[(r * E + e) * INTERP_BLOCK + t] (consecutive threads, consecutive
-// banks), since registers indexed by the program cannot be machine
-// registers and would otherwise go to local memory.
+// registers live in dynamic shared memory (registers indexed by the program
+// cannot be machine registers and would otherwise go to local memory), as
+// many as the program writes: register r of thread t holds its E elements
+// at file[(r * INTERP_BLOCK + t) * E ...], one 16-byte access for E = 4.
 constexpr int INTERP_BLOCK = 128;
 
 template <int E> struct RegFile {
-  float *base;  // this thread's register 0, element 0
-  __device__ __forceinline__ float &at(int r, int e) const { return base[(r * E + e) * INTERP_BLOCK]; }
+  float *base;  // this thread's register 0
+  __device__ __forceinline__ float *row(int r) const { return base + r * (INTERP_BLOCK * E); }
+  __device__ __forceinline__ void get(int r, float v[E]) const {
+    const float *at = base + r * (INTERP_BLOCK * E);
+    if constexpr (E % 4 == 0) {
+#pragma unroll
+      for (int k = 0; k < E / 4; ++k) {
+        const float4 q = reinterpret_cast<const float4 *>(at)[k];
+        v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = at[e];
+    }
+  }
+  __device__ __forceinline__ void put(int r, const float v[E]) const {
+    float *at = base + r * (INTERP_BLOCK * E);
+    if constexpr (E % 4 == 0) {
+#pragma unroll
+      for (int k = 0; k < E / 4; ++k)
+        reinterpret_cast<float4 *>(at)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) at[e] = v[e];
+    }
+  }
 };
 
+__device__ __forceinline__ float *interp_shared() {
+  extern __shared__ float4 interp_smem[];
+  return reinterpret_cast<float *>(interp_smem);
+}
+
 template <int E> __device__ __forceinline__ RegFile<E> thread_registers() {
-  __shared__ float file[REGISTERS * E * INTERP_BLOCK];
-  return RegFile<E>{file + threadIdx.x};
+  return RegFile<E>{interp_shared() + threadIdx.x * E};
+}
+
+// A load of a staged statistic source reads the row's copy on chip.
+template <int E> __device__ __forceinline__ bool read_stage(const OnChip &chip, const Place &pl, float v[E]) {
+  if constexpr (E % 4 == 0) {
+    if (chip.stage && pl.source >= 0) {
+      const float4 *at = reinterpret_cast<const float4 *>(chip.stage + pl.source * chip.stage_cols + chip.col0);
+#pragma unroll
+      for (int k = 0; k < E / 4; ++k) {
+        const float4 q = at[k];
+        v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
+      }
+      return true;
+    }
+  }
+  return false;
 }
 
 template <class T, int E, class Sink>
-__device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, const float *stats, Sink &&sink) {
+__device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, const OnChip &chip, Sink &&sink) {
   const RegFile<E> reg = thread_registers<E>();
   for (int k = 0; k < p.n_code; ++k) {
     const tc_instr in = p.code[k];
@@ -222,8 +276,8 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
         const Place &pl = p.places[in.slot];
         if (pl.stat >= 0) {
 #pragma unroll
-          for (int e = 0; e < E; ++e) v[e] = stats[pl.stat];
-        } else {
+          for (int e = 0; e < E; ++e) v[e] = chip.stats[pl.stat];
+        } else if (!read_stage<E>(chip, pl, v)) {
           load_group<T, E>(pl, g, v);
         }
         break;
@@ -236,8 +290,8 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
       }
       case TC_I_BINARY: {
         float x[E], y[E];
-#pragma unroll
-        for (int e = 0; e < E; ++e) x[e] = reg.at(in.a, e), y[e] = reg.at(in.b, e);
+        reg.get(in.a, x);
+        reg.get(in.b, y);
         // one branch per instruction, not per element
         switch (in.op) {
           case TC_ADD:
@@ -264,14 +318,24 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
         for (int e = 0; e < E; ++e) v[e] = T::load(T::store(v[e]));
         break;
       }
-      case TC_I_UNARY:
+      case TC_I_UNARY: {
+        // element by element between the register file's rows: the analytic
+        // functions' code appears once, not once per element
+        const float *x = reg.row(in.a);
+        float *y = reg.row(in.dst);
+        if (in.op == TC_SQRT) {  // normalisations' root: a few instructions, unrolled
 #pragma unroll
-        for (int e = 0; e < E; ++e) v[e] = T::load(T::store(analytic(in.op, reg.at(in.a, e))));
-        break;
+          for (int e = 0; e < E; ++e) y[e] = T::load(T::store(__fsqrt_rn(x[e])));
+        } else {
+#pragma unroll 1
+          for (int e = 0; e < E; ++e) y[e] = T::load(T::store(analytic(in.op, x[e])));
+        }
+        continue;
+      }
       case TC_I_CMP: {
         float x[E], y[E];
-#pragma unroll
-        for (int e = 0; e < E; ++e) x[e] = reg.at(in.a, e), y[e] = reg.at(in.b, e);
+        reg.get(in.a, x);
+        reg.get(in.b, y);
         switch (in.op) {
           case TC_MIN:
 #pragma unroll
@@ -288,18 +352,18 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
         break;
       }
       default: {  // store
-#pragma unroll
-        for (int e = 0; e < E; ++e) v[e] = reg.at(in.a, e);
+        reg.get(in.a, v);
         sink(int(in.slot), v);
         continue;
       }
     }
-#pragma unroll
-    for (int e = 0; e < E; ++e) reg.at(in.dst, e) = v[e];
+    reg.put(in.dst, v);
   }
 }
 
-constexpr int GROUP = 4;
+// Elements per lane and step in the row kernels (program and statistics),
+// and columns per thread in the column sums.
+constexpr int ROW_GROUP = 8, COL_GROUP = 4;
 
 // Ask L2 for the group at flat index i0 of each in-order place the program
 // loads: a thread's next group arrives while it runs the current one.
@@ -311,112 +375,206 @@ __device__ __forceinline__ void request_ahead(const Program &p, long long i0) {
   }
 }
 
+// Ask L2 for row `row` of an in-order place: the row's `lanes` threads take
+// its 128-byte lines in turn.  Allocations start on 256-byte boundaries, so
+// the lines that hold the row's first and last bytes lie inside the place's
+// allocation.
+__device__ __forceinline__ void request_place_row(const Place &pl, long long row, long long cols, int lane,
+                                                  int lanes) {
+  const long long size = pl.dtype == TC_F32 ? 4 : 2;
+  const uintptr_t first = reinterpret_cast<uintptr_t>(pl.data) + uintptr_t((pl.offset + row * cols) * size);
+  const uintptr_t last = first + uintptr_t(cols * size) - 1;
+  for (uintptr_t at = (first & ~uintptr_t(127)) + uintptr_t(lane) * 128; at <= last; at += uintptr_t(lanes) * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(at));
+}
+
+// The same for each in-order place the program loads.
+__device__ __forceinline__ void request_row(const Program &p, long long row, int lane, int lanes) {
+  for (int k = 0; k < p.n_ahead; ++k) request_place_row(p.places[p.ahead[k]], row, p.cols, lane, lanes);
+}
+
+// The flat kernel's elements per thread and step: each program instruction
+// is decoded once for FLAT_GROUP elements.
+constexpr int FLAT_GROUP = 8;
+
 template <class T>
 __global__ void __launch_bounds__(INTERP_BLOCK) fused_kernel(const __grid_constant__ Program p) {
+  constexpr int E = FLAT_GROUP;
+  const OnChip none{nullptr, nullptr, 0, 0};
   const long long total = p.rows * p.cols;
-  const long long groups = (total + GROUP - 1) / GROUP;
+  const long long groups = (total + E - 1) / E;
   for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < groups;
        q += (long long)gridDim.x * blockDim.x) {
-    const long long i0 = q * GROUP;
-    const long long next = i0 + (long long)gridDim.x * blockDim.x * GROUP;
+    const long long i0 = q * E;
+    const long long next = i0 + (long long)gridDim.x * blockDim.x * E;
     if (next < total) request_ahead(p, next);
-    const Group<GROUP> g = make_group<GROUP>(i0, int(min((long long)GROUP, total - i0)), p.cols, p.needs_rc != 0);
-    run_group<T, GROUP>(p, g, nullptr, [&](int slot, const float *v) { store_group<GROUP>(p.out[slot], p.out_dtype[slot], g, v); });
+    const Group<E> g = make_group<E>(i0, int(min((long long)E, total - i0)), p.cols, p.needs_rc != 0);
+    run_group<T, E>(p, g, none, [&](int slot, const float *v) { store_group<E>(p.out[slot], p.out_dtype[slot], g, v); });
   }
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
+// The sum of v over the LANES threads that share a row (LANES a power of
+// two): each warp's share by an xor tree, then, above 32 lanes, the row's
+// warps in order through `scratch` (a float per warp of the block).  Every
+// thread of the block calls it the same number of times.
+template <int LANES> __device__ __forceinline__ float row_sum(float v, float *scratch) {
+  constexpr int W = LANES < 32 ? LANES : 32;
 #pragma unroll
-  for (int d = 16; d > 0; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, d));
+  for (int d = W / 2; d > 0; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, d));
+  if constexpr (LANES > 32) {
+    const int warp = threadIdx.x >> 5, first = warp / (LANES / 32) * (LANES / 32);
+    __syncthreads();  // the previous sum's reads of scratch are done
+    if ((threadIdx.x & 31) == 0) scratch[warp] = v;
+    __syncthreads();
+    v = scratch[first];
+#pragma unroll
+    for (int w = 1; w < LANES / 32; ++w) v = __fadd_rn(v, scratch[first + w]);
+  }
   return v;
 }
 
 // The mean and the sum of squared deviations of row `row` as `pl` reads it
-// (converted to T), in f32, two passes over the row by one warp; both
-// rounded to T, as Kernels::row_moments returns them (fused/mod.rs:4030-4043,
-// statistics/mod.rs:451-491).
-template <class T>
-__device__ __forceinline__ void row_moments_of(const Place &pl, long long row, long long cols, float &mean,
-                                               float &dev) {
-  const int lane = threadIdx.x & 31;
+// (converted to T), in f32, two passes over the row by its LANES threads;
+// both rounded to T, as Kernels::row_moments returns them
+// (fused/mod.rs:4030-4043, statistics/mod.rs:451-491).  Lane l adds columns
+// 8l + 8·LANES·j onwards, 8 at a time, in order, then the lanes' sums are
+// added (row_sum).  With `stage`, the first pass also keeps the row on chip
+// (lane l's columns at stage[8l + 8·LANES·j ...], read back only by lane l,
+// which takes the same columns in the program) and the second reads
+// it there: the row crosses memory once.  A thread whose row is past the
+// end (`live` false) reads nothing but takes part in the sums.
+template <class T, int LANES>
+__device__ __forceinline__ void row_moments_of(const Place &pl, long long row, long long cols, bool live,
+                                               float &mean, float &dev, float *stage, float *scratch) {
+  const int lane = threadIdx.x & (LANES - 1);
+  const long long n = live ? cols : 0;
   float s = 0.0f;
-  for (long long c0 = (long long)lane * GROUP; c0 < cols; c0 += 32 * GROUP) {
-    Group<GROUP> g = make_group<GROUP>(row * cols + c0, int(min((long long)GROUP, cols - c0)), cols);
-    float v[GROUP];
-    load_group<T, GROUP>(pl, g, v);
+#pragma unroll 2
+  for (long long c0 = (long long)lane * ROW_GROUP; c0 < n; c0 += LANES * ROW_GROUP) {
+    Group<ROW_GROUP> g =
+        make_group<ROW_GROUP>(row * cols + c0, int(min((long long)ROW_GROUP, cols - c0)), cols, !pl.in_order);
+    float v[ROW_GROUP];
+    load_group<T, ROW_GROUP>(pl, g, v);
+    if (stage)
 #pragma unroll
-    for (int e = 0; e < GROUP; ++e)
+      for (int k = 0; k < ROW_GROUP / 4; ++k)
+        reinterpret_cast<float4 *>(stage + c0)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+#pragma unroll
+    for (int e = 0; e < ROW_GROUP; ++e)
       if (e < g.n) s = __fadd_rn(s, v[e]);
   }
-  const float m = __fdiv_rn(warp_sum(s), float(cols));
+  const float m = __fdiv_rn(row_sum<LANES>(s, scratch), float(cols));
   float d = 0.0f;
-  for (long long c0 = (long long)lane * GROUP; c0 < cols; c0 += 32 * GROUP) {
-    Group<GROUP> g = make_group<GROUP>(row * cols + c0, int(min((long long)GROUP, cols - c0)), cols);
-    float v[GROUP];
-    load_group<T, GROUP>(pl, g, v);
+  for (long long c0 = (long long)lane * ROW_GROUP; c0 < n; c0 += LANES * ROW_GROUP) {
+    const int k = int(min((long long)ROW_GROUP, cols - c0));
+    float v[ROW_GROUP];
+    if (stage) {
 #pragma unroll
-    for (int e = 0; e < GROUP; ++e)
-      if (e < g.n) {
+      for (int j = 0; j < ROW_GROUP / 4; ++j) {
+        const float4 q = reinterpret_cast<const float4 *>(stage + c0)[j];
+        v[4 * j] = q.x, v[4 * j + 1] = q.y, v[4 * j + 2] = q.z, v[4 * j + 3] = q.w;
+      }
+    } else {
+      Group<ROW_GROUP> g = make_group<ROW_GROUP>(row * cols + c0, k, cols, !pl.in_order);
+      load_group<T, ROW_GROUP>(pl, g, v);
+    }
+#pragma unroll
+    for (int e = 0; e < ROW_GROUP; ++e)
+      if (e < k) {
         const float x = __fsub_rn(v[e], m);
         d = __fadd_rn(d, __fmul_rn(x, x));
       }
   }
   mean = T::load(T::store(m));
-  dev = T::load(T::store(warp_sum(d)));
+  dev = T::load(T::store(row_sum<LANES>(d, scratch)));
 }
 
-// One warp per row, each lane GROUP consecutive elements at a time.  SUM:
-// the row's values of output 0 are added (f32, rounded once to T) into
-// sums[row] instead of stored.
-template <class T, bool SUM>
-__global__ void __launch_bounds__(INTERP_BLOCK) fused_rows_kernel(const __grid_constant__ Program p, void *sums) {
-  const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.rows; row += warps) {
+// LANES threads per row (8, 32 or a block of 128, by the row's length),
+// INTERP_BLOCK / LANES rows per block at once, each row's next one requested
+// into L2 while it runs.  With `sums`, the row's values of output 0 are added
+// (f32, rounded once to T) into sums[row] instead of stored (fused_sum's
+// programs read no statistics).  With stage_cols > 0, each statistic
+// source's row is kept on chip after its statistics are taken (stage_cols
+// floats per source per row, after the register file), and the program's
+// loads of it read it there.
+template <class T, int LANES>
+__global__ void __launch_bounds__(INTERP_BLOCK, 6) fused_rows_kernel(const __grid_constant__ Program p, void *sums,
+                                                                     int stage_cols) {
+  constexpr int SLOTS = INTERP_BLOCK / LANES;
+  __shared__ float scratch[INTERP_BLOCK / 32];
+  const int slot = threadIdx.x / LANES, lane = threadIdx.x & (LANES - 1);
+  float *stage = nullptr;
+  if (stage_cols > 0)
+    stage = interp_shared() + p.n_regs * INTERP_BLOCK * ROW_GROUP + slot * p.n_stat_sources * stage_cols;
+  for (long long r0 = (long long)blockIdx.x * SLOTS; r0 < p.rows; r0 += (long long)gridDim.x * SLOTS) {
+    const long long row = r0 + slot;
+    const bool live = row < p.rows;
+    const long long next = row + (long long)gridDim.x * SLOTS;
+    if (next < p.rows) request_row(p, next, lane, LANES);
     float stats[2 * MAX_STAT_SOURCES];
     for (int k = 0; k < p.n_stat_sources; ++k)
-      row_moments_of<T>(p.places[p.stat_source[k]], row, p.cols, stats[2 * k], stats[2 * k + 1]);
+      row_moments_of<T, LANES>(p.places[p.stat_source[k]], row, p.cols, live, stats[2 * k], stats[2 * k + 1],
+                               stage ? stage + k * stage_cols : nullptr, scratch);
+    OnChip chip{stats, stage, stage_cols, 0};
     float acc = 0.0f;
-    for (long long c0 = (long long)lane * GROUP; c0 < p.cols; c0 += 32 * GROUP) {
-      if (c0 + 2 * 32 * GROUP < p.cols) request_ahead(p, row * p.cols + c0 + 2 * 32 * GROUP);
-      const Group<GROUP> g = make_group<GROUP>(row * p.cols + c0, int(min((long long)GROUP, p.cols - c0)), p.cols);
-      if (SUM) {
-        run_group<T, GROUP>(p, g, stats, [&](int, const float *v) {
+    const long long n = live ? p.cols : 0;
+    for (long long c0 = (long long)lane * ROW_GROUP; c0 < n; c0 += LANES * ROW_GROUP) {
+      const Group<ROW_GROUP> g = make_group<ROW_GROUP>(row * p.cols + c0, int(min((long long)ROW_GROUP, p.cols - c0)),
+                                                       p.cols, p.needs_rc != 0);
+      chip.col0 = int(c0);
+      run_group<T, ROW_GROUP>(p, g, chip, [&](int slot, const float *v) {
+        if (sums) {
 #pragma unroll
-          for (int e = 0; e < GROUP; ++e)
+          for (int e = 0; e < ROW_GROUP; ++e)
             if (e < g.n) acc = __fadd_rn(acc, v[e]);
-        });
-      } else {
-        run_group<T, GROUP>(p, g, stats,
-                            [&](int slot, const float *v) { store_group<GROUP>(p.out[slot], p.out_dtype[slot], g, v); });
-      }
+        } else {
+          store_group<ROW_GROUP>(p.out[slot], p.out_dtype[slot], g, v);
+        }
+      });
     }
-    if (SUM) {
-      acc = warp_sum(acc);
-      if (lane == 0) static_cast<typename T::S *>(sums)[row] = T::store(acc);
+    if (sums) {
+      acc = row_sum<LANES>(acc, scratch);
+      if (live && lane == 0) static_cast<typename T::S *>(sums)[row] = T::store(acc);
     }
   }
 }
 
-// fused_sum along columns: thread = column, block row = a band of `band`
-// rows; partial[band][col] in f32 (or the rounded sum itself with one band).
+// fused_sum along columns: a thread takes COL_GROUP consecutive columns over
+// a band of `band` rows.  A block holds `groups` column groups side by side
+// and INTERP_BLOCK / groups bands of them one under another (narrow matrices
+// fill the block with bands); band b = blockIdx.y * (INTERP_BLOCK / groups)
+// + the thread's place in the block, for b < bands.  partial[b][col] in f32,
+// or the rounded sums themselves when there is one band.  Each column's
+// values are added row after row (the row four ahead requested into L2),
+// then the bands' sums in band order.
 template <class T>
-__global__ void __launch_bounds__(INTERP_BLOCK) fused_cols_kernel(const __grid_constant__ Program p, long long band,
-                                                         float *partial, void *sums) {
-  const long long col = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= p.cols) return;
-  const long long r0 = (long long)blockIdx.y * band, r1 = min(p.rows, r0 + band);
-  float acc = 0.0f;
+__global__ void __launch_bounds__(INTERP_BLOCK) fused_cols_kernel(const __grid_constant__ Program p, int groups,
+                                                                  long long band, long long bands, float *partial,
+                                                                  void *sums) {
+  const int per_block = INTERP_BLOCK / groups, sub = threadIdx.x / groups;
+  const long long c0 = ((long long)blockIdx.x * groups + threadIdx.x % groups) * COL_GROUP;
+  if (sub >= per_block || c0 >= p.cols) return;
+  const int n = int(min((long long)COL_GROUP, p.cols - c0));
+  const OnChip none{nullptr, nullptr, 0, 0};
+  const long long b = (long long)blockIdx.y * per_block + sub;
+  if (b >= bands) return;
+  const long long r0 = b * band, r1 = min(p.rows, r0 + band);
+  float acc[COL_GROUP] = {};
   for (long long row = r0; row < r1; ++row) {
-    Group<1> g;
-    g.i0 = row * p.cols + col;
-    g.n = 1;
-    g.row[0] = row;
-    g.col[0] = col;
-    run_group<T, 1>(p, g, nullptr, [&](int, const float *v) { acc = __fadd_rn(acc, v[0]); });
+    if (row + 4 < r1) request_ahead(p, (row + 4) * p.cols + c0);
+    Group<COL_GROUP> g;
+    g.i0 = row * p.cols + c0;
+    g.n = n;
+    g.row = row, g.col = c0, g.cols = p.cols;
+    run_group<T, COL_GROUP>(p, g, none, [&](int, const float *v) {
+#pragma unroll
+      for (int e = 0; e < COL_GROUP; ++e) acc[e] = __fadd_rn(acc[e], v[e]);
+    });
   }
-  if (gridDim.y == 1) static_cast<typename T::S *>(sums)[col] = T::store(acc);
-  else partial[(long long)blockIdx.y * p.cols + col] = acc;
+  for (int e = 0; e < n; ++e) {
+    if (bands == 1) static_cast<typename T::S *>(sums)[c0 + e] = T::store(acc[e]);
+    else partial[b * p.cols + c0 + e] = acc[e];
+  }
 }
 
 template <class T>
@@ -428,14 +586,21 @@ __global__ void __launch_bounds__(256) cols_finish(const float *partial, long lo
   }
 }
 
-template <class T>
-__global__ void __launch_bounds__(256) row_moments_kernel(const __grid_constant__ Place pl, long long rows,
-                                                          long long cols, void *means, void *devs) {
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+// tc_row_moments: LANES threads per row, as the row kernels.
+template <class T, int LANES>
+__global__ void __launch_bounds__(INTERP_BLOCK) row_moments_kernel(const __grid_constant__ Place pl, long long rows,
+                                                                   long long cols, void *means, void *devs) {
+  constexpr int SLOTS = INTERP_BLOCK / LANES;
+  __shared__ float scratch[INTERP_BLOCK / 32];
+  const int slot = threadIdx.x / LANES, lane = threadIdx.x & (LANES - 1);
+  for (long long r0 = (long long)blockIdx.x * SLOTS; r0 < rows; r0 += (long long)gridDim.x * SLOTS) {
+    const long long row = r0 + slot;
+    const bool live = row < rows;
+    const long long next = row + (long long)gridDim.x * SLOTS;
+    if (next < rows && pl.in_order) request_place_row(pl, next, cols, lane, LANES);
     float m, d;
-    row_moments_of<T>(pl, row, cols, m, d);
-    if ((threadIdx.x & 31) == 0) {
+    row_moments_of<T, LANES>(pl, row, cols, live, m, d, nullptr, scratch);
+    if (live && lane == 0) {
       static_cast<typename T::S *>(means)[row] = T::store(m);
       static_cast<typename T::S *>(devs)[row] = T::store(d);
     }
@@ -452,6 +617,7 @@ int take_place(const tc_place &q, uint32_t j, size_t rows, size_t cols, Place &p
   pl.dtype = q.dtype;
   pl.lead = int(q.lead);
   pl.stat = -1;
+  pl.source = -1;
   pl.offset = (long long)q.offset;
   pl.col_step = (long long)q.col_step;
   long long rows_folded = 1;
@@ -495,6 +661,7 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
   p.n_outputs = int(n_outputs);
   p.rows = (long long)rows;
   p.cols = (long long)cols;
+  p.n_regs = 1;
   bool written[REGISTERS] = {false};
   for (uint32_t k = 0; k < n_code; ++k) {
     const tc_instr &in = code[k];
@@ -511,6 +678,7 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     if (in.code != TC_I_STORE) {
       if (in.dst >= REGISTERS) return fail(TC_EINVAL, "fused: register %u", in.dst);
       written[in.dst] = true;
+      p.n_regs = std::max(p.n_regs, int(in.dst) + 1);
     }
     p.code[k] = in;
   }
@@ -524,6 +692,8 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
   for (uint32_t j = 0; j < n_places; ++j) {
     if (is_stat[j]) {
       p.places[j] = Place{};
+      p.places[j].stat = -1;
+      p.places[j].source = -1;
       continue;
     }
     if (int st = take_place(places[j], j, rows, cols, p.places[j])) return st;
@@ -538,6 +708,7 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     if (k == p.n_stat_sources) {
       if (k == MAX_STAT_SOURCES) return fail(TC_EINVAL, "fused: statistics of more than %d inputs", MAX_STAT_SOURCES);
       p.stat_source[p.n_stat_sources++] = int(of);
+      p.places[of].source = k;
     }
     p.places[stats[s].into_place].stat = 2 * k + (stats[s].statistic == TC_ROW_DEVIATIONS ? 1 : 0);
   }
@@ -549,15 +720,53 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
   return TC_OK;
 }
 
-// Warps per row for the interpreter's row kernels: INTERP_BLOCK / 32 rows
-// per block, at most 6 blocks per SM (their register files).
-unsigned interp_row_grid(long long rows) {
-  constexpr int W = INTERP_BLOCK / 32;
-  return unsigned(std::max(1LL, std::min<long long>((rows + W - 1) / W, (long long)sm_count() * 6)));
+// The register file of a block of the interpreter: the program's registers,
+// E elements per thread.
+size_t register_file_bytes(const Program &p, int E) { return size_t(p.n_regs) * INTERP_BLOCK * E * sizeof(float); }
+
+// Blocks for an interpreter kernel with `smem` bytes of dynamic shared
+// memory: as many as fit on every SM at once, at most `wanted`.
+template <class K> unsigned interp_grid(K kernel, size_t smem, long long wanted) {
+  // above 48 KB with the kernel's own static shared memory, a launch needs
+  // the kernel's limit raised first
+  if (smem > 40 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, INTERP_BLOCK, smem) != cudaSuccess) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  return unsigned(std::max(1LL, std::min(wanted, (long long)sm_count() * std::max(per_sm, 1))));
 }
 
-unsigned row_grid(long long rows) {
-  return unsigned(std::max(1LL, std::min<long long>((rows + 7) / 8, (long long)sm_count() * 8)));
+// The row kernels stage each statistic source's row on chip while the
+// block's shared memory stays within this bound (four blocks per SM).
+constexpr size_t STAGE_LIMIT = 54 * 1024;
+
+// Threads per row for rows of `cols` elements: 8 lanes up to 4 groups of
+// ROW_GROUP each, a warp up to 8 groups each, else a block of INTERP_BLOCK.  f(lanes) with lanes a
+// compile-time constant.
+template <class F> int with_lanes(long long cols, F &&f) {
+  if (cols <= 4 * 8 * ROW_GROUP) return f(std::integral_constant<int, 8>{});
+  if (cols <= 8 * 32 * ROW_GROUP) return f(std::integral_constant<int, 32>{});
+  return f(std::integral_constant<int, INTERP_BLOCK>{});
+}
+
+// Launch the row kernel (statistics, or sums along rows) for `p`.
+// With `sums`: fused_sum along rows.
+template <class T> int launch_rows(const Program &p, void *sums, cudaStream_t s, const char *what) {
+  return with_lanes(p.cols, [&](auto lanes) {
+    constexpr int LANES = decltype(lanes)::value, SLOTS = INTERP_BLOCK / LANES;
+    const long long wanted = (p.rows + SLOTS - 1) / SLOTS;
+    const size_t regs = register_file_bytes(p, ROW_GROUP);
+    const int stage_cols = int((p.cols + ROW_GROUP - 1) / ROW_GROUP * ROW_GROUP);
+    const size_t staged = regs + size_t(SLOTS) * p.n_stat_sources * stage_cols * sizeof(float);
+    auto k = fused_rows_kernel<T, LANES>;
+    if (p.n_stat_sources > 0 && p.cols <= (1LL << 30) && staged <= STAGE_LIMIT)
+      k<<<interp_grid(k, staged, wanted), INTERP_BLOCK, staged, s>>>(p, sums, stage_cols);
+    else
+      k<<<interp_grid(k, regs, wanted), INTERP_BLOCK, regs, s>>>(p, sums, 0);
+    return check_launch(what);
+  });
 }
 
 }  // namespace
@@ -576,9 +785,10 @@ int tc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t
   if (rows == 0 || cols == 0) return TC_OK;
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
-    // 32 KB of register file per block: 6 blocks per SM
-    fused_kernel<T><<<grid_for((rows * cols + GROUP - 1) / GROUP, INTERP_BLOCK, 6), INTERP_BLOCK, 0,
-                      as_stream(stream)>>>(p);
+    const size_t regs = register_file_bytes(p, FLAT_GROUP);
+    auto k = fused_kernel<T>;
+    const long long wanted = ((long long)(rows * cols) + FLAT_GROUP * INTERP_BLOCK - 1) / (FLAT_GROUP * INTERP_BLOCK);
+    k<<<interp_grid(k, regs, wanted), INTERP_BLOCK, regs, as_stream(stream)>>>(p);
     return check_launch("fused program");
   });
 }
@@ -594,8 +804,7 @@ int tc_fused_with_statistics(int dtype, size_t rows, size_t cols, const tc_instr
   if (rows == 0 || cols == 0) return TC_OK;
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
-    fused_rows_kernel<T, false><<<interp_row_grid((long long)rows), INTERP_BLOCK, 0, as_stream(stream)>>>(p, nullptr);
-    return check_launch("fused program with statistics");
+    return launch_rows<T>(p, nullptr, as_stream(stream), "fused program with statistics");
   });
 }
 
@@ -620,17 +829,22 @@ int tc_fused_sum(int dtype, size_t rows, size_t cols, const tc_instr *code, uint
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     if (axis == TC_ROWS) {
-      fused_rows_kernel<T, true><<<interp_row_grid((long long)rows), INTERP_BLOCK, 0, s>>>(p, sums);
-      return check_launch("fused sum (rows)");
+      return launch_rows<T>(p, sums, s, "fused sum (rows)");
     }
-    const long long col_blocks = ((long long)cols + INTERP_BLOCK - 1) / INTERP_BLOCK;
-    const long long want = std::max(1LL, (long long)sm_count() * 8 / col_blocks);
+    // column groups side by side in a block, the rest of the block bands
+    const long long col_groups = ((long long)cols + COL_GROUP - 1) / COL_GROUP;
+    const int groups = int(std::min<long long>(INTERP_BLOCK, col_groups)), per_block = INTERP_BLOCK / groups;
+    const long long col_blocks = (col_groups + groups - 1) / groups;
+    // about 8 blocks per SM, each band 16 rows or more
+    const long long want = std::max(1LL, (long long)sm_count() * 8 / col_blocks) * per_block;
     const long long band = std::max(16LL, ((long long)rows + want - 1) / want);
     const long long bands = ((long long)rows + band - 1) / band;
+    const long long band_rows = (bands + per_block - 1) / per_block;  // blockIdx.y
     float *partial = nullptr;
     if (bands > 1)
       if (int st = scratch(size_t(bands) * cols * sizeof(float), reinterpret_cast<void **>(&partial), s)) return st;
-    fused_cols_kernel<T><<<dim3(unsigned(col_blocks), unsigned(bands)), INTERP_BLOCK, 0, s>>>(p, band, partial, sums);
+    fused_cols_kernel<T><<<dim3(unsigned(col_blocks), unsigned(band_rows)), INTERP_BLOCK,
+                           register_file_bytes(p, COL_GROUP), s>>>(p, groups, band, bands, partial, sums);
     if (int st = check_launch("fused sum (columns)")) return st;
     if (bands > 1) {
       cols_finish<T><<<grid_for(cols, 256, 4), 256, 0, s>>>(partial, bands, (long long)cols, sums);
@@ -675,9 +889,13 @@ int tc_row_moments(int dtype, const tc_place *place, size_t rows, size_t cols, v
   if (int st = take_place(*place, 0, rows, cols, pl)) return st;
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
-    row_moments_kernel<T><<<row_grid((long long)rows), 256, 0, as_stream(stream)>>>(pl, (long long)rows,
-                                                                                  (long long)cols, means, deviations);
-    return check_launch("row moments");
+    return with_lanes((long long)cols, [&](auto lanes) {
+      constexpr int LANES = decltype(lanes)::value, SLOTS = INTERP_BLOCK / LANES;
+      auto k = row_moments_kernel<T, LANES>;
+      k<<<interp_grid(k, 0, ((long long)rows + SLOTS - 1) / SLOTS), INTERP_BLOCK, 0, as_stream(stream)>>>(
+          pl, (long long)rows, (long long)cols, means, deviations);
+      return check_launch("row moments");
+    });
   });
 }
 

@@ -262,11 +262,16 @@ def test_oracle_layer_norm_doc_example():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("rows,cols", [(2, 2), (64, 1000), (1000, 64), (7, 1), (3, 4099)])
+@pytest.mark.parametrize("rows,cols", [(2, 2), (64, 1000), (1000, 64), (7, 1), (3, 4099), (37, 131), (3, 20001),
+                                       (5, 4096)])
 def test_fused_with_statistics_matches_the_oracle(device, dtype, rows, cols):
     """The row statistics are sums in another order (rel 1e-5·√cols), so
     the normalized values agree within that for f32, and within a step of
-    the element type for f16/bf16; the 2x2 doc example is exact."""
+    the element type for f16/bf16; the 2x2 doc example is exact.  The
+    shapes take each row width the kernel has (8 lanes, a warp or a block
+    per row), with the row kept on chip (4096 and 4099 columns: more than
+    48 KB of shared memory with the register file) and, at 20001 columns,
+    read again from memory."""
     from tensorcrate_b200 import cuda
     x_host = np.array([1.0, 3.0, 10.0, 20.0], np.float32) if (rows, cols) == (2, 2) else normal(rows * cols, 12)
     x = O.narrow(x_host * np.float32(3.0) + np.float32(1.0) if (rows, cols) != (2, 2) else x_host, dtype)
@@ -302,7 +307,7 @@ def sum_program():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("rows,cols", [(100, 300), (3000, 7), (1, 5000), (5000, 1), (2048, 1024)])
+@pytest.mark.parametrize("rows,cols", [(100, 300), (3000, 7), (1, 5000), (5000, 1), (2048, 1024), (37, 1027)])
 @pytest.mark.parametrize("axis", [N.ROWS, N.COLUMNS])
 def test_fused_sum_matches_the_oracle(device, dtype, rows, cols, axis):
     """A program's output summed along an axis without being stored, against
