@@ -1201,7 +1201,9 @@ def run_trait(args, torch, world, rank, comm):
     y = cuda.CudaStorage.store(rng.uniform(0.5, 2.0, n).astype(np.float32), "f32")
     o1, o2 = cuda.CudaStorage("f32", n), cuda.CudaStorage("f32", n)
     ops, hbm_bytes, hbm_ms = {}, 0, 0.0
-    t_args = argparse.Namespace(steps=args.steps, warmup=args.warmup, min_seconds=0.2)
+    # each call timed for 0.2 s at least (less only when asked: a short
+    # profiling run)
+    t_args = argparse.Namespace(steps=args.steps, warmup=args.warmup, min_seconds=min(0.2, args.min_seconds))
 
     def measure(name, fn, byts, flops=None, bound="hbm", peak=None):
         nonlocal hbm_bytes, hbm_ms

@@ -158,6 +158,157 @@ __global__ void __launch_bounds__(256) correlate_input_gradient_direct(const typ
   }
 }
 
+// Windows at most NARROW taps wide, the width WC a compile-time constant:
+// the same sums in the same order as the kernels above, with the tap loop
+// unrolled (no index arithmetic, no register shifts), the taps staged
+// already flipped where the sum flips them (tap (wr, wc) of a flipped sum is
+// staged tap taps-1-(wr·WC+wc)), and each window row's input values for a
+// group loaded at once, four to a vector load when the rows are aligned.
+constexpr int NARROW = 8;
+
+// Four values of storage type S from a 16-byte (f32) or 8-byte (16-bit)
+// aligned address.
+template <class T> __device__ __forceinline__ void load4(const typename T::S *x, float *v) {
+  if constexpr (sizeof(typename T::S) == 4) {
+    const float4 q = __ldg(reinterpret_cast<const float4 *>(x));
+    v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+  } else {
+    const uint2 q = __ldg(reinterpret_cast<const uint2 *>(x));
+    v[0] = T::load(uint16_t(q.x)), v[1] = T::load(uint16_t(q.x >> 16));
+    v[2] = T::load(uint16_t(q.y)), v[3] = T::load(uint16_t(q.y >> 16));
+  }
+}
+
+template <class T> __device__ __forceinline__ void stage_taps(const typename T::S *win, const Window &w, int wc,
+                                                              float *taps_sh) {
+  const int taps = int(w.win_rows) * wc;
+  for (int t = threadIdx.x; t < taps; t += blockDim.x) taps_sh[t] = T::load(win[w.flip ? taps - 1 - t : t]);
+  __syncthreads();
+}
+
+// Output (row, c0 + j) sums in(row + wr, c0 + j + wc) · tap(wr, wc); `vec`:
+// rows start on the vector boundary (in_cols a multiple of 4, `in` aligned).
+template <class T, int WC>
+__global__ void __launch_bounds__(256) correlate_narrow(const typename T::S *in, const typename T::S *win,
+                                                        typename T::S *out, Window w, bool vec) {
+  __shared__ float taps_sh[SMEM_TAPS];
+  stage_taps<T>(win, w, WC, taps_sh);
+  constexpr int NV = (OUTS + WC - 1 + 3) / 4 * 4;  // values a group reads per window row, whole vectors
+  const long long groups = (w.out_cols + OUTS - 1) / OUTS, total = w.out_rows * groups;
+  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (long long)gridDim.x * blockDim.x) {
+    const long long row = o / groups, c0 = (o - row * groups) * OUTS;
+    const int n = int(min((long long)OUTS, w.out_cols - c0));
+    const bool fast = vec && n == OUTS && c0 + NV <= w.in_cols;
+    float sum[OUTS];
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j) sum[j] = 0.0f;
+    for (long long wr = 0; wr < w.win_rows; ++wr) {
+      const typename T::S *x = in + (row + wr) * w.in_cols + c0;
+      float v[NV];
+      if (fast) {
+#pragma unroll
+        for (int q = 0; q < NV / 4; ++q) load4<T>(x + 4 * q, v + 4 * q);
+      } else {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) v[j] = c0 + j < w.in_cols ? T::load(__ldg(x + j)) : 0.0f;
+      }
+      const float *k = taps_sh + wr * WC;
+#pragma unroll
+      for (int wc = 0; wc < WC; ++wc) {
+        const float kk = k[wc];
+#pragma unroll
+        for (int j = 0; j < OUTS; ++j) sum[j] = __fadd_rn(sum[j], __fmul_rn(v[j + wc], kk));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j)
+      if (j < n) out[row * w.out_cols + c0 + j] = T::store(sum[j]);
+  }
+}
+
+// The input gradient for windows at most NARROW wide: output (row, c0 + j)
+// sums adj(row - wr, c0 + j - wc) · tap(wr, wc) over the taps in order,
+// skipping the taps whose adjoint column is outside the row (the fast path
+// takes only groups whose columns are all inside: nothing to skip).
+template <class T, int WC>
+__global__ void __launch_bounds__(256) correlate_input_gradient_narrow(const typename T::S *adj,
+                                                                       const typename T::S *win, typename T::S *out,
+                                                                       Window w, bool vec) {
+  __shared__ float taps_sh[SMEM_TAPS];
+  stage_taps<T>(win, w, WC, taps_sh);
+  // a group reads adjoint columns c0-(WC-1) .. c0+OUTS-1; loaded from c0-LEAD
+  // (a vector boundary), the column c0 + j - wc sits at b[j - wc + LEAD]
+  constexpr int LEAD = (WC - 1 + 3) / 4 * 4, NB = (LEAD + OUTS + 3) / 4 * 4, NV = OUTS + WC - 1;
+  const long long groups = (w.out_cols + OUTS - 1) / OUTS, total = w.out_rows * groups;
+  for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (long long)gridDim.x * blockDim.x) {
+    const long long row = o / groups, c0 = (o - row * groups) * OUTS;
+    const int n = int(min((long long)OUTS, w.out_cols - c0));
+    const long long a0 = c0 - LEAD;
+    const bool fast = vec && n == OUTS && a0 >= 0 && a0 + NB <= w.in_cols;
+    float sum[OUTS];
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j) sum[j] = 0.0f;
+    const long long wr0 = max(0LL, row - (w.in_rows - 1)), wr1 = min(w.win_rows - 1, row);
+    for (long long wr = wr0; wr <= wr1; ++wr) {
+      const typename T::S *a = adj + (row - wr) * w.in_cols;
+      const float *k = taps_sh + wr * WC;
+      if (fast) {
+        float b[NB];
+#pragma unroll
+        for (int q = 0; q < NB / 4; ++q) load4<T>(a + a0 + 4 * q, b + 4 * q);
+#pragma unroll
+        for (int wc = 0; wc < WC; ++wc) {
+          const float kk = k[wc];
+#pragma unroll
+          for (int j = 0; j < OUTS; ++j) sum[j] = __fadd_rn(sum[j], __fmul_rn(b[j - wc + LEAD], kk));
+        }
+      } else {
+        // b[i] holds column c0 - (WC-1) + i (0 outside the row, never added)
+        float b[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const long long col = c0 - (WC - 1) + i;
+          b[i] = col >= 0 && col < w.in_cols ? T::load(__ldg(a + col)) : 0.0f;
+        }
+#pragma unroll
+        for (int wc = 0; wc < WC; ++wc) {
+          const float kk = k[wc];
+#pragma unroll
+          for (int j = 0; j < OUTS; ++j) {
+            const long long col = c0 + j - wc;
+            if (j < n && col >= 0 && col < w.in_cols) sum[j] = __fadd_rn(sum[j], __fmul_rn(b[j - wc + WC - 1], kk));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < OUTS; ++j)
+      if (j < n) out[row * w.out_cols + c0 + j] = T::store(sum[j]);
+  }
+}
+
+// f(width) with width = WC as a compile-time constant, 1 .. NARROW.
+template <class F> int with_width(long long wc, F &&f) {
+  switch (wc) {
+    case 1: return f(std::integral_constant<int, 1>{});
+    case 2: return f(std::integral_constant<int, 2>{});
+    case 3: return f(std::integral_constant<int, 3>{});
+    case 4: return f(std::integral_constant<int, 4>{});
+    case 5: return f(std::integral_constant<int, 5>{});
+    case 6: return f(std::integral_constant<int, 6>{});
+    case 7: return f(std::integral_constant<int, 7>{});
+    default: return f(std::integral_constant<int, 8>{});
+  }
+}
+
+// Rows of `cols` elements of S starting at `p` all start on a 4-element
+// vector boundary.
+template <class S> bool rows_on_vectors(const void *p, long long cols) {
+  return cols % 4 == 0 && (reinterpret_cast<uintptr_t>(p) & (4 * sizeof(S) - 1)) == 0;
+}
+
 // pad (kernels.rs:1575-1601): zeros around the input, bits moved; a block
 // per output row in turn, its threads along the row (no division).
 template <class E>
@@ -213,6 +364,13 @@ int run_correlate(int dtype, const Window &w, const void *in, const void *win, v
       const unsigned grid = unsigned(std::min<long long>(outputs, (long long)sm_count() * 8));
       correlate_shared<T><<<grid, 256, 0, s>>>(static_cast<const S *>(in), static_cast<const S *>(win),
                                                static_cast<S *>(out), w);
+    } else if (w.win_cols <= NARROW && taps <= SMEM_TAPS) {
+      const bool vec = rows_on_vectors<S>(in, w.in_cols);
+      return with_width(w.win_cols, [&](auto width) {
+        correlate_narrow<T, decltype(width)::value><<<grid_for((outputs + OUTS - 1) / OUTS, 256, 8), 256, 0, s>>>(
+            static_cast<const S *>(in), static_cast<const S *>(win), static_cast<S *>(out), w, vec);
+        return check_launch("correlate");
+      });
     } else {
       correlate_direct<T><<<grid_for((outputs + OUTS - 1) / OUTS, 256, 8), 256, 0, s>>>(static_cast<const S *>(in),
                                                                       static_cast<const S *>(win),
@@ -259,8 +417,16 @@ int tc_correlate_input_gradient(int dtype, size_t adjoint_rows, size_t adjoint_c
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     using S = typename T::S;
-    correlate_input_gradient_direct<T><<<grid_for(w.out_rows * ((w.out_cols + OUTS - 1) / OUTS), 256, 8), 256, 0,
-                                         as_stream(stream)>>>(
+    const unsigned grid = grid_for(w.out_rows * ((w.out_cols + OUTS - 1) / OUTS), 256, 8);
+    if (w.win_cols <= NARROW && w.win_rows * w.win_cols <= SMEM_TAPS) {
+      const bool vec = rows_on_vectors<S>(adjoint, w.in_cols);
+      return with_width(w.win_cols, [&](auto width) {
+        correlate_input_gradient_narrow<T, decltype(width)::value><<<grid, 256, 0, as_stream(stream)>>>(
+            static_cast<const S *>(adjoint), static_cast<const S *>(window), static_cast<S *>(out), w, vec);
+        return check_launch("correlate_input_gradient");
+      });
+    }
+    correlate_input_gradient_direct<T><<<grid, 256, 0, as_stream(stream)>>>(
         static_cast<const S *>(adjoint), static_cast<const S *>(window), static_cast<S *>(out), w);
     return check_launch("correlate_input_gradient");
   });

@@ -48,7 +48,9 @@ def test_correlate_worked_examples(device, k):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("shape,wshape", [((8, 9), (3, 2)), ((64, 100), (5, 7)), ((1, 1), (1, 1)),
-                                          ((33, 257), (33, 1)), ((300, 40), (1, 40)), ((60, 60), (60, 60))])
+                                          ((33, 257), (33, 1)), ((300, 40), (1, 40)), ((60, 60), (60, 60)),
+                                          ((40, 136), (5, 5)), ((21, 203), (3, 8)), ((19, 64), (4, 6)),
+                                          ((12, 40), (2, 9))])
 @pytest.mark.parametrize("flip", [False, True])
 def test_correlate_is_the_hosts_bits(device, dtype, shape, wshape, flip):
     x = O.narrow(uniform(shape[0] * shape[1], 1), dtype)
@@ -113,7 +115,8 @@ def test_window_gradient_with_many_taps_within_sum_rounding(device, dtype):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("ashape,wshape", [((30, 40), (3, 5)), ((2, 3), (5, 4)), ((17, 1), (1, 1)),
-                                           ((64, 64), (7, 7))])
+                                           ((64, 64), (7, 7)), ((50, 132), (5, 5)), ((19, 77), (3, 8)),
+                                           ((33, 64), (2, 4)), ((9, 40), (3, 9))])
 @pytest.mark.parametrize("forward_flip", [False, True])
 def test_correlate_input_gradient_is_the_hosts_bits(device, dtype, ashape, wshape, forward_flip):
     (ar, ac), (wr, wc) = ashape, wshape
