@@ -265,11 +265,34 @@ template <int E> __device__ __forceinline__ bool read_stage(const OnChip &chip, 
   return false;
 }
 
+// How a value moves between instructions (in the program's copy of each
+// instruction, the `reserved` field; worked out by build_program): operand a
+// or b is the result of the instruction just before (held in registers, not
+// read from the file), and the result is also needed later than the next
+// instruction (written to the file).  A unary operation other than the root
+// works between the file's rows: its operand is always in the file and its
+// result always goes there.
+enum : uint16_t { A_PREV = 1, B_PREV = 2, SPILL = 4 };
+
+template <int E> __device__ __forceinline__ void operand(const RegFile<E> &reg, int r, bool from_prev,
+                                                         const float prev[E], float x[E]) {
+  if (from_prev) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = prev[e];
+  } else {
+    reg.get(r, x);
+  }
+}
+
 template <class T, int E, class Sink>
 __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, const OnChip &chip, Sink &&sink) {
   const RegFile<E> reg = thread_registers<E>();
+  float prev[E];  // the last instruction's result
+#pragma unroll
+  for (int e = 0; e < E; ++e) prev[e] = 0.0f;
   for (int k = 0; k < p.n_code; ++k) {
     const tc_instr in = p.code[k];
+    const uint16_t f = in.reserved;
     float v[E];
     switch (in.code) {
       case TC_I_LOAD: {
@@ -290,8 +313,8 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
       }
       case TC_I_BINARY: {
         float x[E], y[E];
-        reg.get(in.a, x);
-        reg.get(in.b, y);
+        operand<E>(reg, in.a, f & A_PREV, prev, x);
+        operand<E>(reg, in.b, f & B_PREV, prev, y);
         // one branch per instruction, not per element
         switch (in.op) {
           case TC_ADD:
@@ -319,23 +342,25 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
         break;
       }
       case TC_I_UNARY: {
+        if (in.op == TC_SQRT) {  // normalisations' root: a few instructions, unrolled
+          float x[E];
+          operand<E>(reg, in.a, f & A_PREV, prev, x);
+#pragma unroll
+          for (int e = 0; e < E; ++e) v[e] = T::load(T::store(__fsqrt_rn(x[e])));
+          break;
+        }
         // element by element between the register file's rows: the analytic
         // functions' code appears once, not once per element
         const float *x = reg.row(in.a);
         float *y = reg.row(in.dst);
-        if (in.op == TC_SQRT) {  // normalisations' root: a few instructions, unrolled
-#pragma unroll
-          for (int e = 0; e < E; ++e) y[e] = T::load(T::store(__fsqrt_rn(x[e])));
-        } else {
 #pragma unroll 1
-          for (int e = 0; e < E; ++e) y[e] = T::load(T::store(analytic(in.op, x[e])));
-        }
+        for (int e = 0; e < E; ++e) y[e] = T::load(T::store(analytic(in.op, x[e])));
         continue;
       }
       case TC_I_CMP: {
         float x[E], y[E];
-        reg.get(in.a, x);
-        reg.get(in.b, y);
+        operand<E>(reg, in.a, f & A_PREV, prev, x);
+        operand<E>(reg, in.b, f & B_PREV, prev, y);
         switch (in.op) {
           case TC_MIN:
 #pragma unroll
@@ -352,12 +377,14 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
         break;
       }
       default: {  // store
-        reg.get(in.a, v);
+        operand<E>(reg, in.a, f & A_PREV, prev, v);
         sink(int(in.slot), v);
         continue;
       }
     }
-    reg.put(in.dst, v);
+    if (f & SPILL) reg.put(in.dst, v);
+#pragma unroll
+    for (int e = 0; e < E; ++e) prev[e] = v[e];
   }
 }
 
@@ -644,6 +671,37 @@ int take_place(const tc_place &q, uint32_t j, size_t rows, size_t cols, Place &p
   return TC_OK;
 }
 
+// Which values the interpreter forwards in registers (A_PREV, B_PREV) and
+// which it writes to the register file (SPILL), from the registers each
+// instruction reads and writes.  A result that only the next instruction
+// reads stays in registers; one read later, before the register is written
+// again, goes to the file; a unary operation other than the root neither
+// takes its operand from registers nor leaves its result there.
+void mark_forwarding(Program &p) {
+  auto writes = [](const tc_instr &in) { return in.code != TC_I_STORE; };
+  auto reads_a = [](const tc_instr &in) {
+    return in.code == TC_I_BINARY || in.code == TC_I_UNARY || in.code == TC_I_CMP || in.code == TC_I_STORE;
+  };
+  auto reads_b = [](const tc_instr &in) { return in.code == TC_I_BINARY || in.code == TC_I_CMP; };
+  auto generic_unary = [](const tc_instr &in) { return in.code == TC_I_UNARY && in.op != TC_SQRT; };
+  for (int k = 0; k < p.n_code; ++k) {
+    tc_instr &in = p.code[k];
+    if (!writes(in) || generic_unary(in)) continue;  // no result, or one that goes to the file itself
+    const int r = in.dst;
+    bool to_file = false;
+    for (int j = k + 1; j < p.n_code; ++j) {
+      tc_instr &next = p.code[j];
+      const bool by_a = reads_a(next) && next.a == r, by_b = reads_b(next) && next.b == r;
+      if (by_a || by_b) {
+        if (j == k + 1 && !generic_unary(next)) next.reserved |= (by_a ? A_PREV : 0) | (by_b ? B_PREV : 0);
+        else to_file = true;
+      }
+      if (writes(next) && next.dst == r) break;  // read (if at all) before it is written again
+    }
+    if (to_file) in.reserved |= SPILL;
+  }
+}
+
 // Validate a program and fill `p`.  Places listed as statistics (`stats`)
 // need no data: their loads read the row's statistic instead.
 int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t n_code,
@@ -681,7 +739,9 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
       p.n_regs = std::max(p.n_regs, int(in.dst) + 1);
     }
     p.code[k] = in;
+    p.code[k].reserved = 0;
   }
+  mark_forwarding(p);
   bool is_stat[MAX_PLACES] = {false};
   for (uint32_t s = 0; s < n_stats; ++s) {
     if (stats[s].into_place >= n_places || stats[s].of_place >= n_places ||

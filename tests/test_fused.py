@@ -388,3 +388,59 @@ def test_matmul_program_matches_the_oracle(device, dtype, m, k, n):
     g, w = O.widen(out.as_slice(), dtype).astype(np.float64), O.widen(want, dtype).astype(np.float64)
     tol = 1e-5 * np.sqrt(k) if dtype == "f32" else (2.0 ** -6 if dtype == "bf16" else 2.0 ** -9)
     assert np.all(np.abs(g - w) <= tol * np.maximum(np.abs(w), 1.0))
+
+
+def _through_the_file(code):
+    """The same program with a constant into an otherwise unused register
+    before every instruction: no instruction reads the one just before it,
+    so every value travels through the interpreter's register file."""
+    out = []
+    for i in code:
+        out += [const(15, 0.0), i]
+    return out
+
+
+FORWARDING = [load(0, 0), load(1, 1),
+              binary(2, N.MUL, 1, 1),        # the next instruction's operands both forwarded; y read again later
+              unary(3, N.EXP, 2),            # a transcendental: its operand must be in the file
+              binary(4, N.ADD, 3, 0),        # its result read from the file, x from the file
+              store(4, 0),                   # a forwarded store
+              binary(0, N.SUB, 0, 1),        # after a store: nothing forwarded; a register overwritten by itself
+              unary(5, N.SIN, 0),            # a transcendental of the value just made
+              unary(5, N.COS, 5),            # and of its own result, in place
+              binary(6, N.MUL, 5, 2),        # r2 from the file long after it was made
+              cmp(6, N.MAX, 6, 6),           # both operands forwarded, written back to its own register
+              unary(7, N.SQRT, 6),           # the root takes its operand forwarded
+              binary(7, N.ADD, 7, 6),        # r7 forwarded, r6 (read again) from the file
+              store(6, 1), store(7, 2)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_forwarded_values_match_the_register_file(device, dtype):
+    """The interpreter keeps a result that only the next instruction reads in
+    registers and writes the rest to its register file: the same program
+    with every value forced through the file gives the same bits, through
+    the flat kernel and both summing kernels (rows and columns)."""
+    from tensorcrate_b200 import cuda
+    rows, cols = 37, 203
+    x = O.narrow(uniform(rows * cols, 31), dtype)
+    y = O.narrow(uniform(rows * cols, 32), dtype)
+    places = [(cuda.CudaStorage.store(x, dtype), dtype, 0, 1, cols), (cuda.CudaStorage.store(y, dtype), dtype, 0, 1, cols)]
+    results = []
+    for code in (FORWARDING, _through_the_file(FORWARDING)):
+        outs = [cuda.CudaStorage(dtype, rows * cols) for _ in range(3)]
+        run_gpu(dtype, rows, cols, code, places, outs, [dtype] * 3)
+        results.append([o.as_slice() for o in outs])
+    for k, (a, b) in enumerate(zip(*results)):
+        assert same_bits(a, b, dtype), k
+    one_store = FORWARDING[:5] + [binary(4, N.MUL, 4, 2), store(4, 0)]
+    pl = (N.Place * 2)(*[place(s.ptr, d, rows, cols, o, cs, rs) for s, d, o, cs, rs in places])
+    for axis, n in ((N.ROWS, rows), (N.COLUMNS, cols)):
+        sums = []
+        for code in (one_store, _through_the_file(one_store)):
+            out = cuda.CudaStorage(dtype, n)
+            code_arr = (N.Instr * len(code))(*code)
+            N.call("tc_fused_sum", N.DTYPES[dtype], rows, cols, code_arr, len(code), pl, 2, axis, out.ptr, None)
+            sums.append(out.as_slice())
+        assert same_bits(sums[0], sums[1], dtype), axis
