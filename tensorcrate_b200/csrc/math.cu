@@ -281,12 +281,13 @@ __global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long 
 //   2. turns the counts into each (digit, tile)'s first output position: an
 //      exclusive scan along each digit's row of tiles (a block per digit),
 //      then of the 256 digit totals;
-//   3. moves every key to its position: each block walks its tile in rounds
-//      of 256 keys in index order; a key's place among its round's keys of
-//      the same digit is its lane's rank among the warp's lanes with that
-//      digit (match) plus the counts of the warps before it, and each digit
-//      keeps a running position across rounds, so equal digits keep their
-//      input order.
+//   3. moves every key to its position: each warp of a block ranks its own
+//      contiguous share of the tile (512 keys, 32 at a time in index order)
+//      against warp-private digit counts (a key's rank among the warp's keys
+//      of its digit is the count so far plus its rank among the step's lanes
+//      with that digit, found by a vote per digit bit), then one pass over
+//      the digits turns the warps' counts into each warp's first position
+//      per digit, in warp order, so equal digits keep their input order.
 // ---------------------------------------------------------------------------
 constexpr int RADIX_BINS = 256;
 constexpr int RADIX_THREADS = 256;
@@ -296,17 +297,32 @@ constexpr int RADIX_WARPS = RADIX_THREADS / 32;
 
 template <class K>
 __global__ void __launch_bounds__(RADIX_THREADS) radix_histogram(const K *keys, long long n, int shift,
-                                                                 uint32_t *counts, int tiles) {
+                                                                 uint32_t *counts, int tiles, bool vec) {
   __shared__ uint32_t h[RADIX_WARPS][RADIX_BINS];
   const int tid = threadIdx.x, warp = tid >> 5;
 #pragma unroll
   for (int w = 0; w < RADIX_WARPS; ++w) h[w][tid] = 0;
   __syncthreads();
   const long long base = (long long)blockIdx.x * RADIX_TILE;
+  constexpr int P = 16 / int(sizeof(K));  // keys per 16-byte load
+  if (vec && base + RADIX_TILE <= n) {
+    // a whole tile on 16-byte boundaries: every load in flight at once
+    uint4 q[RADIX_ITEMS / P];
+#pragma unroll
+    for (int j = 0; j < RADIX_ITEMS / P; ++j)
+      q[j] = __ldg(reinterpret_cast<const uint4 *>(keys + base) + j * RADIX_THREADS + tid);
+#pragma unroll
+    for (int j = 0; j < RADIX_ITEMS / P; ++j) {
+      const K *k = reinterpret_cast<const K *>(&q[j]);
+#pragma unroll
+      for (int e = 0; e < P; ++e) atomicAdd(&h[warp][(uint32_t(k[e]) >> shift) & 255u], 1u);
+    }
+  } else {
 #pragma unroll 4
-  for (int i = 0; i < RADIX_ITEMS; ++i) {
-    const long long idx = base + (long long)i * RADIX_THREADS + tid;
-    if (idx < n) atomicAdd(&h[warp][(uint32_t(keys[idx]) >> shift) & 255u], 1u);
+    for (int i = 0; i < RADIX_ITEMS; ++i) {
+      const long long idx = base + (long long)i * RADIX_THREADS + tid;
+      if (idx < n) atomicAdd(&h[warp][(uint32_t(keys[idx]) >> shift) & 255u], 1u);
+    }
   }
   __syncthreads();
   uint32_t total = 0;
@@ -369,39 +385,75 @@ template <class K>
 __global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *out, long long n, int shift,
                                                                const uint32_t *counts, const uint32_t *starts,
                                                                int tiles) {
-  __shared__ uint32_t next[RADIX_BINS];
-  __shared__ uint16_t round_counts[RADIX_WARPS][RADIX_BINS];
+  // counts[w][d]: how many of warp w's keys so far have digit d; then the
+  // position of warp w's first key with digit d
+  __shared__ uint32_t warp_counts[RADIX_WARPS][RADIX_BINS];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  next[tid] = starts[tid] + counts[size_t(tid) * size_t(tiles) + blockIdx.x];
 #pragma unroll
-  for (int w = 0; w < RADIX_WARPS; ++w) round_counts[w][tid] = 0;
+  for (int w = 0; w < RADIX_WARPS; ++w) warp_counts[w][tid] = 0;
   __syncthreads();
   const unsigned below = (1u << lane) - 1u;
-  const long long base = (long long)blockIdx.x * RADIX_TILE;
-  for (int i = 0; i < RADIX_ITEMS; ++i) {
-    const long long idx = base + (long long)i * RADIX_THREADS + tid;
-    const bool valid = idx < n;
-    const K key = valid ? in[idx] : K(0);
-    // Lanes past the end take digit 256, which no key has.
-    const uint32_t digit = valid ? (uint32_t(key) >> shift) & 255u : 256u;
-    const unsigned peers = __match_any_sync(~0u, digit);
-    const uint32_t rank = __popc(peers & below);
-    if (valid && rank == 0) round_counts[warp][digit] = uint16_t(__popc(peers));
-    __syncthreads();
-    if (valid) {
-      uint32_t at = next[digit] + rank;
-      for (int w = 0; w < warp; ++w) at += round_counts[w][digit];
-      out[at] = key;
-    }
-    __syncthreads();
-    uint32_t round_total = 0;
+  // Warp w ranks keys [first, first + 32·RADIX_ITEMS) of the tile, 32 at a
+  // time in index order: a key's rank among the warp's keys of its digit is
+  // the warp's count of that digit so far (read by the digit's first lane
+  // in this step, which adds the step's keys of the digit) plus its rank
+  // among this step's lanes with the digit.  No block barrier.
+  const long long first = (long long)blockIdx.x * RADIX_TILE + (long long)warp * 32 * RADIX_ITEMS;
+  K keys[RADIX_ITEMS];
+  uint32_t place[RADIX_ITEMS];  // digit << 16 | rank among the warp's keys of the digit
+  unsigned peers[RADIX_ITEMS];  // the step's lanes with this lane's digit
 #pragma unroll
-    for (int w = 0; w < RADIX_WARPS; ++w) {
-      round_total += round_counts[w][tid];
-      round_counts[w][tid] = 0;
+  for (int i = 0; i < RADIX_ITEMS; ++i) {
+    const long long idx = first + (long long)i * 32 + lane;
+    keys[i] = idx < n ? in[idx] : K(0);
+  }
+  // Lanes with the same digit, by one vote per digit bit (and one for lanes
+  // past the end, whose keys do not exist): independent of the counts, so
+  // every step's votes are taken before the counting walk.
+#pragma unroll
+  for (int i = 0; i < RADIX_ITEMS; ++i) {
+    const bool valid = first + (long long)i * 32 + lane < n;
+    const uint32_t digit = (uint32_t(keys[i]) >> shift) & 255u;
+    const unsigned live = __ballot_sync(~0u, valid);
+    unsigned same = valid ? live : ~live;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const unsigned ones = __ballot_sync(~0u, (digit >> b) & 1u);
+      same &= ((digit >> b) & 1u) ? ones : ~ones;
     }
-    next[tid] += round_total;
-    __syncthreads();
+    peers[i] = same;
+  }
+#pragma unroll
+  for (int i = 0; i < RADIX_ITEMS; ++i) {
+    const long long idx = first + (long long)i * 32 + lane;
+    const bool valid = idx < n;
+    // Lanes past the end take digit 256, which no key has.
+    const uint32_t digit = valid ? (uint32_t(keys[i]) >> shift) & 255u : 256u;
+    const int leader = __ffs(peers[i]) - 1;
+    uint32_t before = 0;
+    if (valid && lane == leader) {
+      before = warp_counts[warp][digit];
+      warp_counts[warp][digit] = before + uint32_t(__popc(peers[i]));
+    }
+    before = __shfl_sync(~0u, before, leader);
+    place[i] = (digit << 16) | (before + uint32_t(__popc(peers[i] & below)));
+    __syncwarp();  // this step's counts are seen by the next step's leaders
+  }
+  __syncthreads();
+  // Digit `tid`: the tile's first position for it (its scanned count over
+  // the tiles, plus the digit's start), then each warp's share in warp order.
+  uint32_t at = starts[tid] + counts[size_t(tid) * size_t(tiles) + blockIdx.x];
+#pragma unroll
+  for (int w = 0; w < RADIX_WARPS; ++w) {
+    const uint32_t c = warp_counts[w][tid];
+    warp_counts[w][tid] = at;
+    at += c;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < RADIX_ITEMS; ++i) {
+    const uint32_t digit = place[i] >> 16;
+    if (digit < RADIX_BINS) out[warp_counts[warp][digit] + (place[i] & 0xffffu)] = keys[i];
   }
 }
 
@@ -426,7 +478,7 @@ template <class K> int sort_keys(const void *a, void *out, size_t n, bool descen
   if (int st = check_launch("sort (keys)")) return st;
   K *src = keys, *dst = alt;
   for (int shift = 0; shift < int(sizeof(K) * 8); shift += 8) {
-    radix_histogram<K><<<tiles, RADIX_THREADS, 0, s>>>(src, (long long)n, shift, counts, tiles);
+    radix_histogram<K><<<tiles, RADIX_THREADS, 0, s>>>(src, (long long)n, shift, counts, tiles, aligned(src));
     radix_scan_rows<<<RADIX_BINS, RADIX_THREADS, 0, s>>>(counts, tiles, totals);
     radix_scan_totals<<<1, RADIX_BINS, 0, s>>>(totals, starts);
     radix_scatter<K><<<tiles, RADIX_THREADS, 0, s>>>(src, dst, (long long)n, shift, counts, starts, tiles);
