@@ -286,8 +286,10 @@ __global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long 
 //      against warp-private digit counts (a key's rank among the warp's keys
 //      of its digit is the count so far plus its rank among the step's lanes
 //      with that digit, found by a vote per digit bit), then one pass over
-//      the digits turns the warps' counts into each warp's first position
-//      per digit, in warp order, so equal digits keep their input order.
+//      the digits turns the warps' counts into each warp's first place per
+//      digit in the tile sorted by digit, in warp order, so equal digits keep
+//      their input order; the tile is sorted in shared memory and written
+//      out in order, each digit's run of keys to consecutive places.
 // ---------------------------------------------------------------------------
 constexpr int RADIX_BINS = 256;
 constexpr int RADIX_THREADS = 256;
@@ -385,9 +387,11 @@ template <class K>
 __global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *out, long long n, int shift,
                                                                const uint32_t *counts, const uint32_t *starts,
                                                                int tiles) {
-  // counts[w][d]: how many of warp w's keys so far have digit d; then the
-  // position of warp w's first key with digit d
+  // counts[w][d]: how many of warp w's keys so far have digit d; then where
+  // warp w's first key with digit d goes in the tile sorted by digit
   __shared__ uint32_t warp_counts[RADIX_WARPS][RADIX_BINS];
+  __shared__ uint32_t base_of[RADIX_BINS], warp_sums[RADIX_WARPS];
+  __shared__ K sorted[RADIX_TILE];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 #pragma unroll
   for (int w = 0; w < RADIX_WARPS; ++w) warp_counts[w][tid] = 0;
@@ -440,20 +444,42 @@ __global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *o
     __syncwarp();  // this step's counts are seen by the next step's leaders
   }
   __syncthreads();
-  // Digit `tid`: the tile's first position for it (its scanned count over
-  // the tiles, plus the digit's start), then each warp's share in warp order.
-  uint32_t at = starts[tid] + counts[size_t(tid) * size_t(tiles) + blockIdx.x];
+  // Digit `tid`: the tile's count of it and, by a scan over the digits, where
+  // its keys start in the tile sorted by digit; each warp's keys of it follow
+  // in warp order.  base_of[d] + (place in the sorted tile) is the output
+  // position (the digit's start plus this tile's scanned count).
+  uint32_t tile_count = 0;
+#pragma unroll
+  for (int w = 0; w < RADIX_WARPS; ++w) tile_count += warp_counts[w][tid];
+  uint32_t x = tile_count;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t y = __shfl_up_sync(~0u, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  uint32_t local = x - tile_count;
+  for (int w = 0; w < warp; ++w) local += warp_sums[w];
+  base_of[tid] = starts[tid] + counts[size_t(tid) * size_t(tiles) + blockIdx.x] - local;
 #pragma unroll
   for (int w = 0; w < RADIX_WARPS; ++w) {
     const uint32_t c = warp_counts[w][tid];
-    warp_counts[w][tid] = at;
-    at += c;
+    warp_counts[w][tid] = local;
+    local += c;
   }
   __syncthreads();
 #pragma unroll
   for (int i = 0; i < RADIX_ITEMS; ++i) {
     const uint32_t digit = place[i] >> 16;
-    if (digit < RADIX_BINS) out[warp_counts[warp][digit] + (place[i] & 0xffffu)] = keys[i];
+    if (digit < RADIX_BINS) sorted[warp_counts[warp][digit] + (place[i] & 0xffffu)] = keys[i];
+  }
+  __syncthreads();
+  // The sorted tile out in order: each digit's keys to consecutive places.
+  const int in_tile = int(min((long long)RADIX_TILE, n - (long long)blockIdx.x * RADIX_TILE));
+  for (int j = tid; j < in_tile; j += RADIX_THREADS) {
+    const K key = sorted[j];
+    out[base_of[(uint32_t(key) >> shift) & 255u] + j] = key;
   }
 }
 
