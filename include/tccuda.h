@@ -221,7 +221,7 @@ int tc_prefix_sum(int dtype, const void *a, void *out, size_t n, void *stream);
 /* `vector_sort` (kernels.rs:873; Host vector.rs:874-886): the n values in
  * SortOrder's total order (f32::total_cmp / half's total_cmp: -NaN < -inf <
  * ... < -0 < +0 < ... < +inf < +NaN).  TC_EINVAL beyond 2^31-1 elements.
- * Uses the stream's scratch. */
+ * `out` may be `a` (sorted in place).  Uses the stream's scratch. */
 int tc_sort(int dtype, int order, const void *a, void *out, size_t n, void *stream);
 /* `vector_unary`/`matrix_unary` (kernels.rs:876, 941; Host 1257-1268):
  * out = f(a), f a tc_analytic, computed in f32 and rounded once. */

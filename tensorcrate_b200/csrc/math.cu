@@ -250,27 +250,16 @@ template <class K> __device__ __forceinline__ K key_bits(K key) {
   return (key & sign) ? K(key ^ sign) : K(~key);
 }
 
-// The key maps, 16 bytes per thread step when both buffers are 16-byte
-// aligned, the rest element by element.  A descending sort sorts the keys'
-// complements ascending (`flip`).
-template <class K, bool TO>
-__global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long n, bool vec, bool flip) {
-  constexpr int P = 16 / int(sizeof(K));
-  const K x = flip ? K(~K(0)) : K(0);
-  const long long packs = vec ? n / P : 0, stride = (long long)gridDim.x * blockDim.x;
-  for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < packs; q += stride) {
-    union {
-      uint4 raw;
-      K v[P];
-    } u;
-    u.raw = __ldg(reinterpret_cast<const uint4 *>(src) + q);
-#pragma unroll
-    for (int j = 0; j < P; ++j) u.v[j] = TO ? K(order_key(u.v[j]) ^ x) : key_bits(K(u.v[j] ^ x));
-    reinterpret_cast<uint4 *>(dst)[q] = u.raw;
-  }
-  for (long long i = packs * P + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    dst[i] = TO ? K(order_key(src[i]) ^ x) : key_bits(K(src[i] ^ x));
-}
+// What a radix pass does to the words it reads and writes: the first pass
+// reads the values and maps them to keys, the last writes the values back
+// (a descending sort sorts the keys' complements ascending: `flip`); the
+// passes between move keys as they are.
+template <class K> struct KeyMap {
+  bool map_in, map_out;
+  K flip;
+  __device__ __forceinline__ K in(K v) const { return map_in ? K(order_key(v) ^ flip) : v; }
+  __device__ __forceinline__ K out(K k) const { return map_out ? key_bits(K(k ^ flip)) : k; }
+};
 
 // ---------------------------------------------------------------------------
 // LSD radix sort of the keys, 8 bits a pass (4 passes for f32's keys, 2 for
@@ -290,6 +279,8 @@ __global__ void __launch_bounds__(256) map_keys(const K *src, K *dst, long long 
 //      digit in the tile sorted by digit, in warp order, so equal digits keep
 //      their input order; the tile is sorted in shared memory and written
 //      out in order, each digit's run of keys to consecutive places.
+// The first pass maps the values to keys as it reads them and the last maps
+// the keys back as it writes them (KeyMap).
 // ---------------------------------------------------------------------------
 constexpr int RADIX_BINS = 256;
 constexpr int RADIX_THREADS = 256;
@@ -299,7 +290,7 @@ constexpr int RADIX_WARPS = RADIX_THREADS / 32;
 
 template <class K>
 __global__ void __launch_bounds__(RADIX_THREADS) radix_histogram(const K *keys, long long n, int shift,
-                                                                 uint32_t *counts, int tiles, bool vec) {
+                                                                 uint32_t *counts, int tiles, bool vec, KeyMap<K> m) {
   __shared__ uint32_t h[RADIX_WARPS][RADIX_BINS];
   const int tid = threadIdx.x, warp = tid >> 5;
 #pragma unroll
@@ -317,13 +308,13 @@ __global__ void __launch_bounds__(RADIX_THREADS) radix_histogram(const K *keys, 
     for (int j = 0; j < RADIX_ITEMS / P; ++j) {
       const K *k = reinterpret_cast<const K *>(&q[j]);
 #pragma unroll
-      for (int e = 0; e < P; ++e) atomicAdd(&h[warp][(uint32_t(k[e]) >> shift) & 255u], 1u);
+      for (int e = 0; e < P; ++e) atomicAdd(&h[warp][(uint32_t(m.in(k[e])) >> shift) & 255u], 1u);
     }
   } else {
 #pragma unroll 4
     for (int i = 0; i < RADIX_ITEMS; ++i) {
       const long long idx = base + (long long)i * RADIX_THREADS + tid;
-      if (idx < n) atomicAdd(&h[warp][(uint32_t(keys[idx]) >> shift) & 255u], 1u);
+      if (idx < n) atomicAdd(&h[warp][(uint32_t(m.in(keys[idx])) >> shift) & 255u], 1u);
     }
   }
   __syncthreads();
@@ -386,7 +377,7 @@ __global__ void __launch_bounds__(RADIX_BINS) radix_scan_totals(const uint32_t *
 template <class K>
 __global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *out, long long n, int shift,
                                                                const uint32_t *counts, const uint32_t *starts,
-                                                               int tiles) {
+                                                               int tiles, KeyMap<K> m) {
   // counts[w][d]: how many of warp w's keys so far have digit d; then where
   // warp w's first key with digit d goes in the tile sorted by digit
   __shared__ uint32_t warp_counts[RADIX_WARPS][RADIX_BINS];
@@ -409,7 +400,7 @@ __global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *o
 #pragma unroll
   for (int i = 0; i < RADIX_ITEMS; ++i) {
     const long long idx = first + (long long)i * 32 + lane;
-    keys[i] = idx < n ? in[idx] : K(0);
+    keys[i] = idx < n ? m.in(in[idx]) : K(0);
   }
   // Lanes with the same digit, by one vote per digit bit (and one for lanes
   // past the end, whose keys do not exist): independent of the counts, so
@@ -479,14 +470,13 @@ __global__ void __launch_bounds__(RADIX_THREADS) radix_scatter(const K *in, K *o
   const int in_tile = int(min((long long)RADIX_TILE, n - (long long)blockIdx.x * RADIX_TILE));
   for (int j = tid; j < in_tile; j += RADIX_THREADS) {
     const K key = sorted[j];
-    out[base_of[(uint32_t(key) >> shift) & 255u] + j] = key;
+    out[base_of[(uint32_t(key) >> shift) & 255u] + j] = m.out(key);
   }
 }
 
 template <class K> int sort_keys(const void *a, void *out, size_t n, bool descending, cudaStream_t s) {
   if (n > size_t(INT_MAX)) return fail(TC_EINVAL, "sort: %zu elements exceed the radix sort's 2^31-1", n);
-  // Keys go into `out`; the second key buffer and the counts come from the
-  // stream's scratch.
+  // The second key buffer and the counts come from the stream's scratch.
   K *keys = static_cast<K *>(out);
   const int tiles = int((n + RADIX_TILE - 1) / RADIX_TILE);
   const size_t alt_bytes = (n * sizeof(K) + 255) & ~size_t(255);
@@ -497,25 +487,26 @@ template <class K> int sort_keys(const void *a, void *out, size_t n, bool descen
   uint32_t *counts = reinterpret_cast<uint32_t *>(static_cast<char *>(block) + alt_bytes);
   uint32_t *totals = reinterpret_cast<uint32_t *>(static_cast<char *>(block) + alt_bytes + count_bytes);
   uint32_t *starts = totals + RADIX_BINS;
-  const unsigned grid = grid_for((n * sizeof(K) + 15) / 16, 256, 8);
   auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  map_keys<K, true><<<grid, 256, 0, s>>>(static_cast<const K *>(a), keys, (long long)n, aligned(a) && aligned(keys),
-                                         descending);
-  if (int st = check_launch("sort (keys)")) return st;
-  K *src = keys, *dst = alt;
-  for (int shift = 0; shift < int(sizeof(K) * 8); shift += 8) {
-    radix_histogram<K><<<tiles, RADIX_THREADS, 0, s>>>(src, (long long)n, shift, counts, tiles, aligned(src));
+  // The first pass reads the values (mapping them to keys as it goes), the
+  // last writes values (mapping back); an even number of passes ends in
+  // `out`, which the first pass does not write (an in-place sort is safe).
+  const K flip = descending ? K(~K(0)) : K(0);
+  const K *src = static_cast<const K *>(a);
+  K *dst = alt;
+  constexpr int passes = int(sizeof(K) * 8) / 8;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = 8 * pass;
+    const KeyMap<K> m{pass == 0, pass == passes - 1, flip};
+    radix_histogram<K><<<tiles, RADIX_THREADS, 0, s>>>(src, (long long)n, shift, counts, tiles, aligned(src), m);
     radix_scan_rows<<<RADIX_BINS, RADIX_THREADS, 0, s>>>(counts, tiles, totals);
     radix_scan_totals<<<1, RADIX_BINS, 0, s>>>(totals, starts);
-    radix_scatter<K><<<tiles, RADIX_THREADS, 0, s>>>(src, dst, (long long)n, shift, counts, starts, tiles);
+    radix_scatter<K><<<tiles, RADIX_THREADS, 0, s>>>(src, dst, (long long)n, shift, counts, starts, tiles, m);
     if (int st = check_launch("sort (radix pass)")) return st;
-    K *t = src;
     src = dst;
-    dst = t;
+    dst = dst == alt ? keys : alt;
   }
-  // An even number of passes: the sorted keys are back in `out`.
-  map_keys<K, false><<<grid, 256, 0, s>>>(keys, keys, (long long)n, aligned(keys), descending);
-  return check_launch("sort (values)");
+  return TC_OK;
 }
 
 }  // namespace

@@ -174,6 +174,18 @@ def test_sort_of_few_distinct_values(device, dtype):
         assert np.array_equal(bits_of(got, dtype), bits_of(want, dtype))
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_sort_in_place(device, dtype):
+    """tc_sort with out == a: the first pass reads the values before any pass
+    writes `out`."""
+    a = _awkward(70001, 23, dtype)
+    buf = cuda.CudaStorage.store(a, dtype)
+    N.call("tc_sort", N.DTYPES[dtype], N.DESCENDING, buf.ptr, buf.ptr, a.size, None)
+    want = np.empty_like(a)
+    O.call("orc_sort", O.DTYPES[dtype], N.DESCENDING, O.ptr(a), O.ptr(want), a.size)
+    assert np.array_equal(bits_of(buf.as_slice(), dtype), bits_of(want, dtype))
+
+
 def test_sort_orders_nans_and_zeros_like_the_host(device):
     """tests/ordering.rs:422-440: -NaN first, -0.0 before +0.0, +NaN last."""
     bits = np.array([0x7FC00000, 0, 0x80000000, 0xFFC00000, 0x3F800000, 0xFF800000, 0x40200000], np.uint32)
