@@ -44,7 +44,7 @@ struct Place {
 
 struct Program {
   int n_code, n_places, n_outputs, n_stat_sources;
-  int n_regs;    // registers the program writes (1 + the highest index): the register file's height
+  int n_regs;    // rows of the register file: the registers that pass through it (at least 1)
   int needs_rc;  // some place is read out of order: elements need their (row, col)
   int n_ahead;   // places read in order, whose next group is requested into L2 ahead
   int ahead[4];
@@ -673,7 +673,7 @@ int take_place(const tc_place &q, uint32_t j, size_t rows, size_t cols, Place &p
 
 // Which values the interpreter forwards in registers (A_PREV, B_PREV) and
 // which it writes to the register file (SPILL), from the registers each
-// instruction reads and writes.  A result that only the next instruction
+// instruction reads and writes; then the file's rows (n_regs).  A result that only the next instruction
 // reads stays in registers; one read later, before the register is written
 // again, goes to the file; a unary operation other than the root neither
 // takes its operand from registers nor leaves its result there.
@@ -700,6 +700,34 @@ void mark_forwarding(Program &p) {
     }
     if (to_file) in.reserved |= SPILL;
   }
+  // The file keeps rows only for the registers that pass through it (a
+  // result written there, an operand read from there, a generic unary's
+  // operand and result); its register fields are renumbered to those rows.
+  // Fields that never reach the file keep row 0.
+  int row_of[REGISTERS];
+  for (int r = 0; r < REGISTERS; ++r) row_of[r] = -1;
+  int rows = 0;
+  auto use = [&](int r) {
+    if (row_of[r] < 0) row_of[r] = rows++;
+  };
+  for (int k = 0; k < p.n_code; ++k) {
+    const tc_instr &in = p.code[k];
+    if (generic_unary(in)) {
+      use(in.a);
+      use(in.dst);
+      continue;
+    }
+    if (reads_a(in) && !(in.reserved & A_PREV)) use(in.a);
+    if (reads_b(in) && !(in.reserved & B_PREV)) use(in.b);
+    if (in.reserved & SPILL) use(in.dst);
+  }
+  for (int k = 0; k < p.n_code; ++k) {
+    tc_instr &in = p.code[k];
+    in.a = uint8_t(std::max(row_of[in.a < REGISTERS ? in.a : 0], 0));
+    in.b = uint8_t(std::max(row_of[in.b < REGISTERS ? in.b : 0], 0));
+    in.dst = uint8_t(std::max(row_of[in.dst < REGISTERS ? in.dst : 0], 0));
+  }
+  p.n_regs = std::max(rows, 1);
 }
 
 // Validate a program and fill `p`.  Places listed as statistics (`stats`)
@@ -736,7 +764,6 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     if (in.code != TC_I_STORE) {
       if (in.dst >= REGISTERS) return fail(TC_EINVAL, "fused: register %u", in.dst);
       written[in.dst] = true;
-      p.n_regs = std::max(p.n_regs, int(in.dst) + 1);
     }
     p.code[k] = in;
     p.code[k].reserved = 0;
