@@ -48,7 +48,11 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 
 def _compile(src: Path, verbose: bool, extra: list[str]) -> Path:
     obj = BUILD / (src.stem + ".o")
-    if _stale(obj, [src] + _headers()):
+    deps = [src] + _headers()
+    if _stale(obj, deps):
+        # the object is dated from its sources as they were when the compile
+        # began, so a source edited while it runs is rebuilt next time
+        seen = max(d.stat().st_mtime for d in deps)
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
@@ -57,6 +61,7 @@ def _compile(src: Path, verbose: bool, extra: list[str]) -> Path:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
         if verbose and r.stderr.strip():
             print(r.stderr, flush=True)
+        os.utime(obj, (seen, seen))
     return obj
 
 

@@ -715,10 +715,12 @@ __global__ void __launch_bounds__(256) reduce_walk(const typename T::S *in, cons
 }
 
 // var_split: a variance whose slices are few and long, in chunks that fill
-// the machine (a warp per slice would leave it nearly idle).  Pass 1 sums
-// each (slice, chunk) with a block; the chunk sums, added in chunk order,
-// give the f32 mean; pass 2 sums the squared deviations from it the same
-// way; the chunk sums, added in order and divided, give the result.  The
+// the machine (a warp per slice would leave it nearly idle).  Slices that
+// are one contiguous run take one pass (var_split_one below).  Otherwise
+// pass 1 sums each (slice, chunk) with a block; the chunk sums, added in
+// chunk order, give the f32 mean; pass 2 sums the squared deviations from
+// it the same way; the chunk sums, added in order and divided, give the
+// result.  The
 // innermost folded axis is walked as a run (a step of run_stride), the
 // others through their walk, recomputed only when the run changes.
 struct VarSplit {
@@ -829,6 +831,126 @@ __global__ void __launch_bounds__(256) var_split_finish(const VarSplit a, const 
   }
 }
 
+// var_split in one pass, for slices that are one contiguous run: each warp
+// takes 16 elements per lane at a time (a sub-tile of 512, in 16-byte packs
+// when the chunk starts on a 16-byte boundary), takes the sub-tile's sum and
+// its squared deviations from its own mean (both warp trees), and merges
+// that into its running (count, sum, squared deviations) by the pairwise
+// update of Chan, Golub and LeVeque (1979): M2 = M2a + M2b + d²·na·nb/n with
+// d the difference of the two means.  The block merges its warps in warp
+// order into partial[g] = (sum, M2) of its chunk; the input is read once.
+constexpr int VS_PER_LANE = 16;
+
+__device__ __forceinline__ void chan_merge(float &n, float &sum, float &m2, float nb, float sum_b, float m2_b) {
+  if (nb == 0.0f) return;
+  if (n == 0.0f) {
+    n = nb, sum = sum_b, m2 = m2_b;
+    return;
+  }
+  const float d = __fsub_rn(__fdiv_rn(sum_b, nb), __fdiv_rn(sum, n));
+  const float both = __fadd_rn(n, nb);
+  m2 = __fadd_rn(__fadd_rn(m2, m2_b), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(n, nb), both)));
+  sum = __fadd_rn(sum, sum_b);
+  n = both;
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) var_split_one(const typename T::S *in, const VarSplit a, float2 *partial) {
+  __shared__ float3 warp_part[8];  // (count, sum, M2) per warp
+  using P = Pack<T>;
+  constexpr int N = P::N, K = VS_PER_LANE / N, TILE = 32 * VS_PER_LANE;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long groups = a.results * a.chunks;
+  for (long long g = blockIdx.x; g < groups; g += gridDim.x) {
+    const long long r = g / a.chunks;
+    const long long f0 = (g - r * a.chunks) * a.chunk, len = min(a.depth, f0 + a.chunk) - f0;
+    const typename T::S *base = in + walk_pos(a.kept, r) + f0;
+    const bool vec = (reinterpret_cast<uintptr_t>(base) & 15u) == 0;
+    float wn = 0.0f, ws = 0.0f, wm2 = 0.0f;
+    for (long long t0 = (long long)warp * TILE; t0 < len; t0 += 8LL * TILE) {
+      const int cnt = int(min((long long)TILE, len - t0));
+      float v[VS_PER_LANE];
+      bool ok[VS_PER_LANE];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        // pack k of the lane: elements t0 + (k*32 + lane)*N .. +N-1
+        const long long at = t0 + (long long)(k * 32 + lane) * N;
+        if (vec && at + N <= len) {
+          P x;
+          x.raw = __ldg(reinterpret_cast<const uint4 *>(base + at));
+#pragma unroll
+          for (int e = 0; e < N; ++e) v[k * N + e] = T::load(x.v[e]), ok[k * N + e] = true;
+        } else {
+#pragma unroll
+          for (int e = 0; e < N; ++e) {
+            ok[k * N + e] = at + e < len;
+            v[k * N + e] = ok[k * N + e] ? T::load(base[at + e]) : 0.0f;
+          }
+        }
+      }
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < VS_PER_LANE; ++i)
+        if (ok[i]) s = __fadd_rn(s, v[i]);
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, d));
+      const float mean = __fdiv_rn(s, float(cnt));
+      float q = 0.0f;
+#pragma unroll
+      for (int i = 0; i < VS_PER_LANE; ++i)
+        if (ok[i]) {
+          const float d = __fsub_rn(v[i], mean);
+          q = __fadd_rn(q, __fmul_rn(d, d));
+        }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, d));
+      chan_merge(wn, ws, wm2, float(cnt), s, q);
+    }
+    if (lane == 0) warp_part[warp] = make_float3(wn, ws, wm2);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float n = 0.0f, sum = 0.0f, m2 = 0.0f;
+      for (int w = 0; w < 8; ++w) chan_merge(n, sum, m2, warp_part[w].x, warp_part[w].y, warp_part[w].z);
+      partial[g] = make_float2(sum, m2);
+    }
+    __syncthreads();
+  }
+}
+
+// The chunks of each slice merged (a block per slice: thread t merges chunks
+// t, t+256, ... in order, then the threads' results meet in a fixed tree):
+// the mean (the plain sum of the chunk sums over the count, in T into
+// `mean_out` when asked) and the variance M2 / divisor in T into `out`.
+template <class T>
+__global__ void __launch_bounds__(256) var_split_one_finish(const VarSplit a, const float2 *partial,
+                                                            typename T::S *mean_out, typename T::S *out) {
+  __shared__ float3 part[256];
+  for (long long r = blockIdx.x; r < a.results; r += gridDim.x) {
+    float n = 0.0f, sum = 0.0f, m2 = 0.0f;
+    for (int c = threadIdx.x; c < a.chunks; c += 256) {
+      const float cn = float(min(a.chunk, a.depth - (long long)c * a.chunk));
+      const float2 p = partial[r * a.chunks + c];
+      chan_merge(n, sum, m2, cn, p.x, p.y);
+    }
+    part[threadIdx.x] = make_float3(n, sum, m2);
+    __syncthreads();
+    for (int stride = 128; stride > 0; stride >>= 1) {
+      if (threadIdx.x < stride) {
+        float3 x = part[threadIdx.x];
+        const float3 y = part[threadIdx.x + stride];
+        chan_merge(x.x, x.y, x.z, y.x, y.y, y.z);
+        part[threadIdx.x] = x;
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      if (mean_out) mean_out[r] = T::store(__fdiv_rn(part[0].y, a.count));
+      out[r] = T::store(__fdiv_rn(part[0].z, a.divisor));
+    }
+    __syncthreads();
+  }
+}
+
 void fill_walk(Walk &w, const Dims &shape, const Dims &strides) {
   w = Walk{};
   w.rank = int(shape.rank);
@@ -876,10 +998,17 @@ int launch_mode(const typename T::S *in, const Dims &kc, const Dims &kcs, const 
     v.divisor = divisor;
     void *p = nullptr;
     const size_t groups = size_t(results) * size_t(v.chunks);
-    if (int st = scratch_get((groups + size_t(results)) * sizeof(float), &p, stream)) return st;
+    if (int st = scratch_get((2 * groups + size_t(results)) * sizeof(float), &p, stream)) return st;
     float *partial = static_cast<float *>(p), *means = partial + groups;
     const unsigned grid = unsigned(std::min<long long>((long long)groups, (long long)sms * 8));
     const unsigned fgrid = unsigned(std::min<long long>(results, (long long)sms * 8));
+    if (v.outer.rank == 0 && v.run_stride == 1) {
+      // contiguous slices: one read (partial holds (sum, M2) per chunk)
+      var_split_one<T><<<grid, 256, 0, stream>>>(in, v, reinterpret_cast<float2 *>(partial));
+      var_split_one_finish<T><<<fgrid, 256, 0, stream>>>(v, reinterpret_cast<const float2 *>(partial), mo, o);
+      if (mean_out) mean_out->written = true;
+      return check_launch("reduce (variance, split, one pass)");
+    }
     var_split_pass<T, false><<<grid, 256, 0, stream>>>(in, v, nullptr, partial);
     var_split_finish<T, false><<<fgrid, 256, 0, stream>>>(v, partial, means, mo);
     if (mean_out) mean_out->written = true;

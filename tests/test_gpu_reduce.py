@@ -233,10 +233,12 @@ def test_column_arg_reductions_with_nans_ties_and_signed_zeros(device, dtype):
     ([100000, 3], [0], None),          # three long strided columns
     ([7, 8, 4096], [0, 2], None),      # eight slices, each 7 runs of 4096
     ([8, 4096, 6], [0, 1], [1, 2, 0]),  # a permuted view: 8 slices of 24576 over two folded axes
+    ([3, 50001], [1], None),           # three contiguous slices, rows off the 16-byte boundary
 ])
 def test_few_long_slices(device, dtype, shape, axes, offset_perm):
     """Few slices of 16384+ elements: the variance splits each slice into
-    chunks over the whole machine (two passes, chunk sums in order) and a
+    chunks over the whole machine (one pass merging the chunks' sums and
+    squared deviations for contiguous slices, two passes otherwise) and a
     single long run's sum is split between warps; both against the oracle
     within the f32 sum bound (the integral filler makes folds and means
     exact)."""
