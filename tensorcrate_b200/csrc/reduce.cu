@@ -206,8 +206,27 @@ __global__ void __launch_bounds__(256) reduce_finish(const RowsArgs a, const Acc
   }
 }
 
+// Two (count, sum, squared deviations from the mean) merged by the pairwise
+// update of Chan, Golub and LeVeque (1979): M2 = M2a + M2b + d²·na·nb/n, d
+// the difference of the two means.
+__device__ __forceinline__ void chan_merge(float &n, float &sum, float &m2, float nb, float sum_b, float m2_b) {
+  if (nb == 0.0f) return;
+  if (n == 0.0f) {
+    n = nb, sum = sum_b, m2 = m2_b;
+    return;
+  }
+  const float d = __fsub_rn(__fdiv_rn(sum_b, nb), __fdiv_rn(sum, n));
+  const float both = __fadd_rn(n, nb);
+  m2 = __fadd_rn(__fadd_rn(m2, m2_b), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(n, nb), both)));
+  sum = __fadd_rn(sum, sum_b);
+  n = both;
+}
+
 // Variance over rows: a warp per result.  When the slice is one run of at
-// most 32*CACHE_PACKS packs it is held in registers between the passes.
+// most 32*CACHE_PACKS packs it is held in registers between the passes; a
+// longer single run is taken in sub-tiles of that size, each held in
+// registers for its own sum and squared deviations from its own mean, merged
+// pairwise (the run is read once); other slices take two passes.
 constexpr int CACHE_PACKS = 8;
 template <class T>
 __global__ void __launch_bounds__(256, 2) reduce_rows_var(const typename T::S *in, const RowsArgs a,
@@ -242,6 +261,43 @@ __global__ void __launch_bounds__(256, 2) reduce_rows_var(const typename T::S *i
             dev.v = __fadd_rn(dev.v, __fmul_rn(d, d));
           }
         }
+    } else if (a.vec && a.outer == 1) {
+      const long long packs = a.run / N;
+      const uint4 *pp = reinterpret_cast<const uint4 *>(base);
+      float n = 0.0f, s = 0.0f, m2 = 0.0f;
+      for (long long t0 = 0; t0 < packs; t0 += 32 * CACHE_PACKS) {
+        const long long in_tile = min((long long)(32 * CACHE_PACKS), packs - t0);
+        Pack<T> x[CACHE_PACKS];
+#pragma unroll
+        for (int k = 0; k < CACHE_PACKS; ++k)
+          if (32 * k + lane < in_tile) x[k].raw = __ldg(pp + t0 + 32 * k + lane);
+        float ts = 0.0f;
+#pragma unroll
+        for (int k = 0; k < CACHE_PACKS; ++k)
+          if (32 * k + lane < in_tile) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) ts = __fadd_rn(ts, T::load(x[k].v[j]));
+          }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) ts = __fadd_rn(ts, __shfl_xor_sync(0xffffffffu, ts, d));
+        const float tn = float(in_tile * N), tm = __fdiv_rn(ts, tn);
+        float tq = 0.0f;
+#pragma unroll
+        for (int k = 0; k < CACHE_PACKS; ++k)
+          if (32 * k + lane < in_tile) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+              const float d = __fsub_rn(T::load(x[k].v[j]), tm);
+              tq = __fadd_rn(tq, __fmul_rn(d, d));
+            }
+          }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) tq = __fadd_rn(tq, __shfl_xor_sync(0xffffffffu, tq, d));
+        chan_merge(n, s, m2, tn, ts, tq);
+      }
+      // every lane holds the totals: lane 0 carries them into the warp merge below
+      dev.v = lane == 0 ? m2 : 0.0f;
+      if (lane == 0 && mean_out) mean_out[r] = T::store(__fdiv_rn(s, a.count));
     } else {
       // Each pass: packs of the runs, four per lane in flight (the second
       // pass finds the slice in L2); element by element without packs.
@@ -835,24 +891,11 @@ __global__ void __launch_bounds__(256) var_split_finish(const VarSplit a, const 
 // takes 16 elements per lane at a time (a sub-tile of 512, in 16-byte packs
 // when the chunk starts on a 16-byte boundary), takes the sub-tile's sum and
 // its squared deviations from its own mean (both warp trees), and merges
-// that into its running (count, sum, squared deviations) by the pairwise
-// update of Chan, Golub and LeVeque (1979): M2 = M2a + M2b + d²·na·nb/n with
-// d the difference of the two means.  The block merges its warps in warp
-// order into partial[g] = (sum, M2) of its chunk; the input is read once.
+// that into its running (count, sum, squared deviations) with chan_merge.
+// The block merges its warps in warp order into partial[g] = (sum, M2) of
+// its chunk; the input is read once.
 constexpr int VS_PER_LANE = 16;
 
-__device__ __forceinline__ void chan_merge(float &n, float &sum, float &m2, float nb, float sum_b, float m2_b) {
-  if (nb == 0.0f) return;
-  if (n == 0.0f) {
-    n = nb, sum = sum_b, m2 = m2_b;
-    return;
-  }
-  const float d = __fsub_rn(__fdiv_rn(sum_b, nb), __fdiv_rn(sum, n));
-  const float both = __fadd_rn(n, nb);
-  m2 = __fadd_rn(__fadd_rn(m2, m2_b), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(n, nb), both)));
-  sum = __fadd_rn(sum, sum_b);
-  n = both;
-}
 
 template <class T>
 __global__ void __launch_bounds__(256) var_split_one(const typename T::S *in, const VarSplit a, float2 *partial) {
