@@ -1249,6 +1249,12 @@ def run_trait(args, torch, world, rank, comm):
     measure("flip", lambda: N.check("flip", lib.tc_flip(f32, r, c, x.ptr, o1.ptr, sp)), 2 * 4 * r * c)
     scalar = cuda.CudaStorage("f32", 1)
     measure("sgd", lambda: N.check("sgd", lib.tc_sgd(f32, n, o1.ptr, y.ptr, 1e-3, sp)), 3 * 4 * n)
+    # the state-carrying rules: p, g and the state read, p and the state written
+    st = cuda.CudaStorage.store(np.abs(rng.standard_normal(n, dtype=np.float32)) * np.float32(0.01), "f32")
+    measure("momentum", lambda: N.check("momentum", lib.tc_momentum(f32, n, o1.ptr, y.ptr, o2.ptr, 1e-3, 0.9, 0,
+                                                                        sp)), 5 * 4 * n)
+    measure("rmsprop", lambda: N.check("rmsprop", lib.tc_rmsprop(f32, n, o1.ptr, y.ptr, st.ptr, 1e-3, 0.9, 1e-8,
+                                                                     sp)), 5 * 4 * n)
     measure("dot", lambda: N.check("dot", lib.tc_dot(f32, x.ptr, y.ptr, n, scalar.ptr, sp)), 2 * 4 * n)
     measure("vector_sum", lambda: N.check("sum", lib.tc_vector_reduce(f32, N.SUM, x.ptr, n, scalar.ptr, sp)), 4 * n)
     mom = cuda.CudaStorage("f32", 2)

@@ -415,6 +415,21 @@ int tc_adam_multi(int dtype, const tc_adam_tensor *tensors, size_t count, int re
                   void *stream);
 /* Sgd's fused program (optim.rs:773-787): p <- p - g·rate. */
 int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *stream);
+/* The other rules' fused programs, one pass each, p and the state updated in
+ * place; every operation rounded to `dtype` in the order the rule's builder
+ * gives it; the coefficients are values of `dtype`.
+ * Momentum (optim.rs:826-846): v <- v·momentum + g; p <- p - step·rate with
+ * step = v, or g + v·momentum when `nesterov`. */
+int tc_momentum(int dtype, size_t n, void *p, const void *g, void *velocity, double rate,
+                double momentum, int nesterov, void *stream);
+/* AdaGrad (optim.rs:892-904, descend 1146-1159): s <- s + g·g;
+ * p <- p - (g / (sqrt(s) + eps))·rate (the rule's eps is 1e-8 in dtype). */
+int tc_adagrad(int dtype, size_t n, void *p, const void *g, void *total, double rate, double eps,
+               void *stream);
+/* RmsProp (optim.rs:948-964): s <- s·decay + (g·g)·(1 - decay), 1 - decay
+ * rounded to dtype; p as AdaGrad (the rule's decay is 0.9, eps 1e-8). */
+int tc_rmsprop(int dtype, size_t n, void *p, const void *g, void *mean_square, double rate,
+               double decay, double eps, void *stream);
 
 /* Status of bounded device-side waits since the library loaded: TC_ETIMEOUT
  * (and *fault = 1) if a tensor-core GEMM gave up waiting on its pipeline, or

@@ -149,6 +149,9 @@ SIGNATURES = {
     "tc_adam": [_i, _sz, _p, _p, _p, _p, _i, _d, _d, _d, _d, _d, _d, _p],
     "tc_adam_multi": [_i, _p, _sz, _i, _d, _d, _d, _d, _d, _d, _p],
     "tc_sgd": [_i, _sz, _p, _p, _d, _p],
+    "tc_momentum": [_i, _sz, _p, _p, _p, _d, _d, _i, _p],
+    "tc_adagrad": [_i, _sz, _p, _p, _p, _d, _d, _p],
+    "tc_rmsprop": [_i, _sz, _p, _p, _p, _d, _d, _d, _p],
     "tc_coalesce": [_u32, _szp, _u32, _szp, _u32p, _szp, _szp],
     "tc_device_status": [C.POINTER(_i)],
     "tc_device_status_reset": [],

@@ -245,6 +245,74 @@ __global__ void __launch_bounds__(256) sgd_kernel(typename T::S *p, const typena
   }
 }
 
+// The state-carrying rules of optim.rs whose programs the reference builds
+// beside Sgd and Adam, each as the program computes it: every operation in
+// f32 on values of T, its result rounded to T, in the builder's order.
+//   Momentum (optim.rs:826-846): v' = v·μ + g; step = nesterov ? g + v'·μ : v';
+//     p' = p - step·rate.
+//   AdaGrad (optim.rs:892-904): s' = s + g·g; p' = p - (g / (√s' + ε))·rate.
+//   RmsProp (optim.rs:948-964): s' = s·ρ + (g·g)·(1 - ρ); p' as AdaGrad.
+// (`descend`, optim.rs:1146-1159, is the shared p' step.)  The coefficients
+// arrive as values of T.
+enum StateRule { R_MOMENTUM = 0, R_NESTEROV = 1, R_ADAGRAD = 2, R_RMSPROP = 3 };
+
+struct StateCoef {
+  float rate, a, b, c;  // momentum: μ; adagrad: ε; rmsprop: ρ, 1 - ρ, ε
+};
+
+template <class T, int RULE>
+__device__ __forceinline__ void state_rule(float &p, float g, float &s, const StateCoef &k) {
+  float step;
+  if (RULE == R_MOMENTUM || RULE == R_NESTEROV) {
+    s = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(s, k.a)), g));
+    step = RULE == R_NESTEROV ? rnd<T>(__fadd_rn(g, rnd<T>(__fmul_rn(s, k.a)))) : s;
+  } else {
+    const float squared = rnd<T>(__fmul_rn(g, g));
+    if (RULE == R_ADAGRAD) s = rnd<T>(__fadd_rn(s, squared));
+    else s = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(s, k.a)), rnd<T>(__fmul_rn(squared, k.b))));
+    const float eps = RULE == R_ADAGRAD ? k.a : k.c;
+    const float denominator = rnd<T>(__fadd_rn(rnd<T>(__fsqrt_rn(s)), eps));
+    step = rnd<T>(__fdiv_rn(g, denominator));
+  }
+  p = rnd<T>(__fsub_rn(p, rnd<T>(__fmul_rn(step, k.rate))));
+}
+
+// p and the state s updated in place, g read: 16-byte packs when all three
+// are aligned, the tail (or all of an unaligned update) element by element.
+template <class T, int RULE>
+__global__ void __launch_bounds__(256) state_rule_kernel(typename T::S *p, const typename T::S *g,
+                                                         typename T::S *s, size_t n, StateCoef k, bool vec) {
+  using S = typename T::S;
+  constexpr int N = 16 / int(sizeof(S));
+  union Pk {
+    uint4 raw;
+    S v[N];
+  };
+  const size_t stride = size_t(gridDim.x) * blockDim.x, tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t packs = vec ? n / N : 0;
+  for (size_t q = tid; q < packs; q += stride) {
+    Pk pp, gg, ss;
+    pp.raw = reinterpret_cast<const uint4 *>(p)[q];
+    gg.raw = __ldg(reinterpret_cast<const uint4 *>(g) + q);
+    ss.raw = reinterpret_cast<const uint4 *>(s)[q];
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float pv = T::load(pp.v[j]), sv = T::load(ss.v[j]);
+      state_rule<T, RULE>(pv, T::load(gg.v[j]), sv, k);
+      pp.v[j] = T::store(pv);
+      ss.v[j] = T::store(sv);
+    }
+    reinterpret_cast<uint4 *>(p)[q] = pp.raw;
+    reinterpret_cast<uint4 *>(s)[q] = ss.raw;
+  }
+  for (size_t i = packs * N + tid; i < n; i += stride) {
+    float pv = T::load(p[i]), sv = T::load(s[i]);
+    state_rule<T, RULE>(pv, T::load(g[i]), sv, k);
+    p[i] = T::store(pv);
+    s[i] = T::store(sv);
+  }
+}
+
 bool aligned16(const void *q) { return (uintptr_t(q) & 15u) == 0; }
 
 // A 16-byte load that no cache on this GPU may answer from an older copy:
@@ -450,6 +518,46 @@ int tc_sgd(int dtype, size_t n, void *p, const void *g, double rate, void *strea
                                                        float(rate), vec);
     return check_launch("sgd");
   });
+}
+
+static int run_state_rule(const char *what, int dtype, int rule, size_t n, void *p, const void *g, void *s, double rate,
+                          double a, double b, double c, void *stream) {
+  if (n == 0) return TC_OK;
+  if (!p || !g || !s) return fail(TC_EINVAL, "%s: null pointer", what);
+  return with_real(dtype, [&](auto t) {
+    using T = decltype(t);
+    using S = typename T::S;
+    auto in_t = [](double x) { return T::load(T::store(float(x))); };
+    StateCoef k{in_t(rate), in_t(a), in_t(b), in_t(c)};
+    if (rule == R_RMSPROP) k.b = in_t(1.0f - k.a);  // 1 - ρ, in T, as the rule computes it
+    const bool vec = aligned16(p) && aligned16(g) && aligned16(s);
+    const unsigned grid = grid_for(vec ? (n + 15 / sizeof(S)) / (16 / sizeof(S)) : n, 256, 8);
+    cudaStream_t st = as_stream(stream);
+    S *ps = static_cast<S *>(p), *ss = static_cast<S *>(s);
+    const S *gs = static_cast<const S *>(g);
+    switch (rule) {
+      case R_MOMENTUM: state_rule_kernel<T, R_MOMENTUM><<<grid, 256, 0, st>>>(ps, gs, ss, n, k, vec); break;
+      case R_NESTEROV: state_rule_kernel<T, R_NESTEROV><<<grid, 256, 0, st>>>(ps, gs, ss, n, k, vec); break;
+      case R_ADAGRAD: state_rule_kernel<T, R_ADAGRAD><<<grid, 256, 0, st>>>(ps, gs, ss, n, k, vec); break;
+      default: state_rule_kernel<T, R_RMSPROP><<<grid, 256, 0, st>>>(ps, gs, ss, n, k, vec);
+    }
+    return check_launch(what);
+  });
+}
+
+int tc_momentum(int dtype, size_t n, void *p, const void *g, void *velocity, double rate, double momentum,
+                int nesterov, void *stream) {
+  return run_state_rule("momentum", dtype, nesterov ? R_NESTEROV : R_MOMENTUM, n, p, g, velocity, rate, momentum, 0.0,
+                        0.0, stream);
+}
+
+int tc_adagrad(int dtype, size_t n, void *p, const void *g, void *total, double rate, double eps, void *stream) {
+  return run_state_rule("adagrad", dtype, R_ADAGRAD, n, p, g, total, rate, eps, 0.0, 0.0, stream);
+}
+
+int tc_rmsprop(int dtype, size_t n, void *p, const void *g, void *mean_square, double rate, double decay, double eps,
+               void *stream) {
+  return run_state_rule("rmsprop", dtype, R_RMSPROP, n, p, g, mean_square, rate, decay, 0.0, eps, stream);
 }
 
 }  // extern "C"

@@ -1,6 +1,7 @@
-"""The fused Adam and SGD updates against the oracle's restatement of the
-programs (optim.rs:1048-1099, 773-787): every operation rounds to the
-element type in the program's order, so the updates agree bit for bit."""
+"""The fused optimizer updates (Adam, SGD, Momentum, AdaGrad, RmsProp)
+against the oracle's restatement of their programs (optim.rs:1048-1099,
+773-787, 826-846, 892-904, 948-964): every operation rounds to the element
+type in the program's order, so the updates agree bit for bit."""
 from __future__ import annotations
 
 import numpy as np
@@ -101,3 +102,74 @@ def test_adam_over_many_tensors_in_one_launch(device, dtype):
             for k in ("p", "m", "v"):
                 assert np.array_equal(s[k].as_slice(), mu[k].as_slice()), (s["n"], k)
     del C
+
+
+def _in(dtype, x):
+    """x as a value of the element type (the rules' coefficients are)."""
+    return float(O.widen(O.narrow(np.array([x], np.float32), dtype), dtype)[0])
+
+
+def _rule_program(rule, dtype, rate, coef, nesterov=False):
+    """The rule's program as its builder makes it (optim.rs:826-846, 892-904,
+    948-964; descend 1146-1159): places g, p, state; outputs p, state."""
+    from test_fused import binary, const, load, store, unary
+    code = [load(0, 0), load(1, 1)]
+    if rule == "momentum":
+        code += [load(2, 2), const(3, coef), binary(4, N.MUL, 2, 3), binary(5, N.ADD, 4, 0)]
+        step, state = 5, 5
+        if nesterov:
+            code += [binary(6, N.MUL, 5, 3), binary(7, N.ADD, 0, 6)]
+            step = 7
+        code += [const(8, rate), binary(9, N.MUL, step, 8), binary(10, N.SUB, 1, 9)]
+        return code + [store(10, 0), store(state, 1)]
+    code += [binary(2, N.MUL, 0, 0)]
+    if rule == "adagrad":
+        eps = coef
+        code += [load(3, 2), binary(4, N.ADD, 3, 2)]
+        state = 4
+    else:  # rmsprop: coef = decay
+        eps = _in(dtype, 1e-8)
+        code += [const(3, _in(dtype, 1.0 - coef)), binary(4, N.MUL, 2, 3), load(5, 2), const(6, coef),
+                 binary(7, N.MUL, 5, 6), binary(8, N.ADD, 7, 4)]
+        state = 8
+    code += [unary(9, N.SQRT, state), const(10, eps), binary(11, N.ADD, 9, 10), binary(12, N.DIV, 0, 11),
+             const(13, rate), binary(14, N.MUL, 12, 13), binary(15, N.SUB, 1, 14)]
+    return code + [store(15, 0), store(state, 1)]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rule", ["momentum", "nesterov", "adagrad", "rmsprop"])
+@pytest.mark.parametrize("n,shift", [(10007, 0), (4099, 1)])
+def test_state_rules_match_their_programs_bit_for_bit(device, dtype, rule, n, shift):
+    """tc_momentum, tc_adagrad and tc_rmsprop against the oracle's
+    interpreter running the rule's program, twice in a row (the state carried
+    over); `shift` starts every buffer one element past a 16-byte boundary
+    (no 16-byte packs)."""
+    from test_fused import run_oracle
+    rate = _in(dtype, 0.01)
+    coef = {"momentum": _in(dtype, 0.9), "nesterov": _in(dtype, 0.9), "adagrad": _in(dtype, 1e-8),
+            "rmsprop": _in(dtype, 0.9)}[rule]
+    p = O.narrow(normal(n, 31), dtype)
+    s = O.narrow(normal(n, 33) * np.float32(0.01) if rule in ("momentum", "nesterov") else
+                 np.abs(normal(n, 33)) * np.float32(0.01), dtype)
+    dev = {k: cuda.CudaStorage.store(np.concatenate([np.zeros(shift, v.dtype), v]), dtype) for k, v in (("p", p), ("s", s))}
+    code = _rule_program("momentum" if rule == "nesterov" else rule, dtype, rate, coef, nesterov=rule == "nesterov")
+    esz = 4 if dtype == "f32" else 2
+    for step in range(2):
+        g = O.narrow(normal(n, 40 + step) * np.float32(0.1), dtype)
+        dg = cuda.CudaStorage.store(np.concatenate([np.zeros(shift, g.dtype), g]), dtype)
+        at = lambda d: d.ptr + shift * esz
+        if rule in ("momentum", "nesterov"):
+            N.call("tc_momentum", N.DTYPES[dtype], n, at(dev["p"]), at(dg), at(dev["s"]), rate, coef,
+                   int(rule == "nesterov"), None)
+        elif rule == "adagrad":
+            N.call("tc_adagrad", N.DTYPES[dtype], n, at(dev["p"]), at(dg), at(dev["s"]), rate, coef, None)
+        else:
+            N.call("tc_rmsprop", N.DTYPES[dtype], n, at(dev["p"]), at(dg), at(dev["s"]), rate, coef,
+                   _in(dtype, 1e-8), None)
+        new_p, new_s = np.empty_like(p), np.empty_like(s)
+        run_oracle(dtype, 1, n, code, [(g, dtype, 0, 1, n), (p, dtype, 0, 1, n), (s, dtype, 0, 1, n)],
+                   [new_p, new_s], [dtype, dtype])
+        p, s = new_p, new_s
+        assert same_bits(dev["p"].as_slice()[shift:], p, dtype), step
+        assert same_bits(dev["s"].as_slice()[shift:], s, dtype), step
