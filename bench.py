@@ -1250,10 +1250,10 @@ def run_trait(args, torch, world, rank, comm):
     scalar = cuda.CudaStorage("f32", 1)
     measure("sgd", lambda: N.check("sgd", lib.tc_sgd(f32, n, o1.ptr, y.ptr, 1e-3, sp)), 3 * 4 * n)
     # the state-carrying rules: p, g and the state read, p and the state written
-    st = cuda.CudaStorage.store(np.abs(rng.standard_normal(n, dtype=np.float32)) * np.float32(0.01), "f32")
+    state = cuda.CudaStorage.store(np.abs(rng.standard_normal(n, dtype=np.float32)) * np.float32(0.01), "f32")
     measure("momentum", lambda: N.check("momentum", lib.tc_momentum(f32, n, o1.ptr, y.ptr, o2.ptr, 1e-3, 0.9, 0,
                                                                         sp)), 5 * 4 * n)
-    measure("rmsprop", lambda: N.check("rmsprop", lib.tc_rmsprop(f32, n, o1.ptr, y.ptr, st.ptr, 1e-3, 0.9, 1e-8,
+    measure("rmsprop", lambda: N.check("rmsprop", lib.tc_rmsprop(f32, n, o1.ptr, y.ptr, state.ptr, 1e-3, 0.9, 1e-8,
                                                                      sp)), 5 * 4 * n)
     measure("dot", lambda: N.check("dot", lib.tc_dot(f32, x.ptr, y.ptr, n, scalar.ptr, sp)), 2 * 4 * n)
     measure("vector_sum", lambda: N.check("sum", lib.tc_vector_reduce(f32, N.SUM, x.ptr, n, scalar.ptr, sp)), 4 * n)
@@ -1300,6 +1300,29 @@ def run_trait(args, torch, world, rank, comm):
     measure("layer_norm_with_statistics",
             lambda: N.check("stats", lib.tc_fused_with_statistics(f32, rows, cols, ln_code, len(ln), pl3, 3, st, 2,
                                                                   outs, dts, 1, sp)), 2 * 4 * rows * cols)
+    # RmsProp's program (optim.rs:948-964) through Kernels::fused: in place,
+    # tc_fused runs it as the rule's kernel; into fresh outputs, the
+    # interpreter runs it
+    rate, rho, eps = float(np.float32(1e-3)), float(np.float32(0.9)), float(np.float32(1e-8))
+    rms = [ins(N.I_LOAD, 0, slot=0), ins(N.I_LOAD, 1, slot=1), ins(N.I_BINARY, 2, 0, 0, op=2),
+           ins(N.I_CONST, 3, value=float(np.float32(1.0) - np.float32(rho))), ins(N.I_BINARY, 4, 2, 3, op=2),
+           ins(N.I_LOAD, 5, slot=2), ins(N.I_CONST, 6, value=rho), ins(N.I_BINARY, 7, 5, 6, op=2),
+           ins(N.I_BINARY, 8, 7, 4, op=0), ins(N.I_UNARY, 9, 8, op=N.SQRT), ins(N.I_CONST, 10, value=eps),
+           ins(N.I_BINARY, 11, 9, 10, op=0), ins(N.I_BINARY, 12, 0, 11, op=3), ins(N.I_CONST, 13, value=rate),
+           ins(N.I_BINARY, 14, 12, 13, op=2), ins(N.I_BINARY, 15, 1, 14, op=1), ins(N.I_STORE, a=15, slot=0),
+           ins(N.I_STORE, a=8, slot=1)]
+    rms_code = (N.Instr * len(rms))(*rms)
+    o3 = cuda.CudaStorage("f32", n)
+    rms_places = (N.Place * 3)(place(y.ptr), place(o1.ptr), place(state.ptr))
+    dts2 = (C.c_int * 2)(f32, f32)
+    in_place = (C.c_void_p * 2)(o1.ptr, state.ptr)
+    fresh = (C.c_void_p * 2)(o2.ptr, o3.ptr)
+    measure("fused_rmsprop_program_in_place",
+            lambda: N.check("fused", lib.tc_fused(f32, rows, cols, rms_code, len(rms), rms_places, 3, in_place, dts2, 2,
+                                                  sp)), 5 * 4 * rows * cols)
+    measure("fused_rmsprop_program_interpreted",
+            lambda: N.check("fused", lib.tc_fused(f32, rows, cols, rms_code, len(rms), rms_places, 3, fresh, dts2, 2,
+                                                  sp)), 5 * 4 * rows * cols)
     gbs = hbm_bytes / (hbm_ms * 1e-3) / 1e9
     return {"metric": "trait-method kernels HBM throughput (GB/s)", "value": round(gbs, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(hbm_ms, 4),

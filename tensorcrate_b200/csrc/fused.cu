@@ -22,6 +22,7 @@
 // This is the general path; the optimizers' programs have kernels of their
 // own (optim.cu), and dense layers' epilogues run inside the GEMM.
 #include <algorithm>
+#include <vector>
 
 #include "analytic.cuh"
 
@@ -856,6 +857,223 @@ template <class T> int launch_rows(const Program &p, void *sums, cudaStream_t s,
   });
 }
 
+// ---------------------------------------------------------------------------
+// Programs the optimizers build, run by their dedicated kernels.  The
+// reference's rules reach a backend as fused programs (Rule::update calls
+// P::fused with the rule's program, optim.rs:773-787, 826-846, 892-904,
+// 948-964, 1048-1099).  A program whose computation is one of those updates
+// (the same operations on the same operands, each rounded to the program's
+// type, so the same bits) over in-order places of the program's type, with
+// the updated places written in place, runs as the rule's kernel instead of
+// the interpreter.  The match is on the dataflow, not on the instructions'
+// order or registers; commutative operations match either way round.
+// ---------------------------------------------------------------------------
+struct Expr {
+  int kind, op, a, b, place;
+  float value;
+};
+
+struct Dataflow {
+  std::vector<Expr> e;
+  int out[MAX_OUTPUTS];
+  int n_out;
+  int dtype;
+
+  float in_type(float x) const {
+    if (dtype == TC_F32) return x;
+    return dtype == TC_BF16 ? bf16_bits_to_f32(f32_to_bf16_bits(x)) : f16_bits_to_f32(f32_to_f16_bits(x));
+  }
+  bool load(int n, int &place) const {
+    if (n < 0 || e[n].kind != TC_I_LOAD) return false;
+    place = e[n].place;
+    return true;
+  }
+  bool is_load(int n, int place) const { return n >= 0 && e[n].kind == TC_I_LOAD && e[n].place == place; }
+  bool cnst(int n, float &v) const {
+    if (n < 0 || e[n].kind != TC_I_CONST) return false;
+    v = e[n].value;
+    return true;
+  }
+  bool bin(int n, int op, int &x, int &y) const {
+    if (n < 0 || e[n].kind != TC_I_BINARY || e[n].op != op) return false;
+    x = e[n].a, y = e[n].b;
+    return true;
+  }
+  // n = x·c (either way round) with c a constant
+  bool mul_const(int n, int &x, float &c) const {
+    int a, b;
+    if (!bin(n, TC_MUL, a, b)) return false;
+    if (cnst(b, c)) return x = a, true;
+    if (cnst(a, c)) return x = b, true;
+    return false;
+  }
+  // n = g·g with g a load of `place`
+  bool square(int n, int place) const {
+    int a, b;
+    return bin(n, TC_MUL, a, b) && is_load(a, place) && is_load(b, place);
+  }
+  bool same(int a, int b) const {
+    if (a == b) return true;
+    if (a < 0 || b < 0) return false;
+    const Expr &x = e[a], &y = e[b];
+    if (x.kind != y.kind || x.op != y.op) return false;
+    switch (x.kind) {
+      case TC_I_LOAD: return x.place == y.place;
+      case TC_I_CONST: return x.value == y.value;
+      case TC_I_UNARY: return same(x.a, y.a);
+      default: {
+        if (same(x.a, y.a) && same(x.b, y.b)) return true;
+        const bool comm = x.kind == TC_I_BINARY && (x.op == TC_ADD || x.op == TC_MUL);
+        return comm && same(x.a, y.b) && same(x.b, y.a);
+      }
+    }
+  }
+  // n = l + r with one side matching `first` and the other `second`
+  template <class F, class G> bool add_of(int n, F &&first, G &&second) const {
+    int a, b;
+    if (!bin(n, TC_ADD, a, b)) return false;
+    return (first(a) && second(b)) || (first(b) && second(a));
+  }
+  // p' = p - ((g / (sqrt(s) + eps)) · rate), s matching `state` (descend)
+  bool descend(int n, int p_place, int g_place, int state, float &eps, float &rate) const {
+    int x, y, q, num, den;
+    if (!bin(n, TC_SUB, x, y) || !is_load(x, p_place) || !mul_const(y, q, rate)) return false;
+    if (!bin(q, TC_DIV, num, den) || !is_load(num, g_place)) return false;
+    return add_of(den,
+                  [&](int r) { return r >= 0 && e[r].kind == TC_I_UNARY && e[r].op == TC_SQRT && same(e[r].a, state); },
+                  [&](int c) { return cnst(c, eps); });
+  }
+};
+
+bool build_dataflow(int dtype, const tc_instr *code, uint32_t n_code, uint32_t n_outputs, Dataflow &d) {
+  d.dtype = dtype;
+  d.n_out = int(n_outputs);
+  int reg[REGISTERS];
+  for (int &r : reg) r = -1;
+  for (int &o : d.out) o = -1;
+  for (uint32_t k = 0; k < n_code; ++k) {
+    const tc_instr &in = code[k];
+    Expr x{int(in.code), int(in.op), -1, -1, -1, 0.0f};
+    switch (in.code) {
+      case TC_I_LOAD: x.op = 0, x.place = in.slot; break;
+      case TC_I_CONST: x.op = 0, x.value = d.in_type(in.value); break;
+      case TC_I_UNARY: x.a = reg[in.a]; break;
+      case TC_I_STORE:
+        if (d.out[in.slot] >= 0) return false;  // an output stored twice
+        d.out[in.slot] = reg[in.a];
+        continue;
+      default: x.a = reg[in.a], x.b = reg[in.b];
+    }
+    d.e.push_back(x);
+    reg[in.dst] = int(d.e.size()) - 1;
+  }
+  for (uint32_t j = 0; j < n_outputs; ++j)
+    if (d.out[j] < 0) return false;
+  return true;
+}
+
+// TC_OK or an error if a rule's kernel ran; -1 if the program is no rule's.
+int run_as_rule(int dtype, size_t n, const tc_instr *code, uint32_t n_code, const Program &p,
+                void *const *outputs, const int *out_dtypes, uint32_t n_outputs, void *stream) {
+  if (n_outputs < 1 || n_outputs > 3) return -1;
+  Dataflow d;
+  if (!build_dataflow(dtype, code, n_code, n_outputs, d)) return -1;
+  const size_t esz = dtype_bytes(dtype);
+  auto at = [&](int j) { return static_cast<char *>(const_cast<void *>(p.places[j].data)) + p.places[j].offset * esz; };
+  // every place read in order, in the program's type; outputs of that type
+  for (int j = 0; j < p.n_places; ++j)
+    if (!p.places[j].in_order || p.places[j].dtype != dtype || p.places[j].stat >= 0) return -1;
+  for (uint32_t k = 0; k < n_outputs; ++k)
+    if (out_dtypes[k] != dtype) return -1;
+  // `place` is updated in place as output k; `g` is read only
+  auto in_place = [&](int place, int k) { return outputs[k] == at(place); };
+  auto read_only = [&](int place) {
+    for (uint32_t k = 0; k < n_outputs; ++k)
+      if (outputs[k] == at(place)) return false;
+    return true;
+  };
+  int pp = -1, pg = -1, ps = -1;
+  float rate = 0.0f, c = 0.0f, eps = 0.0f;
+  if (n_outputs == 1) {  // Sgd: p - g·rate
+    int x, y, u;
+    if (d.bin(d.out[0], TC_SUB, x, y) && d.load(x, pp) && d.mul_const(y, u, rate) && d.load(u, pg) && pp != pg &&
+        in_place(pp, 0) && read_only(pg))
+      return tc_sgd(dtype, n, outputs[0], at(pg), rate, stream);
+    return -1;
+  }
+  if (n_outputs == 2) {
+    const int s = d.out[1];
+    int x, y, step;
+    // Momentum: v' = v·mu + g; p' = p - step·rate, step = v' or g + v'·mu
+    if (d.add_of(s, [&](int a) { return d.load(a, pg); },
+                 [&](int b) { int v; return d.mul_const(b, v, c) && d.load(v, ps); }) &&
+        d.bin(d.out[0], TC_SUB, x, y) && d.load(x, pp) && d.mul_const(y, step, rate) && pp != pg && ps != pg &&
+        pp != ps && in_place(pp, 0) && in_place(ps, 1) && read_only(pg)) {
+      if (d.same(step, s)) return tc_momentum(dtype, n, outputs[0], at(pg), outputs[1], rate, c, 0, stream);
+      float c2;
+      if (d.add_of(step, [&](int a) { return d.is_load(a, pg); },
+                   [&](int b) { int v; return d.mul_const(b, v, c2) && c2 == c && d.same(v, s); }))
+        return tc_momentum(dtype, n, outputs[0], at(pg), outputs[1], rate, c, 1, stream);
+      return -1;
+    }
+    // AdaGrad: s' = s + g·g, RmsProp: s' = s·rho + (g·g)·(1 - rho); p' by descend
+    int sub_x, sub_y;
+    if (!d.bin(d.out[0], TC_SUB, sub_x, sub_y) || !d.load(sub_x, pp)) return -1;
+    int num, den, q;
+    if (!d.mul_const(sub_y, q, rate) || !d.bin(q, TC_DIV, num, den) || !d.load(num, pg)) return -1;
+    if (pp == pg || !in_place(pp, 0) || !read_only(pg)) return -1;
+    float rho = 0.0f, share = 0.0f;
+    const bool adagrad =
+        d.add_of(s, [&](int a) { return d.load(a, ps); }, [&](int b) { return d.square(b, pg); });
+    const bool rmsprop =
+        !adagrad && d.add_of(s, [&](int a) { int v; return d.mul_const(a, v, rho) && d.load(v, ps); },
+                             [&](int b) { int v; return d.mul_const(b, v, share) && d.square(v, pg); });
+    if ((!adagrad && !rmsprop) || ps == pp || ps == pg || !in_place(ps, 1)) return -1;
+    if (!d.descend(d.out[0], pp, pg, s, eps, rate)) return -1;
+    if (adagrad) return tc_adagrad(dtype, n, outputs[0], at(pg), outputs[1], rate, eps, stream);
+    if (share != d.in_type(1.0f - rho)) return -1;  // the kernel takes 1 - rho in the type from rho
+    return tc_rmsprop(dtype, n, outputs[0], at(pg), outputs[1], rate, rho, eps, stream);
+  }
+  // Adam: m' = m·b1 + g·s1 and v' = v·b2 + (g·g)·s2 (resumed), or g·s1 and
+  // (g·g)·s2 (the first step, into fresh outputs); p' = p - ((m'·c1) /
+  // (sqrt(v'·c2) + eps))·rate, with s = 1 - b in the type.
+  int pm = -1, pv = -1;
+  float b1 = 0.0f, b2 = 0.0f, s1 = 0.0f, s2 = 0.0f, c1 = 0.0f, c2 = 0.0f;
+  const int m = d.out[1], v = d.out[2];
+  auto fresh_first = [&](int r) { int u; return d.mul_const(r, u, s1) && d.load(u, pg); };
+  auto fresh_second = [&](int r) { int u; return d.mul_const(r, u, s2) && d.square(u, pg); };
+  bool resumed = d.add_of(m, [&](int a) { int u; return d.mul_const(a, u, b1) && d.load(u, pm); }, fresh_first) &&
+                 d.add_of(v, [&](int a) { int u; return d.mul_const(a, u, b2) && d.load(u, pv); }, fresh_second);
+  if (!resumed) {
+    if (!fresh_first(m) || !fresh_second(v)) return -1;
+    // the kernel derives the shares from the betas: the betas that give them
+    b1 = d.in_type(1.0f - s1), b2 = d.in_type(1.0f - s2);
+  }
+  if (s1 != d.in_type(1.0f - b1) || s2 != d.in_type(1.0f - b2)) return -1;
+  int x, y, q, num, den, mx, vx;
+  if (!d.bin(d.out[0], TC_SUB, x, y) || !d.load(x, pp) || !d.mul_const(y, q, rate) || !d.bin(q, TC_DIV, num, den))
+    return -1;
+  if (!d.mul_const(num, mx, c1) || !d.same(mx, m)) return -1;
+  if (!d.add_of(den,
+                [&](int r) {
+                  return r >= 0 && d.e[r].kind == TC_I_UNARY && d.e[r].op == TC_SQRT && d.mul_const(d.e[r].a, vx, c2) &&
+                         d.same(vx, v);
+                },
+                [&](int r) { return d.cnst(r, eps); }))
+    return -1;
+  if (pp == pg || !in_place(pp, 0) || !read_only(pg)) return -1;
+  if (resumed) {
+    if (pm == pv || pm == pp || pv == pp || pm == pg || pv == pg || !in_place(pm, 1) || !in_place(pv, 2)) return -1;
+  } else {
+    // fresh outputs: none of them may be a place the program reads
+    for (int j = 0; j < p.n_places; ++j)
+      if (outputs[1] == at(j) || outputs[2] == at(j)) return -1;
+    if (outputs[1] == outputs[2] || outputs[1] == outputs[0] || outputs[2] == outputs[0]) return -1;
+  }
+  return tc_adam(dtype, n, outputs[0], at(pg), outputs[1], outputs[2], resumed ? 1 : 0, rate, b1, b2, eps, c1, c2,
+                 stream);
+}
+
 }  // namespace
 }  // namespace tc
 
@@ -870,6 +1088,8 @@ int tc_fused(int dtype, size_t rows, size_t cols, const tc_instr *code, uint32_t
                              n_outputs, p))
     return st;
   if (rows == 0 || cols == 0) return TC_OK;
+  if (int st = run_as_rule(dtype, rows * cols, code, n_code, p, outputs, out_dtypes, n_outputs, stream); st != -1)
+    return st;
   return with_real(dtype, [&](auto t) {
     using T = decltype(t);
     const size_t regs = register_file_bytes(p, FLAT_GROUP);

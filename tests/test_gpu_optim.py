@@ -173,3 +173,62 @@ def test_state_rules_match_their_programs_bit_for_bit(device, dtype, rule, n, sh
         p, s = new_p, new_s
         assert same_bits(dev["p"].as_slice()[shift:], p, dtype), step
         assert same_bits(dev["s"].as_slice()[shift:], s, dtype), step
+
+
+def _adam_first_step_program(dtype, coef):
+    """Adam's first-step program (optim.rs:1048-1099 with `resumed` false):
+    the moments go to fresh outputs; places p, g."""
+    from test_fused import binary, const, load, store, unary
+    rate, b1, b2, eps, c1, c2 = coef
+    one = lambda x: _in(dtype, x)
+    s1, s2 = one(1.0 - np.float32(b1)), one(1.0 - np.float32(b2))
+    return [load(0, 0), load(1, 1), const(2, s1), binary(3, N.MUL, 1, 2), binary(4, N.MUL, 1, 1), const(5, s2),
+            binary(6, N.MUL, 4, 5), const(7, c1), binary(8, N.MUL, 3, 7), const(7, c2), binary(9, N.MUL, 6, 7),
+            unary(9, N.SQRT, 9), const(7, eps), binary(9, N.ADD, 9, 7), binary(8, N.DIV, 8, 9), const(7, rate),
+            binary(8, N.MUL, 8, 7), binary(0, N.SUB, 0, 8), store(0, 0), store(3, 1), store(6, 2)]
+
+
+def _rule_case(rule, dtype):
+    """(program, place names in load order, output names in store order,
+    names updated in place) for each rule the reference's optimizers build."""
+    from test_fused import adam_program, binary, const, load, store
+    rate = _in(dtype, 0.01)
+    if rule == "sgd":
+        code = [load(0, 0), load(1, 1), const(2, rate), binary(3, N.MUL, 0, 2), binary(4, N.SUB, 1, 3), store(4, 0)]
+        return code, ["g", "p"], ["p"], {"p"}
+    if rule in ("momentum", "nesterov", "adagrad", "rmsprop"):
+        coef = _in(dtype, 1e-8) if rule == "adagrad" else _in(dtype, 0.9)
+        code = _rule_program("momentum" if rule == "nesterov" else rule, dtype, rate, coef, rule == "nesterov")
+        return code, ["g", "p", "s"], ["p", "s"], {"p", "s"}
+    beta2 = 0.99 if dtype == "bf16" else 0.999
+    coef = O.adam_coefficients(dtype, 1e-3, 0.9, beta2, 1e-8, 3)
+    if rule == "adam":
+        return adam_program(dtype, coef), ["p", "g", "m", "v"], ["p", "m", "v"], {"p", "m", "v"}
+    return _adam_first_step_program(dtype, coef), ["p", "g"], ["p", "m", "v"], {"p"}
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rule", ["sgd", "momentum", "nesterov", "adagrad", "rmsprop", "adam", "adam_first"])
+def test_rule_programs_through_tc_fused(device, dtype, rule):
+    """The reference's optimizers hand their programs to Kernels::fused.
+    tc_fused runs a program that is a rule's update, written in place, as
+    the rule's kernel, and any other program (here the same one into fresh
+    outputs) by the interpreter: both give the bits of the oracle's
+    interpreter."""
+    from test_fused import run_gpu, run_oracle
+    n = 20011
+    code, loads, stores, updated = _rule_case(rule, dtype)
+    host = {"p": O.narrow(normal(n, 51), dtype), "g": O.narrow(normal(n, 52) * np.float32(0.1), dtype),
+            "m": O.narrow(normal(n, 53) * np.float32(0.01), dtype),
+            "v": O.narrow(np.abs(normal(n, 54)) * np.float32(1e-4), dtype),
+            "s": O.narrow(np.abs(normal(n, 55)) * np.float32(0.01), dtype)}
+    want = {k: np.empty_like(host["p"]) for k in stores}
+    run_oracle(dtype, 1, n, code, [(host[k], dtype, 0, 1, n) for k in loads], [want[k] for k in stores],
+               [dtype] * len(stores))
+    for in_place in (True, False):
+        dev = {k: cuda.CudaStorage.store(host[k], dtype) for k in loads}
+        outs = {k: dev[k] if in_place and k in updated else cuda.CudaStorage(dtype, n) for k in stores}
+        run_gpu(dtype, 1, n, code, [(dev[k], dtype, 0, 1, n) for k in loads], [outs[k] for k in stores],
+                [dtype] * len(stores))
+        for k in stores:
+            assert same_bits(outs[k].as_slice(), want[k], dtype), (in_place, k)
