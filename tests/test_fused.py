@@ -446,3 +446,30 @@ def test_forwarded_values_match_the_register_file(device, dtype):
             N.call("tc_fused_sum", N.DTYPES[dtype], rows, cols, code_arr, len(code), pl, 2, axis, out.ptr, None)
             sums.append(out.as_slice())
         assert same_bits(sums[0], sums[1], dtype), axis
+
+
+def test_oracle_runs_the_rules_programs_as_their_formulas():
+    """The programs the optimizer tests build for Momentum, Nesterov, AdaGrad
+    and RmsProp (optim.rs:826-846, 892-904, 948-964) compute the rules'
+    formulas: the oracle's interpreter against numpy's f32 arithmetic in the
+    same order (f32: every operation rounds once either way)."""
+    from test_gpu_optim import _in, _rule_program
+    n, f = 1000, np.float32
+    p, g, s = normal(n, 61), normal(n, 62) * f(0.1), np.abs(normal(n, 63)) * f(0.01)
+    rate = _in("f32", 0.01)
+    for rule in ("momentum", "nesterov", "adagrad", "rmsprop"):
+        c = _in("f32", 1e-8) if rule == "adagrad" else _in("f32", 0.9)
+        code = _rule_program("momentum" if rule == "nesterov" else rule, "f32", rate, c, nesterov=rule == "nesterov")
+        got_p, got_s = np.empty_like(p), np.empty_like(s)
+        run_oracle("f32", 1, n, code, [(g, "f32", 0, 1, n), (p, "f32", 0, 1, n), (s, "f32", 0, 1, n)],
+                   [got_p, got_s], ["f32", "f32"])
+        k, r, eps = f(c), f(rate), f(_in("f32", 1e-8))
+        if rule in ("momentum", "nesterov"):
+            want_s = s * k + g
+            step = want_s if rule == "momentum" else g + want_s * k
+            want_p = p - step * r
+        else:
+            want_s = s + g * g if rule == "adagrad" else s * k + (g * g) * (f(1) - k)
+            want_p = p - (g / (np.sqrt(want_s) + (k if rule == "adagrad" else eps))) * r
+        assert np.array_equal(got_s, want_s.astype(f)), rule
+        assert np.array_equal(got_p, want_p.astype(f)), rule
