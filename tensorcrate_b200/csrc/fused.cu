@@ -273,13 +273,19 @@ template <int E> __device__ __forceinline__ bool read_stage(const OnChip &chip, 
 // instruction (written to the file).  A unary operation other than the root
 // works between the file's rows: its operand is always in the file and its
 // result always goes there.
-enum : uint16_t { A_PREV = 1, B_PREV = 2, SPILL = 4 };
+enum : uint16_t { A_PREV = 1, B_PREV = 2, SPILL = 4, A_STAT = 8, B_STAT = 16 };
+// With A_STAT (B_STAT), operand a (b) is a row statistic, read where the row
+// kernel keeps it (its index in bits 8-11, for b 12-15), not from the file.
 
-template <int E> __device__ __forceinline__ void operand(const RegFile<E> &reg, int r, bool from_prev,
-                                                         const float prev[E], float x[E]) {
-  if (from_prev) {
+template <int E> __device__ __forceinline__ void operand(const RegFile<E> &reg, const OnChip &chip, int r,
+                                                         uint16_t f, bool is_b, const float prev[E], float x[E]) {
+  if (f & (is_b ? B_PREV : A_PREV)) {
 #pragma unroll
     for (int e = 0; e < E; ++e) x[e] = prev[e];
+  } else if (f & (is_b ? B_STAT : A_STAT)) {
+    const float v = chip.stats[(f >> (is_b ? 12 : 8)) & 15];
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = v;
   } else {
     reg.get(r, x);
   }
@@ -314,8 +320,8 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
       }
       case TC_I_BINARY: {
         float x[E], y[E];
-        operand<E>(reg, in.a, f & A_PREV, prev, x);
-        operand<E>(reg, in.b, f & B_PREV, prev, y);
+        operand<E>(reg, chip, in.a, f, false, prev, x);
+        operand<E>(reg, chip, in.b, f, true, prev, y);
         // one branch per instruction, not per element
         switch (in.op) {
           case TC_ADD:
@@ -345,7 +351,7 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
       case TC_I_UNARY: {
         if (in.op == TC_SQRT) {  // normalisations' root: a few instructions, unrolled
           float x[E];
-          operand<E>(reg, in.a, f & A_PREV, prev, x);
+          operand<E>(reg, chip, in.a, f, false, prev, x);
 #pragma unroll
           for (int e = 0; e < E; ++e) v[e] = T::load(T::store(__fsqrt_rn(x[e])));
           break;
@@ -360,8 +366,8 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
       }
       case TC_I_CMP: {
         float x[E], y[E];
-        operand<E>(reg, in.a, f & A_PREV, prev, x);
-        operand<E>(reg, in.b, f & B_PREV, prev, y);
+        operand<E>(reg, chip, in.a, f, false, prev, x);
+        operand<E>(reg, chip, in.b, f, true, prev, y);
         switch (in.op) {
           case TC_MIN:
 #pragma unroll
@@ -378,7 +384,7 @@ __device__ __forceinline__ void run_group(const Program &p, const Group<E> &g, c
         break;
       }
       default: {  // store
-        operand<E>(reg, in.a, f & A_PREV, prev, v);
+        operand<E>(reg, chip, in.a, f, false, prev, v);
         sink(int(in.slot), v);
         continue;
       }
@@ -674,7 +680,9 @@ int take_place(const tc_place &q, uint32_t j, size_t rows, size_t cols, Place &p
 
 // Which values the interpreter forwards in registers (A_PREV, B_PREV) and
 // which it writes to the register file (SPILL), from the registers each
-// instruction reads and writes; then the file's rows (n_regs).  A result that only the next instruction
+// instruction reads and writes; then the file's rows (n_regs).  A row
+// statistic's readers (other than a transcendental unary, which works
+// between file rows) read it where the row kernel keeps it (A_STAT, B_STAT).  A result that only the next instruction
 // reads stays in registers; one read later, before the register is written
 // again, goes to the file; a unary operation other than the root neither
 // takes its operand from registers nor leaves its result there.
@@ -689,13 +697,21 @@ void mark_forwarding(Program &p) {
     tc_instr &in = p.code[k];
     if (!writes(in) || generic_unary(in)) continue;  // no result, or one that goes to the file itself
     const int r = in.dst;
+    // a row statistic stays where the row kernel keeps it: its readers take it from there
+    const int stat = in.code == TC_I_LOAD ? p.places[in.slot].stat : -1;
     bool to_file = false;
     for (int j = k + 1; j < p.n_code; ++j) {
       tc_instr &next = p.code[j];
       const bool by_a = reads_a(next) && next.a == r, by_b = reads_b(next) && next.b == r;
       if (by_a || by_b) {
-        if (j == k + 1 && !generic_unary(next)) next.reserved |= (by_a ? A_PREV : 0) | (by_b ? B_PREV : 0);
-        else to_file = true;
+        if (j == k + 1 && !generic_unary(next)) {
+          next.reserved |= (by_a ? A_PREV : 0) | (by_b ? B_PREV : 0);
+        } else if (stat >= 0 && !generic_unary(next)) {
+          if (by_a) next.reserved |= A_STAT | uint16_t(stat << 8);
+          if (by_b) next.reserved |= B_STAT | uint16_t(stat << 12);
+        } else {
+          to_file = true;
+        }
       }
       if (writes(next) && next.dst == r) break;  // read (if at all) before it is written again
     }
@@ -718,8 +734,8 @@ void mark_forwarding(Program &p) {
       use(in.dst);
       continue;
     }
-    if (reads_a(in) && !(in.reserved & A_PREV)) use(in.a);
-    if (reads_b(in) && !(in.reserved & B_PREV)) use(in.b);
+    if (reads_a(in) && !(in.reserved & (A_PREV | A_STAT))) use(in.a);
+    if (reads_b(in) && !(in.reserved & (B_PREV | B_STAT))) use(in.b);
     if (in.reserved & SPILL) use(in.dst);
   }
   for (int k = 0; k < p.n_code; ++k) {
@@ -769,7 +785,6 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     p.code[k] = in;
     p.code[k].reserved = 0;
   }
-  mark_forwarding(p);
   bool is_stat[MAX_PLACES] = {false};
   for (uint32_t s = 0; s < n_stats; ++s) {
     if (stats[s].into_place >= n_places || stats[s].of_place >= n_places ||
@@ -805,6 +820,7 @@ int build_program(int dtype, size_t rows, size_t cols, const tc_instr *code, uin
     p.out[j] = outputs[j];
     p.out_dtype[j] = out_dtypes[j];
   }
+  mark_forwarding(p);  // after the places: a statistic's loads are known
   return TC_OK;
 }
 
